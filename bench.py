@@ -1,0 +1,341 @@
+#!/usr/bin/env python
+"""Decode benchmark: bs1 greedy decode tok/s of the E4B-shaped q4_0 model
+(35 layers, H=2048, 8q/2kv x 256, FF 16384, V 262144, PLE
+256/layer, 4 sliding (W=512) : 1 global), as a fraction of the HBM roofline.
+
+A step is one decoded token (one pass of the per-token plan).  Flow:
+synthetic GGUF (seeded, in memory) -> Engine (weights resident in HBM) ->
+512-token prefill -> W warm-up tokens -> K timed tokens (CUDA events on the
+engine's stream; weights >> L2, so no flush is needed between steps) -> the
+same K-token decode again through the host API with a host->device parameter
+write and a device->host token read every step (`e2e`) -> the dominant
+kernel's launches timed alone for the roofline -> the CPU oracle timed on a
+bounded sample (`cpu_baseline`).
+
+Multi-GPU: the dense decode does not shard, so N GPUs run N independent
+replicas ("replicas only"); value = all tokens / max-over-ranks time.
+`--impl reference` times the reference path's CPU restatement (the oracle) on
+the host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import importlib
+import io
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s bs1 E4B-shaped q4_0 (% of HBM roofline)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class Dist:
+    """Barrier and max-over-ranks for N > 1 (torch.distributed is plumbing only)."""
+
+    def __init__(self, world, local_rank, backend):
+        self.world = world
+        self.pg = None
+        if world > 1:
+            import datetime
+            import torch
+            import torch.distributed as td
+            if backend == "nccl":
+                torch.cuda.set_device(local_rank)
+            td.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            self.td, self.torch = td, torch
+            self.dev = f"cuda:{local_rank}" if backend == "nccl" else "cpu"
+
+    def barrier(self):
+        if self.world > 1:
+            self.td.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.dev)
+        self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.td.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.p = gpu, None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return None
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if "Active" in v and "Not" not in v:
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip().replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def traffic_from_profile(name: str):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+def token_bytes(cfg, ctx_len: int) -> dict:
+    """Algorithmic HBM bytes of one decode token (all weights touched once, the
+    q6_K LM head, the embedding and PLE-table rows, and the KV cache read over
+    the attended positions plus the new K/V write)."""
+    H, L = cfg.hidden, cfg.layers
+    q4 = lambda rows, n_in: rows * n_in // 32 * 18
+    w = 0
+    for l in range(L):
+        w += q4(cfg.qkv_rows(l), H) + q4(H, cfg.q_dim) + q4(2 * cfg.ff, H) + q4(H, cfg.ff)
+        if cfg.ple_dim:
+            w += q4(cfg.ple_dim, H) + q4(H, cfg.ple_dim)
+    if cfg.ple_dim:
+        w += q4(L * cfg.ple_dim, H) + L * cfg.ple_dim // 256 * 210
+    head = cfg.vocab * H // 256 * 210
+    emb_row = H // 256 * 210
+    kv = 0
+    per_pos = cfg.kv_heads * cfg.head_dim * 2 * 2
+    for l in range(L):
+        att = min(ctx_len, cfg.window) if cfg.is_sliding(l) else ctx_len
+        kv += att * per_pos + per_pos
+    return {"weights": w, "lm_head": head, "embed": emb_row, "kv": kv, "total": w + head + emb_row + kv}
+
+
+def run_ours(args, rank, world, local_rank):
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    import __graft_entry__
+    __graft_entry__.build()
+    dist = Dist(world, local_rank, "nccl" if world > 1 else None)
+    cfg = e4b.config.get(args.config)
+    t0 = time.time()
+    img = e4b.synth.build_model(cfg, seed=0)
+    t_build = time.time() - t0
+    eng = e4b.Engine(img, local_rank)
+    dev = eng.dev
+    prompt = e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=0)
+    eng.prefill(prompt)
+    dev.sync()
+    pos = len(prompt)
+    # warm-up (plan already recorded by the prefill)
+    eng.decode_chunk(args.warmup)
+    dev.sync()
+    pos += args.warmup
+    ctx_mid = pos + args.steps // 2
+    # ---- device-resident timed region
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    dist.barrier()
+    dev.sync()
+    dev.call("e4b_event_record", 0)
+    eng.decode_chunk(args.steps)
+    dev.call("e4b_event_record", 1)
+    dev.sync()
+    import ctypes
+    ms = ctypes.c_float()
+    dev.call("e4b_event_elapsed", 0, 1, ctypes.byref(ms))
+    t_dev = dist.max(ms.value / 1000.0)
+    pos += args.steps
+    clk = clocks.stop()
+    # ---- end to end through the host API: per step one H2D parameter write from
+    # pinned memory, the token plan, one D2H token read, host sync.
+    tok = int(eng.read_ring(pos - 1, 1)[0])
+    dist.barrier()
+    dev.sync()
+    dev.call("e4b_event_record", 2)
+    for i in range(args.steps):
+        eng.set_params(tok, pos)
+        eng.run_token(1)
+        dev.call("e4b_download_async", ctypes.c_void_p(eng._host_tok_ptr), eng.A.amax.ptr, ctypes.c_size_t(4))
+        dev.sync()
+        tok = int(eng.host_tok[0])
+        pos += 1
+    dev.call("e4b_event_record", 3)
+    dev.sync()
+    dev.call("e4b_event_elapsed", 2, 3, ctypes.byref(ms))
+    t_e2e = dist.max(ms.value / 1000.0)
+    # ---- dominant kernel timed alone: the dense gate|up GEMV (+GeGLU) of every
+    # layer, each launch over different weights (cold L2), CUDA events on the stream
+    A = eng.A
+    H, FF = cfg.hidden, cfg.ff
+    nrep = 3
+    dev.call("e4b_event_record", 4)
+    for _ in range(nrep):
+        for L in eng.layers:
+            e4b.ops.q40gu(dev, None, None, None, None, A.normed, L.gu, A.geglu, IN=H, FF=0, FF2=FF, K=0)
+    dev.call("e4b_event_record", 5)
+    dev.sync()
+    dev.call("e4b_event_elapsed", 4, 5, ctypes.byref(ms))
+    gu_launch_s = ms.value / 1000.0 / (nrep * cfg.layers)
+    gu_bytes = 2 * FF * H // 32 * 18 + H * 2 + FF * 2
+    peak, peak_kind = peaks()
+    tb = token_bytes(cfg, ctx_mid)
+    kernels_per_token = eng.kernels_per_token
+    status = dev.status()
+    eng.close()
+    if status:
+        raise RuntimeError(f"device status word {status:#x} after the run")
+    value = world * args.steps / t_dev
+    e2e = world * args.steps / t_e2e
+    out = None
+    if rank == 0:
+        ach = gu_bytes / gu_launch_s / 1e9
+        traffic = traffic_from_profile("q40gu_e4b.md")
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000 * t_dev / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0/q6_K weights, f32 accumulate, f16 activations",
+            "data": "synthetic: seeded N(0,0.02) weights quantised to q4_0/q6_K, uniform prompt ids (seed 0)",
+            "config": {"workload": f"{cfg.name}: bs1 greedy decode after a {args.prefill}-token prefill",
+                       "model": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "ff": cfg.ff,
+                       "vocab": cfg.vocab, "global_batch": world, "seq_len": ctx_mid,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "weights (%.2f GB/token) >> 126 MB L2: no flush needed" % (tb["total"] / 1e9)},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "hbm", "kernel": "q40gu (dense gate|up + GeGLU, 2048 -> 2x16384)",
+                         "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(ach / peak, 4), "peak_source": peak_kind,
+                         "bytes_per_launch": gu_bytes, "launch_us": round(gu_launch_s * 1e6, 2),
+                         "traffic": traffic},
+            "token_roofline": {"bytes_per_token": tb["total"], "breakdown": tb,
+                               "achieved_gbs": round(tb["total"] * value / world / 1e9, 1),
+                               "frac": round(tb["total"] * value / world / 1e9 / peak, 4),
+                               "roofline_tok_s": round(peak * 1e9 / tb["total"], 1)},
+            "clocks": clk,
+            "gpu_launches": int(kernels_per_token * args.steps),
+            "kernels_per_token": kernels_per_token,
+            "model_build_s": round(t_build, 1),
+        }
+    dist.close()
+    return out, img, cfg
+
+
+def cpu_baseline(img, cfg, budget_s: float, max_steps: int):
+    """The oracle (CPU restatement of the reference path) on this host's cores:
+    a short prompt, then timed greedy decode steps (bounded by budget_s)."""
+    from oracle import ops as O
+    from oracle.model import OracleModel
+    m = OracleModel(img)
+    lib = O.qlib()
+    cores = int(lib.oracle_threads())
+    prompt = [1, 2, 3, 4]
+    tok = None
+    for p, t in enumerate(prompt):
+        tok, _ = m.step(t, p)
+    pos = len(prompt)
+    n, t0 = 0, time.time()
+    while n < max_steps and (time.time() - t0) < budget_s:
+        tok, _ = m.step(tok, pos)
+        pos += 1
+        n += 1
+    dt = time.time() - t0
+    return {"value": round(n / dt, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} greedy decode steps of {cfg.name} after a {len(prompt)}-token prompt "
+                      f"(context {len(prompt)}..{pos}; attention is <2% of a token's bytes), oracle C q4_0/q6_K "
+                      f"matvecs on {cores} OpenMP threads + numpy"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    import __graft_entry__
+    __graft_entry__.build()
+    cfg = e4b.config.get(args.config)
+    img = e4b.synth.build_model(cfg, seed=0)
+    # each "step" of the reference arm is a bounded sample of CPU decode steps
+    steps = max(1, min(args.steps, 16))
+    warm = min(args.warmup, 1)
+    base = cpu_baseline(img, cfg, budget_s=60.0, max_steps=steps + warm)
+    v = base["value"]
+    return {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": round(1000.0 / v, 2) if v else None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_0/q6_K weights, f32 accumulate, f16 activations",
+            "data": "synthetic (same seeded model as the ours arm)", "impl": "reference",
+            "config": {"workload": f"{cfg.name}: bs1 greedy decode", "model": cfg.name},
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="e4b")
+    ap.add_argument("--prefill", type=int, default=512)
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank, world, local_rank = dist_env()
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+    else:
+        out, img, cfg = run_ours(args, rank, world, local_rank)
+        if rank == 0:
+            out["cpu_baseline"] = None if args.no_cpu else cpu_baseline(img, cfg, args.cpu_budget, 64)
+    if rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

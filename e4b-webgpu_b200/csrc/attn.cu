@@ -1,0 +1,253 @@
+// Decode attention: head prep (q/k RMSNorm + RoPE, v norm, f16 KV write),
+// RoPE, KV write, and split-KV flash-decode (phase A partials + phase B LSE merge)
+// over the f16 KV cache with GQA, sliding ring and global (linear) layers.
+#include "common.cuh"
+
+namespace {
+
+E4B_DEV float rope_theta(uint32_t pos, int p, int HD, float theta) {
+  // pos * THETA^(-2p/HD), in f32 (kernels/headprep.wgsl:55)
+  const float ex = (-2.0f * (float)p) / (float)HD;
+  return (float)pos * powf(theta, ex);
+}
+
+__global__ void k_headprep(const float* __restrict__ qkv, const float* __restrict__ qw, const float* __restrict__ kw,
+                           const uint32_t* __restrict__ params, uint16_t* __restrict__ kcache,
+                           uint16_t* __restrict__ vcache, float* __restrict__ q_out, int QH, int KVH, int HD,
+                           int angles, float theta, float eps, int keqv, int cachemode, int ring, int cache_slots,
+                           uint32_t* status) {
+  pdl_wait();
+  __shared__ float sh[32];
+  const int head = blockIdx.x, b = blockIdx.y;
+  int src = head;
+  if (keqv && head >= QH + KVH) src = head - KVH;  // v reads the k slice
+  const size_t qkvS = (size_t)(QH + KVH * (2 - keqv)) * HD;
+  const size_t base = (size_t)b * qkvS + (size_t)src * HD;
+  float s = 0.f;
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) s = fmaf(qkv[base + d], qkv[base + d], s);
+  const float inv = rms_scale(block_sum(s, sh), HD, eps);
+  const int half = HD / 2;
+  const uint32_t pos = params[0] + b;
+  uint32_t slot = pos;
+  if (cachemode == 1) slot = pos % (uint32_t)ring;
+  if (cachemode == 2) slot = params[4] + b;
+  if (head >= QH && slot >= (uint32_t)cache_slots) {
+    if (threadIdx.x == 0) set_status(status, E4B_ST_BADINDEX);
+    return;
+  }
+  if (head < QH) {
+    float* qo = q_out + ((size_t)b * QH + head) * HD;
+    for (int p = threadIdx.x; p < half; p += blockDim.x) {
+      const float x0 = qkv[base + p] * inv * qw[p];
+      const float x1 = qkv[base + p + half] * inv * qw[p + half];
+      if (p < angles) {
+        float sn, cs;
+        sincosf(rope_theta(pos, p, HD, theta), &sn, &cs);
+        qo[p] = x0 * cs - x1 * sn;
+        qo[p + half] = x0 * sn + x1 * cs;
+      } else {
+        qo[p] = x0;
+        qo[p + half] = x1;
+      }
+    }
+  } else if (head < QH + KVH) {
+    const int h = head - QH;
+    uint16_t* kc = kcache + ((size_t)slot * KVH + h) * HD;
+    for (int p = threadIdx.x; p < half; p += blockDim.x) {
+      const float x0 = qkv[base + p] * inv * kw[p];
+      const float x1 = qkv[base + p + half] * inv * kw[p + half];
+      if (p < angles) {
+        float sn, cs;
+        sincosf(rope_theta(pos, p, HD, theta), &sn, &cs);
+        kc[p] = f2h(x0 * cs - x1 * sn);
+        kc[p + half] = f2h(x0 * sn + x1 * cs);
+      } else {
+        kc[p] = f2h(x0);
+        kc[p + half] = f2h(x1);
+      }
+    }
+  } else {
+    const int h = head - QH - KVH;
+    uint16_t* vc = vcache + ((size_t)slot * KVH + h) * HD;
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) vc[d] = f2h(qkv[base + d] * inv);
+  }
+}
+
+__global__ void k_rope(float* __restrict__ x, const uint32_t* __restrict__ params, int heads, int HD, int angles,
+                       float theta) {
+  pdl_wait();
+  const int half = HD / 2;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= heads * half) return;
+  const int h = idx / half, p = idx % half;
+  if (p >= angles) return;
+  float sn, cs;
+  sincosf(rope_theta(params[0], p, HD, theta), &sn, &cs);
+  const size_t i0 = (size_t)h * HD + p, i1 = i0 + half;
+  const float x0 = x[i0], x1 = x[i1];
+  x[i0] = x0 * cs - x1 * sn;
+  x[i1] = x0 * sn + x1 * cs;
+}
+
+__global__ void k_kvwrite(const float* __restrict__ src, const uint32_t* __restrict__ params, float* __restrict__ dst,
+                          int N) {
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < N) dst[(size_t)params[0] * N + i] = src[i];
+}
+
+// Number of addressable slots and whether slot t is attended, for the query at
+// position qp (kernels/attnf32.wgsl:28-53, attsplit.wgsl:21-23).
+struct SlotRule {
+  int cachemode, ring, window;
+  uint32_t qp, len;
+  E4B_DEV uint32_t nslots() const {
+    if (cachemode == 1) return min(qp + 1, (uint32_t)ring);
+    return len;
+  }
+  E4B_DEV bool valid(uint32_t t) const {
+    if (cachemode == 1) {
+      const uint32_t ps = qp - ((qp + (uint32_t)ring - t) % (uint32_t)ring);  // slot t's true position
+      return ps <= qp && ps + (uint32_t)window > qp;
+    }
+    if (t >= len) return false;
+    if (cachemode == 0 && window > 0 && len > (uint32_t)window) return t >= len - (uint32_t)window;
+    return true;
+  }
+};
+
+// Phase A: CTA (head h, chunk c) scores `chunk` slots (one per thread), then
+// accumulates p_t * v_t over its dims.  Output unnormalised with local (m, l).
+__global__ void k_attsplit(const float* __restrict__ q, const uint16_t* __restrict__ kcache,
+                           const uint16_t* __restrict__ vcache, const uint32_t* __restrict__ params,
+                           float* __restrict__ part_o, float* __restrict__ part_ml, int QH, int KVH, int HD,
+                           int window, int cachemode, int ring, int max_chunks, float scale) {
+  pdl_wait();
+  extern __shared__ float smem[];
+  float* qs = smem;            // [HD]
+  float* ps = smem + HD;       // [chunk]
+  __shared__ float sh[32];
+  const int h = blockIdx.x, c = blockIdx.y, chunk = blockDim.x;
+  const int kvh = h / (QH / KVH);
+  SlotRule rule{cachemode, ring, window, 0, 0};
+  rule.qp = params[0];
+  rule.len = cachemode == 2 ? params[5] : params[1];
+  const uint32_t n = rule.nslots();
+  const uint32_t t0 = (uint32_t)c * chunk;
+  const size_t pi = (size_t)h * max_chunks + c;
+  for (int d = threadIdx.x; d < HD; d += chunk) qs[d] = q[(size_t)h * HD + d];
+  __syncthreads();
+  const uint32_t t = t0 + threadIdx.x;
+  const bool ok = t < n && rule.valid(t);
+  float s = -INFINITY;
+  if (ok) {
+    const uint16_t* kr = kcache + ((size_t)t * KVH + kvh) * HD;
+    float acc = 0.f;
+    for (int d = 0; d < HD; d += 2) {
+      const __half2 kv = *reinterpret_cast<const __half2*>(kr + d);
+      const float2 kf = __half22float2(kv);
+      acc = fmaf(qs[d], kf.x, acc);
+      acc = fmaf(qs[d + 1], kf.y, acc);
+    }
+    s = acc * scale;
+  }
+  const float m = block_max(s, sh);
+  const float p = ok ? expf(s - m) : 0.f;
+  ps[threadIdx.x] = p;
+  const float l = block_sum(p, sh);
+  if (threadIdx.x == 0) {
+    part_ml[2 * pi] = l > 0.f ? m : -INFINITY;
+    part_ml[2 * pi + 1] = l;
+  }
+  const uint32_t hi = min(t0 + (uint32_t)chunk, n);
+  for (int d = threadIdx.x; d < HD; d += chunk) {
+    float acc = 0.f;
+    for (uint32_t tt = t0; tt < hi; tt++) {
+      const float pp = ps[tt - t0];
+      if (pp != 0.f) acc = fmaf(pp, h2f(vcache[((size_t)tt * KVH + kvh) * HD + d]), acc);
+    }
+    part_o[pi * HD + d] = acc;
+  }
+}
+
+__global__ void k_attcomb(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                          uint16_t* __restrict__ out_h, float* __restrict__ out_f, float* __restrict__ lse, int HD,
+                          int max_chunks) {
+  pdl_wait();
+  const int h = blockIdx.x;
+  const float* ml = part_ml + (size_t)h * max_chunks * 2;
+  float M = -INFINITY;
+  for (int c = 0; c < max_chunks; c++)
+    if (ml[2 * c + 1] > 0.f) M = fmaxf(M, ml[2 * c]);
+  float den = 0.f;
+  for (int c = 0; c < max_chunks; c++)
+    if (ml[2 * c + 1] > 0.f) den += ml[2 * c + 1] * expf(ml[2 * c] - M);
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float acc = 0.f;
+    for (int c = 0; c < max_chunks; c++)
+      if (ml[2 * c + 1] > 0.f) acc = fmaf(part_o[((size_t)h * max_chunks + c) * HD + d], expf(ml[2 * c] - M), acc);
+    const float v = den > 0.f ? acc / den : 0.f;
+    if (out_h) out_h[(size_t)h * HD + d] = f2h(v);
+    if (out_f) out_f[(size_t)h * HD + d] = v;
+  }
+  if (lse && threadIdx.x == 0) lse[h] = den > 0.f ? M + logf(den) : -INFINITY;
+}
+
+}  // namespace
+
+extern "C" {
+
+E4B_API int e4b_headprep(e4b_ctx* c, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
+                         uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD, int rope_angles,
+                         float theta, float eps, int keqv, int cachemode, int ring, int cache_slots, int batch) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, qkv && qw && kw && params && kcache && vcache && q_out, "headprep: null buffer");
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD % 2 == 0 && rope_angles >= 0 &&
+                     rope_angles <= HD / 2 && cache_slots > 0,
+              "headprep: bad geometry QH=%d KVH=%d HD=%d angles=%d", QH, KVH, HD, rope_angles);
+  E4B_REQUIRE(c, cachemode >= 0 && cachemode <= 2 && (cachemode != 1 || (ring > 0 && ring <= cache_slots)),
+              "headprep: bad cache mode %d / ring %d", cachemode, ring);
+  if (batch < 1) batch = 1;
+  return e4b_launch(c, "headprep", k_headprep, dim3(QH + 2 * KVH, batch), dim3(128), 0, qkv, qw, kw, params, kcache,
+                    vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring, cache_slots,
+                    c->status);
+}
+
+E4B_API int e4b_rope(e4b_ctx* c, float* x, const uint32_t* params, int heads, int HD, int rope_angles, float theta) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && params && heads > 0 && HD > 0 && HD % 2 == 0 && rope_angles <= HD / 2, "rope: bad args");
+  const int n = heads * HD / 2;
+  return e4b_launch(c, "rope", k_rope, dim3((n + 127) / 128), dim3(128), 0, x, params, heads, HD, rope_angles, theta);
+}
+
+E4B_API int e4b_kvwrite(e4b_ctx* c, const float* src, const uint32_t* params, float* dst, int N) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, src && params && dst && N > 0, "kvwrite: bad args");
+  return e4b_launch(c, "kvwrite", k_kvwrite, dim3((N + 127) / 128), dim3(128), 0, src, params, dst, N);
+}
+
+E4B_API int e4b_attsplit(e4b_ctx* c, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                         const uint32_t* params, float* part_o, float* part_ml, int QH, int KVH, int HD, int window,
+                         int cachemode, int ring, int chunk, int max_chunks, float scale) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, q && kcache && vcache && params && part_o && part_ml, "attsplit: null buffer");
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD % 2 == 0 && max_chunks > 0,
+              "attsplit: bad geometry");
+  E4B_REQUIRE(c, chunk >= 32 && chunk <= 1024 && (chunk & 31) == 0, "attsplit: chunk %d must be 32..1024, x32",
+              chunk);
+  E4B_REQUIRE(c, cachemode >= 0 && cachemode <= 2 && (cachemode != 1 || (ring > 0 && window > 0)),
+              "attsplit: bad cache mode");
+  const size_t sm = (size_t)(HD + chunk) * 4;
+  return e4b_launch(c, "attsplit", k_attsplit, dim3(QH, max_chunks), dim3(chunk), sm, q, kcache, vcache, params,
+                    part_o, part_ml, QH, KVH, HD, window, cachemode, ring, max_chunks, scale);
+}
+
+E4B_API int e4b_attcomb(e4b_ctx* c, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
+                        float* lse, int QH, int HD, int max_chunks) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, part_o && part_ml && (out_h || out_f) && QH > 0 && HD > 0 && max_chunks > 0, "attcomb: bad args");
+  return e4b_launch(c, "attcomb", k_attcomb, dim3(QH), dim3(128), 0, part_o, part_ml, out_h, out_f, lse, HD,
+                    max_chunks);
+}
+
+}  // extern "C"

@@ -1,0 +1,204 @@
+// MoE routing (routertop / router / top8), two-stage argmax and the GPU-side
+// token feedback that makes a recorded per-token plan replayable.
+#include "common.cuh"
+
+namespace {
+
+// Softmax over E scores (p in shared memory, overwritten with exp(s-max)),
+// then K rounds of first-maximum selection, renormalisation and x pes
+// (kernels/routertop.wgsl:51-69).  Run by warp 0 of the CTA.
+E4B_DEV void softmax_topk(float* p, int E, int K, const float* __restrict__ pes, uint32_t* __restrict__ idx_out,
+                          float* __restrict__ w_out) {
+  const int lane = threadIdx.x & 31;
+  float mx = -3.0e38f;
+  for (int i = lane; i < E; i += 32) mx = fmaxf(mx, p[i]);
+  mx = warp_max(mx);
+  for (int i = lane; i < E; i += 32) p[i] = expf(p[i] - mx);
+  __syncwarp();
+  float sum = 0.f;
+  if (lane == 0)
+    for (int i = 0; i < E; i++) sum += p[i];  // sequential, as the reference's single-thread epilogue
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  float wsum = 0.f;
+  float wk[32];
+  uint32_t ik[32];
+  for (int k = 0; k < K; k++) {
+    float bv = -1.0f;
+    int bi = 0x7fffffff;
+    for (int i = lane; i < E; i += 32)
+      if (p[i] > bv) { bv = p[i]; bi = i; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    const float w = bv / sum;
+    if (k < 32) { wk[k] = w; ik[k] = (uint32_t)bi; }
+    wsum += w;
+    __syncwarp();
+    if (lane == 0) p[bi] = -2.0f;
+    __syncwarp();
+  }
+  if (lane == 0)
+    for (int k = 0; k < K && k < 32; k++) {
+      idx_out[k] = ik[k];
+      w_out[k] = wk[k] / wsum * pes[ik[k]];
+    }
+}
+
+// One CTA per token: warps split the E expert dot products over H.
+__global__ void __launch_bounds__(256) k_routertop(const float* __restrict__ x, const float* __restrict__ wr,
+                                                   const float* __restrict__ pes, uint32_t* __restrict__ topk_idx,
+                                                   float* __restrict__ topk_w, int H, int E, int K) {
+  pdl_wait();
+  extern __shared__ float p[];
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const float* xr = x + (size_t)b * H;
+  for (int e = warp; e < E; e += nw) {
+    const float* w = wr + (size_t)e * H;
+    float acc = 0.f;
+    for (int j = lane; j < H; j += 32) acc = fmaf(xr[j], w[j], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) p[e] = acc;
+  }
+  __syncthreads();
+  if (warp == 0) softmax_topk(p, E, K, pes, topk_idx + (size_t)b * K, topk_w + (size_t)b * K);
+}
+
+// kernels/router.wgsl: scale-less RMS of h, x H^-0.5 x scale, then scores + top-K.
+__global__ void __launch_bounds__(256) k_router(const float* __restrict__ h, const float* __restrict__ scale,
+                                                const float* __restrict__ wr, const float* __restrict__ pes,
+                                                uint32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int H,
+                                                int E, int K, float eps) {
+  pdl_wait();
+  extern __shared__ float p[];
+  __shared__ float sh[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) s = fmaf(h[i], h[i], s);
+  const float inv = rms_scale(block_sum(s, sh), H, eps) * (1.0f / sqrtf((float)H));
+  for (int e = warp; e < E; e += nw) {
+    const float* w = wr + (size_t)e * H;
+    float acc = 0.f;
+    for (int j = lane; j < H; j += 32) acc = fmaf(h[j] * inv * scale[j], w[j], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) p[e] = acc;
+  }
+  __syncthreads();
+  if (warp == 0) softmax_topk(p, E, K, pes, topk_idx, topk_w);
+}
+
+__global__ void k_top8(const float* __restrict__ scores, const float* __restrict__ pes, uint32_t* __restrict__ idx,
+                       float* __restrict__ w, int E, int K) {
+  pdl_wait();
+  extern __shared__ float p[];
+  for (int i = threadIdx.x; i < E; i += 32) p[i] = scores[i];
+  __syncwarp();
+  softmax_topk(p, E, K, pes, idx, w);
+}
+
+// argmax stage 0: CTA i reduces slice i -> part[2i] = index, part[2i+1] = f32 bits
+// (kernels/argmax2.wgsl:15-22); ties -> lowest index.
+E4B_DEV void argmax_merge(float& bv, uint32_t& bi, float ov, uint32_t oi) {
+  if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+}
+E4B_DEV void block_argmax(float& bv, uint32_t& bi) {
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    argmax_merge(bv, bi, ov, oi);
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = 1; i < nw; i++) argmax_merge(bv, bi, sv[i], si[i]);
+}
+__global__ void k_argmax0(const float* __restrict__ x, uint32_t* __restrict__ part, int N, int parts) {
+  pdl_wait();
+  const int per = (N + parts - 1) / parts;
+  const int lo = blockIdx.x * per, hi = min(lo + per, N);
+  float bv = -3.0e38f;
+  uint32_t bi = 0xffffffffu;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) argmax_merge(bv, bi, x[i], (uint32_t)i);
+  block_argmax(bv, bi);
+  if (threadIdx.x == 0) {
+    part[2 * blockIdx.x] = bi;
+    part[2 * blockIdx.x + 1] = __float_as_uint(bv);
+  }
+}
+__global__ void k_argmax1(const uint32_t* __restrict__ part, uint32_t* __restrict__ out, int parts) {
+  pdl_wait();
+  float bv = -3.0e38f;
+  uint32_t bi = 0xffffffffu;
+  for (int i = threadIdx.x; i < parts; i += blockDim.x) argmax_merge(bv, bi, __uint_as_float(part[2 * i + 1]), part[2 * i]);
+  block_argmax(bv, bi);
+  if (threadIdx.x == 0) {
+    out[0] = bi;
+    out[1] = __float_as_uint(bv);
+  }
+}
+
+__global__ void k_feedtok(const uint32_t* __restrict__ amax, uint32_t* __restrict__ params, uint32_t* __restrict__ ring,
+                          int ring_cap) {
+  pdl_wait();
+  const uint32_t t = amax[0];
+  if (ring) ring[params[6] % (uint32_t)ring_cap] = t;
+  params[2] = t;
+  params[0] += 1;
+  params[1] += 1;
+  params[4] += 1;
+  params[5] += 1;
+  params[6] += 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+E4B_API int e4b_routertop(e4b_ctx* c, const float* x, const float* wr, const float* pes, uint32_t* topk_idx,
+                          float* topk_w, int H, int E, int K, int batch) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && wr && pes && topk_idx && topk_w, "routertop: null buffer");
+  E4B_REQUIRE(c, H > 0 && E > 0 && E <= 4096 && K > 0 && K <= 32 && K <= E, "routertop: bad sizes H=%d E=%d K=%d", H,
+              E, K);
+  if (batch < 1) batch = 1;
+  return e4b_launch(c, "routertop", k_routertop, dim3(batch), dim3(256), (size_t)E * 4, x, wr, pes, topk_idx, topk_w,
+                    H, E, K);
+}
+
+E4B_API int e4b_router(e4b_ctx* c, const float* h, const float* scale, const float* wr, const float* pes,
+                       uint32_t* topk_idx, float* topk_w, int H, int E, int K, float eps) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, h && scale && wr && pes && topk_idx && topk_w, "router: null buffer");
+  E4B_REQUIRE(c, H > 0 && E > 0 && E <= 4096 && K > 0 && K <= 32 && K <= E, "router: bad sizes");
+  return e4b_launch(c, "router", k_router, dim3(1), dim3(256), (size_t)E * 4, h, scale, wr, pes, topk_idx, topk_w, H,
+                    E, K, eps);
+}
+
+E4B_API int e4b_top8(e4b_ctx* c, const float* scores, const float* pes, uint32_t* topk_idx, float* topk_w, int E,
+                     int K) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, scores && pes && topk_idx && topk_w && E > 0 && E <= 4096 && K > 0 && K <= 32 && K <= E,
+              "top8: bad args");
+  return e4b_launch(c, "top8", k_top8, dim3(1), dim3(32), (size_t)E * 4, scores, pes, topk_idx, topk_w, E, K);
+}
+
+E4B_API int e4b_argmax(e4b_ctx* c, const float* x, uint32_t* part, uint32_t* out, int N, int parts) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && part && out && N > 0 && parts > 0 && parts <= 4096, "argmax: bad args");
+  if (int r = e4b_launch(c, "argmax0", k_argmax0, dim3(parts), dim3(256), 0, x, part, N, parts)) return r;
+  return e4b_launch(c, "argmax1", k_argmax1, dim3(1), dim3(256), 0, (const uint32_t*)part, out, parts);
+}
+
+E4B_API int e4b_feedtok(e4b_ctx* c, const uint32_t* amax, uint32_t* params, uint32_t* ring, int ring_cap) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, amax && params && (!ring || ring_cap > 0), "feedtok: bad args");
+  return e4b_launch(c, "feedtok", k_feedtok, dim3(1), dim3(1), 0, amax, params, ring, ring_cap);
+}
+
+}  // extern "C"

@@ -1,0 +1,223 @@
+// Context, memory, timing, status word and plan (CUDA graph) management.
+// Replaces the reference's WebGPU runtime helpers (src/gpu.js:4-50) and its
+// per-token plan record/replay (src/engine-a4b.js:800-818).
+#include "common.cuh"
+
+int e4b_fail(e4b_ctx* c, int code, const char* fmt, ...) {
+  if (c) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(c->err, sizeof(c->err), fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+extern "C" {
+
+E4B_API int e4b_create(int device, e4b_ctx** out) {
+  if (!out) return E4B_EINVAL;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return E4B_ECUDA;
+  e4b_ctx* c = new e4b_ctx();
+  c->device = device;
+  if (cudaSetDevice(device) != cudaSuccess) { delete c; return E4B_ECUDA; }
+  cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { delete c; return E4B_ECUDA; }
+  for (auto& e : c->ev) cudaEventCreate(&e);
+  if (cudaMalloc(&c->status, 256) != cudaSuccess) { delete c; return E4B_ENOMEM; }
+  cudaMemset(c->status, 0, 256);
+  cudaDeviceSynchronize();
+  *out = c;
+  return E4B_OK;
+}
+
+E4B_API int e4b_destroy(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (auto& g : c->plans)
+    if (g) cudaGraphExecDestroy(g);
+  for (auto& e : c->ev) cudaEventDestroy(e);
+  cudaFree(c->status);
+  cudaStreamDestroy(c->stream);
+  delete c;
+  return E4B_OK;
+}
+
+E4B_API const char* e4b_last_error(const e4b_ctx* c) { return c ? c->err : "null context"; }
+
+E4B_API int e4b_device_info(e4b_ctx* c, int* sm_count, int* cc_major, int* cc_minor, size_t* total_mem) {
+  E4B_CHECK_CTX(c);
+  cudaDeviceProp p;
+  E4B_CUDA(c, cudaGetDeviceProperties(&p, c->device));
+  if (sm_count) *sm_count = p.multiProcessorCount;
+  if (cc_major) *cc_major = p.major;
+  if (cc_minor) *cc_minor = p.minor;
+  if (total_mem) *total_mem = p.totalGlobalMem;
+  return E4B_OK;
+}
+
+E4B_API int e4b_alloc(e4b_ctx* c, size_t bytes, void** out) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, out, "e4b_alloc: null out");
+  *out = nullptr;
+  cudaError_t e = cudaMalloc(out, bytes ? bytes : 16);
+  if (e != cudaSuccess) return e4b_fail(c, E4B_ENOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  return E4B_OK;
+}
+E4B_API int e4b_free(e4b_ctx* c, void* p) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaFree(p));
+  return E4B_OK;
+}
+E4B_API int e4b_host_alloc(e4b_ctx* c, size_t bytes, void** out) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, out, "e4b_host_alloc: null out");
+  cudaError_t e = cudaMallocHost(out, bytes ? bytes : 16);
+  if (e != cudaSuccess) return e4b_fail(c, E4B_ENOMEM, "cudaMallocHost(%zu): %s", bytes, cudaGetErrorString(e));
+  return E4B_OK;
+}
+E4B_API int e4b_host_free(e4b_ctx* c, void* p) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaFreeHost(p));
+  return E4B_OK;
+}
+E4B_API int e4b_upload(e4b_ctx* c, void* dst, const void* src, size_t n) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, c->stream));
+  E4B_CUDA(c, cudaStreamSynchronize(c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_download(e4b_ctx* c, void* dst, const void* src, size_t n) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, c->stream));
+  E4B_CUDA(c, cudaStreamSynchronize(c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_upload_async(e4b_ctx* c, void* dst, const void* src, size_t n) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_download_async(e4b_ctx* c, void* dst, const void* src, size_t n) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_memset(e4b_ctx* c, void* dst, int v, size_t n) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaMemsetAsync(dst, v, n, c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_copy(e4b_ctx* c, void* dst, const void* src, size_t n) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_sync(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  E4B_CUDA(c, cudaStreamSynchronize(c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_event_record(e4b_ctx* c, int slot) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, slot >= 0 && slot < 64, "event slot %d out of range", slot);
+  E4B_CUDA(c, cudaEventRecord(c->ev[slot], c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_event_elapsed(e4b_ctx* c, int a, int b, float* ms) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, a >= 0 && a < 64 && b >= 0 && b < 64 && ms, "bad event args");
+  E4B_CUDA(c, cudaEventSynchronize(c->ev[b]));
+  E4B_CUDA(c, cudaEventElapsedTime(ms, c->ev[a], c->ev[b]));
+  return E4B_OK;
+}
+E4B_API int e4b_set_pdl(e4b_ctx* c, int enable) {
+  E4B_CHECK_CTX(c);
+  c->pdl = enable != 0;
+  return E4B_OK;
+}
+E4B_API int e4b_device_status(e4b_ctx* c, uint32_t* st) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, st, "null status out");
+  E4B_CUDA(c, cudaMemcpyAsync(st, c->status, 4, cudaMemcpyDeviceToHost, c->stream));
+  E4B_CUDA(c, cudaMemsetAsync(c->status, 0, 4, c->stream));
+  E4B_CUDA(c, cudaStreamSynchronize(c->stream));
+  return E4B_OK;
+}
+
+E4B_API int e4b_plan_begin(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, !c->capturing, "plan already being recorded");
+  E4B_CUDA(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  c->capturing = true;
+  return E4B_OK;
+}
+E4B_API int e4b_plan_end(e4b_ctx* c, int* plan) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, c->capturing && plan, "no plan being recorded");
+  c->capturing = false;
+  cudaGraph_t g = nullptr;
+  E4B_CUDA(c, cudaStreamEndCapture(c->stream, &g));
+  cudaGraphExec_t ex = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+  c->plans.push_back(ex);
+  *plan = (int)c->plans.size() - 1;
+  return E4B_OK;
+}
+E4B_API int e4b_plan_launch(e4b_ctx* c, int plan, int count) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, plan >= 0 && plan < (int)c->plans.size() && c->plans[plan], "bad plan %d", plan);
+  for (int i = 0; i < count; i++) E4B_CUDA(c, cudaGraphLaunch(c->plans[plan], c->stream));
+  return E4B_OK;
+}
+E4B_API int e4b_plan_destroy(e4b_ctx* c, int plan) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, plan >= 0 && plan < (int)c->plans.size() && c->plans[plan], "bad plan %d", plan);
+  E4B_CUDA(c, cudaGraphExecDestroy(c->plans[plan]));
+  c->plans[plan] = nullptr;
+  return E4B_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ dequant
+__global__ void k_dequant_q40(const uint8_t* __restrict__ w, float* __restrict__ out, int64_t nblocks) {
+  pdl_wait();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nblocks * 32) return;
+  const int64_t b = i >> 5;
+  const int e = (int)(i & 31);
+  const uint8_t* blk = w + b * 18;
+  const float d = h2f(*reinterpret_cast<const unsigned short*>(blk));
+  const int byte = blk[2 + (e & 15)];
+  const int n = e < 16 ? (byte & 15) : (byte >> 4);
+  out[i] = d * (float)(n - 8);
+}
+__global__ void k_dequant_q6k(const uint8_t* __restrict__ w, float* __restrict__ out, int64_t nblocks) {
+  pdl_wait();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nblocks * 256) return;
+  out[i] = q6k_elem(w + (i >> 8) * 210, (int)(i & 255));
+}
+
+extern "C" {
+E4B_API int e4b_dequant_q40(e4b_ctx* c, const uint8_t* w, float* out, int64_t nblocks) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, w && out && nblocks >= 0, "dequant_q40: bad args");
+  const int64_t n = nblocks * 32;
+  return e4b_launch(c, "dequant_q40", k_dequant_q40, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, w, out,
+                    nblocks);
+}
+E4B_API int e4b_dequant_q6k(e4b_ctx* c, const uint8_t* w, float* out, int64_t nblocks) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, w && out && nblocks >= 0, "dequant_q6k: bad args");
+  const int64_t n = nblocks * 256;
+  return e4b_launch(c, "dequant_q6k", k_dequant_q6k, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, w, out,
+                    nblocks);
+}
+}

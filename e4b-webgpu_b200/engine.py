@@ -1,0 +1,336 @@
+"""Per-token decode engine (host side).
+
+Mirrors the reference engines' public surface -- `loadEngineA4B()` /
+`loadEngine()` returning {step, decodeChunk, generateFast, argmaxFast,
+readHidden, ...} (src/engine-a4b.js:75-857, src/engine.js:10-485) -- on top of
+the C-ABI kernels:
+
+  load     GGUF -> config from kv (src/engine-a4b.js:100-116) -> every q4_0 /
+           q6_K tensor uploaded UNCHANGED; same-IN linears (q|k|v, gate|up) are
+           placed back to back in one allocation (byte concatenation, no repack).
+  encode   one token's operator sequence (src/engine-a4b.js:424-463, 683-693 for
+           "moe"; src/engine.js:282-337 for "dense" with q4_0 / q6_K weights).
+  plan     the token sequence recorded once as a CUDA graph and replayed
+           (src/engine-a4b.js:800-818); the token id, positions and the greedy
+           token ring advance on the device (kernels/feedtok.wgsl), so a decode
+           chunk is `count` graph launches with no host work in between.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from types import SimpleNamespace
+
+import numpy as np
+
+from . import gguf, ops
+from .config import ModelConfig
+from .device import Device
+
+F32 = np.float32
+RING_CAP = 16384        # greedy-token ring (src/engine-a4b.js:250 uses 1024)
+ARGMAX_PARTS = 256
+
+
+class Engine:
+    def __init__(self, src, device: int | Device = 0, *, chunk: int = 64, record: bool = False):
+        self.g = gguf.open_gguf(src)
+        self.cfg = ModelConfig.from_kv(self.g.kv)
+        self.dev = device if isinstance(device, Device) else Device(device)
+        self.own_dev = not isinstance(device, Device)
+        self.chunk = chunk
+        self.record = record
+        self.plan = None
+        self.weight_bytes = 0
+        self._load_weights()
+        self._alloc_activations()
+
+    # ------------------------------------------------------------ loading
+    def _raw(self, name: str):
+        t = self.g.fetch(name)
+        self.weight_bytes += t.nbytes
+        return self.dev.upload(t, name)
+
+    def _cat(self, names):
+        """Upload same-IN linears back to back (rows concatenate in memory)."""
+        parts = [self.g.fetch(n) for n in names]
+        total = sum(p.nbytes for p in parts)
+        buf = self.dev.alloc(total, "+".join(names), zero=False)
+        off = 0
+        for p in parts:
+            self.dev.write(buf, p, off)
+            off += p.nbytes
+        self.weight_bytes += total
+        return buf
+
+    def _f32(self, name: str, scale: float | None = None):
+        a = self.g.f32(name)
+        if scale is not None:   # host fold, like the reference's router-scale fold (src/engine-a4b.js:174-179)
+            a = (a.astype(np.float64) * scale).astype(F32)
+        return self.dev.upload(np.ascontiguousarray(a, dtype=F32), name)
+
+    def _load_weights(self):
+        c = self.cfg
+        H = c.hidden
+        self.emb = self._raw("token_embd.weight")
+        self.out_norm = self._f32("output_norm.weight")
+        if c.ple_dim:
+            self.ple_table = self._raw("per_layer_token_embd.weight")
+            self.ple_proj_w = self._raw("per_layer_model_proj.weight")
+            self.ple_norm = self._f32("per_layer_proj_norm.weight")
+        self.layers = []
+        for l in range(c.layers):
+            p = f"blk.{l}."
+            L = SimpleNamespace(i=l, sliding=c.is_sliding(l), keqv=c.keqv(l))
+            L.attn_norm = self._f32(p + "attn_norm.weight")
+            L.qkv = self._cat([p + "attn_q.weight", p + "attn_k.weight"] + ([] if L.keqv else [p + "attn_v.weight"]))
+            L.qkv_rows = c.qkv_rows(l)
+            L.q_norm = self._f32(p + "attn_q_norm.weight")
+            L.k_norm = self._f32(p + "attn_k_norm.weight")
+            L.o = self._raw(p + "attn_output.weight")
+            L.post_attn = self._f32(p + "post_attention_norm.weight")
+            L.ffn_norm = self._f32(p + "ffn_norm.weight")
+            L.gu = self._cat([p + "ffn_gate.weight", p + "ffn_up.weight"])
+            L.down = self._raw(p + "ffn_down.weight")
+            L.post_ffw = self._f32(p + "post_ffw_norm.weight")
+            L.scale = float(self.g.f32(p + "layer_output_scale.weight")[0])
+            if c.ple_dim:
+                L.inp_gate = self._raw(p + "inp_gate.weight")
+                L.proj = self._raw(p + "proj.weight")
+                L.post_norm = self._f32(p + "post_norm.weight")
+            if c.moe:
+                L.post_ffw1 = self._f32(p + "post_ffw_norm_1.weight")
+                L.post_ffw2 = self._f32(p + "post_ffw_norm_2.weight")
+                L.pre_ffw2 = self._f32(p + "pre_ffw_norm_2.weight")
+                L.router_s = self._f32(p + "ffn_gate_inp.scale", 1.0 / math.sqrt(H))
+                L.wr = self._f32(p + "ffn_gate_inp.weight")
+                L.pes = self._f32(p + "ffn_down_exps.scale")
+                L.gu_exps = self._raw(p + "ffn_gate_up_exps.weight")
+                L.down_exps = self._raw(p + "ffn_down_exps.weight")
+            L.angles = c.rope_angles(l)
+            L.theta = c.theta(l)
+            L.ring = c.ring(l)
+            L.slots = c.kv_slots(l)
+            L.cachemode = 1 if L.sliding else 2
+            kvb = L.slots * c.kv_heads * c.head_dim * 2
+            L.kc = self.dev.alloc(kvb, f"kcache{l}")
+            L.vc = self.dev.alloc(kvb, f"vcache{l}")
+            L.max_chunks = (L.slots + self.chunk - 1) // self.chunk
+            self.layers.append(L)
+
+    def _alloc_activations(self):
+        c, d = self.cfg, self.dev
+        H, FF, QD = c.hidden, c.ff, c.q_dim
+        maxrows = max(c.qkv_rows(l) for l in range(c.layers))
+        maxch = max(L.max_chunks for L in self.layers)
+        A = SimpleNamespace()
+        A.params = d.alloc(32, "params")
+        A.hidden = d.alloc(H * 4, "hidden")
+        A.hidden_b = d.alloc(H * 4, "hiddenB")
+        A.normed = d.alloc(H * 2, "normed")
+        A.qkv = d.alloc(maxrows * 4, "qkv")
+        A.q = d.alloc(QD * 4, "qPrep")
+        A.attn = d.alloc(QD * 2, "attnOut")
+        A.part_o = d.alloc(c.q_heads * maxch * c.head_dim * 4, "partO")
+        A.part_ml = d.alloc(c.q_heads * maxch * 2 * 4, "partML")
+        A.tmp = d.alloc(H * 4, "tmp")
+        A.geglu = d.alloc(FF * 2, "geglu")
+        A.xf = d.alloc(H * 4, "xfinal")
+        A.logits = d.alloc(c.vocab * 4, "logits")
+        A.amax_part = d.alloc(ARGMAX_PARTS * 8, "amaxPart")
+        A.amax = d.alloc(16, "amax")
+        A.ring = d.alloc(RING_CAP * 4, "tokRing")
+        if c.ple_dim:
+            A.ple_proj = d.alloc(c.layers * c.ple_dim * 4, "pleProj")
+            A.ple_in = d.alloc(c.layers * c.ple_dim * 4, "pleIn")
+            A.hraw = d.alloc(H * 2, "hraw")
+            A.ple_g = d.alloc(c.ple_dim * 2, "pleGate")
+        if c.moe:
+            A.router_in = d.alloc(H * 4, "routerIn")
+            A.moe_in = d.alloc(H * 2, "moeIn")
+            A.topk_idx = d.alloc(c.topk * 4, "topkIdx")
+            A.topk_w = d.alloc(c.topk * 4, "topkW")
+            A.geglu_slots = d.alloc(c.topk * c.expert_ff * 2, "gegluSlots")
+            A.moe_out = d.alloc(H * 4, "moeOut")
+        if self.record:
+            A.dump = d.alloc(c.layers * H * 4, "hiddenDump")
+        self.A = A
+        # pinned per-step parameter slots (host -> device copies stay async)
+        self.host_params_n = 8192
+        p = ctypes.c_void_p()
+        d.call("e4b_host_alloc", ctypes.c_size_t(self.host_params_n * 32), ctypes.byref(p))
+        self.host_params = np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint32)),
+                                                 shape=(self.host_params_n, 8))
+        self._host_params_ptr = p.value
+        self._hp_next = 0
+        p2 = ctypes.c_void_p()
+        d.call("e4b_host_alloc", ctypes.c_size_t(64), ctypes.byref(p2))
+        self.host_tok = np.ctypeslib.as_array(ctypes.cast(p2, ctypes.POINTER(ctypes.c_uint32)), shape=(16,))
+        self._host_tok_ptr = p2.value
+
+    # ------------------------------------------------------------ one token
+    def encode_forward(self):
+        """Enqueue one token (src/engine-a4b.js:683-693)."""
+        c, d, A = self.cfg, self.dev, self.A
+        H, V = c.hidden, c.vocab
+        ops.q6k_embed(d, self.emb, A.params, None, A.hidden, N=H, ROWS=V, MULT=float(F32(math.sqrt(H))))
+        if c.ple_dim:
+            L, PD = c.layers, c.ple_dim
+            ops.q40mv(d, A.hidden, self.ple_proj_w, None, A.ple_proj, IN=H, OUT=L * PD, XF16=0)
+            ops.pleprep(d, self.ple_table, A.params, None, A.ple_proj, self.ple_norm, A.ple_in, PD=PD, LAYERS=L,
+                        ROWS=V, MULT=float(F32(math.sqrt(PD))), PROJ_SCALE=float(F32(1.0 / math.sqrt(H))), EPS=c.eps)
+        ops.rmsnorm(d, A.hidden, self.layers[0].attn_norm, None, None, A.normed, DIM=H, EPS=c.eps, F16OUT=1)
+        for L in self.layers:
+            self._encode_attention(L)
+            if c.moe:
+                self._encode_moe_ffn(L)
+            else:
+                self._encode_dense_ffn(L)
+            if self.record:
+                d.call("e4b_copy", A.dump.at(L.i * H * 4), A.hidden.ptr, ctypes.c_size_t(H * 4))
+        ops.rmsnorm(d, A.hidden, self.out_norm, A.xf, None, None, DIM=H, EPS=c.eps, F16OUT=0)
+        ops.q6k_lmhead(d, self.emb, A.xf, A.logits, N=H, OUT=V, SOFTCAP=c.softcap)
+        ops.argmax(d, A.logits, A.amax_part, A.amax, N=V, PARTS=ARGMAX_PARTS)
+        ops.feedtok(d, A.amax, A.params, A.ring, RING_CAP=RING_CAP)
+
+    def _encode_attention(self, L):
+        c, d, A = self.cfg, self.dev, self.A
+        H = c.hidden
+        ops.q40mv(d, A.normed, L.qkv, None, A.qkv, IN=H, OUT=L.qkv_rows, XF16=1)
+        ops.headprep(d, A.qkv, L.q_norm, L.k_norm, A.params, L.kc, L.vc, A.q, QH=c.q_heads, KVH=c.kv_heads,
+                     HEAD_DIM=c.head_dim, ROPE_ANGLES=L.angles, THETA=L.theta, EPS=c.eps, KEQV=int(L.keqv),
+                     CACHEMODE=L.cachemode, RING=L.ring, SLOTS=L.slots)
+        ops.attsplit(d, A.q, L.kc, L.vc, A.params, A.part_o, A.part_ml, Q_HEADS=c.q_heads, KV_HEADS=c.kv_heads,
+                     HEAD_DIM=c.head_dim, WINDOW=c.window if L.sliding else 0, CACHEMODE=L.cachemode, RING=L.ring,
+                     CS=self.chunk, CHUNKS=L.max_chunks)
+        ops.attcomb(d, A.part_o, A.part_ml, A.attn, None, None, Q_HEADS=c.q_heads, HEAD_DIM=c.head_dim,
+                    CHUNKS=L.max_chunks)
+        ops.q40mv(d, A.attn, L.o, None, A.tmp, IN=c.q_dim, OUT=H, XF16=1)
+
+    def _next_norm(self, L):
+        return self.layers[L.i + 1].attn_norm if L.i + 1 < self.cfg.layers else None
+
+    def _encode_dense_ffn(self, L):
+        """src/engine.js:308-322 (post-attn residual, pre-FFN norm, GeGLU FFN, PLE block)."""
+        c, d, A = self.cfg, self.dev, self.A
+        H, FF = c.hidden, c.ff
+        ops.rmsaccn(d, A.tmp, L.post_attn, A.hidden, L.ffn_norm, A.normed, DIM=H, EPS=c.eps, MUL=1.0, NORM2=1)
+        ops.q40gu(d, None, None, None, None, A.normed, L.gu, A.geglu, IN=H, FF=0, FF2=FF, K=0)
+        ops.q40mv(d, A.geglu, L.down, None, A.tmp, IN=FF, OUT=H, XF16=1)
+        nxt = self._next_norm(L)
+        if c.ple_dim:
+            PD = c.ple_dim
+            ops.rmsaccn(d, A.tmp, L.post_ffw, A.hidden, None, A.hraw, DIM=H, EPS=c.eps, MUL=1.0, NORM2=0)
+            ops.plegatemv(d, A.hraw, L.inp_gate, A.ple_in, A.ple_g, IN=H, OUT=PD, OFF=L.i * PD)
+            ops.q40mv(d, A.ple_g, L.proj, None, A.tmp, IN=PD, OUT=H, XF16=1)
+            last_w = L.post_norm
+        else:
+            last_w = L.post_ffw
+        if nxt is not None:
+            ops.rmsaccn(d, A.tmp, last_w, A.hidden, nxt, A.normed, DIM=H, EPS=c.eps, MUL=L.scale, NORM2=1)
+        else:
+            ops.rmsacc(d, A.tmp, last_w, A.hidden, DIM=H, EPS=c.eps, MUL=L.scale)
+
+    def _encode_moe_ffn(self, L):
+        """src/engine-a4b.js:437-462."""
+        c, d, A = self.cfg, self.dev, self.A
+        H, FF, EF, K = c.hidden, c.ff, c.expert_ff, c.topk
+        ops.rmsacc3(d, A.tmp, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed, A.router_in,
+                    A.moe_in, A.hidden_b, DIM=H, EPS=c.eps)
+        ops.routertop(d, A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H=H, E=c.experts, K=K)
+        ops.q40gu(d, A.moe_in, L.gu_exps, A.topk_idx, A.geglu_slots, A.normed, L.gu, A.geglu, IN=H, FF=EF, FF2=FF,
+                  K=K)
+        ops.q40mv(d, A.geglu, L.down, None, A.tmp, IN=FF, OUT=H, XF16=1)
+        ops.q40moedown(d, A.geglu_slots, L.down_exps, A.topk_idx, A.topk_w, A.moe_out, IN=EF, OUT=H, K=K)
+        nxt = self._next_norm(L)
+        ops.a4btail(d, A.tmp, L.post_ffw1, A.moe_out, L.post_ffw2, L.post_ffw, A.hidden_b,
+                    nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H=H, EPS=c.eps, MUL=L.scale,
+                    NEXT=int(nxt is not None))
+
+    # ------------------------------------------------------------ plan
+    def build_plan(self):
+        """Record encode_forward() once as a replayable CUDA graph."""
+        if self.plan is None:
+            n0 = self.dev.kernel_launches
+            self.dev.call("e4b_plan_begin")
+            try:
+                self.encode_forward()
+            finally:
+                p = ctypes.c_int()
+                self.dev.call("e4b_plan_end", ctypes.byref(p))
+            self.plan = p.value
+            self.kernels_per_token = self.dev.kernel_launches - n0
+        return self.plan
+
+    def run_token(self, count: int = 1):
+        """Enqueue `count` tokens (graph replays)."""
+        self.dev.call("e4b_plan_launch", self.build_plan(), count)
+
+    # ------------------------------------------------------------ host API
+    def set_params(self, token: int, pos: int, ring_index: int | None = None, sync_slot: bool = False):
+        """Queue [pos, pos+1, token, 0, kvCount, kvCount+1, ringIndex, 0] (src/engine-a4b.js:697-698)."""
+        if self._hp_next >= self.host_params_n:
+            self.dev.sync()
+            self._hp_next = 0
+        i = self._hp_next
+        self._hp_next += 1
+        ri = pos if ring_index is None else ring_index
+        self.host_params[i] = (pos, pos + 1, token, 0, pos, pos + 1, ri, 0)
+        self.dev.call("e4b_upload_async", self.A.params.ptr, ctypes.c_void_p(self._host_params_ptr + i * 32),
+                      ctypes.c_size_t(32))
+
+    def step(self, token: int, pos: int):
+        """One token at `pos` (src/engine-a4b.js:695-705); the result stays on the device."""
+        self.set_params(token, pos)
+        self.run_token(1)
+
+    def argmax_fast(self) -> int:
+        """src/engine-a4b.js:781-784"""
+        return int(self.dev.read(self.A.amax, np.uint32, 1)[0])
+
+    def decode_chunk(self, count: int):
+        """`count` greedy tokens continuing from the device-side parameters
+        (src/engine-a4b.js:786-823)."""
+        self.run_token(count)
+
+    def read_ring(self, start: int, n: int) -> np.ndarray:
+        return self.dev.read(self.A.ring, np.uint32, n, offset=start * 4)
+
+    def read_hidden(self) -> np.ndarray:
+        """src/engine-a4b.js:850-852"""
+        return self.dev.read(self.A.hidden, F32, self.cfg.hidden)
+
+    def read_dump(self) -> np.ndarray:
+        assert self.record
+        return self.dev.read(self.A.dump, F32, self.cfg.layers * self.cfg.hidden).reshape(self.cfg.layers, -1)
+
+    def read_logits(self) -> np.ndarray:
+        return self.dev.read(self.A.logits, F32, self.cfg.vocab)
+
+    def prefill(self, prompt):
+        """Token-by-token prefill (the reference's generateFast path, src/engine-a4b.js:828)."""
+        if self._hp_next:
+            self.dev.sync()          # pinned parameter slots are reused from the start
+            self._hp_next = 0
+        for pos, t in enumerate(prompt):
+            self.step(int(t), pos)
+
+    def generate(self, prompt, n_new: int, eos=None):
+        """generateFast (src/engine-a4b.js:826-847): prefill, then greedy decode
+        with the token id fed back on the device; returns n_new ids (cut at eos)."""
+        P = len(prompt)
+        assert P >= 1 and P + n_new <= RING_CAP
+        self.prefill(prompt)
+        if n_new > 1:
+            self.decode_chunk(n_new - 1)
+        self.dev.sync()
+        ids = [int(x) for x in self.read_ring(P - 1, n_new)]
+        if eos:
+            for i, t in enumerate(ids):
+                if t in eos:
+                    return ids[:i + 1]
+        return ids
+
+    def close(self):
+        if self.own_dev:
+            self.dev.close()

@@ -1,0 +1,224 @@
+/*
+ * e4b_b200.h -- C ABI of the B200 (sm_100a) per-token decode path.
+ *
+ * Drop-in boundary for the reference's WebGPU operator API: where the reference
+ * compiles kernels/<op>.wgsl with ${NAME} substitution and dispatches it with an
+ * ordered list of storage buffers (src/gpu.js:67-84 `Kernels.pipeline`,
+ * src/gpu.js:95-108 / src/engine-a4b.js:401-420 `run`), this library exports one
+ * C function per operator.  Device buffers are passed as plain pointers in the
+ * reference's binding order; the former ${} compile-time parameters become int /
+ * float arguments.  Weights are the GGUF q4_0 (18 B / 32 weights) and q6_K
+ * (210 B / 256 weights) blocks exactly as stored in the file.
+ *
+ * Conventions
+ *   - Every function returns E4B_OK (0) or a negative E4B_E* code; the message
+ *     of the last failure on a context is e4b_last_error(ctx).
+ *   - Kernels are enqueued on the context's stream and never allocate; the
+ *     caller owns all device memory (e4b_alloc / e4b_free).  Scratch buffers an
+ *     operator needs (split-KV partials, argmax partials) are caller-provided.
+ *   - A context is bound to one device and is not thread-safe.
+ *   - f16 buffers are IEEE binary16 stored as uint16_t.
+ *   - `params` is the reference's per-token parameter block (8 x u32,
+ *     src/engine-a4b.js:697-698): [0]=pos [1]=pos+1 [2]=token [3]=0
+ *     [4]=kvCount (global-layer slot) [5]=kvCount+1 [6]=token-ring index [7]=0.
+ */
+#ifndef E4B_B200_H
+#define E4B_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define E4B_API __attribute__((visibility("default")))
+#else
+#define E4B_API
+#endif
+
+enum {
+  E4B_OK = 0,
+  E4B_EINVAL = -1,    /* bad argument (null pointer, size not a block multiple, ...) */
+  E4B_ECUDA = -2,     /* CUDA runtime error */
+  E4B_ETIMEOUT = -3,  /* a bounded device-side wait gave up (device status word) */
+  E4B_ENCCL = -4,     /* NCCL error */
+  E4B_ENOMEM = -5,    /* allocation failed */
+  E4B_EDEVICE = -6    /* device-side check failed (index out of range, ...) */
+};
+
+typedef struct e4b_ctx e4b_ctx;
+
+/* ------------------------------------------------------------------ runtime */
+/* Replaces initDevice (src/gpu.js:4-24). */
+E4B_API int e4b_create(int device, e4b_ctx** out);
+E4B_API int e4b_destroy(e4b_ctx* ctx);
+E4B_API const char* e4b_last_error(const e4b_ctx* ctx);
+E4B_API int e4b_device_info(e4b_ctx* ctx, int* sm_count, int* cc_major, int* cc_minor, size_t* total_mem);
+/* Buffers: replaces alloc / upload / readback (src/gpu.js:26-50). */
+E4B_API int e4b_alloc(e4b_ctx* ctx, size_t bytes, void** out);
+E4B_API int e4b_free(e4b_ctx* ctx, void* ptr);
+E4B_API int e4b_host_alloc(e4b_ctx* ctx, size_t bytes, void** out); /* pinned host memory */
+E4B_API int e4b_host_free(e4b_ctx* ctx, void* ptr);
+E4B_API int e4b_upload(e4b_ctx* ctx, void* dst, const void* src, size_t bytes);   /* synchronous */
+E4B_API int e4b_download(e4b_ctx* ctx, void* dst, const void* src, size_t bytes); /* synchronous */
+E4B_API int e4b_upload_async(e4b_ctx* ctx, void* dst, const void* src, size_t bytes);
+E4B_API int e4b_download_async(e4b_ctx* ctx, void* dst, const void* src, size_t bytes);
+E4B_API int e4b_memset(e4b_ctx* ctx, void* dst, int value, size_t bytes);           /* stream-ordered */
+E4B_API int e4b_copy(e4b_ctx* ctx, void* dst, const void* src, size_t bytes);        /* device to device, stream-ordered */
+E4B_API int e4b_sync(e4b_ctx* ctx);
+/* Timing: events recorded on the context stream (slots 0..63). */
+E4B_API int e4b_event_record(e4b_ctx* ctx, int slot);
+E4B_API int e4b_event_elapsed(e4b_ctx* ctx, int slot_a, int slot_b, float* ms);
+/* Programmatic dependent launch between consecutive kernels (default on). */
+E4B_API int e4b_set_pdl(e4b_ctx* ctx, int enable);
+/* Device status word: nonzero after a device-side check or bounded wait failed;
+ * reading it resets it to zero. */
+E4B_API int e4b_device_status(e4b_ctx* ctx, uint32_t* status);
+
+/* Plan = one recorded per-token dispatch sequence, replayed as a CUDA graph.
+ * Replaces the token-plan record/replay of src/engine-a4b.js:800-818. */
+E4B_API int e4b_plan_begin(e4b_ctx* ctx);
+E4B_API int e4b_plan_end(e4b_ctx* ctx, int* plan);
+E4B_API int e4b_plan_launch(e4b_ctx* ctx, int plan, int count);
+E4B_API int e4b_plan_destroy(e4b_ctx* ctx, int plan);
+
+/* ----------------------------------------------------------- dequantisation */
+/* Bit-exact block decoders (for parity checks of the in-kernel decode).
+ * q4_0: scripts/ternarize_a4b.py:80-87; q6_K: kernels/q6k.wgsl:44-68. */
+E4B_API int e4b_dequant_q40(e4b_ctx* ctx, const uint8_t* w, float* out, int64_t nblocks);
+E4B_API int e4b_dequant_q6k(e4b_ctx* ctx, const uint8_t* w, float* out, int64_t nblocks);
+
+/* --------------------------------------------------------- q6_K embed / head */
+/* kernels/q6k.wgsl MODE 0 (:37-73): y[b*N+i] = ((d*sc)*(q-32))*mult of row
+ * tok[b] (batch > 0), else of row tok[0] (toksrc=1) or params[2] (toksrc=0).
+ * A row >= rows sets the device status word and writes zeros. */
+E4B_API int e4b_q6k_embed(e4b_ctx* ctx, const uint8_t* w, const uint32_t* params, const uint32_t* tok,
+                          float* y, int N, int rows, float mult, int toksrc, int batch);
+/* kernels/q6k.wgsl MODE 1 (:75-131): y[o] = softcap(sum d*sc*(q-32)*x), OUT rows
+ * of N; softcap = 0 disables.  batch rows of x / y (stride N / OUT). */
+E4B_API int e4b_q6k_lmhead(e4b_ctx* ctx, const uint8_t* w, const float* x, float* y, int N, int OUT,
+                           float softcap, int batch);
+
+/* ------------------------------------------------------------ norms / tails */
+/* kernels/rmsnorm.wgsl:13-51.  rows x dim; y (f32) or yh (f16) per f16out;
+ * sums[row] = sum(y) if sumout. */
+E4B_API int e4b_rmsnorm(e4b_ctx* ctx, const float* x, const float* w, float* y, float* sums, uint16_t* yh,
+                        int dim, int rows, float eps, int with_scale, int sumout, int f16out);
+/* kernels/rmsacc.wgsl:10-26: hidden = (hidden + rms(x)*w) * mul. */
+E4B_API int e4b_rmsacc(e4b_ctx* ctx, const float* x, const float* w, float* hidden, int dim, float eps,
+                       float mul);
+/* kernels/rmsaccsrq.wgsl:30-76 without its int8 activation quantisation:
+ * hidden = (hidden + rms(t)*w1) * mul; yh = f16(rms(hidden)*w2) (norm2=1) or
+ * f16(hidden) (norm2=0). */
+E4B_API int e4b_rmsaccn(e4b_ctx* ctx, const float* t, const float* w1, float* hidden, const float* w2,
+                        uint16_t* yh, int dim, float eps, float mul, int norm2);
+/* kernels/rmsacc3.wgsl:27-53 (rows = batch). */
+E4B_API int e4b_rmsacc3(e4b_ctx* ctx, const float* t, const float* w_acc, const float* w1, const float* w2,
+                        const float* w3, const float* h_in, uint16_t* y1, float* y2, uint16_t* y3,
+                        float* h_out, int dim, float eps, int rows);
+/* kernels/a4btail.wgsl:26-71 (rows = batch). */
+E4B_API int e4b_a4btail(e4b_ctx* ctx, const float* t1, const float* w1, const float* m, const float* w2,
+                        const float* wp, const float* h_in, const float* w_next, uint16_t* y_next,
+                        float* h_out, int H, float eps, float mul, int next, int rows);
+
+/* ------------------------------------------------------------ q4_0 GEMVs */
+/* kernels/q40mv.wgsl:56-89: y[z*OUT+o] = sum_b d_b sum_i (n_i-8) x_i.
+ * x is f32 (x_f16=0) or f16 (x_f16=1).  expert=1: weights of expert topk[z]
+ * (stride OUT*IN/32 blocks); xslot=1: x row z (stride IN); nz = slots (1 if
+ * neither).  batch > 1: rows of x / y per token (stride IN / nz*OUT). */
+E4B_API int e4b_q40mv(e4b_ctx* ctx, const void* x, const uint8_t* w, const uint32_t* topk, float* y,
+                      int IN, int OUT, int expert, int xslot, int x_f16, int nz, int batch);
+/* kernels/q40gu.wgsl:62-119 (EXPERT=2 merged grid): dense rows [gate FF2 | up FF2]
+ * of w2 on x2 -> yh2 = f16(gelu(g)*u) [FF2]; expert slot k: rows of expert
+ * topk[k] of w ([E][2*FF][IN]) on x -> yh[k*FF ..]; w2 == NULL skips the dense
+ * part, K == 0 skips the experts.  batch rows (token stride IN in x/x2, FF2 in
+ * yh2, K*FF in yh, K in topk). */
+E4B_API int e4b_q40gu(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* topk, uint16_t* yh,
+                      const uint16_t* x2, const uint8_t* w2, uint16_t* yh2, int IN, int FF, int FF2, int K,
+                      int batch);
+/* kernels/q40moedown.wgsl:42-75: y[o] = sum_k tkw[k] * (W_topk[k] x_k)[o],
+ * x f16 [K][IN], W [E][OUT][IN]. */
+E4B_API int e4b_q40moedown(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* topk,
+                           const float* tkw, float* y, int IN, int OUT, int K, int batch);
+/* kernels/moecomb.wgsl:6-15: y[i] = sum_k topkW[k] * slots[k*H+i]. */
+E4B_API int e4b_moecomb(e4b_ctx* ctx, const float* slots, const float* topk_w, float* y, int H, int K);
+
+/* ------------------------------------------------------------ router */
+/* kernels/routertop.wgsl:19-71: scores = Wr[E][H] . x (f32), softmax, K-way
+ * iterative argmax (ties -> lowest index), renormalise, x pes[e].  One token
+ * per row of x (batch rows). */
+E4B_API int e4b_routertop(e4b_ctx* ctx, const float* x, const float* wr, const float* pes, uint32_t* topk_idx,
+                          float* topk_w, int H, int E, int K, int batch);
+/* kernels/router.wgsl:16-63: scale-less RMS of h, x scale x H^-0.5, then as routertop. */
+E4B_API int e4b_router(e4b_ctx* ctx, const float* h, const float* scale, const float* wr, const float* pes,
+                       uint32_t* topk_idx, float* topk_w, int H, int E, int K, float eps);
+/* kernels/top8.wgsl:8-30 on precomputed scores. */
+E4B_API int e4b_top8(e4b_ctx* ctx, const float* scores, const float* pes, uint32_t* topk_idx, float* topk_w,
+                     int E, int K);
+
+/* ------------------------------------------------------------ attention */
+/* kernels/headprep.wgsl:19-87: q/k per-head RMSNorm (q_norm/k_norm) + RoPE on
+ * pairs (p, p+hd/2) for p < rope_angles; v scale-less RMSNorm (v = k slice when
+ * keqv); K/V f16 written at slot pos % ring (cachemode 1) or params[4]+b
+ * (cachemode 2); cache layout [cache_slots][KVH][HD].  batch tokens at pos
+ * params[0]+b.  A slot >= cache_slots sets the device status word, no write. */
+E4B_API int e4b_headprep(e4b_ctx* ctx, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
+                         uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
+                         int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
+                         int cache_slots, int batch);
+/* kernels/rope.wgsl:8-27 (in place, pos = params[0]). */
+E4B_API int e4b_rope(e4b_ctx* ctx, float* x, const uint32_t* params, int heads, int HD, int rope_angles,
+                     float theta);
+/* kernels/kvwrite.wgsl:5-10: dst[params[0]*N + i] = src[i] (f32). */
+E4B_API int e4b_kvwrite(e4b_ctx* ctx, const float* src, const uint32_t* params, float* dst, int N);
+/* kernels/attsplit.wgsl:16-76 (flash-decode phase A) over the f16 cache.
+ * Chunk c of `chunk` positions of head h -> part_o[(h*max_chunks+c)*HD] (unnormalised)
+ * and part_ml[2*(h*max_chunks+c)] = (m, l); empty chunks write (-inf, 0).
+ * cachemode 1: sliding ring (ring slots, window), query pos params[0];
+ * cachemode 2: linear slots [0, params[5]); cachemode 0: linear [0, params[1]),
+ * window applied if > 0.  scale multiplies q.k (the Gemma path uses 1.0). */
+E4B_API int e4b_attsplit(e4b_ctx* ctx, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                         const uint32_t* params, float* part_o, float* part_ml, int QH, int KVH, int HD,
+                         int window, int cachemode, int ring, int chunk, int max_chunks, float scale);
+/* kernels/attcomb.wgsl:10-36 (phase B): LSE-merge of the chunk partials ->
+ * out_h (f16, may be NULL), out_f (f32, may be NULL), lse (f32, may be NULL). */
+E4B_API int e4b_attcomb(e4b_ctx* ctx, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
+                        float* lse, int QH, int HD, int max_chunks);
+
+/* ------------------------------------------------------------ GeGLU */
+/* kernels/geglumul.wgsl:5-11: y = gelu_tanh(a) * b (f32). */
+E4B_API int e4b_geglumul(e4b_ctx* ctx, const float* a, const float* b, float* y, int N);
+/* kernels/geglusl.wgsl:5-13: out[k*FF+i] = gelu(gu[k*2FF+i]) * gu[k*2FF+FF+i] (f32). */
+E4B_API int e4b_geglusl(e4b_ctx* ctx, const float* gu, float* out, int FF, int K);
+/* kernels/geglub.wgsl:9-19: yh[r*N+j] = f16(gelu(gu[r*2N+j]) * gu[r*2N+N+j]), rows r. */
+E4B_API int e4b_geglub(e4b_ctx* ctx, const float* gu, uint16_t* yh, int N, int rows);
+
+/* ------------------------------------------------------------ PLE */
+/* kernels/pleprep.wgsl:15-46 with a q6_K table: for layer block b,
+ * pleIn[b*PD+i] = (rms(proj_b*proj_scale)[i]*normW[i] + row_b[i]*mult) * sqrt(1/2),
+ * row = q6_K row tok[0] (toksrc=1) or params[2] of the [LAYERS*PD]-wide table. */
+E4B_API int e4b_pleprep(e4b_ctx* ctx, const uint8_t* table, const uint32_t* params, const uint32_t* tok,
+                        const float* proj, const float* norm_w, float* ple_in, int PD, int LAYERS, int rows,
+                        float mult, float proj_scale, float eps, int toksrc);
+/* kernels/plegatemv.wgsl:20-60 with q4_0 weights and f16 activations (no int8
+ * activation quantisation): y[o] = f16(gelu_tanh(W x)[o] * ple[off+o]). */
+E4B_API int e4b_plegatemv(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const float* ple, uint16_t* y,
+                          int IN, int OUT, int off);
+/* kernels/plemul.wgsl:6-12: y[i] = gelu_tanh(a[i]) * ple[off+i]. */
+E4B_API int e4b_plemul(e4b_ctx* ctx, const float* a, const float* ple, float* y, int N, int off);
+
+/* ------------------------------------------------------------ argmax / feed */
+/* kernels/argmax2.wgsl:8-48 (both stages): out[0] = index of the largest x (ties
+ * -> lowest index), out[1] = its f32 bits.  part: scratch of 2*parts u32. */
+E4B_API int e4b_argmax(e4b_ctx* ctx, const float* x, uint32_t* part, uint32_t* out, int N, int parts);
+/* kernels/feedtok.wgsl:5-6 plus the token-ring copy (src/engine-a4b.js:820) and
+ * the per-token parameter advance (src/engine-a4b.js:793-795), on the device:
+ * ring[params[6] % ring_cap] = amax[0]; params[2] = amax[0]; pos/len/kvCount/index += 1. */
+E4B_API int e4b_feedtok(e4b_ctx* ctx, const uint32_t* amax, uint32_t* params, uint32_t* ring, int ring_cap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* E4B_B200_H */
