@@ -313,6 +313,103 @@ def run_reference(args, rank, world):
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+KERNELS = {
+    # name: (description, rows, IN, kind)   -- weights > 126 MB L2 so every launch streams from HBM
+    "q40gu": ("dense gate|up + GeGLU, E4B layer shape (2048 -> 2x16384), 4 layers of weights", 2 * 16384, 2048, "gu"),
+    "q40down": ("down projection, E4B shape (16384 -> 2048), 8 layers of weights", 2048, 16384, "mv"),
+    "q40qkv": ("qkv projection, E4B shape (2048 -> 3072), 48 layers of weights", 3072, 2048, "mv"),
+    "q40big": ("gate|up + GeGLU, 2048 -> 2x65536 (4x the E4B layer), 2 copies", 2 * 65536, 2048, "gu"),
+}
+
+
+def graph_time(dev, enqueue, reps: int = 5) -> float:
+    """Record enqueue() as a CUDA graph, replay it `reps` times (after one warm-up
+    replay) and return the device time of one replay in microseconds, so host
+    launch overhead is not part of the measurement."""
+    import ctypes
+    dev.call("e4b_plan_begin")
+    try:
+        enqueue()
+    finally:
+        pl = ctypes.c_int()
+        dev.call("e4b_plan_end", ctypes.byref(pl))
+    dev.call("e4b_plan_launch", pl.value, 1)
+    dev.sync()
+    ms = ctypes.c_float()
+    dev.call("e4b_event_record", 0)
+    dev.call("e4b_plan_launch", pl.value, reps)
+    dev.call("e4b_event_record", 1)
+    dev.sync()
+    dev.call("e4b_event_elapsed", 0, 1, ctypes.byref(ms))
+    dev.call("e4b_plan_destroy", pl.value)
+    return ms.value * 1000.0 / reps
+
+
+def run_rmschain(e4b, dev, args):
+    """Launch-to-launch latency floor: a chain of dependent single-CTA RMSNorms."""
+    import ctypes
+    dev.call("e4b_set_pdl", int(args.pdl))
+    H = 2048
+    x = dev.upload(np.random.default_rng(0).standard_normal(H).astype(np.float32))
+    w = dev.upload(np.ones(H, np.float32))
+    y = dev.alloc(H * 4)
+    def chain():
+        for i in range(args.launches):
+            e4b.ops.rmsnorm(dev, x if i % 2 == 0 else y, w, y if i % 2 == 0 else x, None, None, DIM=H)
+    us = graph_time(dev, chain) / args.launches
+    print(json.dumps({"kernel": "rmschain", "pdl": args.pdl, "launches": args.launches,
+                      "us_per_launch": round(us, 3)}))
+    dev.close()
+
+
+def run_kernel(args):
+    """Time one streaming kernel alone: `launches` launches cycling over enough
+    distinct weight copies that the working set exceeds L2."""
+    import ctypes
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    import __graft_entry__
+    __graft_entry__.build()
+    dev = e4b.Device(0)
+    if args.kernel == "rmschain":
+        return run_rmschain(e4b, dev, args)
+    desc, rows, n_in, kind = KERNELS[args.kernel]
+    ws = int(dev.L.e4b_workspace_bytes())
+    wsb = dev.alloc(ws, "workspace")
+    dev.call("e4b_set_workspace", wsb.ptr, ctypes.c_size_t(ws))
+    dev.call("e4b_set_pdl", int(args.pdl))
+    dev.call("e4b_set_option", b"stream_ctas_per_sm", args.ctas_per_sm)
+    dev.call("e4b_set_option", b"stream_stages", args.stages)
+    dev.call("e4b_set_option", b"stream_variant", args.variant)
+    per = rows * n_in // 32 * 18
+    copies = max(2, int(math.ceil(160e6 / per)))
+    w = e4b.synth.quant_q4_0(e4b.synth.normal_f32(rows * n_in, 0, "kernel", 0.02))
+    bufs = [dev.upload(w, f"w{i}") for i in range(copies)]
+    x = dev.upload(np.random.default_rng(0).standard_normal(n_in).astype(np.float16))
+    y = dev.alloc(rows * 4)
+
+    def one(i):
+        b = bufs[i % copies]
+        if kind == "gu":
+            e4b.ops.q40gu(dev, None, None, None, None, x, b, y, IN=n_in, FF=0, FF2=rows // 2, K=0)
+        else:
+            e4b.ops.q40mv(dev, x, b, None, y, IN=n_in, OUT=rows, XF16=1)
+    def loop():
+        for i in range(args.launches):
+            one(i)
+    us = graph_time(dev, loop) / args.launches
+    nbytes = per + n_in * 2 + (rows // 2 * 2 if kind == "gu" else rows * 4)
+    peak, kind_p = peaks()
+    st = dev.status()
+    dev.close()
+    print(json.dumps({"kernel": args.kernel, "desc": desc, "pdl": args.pdl, "ctas_per_sm": args.ctas_per_sm,
+                      "stages": args.stages, "variant": args.variant, "launches": args.launches, "us_per_launch": round(us, 2),
+                      "bytes_per_launch": nbytes, "gbs": round(nbytes / us / 1e3, 1),
+                      "frac": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_source": kind_p,
+                      "weight_copies": copies, "status": st}))
+    if st:
+        raise SystemExit(f"device status {st:#x}")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -323,7 +420,16 @@ def main():
     ap.add_argument("--prefill", type=int, default=512)
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain"], help="time one kernel alone instead of the decode")
+    ap.add_argument("--launches", type=int, default=200)
+    ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1/0)")
+    ap.add_argument("--ctas-per-sm", type=int, default=1)
+    ap.add_argument("--stages", type=int, default=4)
+    ap.add_argument("--variant", type=int, default=0, help="GEMV variant (warps x piece blocks): 0=8x32 1=16x16 2=16x8")
     args = ap.parse_args()
+    if args.kernel:
+        run_kernel(args)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local_rank = dist_env()

@@ -27,6 +27,8 @@ def _arg_type(decl: str):
     decl = " ".join(decl.replace("const ", "").split())
     if "**" in decl:
         return ctypes.POINTER(ctypes.c_void_p)
+    if decl.startswith("char*") or decl.startswith("char *"):
+        return ctypes.c_char_p
     if "*" in decl:
         return ctypes.c_void_p
     base = decl.rsplit(" ", 1)[0] if " " in decl else decl

@@ -21,6 +21,11 @@ struct e4b_ctx {
   bool pdl = true;
   bool capturing = false;
   uint32_t* status = nullptr;       // device status word (bounded waits / checks)
+  void* ws = nullptr;               // caller-provided workspace (split-K partials, counters)
+  size_t ws_bytes = 0;
+  int stream_ctas_per_sm = 1;       // tuning knobs (e4b_set_option)
+  int stream_stages = 4;
+  int stream_variant = 0;           // GEMV warps x piece size: 0 = 8x32, 1 = 16x16, 2 = 16x8
   cudaEvent_t ev[64] = {};
   std::vector<cudaGraphExec_t> plans;
   cudaGraph_t cap_graph = nullptr;

@@ -2,6 +2,7 @@
 // moecomb, plegatemv.  One warp per output row, lanes striding over the row's
 // 18-byte blocks, f32 accumulation, warp-shuffle reduction.
 #include "common.cuh"
+#include "q40_stream.cuh"
 
 namespace {
 
@@ -127,6 +128,8 @@ E4B_API int e4b_q40mv(e4b_ctx* c, const void* x, const uint8_t* w, const uint32_
   E4B_REQUIRE(c, !expert || topk, "q40mv: expert=1 needs topk");
   if (nz < 1) nz = 1;
   if (batch < 1) batch = 1;
+  if (!expert && !xslot && nz == 1 && batch == 1 && c->ws && e4b::q40_stream_supported(w, x, IN, OUT))
+    return e4b::q40_stream(c, w, x, !x_f16, y, nullptr, nullptr, IN, OUT, 0, 0, 0);
   dim3 grid((OUT + kWarps - 1) / kWarps, batch, nz);
   if (x_f16)
     return e4b_launch(c, "q40mv", k_q40mv<uint16_t>, grid, dim3(kWarps * 32), 0, (const uint16_t*)x, w, topk, y,
@@ -146,6 +149,8 @@ E4B_API int e4b_q40gu(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const uin
   if (batch < 1) batch = 1;
   const int nzz = has_dense + K;
   if (nzz == 0) return E4B_OK;
+  if (has_dense && K == 0 && batch == 1 && c->ws && FF2 % 16 == 0 && e4b::q40_stream_supported(w2, x2, IN, FF2))
+    return e4b::q40_stream(c, w2, x2, 0, nullptr, yh2, nullptr, IN, 2 * FF2, 1, FF2, 0);
   const int ffmax = has_dense ? (FF2 > FF ? FF2 : FF) : FF;
   dim3 grid((ffmax + 3) / 4, batch, nzz);
   return e4b_launch(c, "q40gu", k_q40gu, grid, dim3(256), 0, x, w, topk, yh, x2, w2, yh2, IN, FF, FF2, K,
@@ -174,6 +179,8 @@ E4B_API int e4b_plegatemv(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, x && w && ple && y, "plegatemv: null buffer");
   E4B_REQUIRE(c, IN > 0 && IN % 32 == 0 && OUT > 0 && off >= 0, "plegatemv: bad sizes");
+  if (c->ws && e4b::q40_stream_supported(w, x, IN, OUT))
+    return e4b::q40_stream(c, w, x, 0, nullptr, y, ple, IN, OUT, 2, 0, off);
   return e4b_launch(c, "plegatemv", k_plegatemv, dim3((OUT + kWarps - 1) / kWarps), dim3(kWarps * 32), 0, x, w,
                     ple, y, IN, OUT, off);
 }

@@ -1,0 +1,21 @@
+// Internal interface of the streaming q4_0 GEMV (q40_stream.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace e4b {
+
+// Workspace layout shared by the streaming kernels: a counter area that is
+// zero between launches (each split row tile's last CTA resets its counter),
+// followed by split-K partials.
+constexpr size_t kWsMaxTiles = 16384;                       // u32 counters + u64 start masks
+constexpr size_t kWsCounterBytes = kWsMaxTiles * (4 + 8);
+
+// rows: output rows (OUT, or FF for the fused gate|up).
+bool q40_stream_supported(const void* w, const void* x, int IN, int rows);
+// epi 0: y = W x (f32); 1: gate|up rows [0,ff) and [ff,2ff) -> yh = f16(gelu(g)*u);
+// 2: yh = f16(gelu(W x) * ple[off + o]).
+int q40_stream(e4b_ctx* c, const uint8_t* w, const void* x, int x_f32, float* y, uint16_t* yh, const float* ple,
+               int IN, int OUT, int epi, int ff, int off);
+
+}  // namespace e4b

@@ -1,6 +1,8 @@
 // Context, memory, timing, status word and plan (CUDA graph) management.
 // Replaces the reference's WebGPU runtime helpers (src/gpu.js:4-50) and its
 // per-token plan record/replay (src/engine-a4b.js:800-818).
+#include <string.h>
+
 #include "common.cuh"
 
 int e4b_fail(e4b_ctx* c, int code, const char* fmt, ...) {
@@ -137,6 +139,38 @@ E4B_API int e4b_event_elapsed(e4b_ctx* c, int a, int b, float* ms) {
 E4B_API int e4b_set_pdl(e4b_ctx* c, int enable) {
   E4B_CHECK_CTX(c);
   c->pdl = enable != 0;
+  return E4B_OK;
+}
+E4B_API size_t e4b_workspace_bytes(void) { return (size_t)32 << 20; }
+E4B_API int e4b_set_option(e4b_ctx* c, const char* name, int value) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, name, "null option name");
+  if (!strcmp(name, "stream_ctas_per_sm")) {
+    E4B_REQUIRE(c, value >= 1 && value <= 2, "stream_ctas_per_sm must be 1 or 2");
+    c->stream_ctas_per_sm = value;
+  } else if (!strcmp(name, "stream_variant")) {
+    E4B_REQUIRE(c, value >= 0 && value <= 2, "stream_variant must be 0..2");
+    c->stream_variant = value;
+  } else if (!strcmp(name, "stream_stages")) {
+    E4B_REQUIRE(c, value >= 2 && value <= 4, "stream_stages must be 2..4");
+    c->stream_stages = value;
+  } else {
+    return e4b_fail(c, E4B_EINVAL, "unknown option %s", name);
+  }
+  return E4B_OK;
+}
+E4B_API int e4b_set_workspace(e4b_ctx* c, void* ws, size_t bytes) {
+  E4B_CHECK_CTX(c);
+  if (!ws && bytes == 0) {
+    c->ws = nullptr;
+    c->ws_bytes = 0;
+    return E4B_OK;
+  }
+  E4B_REQUIRE(c, ws && bytes >= (size_t)(1 << 20), "workspace must be at least 1 MiB");
+  E4B_CUDA(c, cudaMemsetAsync(ws, 0, bytes, c->stream));
+  E4B_CUDA(c, cudaStreamSynchronize(c->stream));
+  c->ws = ws;
+  c->ws_bytes = bytes;
   return E4B_OK;
 }
 E4B_API int e4b_device_status(e4b_ctx* c, uint32_t* st) {

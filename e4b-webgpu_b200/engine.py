@@ -155,6 +155,9 @@ class Engine:
         if self.record:
             A.dump = d.alloc(c.layers * H * 4, "hiddenDump")
         self.A = A
+        ws = int(d.L.e4b_workspace_bytes())
+        A.ws = d.alloc(ws, "workspace")
+        d.call("e4b_set_workspace", A.ws.ptr, ctypes.c_size_t(ws))
         # pinned per-step parameter slots (host -> device copies stay async)
         self.host_params_n = 8192
         p = ctypes.c_void_p()

@@ -54,8 +54,8 @@ def tensor_bytes(ttype: int, dims) -> int:
     n = 1
     for d in dims:
         n *= int(d)
-    if n % be:
-        raise GGUFError(f"{n} elements is not a whole number of type-{ttype} blocks")
+    if dims and int(dims[0]) % be:
+        raise GGUFError(f"row length {dims[0]} is not a whole number of type-{ttype} blocks ({be})")
     return (n // be) * bb
 
 

@@ -73,6 +73,16 @@ E4B_API int e4b_event_record(e4b_ctx* ctx, int slot);
 E4B_API int e4b_event_elapsed(e4b_ctx* ctx, int slot_a, int slot_b, float* ms);
 /* Programmatic dependent launch between consecutive kernels (default on). */
 E4B_API int e4b_set_pdl(e4b_ctx* ctx, int enable);
+/* Workspace for the streaming GEMVs (split-K partials and arrival counters).
+ * Caller-owned device memory of at least e4b_workspace_bytes(); it is zeroed
+ * here and must not be shared by two contexts.  Ops that need it fail with
+ * E4B_EINVAL until one is set. */
+E4B_API int e4b_set_workspace(e4b_ctx* ctx, void* ws, size_t bytes); /* ws = NULL, bytes = 0 detaches */
+E4B_API size_t e4b_workspace_bytes(void);
+/* Tuning knobs of the streaming kernels: "stream_ctas_per_sm" (1..2, default 1),
+ * "stream_stages" (2..4, default 4), "stream_variant" (GEMV warps per CTA x
+ * blocks per staged piece: 0 = 8 x 32, 1 = 16 x 16, 2 = 16 x 8). */
+E4B_API int e4b_set_option(e4b_ctx* ctx, const char* name, int value);
 /* Device status word: nonzero after a device-side check or bounded wait failed;
  * reading it resets it to zero. */
 E4B_API int e4b_device_status(e4b_ctx* ctx, uint32_t* status);

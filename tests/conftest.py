@@ -23,7 +23,12 @@ def e4b():
 
 @pytest.fixture(scope="session")
 def dev(e4b):
+    """Device with a workspace attached, so GEMVs take the streaming tensor-core path."""
+    import ctypes
     d = e4b.Device(0)
+    ws = int(d.L.e4b_workspace_bytes())
+    buf = d.alloc(ws, "workspace")
+    d.call("e4b_set_workspace", buf.ptr, ctypes.c_size_t(ws))
     yield d
     d.close()
 

@@ -63,7 +63,8 @@ def test_dequant_bit_exact(e4b, dev):
 
 # ------------------------------------------------------------------ q4_0 GEMVs
 @pytest.mark.parametrize("n_in,rows,xf16", [(256, 2048, 1), (512, 768, 0), (704, 2816, 1), (2048, 3072, 1),
-                                             (2112, 2816, 1), (16384, 256, 1), (2048, 8960, 0), (32, 5, 0)])
+                                             (2112, 2816, 1), (16384, 256, 1), (16384, 2048, 1), (2048, 8960, 0),
+                                             (4096, 2816, 1), (192, 96, 1), (64, 40, 0), (32, 5, 0)])
 def test_q40mv(e4b, dev, n_in, rows, xf16):
     raw = q40(e4b, rows, n_in, 3)
     x = rng(n_in).standard_normal(n_in).astype(F32)
@@ -73,6 +74,40 @@ def test_q40mv(e4b, dev, n_in, rows, xf16):
     y = dev.alloc(rows * 4)
     e4b.ops.q40mv(dev, xd, up(dev, raw), None, y, IN=n_in, OUT=rows, XF16=xf16)
     assert rel_err(get(dev, y, F32, rows), O.q40mv(raw, x, rows, n_in)) < RTOL
+
+
+def test_q40mv_stream_matches_simple_kernel(e4b, dev):
+    """The streaming tensor-core GEMV and the one-warp-per-row kernel agree to
+    fp32 summation order on a split-K shape, with the f32-input path too."""
+    import ctypes
+    for n_in, rows, xf16 in [(16384, 512, 1), (2048, 1024, 0)]:
+        raw = up(dev, q40(e4b, rows, n_in, 33))
+        x = rng(34).standard_normal(n_in).astype(F32)
+        xd = up(dev, x.astype(np.float16) if xf16 else x)
+        y1, y2 = dev.alloc(rows * 4), dev.alloc(rows * 4)
+        e4b.ops.q40mv(dev, xd, raw, None, y1, IN=n_in, OUT=rows, XF16=xf16)
+        ws = dev.L.e4b_workspace_bytes()
+        wsbuf = [b for b in dev.buffers if b.name == "workspace"][0]
+        dev.call("e4b_set_workspace", None, ctypes.c_size_t(0))
+        try:
+            e4b.ops.q40mv(dev, xd, raw, None, y2, IN=n_in, OUT=rows, XF16=xf16)
+        finally:
+            dev.call("e4b_set_workspace", wsbuf.ptr, ctypes.c_size_t(ws))
+        a, b = get(dev, y1, F32, rows), get(dev, y2, F32, rows)
+        assert rel_err(a, b) < RTOL
+        # run-to-run determinism of the split-K merge
+        e4b.ops.q40mv(dev, xd, raw, None, y2, IN=n_in, OUT=rows, XF16=xf16)
+        assert np.array_equal(get(dev, y2, F32, rows), a)
+
+
+@pytest.mark.parametrize("H,FF", [(2048, 16384), (512, 1024), (2816, 2112)])
+def test_q40gu_dense_stream(e4b, dev, H, FF):
+    wd = q40(e4b, 2 * FF, H, 35)
+    x = O.f16r(rng(36).standard_normal(H).astype(F32))
+    yh = dev.alloc(FF * 2)
+    e4b.ops.q40gu(dev, None, None, None, None, up(dev, x.astype(np.float16)), up(dev, wd), yh, IN=H, FF=0, FF2=FF, K=0)
+    gu = O.q40mv(wd, x, 2 * FF, H)
+    assert f16_close(get(dev, yh, np.float16, FF), O.gelu_tanh(gu[:FF]) * gu[FF:])
 
 
 def test_q40mv_expert_slots(e4b, dev):
