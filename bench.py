@@ -157,16 +157,28 @@ def token_bytes(cfg, ctx_len: int) -> dict:
     return {"weights": w, "lm_head": head, "embed": emb_row, "kv": kv, "total": w + head + emb_row + kv}
 
 
+def bench_config(e4b, args):
+    """BASELINE's config by name; --layers keeps its layer shapes with fewer
+    layers (small cases for ncu captures)."""
+    import dataclasses
+    cfg = e4b.config.get(args.config)
+    if args.layers:
+        n = args.layers
+        cfg = dataclasses.replace(cfg, name=f"{cfg.name}-{n}l", layers=n,
+                                  sliding=list(cfg.sliding[:n]) if cfg.sliding else cfg.sliding)
+    return cfg
+
+
 def run_ours(args, rank, world, local_rank):
     e4b = importlib.import_module("e4b-webgpu_b200")
     import __graft_entry__
     __graft_entry__.build()
     dist = Dist(world, local_rank, "nccl" if world > 1 else None)
-    cfg = e4b.config.get(args.config)
+    cfg = bench_config(e4b, args)
     t0 = time.time()
     img = e4b.synth.build_model(cfg, seed=0)
     t_build = time.time() - t0
-    eng = e4b.Engine(img, local_rank)
+    eng = e4b.Engine(img, local_rank, fused=None if args.fused else False)
     dev = eng.dev
     prompt = e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=0)
     eng.prefill(prompt)
@@ -210,23 +222,42 @@ def run_ours(args, rank, world, local_rank):
     dev.sync()
     dev.call("e4b_event_elapsed", 2, 3, ctypes.byref(ms))
     t_e2e = dist.max(ms.value / 1000.0)
-    # ---- dominant kernel timed alone: the dense gate|up GEMV (+GeGLU) of every
-    # layer, each launch over different weights (cold L2), CUDA events on the stream
-    A = eng.A
-    H, FF = cfg.hidden, cfg.ff
-    nrep = 3
-    dev.call("e4b_event_record", 4)
-    for _ in range(nrep):
-        for L in eng.layers:
-            e4b.ops.q40gu(dev, None, None, None, None, A.normed, L.gu, A.geglu, IN=H, FF=0, FF2=FF, K=0)
-    dev.call("e4b_event_record", 5)
-    dev.sync()
-    dev.call("e4b_event_elapsed", 4, 5, ctypes.byref(ms))
-    gu_launch_s = ms.value / 1000.0 / (nrep * cfg.layers)
-    gu_bytes = 2 * FF * H // 32 * 18 + H * 2 + FF * 2
     peak, peak_kind = peaks()
     tb = token_bytes(cfg, ctx_mid)
+    A = eng.A
+    H, FF = cfg.hidden, cfg.ff
+    if eng.fused:
+        # ---- dominant kernel timed alone: the fused token kernel (every layer's
+        # weights, 2.2 GB >> L2, streamed once per launch), repeated on the same
+        # token; CUDA events on the engine's stream
+        nrep = 10
+        dev.call("e4b_event_record", 4)
+        for _ in range(nrep):
+            dev.call("e4b_dense_plan_run", eng.dense_plan)
+        dev.call("e4b_event_record", 5)
+        dev.sync()
+        dev.call("e4b_event_elapsed", 4, 5, ctypes.byref(ms))
+        dom_launch_s = ms.value / 1000.0 / nrep
+        dom_bytes = tb["weights"] + tb["kv"] + tb["embed"]
+        dom_name = "k_decode_dense (fused token: all layers' q4_0 weights + KV, one persistent kernel)"
+        dom_profile = "decode_dense_e4b.md"
+    else:
+        # ---- dominant kernel timed alone: the dense gate|up GEMV (+GeGLU) of every
+        # layer, each launch over different weights (cold L2), CUDA events on the stream
+        nrep = 3
+        dev.call("e4b_event_record", 4)
+        for _ in range(nrep):
+            for L in eng.layers:
+                e4b.ops.q40gu(dev, None, None, None, None, A.normed, L.gu, A.geglu, IN=H, FF=0, FF2=FF, K=0)
+        dev.call("e4b_event_record", 5)
+        dev.sync()
+        dev.call("e4b_event_elapsed", 4, 5, ctypes.byref(ms))
+        dom_launch_s = ms.value / 1000.0 / (nrep * cfg.layers)
+        dom_bytes = 2 * FF * H // 32 * 18 + H * 2 + FF * 2
+        dom_name = "q40gu (dense gate|up + GeGLU, 2048 -> 2x16384)"
+        dom_profile = "q40gu_e4b.md"
     kernels_per_token = eng.kernels_per_token
+    eng_fused, plan_mode = eng.fused, eng.plan_mode
     status = dev.status()
     eng.close()
     if status:
@@ -235,8 +266,8 @@ def run_ours(args, rank, world, local_rank):
     e2e = world * args.steps / t_e2e
     out = None
     if rank == 0:
-        ach = gu_bytes / gu_launch_s / 1e9
-        traffic = traffic_from_profile("q40gu_e4b.md")
+        ach = dom_bytes / dom_launch_s / 1e9
+        traffic = traffic_from_profile(dom_profile)
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1000 * t_dev / args.steps, 4), "higher_is_better": True,
@@ -248,10 +279,10 @@ def run_ours(args, rank, world, local_rank):
                        "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": "weights (%.2f GB/token) >> 126 MB L2: no flush needed" % (tb["total"] / 1e9)},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 4},
-            "roofline": {"bound": "hbm", "kernel": "q40gu (dense gate|up + GeGLU, 2048 -> 2x16384)",
+            "roofline": {"bound": "hbm", "kernel": dom_name,
                          "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(ach / peak, 4), "peak_source": peak_kind,
-                         "bytes_per_launch": gu_bytes, "launch_us": round(gu_launch_s * 1e6, 2),
+                         "bytes_per_launch": dom_bytes, "launch_us": round(dom_launch_s * 1e6, 2),
                          "traffic": traffic},
             "token_roofline": {"bytes_per_token": tb["total"], "breakdown": tb,
                                "achieved_gbs": round(tb["total"] * value / world / 1e9, 1),
@@ -260,6 +291,7 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clk,
             "gpu_launches": int(kernels_per_token * args.steps),
             "kernels_per_token": kernels_per_token,
+            "fused": eng_fused, "plan_mode": plan_mode,
             "model_build_s": round(t_build, 1),
         }
     dist.close()
@@ -297,7 +329,7 @@ def run_reference(args, rank, world):
     e4b = importlib.import_module("e4b-webgpu_b200")
     import __graft_entry__
     __graft_entry__.build()
-    cfg = e4b.config.get(args.config)
+    cfg = bench_config(e4b, args)
     img = e4b.synth.build_model(cfg, seed=0)
     # each "step" of the reference arm is a bounded sample of CPU decode steps
     steps = max(1, min(args.steps, 16))
@@ -362,6 +394,53 @@ def run_rmschain(e4b, dev, args):
     dev.close()
 
 
+PHASE_NAMES = ["ple_proj", "qkv", "attention", "o", "gate_up", "down", "ple_gate", "ple_layer_proj", "final"]
+
+
+def run_trace(args):
+    """Per-phase timing of the fused token kernel (e4b_dense_plan_trace): mean
+    microseconds per phase kind of CTA 0's residual step, input build, GEMV
+    (and the part of it spent waiting for weight copies), epilogue, the latest
+    CTA's finish and the grid barrier, after a prefill of --prefill tokens."""
+    import ctypes
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    import __graft_entry__
+    __graft_entry__.build()
+    cfg = bench_config(e4b, args)
+    eng = e4b.Engine(e4b.synth.build_model(cfg, seed=0), 0)
+    if not eng.fused:
+        raise SystemExit("--trace needs the fused token kernel")
+    d = eng.dev
+    eng.prefill(e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=0))
+    d.sync()
+    kinds = (ctypes.c_int * 8192)()
+    nph = d.L.e4b_dense_plan_phases(d.ctx, eng.dense_plan, kinds, 8192)
+    kinds = np.array(kinds[:nph])
+    tb = d.alloc(nph * 64, "trace")
+    d.call("e4b_dense_plan_trace", eng.dense_plan, tb.ptr)
+    for _ in range(max(2, args.steps)):
+        d.memset(tb, 0)
+        d.call("e4b_dense_plan_run", eng.dense_plan)
+        d.sync()
+    t = d.read(tb, np.uint64, nph * 8).reshape(nph, 8).astype(np.int64)
+    d.call("e4b_dense_plan_trace", eng.dense_plan, None)
+    out = {"workload": cfg.name, "context": args.prefill, "phases": int(nph),
+           "kernel_us": round((t[-1, 0] - t[0, 0]) / 1e3, 1), "kinds": {}}
+    for k, name in enumerate(PHASE_NAMES[:-1]):
+        sel = np.nonzero(kinds[:-1] == k)[0]
+        if len(sel) == 0:
+            continue
+        m = lambda a, b: round(float(((t[sel, b] - t[sel, a]) / 1e3).mean()), 2)
+        row = {"n": int(len(sel)), "residual": m(0, 1), "slowest_done": m(0, 5), "barrier": m(5, 6),
+               "phase": m(0, 6)}
+        if name != "attention":
+            row.update({"input": m(1, 2), "gemv": m(2, 3), "weight_wait": round(float((t[sel, 7] / 1e3).mean()), 2),
+                        "epilogue": m(3, 4)})
+        out["kinds"][name] = row
+    eng.close()
+    print(json.dumps(out))
+
+
 def run_kernel(args):
     """Time one streaming kernel alone: `launches` launches cycling over enough
     distinct weight copies that the working set exceeds L2."""
@@ -418,9 +497,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="e4b")
     ap.add_argument("--prefill", type=int, default=512)
+    ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling cases)")
+    ap.add_argument("--fused", type=int, default=1, help="1: fused token kernel where the model allows it; "
+                                                          "0: one kernel per operator")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain"], help="time one kernel alone instead of the decode")
+    ap.add_argument("--trace", action="store_true", help="per-phase timing of the fused token kernel")
     ap.add_argument("--launches", type=int, default=200)
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1/0)")
     ap.add_argument("--ctas-per-sm", type=int, default=1)
@@ -429,6 +512,9 @@ def main():
     args = ap.parse_args()
     if args.kernel:
         run_kernel(args)
+        return
+    if args.trace:
+        run_trace(args)
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -17,7 +17,7 @@ LIBPATH = os.path.join(_HERE, "libe4b_b200.so")
 
 _CTYPE = {
     "int": ctypes.c_int, "float": ctypes.c_float, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t,
-    "uint32_t": ctypes.c_uint32, "double": ctypes.c_double,
+    "uint32_t": ctypes.c_uint32, "double": ctypes.c_double, "unsigned long long": ctypes.c_ulonglong,
 }
 
 _PROTO = re.compile(r"E4B_API\s+([\w\s\*]+?)\s*\b(e4b_\w+)\s*\(([^)]*)\)\s*;", re.S)

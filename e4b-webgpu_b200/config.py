@@ -169,10 +169,10 @@ def a4b() -> ModelConfig:
 
 
 def tiny_ple() -> ModelConfig:
-    # 4 layers x PLE 64 = one 256-wide q6_K block per table row
+    # sliding rings of 24 slots (wrap early), one global layer, PLE width 256
     return ModelConfig(name="tiny_ple", arch="dense", hidden=512, layers=4, q_heads=4, kv_heads=2,
                        head_dim=128, ff=1024, vocab=4096, window=16, ring_slack=8,
-                       sliding=[True, True, False, True], ple_dim=64, max_ctx=1024)
+                       sliding=[True, True, False, True], ple_dim=256, max_ctx=1024)
 
 
 def tiny_moe() -> ModelConfig:

@@ -33,6 +33,9 @@ struct e4b_ctx {
 };
 
 int e4b_fail(e4b_ctx* c, int code, const char* fmt, ...);
+namespace e4b {
+void dense_plans_release(e4b_ctx* c);   // frees a context's fused token plans
+}
 
 #define E4B_CHECK_CTX(c) \
   do {                   \

@@ -287,6 +287,8 @@ int launch_variant(e4b_ctx* c, const Q40P& p, const CUtensorMap& map, const char
 
 namespace e4b {
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+
 bool q40_stream_supported(const void* w, const void* x, int IN, int rows) {
   (void)rows;
   if (IN <= 0 || IN % 256 || IN > 16384) return false;           // whole 8-block groups, 16-byte rows

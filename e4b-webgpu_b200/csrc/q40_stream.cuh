@@ -18,4 +18,8 @@ bool q40_stream_supported(const void* w, const void* x, int IN, int rows);
 int q40_stream(e4b_ctx* c, const uint8_t* w, const void* x, int x_f32, float* y, uint16_t* yh, const float* ple,
                int IN, int OUT, int epi, int ff, int off);
 
+// Streaming q6_K LM head (q6k_stream.cu): batch 1, hidden a multiple of 2048.
+bool lmhead_stream_supported(const uint8_t* w, const float* x, int N);
+int lmhead_stream(e4b_ctx* c, const uint8_t* w, const float* x, float* y, int N, int OUT, float softcap);
+
 }  // namespace e4b

@@ -1,6 +1,7 @@
 // q6_K operators over raw GGUF blocks: token-embedding row (q6k MODE 0), LM head
 // (q6k MODE 1, softcap) and the per-layer-embedding input prep (pleprep).
 #include "common.cuh"
+#include "q40_stream.cuh"
 
 namespace {
 
@@ -114,6 +115,7 @@ E4B_API int e4b_q6k_lmhead(e4b_ctx* c, const uint8_t* w, const float* x, float* 
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, w && x && y && N > 0 && N % 256 == 0 && OUT > 0, "q6k_lmhead: bad args");
   if (batch < 1) batch = 1;
+  if (batch == 1 && e4b::lmhead_stream_supported(w, x, N)) return e4b::lmhead_stream(c, w, x, y, N, OUT, softcap);
   return e4b_launch(c, "q6k_lmhead", k_q6k_lmhead, dim3((OUT + 7) / 8, batch), dim3(256), 0, w, x, y, N, OUT,
                     softcap);
 }

@@ -41,6 +41,7 @@ E4B_API int e4b_destroy(e4b_ctx* c) {
   cudaStreamSynchronize(c->stream);
   for (auto& g : c->plans)
     if (g) cudaGraphExecDestroy(g);
+  e4b::dense_plans_release(c);
   for (auto& e : c->ev) cudaEventDestroy(e);
   cudaFree(c->status);
   cudaStreamDestroy(c->stream);

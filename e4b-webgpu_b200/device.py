@@ -35,7 +35,8 @@ _RUNTIME = {"e4b_create", "e4b_destroy", "e4b_device_info", "e4b_alloc", "e4b_fr
             "e4b_host_free", "e4b_upload", "e4b_download", "e4b_upload_async", "e4b_download_async", "e4b_memset",
             "e4b_copy", "e4b_sync", "e4b_event_record", "e4b_event_elapsed", "e4b_set_pdl", "e4b_device_status",
             "e4b_plan_begin", "e4b_plan_end", "e4b_plan_launch", "e4b_plan_destroy", "e4b_set_workspace",
-            "e4b_set_option"}
+            "e4b_set_option", "e4b_dense_plan_create", "e4b_dense_plan_destroy",
+            "e4b_dense_plan_trace", "e4b_dense_plan_phases"}
 
 
 def _ptr(x):

@@ -32,8 +32,37 @@ RING_CAP = 16384        # greedy-token ring (src/engine-a4b.js:250 uses 1024)
 ARGMAX_PARTS = 256
 
 
+class DenseLayer(ctypes.Structure):
+    """e4b_dense_layer (include/e4b_b200.h)"""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("qkv", "o", "gu", "down", "ple_gate", "ple_proj", "attn_norm",
+                                               "q_norm", "k_norm", "post_attn", "ffn_norm", "post_ffw",
+                                               "post_norm")] + \
+        [("scale", ctypes.c_float), ("theta", ctypes.c_float), ("kcache", ctypes.c_void_p),
+         ("vcache", ctypes.c_void_p)] + \
+        [(n, ctypes.c_int) for n in ("sliding", "ring", "slots", "rope_angles", "keqv", "qkv_rows")]
+
+
+class DenseModel(ctypes.Structure):
+    """e4b_dense_model (include/e4b_b200.h)"""
+    _fields_ = [(n, ctypes.c_int) for n in ("layers", "hidden", "q_heads", "kv_heads", "head_dim", "ff", "vocab",
+                                            "ple_dim", "window")] + \
+        [("eps", ctypes.c_float)] + \
+        [(n, ctypes.c_void_p) for n in ("token_embd", "ple_table", "ple_proj_w", "ple_norm", "out_norm")] + \
+        [("layer", ctypes.POINTER(DenseLayer))] + \
+        [(n, ctypes.c_void_p) for n in ("params", "hidden_out", "xf", "dump")]
+
+
+def fused_supported(c: ModelConfig) -> bool:
+    """Shapes the fused token kernel takes (e4b_dense_plan_create checks the same)."""
+    return (not c.moe and c.hidden % 256 == 0 and c.hidden <= 4096 and c.q_dim % 256 == 0 and c.ff % 256 == 0
+            and c.head_dim % 64 == 0 and (c.ple_dim == 0 or (c.ple_dim % 256 == 0 and c.ple_dim <= 4096)))
+
+
 class Engine:
-    def __init__(self, src, device: int | Device = 0, *, chunk: int = 64, record: bool = False):
+    def __init__(self, src, device: int | Device = 0, *, chunk: int = 64, record: bool = False,
+                 fused: bool | None = None):
+        """fused: run each token's layers as one persistent kernel (dense graph
+        only; None = whenever the model's shapes allow it)."""
         self.g = gguf.open_gguf(src)
         self.cfg = ModelConfig.from_kv(self.g.kv)
         self.dev = device if isinstance(device, Device) else Device(device)
@@ -41,9 +70,16 @@ class Engine:
         self.chunk = chunk
         self.record = record
         self.plan = None
+        self.plan_mode = None
         self.weight_bytes = 0
+        if fused is None:
+            fused = fused_supported(self.cfg)
+        if fused and not fused_supported(self.cfg):
+            raise ValueError(f"model {self.cfg.name!r} has shapes the fused token kernel does not take")
+        self.fused = bool(fused)
         self._load_weights()
         self._alloc_activations()
+        self.dense_plan = self._create_dense_plan() if self.fused else None
 
     # ------------------------------------------------------------ loading
     def _raw(self, name: str):
@@ -171,11 +207,46 @@ class Engine:
         self.host_tok = np.ctypeslib.as_array(ctypes.cast(p2, ctypes.POINTER(ctypes.c_uint32)), shape=(16,))
         self._host_tok_ptr = p2.value
 
+    def _create_dense_plan(self) -> int:
+        """Describe the dense model to e4b_dense_plan_create (fused token kernel)."""
+        c, A = self.cfg, self.A
+        lay = (DenseLayer * c.layers)()
+        for L in self.layers:
+            e = lay[L.i]
+            e.qkv, e.o, e.gu, e.down = L.qkv.ptr, L.o.ptr, L.gu.ptr, L.down.ptr
+            if c.ple_dim:
+                e.ple_gate, e.ple_proj, e.post_norm = L.inp_gate.ptr, L.proj.ptr, L.post_norm.ptr
+            e.attn_norm, e.q_norm, e.k_norm = L.attn_norm.ptr, L.q_norm.ptr, L.k_norm.ptr
+            e.post_attn, e.ffn_norm, e.post_ffw = L.post_attn.ptr, L.ffn_norm.ptr, L.post_ffw.ptr
+            e.scale, e.theta = L.scale, L.theta
+            e.kcache, e.vcache = L.kc.ptr, L.vc.ptr
+            e.sliding, e.ring, e.slots = int(L.sliding), L.ring, L.slots
+            e.rope_angles, e.keqv, e.qkv_rows = L.angles, int(L.keqv), L.qkv_rows
+        m = DenseModel()
+        m.layers, m.hidden, m.q_heads, m.kv_heads = c.layers, c.hidden, c.q_heads, c.kv_heads
+        m.head_dim, m.ff, m.vocab, m.ple_dim, m.window = c.head_dim, c.ff, c.vocab, c.ple_dim, c.window
+        m.eps = c.eps
+        m.token_embd, m.out_norm = self.emb.ptr, self.out_norm.ptr
+        if c.ple_dim:
+            m.ple_table, m.ple_proj_w, m.ple_norm = self.ple_table.ptr, self.ple_proj_w.ptr, self.ple_norm.ptr
+        m.layer = lay
+        m.params, m.hidden_out, m.xf = A.params.ptr, A.hidden.ptr, A.xf.ptr
+        m.dump = A.dump.ptr if self.record else None
+        h = ctypes.c_int()
+        self.dev.call("e4b_dense_plan_create", ctypes.byref(m), ctypes.byref(h))
+        return h.value
+
     # ------------------------------------------------------------ one token
     def encode_forward(self):
         """Enqueue one token (src/engine-a4b.js:683-693)."""
         c, d, A = self.cfg, self.dev, self.A
         H, V = c.hidden, c.vocab
+        if self.fused:
+            d.call("e4b_dense_plan_run", self.dense_plan)
+            ops.q6k_lmhead(d, self.emb, A.xf, A.logits, N=H, OUT=V, SOFTCAP=c.softcap)
+            ops.argmax(d, A.logits, A.amax_part, A.amax, N=V, PARTS=ARGMAX_PARTS)
+            ops.feedtok(d, A.amax, A.params, A.ring, RING_CAP=RING_CAP)
+            return
         ops.q6k_embed(d, self.emb, A.params, None, A.hidden, N=H, ROWS=V, MULT=float(F32(math.sqrt(H))))
         if c.ple_dim:
             L, PD = c.layers, c.ple_dim
@@ -252,22 +323,40 @@ class Engine:
 
     # ------------------------------------------------------------ plan
     def build_plan(self):
-        """Record encode_forward() once as a replayable CUDA graph."""
-        if self.plan is None:
+        """Record encode_forward() once as a replayable CUDA graph.  If the
+        driver refuses to record the fused (cooperative) kernel into a graph,
+        tokens are enqueued kernel by kernel instead (plan_mode "direct")."""
+        if self.plan_mode is None:
             n0 = self.dev.kernel_launches
             self.dev.call("e4b_plan_begin")
+            err = None
             try:
                 self.encode_forward()
-            finally:
-                p = ctypes.c_int()
+            except Exception as e:      # recorded below; capture must still be ended
+                err = e
+            p = ctypes.c_int()
+            try:
                 self.dev.call("e4b_plan_end", ctypes.byref(p))
-            self.plan = p.value
+            except Exception as e:
+                err = err or e
             self.kernels_per_token = self.dev.kernel_launches - n0
+            if err is None:
+                self.plan, self.plan_mode = p.value, "graph"
+            elif self.fused:
+                self.plan_mode, self.plan_error = "direct", str(err)
+                self.dev.sync()
+            else:
+                raise err
         return self.plan
 
     def run_token(self, count: int = 1):
-        """Enqueue `count` tokens (graph replays)."""
-        self.dev.call("e4b_plan_launch", self.build_plan(), count)
+        """Enqueue `count` tokens (graph replays, or direct launches)."""
+        self.build_plan()
+        if self.plan_mode == "graph":
+            self.dev.call("e4b_plan_launch", self.plan, count)
+        else:
+            for _ in range(count):
+                self.encode_forward()
 
     # ------------------------------------------------------------ host API
     def set_params(self, token: int, pos: int, ring_index: int | None = None, sync_slot: bool = False):
@@ -335,5 +424,8 @@ class Engine:
         return ids
 
     def close(self):
+        if self.dense_plan is not None:
+            self.dev.call("e4b_dense_plan_destroy", self.dense_plan)
+            self.dense_plan = None
         if self.own_dev:
             self.dev.close()

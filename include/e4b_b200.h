@@ -228,6 +228,73 @@ E4B_API int e4b_argmax(e4b_ctx* ctx, const float* x, uint32_t* part, uint32_t* o
  * ring[params[6] % ring_cap] = amax[0]; params[2] = amax[0]; pos/len/kvCount/index += 1. */
 E4B_API int e4b_feedtok(e4b_ctx* ctx, const uint32_t* amax, uint32_t* params, uint32_t* ring, int ring_cap);
 
+/* ------------------------------------------------------------ fused token plan */
+/* One dense (E4B-graph) decoder layer: q4_0 weights as stored in the GGUF
+ * (qkv = q|k|v rows back to back, gu = gate|up rows back to back), f32 norm
+ * weights, f16 KV cache [slots][KVH][HD]. */
+typedef struct {
+  const uint8_t* qkv;
+  const uint8_t* o;
+  const uint8_t* gu;
+  const uint8_t* down;
+  const uint8_t* ple_gate; /* may be NULL when the model has no per-layer embeddings */
+  const uint8_t* ple_proj;
+  const float* attn_norm;
+  const float* q_norm;
+  const float* k_norm;
+  const float* post_attn;
+  const float* ffn_norm;
+  const float* post_ffw;
+  const float* post_norm; /* post-PLE norm */
+  float scale;            /* layer output scale */
+  float theta;
+  uint16_t* kcache;
+  uint16_t* vcache;
+  int sliding, ring, slots, rope_angles, keqv, qkv_rows;
+} e4b_dense_layer;
+
+/* The dense model: weights as uploaded from the GGUF, the per-token parameter
+ * block, and the outputs the fused plan writes (caller-owned device memory).
+ * The plan allocates its own intermediate activations at creation. */
+typedef struct {
+  int layers, hidden, q_heads, kv_heads, head_dim, ff, vocab, ple_dim, window;
+  float eps;
+  const uint8_t* token_embd;    /* q6_K [vocab][hidden] */
+  const uint8_t* ple_table;     /* q6_K [vocab][layers*ple_dim] (ple_dim > 0) */
+  const uint8_t* ple_proj_w;    /* q4_0 [layers*ple_dim][hidden] */
+  const float* ple_norm;        /* [ple_dim] */
+  const float* out_norm;        /* [hidden] */
+  const e4b_dense_layer* layer; /* host array of `layers` entries */
+  const uint32_t* params;       /* [8] per-token parameter block (token = params[2]) */
+  float* hidden_out;            /* [hidden] residual stream after the last layer */
+  float* xf;                    /* [hidden] final-norm output (LM-head input) */
+  float* dump;                  /* [layers][hidden] per-layer residual, or NULL */
+} e4b_dense_model;
+
+/* Fused token plan.  It has no single counterpart in the reference: one run
+ * performs the reference's per-token operator sequence of the dense graph up
+ * to the final norm (src/engine.js:282-331; embedding, PLE prep, per layer
+ * qkvMv/headprep/attsplit/attcomb/oMv/rmsacc/q40gu/downMv/plegate/proj/rmsacc,
+ * final rmsnorm) as one persistent cooperative kernel, one CTA per SM, with
+ * grid barriers between dependent steps.  Creation checks the shapes (hidden,
+ * q_heads*head_dim, ff and ple_dim multiples of 256; head_dim a multiple of
+ * 64), encodes the TMA descriptors and allocates the plan's activations; run
+ * enqueues one token on the context stream, reading params[] on the device. */
+E4B_API int e4b_dense_plan_create(e4b_ctx* ctx, const e4b_dense_model* model, int* handle);
+E4B_API int e4b_dense_plan_run(e4b_ctx* ctx, int handle);
+/* Phase timing: with buf non-NULL every later run writes globaltimer stamps
+ * (ns) for each phase p into buf[8p .. 8p+7]: CTA 0's start, after its residual
+ * step, after its input build, after its GEMV, after its epilogue, the latest
+ * "work done" time over all CTAs (atomic max: zero buf before the run), and
+ * CTA 0 past the phase's grid barrier, and the time CTA 0's warp 0 spent
+ * waiting for weight copies in the phase.  NULL turns it off.
+ * e4b_dense_plan_phases returns the number of phases and their kinds: 0 PLE
+ * projection, 1 q|k|v, 2 attention, 3 o, 4 gate|up, 5 down, 6 PLE gate, 7 PLE
+ * layer projection, 8 final norm. */
+E4B_API int e4b_dense_plan_trace(e4b_ctx* ctx, int handle, unsigned long long* buf);
+E4B_API int e4b_dense_plan_phases(e4b_ctx* ctx, int handle, int* kinds, int max);
+E4B_API int e4b_dense_plan_destroy(e4b_ctx* ctx, int handle);
+
 #ifdef __cplusplus
 }
 #endif

