@@ -1,5 +1,7 @@
 // MoE routing (routertop / router / top8), two-stage argmax and the GPU-side
 // token feedback that makes a recorded per-token plan replayable.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -191,6 +193,54 @@ E4B_API int e4b_top8(e4b_ctx* c, const float* scores, const float* pes, uint32_t
 E4B_API int e4b_argmax(e4b_ctx* c, const float* x, uint32_t* part, uint32_t* out, int N, int parts) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, x && part && out && N > 0 && parts > 0 && parts <= 4096, "argmax: bad args");
+  if (int r = e4b_launch(c, "argmax0", k_argmax0, dim3(parts), dim3(256), 0, x, part, N, parts)) return r;
+  return e4b_launch(c, "argmax1", k_argmax1, dim3(1), dim3(256), 0, (const uint32_t*)part, out, parts);
+}
+
+}  // extern "C"
+
+// ---- argmax without caller scratch.
+// Some hosts may not allocate device memory once they are serving: a runtime
+// that handed all free HBM to its KV cache at start-up, or one that must not
+// call cudaMalloc on the decode path because it synchronises the device and can
+// fail under memory pressure in the middle of a request.  For them the stage-0
+// partials of the argmax live in this fixed module-level array instead of a
+// caller-provided buffer.  Its address is looked up once per device (with that
+// device current) and cached; nothing in it needs to start at zero, because
+// stage 0 writes every partial stage 1 reads.  All callers on a device share
+// it, so two such argmax calls in flight at the same time race.
+namespace {
+constexpr int kStaticArgmaxParts = 4096;
+__device__ __align__(256) uint32_t g_argmax_part[2 * kStaticArgmaxParts];
+constexpr int kMaxDevices = 64;
+std::mutex g_argmax_mu;
+uint32_t* g_argmax_addr[kMaxDevices] = {};
+
+int static_part_addr(e4b_ctx* c, uint32_t** out) {
+  E4B_REQUIRE(c, c->device >= 0 && c->device < kMaxDevices, "argmax_static: device %d out of range", c->device);
+  std::lock_guard<std::mutex> lock(g_argmax_mu);
+  if (!g_argmax_addr[c->device]) {
+    E4B_CUDA(c, cudaSetDevice(c->device));
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_part);
+    if (e != cudaSuccess || !p)
+      return e4b_fail(c, E4B_ECUDA, "argmax_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_argmax_addr[c->device] = static_cast<uint32_t*>(p);
+  }
+  *out = g_argmax_addr[c->device];
+  return E4B_OK;
+}
+}  // namespace
+
+extern "C" {
+
+E4B_API int e4b_argmax_static(e4b_ctx* c, const float* x, uint32_t* out, int N, int parts) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && out && N > 0, "argmax_static: bad args");
+  E4B_REQUIRE(c, parts > 0 && parts <= kStaticArgmaxParts, "argmax_static: parts %d outside 1..%d", parts,
+              kStaticArgmaxParts);
+  uint32_t* part = nullptr;
+  if (int r = static_part_addr(c, &part)) return r;
   if (int r = e4b_launch(c, "argmax0", k_argmax0, dim3(parts), dim3(256), 0, x, part, N, parts)) return r;
   return e4b_launch(c, "argmax1", k_argmax1, dim3(1), dim3(256), 0, (const uint32_t*)part, out, parts);
 }

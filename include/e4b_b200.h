@@ -223,6 +223,12 @@ E4B_API int e4b_plemul(e4b_ctx* ctx, const float* a, const float* ple, float* y,
 /* kernels/argmax2.wgsl:8-48 (both stages): out[0] = index of the largest x (ties
  * -> lowest index), out[1] = its f32 bits.  part: scratch of 2*parts u32. */
 E4B_API int e4b_argmax(e4b_ctx* ctx, const float* x, uint32_t* part, uint32_t* out, int N, int parts);
+/* e4b_argmax without caller scratch (no counterpart in the reference): the
+ * partials live in a fixed device array of the library, so the call allocates
+ * nothing.  parts must be 1..4096.  The first call on a device looks the array's
+ * address up (make it before any stream capture); all such calls on one device
+ * share the array, so overlapping calls race. */
+E4B_API int e4b_argmax_static(e4b_ctx* ctx, const float* x, uint32_t* out, int N, int parts);
 /* kernels/feedtok.wgsl:5-6 plus the token-ring copy (src/engine-a4b.js:820) and
  * the per-token parameter advance (src/engine-a4b.js:793-795), on the device:
  * ring[params[6] % ring_cap] = amax[0]; params[2] = amax[0]; pos/len/kvCount/index += 1. */
