@@ -57,11 +57,12 @@ constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kStages = 4;
 constexpr int kPrefetch = 6;          // quanta per warp prefetched into L2 beyond the ring
-constexpr int kMaxPer = 16;           // hidden <= 16 * kThreads
+constexpr int kMaxPer = 8;            // hidden and PLE width <= 8 * kThreads
 
 enum : int { PH_GEMV = 0, PH_ATTN = 1, PH_FINAL = 2 };
 enum : int { XB_NONE = 0, XB_NORM = 1, XB_RAW = 2, XB_F32 = 3, XB_ATTN = 4, XB_PLE = 5 };
-enum : int { XK_SMEM_F16 = 0, XK_GLOBAL_F16 = 1, XK_SMEM_F32 = 2 };
+enum : int { XK_SMEM_F16 = 0, XK_STAGED_F16 = 1, XK_SMEM_F32 = 2 };
+constexpr int kMaxRope = 4;           // distinct (theta, rotated pairs) layer kinds
 enum : int { EPI_SLOTS = 0, EPI_GEGLU = 1 };
 
 // A GEMV output as partials: buf[row / 32][s][row % 32]; the value of a row is
@@ -75,7 +76,7 @@ struct MkGemv {
   int T, qpr, s, rot;   // tiles, quanta per tile, k-splits, CTA rotation
   int gu, ff;           // gate|up row layout: subtile 1 rows start at ff
   int xk;               // XK_*
-  const uint16_t* xg;   // XK_GLOBAL_F16 source
+  const uint16_t* xg;   // XK_STAGED_F16: global f16 x, the CTA's k-range is staged in shared memory
   int epi;
   float* out;           // EPI_SLOTS: [T][s][32]
   uint16_t* outh;       // EPI_GEGLU: [ff]
@@ -90,6 +91,7 @@ struct MkAttn {
   float* part_o;        // [QH][nct][HD]
   float* part_ml;       // [QH][nct][2]
   int cachemode, ring, window, slots, angles, keqv, nct;
+  int rope;             // index into the per-token RoPE table
   float theta, scale;
 };
 
@@ -134,6 +136,9 @@ struct MkArgs {
   float* hout;
   unsigned long long* trace;   // optional [nph][8] globaltimer stamps (see e4b_dense_plan_trace)
   int xs_bytes, scr_bytes;
+  int nrope;                   // RoPE kinds: theta and rotated pairs
+  float rope_theta[kMaxRope];
+  int rope_angles[kMaxRope];
 };
 
 // ------------------------------------------------------------------ partition
@@ -172,23 +177,12 @@ E4B_DEV float slot_sum(const SlotSrc& S, int row) {
   return v;
 }
 
-// Global f16 activations written earlier in this kernel: L2-coherent loads.
-E4B_DEV uint4 xfrag_f16_cg(const uint16_t* x, int blk, const XLane& X) {
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(x + 32 * blk);
-  const uint32_t a = __ldcg(w + X.wa), b = __ldcg(w + X.wb), ah = __ldcg(w + 8 + X.wa), bh = __ldcg(w + 8 + X.wb);
-  return make_uint4(__byte_perm(a, b, 0x5410), __byte_perm(a, b, 0x7632), __byte_perm(ah, bh, 0x5410),
-                    __byte_perm(ah, bh, 0x7632));
-}
-
-template <int XK>
-E4B_DEV void xget(const void* xs, const uint16_t* xg, int blk, const XLane& X, uint4& hi, uint4& lo) {
-  if (XK == XK_SMEM_F32) {
-    xfrag_f32_any(reinterpret_cast<const float*>(xs), blk, X, hi, lo);
-  } else if (XK == XK_SMEM_F16) {
-    hi = xfrag_f16_any(reinterpret_cast<const uint16_t*>(xs), blk, X);
-    lo = make_uint4(0, 0, 0, 0);
+// B fragments from shared memory: f16 x, or f32 x split into f16 hi + lo.
+E4B_DEV void xget(const void* x, bool xf32, int blk, const XLane& X, uint4& hi, uint4& lo) {
+  if (xf32) {
+    xfrag_f32_any(reinterpret_cast<const float*>(x), blk, X, hi, lo);
   } else {
-    hi = xfrag_f16_cg(xg, blk, X);
+    hi = xfrag_f16_any(reinterpret_cast<const uint16_t*>(x), blk, X);
     lo = make_uint4(0, 0, 0, 0);
   }
 }
@@ -295,31 +289,43 @@ E4B_DEV bool grid_sync(unsigned* ctr, unsigned target, uint32_t* status, volatil
 struct Prod {
   SchedEnt e, nx;
   int idx, end, j;
+  int tl, kk;           // local tile and quantum of item j (warp + 8 j = tl * kq + kk)
 };
+
+E4B_DEV void prod_seek(Prod& u, int warp) {
+  u.j = 0;
+  u.tl = warp / u.e.kq;
+  u.kk = warp - u.tl * u.e.kq;
+}
 
 E4B_DEV void prod_init(const MkArgs& A, Prod& u, int c, int warp) {
   const int2 r = A.sched_rng[c * kWarps + warp];
   u.idx = r.x;
   u.end = r.x + r.y;
-  u.j = 0;
-  if (u.idx < u.end) u.e = A.sched[u.idx];
+  if (u.idx < u.end) {
+    u.e = A.sched[u.idx];
+    prod_seek(u, warp);
+  }
   if (u.idx + 1 < u.end) u.nx = A.sched[u.idx + 1];
 }
 
-// The cursor's quantum: tensor map, x coordinate, rows of its two boxes.
-E4B_DEV void prod_coords(const Prod& u, int warp, int& x, int& r0, int& r1) {
-  const int i = warp + kWarps * u.j;
-  const int tl = i / u.e.kq;
-  const int tile = u.e.t0 + tl, k = u.e.k0 + (i - tl * u.e.kq);
-  x = k * 18;
+// The cursor's quantum: x coordinate and rows of its two boxes.
+E4B_DEV void prod_coords(const Prod& u, int& x, int& r0, int& r1) {
+  const int tile = u.e.t0 + u.tl;
+  x = (u.e.k0 + u.kk) * 18;
   r0 = u.e.gu ? 16 * tile : 32 * tile;
   r1 = u.e.gu ? u.e.ff + 16 * tile : 32 * tile + 16;
 }
-E4B_DEV void prod_advance(const MkArgs& A, Prod& u) {
+E4B_DEV void prod_advance(const MkArgs& A, Prod& u, int warp) {
+  u.kk += kWarps;
+  while (u.kk >= u.e.kq) {
+    u.kk -= u.e.kq;
+    u.tl++;
+  }
   if (++u.j == u.e.nw) {
-    u.j = 0;
     if (++u.idx < u.end) {
       u.e = u.nx;
+      prod_seek(u, warp);
       if (u.idx + 1 < u.end) u.nx = A.sched[u.idx + 1];
     }
   }
@@ -328,22 +334,22 @@ E4B_DEV void prod_advance(const MkArgs& A, Prod& u) {
 E4B_DEV void prod_issue(const MkArgs& A, Prod& u, uint8_t* stage, uint64_t* bar, int warp, int lane, uint64_t pol) {
   if (lane == 0) {
     int x, r0, r1;
-    prod_coords(u, warp, x, r0, r1);
+    prod_coords(u, x, r0, r1);
     mbar_expect_tx(bar, (uint32_t)kQuantumBytes);
     tma_load_2d_hint(stage, u.e.map, x, r0, bar, pol);
     tma_load_2d_hint(stage + kSubBytes, u.e.map, x, r1, bar, pol);
   }
-  prod_advance(A, u);
+  prod_advance(A, u, warp);
 }
 // L2 prefetch of the prefetch cursor's quantum, then advance it.
 E4B_DEV void prod_prefetch(const MkArgs& A, Prod& u, int warp, int lane) {
   if (lane == 0) {
     int x, r0, r1;
-    prod_coords(u, warp, x, r0, r1);
+    prod_coords(u, x, r0, r1);
     tma_prefetch_2d(u.e.map, x, r0);
     tma_prefetch_2d(u.e.map, x, r1);
   }
-  prod_advance(A, u);
+  prod_advance(A, u, warp);
 }
 
 struct Ring {
@@ -356,9 +362,12 @@ struct Ring {
 };
 
 // ------------------------------------------------------------------ GEMV phase
-template <int XK>
-E4B_DEV void gemv_phase(const MkArgs& A, const MkGemv& g, const Work& W, int warp, int lane, Ring& R, Prod& u,
-                        Prod& pf, uint64_t pol, const void* xs, float* P) {
+// x: activations in shared memory indexed by absolute block (8 k + g); XF32:
+// f32 x split into f16 hi + lo (twice the MMAs; one GEMV per token uses it).
+template <bool XF32>
+E4B_DEV void gemv_phase(const MkArgs& A, const Work& W, int warp, int lane, Ring& R, Prod& u, Prod& pf,
+                        uint64_t pol, const void* x, float* P) {
+  constexpr bool xf32 = XF32;
   const int nw = warp_items(W, warp);
   if (nw == 0) return;
   const int gg = lane >> 2, t = lane & 3;
@@ -368,19 +377,23 @@ E4B_DEV void gemv_phase(const MkArgs& A, const MkGemv& g, const Work& W, int war
   L.sel = t < 3 ? 0x3210u : 0x5432u;
   const XLane X = xlane(gg, t);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int tl = warp / W.kq, kk = warp - tl * W.kq;      // item j: warp + 8 j = tl * kq + kk
   uint4 xh, xl;
-  xget<XK>(xs, g.xg, (W.k0 + warp % W.kq) * 8 + gg, X, xh, xl);
+  xget(x, xf32, (W.k0 + kk) * 8 + gg, X, xh, xl);
   for (int j = 0; j < nw; j++) {
-    const int i = warp + kWarps * j;
-    const int tl = i / W.kq;
+    int ntl = tl, nkk = kk + kWarps;
+    while (nkk >= W.kq) {
+      nkk -= W.kq;
+      ntl++;
+    }
     uint4 nh = make_uint4(0, 0, 0, 0), nl = make_uint4(0, 0, 0, 0);
-    if (j + 1 < nw) xget<XK>(xs, g.xg, (W.k0 + (i + kWarps) % W.kq) * 8 + gg, X, nh, nl);
+    if (j + 1 < nw) xget(x, xf32, (W.k0 + nkk) * 8 + gg, X, nh, nl);
     const uint32_t s = R.cnt % kStages;
     const bool tw = A.trace && blockIdx.x == 0 && warp == 0 && lane == 0;
     const unsigned long long tw0 = tw ? globaltimer_ns() : 0ull;
     if (R.ok) R.ok = mbar_wait(&R.full[s], (R.cnt / kStages) & 1u, A.status);
     if (tw) R.wait_ns += globaltimer_ns() - tw0;
-    if (R.ok) quantum_mma<XK == XK_SMEM_F32>(R.base + s * kQuantumBytes, xh, xl, L, gg, t, acc);
+    if (R.ok) quantum_mma_rt(R.base + s * kQuantumBytes, xh, xl, L, gg, t, acc, xf32);
     R.cnt++;
     // every lane's shared-memory reads of the stage are complete (their values
     // fed the MMAs) before the TMA unit overwrites it
@@ -392,7 +405,7 @@ E4B_DEV void gemv_phase(const MkArgs& A, const MkGemv& g, const Work& W, int war
     }
     xh = nh;
     xl = nl;
-    if (j + 1 == nw || (i + kWarps) / W.kq != tl) {
+    if (j + 1 == nw || ntl != tl) {
       float v[4];
 #pragma unroll
       for (int r = 0; r < 4; r++) {
@@ -409,6 +422,8 @@ E4B_DEV void gemv_phase(const MkArgs& A, const MkGemv& g, const Work& W, int war
         pp[24 + gg] = v[3];
       }
     }
+    tl = ntl;
+    kk = nkk;
   }
 }
 
@@ -453,14 +468,32 @@ E4B_DEV void gemv_epilogue(const MkGemv& g, const Work& W, const float* P) {
 }
 
 // ------------------------------------------------------------------ prologues
-// h = (h + t * rms(t) * w) * mul (kernels/rmsacc.wgsl); all loads of t first.
-E4B_DEV void residual(const MkArgs& A, const MkPhase& P, float* hs, const float* rw, float* red) {
-  float tv[kMaxPer];
+// v[k] = row tid + 256 k of a GEMV output (sum of its s <= 2 partials), for the
+// rows below n; every load is issued before any of them is used.
+E4B_DEV void slot_rows(const SlotSrc& S, int n, float (&v)[kMaxPer]) {
+  float b[kMaxPer];
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) {
     const int i = threadIdx.x + k * kThreads;
-    tv[k] = i < A.H ? slot_sum(P.rt, i) : 0.f;
+    v[k] = 0.f;
+    b[k] = 0.f;
+    if (i < n) v[k] = __ldcg(S.buf + (size_t)(i >> 5) * S.s * 32 + (i & 31));
   }
+  if (S.s > 1) {
+#pragma unroll
+    for (int k = 0; k < kMaxPer; k++) {
+      const int i = threadIdx.x + k * kThreads;
+      if (i < n) b[k] = __ldcg(S.buf + (size_t)(i >> 5) * S.s * 32 + 32 + (i & 31));
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxPer; k++) v[k] += b[k];
+  }
+}
+
+// h = (h + t * rms(t) * w) * mul (kernels/rmsacc.wgsl).
+E4B_DEV void residual(const MkArgs& A, const MkPhase& P, float* hs, const float* rw, float* red) {
+  float tv[kMaxPer];
+  slot_rows(P.rt, A.H, tv);
   float s = 0.f;
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) s = fmaf(tv[k], tv[k], s);
@@ -500,38 +533,53 @@ E4B_DEV void build_x_attn(const MkArgs& A, const MkPhase& P, const Work& W, uint
   const Rule rule = make_rule(a, A.params);
   int CH, nch;
   chunking(rule.nslots(), a.nct, CH, nch);
-  float* ew = scr;                     // [QH][nct]: e^(m_c - M), 0 for empty chunks
-  float* dens = scr + A.QH * a.nct;    // [QH]: sum_c l_c e^(m_c - M)
+  float* mm = scr;                       // [QH][nct]: chunk maxima, then e^(m_c - M) (0: empty chunk)
+  float* ll = scr + A.QH * a.nct;        // [QH][nct]: chunk sums
+  float* dens = ll + A.QH * a.nct;       // [QH]
+  for (int i = threadIdx.x; i < A.QH * nch; i += kThreads) {
+    const int h = i / nch, k = i - h * nch;
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + (size_t)h * a.nct + k);
+    mm[h * a.nct + k] = ml.x;
+    ll[h * a.nct + k] = ml.y;
+  }
+  __syncthreads();
   for (int h = threadIdx.x; h < A.QH; h += kThreads) {
-    const float* ml = a.part_ml + (size_t)h * a.nct * 2;
+    float* m = mm + h * a.nct;
+    const float* l = ll + h * a.nct;
     float M = -INFINITY;
     for (int k = 0; k < nch; k++)
-      if (__ldcg(ml + 2 * k + 1) > 0.f) M = fmaxf(M, __ldcg(ml + 2 * k));
+      if (l[k] > 0.f) M = fmaxf(M, m[k]);
     float den = 0.f;
     for (int k = 0; k < nch; k++) {
-      const float l = __ldcg(ml + 2 * k + 1);
-      const float e = l > 0.f ? expf(__ldcg(ml + 2 * k) - M) : 0.f;
-      den += l > 0.f ? l * e : 0.f;
-      ew[h * a.nct + k] = e;
+      const float e = l[k] > 0.f ? expf(m[k] - M) : 0.f;
+      den += l[k] > 0.f ? l[k] * e : 0.f;
+      m[k] = e;
     }
     dens[h] = den;
   }
   __syncthreads();
-  // four consecutive elements (same head) per step, float4 partial loads
+  // four consecutive elements (same head) per step; chunk loads in groups of 4
   const int n4 = W.kq * 64;
   for (int idx = threadIdx.x; idx < n4; idx += kThreads) {
     const int e = 256 * W.k0 + 4 * idx;
     if (e >= A.qdim) continue;
     const int h = e / A.HD, d = e - h * A.HD;
-    const float* w = ew + h * a.nct;
+    const float* w = mm + h * a.nct;
     const float4* po = reinterpret_cast<const float4*>(a.part_o + (size_t)h * a.nct * A.HD + d);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < nch; k++) {
-      const float4 o = __ldcg(po + (size_t)k * (A.HD / 4));
-      acc.x = fmaf(o.x, w[k], acc.x);
-      acc.y = fmaf(o.y, w[k], acc.y);
-      acc.z = fmaf(o.z, w[k], acc.z);
-      acc.w = fmaf(o.w, w[k], acc.w);
+    for (int k0 = 0; k0 < nch; k0 += 4) {
+      float4 o[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        o[u] = k0 + u < nch ? __ldcg(po + (size_t)(k0 + u) * (A.HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        if (k0 + u >= nch) break;
+        acc.x = fmaf(o[u].x, w[k0 + u], acc.x);
+        acc.y = fmaf(o[u].y, w[k0 + u], acc.y);
+        acc.z = fmaf(o[u].z, w[k0 + u], acc.z);
+        acc.w = fmaf(o[u].w, w[k0 + u], acc.w);
+      }
     }
     const float den = dens[h];
     xs[e] = f2h(den > 0.f ? acc.x / den : 0.f);
@@ -544,28 +592,36 @@ E4B_DEV void build_x_attn(const MkArgs& A, const MkPhase& P, const Work& W, uint
 // PLE input of layer l (kernels/pleprep.wgsl) times GeGLU of the gate GEMV:
 // x[o] = f16(gelu(gate[o]) * ((p_o rms(p) nw[o] + table[tok][l PD + o] sqrt(PD)) / sqrt 2)), p = Wp h / sqrt(H).
 E4B_DEV void build_x_ple(const MkArgs& A, const MkPhase& P, const float* nw, uint16_t* xs, float* red) {
-  float pv[kMaxPer], gv[kMaxPer];
+  float pv[kMaxPer], gv[kMaxPer], idv[kMaxPer];
   const int base = P.layer * A.PD;
-#pragma unroll
-  for (int k = 0; k < kMaxPer; k++) {
-    const int o = threadIdx.x + k * kThreads;
-    pv[k] = o < A.PD ? slot_sum(A.pleproj, base + o) * A.proj_scale : 0.f;
-    gv[k] = o < A.PD ? slot_sum(P.ple_gate, o) : 0.f;
-  }
-  float s = 0.f;
-#pragma unroll
-  for (int k = 0; k < kMaxPer; k++) s = fmaf(pv[k], pv[k], s);
-  const float inv = rms_scale(block_sum(s, red), A.PD, A.eps);
   const uint32_t row = __ldcg(A.params + 2);
   const bool tok_ok = row < (uint32_t)A.V;
   const uint8_t* r = A.ple_table + (size_t)(tok_ok ? row : 0) * ((size_t)A.L * A.PD / 256) * 210;
+  // issue every load first: projection and gate partials, table weights
+  const SlotSrc pp{A.pleproj.buf + (size_t)(base >> 5) * A.pleproj.s * 32, A.pleproj.s};
+  slot_rows(pp, A.PD, pv);
+  slot_rows(P.ple_gate, A.PD, gv);
+#pragma unroll
+  for (int k = 0; k < kMaxPer; k++) {
+    const int o = threadIdx.x + k * kThreads;
+    idv[k] = 0.f;
+    if (o < A.PD && tok_ok) {
+      const int gi = base + o;
+      idv[k] = q6k_elem(r + (size_t)(gi >> 8) * 210, gi & 255);
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxPer; k++) {
+    pv[k] *= A.proj_scale;
+    s = fmaf(pv[k], pv[k], s);
+  }
+  const float inv = rms_scale(block_sum(s, red), A.PD, A.eps);
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) {
     const int o = threadIdx.x + k * kThreads;
     if (o < A.PD) {
-      const int gi = base + o;
-      const float idv = tok_ok ? q6k_elem(r + (size_t)(gi >> 8) * 210, gi & 255) * A.ple_mult : 0.f;
-      const float ple = (pv[k] * inv * nw[o] + idv) * 0.70710678118654752f;
+      const float ple = (pv[k] * inv * nw[o] + idv[k] * A.ple_mult) * 0.70710678118654752f;
       xs[o] = f2h(gelu_tanh(gv[k]) * ple);
     }
   }
@@ -577,8 +633,8 @@ E4B_DEV void build_x_ple(const MkArgs& A, const MkPhase& P, const float* nw, uin
 // softmax and p.V over the chunk (kernels/headprep.wgsl + attsplit.wgsl).
 // Scores: 4 threads per slot, 16-byte K loads; p.V: each thread 8 dims of a
 // slot subset, 16-byte V loads, then a shared-memory reduction over subsets.
-E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const float* qn, const float* kn, float* scr,
-                             float* red) {
+E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const float* qn, const float* kn,
+                             const float* rope_tab, float* scr, float* red) {
   const Rule rule = make_rule(a, A.params);
   const uint32_t nslots = rule.nslots();
   int CH, nch;
@@ -625,9 +681,9 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
     uint16_t* kcw = a.kc + ((size_t)cur * A.KVH + kvh) * HD;
     uint16_t* vcw = a.vc + ((size_t)cur * A.KVH + kvh) * HD;
     for (int p = tid; p < half; p += kThreads) {
-      float sn = 0.f, cs = 1.f;
       const bool rot = p < a.angles;
-      if (rot) sincosf(rope_angle(qp, p, HD, a.theta), &sn, &cs);
+      const float cs = rot ? rope_tab[(2 * a.rope) * half + p] : 1.f;
+      const float sn = rot ? rope_tab[(2 * a.rope + 1) * half + p] : 0.f;
       const float x0 = qs[p] * qinv * qn[p];
       const float x1 = qs[p + half] * qinv * qn[p + half];
       qs[p] = rot ? x0 * cs - x1 * sn : x0;
@@ -652,9 +708,10 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
       }
     }
     __syncthreads();
-    // scores: 4 threads per slot, each a quarter of the dims in 8-dim vectors
+    // scores: 4 threads per slot, each a quarter of the dims in 16-byte vectors
+    // (loaded in groups of 8 before use)
     {
-      const int part = tid & 3, q4 = HD / 4;
+      const int part = tid & 3, q4 = HD / 4, nv = q4 / 8;
       for (int sb = 0; sb < CH; sb += kThreads / 4) {
         const int tt = sb + (tid >> 2);
         const uint32_t ts = t0 + (uint32_t)tt;
@@ -665,15 +722,22 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
             for (int d = part * q4; d < (part + 1) * q4; d++) acc = fmaf(qs[d], kcur[d], acc);
           } else {
             const uint4* kr = reinterpret_cast<const uint4*>(a.kc + ((size_t)ts * A.KVH + kvh) * HD + part * q4);
-            for (int v8 = 0; v8 < q4 / 8; v8++) {
-              const uint4 kw = kr[v8];
-              const float* qd = qs + part * q4 + 8 * v8;
-              const __half2* k2 = reinterpret_cast<const __half2*>(&kw);
+            for (int v0 = 0; v0 < nv; v0 += 8) {
+              uint4 kw[8];
 #pragma unroll
-              for (int e = 0; e < 4; e++) {
-                const float2 kf = __half22float2(k2[e]);
-                acc = fmaf(qd[2 * e], kf.x, acc);
-                acc = fmaf(qd[2 * e + 1], kf.y, acc);
+              for (int u = 0; u < 8; u++)
+                if (v0 + u < nv) kw[u] = kr[v0 + u];
+#pragma unroll
+              for (int u = 0; u < 8; u++) {
+                if (v0 + u >= nv) break;
+                const float* qd = qs + part * q4 + 8 * (v0 + u);
+                const __half2* k2 = reinterpret_cast<const __half2*>(&kw[u]);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                  const float2 kf = __half22float2(k2[e]);
+                  acc = fmaf(qd[2 * e], kf.x, acc);
+                  acc = fmaf(qd[2 * e + 1], kf.y, acc);
+                }
               }
             }
           }
@@ -701,20 +765,34 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
       const int dg = tid % ndg, sg = tid / ndg;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       const uint32_t hi = min(t0 + (uint32_t)CH, nslots);
-      for (uint32_t ts = t0 + (uint32_t)sg; ts < hi; ts += (uint32_t)nsg) {
-        const float p = sc[ts - t0];
-        if (p == 0.f) continue;
-        if (has_cur && ts == cur) {
+      // four slots per step, their V vectors loaded before use
+      for (uint32_t ts0 = t0 + (uint32_t)sg; ts0 < hi; ts0 += 4u * (uint32_t)nsg) {
+        uint4 vw[4];
+        float pu[4];
 #pragma unroll
-          for (int e = 0; e < 8; e++) acc[e] = fmaf(p, vcur[8 * dg + e], acc[e]);
-        } else {
-          const uint4 vw = *reinterpret_cast<const uint4*>(a.vc + ((size_t)ts * A.KVH + kvh) * HD + 8 * dg);
-          const __half2* v2 = reinterpret_cast<const __half2*>(&vw);
+        for (int u = 0; u < 4; u++) {
+          const uint32_t ts = ts0 + (uint32_t)(u * nsg);
+          pu[u] = ts < hi ? sc[ts - t0] : 0.f;
+          vw[u] = make_uint4(0, 0, 0, 0);
+          if (pu[u] != 0.f && !(has_cur && ts == cur))
+            vw[u] = *reinterpret_cast<const uint4*>(a.vc + ((size_t)ts * A.KVH + kvh) * HD + 8 * dg);
+        }
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const float2 vf = __half22float2(v2[e]);
-            acc[2 * e] = fmaf(p, vf.x, acc[2 * e]);
-            acc[2 * e + 1] = fmaf(p, vf.y, acc[2 * e + 1]);
+        for (int u = 0; u < 4; u++) {
+          const uint32_t ts = ts0 + (uint32_t)(u * nsg);
+          const float p = pu[u];
+          if (p == 0.f) continue;
+          if (has_cur && ts == cur) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[e] = fmaf(p, vcur[8 * dg + e], acc[e]);
+          } else {
+            const __half2* v2 = reinterpret_cast<const __half2*>(&vw[u]);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const float2 vf = __half22float2(v2[e]);
+              acc[2 * e] = fmaf(p, vf.x, acc[2 * e]);
+              acc[2 * e + 1] = fmaf(p, vf.y, acc[2 * e + 1]);
+            }
           }
         }
       }
@@ -775,6 +853,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(phs + 3);
   float* red = reinterpret_cast<float*>(bars + kWarps * kStages);
   volatile int* flag = reinterpret_cast<volatile int*>(red + 32);
+  float* rope_tab = red + 36;   // [nrope][cos, sin][HD / 2]
   constexpr int kPh16 = (int)(sizeof(MkPhase) / 16);
   auto fetch_desc = [&](int p) {   // descriptor p -> phs[p % 3], asynchronously
     const uint8_t* src = reinterpret_cast<const uint8_t*>(A.ph + p);
@@ -801,7 +880,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
   for (int s = 0; s < kStages && u.idx < u.end; s++) {
     prod_issue(A, u, R.base + s * kQuantumBytes, &R.full[s], warp, lane, pol);
     R.issued++;
-    prod_advance(A, pf);
+    prod_advance(A, pf, warp);
   }
   for (int s = 0; s < kPrefetch && pf.idx < pf.end; s++) prod_prefetch(A, pf, warp, lane);
 
@@ -819,6 +898,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
       const uint8_t* r = A.ple_table + (size_t)row * rb;
       for (size_t o = (size_t)threadIdx.x * 128; o < rb + 128; o += (size_t)kThreads * 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(r + (o < rb ? o : rb - 1)));
+    }
+  }
+
+  // RoPE cos / sin of this token's position for every layer kind
+  // (kernels/headprep.wgsl:55: theta_p = pos * THETA^(-2p/HD))
+  {
+    const uint32_t pos = __ldcg(A.params + 0);
+    const int half = A.HD / 2;
+    for (int i = threadIdx.x; i < A.nrope * half; i += kThreads) {
+      const int r = i / half, p = i - r * half;
+      float sn = 0.f, cs = 1.f;
+      if (p < A.rope_angles[r]) sincosf(rope_angle(pos, p, A.HD, A.rope_theta[r]), &sn, &cs);
+      rope_tab[2 * r * half + p] = cs;
+      rope_tab[(2 * r + 1) * half + p] = sn;
     }
   }
 
@@ -860,13 +953,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
       break;
     }
     if (P.kind == PH_ATTN) {
-      attention_phase(A, P.a, c, wbuf + 2 * A.H, wbuf + 2 * A.H + A.HD, scr, red);
+      attention_phase(A, P.a, c, wbuf + 2 * A.H, wbuf + 2 * A.H + A.HD, rope_tab, scr, red);
       __syncthreads();
       if (p + 1 < A.nph) stage_vectors(A, phs[(p + 1) % 3], wbuf);
     } else {
       const Work W = cta_work(P.g, A.G, c);
       // prologue: activations of this GEMV (only CTAs with work in it)
       if (W.nt > 0) {
+        if (P.g.xk == XK_STAGED_F16) {   // the CTA's k-range of a global f16 input
+          const uint16_t* src = P.g.xg + 256 * W.k0;
+          for (int i = threadIdx.x; i < W.kq * 32; i += kThreads) cp_async16(xs + 16 * i, src + 8 * i);
+          cp_async_commit();
+          cp_async_wait_all();
+        }
         if (P.xb == XB_NORM || P.xb == XB_RAW)
           build_x_norm(A, hs, wbuf + A.H, reinterpret_cast<uint16_t*>(xs), red, P.xb == XB_NORM);
         else if (P.xb == XB_ATTN)
@@ -878,9 +977,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
       __syncthreads();
       if (p + 1 < A.nph) stage_vectors(A, phs[(p + 1) % 3], wbuf);
       if (tr) A.trace[8 * p + 2] = globaltimer_ns();
-      if (P.g.xk == XK_SMEM_F32) gemv_phase<XK_SMEM_F32>(A, P.g, W, warp, lane, R, u, pf, pol, hs, scr);
-      else if (P.g.xk == XK_GLOBAL_F16) gemv_phase<XK_GLOBAL_F16>(A, P.g, W, warp, lane, R, u, pf, pol, xs, scr);
-      else gemv_phase<XK_SMEM_F16>(A, P.g, W, warp, lane, R, u, pf, pol, xs, scr);
+      {
+        const bool xf32 = P.g.xk == XK_SMEM_F32;
+        const void* xp = xf32 ? static_cast<const void*>(hs)
+                              : (P.g.xk == XK_STAGED_F16   // staged block k0 sits at xs[0]
+                                     ? static_cast<const void*>(reinterpret_cast<uint16_t*>(xs) - 256 * W.k0)
+                                     : static_cast<const void*>(xs));
+        if (xf32) gemv_phase<true>(A, W, warp, lane, R, u, pf, pol, xp, scr);
+        else gemv_phase<false>(A, W, warp, lane, R, u, pf, pol, xp, scr);
+      }
       if (!R.ok) *flag = 0;    // every writer stores the same value
       __syncthreads();
       if (tr) {
@@ -952,11 +1057,11 @@ void plan_free(DensePlan* p) {
 }
 
 // k-split of a GEMV: 1 for the gate|up GEMV (GeGLU needs whole sums) and
-// whenever there are at least G/2 tiles; else as many splits as fit the grid
-// while every split keeps >= 8 quanta (one per warp).
+// whenever there are at least G/2 tiles; else as many splits (at most 2, the
+// consumers' load pattern) as fit the grid while every split keeps >= 8 quanta.
 int split_for(int T, int qpr, int gu, int G) {
   if (gu) return 1;
-  return std::max(1, std::min(G / T, qpr / 8));
+  return std::max(1, std::min(std::min(G / T, qpr / 8), 2));
 }
 
 struct Builder {
@@ -1183,6 +1288,15 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
     at.nct = nct;
     at.theta = ly.theta;
     at.scale = 1.0f;
+    at.rope = -1;
+    for (int r = 0; r < A.nrope; r++)
+      if (A.rope_theta[r] == ly.theta && A.rope_angles[r] == ly.rope_angles) at.rope = r;
+    if (at.rope < 0) {
+      if (A.nrope == kMaxRope) return fail(e4b_fail(c, E4B_EINVAL, "dense plan: more than %d RoPE kinds", kMaxRope));
+      A.rope_theta[A.nrope] = ly.theta;
+      A.rope_angles[A.nrope] = ly.rope_angles;
+      at.rope = A.nrope++;
+    }
     b.ph.back().a = at;   // the q|k|v phase prefetches this layer's cache
     {
       MkPhase& P = b.add(PH_ATTN);
@@ -1207,7 +1321,7 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
     {   // down
       MkPhase& P = b.add(PH_GEMV);
       P.xb = XB_NONE;
-      if ((rc = b.gemv(P, ly.down, FF, H, 0, 0, XK_GLOBAL_F16, geglu, td_s, nullptr, &td_src))) return fail(rc);
+      if ((rc = b.gemv(P, ly.down, FF, H, 0, 0, XK_STAGED_F16, geglu, td_s, nullptr, &td_src))) return fail(rc);
     }
     if (PD) {
       {   // PLE gate: h += rms(t_d) post_ffw; x = f16(h)
@@ -1308,12 +1422,18 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
   // ---- shared memory
   int maxCH = 32, nch_unused = 0;
   chunking((uint32_t)max_slots, nct, maxCH, nch_unused);
-  const size_t xs_bytes = ((size_t)std::max(std::max(2 * H, 2 * qdim), 2 * std::max(PD, 1)) + 127) & ~(size_t)127;
+  size_t xs_need = (size_t)std::max(std::max(2 * H, 2 * qdim), 2 * std::max(PD, 1));
+  for (const MkPhase& P : b.ph)
+    if (P.kind == PH_GEMV && P.g.xk == XK_STAGED_F16)
+      for (int cc = 0; cc < G; cc++)
+        xs_need = std::max(xs_need, (size_t)512 * cta_work(P.g.T, P.g.qpr, P.g.s, P.g.rot, G, cc).kq);
+  const size_t xs_bytes = (xs_need + 127) & ~(size_t)127;
   const size_t scr_bytes =
       (std::max(std::max((size_t)max_tiles * kWarps * 32 * 4, (size_t)(3 * HD + kThreads * 8 + maxCH) * 4),
                 (size_t)(QH * nct + QH) * 4) + 127) & ~(size_t)127;
   const size_t smem = (size_t)kWarps * kStages * kQuantumBytes + (size_t)H * 4 + xs_bytes + scr_bytes +
-                      (size_t)(2 * H + 2 * HD) * 4 + 3 * sizeof(MkPhase) + (size_t)kWarps * kStages * 8 + 33 * 4 + 16;
+                      (size_t)(2 * H + 2 * HD) * 4 + 3 * sizeof(MkPhase) + (size_t)kWarps * kStages * 8 + 36 * 4 +
+                      (size_t)kMaxRope * HD * 4 + 16;
   A.xs_bytes = (int)xs_bytes;
   A.scr_bytes = (int)scr_bytes;
   e = cudaFuncSetAttribute(k_decode_dense, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
