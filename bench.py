@@ -436,6 +436,8 @@ def run_trace(args):
         if name != "attention":
             row.update({"input": m(1, 2), "gemv": m(2, 3), "weight_wait": round(float((t[sel, 7] / 1e3).mean()), 2),
                         "epilogue": m(3, 4)})
+        else:   # CTA 0's first item: q/k/v prep, scores + softmax, p.V + partials
+            row.update({"prep": m(1, 2), "scores_softmax": m(2, 3), "pv": m(3, 4)})
         out["kinds"][name] = row
     eng.close()
     print(json.dumps(out))

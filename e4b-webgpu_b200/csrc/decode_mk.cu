@@ -66,20 +66,24 @@ constexpr int kMaxRope = 4;           // distinct (theta, rotated pairs) layer k
 enum : int { EPI_SLOTS = 0, EPI_GEGLU = 1 };
 
 // A GEMV output as partials: buf[row / 32][s][row % 32]; the value of a row is
-// the in-order sum of its s partials.
+// the in-order sum of its s partials.  Every partial is published as one 64-bit
+// word (epoch << 32 | f32 bits), epoch = token counter * 256 + tag, tag = the
+// producing layer (255: the per-token PLE projection), so a consumer polls
+// exactly the words it needs instead of waiting at a grid barrier.
 struct SlotSrc {
-  const float* buf;
-  int s;
+  const uint64_t* buf;
+  int s, tag;
 };
 
 struct MkGemv {
   int T, qpr, s, rot;   // tiles, quanta per tile, k-splits, CTA rotation
   int gu, ff;           // gate|up row layout: subtile 1 rows start at ff
   int xk;               // XK_*
-  const uint16_t* xg;   // XK_STAGED_F16: global f16 x, the CTA's k-range is staged in shared memory
-  int epi;
-  float* out;           // EPI_SLOTS: [T][s][32]
-  uint16_t* outh;       // EPI_GEGLU: [ff]
+  const uint32_t* xg;   // XK_STAGED_F16: global f16 x as (epoch16 << 16 | f16) words; the CTA's k-range is staged
+  int xtag;             // producing layer of xg
+  int epi, tag;         // tag: this layer (epoch of the outputs)
+  uint64_t* out;        // EPI_SLOTS: [T][s][32] epoch words
+  uint32_t* outh;       // EPI_GEGLU: [ff] (epoch16 << 16 | f16) words
 };
 
 struct MkAttn {
@@ -88,9 +92,11 @@ struct MkAttn {
   const float* kn;
   uint16_t* kc;
   uint16_t* vc;
-  float* part_o;        // [QH][nct][HD]
-  float* part_ml;       // [QH][nct][2]
-  int cachemode, ring, window, slots, angles, keqv, nct;
+  float* part_o;        // [QH][nct][HD] chunk partials (unnormalised)
+  float* part_ml;       // [QH][nct][2] chunk max and sum
+  unsigned* cnt;        // [QH] finished chunks per head (zero at rest)
+  uint32_t* out;        // [QH * HD] combined head outputs, (epoch16 << 16 | f16) words
+  int cachemode, ring, window, slots, angles, keqv, nct, tag;
   int rope;             // index into the per-token RoPE table
   float theta, scale;
 };
@@ -98,6 +104,7 @@ struct MkAttn {
 struct alignas(16) MkPhase {
   int kind;
   int kvpf;             // prefetch this layer's KV cache into L2 (q|k|v phase)
+  int sync_after;       // grid barrier at the end of the phase (last phase of a layer)
   int res;              // residual first: h = (h + rms(t) * rw) * rmul, t from rt
   SlotSrc rt;
   const float* rw;
@@ -131,7 +138,7 @@ struct MkArgs {
   const float* out_norm;
   const uint32_t* params;
   uint32_t* status;
-  unsigned* bar;        // [0] arrivals, [1] finished CTAs (zero at rest)
+  unsigned* bar;        // [0] arrivals, [1] finished CTAs (zero at rest), [2] token counter, [3] abort flag
   float* xf;
   float* hout;
   unsigned long long* trace;   // optional [nph][8] globaltimer stamps (see e4b_dense_plan_trace)
@@ -140,6 +147,30 @@ struct MkArgs {
   float rope_theta[kMaxRope];
   int rope_angles[kMaxRope];
 };
+
+// ------------------------------------------------------------------ CTA reductions
+// Sum / max over the CTA: warp shuffles, one barrier, then every thread reads
+// the 8 warp results as two 16-byte words (no serial chain); a trailing
+// barrier frees `sh` (16-byte aligned, >= 8 floats) for the next reduction.
+E4B_DEV float cta_sum(float v, float* sh) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const float4 a = reinterpret_cast<const float4*>(sh)[0], b = reinterpret_cast<const float4*>(sh)[1];
+  const float t = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+  __syncthreads();
+  return t;
+}
+E4B_DEV float cta_max(float v, float* sh) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const float4 a = reinterpret_cast<const float4*>(sh)[0], b = reinterpret_cast<const float4*>(sh)[1];
+  const float t = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(b.x, b.y), fmaxf(b.z, b.w)));
+  __syncthreads();
+  return t;
+}
+static_assert(kWarps == 8, "cta_sum / cta_max read exactly 8 warp results");
 
 // ------------------------------------------------------------------ partition
 struct Work {
@@ -170,10 +201,72 @@ __host__ __device__ inline int warp_items(const Work& w, int warp) {
 
 E4B_DEV Work cta_work(const MkGemv& g, int G, int c) { return cta_work(g.T, g.qpr, g.s, g.rot, G, c); }
 
-E4B_DEV float slot_sum(const SlotSrc& S, int row) {
-  const float* b = S.buf + (size_t)(row >> 5) * S.s * 32 + (row & 31);
-  float v = __ldcg(b);
-  for (int k = 1; k < S.s; k++) v += __ldcg(b + 32 * k);
+// ---- epoch-tagged publication (flag-in-data)
+E4B_DEV void st_ll64(uint64_t* p, float v, uint32_t e) {
+  const uint64_t w = ((uint64_t)e << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+E4B_DEV void st_ll32(uint32_t* p, uint16_t h, uint32_t e) {
+  const uint32_t w = (e << 16) | h;
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
+}
+E4B_DEV uint64_t ld_ll64(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Two epoch words (each loaded as one 64-bit element: value and epoch never tear).
+E4B_DEV void ld_ll64x2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// Four 32-bit (epoch16 << 16 | f16) words.
+E4B_DEV uint4 ld_ll32x4(const uint32_t* p) {
+  uint4 w;
+  asm volatile("ld.relaxed.gpu.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+               : "l"(p)
+               : "memory");
+  return w;
+}
+E4B_DEV uint32_t ep_of(uint64_t w) { return (uint32_t)(w >> 32); }
+E4B_DEV float val_of(uint64_t w) { return __uint_as_float((uint32_t)w); }
+
+// Bounded polling: gives up after ~1 s (status TIMEOUT) or when another CTA
+// has given up (abort flag), returning false.
+struct Spin {
+  uint32_t it = 0;
+  uint64_t t0 = 0;
+};
+E4B_DEV bool spin_more(Spin& sp, const MkArgs& A) {
+  ++sp.it;
+  if (sp.it == 8) sp.t0 = globaltimer_ns();
+  if (sp.it > 8 && (sp.it & 7u) == 0) {
+    unsigned ab;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ab) : "l"(A.bar + 3) : "memory");
+    if (ab) return false;
+    if (globaltimer_ns() - sp.t0 > 1000000000ull) {
+      set_status(A.status, E4B_ST_TIMEOUT);
+      atomicExch(A.bar + 3, 1u);
+      return false;
+    }
+  }
+  return true;
+}
+
+// One output row (sum of its s partials), polled until published.
+E4B_DEV float ll_row(const MkArgs& A, const SlotSrc& S, int row, uint32_t ebase, bool& dead) {
+  const uint64_t* b = S.buf + (size_t)(row >> 5) * S.s * 32 + (row & 31);
+  const uint32_t e = ebase + (uint32_t)S.tag;
+  float v = 0.f;
+  for (int k = 0; k < S.s; k++) {
+    uint64_t w = ld_ll64(b + 32 * k);
+    Spin sp;
+    while (ep_of(w) != e && !dead) {
+      if (!spin_more(sp, A)) dead = true;
+      w = ld_ll64(b + 32 * k);
+    }
+    v = k == 0 ? val_of(w) : v + val_of(w);
+  }
   return v;
 }
 
@@ -437,7 +530,8 @@ E4B_DEV uint32_t warps_of_tile(const Work& W, int tl) {
 }
 
 // CTA-wide: sum the warps' partials per tile (in warp order) and publish.
-E4B_DEV void gemv_epilogue(const MkGemv& g, const Work& W, const float* P) {
+E4B_DEV void gemv_epilogue(const MkGemv& g, const Work& W, const float* P, uint32_t ebase) {
+  const uint32_t ep = ebase + (uint32_t)g.tag;
   if (g.epi == EPI_GEGLU) {
     for (int idx = threadIdx.x; idx < W.nt * 16; idx += kThreads) {
       const int tl = idx >> 4, r = idx & 15;
@@ -450,8 +544,8 @@ E4B_DEV void gemv_epilogue(const MkGemv& g, const Work& W, const float* P) {
         gv += pp[w * 32 + r];
         uv += pp[w * 32 + 16 + r];
       }
-      const int e = 16 * (W.t0 + tl) + r;
-      if (e < g.ff) g.outh[e] = f2h(gelu_tanh(gv) * uv);
+      const int o = 16 * (W.t0 + tl) + r;
+      if (o < g.ff) st_ll32(g.outh + o, f2h(gelu_tanh(gv) * uv), ep);
     }
   } else {
     for (int idx = threadIdx.x; idx < W.nt * 32; idx += kThreads) {
@@ -462,42 +556,62 @@ E4B_DEV void gemv_epilogue(const MkGemv& g, const Work& W, const float* P) {
 #pragma unroll
       for (int w = 0; w < kWarps; w++)
         if (wm >> w & 1u) v += pp[w * 32 + r];
-      g.out[((size_t)(W.t0 + tl) * g.s + W.sp) * 32 + r] = v;
+      st_ll64(g.out + ((size_t)(W.t0 + tl) * g.s + W.sp) * 32 + r, v, ep);
     }
   }
 }
 
 // ------------------------------------------------------------------ prologues
 // v[k] = row tid + 256 k of a GEMV output (sum of its s <= 2 partials), for the
-// rows below n; every load is issued before any of them is used.
-E4B_DEV void slot_rows(const SlotSrc& S, int n, float (&v)[kMaxPer]) {
-  float b[kMaxPer];
+// rows below n; every load is issued before any is checked, stale words
+// (older epoch) are re-read until published.
+E4B_DEV void slot_rows(const MkArgs& A, const SlotSrc& S, int n, uint32_t ebase, float (&v)[kMaxPer], bool& dead) {
+  uint64_t a[kMaxPer], b[kMaxPer];
+  const uint32_t e = ebase + (uint32_t)S.tag;
+  const bool two = S.s > 1;
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) {
     const int i = threadIdx.x + k * kThreads;
-    v[k] = 0.f;
-    b[k] = 0.f;
-    if (i < n) v[k] = __ldcg(S.buf + (size_t)(i >> 5) * S.s * 32 + (i & 31));
+    a[k] = b[k] = (uint64_t)e << 32;
+    if (i < n) {
+      const uint64_t* p = S.buf + (size_t)(i >> 5) * S.s * 32 + (i & 31);
+      a[k] = ld_ll64(p);
+      if (two) b[k] = ld_ll64(p + 32);
+    }
   }
-  if (S.s > 1) {
+  Spin sp;
+  for (;;) {
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < kMaxPer; k++) ok = ok && ep_of(a[k]) == e && ep_of(b[k]) == e;
+    if (ok || dead) break;
+    if (!spin_more(sp, A)) {
+      dead = true;
+      break;
+    }
 #pragma unroll
     for (int k = 0; k < kMaxPer; k++) {
       const int i = threadIdx.x + k * kThreads;
-      if (i < n) b[k] = __ldcg(S.buf + (size_t)(i >> 5) * S.s * 32 + 32 + (i & 31));
+      if (i >= n) continue;
+      const uint64_t* p = S.buf + (size_t)(i >> 5) * S.s * 32 + (i & 31);
+      if (ep_of(a[k]) != e) a[k] = ld_ll64(p);
+      if (two && ep_of(b[k]) != e) b[k] = ld_ll64(p + 32);
     }
-#pragma unroll
-    for (int k = 0; k < kMaxPer; k++) v[k] += b[k];
   }
+#pragma unroll
+  for (int k = 0; k < kMaxPer; k++) v[k] = two ? val_of(a[k]) + val_of(b[k]) : val_of(a[k]);
 }
 
 // h = (h + t * rms(t) * w) * mul (kernels/rmsacc.wgsl).
-E4B_DEV void residual(const MkArgs& A, const MkPhase& P, float* hs, const float* rw, float* red) {
+E4B_DEV void residual(const MkArgs& A, const MkPhase& P, float* hs, const float* rw, float* red, uint32_t ebase,
+                      bool& dead) {
   float tv[kMaxPer];
-  slot_rows(P.rt, A.H, tv);
+  slot_rows(A, P.rt, A.H, ebase, tv, dead);
   float s = 0.f;
 #pragma unroll
-  for (int k = 0; k < kMaxPer; k++) s = fmaf(tv[k], tv[k], s);
-  const float inv = rms_scale(block_sum(s, red), A.H, A.eps);
+  for (int k = 0; k < kMaxPer; k++)
+    if (threadIdx.x + k * kThreads < A.H) s = fmaf(tv[k], tv[k], s);
+  const float inv = rms_scale(cta_sum(s, red), A.H, A.eps);
   const bool dump = P.dump && blockIdx.x == 0;
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) {
@@ -516,7 +630,7 @@ E4B_DEV void build_x_norm(const MkArgs& A, const float* hs, const float* w, uint
   if (norm) {
     float s = 0.f;
     for (int i = threadIdx.x; i < A.H; i += kThreads) s = fmaf(hs[i], hs[i], s);
-    inv = rms_scale(block_sum(s, red), A.H, A.eps);
+    inv = rms_scale(cta_sum(s, red), A.H, A.eps);
   }
   for (int i = threadIdx.x; i < A.H; i += kThreads) {
     float v = hs[i];
@@ -525,82 +639,38 @@ E4B_DEV void build_x_norm(const MkArgs& A, const float* hs, const float* w, uint
   }
 }
 
-// Attention combine for the columns the CTA's o-GEMV quanta read
-// (kernels/attcomb.wgsl): x[e] = sum_c o_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M).
-E4B_DEV void build_x_attn(const MkArgs& A, const MkPhase& P, const Work& W, uint16_t* xs, float* scr) {
+// The o-GEMV input: the combined attention outputs of the columns the CTA's
+// quanta read, polled until the attention phase published them.
+E4B_DEV void build_x_attn(const MkArgs& A, const MkPhase& P, const Work& W, uint16_t* xs, uint32_t ebase,
+                          bool& dead) {
   if (W.nt == 0) return;
-  const MkAttn& a = P.a;
-  const Rule rule = make_rule(a, A.params);
-  int CH, nch;
-  chunking(rule.nslots(), a.nct, CH, nch);
-  float* mm = scr;                       // [QH][nct]: chunk maxima, then e^(m_c - M) (0: empty chunk)
-  float* ll = scr + A.QH * a.nct;        // [QH][nct]: chunk sums
-  float* dens = ll + A.QH * a.nct;       // [QH]
-  for (int i = threadIdx.x; i < A.QH * nch; i += kThreads) {
-    const int h = i / nch, k = i - h * nch;
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + (size_t)h * a.nct + k);
-    mm[h * a.nct + k] = ml.x;
-    ll[h * a.nct + k] = ml.y;
-  }
-  __syncthreads();
-  for (int h = threadIdx.x; h < A.QH; h += kThreads) {
-    float* m = mm + h * a.nct;
-    const float* l = ll + h * a.nct;
-    float M = -INFINITY;
-    for (int k = 0; k < nch; k++)
-      if (l[k] > 0.f) M = fmaxf(M, m[k]);
-    float den = 0.f;
-    for (int k = 0; k < nch; k++) {
-      const float e = l[k] > 0.f ? expf(m[k] - M) : 0.f;
-      den += l[k] > 0.f ? l[k] * e : 0.f;
-      m[k] = e;
+  const uint32_t e16 = (ebase + (uint32_t)P.a.tag) & 0xFFFFu;
+  const uint32_t* src = P.a.out + 256 * W.k0;
+  for (int i = threadIdx.x; i < W.kq * 64; i += kThreads) {
+    if (256 * W.k0 + 4 * i >= A.qdim) break;
+    uint4 w = ld_ll32x4(src + 4 * i);
+    Spin sp;
+    while (((w.x >> 16) != e16 || (w.y >> 16) != e16 || (w.z >> 16) != e16 || (w.w >> 16) != e16) && !dead) {
+      if (!spin_more(sp, A)) dead = true;
+      w = ld_ll32x4(src + 4 * i);
     }
-    dens[h] = den;
-  }
-  __syncthreads();
-  // four consecutive elements (same head) per step; chunk loads in groups of 4
-  const int n4 = W.kq * 64;
-  for (int idx = threadIdx.x; idx < n4; idx += kThreads) {
-    const int e = 256 * W.k0 + 4 * idx;
-    if (e >= A.qdim) continue;
-    const int h = e / A.HD, d = e - h * A.HD;
-    const float* w = mm + h * a.nct;
-    const float4* po = reinterpret_cast<const float4*>(a.part_o + (size_t)h * a.nct * A.HD + d);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k0 = 0; k0 < nch; k0 += 4) {
-      float4 o[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++)
-        o[u] = k0 + u < nch ? __ldcg(po + (size_t)(k0 + u) * (A.HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        if (k0 + u >= nch) break;
-        acc.x = fmaf(o[u].x, w[k0 + u], acc.x);
-        acc.y = fmaf(o[u].y, w[k0 + u], acc.y);
-        acc.z = fmaf(o[u].z, w[k0 + u], acc.z);
-        acc.w = fmaf(o[u].w, w[k0 + u], acc.w);
-      }
-    }
-    const float den = dens[h];
-    xs[e] = f2h(den > 0.f ? acc.x / den : 0.f);
-    xs[e + 1] = f2h(den > 0.f ? acc.y / den : 0.f);
-    xs[e + 2] = f2h(den > 0.f ? acc.z / den : 0.f);
-    xs[e + 3] = f2h(den > 0.f ? acc.w / den : 0.f);
+    reinterpret_cast<uint2*>(xs + 256 * W.k0)[i] = make_uint2(__byte_perm(w.x, w.y, 0x5410), __byte_perm(w.z, w.w, 0x5410));
   }
 }
 
 // PLE input of layer l (kernels/pleprep.wgsl) times GeGLU of the gate GEMV:
 // x[o] = f16(gelu(gate[o]) * ((p_o rms(p) nw[o] + table[tok][l PD + o] sqrt(PD)) / sqrt 2)), p = Wp h / sqrt(H).
-E4B_DEV void build_x_ple(const MkArgs& A, const MkPhase& P, const float* nw, uint16_t* xs, float* red) {
+E4B_DEV void build_x_ple(const MkArgs& A, const MkPhase& P, const float* nw, uint16_t* xs, float* red, uint32_t ebase,
+                         bool& dead) {
   float pv[kMaxPer], gv[kMaxPer], idv[kMaxPer];
   const int base = P.layer * A.PD;
   const uint32_t row = __ldcg(A.params + 2);
   const bool tok_ok = row < (uint32_t)A.V;
   const uint8_t* r = A.ple_table + (size_t)(tok_ok ? row : 0) * ((size_t)A.L * A.PD / 256) * 210;
   // issue every load first: projection and gate partials, table weights
-  const SlotSrc pp{A.pleproj.buf + (size_t)(base >> 5) * A.pleproj.s * 32, A.pleproj.s};
-  slot_rows(pp, A.PD, pv);
-  slot_rows(P.ple_gate, A.PD, gv);
+  const SlotSrc pp{A.pleproj.buf + (size_t)(base >> 5) * A.pleproj.s * 32, A.pleproj.s, A.pleproj.tag};
+  slot_rows(A, pp, A.PD, ebase, pv, dead);
+  slot_rows(A, P.ple_gate, A.PD, ebase, gv, dead);
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) {
     const int o = threadIdx.x + k * kThreads;
@@ -614,9 +684,9 @@ E4B_DEV void build_x_ple(const MkArgs& A, const MkPhase& P, const float* nw, uin
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) {
     pv[k] *= A.proj_scale;
-    s = fmaf(pv[k], pv[k], s);
+    if (threadIdx.x + k * kThreads < A.PD) s = fmaf(pv[k], pv[k], s);
   }
-  const float inv = rms_scale(block_sum(s, red), A.PD, A.eps);
+  const float inv = rms_scale(cta_sum(s, red), A.PD, A.eps);
 #pragma unroll
   for (int k = 0; k < kMaxPer; k++) {
     const int o = threadIdx.x + k * kThreads;
@@ -634,7 +704,9 @@ E4B_DEV void build_x_ple(const MkArgs& A, const MkPhase& P, const float* nw, uin
 // Scores: 4 threads per slot, 16-byte K loads; p.V: each thread 8 dims of a
 // slot subset, 16-byte V loads, then a shared-memory reduction over subsets.
 E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const float* qn, const float* kn,
-                             const float* rope_tab, float* scr, float* red) {
+                             const float* rope_tab, float* scr, float* red, unsigned long long* tr, uint32_t ebase,
+                             bool& dead) {
+  const uint32_t ep = ebase + (uint32_t)a.tag;
   const Rule rule = make_rule(a, A.params);
   const uint32_t nslots = rule.nslots();
   int CH, nch;
@@ -645,37 +717,63 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
   if (!cur_ok && c == 0 && threadIdx.x == 0) set_status(A.status, E4B_ST_BADINDEX);
   const int HD = A.HD, half = HD / 2, grp = A.QH / A.KVH;
   const int tid = threadIdx.x;
-  float* qs = scr;
-  float* kcur = scr + HD;
-  float* vcur = scr + 2 * HD;
-  float* red2 = scr + 3 * HD;                 // [kThreads * 8]
+  // qs: q in 4 quarters of HD/4 floats with 4 floats of padding between them,
+  // so the 4 threads of a slot read conflict-free 16-byte words
+  const int qpad = HD / 4 + 4;
+  float* qs = scr;                            // [4 * qpad]
+  float* kcur = scr + 4 * qpad;
+  float* vcur = kcur + HD;
+  float* red2 = vcur + HD;                    // [kThreads * 8]
   float* sc = red2 + kThreads * 8;            // [CH]
+  auto qix = [&](int d) { return (d / (HD / 4)) * qpad + d % (HD / 4); };
   const int items = A.QH * nch;
+  const int part = tid & 3, q4 = HD / 4, nv = q4 / 8;          // scores: 4 threads per slot
+  const int ndg = HD / 8, nsg = kThreads / ndg;                // p.V: dim group of 8 x slot subset
+  const int dg = tid % ndg, sg = tid / ndg;
   for (int item = c; item < items; item += A.G) {
     const int h = item / nch, ch = item - h * nch, kvh = h / grp;
     const uint32_t t0 = (uint32_t)ch * CH;
+    const uint32_t hi = min(t0 + (uint32_t)CH, nslots);
     const bool has_cur = cur_ok && cur >= t0 && cur < t0 + (uint32_t)CH && cur < nslots;
     const int krow = A.QH * HD + kvh * HD;
     const int vrow = a.keqv ? krow : A.QH * HD + A.KVH * HD + kvh * HD;
-    // raw q (and the current k / v) with all loads issued up front
+    // K and V of the chunk's first slots do not depend on this token's q: load
+    // them first, so their latency overlaps the q preparation
+    uint4 kw[8], vw[4];
+    const uint32_t tk = t0 + (uint32_t)(tid >> 2);
+    const bool kpre = nv <= 8 && (tid >> 2) < CH && tk < hi && !(has_cur && tk == cur);
+    if (kpre) {
+      const uint4* kr = reinterpret_cast<const uint4*>(a.kc + ((size_t)tk * A.KVH + kvh) * HD + part * q4);
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (u < nv) kw[u] = kr[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const uint32_t ts = t0 + (uint32_t)(sg + u * nsg);
+      vw[u] = make_uint4(0, 0, 0, 0);
+      if (ts < hi && !(has_cur && ts == cur))
+        vw[u] = *reinterpret_cast<const uint4*>(a.vc + ((size_t)ts * A.KVH + kvh) * HD + 8 * dg);
+    }
+    // raw q (and the current k / v)
     float sq = 0.f, sk = 0.f, sv = 0.f;
     for (int d = tid; d < HD; d += kThreads) {
-      const float qv = slot_sum(a.qkv, h * HD + d);
-      qs[d] = qv;
+      const float qv = ll_row(A, a.qkv, h * HD + d, ebase, dead);
+      qs[qix(d)] = qv;
       sq = fmaf(qv, qv, sq);
       if (has_cur) {
-        const float kv = slot_sum(a.qkv, krow + d), vv = slot_sum(a.qkv, vrow + d);
+        const float kv = ll_row(A, a.qkv, krow + d, ebase, dead), vv = ll_row(A, a.qkv, vrow + d, ebase, dead);
         kcur[d] = kv;
         vcur[d] = vv;
         sk = fmaf(kv, kv, sk);
         sv = fmaf(vv, vv, sv);
       }
     }
-    const float qinv = rms_scale(block_sum(sq, red), HD, A.eps);
+    const float qinv = rms_scale(cta_sum(sq, red), HD, A.eps);
     float kinv = 0.f, vinv = 0.f;
     if (has_cur) {
-      kinv = rms_scale(block_sum(sk, red), HD, A.eps);
-      vinv = rms_scale(block_sum(sv, red), HD, A.eps);
+      kinv = rms_scale(cta_sum(sk, red), HD, A.eps);
+      vinv = rms_scale(cta_sum(sv, red), HD, A.eps);
     }
     const bool writer = has_cur && (h % grp) == 0;
     uint16_t* kcw = a.kc + ((size_t)cur * A.KVH + kvh) * HD;
@@ -684,10 +782,11 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
       const bool rot = p < a.angles;
       const float cs = rot ? rope_tab[(2 * a.rope) * half + p] : 1.f;
       const float sn = rot ? rope_tab[(2 * a.rope + 1) * half + p] : 0.f;
-      const float x0 = qs[p] * qinv * qn[p];
-      const float x1 = qs[p + half] * qinv * qn[p + half];
-      qs[p] = rot ? x0 * cs - x1 * sn : x0;
-      qs[p + half] = rot ? x0 * sn + x1 * cs : x1;
+      const int i0 = qix(p), i1 = qix(p + half);
+      const float x0 = qs[i0] * qinv * qn[p];
+      const float x1 = qs[i1] * qinv * qn[p + half];
+      qs[i0] = rot ? x0 * cs - x1 * sn : x0;
+      qs[i1] = rot ? x0 * sn + x1 * cs : x1;
       if (has_cur) {
         const float y0 = kcur[p] * kinv * kn[p];
         const float y1 = kcur[p + half] * kinv * kn[p + half];
@@ -708,49 +807,52 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
       }
     }
     __syncthreads();
+    if (tr && item == c) tr[2] = globaltimer_ns();
     // scores: 4 threads per slot, each a quarter of the dims in 16-byte vectors
-    // (loaded in groups of 8 before use)
-    {
-      const int part = tid & 3, q4 = HD / 4, nv = q4 / 8;
-      for (int sb = 0; sb < CH; sb += kThreads / 4) {
-        const int tt = sb + (tid >> 2);
-        const uint32_t ts = t0 + (uint32_t)tt;
-        const bool ok = tt < CH && ts < nslots && rule.valid(ts);
-        float acc = 0.f;
-        if (ok) {
-          if (has_cur && ts == cur) {
-            for (int d = part * q4; d < (part + 1) * q4; d++) acc = fmaf(qs[d], kcur[d], acc);
-          } else {
-            const uint4* kr = reinterpret_cast<const uint4*>(a.kc + ((size_t)ts * A.KVH + kvh) * HD + part * q4);
-            for (int v0 = 0; v0 < nv; v0 += 8) {
-              uint4 kw[8];
+    for (int sb = 0; sb < CH; sb += kThreads / 4) {
+      const int tt = sb + (tid >> 2);
+      const uint32_t ts = t0 + (uint32_t)tt;
+      const bool ok = tt < CH && ts < nslots && rule.valid(ts);
+      float acc = 0.f;
+      if (ok) {
+        if (has_cur && ts == cur) {
+          for (int d = 0; d < q4; d++) acc = fmaf(qs[part * qpad + d], kcur[part * q4 + d], acc);
+        } else {
+          const uint4* kr = reinterpret_cast<const uint4*>(a.kc + ((size_t)ts * A.KVH + kvh) * HD + part * q4);
+          for (int v0 = 0; v0 < nv; v0 += 8) {
+            uint4 kk[8];
+            const bool pre = sb == 0 && v0 == 0 && kpre;
 #pragma unroll
-              for (int u = 0; u < 8; u++)
-                if (v0 + u < nv) kw[u] = kr[v0 + u];
+            for (int u = 0; u < 8; u++)
+              if (v0 + u < nv) kk[u] = pre ? kw[u] : kr[v0 + u];
 #pragma unroll
-              for (int u = 0; u < 8; u++) {
-                if (v0 + u >= nv) break;
-                const float* qd = qs + part * q4 + 8 * (v0 + u);
-                const __half2* k2 = reinterpret_cast<const __half2*>(&kw[u]);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                  const float2 kf = __half22float2(k2[e]);
-                  acc = fmaf(qd[2 * e], kf.x, acc);
-                  acc = fmaf(qd[2 * e + 1], kf.y, acc);
-                }
-              }
+            for (int u = 0; u < 8; u++) {
+              if (v0 + u >= nv) break;
+              const float4* qd = reinterpret_cast<const float4*>(qs + part * qpad + 8 * (v0 + u));
+              const float4 qa = qd[0], qb = qd[1];
+              const __half2* k2 = reinterpret_cast<const __half2*>(&kk[u]);
+              const float2 k0 = __half22float2(k2[0]), k1 = __half22float2(k2[1]);
+              const float2 k2f = __half22float2(k2[2]), k3 = __half22float2(k2[3]);
+              acc = fmaf(qa.x, k0.x, acc);
+              acc = fmaf(qa.y, k0.y, acc);
+              acc = fmaf(qa.z, k1.x, acc);
+              acc = fmaf(qa.w, k1.y, acc);
+              acc = fmaf(qb.x, k2f.x, acc);
+              acc = fmaf(qb.y, k2f.y, acc);
+              acc = fmaf(qb.z, k3.x, acc);
+              acc = fmaf(qb.w, k3.y, acc);
             }
           }
         }
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        if (part == 0 && tt < CH) sc[tt] = ok ? acc * a.scale : -INFINITY;
       }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (part == 0 && tt < CH) sc[tt] = ok ? acc * a.scale : -INFINITY;
     }
     __syncthreads();
     float m = -INFINITY;
     for (int tt = tid; tt < CH; tt += kThreads) m = fmaxf(m, sc[tt]);
-    m = block_max(m, red);
+    m = cta_max(m, red);
     float l = 0.f;
     for (int tt = tid; tt < CH; tt += kThreads) {
       const float sv2 = sc[tt];
@@ -758,24 +860,22 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
       sc[tt] = p;
       l += p;
     }
-    l = block_sum(l, red);   // also orders the p writes before the reads below
-    // p.V: thread = (dim group of 8, slot subset)
+    l = cta_sum(l, red);   // also orders the p writes before the reads below
+    if (tr && item == c) tr[3] = globaltimer_ns();
+    // p.V: four slots per step, V vectors loaded before use (the first four early)
     {
-      const int ndg = HD / 8, nsg = kThreads / ndg;
-      const int dg = tid % ndg, sg = tid / ndg;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      const uint32_t hi = min(t0 + (uint32_t)CH, nslots);
-      // four slots per step, their V vectors loaded before use
       for (uint32_t ts0 = t0 + (uint32_t)sg; ts0 < hi; ts0 += 4u * (uint32_t)nsg) {
-        uint4 vw[4];
         float pu[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
           const uint32_t ts = ts0 + (uint32_t)(u * nsg);
           pu[u] = ts < hi ? sc[ts - t0] : 0.f;
-          vw[u] = make_uint4(0, 0, 0, 0);
-          if (pu[u] != 0.f && !(has_cur && ts == cur))
-            vw[u] = *reinterpret_cast<const uint4*>(a.vc + ((size_t)ts * A.KVH + kvh) * HD + 8 * dg);
+          if (ts0 != t0 + (uint32_t)sg) {
+            vw[u] = make_uint4(0, 0, 0, 0);
+            if (pu[u] != 0.f && !(has_cur && ts == cur))
+              vw[u] = *reinterpret_cast<const uint4*>(a.vc + ((size_t)ts * A.KVH + kvh) * HD + 8 * dg);
+          }
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
@@ -808,6 +908,46 @@ E4B_DEV void attention_phase(const MkArgs& A, const MkAttn& a, int c, const floa
       if (tid == 0) {
         a.part_ml[2 * pi] = l > 0.f ? m : -INFINITY;
         a.part_ml[2 * pi + 1] = l;
+      }
+    }
+    // the head's last finishing chunk merges all its chunks (kernels/attcomb.wgsl):
+    // out[d] = sum_c o_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M)
+    __syncthreads();
+    volatile int* lastp = reinterpret_cast<volatile int*>(red + 16);
+    if (tid == 0) {
+      unsigned old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.cnt + h) : "memory");
+      *lastp = old == (unsigned)nch - 1u;
+    }
+    __syncthreads();
+    if (*lastp) {
+      float* ew = red2;                       // [nch] weights e^(m_c - M), then den at [nch]
+      if (tid < nch) {
+        ew[tid] = __ldcg(a.part_ml + 2 * ((size_t)h * a.nct + tid));
+        ew[64 + tid] = __ldcg(a.part_ml + 2 * ((size_t)h * a.nct + tid) + 1);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        float M = -INFINITY;
+        for (int k = 0; k < nch; k++)
+          if (ew[64 + k] > 0.f) M = fmaxf(M, ew[k]);
+        float den = 0.f;
+        for (int k = 0; k < nch; k++) {
+          const float lk = ew[64 + k];
+          const float wk = lk > 0.f ? expf(ew[k] - M) : 0.f;
+          den += lk > 0.f ? lk * wk : 0.f;
+          ew[k] = wk;
+        }
+        ew[128] = den;
+        a.cnt[h] = 0u;                        // next use is after the layer's grid barrier
+      }
+      __syncthreads();
+      const float den = ew[128];
+      for (int d = tid; d < HD; d += kThreads) {
+        const float* po = a.part_o + (size_t)h * a.nct * HD + d;
+        float acc = 0.f;
+        for (int k = 0; k < nch; k++) acc = fmaf(__ldcg(po + (size_t)k * HD), ew[k], acc);
+        st_ll32(a.out + (size_t)h * HD + d, f2h(den > 0.f ? acc / den : 0.f), ep);
       }
     }
     __syncthreads();
@@ -925,6 +1065,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
       hs[i] = ok ? q6k_elem(r + (size_t)(i >> 8) * 210, i & 255) * A.emb_mult : 0.f;
   }
 
+  // epochs of this launch: token counter * 256 + producing layer
+  const uint32_t ebase = __ldcg(A.bar + 2) << 8;
+  bool dead = false;          // this thread gave up polling (status TIMEOUT / abort)
   unsigned nbar = 0;
   bool alive = true;
   for (int p = 0; p < A.nph && alive; p++) {
@@ -938,12 +1081,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
     const bool tr = A.trace && c == 0 && threadIdx.x == 0;
     if (tr) A.trace[8 * p] = globaltimer_ns();
     if (P.kvpf && threadIdx.x == 0) prefetch_kv(A, P.a, c);
-    if (P.res) residual(A, P, hs, wbuf, red);
+    if (P.res) residual(A, P, hs, wbuf, red, ebase, dead);
     if (tr) A.trace[8 * p + 1] = globaltimer_ns();
     if (P.kind == PH_FINAL) {
       float s = 0.f;
       for (int i = threadIdx.x; i < A.H; i += kThreads) s = fmaf(hs[i], hs[i], s);
-      const float inv = rms_scale(block_sum(s, red), A.H, A.eps);
+      const float inv = rms_scale(cta_sum(s, red), A.H, A.eps);
       if (c == 0) {
         for (int i = threadIdx.x; i < A.H; i += kThreads) {
           A.hout[i] = hs[i];
@@ -953,27 +1096,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
       break;
     }
     if (P.kind == PH_ATTN) {
-      attention_phase(A, P.a, c, wbuf + 2 * A.H, wbuf + 2 * A.H + A.HD, rope_tab, scr, red);
+      attention_phase(A, P.a, c, wbuf + 2 * A.H, wbuf + 2 * A.H + A.HD, rope_tab, scr, red,
+                      tr ? A.trace + 8 * p : nullptr, ebase, dead);
+      if (tr) A.trace[8 * p + 4] = globaltimer_ns();
       __syncthreads();
       if (p + 1 < A.nph) stage_vectors(A, phs[(p + 1) % 3], wbuf);
     } else {
       const Work W = cta_work(P.g, A.G, c);
       // prologue: activations of this GEMV (only CTAs with work in it)
       if (W.nt > 0) {
-        if (P.g.xk == XK_STAGED_F16) {   // the CTA's k-range of a global f16 input
-          const uint16_t* src = P.g.xg + 256 * W.k0;
-          for (int i = threadIdx.x; i < W.kq * 32; i += kThreads) cp_async16(xs + 16 * i, src + 8 * i);
-          cp_async_commit();
-          cp_async_wait_all();
+        if (P.g.xk == XK_STAGED_F16) {   // the CTA's k-range of a global f16 input, polled
+          const uint32_t* src = P.g.xg + 256 * W.k0;
+          const uint32_t e16 = (ebase + (uint32_t)P.g.xtag) & 0xFFFFu;
+          for (int i = threadIdx.x; i < W.kq * 64; i += kThreads) {
+            uint4 w = ld_ll32x4(src + 4 * i);
+            Spin sp;
+            while (((w.x >> 16) != e16 || (w.y >> 16) != e16 || (w.z >> 16) != e16 || (w.w >> 16) != e16) && !dead) {
+              if (!spin_more(sp, A)) dead = true;
+              w = ld_ll32x4(src + 4 * i);
+            }
+            reinterpret_cast<uint2*>(xs)[i] = make_uint2(__byte_perm(w.x, w.y, 0x5410), __byte_perm(w.z, w.w, 0x5410));
+          }
         }
         if (P.xb == XB_NORM || P.xb == XB_RAW)
           build_x_norm(A, hs, wbuf + A.H, reinterpret_cast<uint16_t*>(xs), red, P.xb == XB_NORM);
         else if (P.xb == XB_ATTN)
-          build_x_attn(A, P, W, reinterpret_cast<uint16_t*>(xs), scr);
+          build_x_attn(A, P, W, reinterpret_cast<uint16_t*>(xs), ebase, dead);
         else if (P.xb == XB_PLE)
-          build_x_ple(A, P, wbuf + A.H, reinterpret_cast<uint16_t*>(xs), red);
+          build_x_ple(A, P, wbuf + A.H, reinterpret_cast<uint16_t*>(xs), red, ebase, dead);
       }
-      if (threadIdx.x == 0) *flag = 1;
       __syncthreads();
       if (p + 1 < A.nph) stage_vectors(A, phs[(p + 1) % 3], wbuf);
       if (tr) A.trace[8 * p + 2] = globaltimer_ns();
@@ -986,20 +1137,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
         if (xf32) gemv_phase<true>(A, W, warp, lane, R, u, pf, pol, xp, scr);
         else gemv_phase<false>(A, W, warp, lane, R, u, pf, pol, xp, scr);
       }
-      if (!R.ok) *flag = 0;    // every writer stores the same value
+      if (!R.ok) dead = true;
       __syncthreads();
       if (tr) {
         A.trace[8 * p + 3] = globaltimer_ns();
         A.trace[8 * p + 7] = R.wait_ns;
         R.wait_ns = 0;
       }
-      if (!*flag) {
-        // a weight copy never arrived (status TIMEOUT): leave without arriving,
-        // so the other CTAs give up at their next barrier
-        alive = false;
-        break;
-      }
-      gemv_epilogue(P.g, W, scr);
+      gemv_epilogue(P.g, W, scr, ebase);
     }
     if (A.trace) {
       __syncthreads();
@@ -1009,8 +1154,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
         atomicMax(A.trace + 8 * p + 5, t);
       }
     }
-    nbar++;
-    alive = grid_sync(A.bar, nbar * (unsigned)A.G, A.status, flag);
+    // end of phase: the CTA's shared scratch is free again; a thread that gave
+    // up stops the CTA (the others give up through the abort flag)
+    if (__syncthreads_or(dead ? 1 : 0)) {
+      alive = false;
+      break;
+    }
+    if (P.sync_after) {
+      nbar++;
+      alive = grid_sync(A.bar, nbar * (unsigned)A.G, A.status, flag);
+    }
     if (tr) A.trace[8 * p + 6] = globaltimer_ns();
   }
 
@@ -1028,6 +1181,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_dense(const MkArgs A) {
       if (done == (unsigned)A.G - 1u) {
         A.bar[0] = 0u;
         A.bar[1] = 0u;
+        A.bar[2] = A.bar[2] + 1u;   // next launch's epochs
         __threadfence();
       }
     }
@@ -1093,8 +1247,8 @@ struct Builder {
   }
 
   // One q4_0 GEMV [rows][IN] in phase P (the last added).
-  int gemv(MkPhase& P, const uint8_t* w, int IN, int OUT, int gu, int ff, int xk, const uint16_t* xg, float* out,
-           uint16_t* outh, SlotSrc* src) {
+  int gemv(MkPhase& P, const uint8_t* w, int IN, int OUT, int gu, int ff, int xk, const uint32_t* xg, int xtag,
+           uint64_t* out, uint32_t* outh, int tag, SlotSrc* src) {
     E4B_REQUIRE(c, w && IN > 0 && IN % 256 == 0 && IN <= 65536, "dense plan: GEMV IN=%d must be a multiple of 256", IN);
     E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 16 == 0, "dense plan: weight not 16-byte aligned");
     MkGemv& g = P.g;
@@ -1105,6 +1259,8 @@ struct Builder {
     g.s = split_for(g.T, g.qpr, gu, G);
     g.xk = xk;
     g.xg = xg;
+    g.xtag = xtag;
+    g.tag = tag;
     g.epi = gu ? EPI_GEGLU : EPI_SLOTS;
     g.out = out;
     g.outh = outh;
@@ -1134,7 +1290,7 @@ struct Builder {
       if (v < 0) v += G;
       load[cc] += b[v];
     }
-    if (src) *src = SlotSrc{out, g.s};
+    if (src) *src = SlotSrc{out, g.s, tag};
     // tensor map over the raw rows as 8-byte words, boxes of 16 rows x 8 blocks
     const int rowbytes = IN / 32 * 18;
     const int rows_total = gu ? 2 * ff : OUT;
@@ -1195,29 +1351,48 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
   }
   const int nct = std::max(1, G / QH);
 
-  // activations owned by the plan
+  // activations owned by the plan: every channel a layer writes is double
+  // buffered by layer parity (a buffer is rewritten two layers later, after a
+  // grid barrier), published as epoch words
+  E4B_REQUIRE(c, L < 255, "dense plan: at most 254 layers");
   auto out_bytes = [&](int rows, int IN) {
     const int T = (rows + 31) / 32;
-    return (size_t)T * split_for(T, IN / 256, 0, G) * 32 * 4;
+    return (size_t)T * split_for(T, IN / 256, 0, G) * 32 * 8;
   };
-  float *qkv_s, *to_s, *td_s, *pg_s = nullptr, *tp_s = nullptr, *wp_s = nullptr, *part_o, *part_ml;
-  uint16_t* geglu;
+  uint64_t *qkv_s[2], *to_s[2], *td_s[2], *pg_s[2] = {nullptr, nullptr}, *tp_s[2] = {nullptr, nullptr};
+  uint64_t* wp_s = nullptr;
+  float *part_o[2], *part_ml[2];
+  uint32_t* att_out[2];
+  unsigned* att_cnt;
+  uint32_t* geglu[2];
   unsigned* bar;
   int rc;
   size_t qkv_bytes = 0;
   for (int l = 0; l < L; l++) qkv_bytes = std::max(qkv_bytes, out_bytes(m->layer[l].qkv_rows, H));
-  if ((rc = b.alloc(qkv_bytes, (void**)&qkv_s))) return fail(rc);
-  if ((rc = b.alloc(out_bytes(H, qdim), (void**)&to_s))) return fail(rc);
-  if ((rc = b.alloc(out_bytes(H, FF), (void**)&td_s))) return fail(rc);
-  if ((rc = b.alloc((size_t)FF * 2, (void**)&geglu))) return fail(rc);
-  if (PD) {
-    if ((rc = b.alloc(out_bytes(PD, H), (void**)&pg_s))) return fail(rc);
-    if ((rc = b.alloc(out_bytes(H, PD), (void**)&tp_s))) return fail(rc);
-    if ((rc = b.alloc(out_bytes(L * PD, H), (void**)&wp_s))) return fail(rc);
+  for (int k = 0; k < 2; k++) {
+    if ((rc = b.alloc(qkv_bytes, (void**)&qkv_s[k]))) return fail(rc);
+    if ((rc = b.alloc(out_bytes(H, qdim), (void**)&to_s[k]))) return fail(rc);
+    if ((rc = b.alloc(out_bytes(H, FF), (void**)&td_s[k]))) return fail(rc);
+    if ((rc = b.alloc((size_t)FF * 4, (void**)&geglu[k]))) return fail(rc);
+    if (PD) {
+      if ((rc = b.alloc(out_bytes(PD, H), (void**)&pg_s[k]))) return fail(rc);
+      if ((rc = b.alloc(out_bytes(H, PD), (void**)&tp_s[k]))) return fail(rc);
+    }
+    if ((rc = b.alloc((size_t)QH * nct * HD * 4, (void**)&part_o[k]))) return fail(rc);
+    if ((rc = b.alloc((size_t)QH * nct * 2 * 4, (void**)&part_ml[k]))) return fail(rc);
+    if ((rc = b.alloc((size_t)QH * HD * 4, (void**)&att_out[k]))) return fail(rc);
   }
-  if ((rc = b.alloc((size_t)QH * nct * HD * 4, (void**)&part_o))) return fail(rc);
-  if ((rc = b.alloc((size_t)QH * nct * 2 * 4, (void**)&part_ml))) return fail(rc);
+  if (PD && (rc = b.alloc(out_bytes(L * PD, H), (void**)&wp_s))) return fail(rc);
   if ((rc = b.alloc(64, (void**)&bar))) return fail(rc);
+  if ((rc = b.alloc((size_t)QH * 4, (void**)&att_cnt))) return fail(rc);
+  E4B_REQUIRE(c, nct <= 64, "dense plan: at most 64 attention chunks per head");
+  {
+    // token counter starts at 1: zero-initialised words carry epoch 0, never current
+    const unsigned one = 1u;
+    cudaError_t e = cudaMemcpyAsync(bar + 2, &one, 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return fail(e4b_fail(c, E4B_ECUDA, "dense plan: %s", cudaGetErrorString(e)));
+  }
 
   MkArgs& A = plan->args;
   A.G = G;
@@ -1247,7 +1422,7 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
   if (PD) {
     MkPhase& P = b.add(PH_GEMV);
     P.xb = XB_F32;
-    if ((rc = b.gemv(P, m->ple_proj_w, H, L * PD, 0, 0, XK_SMEM_F32, nullptr, wp_s, nullptr, &A.pleproj)))
+    if ((rc = b.gemv(P, m->ple_proj_w, H, L * PD, 0, 0, XK_SMEM_F32, nullptr, 0, wp_s, nullptr, 255, &A.pleproj)))
       return fail(rc);
   }
   SlotSrc prev_t{};
@@ -1255,6 +1430,7 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
   float prev_mul = 1.f;
   for (int l = 0; l < L; l++) {
     const e4b_dense_layer& ly = m->layer[l];
+    const int pb = l & 1;   // buffer parity of this layer
     SlotSrc qkv_src, to_src, td_src, pg_src, tp_src;
     {   // q|k|v (and the L2 prefetch of this layer's KV cache)
       MkPhase& P = b.add(PH_GEMV);
@@ -1268,7 +1444,7 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
       }
       P.xb = XB_NORM;
       P.xw = ly.attn_norm;
-      if ((rc = b.gemv(P, ly.qkv, H, ly.qkv_rows, 0, 0, XK_SMEM_F16, nullptr, qkv_s, nullptr, &qkv_src)))
+      if ((rc = b.gemv(P, ly.qkv, H, ly.qkv_rows, 0, 0, XK_SMEM_F16, nullptr, 0, qkv_s[pb], nullptr, l, &qkv_src)))
         return fail(rc);
     }
     MkAttn at{};
@@ -1277,8 +1453,11 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
     at.kn = ly.k_norm;
     at.kc = ly.kcache;
     at.vc = ly.vcache;
-    at.part_o = part_o;
-    at.part_ml = part_ml;
+    at.part_o = part_o[pb];
+    at.part_ml = part_ml[pb];
+    at.cnt = att_cnt;
+    at.out = att_out[pb];
+    at.tag = l;
     at.cachemode = ly.sliding ? 1 : 2;
     at.ring = ly.sliding ? ly.ring : 1;
     at.window = ly.sliding ? m->window : 0;
@@ -1306,7 +1485,8 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
       MkPhase& P = b.add(PH_GEMV);
       P.xb = XB_ATTN;
       P.a = at;
-      if ((rc = b.gemv(P, ly.o, qdim, H, 0, 0, XK_SMEM_F16, nullptr, to_s, nullptr, &to_src))) return fail(rc);
+      if ((rc = b.gemv(P, ly.o, qdim, H, 0, 0, XK_SMEM_F16, nullptr, 0, to_s[pb], nullptr, l, &to_src)))
+        return fail(rc);
     }
     {   // gate|up + GeGLU
       MkPhase& P = b.add(PH_GEMV);
@@ -1316,12 +1496,15 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
       P.rmul = 1.f;
       P.xb = XB_NORM;
       P.xw = ly.ffn_norm;
-      if ((rc = b.gemv(P, ly.gu, H, 2 * FF, 1, FF, XK_SMEM_F16, nullptr, nullptr, geglu, nullptr))) return fail(rc);
+      if ((rc = b.gemv(P, ly.gu, H, 2 * FF, 1, FF, XK_SMEM_F16, nullptr, 0, nullptr, geglu[pb], l, nullptr)))
+        return fail(rc);
     }
     {   // down
       MkPhase& P = b.add(PH_GEMV);
       P.xb = XB_NONE;
-      if ((rc = b.gemv(P, ly.down, FF, H, 0, 0, XK_STAGED_F16, geglu, td_s, nullptr, &td_src))) return fail(rc);
+      if ((rc = b.gemv(P, ly.down, FF, H, 0, 0, XK_STAGED_F16, geglu[pb], l, td_s[pb], nullptr, l, &td_src)))
+        return fail(rc);
+      if (!PD) P.sync_after = 1;
     }
     if (PD) {
       {   // PLE gate: h += rms(t_d) post_ffw; x = f16(h)
@@ -1331,7 +1514,8 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
         P.rw = ly.post_ffw;
         P.rmul = 1.f;
         P.xb = XB_RAW;
-        if ((rc = b.gemv(P, ly.ple_gate, H, PD, 0, 0, XK_SMEM_F16, nullptr, pg_s, nullptr, &pg_src))) return fail(rc);
+        if ((rc = b.gemv(P, ly.ple_gate, H, PD, 0, 0, XK_SMEM_F16, nullptr, 0, pg_s[pb], nullptr, l, &pg_src)))
+          return fail(rc);
       }
       {   // PLE projection
         MkPhase& P = b.add(PH_GEMV);
@@ -1339,7 +1523,9 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
         P.xw = m->ple_norm;
         P.layer = l;
         P.ple_gate = pg_src;
-        if ((rc = b.gemv(P, ly.ple_proj, PD, H, 0, 0, XK_SMEM_F16, nullptr, tp_s, nullptr, &tp_src))) return fail(rc);
+        if ((rc = b.gemv(P, ly.ple_proj, PD, H, 0, 0, XK_SMEM_F16, nullptr, 0, tp_s[pb], nullptr, l, &tp_src)))
+          return fail(rc);
+        P.sync_after = 1;
       }
       prev_t = tp_src;
       prev_w = ly.post_norm;
@@ -1429,7 +1615,7 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
         xs_need = std::max(xs_need, (size_t)512 * cta_work(P.g.T, P.g.qpr, P.g.s, P.g.rot, G, cc).kq);
   const size_t xs_bytes = (xs_need + 127) & ~(size_t)127;
   const size_t scr_bytes =
-      (std::max(std::max((size_t)max_tiles * kWarps * 32 * 4, (size_t)(3 * HD + kThreads * 8 + maxCH) * 4),
+      (std::max(std::max((size_t)max_tiles * kWarps * 32 * 4, (size_t)(4 * (HD / 4 + 4) + 2 * HD + kThreads * 8 + maxCH) * 4),
                 (size_t)(QH * nct + QH) * 4) + 127) & ~(size_t)127;
   const size_t smem = (size_t)kWarps * kStages * kQuantumBytes + (size_t)H * 4 + xs_bytes + scr_bytes +
                       (size_t)(2 * H + 2 * HD) * 4 + 3 * sizeof(MkPhase) + (size_t)kWarps * kStages * 8 + 36 * 4 +

@@ -293,7 +293,9 @@ E4B_API int e4b_dense_plan_run(e4b_ctx* ctx, int handle);
  * step, after its input build, after its GEMV, after its epilogue, the latest
  * "work done" time over all CTAs (atomic max: zero buf before the run), and
  * CTA 0 past the phase's grid barrier, and the time CTA 0's warp 0 spent
- * waiting for weight copies in the phase.  NULL turns it off.
+ * waiting for weight copies in the phase (attention phases: slots 2-4 are the
+ * ends of CTA 0's first item's head prep, scores + softmax, and p.V).  NULL
+ * turns it off.
  * e4b_dense_plan_phases returns the number of phases and their kinds: 0 PLE
  * projection, 1 q|k|v, 2 attention, 3 o, 4 gate|up, 5 down, 6 PLE gate, 7 PLE
  * layer projection, 8 final norm. */
