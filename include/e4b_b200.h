@@ -152,6 +152,23 @@ E4B_API int e4b_q40gu(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const u
  * x f16 [K][IN], W [E][OUT][IN]. */
 E4B_API int e4b_q40moedown(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* topk,
                            const float* tkw, float* y, int IN, int OUT, int K, int batch);
+/* ---- grouped MoE for batched decode (kernels/expgroup.wgsl, q40gugrp.wgsl,
+ * q40downgrp.wgsl, wacc.wgsl).  Entries are (token, slot) pairs e = token*K + slot.
+ * expgroup: sort the n_tok*K entries of topk[n_tok][K] by expert (stable):
+ *   offsets[E+1], entries[pos] = e, inv[e] = pos.
+ * q40gugrp: per entry at sorted position pos, yh[pos][FF] = f16(gelu(gate)*up)
+ *   with expert rows [gate FF | up FF] of w[E][2FF][IN] and x = x[token][IN] (f16).
+ * q40downgrp: y[pos][OUT] = W_e x[pos] (x rows by position, f16; w[E][OUT][IN]).
+ * wacc: out[t][o] = sum_k topk_w[t][k] * y[inv[t*K+k]][o], slots in order.
+ * IN/32 must be even for the grouped GEMMs. */
+E4B_API int e4b_expgroup(e4b_ctx* ctx, const uint32_t* topk, int n_tok, int K, int E, uint32_t* offsets,
+                         uint32_t* entries, uint32_t* inv);
+E4B_API int e4b_q40gugrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
+                         const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K);
+E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
+                           const uint32_t* entries, float* y, int IN, int OUT, int E);
+E4B_API int e4b_wacc(e4b_ctx* ctx, const float* y, const uint32_t* inv, const float* topk_w, float* out, int n_tok,
+                     int K, int OUT);
 /* kernels/moecomb.wgsl:6-15: y[i] = sum_k topkW[k] * slots[k*H+i]. */
 E4B_API int e4b_moecomb(e4b_ctx* ctx, const float* slots, const float* topk_w, float* y, int H, int K);
 
