@@ -1,0 +1,154 @@
+"""Batched decode of B sequences in lockstep (BASELINE configs 4/5: A4B-shaped
+MoE at batch 1/16/64).
+
+All B sequences share the position block (same prompt length, one token per
+step each); every sequence has its own KV cache region.  Per layer
+(src/engine-a4b.js:424-463 per token, batched as the reference's grouped path
+src/engine-a4b.js:467-585 does for prefill):
+
+  q|k|v        e4b_q40mm          (tensor-core GEMM, tokens as columns)
+  head prep    e4b_headprep_seq   (per-sequence cache)
+  attention    e4b_attsplit_seq + e4b_attcomb_seq
+  o            e4b_q40mm
+  norms        e4b_rmsacc3        (rows = B)
+  router       e4b_routertop      (batch = B)
+  dense FFN    e4b_q40gumm + e4b_q40mm
+  experts      e4b_expgroup -> e4b_q40gugrp -> e4b_q40downgrp -> e4b_wacc
+  tail         e4b_a4btail        (rows = B)
+
+then the final norm, e4b_q6k_lmhead_rows, e4b_argmax_rows and
+e4b_feedtok_rows (each sequence's greedy token fed back on the device).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+
+from . import ops
+from .engine import Engine, RING_CAP, ARGMAX_PARTS, F32
+
+C = ctypes.c_void_p
+
+
+class BatchEngine(Engine):
+    def __init__(self, src, nseq: int, device=0, *, chunk: int = 64):
+        self.nseq = int(nseq)
+        super().__init__(src, device, chunk=chunk, record=False, fused=False)
+        if not self.cfg.moe:
+            raise ValueError("BatchEngine drives the MoE (A4B) graph")
+        H, IN = self.cfg.hidden, self.cfg.hidden
+        for n, what in ((H, "hidden"), (self.cfg.q_dim, "q_dim"), (self.cfg.ff, "ff"), (self.cfg.expert_ff, "expert ff")):
+            if n % 64:
+                raise ValueError(f"{what} {n} must be a multiple of 64 for the batched GEMMs")
+
+    def _alloc_activations(self):
+        c, d, B = self.cfg, self.dev, self.nseq
+        H, FF, QD, E, K, EF = c.hidden, c.ff, c.q_dim, c.experts, c.topk, c.expert_ff
+        maxrows = max(c.qkv_rows(l) for l in range(c.layers))
+        maxch = max(L.max_chunks for L in self.layers)
+        A = type("Acts", (), {})()
+        A.params = d.alloc(32, "params")
+        A.tok = d.alloc(B * 4, "tok")
+        A.hidden = d.alloc(B * H * 4, "hidden")
+        A.hidden_b = d.alloc(B * H * 4, "hiddenB")
+        A.normed = d.alloc(B * H * 2, "normed")
+        A.qkv = d.alloc(B * maxrows * 4, "qkv")
+        A.q = d.alloc(B * QD * 4, "qPrep")
+        A.attn = d.alloc(B * QD * 2, "attnOut")
+        A.part_o = d.alloc(B * c.q_heads * maxch * c.head_dim * 4, "partO")
+        A.part_ml = d.alloc(B * c.q_heads * maxch * 2 * 4, "partML")
+        A.tmp = d.alloc(B * H * 4, "tmp")
+        A.geglu = d.alloc(B * FF * 2, "geglu")
+        A.router_in = d.alloc(B * H * 4, "routerIn")
+        A.moe_in = d.alloc(B * H * 2, "moeIn")
+        A.topk_idx = d.alloc(B * K * 4, "topkIdx")
+        A.topk_w = d.alloc(B * K * 4, "topkW")
+        A.offsets = d.alloc((E + 1) * 4, "expOffsets")
+        A.entries = d.alloc(B * K * 4, "expEntries")
+        A.inv = d.alloc(B * K * 4, "expInv")
+        A.gl = d.alloc(B * K * EF * 2, "expGeglu")
+        A.yo = d.alloc(B * K * H * 4, "expOut")
+        A.moe_out = d.alloc(B * H * 4, "moeOut")
+        A.xf = d.alloc(B * H * 4, "xfinal")
+        A.xsplit = d.alloc(2 * B * H * 2, "xSplit")
+        A.logits = d.alloc(B * c.vocab * 4, "logits")
+        A.amax_part = d.alloc(B * ARGMAX_PARTS * 8, "amaxPart")
+        A.amax = d.alloc(B * 8, "amax")
+        A.ring = d.alloc(B * RING_CAP * 4, "tokRing")
+        self.A = A
+        p = ctypes.c_void_p()
+        d.call("e4b_host_alloc", ctypes.c_size_t(32), ctypes.byref(p))
+        self.host_params = np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint32)), shape=(8,))
+        self._host_params_ptr = p.value
+
+    # ------------------------------------------------------------ one step (B tokens)
+    def encode_forward(self):
+        c, d, A, B = self.cfg, self.dev, self.A, self.nseq
+        H, V, E, K, EF, FF = c.hidden, c.vocab, c.experts, c.topk, c.expert_ff, c.ff
+        d.call("e4b_q6k_embed", self.emb, A.params, A.tok, A.hidden, H, V, ctypes.c_float(F32(math.sqrt(H))), 1, B)
+        d.call("e4b_rmsnorm", A.hidden, self.layers[0].attn_norm, None, None, A.normed, H, B, ctypes.c_float(c.eps),
+               1, 0, 1)
+        for L in self.layers:
+            nxt = self.layers[L.i + 1].attn_norm if L.i + 1 < c.layers else None
+            d.call("e4b_q40mm", A.normed, L.qkv, A.qkv, H, L.qkv_rows, B)
+            d.call("e4b_headprep_seq", A.qkv, L.q_norm, L.k_norm, A.params, L.kc, L.vc, A.q, c.q_heads, c.kv_heads,
+                   c.head_dim, L.angles, ctypes.c_float(L.theta), ctypes.c_float(c.eps), int(L.keqv), L.cachemode,
+                   L.ring, L.slots, B)
+            d.call("e4b_attsplit_seq", A.q, L.kc, L.vc, A.params, A.part_o, A.part_ml, c.q_heads, c.kv_heads,
+                   c.head_dim, c.window if L.sliding else 0, L.cachemode, L.ring, self.chunk, L.max_chunks,
+                   ctypes.c_float(1.0), L.slots, B)
+            d.call("e4b_attcomb_seq", A.part_o, A.part_ml, A.attn, None, None, c.q_heads, c.head_dim, L.max_chunks, B)
+            d.call("e4b_q40mm", A.attn, L.o, A.tmp, c.q_dim, H, B)
+            d.call("e4b_rmsacc3", A.tmp, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
+                   A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B)
+            d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
+            d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
+            d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
+            d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
+            d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
+            d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
+            d.call("e4b_wacc", A.yo, A.inv, A.topk_w, A.moe_out, B, K, H)
+            d.call("e4b_a4btail", A.tmp, L.post_ffw1, A.moe_out, L.post_ffw2, L.post_ffw, A.hidden_b,
+                   nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
+                   ctypes.c_float(L.scale), int(nxt is not None), B)
+        d.call("e4b_rmsnorm", A.hidden, self.out_norm, A.xf, None, None, H, B, ctypes.c_float(c.eps), 1, 0, 0)
+        d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)
+        d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
+        d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
+
+    # ------------------------------------------------------------ host API
+    def set_step(self, tokens, pos: int):
+        """Tokens of all B sequences at position `pos`."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.uint32).reshape(self.nseq))
+        self.dev.write(self.A.tok, t)
+        self.host_params[:] = (pos, pos + 1, int(t[0]), 0, pos, pos + 1, pos, 0)
+        self.dev.write(self.A.params, self.host_params)
+
+    def step(self, tokens, pos: int):
+        self.set_step(tokens, pos)
+        self.run_token(1)
+
+    def prefill(self, prompts):
+        prompts = np.asarray(prompts)
+        for pos in range(prompts.shape[1]):
+            self.step(prompts[:, pos], pos)
+
+    def generate(self, prompts, n_new: int):
+        """prompts [B][P] (same length) -> [B][n_new] greedy ids."""
+        prompts = np.asarray(prompts)
+        P = prompts.shape[1]
+        assert P + n_new <= RING_CAP
+        self.prefill(prompts)
+        if n_new > 1:
+            self.decode_chunk(n_new - 1)
+        self.dev.sync()
+        ring = self.dev.read(self.A.ring, np.uint32, self.nseq * RING_CAP).reshape(self.nseq, RING_CAP)
+        return ring[:, P - 1:P - 1 + n_new].astype(np.int64)
+
+    def read_hidden(self) -> np.ndarray:
+        return self.dev.read(self.A.hidden, F32, self.nseq * self.cfg.hidden).reshape(self.nseq, -1)
+
+    def read_logits(self) -> np.ndarray:
+        return self.dev.read(self.A.logits, F32, self.nseq * self.cfg.vocab).reshape(self.nseq, -1)

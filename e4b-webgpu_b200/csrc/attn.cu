@@ -15,10 +15,18 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
                            const uint32_t* __restrict__ params, uint16_t* __restrict__ kcache,
                            uint16_t* __restrict__ vcache, float* __restrict__ q_out, int QH, int KVH, int HD,
                            int angles, float theta, float eps, int keqv, int cachemode, int ring, int cache_slots,
-                           uint32_t* status) {
+                           uint32_t* status, size_t seq_stride) {
   pdl_wait();
   __shared__ float sh[32];
   const int head = blockIdx.x, b = blockIdx.y;
+  // seq_stride > 0: row b is sequence b at the common position params[0], with
+  // its own cache at kcache / vcache + b * seq_stride; else rows are consecutive
+  // positions of one sequence
+  if (seq_stride) {
+    kcache += (size_t)b * seq_stride;
+    vcache += (size_t)b * seq_stride;
+  }
+  const uint32_t pb = seq_stride ? 0u : (uint32_t)b;
   int src = head;
   if (keqv && head >= QH + KVH) src = head - KVH;  // v reads the k slice
   const size_t qkvS = (size_t)(QH + KVH * (2 - keqv)) * HD;
@@ -27,10 +35,10 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
   for (int d = threadIdx.x; d < HD; d += blockDim.x) s = fmaf(qkv[base + d], qkv[base + d], s);
   const float inv = rms_scale(block_sum(s, sh), HD, eps);
   const int half = HD / 2;
-  const uint32_t pos = params[0] + b;
+  const uint32_t pos = params[0] + pb;
   uint32_t slot = pos;
   if (cachemode == 1) slot = pos % (uint32_t)ring;
-  if (cachemode == 2) slot = params[4] + b;
+  if (cachemode == 2) slot = params[4] + pb;
   if (head >= QH && slot >= (uint32_t)cache_slots) {
     if (threadIdx.x == 0) set_status(status, E4B_ST_BADINDEX);
     return;
@@ -121,8 +129,16 @@ struct SlotRule {
 __global__ void k_attsplit(const float* __restrict__ q, const uint16_t* __restrict__ kcache,
                            const uint16_t* __restrict__ vcache, const uint32_t* __restrict__ params,
                            float* __restrict__ part_o, float* __restrict__ part_ml, int QH, int KVH, int HD,
-                           int window, int cachemode, int ring, int max_chunks, float scale) {
+                           int window, int cachemode, int ring, int max_chunks, float scale, size_t seq_stride) {
   pdl_wait();
+  {   // sequence blockIdx.z: its q rows, cache and partials
+    const size_t z = blockIdx.z;
+    q += z * QH * HD;
+    kcache += z * seq_stride;
+    vcache += z * seq_stride;
+    part_o += z * QH * max_chunks * HD;
+    part_ml += z * QH * max_chunks * 2;
+  }
   extern __shared__ float smem[];
   float* qs = smem;            // [HD]
   float* ps = smem + HD;       // [chunk]
@@ -174,6 +190,14 @@ __global__ void k_attcomb(const float* __restrict__ part_o, const float* __restr
                           uint16_t* __restrict__ out_h, float* __restrict__ out_f, float* __restrict__ lse, int HD,
                           int max_chunks) {
   pdl_wait();
+  {   // sequence blockIdx.y
+    const size_t z = blockIdx.y, QH = gridDim.x;
+    part_o += z * QH * max_chunks * HD;
+    part_ml += z * QH * max_chunks * 2;
+    if (out_h) out_h += z * QH * HD;
+    if (out_f) out_f += z * QH * HD;
+    if (lse) lse += z * QH;
+  }
   const int h = blockIdx.x;
   const float* ml = part_ml + (size_t)h * max_chunks * 2;
   float M = -INFINITY;
@@ -210,7 +234,24 @@ E4B_API int e4b_headprep(e4b_ctx* c, const float* qkv, const float* qw, const fl
   if (batch < 1) batch = 1;
   return e4b_launch(c, "headprep", k_headprep, dim3(QH + 2 * KVH, batch), dim3(128), 0, qkv, qw, kw, params, kcache,
                     vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring, cache_slots,
-                    c->status);
+                    c->status, (size_t)0);
+}
+
+E4B_API int e4b_headprep_seq(e4b_ctx* c, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
+                             uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
+                             int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
+                             int cache_slots, int nseq) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, qkv && qw && kw && params && kcache && vcache && q_out && nseq > 0, "headprep_seq: bad args");
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD % 2 == 0 && rope_angles >= 0 &&
+                     rope_angles <= HD / 2 && cache_slots > 0,
+              "headprep_seq: bad geometry QH=%d KVH=%d HD=%d angles=%d", QH, KVH, HD, rope_angles);
+  E4B_REQUIRE(c, cachemode >= 0 && cachemode <= 2 && (cachemode != 1 || (ring > 0 && ring <= cache_slots)),
+              "headprep_seq: bad cache mode %d / ring %d", cachemode, ring);
+  const size_t stride = (size_t)cache_slots * KVH * HD;
+  return e4b_launch(c, "headprep_seq", k_headprep, dim3(QH + 2 * KVH, nseq), dim3(128), 0, qkv, qw, kw, params,
+                    kcache, vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring,
+                    cache_slots, c->status, stride);
 }
 
 E4B_API int e4b_rope(e4b_ctx* c, float* x, const uint32_t* params, int heads, int HD, int rope_angles, float theta) {
@@ -239,7 +280,26 @@ E4B_API int e4b_attsplit(e4b_ctx* c, const float* q, const uint16_t* kcache, con
               "attsplit: bad cache mode");
   const size_t sm = (size_t)(HD + chunk) * 4;
   return e4b_launch(c, "attsplit", k_attsplit, dim3(QH, max_chunks), dim3(chunk), sm, q, kcache, vcache, params,
-                    part_o, part_ml, QH, KVH, HD, window, cachemode, ring, max_chunks, scale);
+                    part_o, part_ml, QH, KVH, HD, window, cachemode, ring, max_chunks, scale, (size_t)0);
+}
+
+E4B_API int e4b_attsplit_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                             const uint32_t* params, float* part_o, float* part_ml, int QH, int KVH, int HD,
+                             int window, int cachemode, int ring, int chunk, int max_chunks, float scale,
+                             int cache_slots, int nseq) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, q && kcache && vcache && params && part_o && part_ml && nseq > 0 && cache_slots > 0,
+              "attsplit_seq: bad args");
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD % 2 == 0 && max_chunks > 0,
+              "attsplit_seq: bad geometry");
+  E4B_REQUIRE(c, chunk >= 32 && chunk <= 1024 && (chunk & 31) == 0, "attsplit_seq: chunk %d must be 32..1024, x32",
+              chunk);
+  E4B_REQUIRE(c, cachemode >= 0 && cachemode <= 2 && (cachemode != 1 || (ring > 0 && window > 0)),
+              "attsplit_seq: bad cache mode");
+  const size_t sm = (size_t)(HD + chunk) * 4;
+  const size_t stride = (size_t)cache_slots * KVH * HD;
+  return e4b_launch(c, "attsplit_seq", k_attsplit, dim3(QH, max_chunks, nseq), dim3(chunk), sm, q, kcache, vcache,
+                    params, part_o, part_ml, QH, KVH, HD, window, cachemode, ring, max_chunks, scale, stride);
 }
 
 E4B_API int e4b_attcomb(e4b_ctx* c, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
@@ -248,6 +308,15 @@ E4B_API int e4b_attcomb(e4b_ctx* c, const float* part_o, const float* part_ml, u
   E4B_REQUIRE(c, part_o && part_ml && (out_h || out_f) && QH > 0 && HD > 0 && max_chunks > 0, "attcomb: bad args");
   return e4b_launch(c, "attcomb", k_attcomb, dim3(QH), dim3(128), 0, part_o, part_ml, out_h, out_f, lse, HD,
                     max_chunks);
+}
+
+E4B_API int e4b_attcomb_seq(e4b_ctx* c, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
+                            float* lse, int QH, int HD, int max_chunks, int nseq) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, part_o && part_ml && (out_h || out_f) && QH > 0 && HD > 0 && max_chunks > 0 && nseq > 0,
+              "attcomb_seq: bad args");
+  return e4b_launch(c, "attcomb_seq", k_attcomb, dim3(QH, nseq), dim3(128), 0, part_o, part_ml, out_h, out_f, lse,
+                    HD, max_chunks);
 }
 
 }  // extern "C"

@@ -70,11 +70,13 @@ template <int EPI, int XPOS>
 __global__ void __launch_bounds__(32 * kGW) k_grp(const uint16_t* __restrict__ x, const uint8_t* __restrict__ w,
                                                    const uint32_t* __restrict__ offsets,
                                                    const uint32_t* __restrict__ entries, float* __restrict__ y,
-                                                   uint16_t* __restrict__ yh, int IN, int ROWS, int FF, int K) {
+                                                   uint16_t* __restrict__ yh, int IN, int ROWS, int FF, int K,
+                                                   int n_direct) {
   pdl_wait();
   __shared__ float red[kGW][32][kGroups * 8];
   const int e = blockIdx.y, tile = blockIdx.x;
-  const uint32_t p0 = offsets[e], ne = offsets[e + 1] - p0;
+  // n_direct > 0: one matrix, tokens 0..n_direct-1 in order (dense batched GEMM)
+  const uint32_t p0 = n_direct > 0 ? 0u : offsets[e], ne = n_direct > 0 ? (uint32_t)n_direct : offsets[e + 1] - p0;
   if (ne == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int nb = IN >> 5;
@@ -220,7 +222,7 @@ E4B_API int e4b_q40gugrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const 
   E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 4 == 0 && (IN / 32) % 2 == 0,
               "q40gugrp: IN/32 must be even (rows on 4-byte boundaries, word reads inside each row)");
   return e4b_launch(c, "q40gugrp", k_grp<1, 0>, dim3((FF + 15) / 16, E), dim3(32 * kGW), 0, x, w, offsets, entries,
-                    (float*)nullptr, yh, IN, 2 * FF, FF, K);
+                    (float*)nullptr, yh, IN, 2 * FF, FF, K, 0);
 }
 
 E4B_API int e4b_q40downgrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
@@ -231,7 +233,25 @@ E4B_API int e4b_q40downgrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, cons
   E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 4 == 0 && (IN / 32) % 2 == 0,
               "q40downgrp: IN/32 must be even (rows on 4-byte boundaries, word reads inside each row)");
   return e4b_launch(c, "q40downgrp", k_grp<0, 1>, dim3((OUT + 31) / 32, E), dim3(32 * kGW), 0, x, w, offsets,
-                    entries, y, (uint16_t*)nullptr, IN, OUT, 0, 1);
+                    entries, y, (uint16_t*)nullptr, IN, OUT, 0, 1, 0);
+}
+
+E4B_API int e4b_q40mm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, float* y, int IN, int OUT, int n) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && w && y && n > 0, "q40mm: bad args");
+  E4B_REQUIRE(c, IN > 0 && IN % 64 == 0 && OUT > 0 && reinterpret_cast<uintptr_t>(w) % 4 == 0,
+              "q40mm: IN=%d must be a multiple of 64", IN);
+  return e4b_launch(c, "q40mm", k_grp<0, 1>, dim3((OUT + 31) / 32, 1), dim3(32 * kGW), 0, x, w,
+                    (const uint32_t*)nullptr, (const uint32_t*)nullptr, y, (uint16_t*)nullptr, IN, OUT, 0, 1, n);
+}
+
+E4B_API int e4b_q40gumm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, uint16_t* yh, int IN, int FF, int n) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && w && yh && n > 0, "q40gumm: bad args");
+  E4B_REQUIRE(c, IN > 0 && IN % 64 == 0 && FF > 0 && reinterpret_cast<uintptr_t>(w) % 4 == 0,
+              "q40gumm: IN=%d must be a multiple of 64", IN);
+  return e4b_launch(c, "q40gumm", k_grp<1, 1>, dim3((FF + 15) / 16, 1), dim3(32 * kGW), 0, x, w,
+                    (const uint32_t*)nullptr, (const uint32_t*)nullptr, (float*)nullptr, yh, IN, 2 * FF, FF, 1, n);
 }
 
 E4B_API int e4b_wacc(e4b_ctx* c, const float* y, const uint32_t* inv, const float* topk_w, float* out, int n_tok,

@@ -137,3 +137,130 @@ int lmhead_stream(e4b_ctx* c, const uint8_t* w, const float* x, float* y, int N,
 }
 
 }  // namespace e4b
+
+// ---- batched LM head: n token rows of x against every q6_K row, on the tensor
+// cores (mma.sync m16n8k16, tokens as the 8 columns).  A k16 step is exactly one
+// q6_K sub-block (16 weights sharing an int8 scale), so each step's products are
+// scaled by sc * d in f32 and accumulated.  A = (q - 32) in f16 (exact); x is
+// used as f16 hi + lo (x = hi + lo to ~2^-22), so the products carry f32-level
+// precision.  One warp = 16 rows x all tokens.
+namespace {
+
+__global__ void k_split_f32(const float* __restrict__ x, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo,
+                            size_t n) {
+  pdl_wait();
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = x[i];
+  const __half h = __float2half_rn(v);
+  hi[i] = __half_as_ushort(h);
+  lo[i] = f2h(v - __half2float(h));
+}
+
+// f16x2 of (q(e) - 32, q(e+1) - 32) for elements e (even) and e+1 of a q6_K block.
+E4B_DEV uint32_t q6_pair(const uint8_t* blk, int e) {
+  const int h = e >> 7, r = e & 127, jj = r >> 5, l = r & 31;
+  const uint32_t ql = *reinterpret_cast<const uint16_t*>(blk + h * 64 + l + 32 * (jj & 1));
+  const uint32_t qh = *reinterpret_cast<const uint16_t*>(blk + 128 + h * 32 + l);
+  const uint32_t lo = (ql >> (4 * (jj >> 1))) & 0x0F0Fu;           // both bytes' nibble
+  const uint32_t hi = ((qh >> (2 * jj)) & 0x0303u) << 4;
+  const uint32_t q = lo | hi;                                        // two 6-bit values, one per byte
+  const uint32_t f = __byte_perm(q, 0x64646464u, 0x5140);            // 0x64qq halves = 1024 + q
+  uint32_t r16;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r16) : "r"(f), "r"(0x64206420u));   // - 1056 -> q - 32
+  return r16;
+}
+
+template <int NG>
+__global__ void __launch_bounds__(256) k_q6k_mm(const uint8_t* __restrict__ w, const uint16_t* __restrict__ xh,
+                                                const uint16_t* __restrict__ xl, float* __restrict__ y, int N, int OUT,
+                                                int n, float softcap) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int r0 = (blockIdx.x * 8 + warp) * 16;
+  if (r0 >= OUT) return;
+  const int nb = N >> 8;
+  const int ra = min(r0 + g, OUT - 1), rb = min(r0 + g + 8, OUT - 1);
+  const uint8_t* wa = w + (size_t)ra * nb * 210;
+  const uint8_t* wb = w + (size_t)rb * nb * 210;
+  for (int g0 = 0; g0 < n; g0 += 8 * NG) {
+    float acc[NG][4];
+#pragma unroll
+    for (int q = 0; q < NG; q++) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+    // this lane's token (column g) per group
+    const uint16_t* xhr[NG];
+    const uint16_t* xlr[NG];
+#pragma unroll
+    for (int q = 0; q < NG; q++) {
+      const int tok = g0 + 8 * q + g;
+      xhr[q] = tok < n ? xh + (size_t)tok * N : nullptr;
+      xlr[q] = tok < n ? xl + (size_t)tok * N : nullptr;
+    }
+    for (int b = 0; b < nb; b++) {
+      const uint8_t* ba = wa + (size_t)b * 210;
+      const uint8_t* bb = wb + (size_t)b * 210;
+      const float da = h2f(*reinterpret_cast<const uint16_t*>(ba + 208));
+      const float db = h2f(*reinterpret_cast<const uint16_t*>(bb + 208));
+      for (int sb = 0; sb < 16; sb++) {
+        const int e0 = 16 * sb + 2 * t;
+        const uint32_t a0 = q6_pair(ba, e0), a1 = q6_pair(bb, e0), a2 = q6_pair(ba, e0 + 8), a3 = q6_pair(bb, e0 + 8);
+        const float sa = da * (float)(int8_t)ba[192 + sb], sbb = db * (float)(int8_t)bb[192 + sb];
+        const int xo = 256 * b + e0;
+#pragma unroll
+        for (int q = 0; q < NG; q++) {
+          if (g0 + 8 * q >= n) break;
+          uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+          if (xhr[q]) {
+            h0 = *reinterpret_cast<const uint32_t*>(xhr[q] + xo);
+            h1 = *reinterpret_cast<const uint32_t*>(xhr[q] + xo + 8);
+            l0 = *reinterpret_cast<const uint32_t*>(xlr[q] + xo);
+            l1 = *reinterpret_cast<const uint32_t*>(xlr[q] + xo + 8);
+          }
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816(c, a0, a1, a2, a3, h0, h1);
+          mma16816(c, a0, a1, a2, a3, l0, l1);
+          acc[q][0] = fmaf(sa, c[0], acc[q][0]);
+          acc[q][1] = fmaf(sa, c[1], acc[q][1]);
+          acc[q][2] = fmaf(sbb, c[2], acc[q][2]);
+          acc[q][3] = fmaf(sbb, c[3], acc[q][3]);
+        }
+      }
+    }
+    // C: c0, c1 = row g, tokens 2t, 2t+1; c2, c3 = row g+8
+#pragma unroll
+    for (int q = 0; q < NG; q++) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int row = r0 + g + (i >> 1) * 8, tok = g0 + 8 * q + 2 * t + (i & 1);
+        if (row < OUT && tok < n) {
+          const float v = acc[q][i];
+          y[(size_t)tok * OUT + row] = softcap != 0.f ? softcap * tanhf(v / softcap) : v;
+        }
+      }
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* c, const uint8_t* w, const float* x, uint16_t* scratch, float* y, int N,
+                                int OUT, float softcap, int n) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, w && x && scratch && y && N > 0 && N % 256 == 0 && OUT > 0 && n > 0, "q6k_lmhead_rows: bad args");
+  uint16_t* xh = scratch;
+  uint16_t* xl = scratch + (size_t)n * N;
+  const size_t tot = (size_t)n * N;
+  if (int r = e4b_launch(c, "split_f32", k_split_f32, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, x, xh, xl,
+                         tot))
+    return r;
+  const unsigned grid = (unsigned)((OUT + 127) / 128);
+  if (n <= 8)
+    return e4b_launch(c, "q6k_mm", k_q6k_mm<1>, dim3(grid), dim3(256), 0, w, (const uint16_t*)xh,
+                      (const uint16_t*)xl, y, N, OUT, n, softcap);
+  return e4b_launch(c, "q6k_mm", k_q6k_mm<8>, dim3(grid), dim3(256), 0, w, (const uint16_t*)xh, (const uint16_t*)xl,
+                    y, N, OUT, n, softcap);
+}
+
+}  // extern "C"

@@ -122,6 +122,8 @@ E4B_DEV void block_argmax(float& bv, uint32_t& bi) {
 }
 __global__ void k_argmax0(const float* __restrict__ x, uint32_t* __restrict__ part, int N, int parts) {
   pdl_wait();
+  x += (size_t)blockIdx.y * N;                  // row blockIdx.y
+  part += (size_t)blockIdx.y * parts * 2;
   const int per = (N + parts - 1) / parts;
   const int lo = blockIdx.x * per, hi = min(lo + per, N);
   float bv = -3.0e38f;
@@ -135,6 +137,8 @@ __global__ void k_argmax0(const float* __restrict__ x, uint32_t* __restrict__ pa
 }
 __global__ void k_argmax1(const uint32_t* __restrict__ part, uint32_t* __restrict__ out, int parts) {
   pdl_wait();
+  part += (size_t)blockIdx.x * parts * 2;       // row blockIdx.x
+  out += (size_t)blockIdx.x * 2;
   float bv = -3.0e38f;
   uint32_t bi = 0xffffffffu;
   for (int i = threadIdx.x; i < parts; i += blockDim.x) argmax_merge(bv, bi, __uint_as_float(part[2 * i + 1]), part[2 * i]);
@@ -156,6 +160,28 @@ __global__ void k_feedtok(const uint32_t* __restrict__ amax, uint32_t* __restric
   params[4] += 1;
   params[5] += 1;
   params[6] += 1;
+}
+
+// Batched token feedback: token b of the step -> tok[b] and ring[b][params[6] % cap];
+// the shared position block advances once.
+__global__ void k_feedtok_rows(const uint32_t* __restrict__ amax, uint32_t* __restrict__ params,
+                               uint32_t* __restrict__ ring, int ring_cap, uint32_t* __restrict__ tok, int rows) {
+  pdl_wait();
+  const uint32_t ri = params[6];
+  for (int b = threadIdx.x; b < rows; b += blockDim.x) {
+    const uint32_t t = amax[2 * b];
+    tok[b] = t;
+    if (ring) ring[(size_t)b * ring_cap + ri % (uint32_t)ring_cap] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    params[2] = amax[0];
+    params[0] += 1;
+    params[1] += 1;
+    params[4] += 1;
+    params[5] += 1;
+    params[6] += 1;
+  }
 }
 
 }  // namespace
@@ -243,6 +269,20 @@ E4B_API int e4b_argmax_static(e4b_ctx* c, const float* x, uint32_t* out, int N, 
   if (int r = static_part_addr(c, &part)) return r;
   if (int r = e4b_launch(c, "argmax0", k_argmax0, dim3(parts), dim3(256), 0, x, part, N, parts)) return r;
   return e4b_launch(c, "argmax1", k_argmax1, dim3(1), dim3(256), 0, (const uint32_t*)part, out, parts);
+}
+
+E4B_API int e4b_argmax_rows(e4b_ctx* c, const float* x, uint32_t* part, uint32_t* out, int N, int parts, int rows) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && part && out && N > 0 && parts > 0 && parts <= 4096 && rows > 0, "argmax_rows: bad args");
+  if (int r = e4b_launch(c, "argmax0", k_argmax0, dim3(parts, rows), dim3(256), 0, x, part, N, parts)) return r;
+  return e4b_launch(c, "argmax1", k_argmax1, dim3(rows), dim3(256), 0, (const uint32_t*)part, out, parts);
+}
+
+E4B_API int e4b_feedtok_rows(e4b_ctx* c, const uint32_t* amax, uint32_t* params, uint32_t* ring, int ring_cap,
+                             uint32_t* tok, int rows) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, amax && params && tok && rows > 0 && (!ring || ring_cap > 0), "feedtok_rows: bad args");
+  return e4b_launch(c, "feedtok_rows", k_feedtok_rows, dim3(1), dim3(256), 0, amax, params, ring, ring_cap, tok, rows);
 }
 
 E4B_API int e4b_feedtok(e4b_ctx* c, const uint32_t* amax, uint32_t* params, uint32_t* ring, int ring_cap) {

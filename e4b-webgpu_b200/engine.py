@@ -148,7 +148,7 @@ class Engine:
             L.ring = c.ring(l)
             L.slots = c.kv_slots(l)
             L.cachemode = 1 if L.sliding else 2
-            kvb = L.slots * c.kv_heads * c.head_dim * 2
+            kvb = L.slots * c.kv_heads * c.head_dim * 2 * getattr(self, "nseq", 1)
             L.kc = self.dev.alloc(kvb, f"kcache{l}")
             L.vc = self.dev.alloc(kvb, f"vcache{l}")
             L.max_chunks = (L.slots + self.chunk - 1) // self.chunk

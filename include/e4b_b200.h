@@ -167,6 +167,11 @@ E4B_API int e4b_q40gugrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, cons
                          const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K);
 E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
                            const uint32_t* entries, float* y, int IN, int OUT, int E);
+/* Dense batched GEMMs on the same tensor-core path (n token rows, f16 x):
+ * q40mm: y[n][OUT] = W x[n] (f32); q40gumm: yh[n][FF] = f16(gelu(gate)*up) with
+ * rows [gate FF | up FF] (kernels/q40gu.wgsl dense part, per token). */
+E4B_API int e4b_q40mm(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, float* y, int IN, int OUT, int n);
+E4B_API int e4b_q40gumm(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, uint16_t* yh, int IN, int FF, int n);
 E4B_API int e4b_wacc(e4b_ctx* ctx, const float* y, const uint32_t* inv, const float* topk_w, float* out, int n_tok,
                      int K, int OUT);
 /* kernels/moecomb.wgsl:6-15: y[i] = sum_k topkW[k] * slots[k*H+i]. */
@@ -226,6 +231,10 @@ E4B_API int e4b_geglub(e4b_ctx* ctx, const float* gu, uint16_t* yh, int N, int r
 /* kernels/pleprep.wgsl:15-46 with a q6_K table: for layer block b,
  * pleIn[b*PD+i] = (rms(proj_b*proj_scale)[i]*normW[i] + row_b[i]*mult) * sqrt(1/2),
  * row = q6_K row tok[0] (toksrc=1) or params[2] of the [LAYERS*PD]-wide table. */
+/* LM head for n token rows (batched decode): y[n][OUT] = softcap(W x[n][N]) on the
+ * tensor cores; scratch: 2*n*N u16 (x split into f16 hi + lo). */
+E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* ctx, const uint8_t* w, const float* x, uint16_t* scratch, float* y, int N,
+                                int OUT, float softcap, int n);
 E4B_API int e4b_pleprep(e4b_ctx* ctx, const uint8_t* table, const uint32_t* params, const uint32_t* tok,
                         const float* proj, const float* norm_w, float* ple_in, int PD, int LAYERS, int rows,
                         float mult, float proj_scale, float eps, int toksrc);
@@ -235,6 +244,20 @@ E4B_API int e4b_plegatemv(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, con
                           int IN, int OUT, int off);
 /* kernels/plemul.wgsl:6-12: y[i] = gelu_tanh(a[i]) * ple[off+i]. */
 E4B_API int e4b_plemul(e4b_ctx* ctx, const float* a, const float* ple, float* y, int N, int off);
+
+/* ---- batched decode of nseq sequences at one common position (params[0],
+ * kvCount params[4]); sequence b's KV cache starts at cache + b * slots*KVH*HD,
+ * its q / qkv / partial / output rows are row b of the per-sequence layouts. */
+E4B_API int e4b_headprep_seq(e4b_ctx* ctx, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
+                             uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
+                             int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
+                             int cache_slots, int nseq);
+E4B_API int e4b_attsplit_seq(e4b_ctx* ctx, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                             const uint32_t* params, float* part_o, float* part_ml, int QH, int KVH, int HD,
+                             int window, int cachemode, int ring, int chunk, int max_chunks, float scale,
+                             int cache_slots, int nseq);
+E4B_API int e4b_attcomb_seq(e4b_ctx* ctx, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
+                            float* lse, int QH, int HD, int max_chunks, int nseq);
 
 /* ------------------------------------------------------------ argmax / feed */
 /* kernels/argmax2.wgsl:8-48 (both stages): out[0] = index of the largest x (ties
@@ -250,6 +273,12 @@ E4B_API int e4b_argmax_static(e4b_ctx* ctx, const float* x, uint32_t* out, int N
  * the per-token parameter advance (src/engine-a4b.js:793-795), on the device:
  * ring[params[6] % ring_cap] = amax[0]; params[2] = amax[0]; pos/len/kvCount/index += 1. */
 E4B_API int e4b_feedtok(e4b_ctx* ctx, const uint32_t* amax, uint32_t* params, uint32_t* ring, int ring_cap);
+/* argmax of each of `rows` rows of x[rows][N] -> out[rows][2]; part: 2*parts*rows u32. */
+E4B_API int e4b_argmax_rows(e4b_ctx* ctx, const float* x, uint32_t* part, uint32_t* out, int N, int parts, int rows);
+/* feedtok for `rows` sequences in lockstep: tok[b] = amax[2b], ring[b][params[6] % ring_cap]
+ * = tok[b] (ring may be NULL), params[2] = tok[0]; the shared positions advance once. */
+E4B_API int e4b_feedtok_rows(e4b_ctx* ctx, const uint32_t* amax, uint32_t* params, uint32_t* ring, int ring_cap,
+                             uint32_t* tok, int rows);
 
 /* ------------------------------------------------------------ fused token plan */
 /* One dense (E4B-graph) decoder layer: q4_0 weights as stored in the GGUF
