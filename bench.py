@@ -169,6 +169,115 @@ def bench_config(e4b, args):
     return cfg
 
 
+def moe_step_bytes(cfg, B: int, ctx_len: int) -> dict:
+    """Algorithmic HBM bytes of one batched MoE decode step (B tokens): every dense
+    / attention / router weight once, the experts the step touches (expected
+    unique experts of B tokens x top-K without replacement: E (1 - (1 - K/E)^B)),
+    the q6_K LM head, the B embedding rows and every sequence's KV over its
+    attended positions plus the new K/V."""
+    H, L, E, K = cfg.hidden, cfg.layers, cfg.experts, cfg.topk
+    q4 = lambda rows, n_in: rows * n_in // 32 * 18
+    uniq = E * (1.0 - (1.0 - K / E) ** B)
+    expert = q4(2 * cfg.expert_ff, H) + q4(H, cfg.expert_ff)
+    w = 0
+    for l in range(L):
+        w += q4(cfg.qkv_rows(l), H) + q4(H, cfg.q_dim) + q4(2 * cfg.ff, H) + q4(H, cfg.ff) + E * H * 4
+        w += int(uniq * expert)
+    head = cfg.vocab * H // 256 * 210
+    per_pos = cfg.kv_heads * cfg.head_dim * 2 * 2
+    kv = 0
+    for l in range(L):
+        att = min(ctx_len, cfg.window) if cfg.is_sliding(l) else ctx_len
+        kv += B * (att + 1) * per_pos
+    emb = B * (H // 256 * 210)
+    return {"weights": w, "lm_head": head, "embed": emb, "kv": kv, "unique_experts_per_layer": round(uniq, 1),
+            "total": w + head + emb + kv}
+
+
+def run_moe_batch(args, rank, world, local_rank):
+    """BASELINE configs 4/5: B sequences decoded in lockstep through the grouped
+    MoE path; value = tokens of all sequences / device time."""
+    import ctypes
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    import __graft_entry__
+    __graft_entry__.build()
+    dist = Dist(world, local_rank, "nccl" if world > 1 else None)
+    if world > 1:
+        raise SystemExit("--batch on more than one GPU needs expert parallelism (not in this build)")
+    cfg = bench_config(e4b, args)
+    B = args.batch
+    t0 = time.time()
+    img = e4b.synth.build_model(cfg, seed=0)
+    t_build = time.time() - t0
+    eng = e4b.BatchEngine(img, B, local_rank)
+    dev = eng.dev
+    prompts = np.stack([e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=1000 + b) for b in range(B)])
+    t1 = time.time()
+    eng.prefill(prompts)
+    dev.sync()
+    t_prefill = time.time() - t1
+    pos = args.prefill
+    eng.decode_chunk(args.warmup)
+    dev.sync()
+    pos += args.warmup
+    ctx_mid = pos + args.steps // 2
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    dev.sync()
+    dev.call("e4b_event_record", 0)
+    eng.decode_chunk(args.steps)
+    dev.call("e4b_event_record", 1)
+    dev.sync()
+    ms = ctypes.c_float()
+    dev.call("e4b_event_elapsed", 0, 1, ctypes.byref(ms))
+    t_dev = ms.value / 1000.0
+    pos += args.steps
+    clk = clocks.stop()
+    # end to end: per step the B tokens go host -> device and the B results come back
+    toks = eng.dev.read(eng.A.tok, np.uint32, B)
+    host = np.empty(B, np.uint32)
+    dev.sync()
+    dev.call("e4b_event_record", 2)
+    for i in range(args.steps):
+        eng.step(toks, pos)
+        dev.call("e4b_download", host.ctypes.data_as(ctypes.c_void_p), eng.A.tok.ptr, ctypes.c_size_t(4 * B))
+        toks = host.copy()
+        pos += 1
+    dev.call("e4b_event_record", 3)
+    dev.sync()
+    dev.call("e4b_event_elapsed", 2, 3, ctypes.byref(ms))
+    t_e2e = ms.value / 1000.0
+    status = dev.status()
+    kpt = eng.kernels_per_token
+    eng.close()
+    if status:
+        raise RuntimeError(f"device status word {status:#x} after the run")
+    peak, peak_kind = peaks()
+    sb = moe_step_bytes(cfg, B, ctx_mid)
+    value = B * args.steps / t_dev
+    ach = sb["total"] * args.steps / t_dev / 1e9
+    out = {
+        "metric": f"MoE decode tok/s bs{B} A4B-shaped (batched, grouped experts)", "value": round(value, 2),
+        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * t_dev / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_0/q6_K weights, f32 accumulate, f16 activations",
+        "data": "synthetic: seeded N(0,0.02) weights quantised to q4_0/q6_K, uniform prompt ids",
+        "config": {"workload": f"{cfg.name}: {B} sequences in lockstep after a {args.prefill}-token prefill",
+                   "model": cfg.name, "global_batch": B, "seq_len": ctx_mid, "parallelism": "single",
+                   "l2": "weights (%.1f GB/step) >> 126 MB L2: no flush needed" % (sb["total"] / 1e9)},
+        "e2e": {"value": round(B * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B + 32,
+                "d2h_bytes_per_step": 4 * B},
+        "roofline": {"bound": "hbm", "kernel": "whole step (all kernels)", "achieved": round(ach, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(ach / peak, 4), "peak_source": peak_kind,
+                     "bytes_per_step": sb, "traffic": None},
+        "clocks": clk, "gpu_launches": int(kpt * args.steps), "kernels_per_step": kpt,
+        "prefill_s": round(t_prefill, 1), "model_build_s": round(t_build, 1),
+    }
+    dist.close()
+    return out, img, cfg
+
+
 def run_ours(args, rank, world, local_rank):
     e4b = importlib.import_module("e4b-webgpu_b200")
     import __graft_entry__
@@ -500,6 +609,7 @@ def main():
     ap.add_argument("--config", default="e4b")
     ap.add_argument("--prefill", type=int, default=512)
     ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling cases)")
+    ap.add_argument("--batch", type=int, default=1, help="sequences decoded in lockstep (MoE configs)")
     ap.add_argument("--fused", type=int, default=1, help="1: fused token kernel where the model allows it; "
                                                           "0: one kernel per operator")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
@@ -523,6 +633,10 @@ def main():
     rank, world, local_rank = dist_env()
     if args.impl == "reference":
         out = run_reference(args, rank, world)
+    elif args.batch > 1:
+        out, img, cfg = run_moe_batch(args, rank, world, local_rank)
+        if rank == 0:
+            out["cpu_baseline"] = None if args.no_cpu else cpu_baseline(img, cfg, args.cpu_budget, 8)
     else:
         out, img, cfg = run_ours(args, rank, world, local_rank)
         if rank == 0:

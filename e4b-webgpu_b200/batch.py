@@ -16,6 +16,10 @@ src/engine-a4b.js:467-585 does for prefill):
   experts      e4b_expgroup -> e4b_q40gugrp -> e4b_q40downgrp -> e4b_wacc
   tail         e4b_a4btail        (rows = B)
 
+Every f16 activation that feeds a q4_0 GEMM (normed rows, attention output,
+MoE input, GeGLU outputs) is kept in fragment order (xfo_perm), written so
+by its producer.
+
 then the final norm, e4b_q6k_lmhead_rows, e4b_argmax_rows and
 e4b_feedtok_rows (each sequence's greedy token fed back on the device).
 """
@@ -30,6 +34,39 @@ from . import ops
 from .engine import Engine, RING_CAP, ARGMAX_PARTS, F32
 
 C = ctypes.c_void_p
+
+
+def xfo_perm(n: int) -> np.ndarray:
+    """Fragment order of an f16 activation row of n elements (n % 32 == 0):
+    element i is stored at half xfo_perm(n)[i].  Inside each 32-element block
+    the 8 values MMA lane t reads (indices 4t..4t+3 in odd blocks, 2+4t..5+4t or
+    {0, 1, 14, 15} for t = 3 in even blocks, and the same + 16) are contiguous
+    at halves 8t..8t+7 in the order [j0, j2, j1, j3, j0+16, j2+16, j1+16, j3+16]."""
+    assert n % 32 == 0
+    pos = np.empty(n, np.int64)
+    for i in range(n):
+        b, j = divmod(i, 32)
+        hi, jj = divmod(j, 16)
+        if b & 1:
+            t, r = divmod(jj, 4)
+        elif 2 <= jj < 14:
+            t, r = divmod(jj - 2, 4)
+        else:
+            t, r = 3, (jj if jj < 2 else jj - 12)
+        slot = {0: 0, 1: 2, 2: 1, 3: 3}[r]
+        pos[i] = 32 * b + 8 * t + 4 * hi + slot
+    return pos
+
+
+def to_xfo(x: np.ndarray) -> np.ndarray:
+    """Rows of x (last axis) permuted into fragment order."""
+    out = np.empty_like(x)
+    out[..., xfo_perm(x.shape[-1])] = x
+    return out
+
+
+def from_xfo(x: np.ndarray) -> np.ndarray:
+    return x[..., xfo_perm(x.shape[-1])]
 
 
 class BatchEngine(Engine):
@@ -72,12 +109,15 @@ class BatchEngine(Engine):
         A.yo = d.alloc(B * K * H * 4, "expOut")
         A.moe_out = d.alloc(B * H * 4, "moeOut")
         A.xf = d.alloc(B * H * 4, "xfinal")
-        A.xsplit = d.alloc(2 * B * H * 2, "xSplit")
+        A.xsplit = d.alloc(2 * ((B + 7) // 8 * 8) * H * 2, "xSplit")
         A.logits = d.alloc(B * c.vocab * 4, "logits")
         A.amax_part = d.alloc(B * ARGMAX_PARTS * 8, "amaxPart")
         A.amax = d.alloc(B * 8, "amax")
         A.ring = d.alloc(B * RING_CAP * 4, "tokRing")
         self.A = A
+        ws = int(d.L.e4b_workspace_bytes())
+        A.ws = d.alloc(ws, "workspace")
+        d.call("e4b_set_workspace", A.ws.ptr, ctypes.c_size_t(ws))
         p = ctypes.c_void_p()
         d.call("e4b_host_alloc", ctypes.c_size_t(32), ctypes.byref(p))
         self.host_params = np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint32)), shape=(8,))
@@ -89,7 +129,7 @@ class BatchEngine(Engine):
         H, V, E, K, EF, FF = c.hidden, c.vocab, c.experts, c.topk, c.expert_ff, c.ff
         d.call("e4b_q6k_embed", self.emb, A.params, A.tok, A.hidden, H, V, ctypes.c_float(F32(math.sqrt(H))), 1, B)
         d.call("e4b_rmsnorm", A.hidden, self.layers[0].attn_norm, None, None, A.normed, H, B, ctypes.c_float(c.eps),
-               1, 0, 1)
+               1, 0, 2)
         for L in self.layers:
             nxt = self.layers[L.i + 1].attn_norm if L.i + 1 < c.layers else None
             d.call("e4b_q40mm", A.normed, L.qkv, A.qkv, H, L.qkv_rows, B)
@@ -99,10 +139,11 @@ class BatchEngine(Engine):
             d.call("e4b_attsplit_seq", A.q, L.kc, L.vc, A.params, A.part_o, A.part_ml, c.q_heads, c.kv_heads,
                    c.head_dim, c.window if L.sliding else 0, L.cachemode, L.ring, self.chunk, L.max_chunks,
                    ctypes.c_float(1.0), L.slots, B)
-            d.call("e4b_attcomb_seq", A.part_o, A.part_ml, A.attn, None, None, c.q_heads, c.head_dim, L.max_chunks, B)
+            d.call("e4b_attcomb_seq", A.part_o, A.part_ml, A.attn, None, None, c.q_heads, c.head_dim, L.max_chunks, B,
+                   1)
             d.call("e4b_q40mm", A.attn, L.o, A.tmp, c.q_dim, H, B)
             d.call("e4b_rmsacc3", A.tmp, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
-                   A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B)
+                   A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B, 1)
             d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
             d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
             d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
@@ -112,7 +153,7 @@ class BatchEngine(Engine):
             d.call("e4b_wacc", A.yo, A.inv, A.topk_w, A.moe_out, B, K, H)
             d.call("e4b_a4btail", A.tmp, L.post_ffw1, A.moe_out, L.post_ffw2, L.post_ffw, A.hidden_b,
                    nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
-                   ctypes.c_float(L.scale), int(nxt is not None), B)
+                   ctypes.c_float(L.scale), int(nxt is not None), B, 1)
         d.call("e4b_rmsnorm", A.hidden, self.out_norm, A.xf, None, None, H, B, ctypes.c_float(c.eps), 1, 0, 0)
         d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)
         d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)

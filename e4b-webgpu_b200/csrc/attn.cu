@@ -188,7 +188,7 @@ __global__ void k_attsplit(const float* __restrict__ q, const uint16_t* __restri
 
 __global__ void k_attcomb(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                           uint16_t* __restrict__ out_h, float* __restrict__ out_f, float* __restrict__ lse, int HD,
-                          int max_chunks) {
+                          int max_chunks, int xfo) {
   pdl_wait();
   {   // sequence blockIdx.y
     const size_t z = blockIdx.y, QH = gridDim.x;
@@ -211,7 +211,7 @@ __global__ void k_attcomb(const float* __restrict__ part_o, const float* __restr
     for (int c = 0; c < max_chunks; c++)
       if (ml[2 * c + 1] > 0.f) acc = fmaf(part_o[((size_t)h * max_chunks + c) * HD + d], expf(ml[2 * c] - M), acc);
     const float v = den > 0.f ? acc / den : 0.f;
-    if (out_h) out_h[(size_t)h * HD + d] = f2h(v);
+    if (out_h) out_h[xfo ? xfo_pos(h * HD + d) : h * HD + d] = f2h(v);
     if (out_f) out_f[(size_t)h * HD + d] = v;
   }
   if (lse && threadIdx.x == 0) lse[h] = den > 0.f ? M + logf(den) : -INFINITY;
@@ -307,16 +307,17 @@ E4B_API int e4b_attcomb(e4b_ctx* c, const float* part_o, const float* part_ml, u
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, part_o && part_ml && (out_h || out_f) && QH > 0 && HD > 0 && max_chunks > 0, "attcomb: bad args");
   return e4b_launch(c, "attcomb", k_attcomb, dim3(QH), dim3(128), 0, part_o, part_ml, out_h, out_f, lse, HD,
-                    max_chunks);
+                    max_chunks, 0);
 }
 
 E4B_API int e4b_attcomb_seq(e4b_ctx* c, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
-                            float* lse, int QH, int HD, int max_chunks, int nseq) {
+                            float* lse, int QH, int HD, int max_chunks, int nseq, int xfo) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, part_o && part_ml && (out_h || out_f) && QH > 0 && HD > 0 && max_chunks > 0 && nseq > 0,
               "attcomb_seq: bad args");
+  E4B_REQUIRE(c, !xfo || (QH * HD) % 32 == 0, "attcomb_seq: fragment order needs QH*HD %% 32 == 0");
   return e4b_launch(c, "attcomb_seq", k_attcomb, dim3(QH, nseq), dim3(128), 0, part_o, part_ml, out_h, out_f, lse,
-                    HD, max_chunks);
+                    HD, max_chunks, xfo);
 }
 
 }  // extern "C"

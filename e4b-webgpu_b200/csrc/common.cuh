@@ -128,6 +128,30 @@ E4B_DEV float gelu_tanh(float g) {
   return (0.5f * g) * (1.0f + tanhf(t));
 }
 
+// ---- fragment order ("xfo") of an f16 activation row that feeds a multi-token
+// q4_0 GEMM: inside each 32-element block, the 8 values lane t of an
+// m16n8k16 B fragment needs (the k order the q4_0 nibble bytes give its A
+// fragment) sit contiguously at halves 8t..8t+7, so one 16-byte load fetches
+// them.  Lane t's indices j0..j3 (low half; +16 for the high half) are
+// 4t..4t+3 in odd blocks, 2+4t..5+4t (t < 3) or {0, 1, 14, 15} (t = 3) in even
+// blocks, stored as [j0, j2, j1, j3, j0+16, j2+16, j1+16, j3+16].
+E4B_DEV int xfo_pos(int i) {
+  const int b = i >> 5, j = i & 31, hi = j >> 4, jj = j & 15;
+  int t, r;
+  if (b & 1) {
+    t = jj >> 2;
+    r = jj & 3;
+  } else if (jj >= 2 && jj < 14) {
+    t = (jj - 2) >> 2;
+    r = (jj - 2) & 3;
+  } else {
+    t = 3;
+    r = jj < 2 ? jj : jj - 12;
+  }
+  const int slot = r == 1 ? 2 : (r == 2 ? 1 : r);
+  return (b << 5) + (t << 3) + (hi << 2) + slot;
+}
+
 // ---- q4_0: 18-byte block = f16 d, 16 bytes of nibbles (byte j: elem j | elem j+16 << 4)
 struct Q40Block {
   float d;

@@ -1,22 +1,18 @@
-// Grouped MoE for batched decode (kernels/expgroup.wgsl, q40gugrp.wgsl,
-// q40downgrp.wgsl, wacc.wgsl): the B x K (token, slot) routing entries are
-// sorted by expert, each expert's weights are read once for all the tokens
-// routed to it, and the per-entry outputs are combined per token in slot order.
-//
-// GEMM formulation: an expert's rows x its tokens on the tensor cores
-// (mma.sync m16n8k16, f16 x f16 -> f32), tokens as the 8 columns of B.  A q4_0
-// block's scale multiplies all of that block's products, so each block is one
-// K-step with its own accumulator that is scaled in f32 and added, keeping the
-// reference's arithmetic (d * sum (n-8) x per block, f32 sums) exactly as the
-// single-token kernels do.  Warps of a CTA split the blocks of the row and
-// reduce through shared memory.
+// Grouped MoE and multi-token q4_0 GEMMs for batched decode (kernels/expgroup.wgsl,
+// q40gugrp.wgsl, q40downgrp.wgsl, wacc.wgsl): the B x K (token, slot) routing
+// entries are sorted by expert, each expert's weights are streamed once for all
+// the tokens routed to it, and the per-entry outputs are combined per token in
+// slot order.  The dense batched GEMMs of the same step (q|k|v, o, shared FFN)
+// run through the same kernel with one matrix and the batch's tokens.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "q40_frag.cuh"
+#include "q40_stream.cuh"
 
 namespace {
 using namespace e4b;
 
-constexpr int kGW = 4;          // warps per CTA
-constexpr int kGroups = 8;      // 8-token groups per pass (64 tokens)
 
 // ---- routing entries sorted by expert (stable: increasing token * K + slot)
 __global__ void k_expgroup(const uint32_t* __restrict__ topk, int n, int E, uint32_t* __restrict__ offsets,
@@ -62,83 +58,120 @@ __global__ void k_expgroup(const uint32_t* __restrict__ topk, int n, int E, uint
   }
 }
 
-// ---- grouped q4_0 GEMM: rows of expert e x the tokens routed to it.
-// EPI 0: y[pos][row] = W_e x_token (f32); EPI 1: rows [gate FF | up FF] ->
-// yh[pos][o] = f16(gelu(gate_o) * up_o).  Tile = 32 rows (EPI 1: 16 gate + 16 up).
-// XPOS: x row of entry p is x[entries[p] / K] (token rows) or x[p] (entry rows).
-template <int EPI, int XPOS>
-__global__ void __launch_bounds__(32 * kGW) k_grp(const uint16_t* __restrict__ x, const uint8_t* __restrict__ w,
-                                                   const uint32_t* __restrict__ offsets,
-                                                   const uint32_t* __restrict__ entries, float* __restrict__ y,
-                                                   uint16_t* __restrict__ yh, int IN, int ROWS, int FF, int K,
-                                                   int n_direct) {
-  pdl_wait();
-  __shared__ float red[kGW][32][kGroups * 8];
-  const int e = blockIdx.y, tile = blockIdx.x;
-  // n_direct > 0: one matrix, tokens 0..n_direct-1 in order (dense batched GEMM)
-  const uint32_t p0 = n_direct > 0 ? 0u : offsets[e], ne = n_direct > 0 ? (uint32_t)n_direct : offsets[e + 1] - p0;
-  if (ne == 0) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int nb = IN >> 5;
-  const size_t rowbytes = (size_t)nb * 18;
-  const uint8_t* we = w + (size_t)e * ROWS * rowbytes;
-  // this lane's rows: subtile s, row g (+8)
-  int rows[2][2];
-  for (int s = 0; s < 2; s++) {
-    const int base = EPI == 1 ? (s == 0 ? 16 * tile : FF + 16 * tile) : 32 * tile + 16 * s;
-    rows[s][0] = base + g;
-    rows[s][1] = base + g + 8;
+// ---- multi-token q4_0 GEMM (grouped experts or one dense matrix).
+//
+// Work: a chunk is up to kTokC tokens of one matrix (an expert's sorted
+// entries, or consecutive tokens of the dense batch); an item is a chunk x W
+// consecutive row tiles, one tile per warp.  Every CTA of a persistent grid owns
+// a contiguous range of items (chunk-major, so consecutive items share their
+// activations).  Per chunk the CTA stages the tokens' activation rows, already
+// in fragment order, into shared memory once (one bulk copy per token); each
+// warp streams its tile's weights through its own mbarrier ring:
+//   MODE 0: 2-D TMA boxes of 16 rows x 8 blocks (144 B per row, conflict-free
+//           nibble reads); a quantum is two boxes (32 rows x 8 blocks).  Needs
+//           16-byte row strides (IN % 256 == 0).
+//   MODE 1: one 1-D bulk copy of 16 whole rows (any IN with 4-byte rows); a
+//           tile is 16 rows and one quantum holds all of K.
+// Math: per q4_0 block and 16-row subtile, two m16n8k16 MMAs (A = nibbles - 8,
+// exact in f16; B = 8 tokens' activations) give sum (n-8) x for the block; its
+// f16 scale multiplies that in f32 (the single-token kernels' arithmetic).
+// Epilogues: EPI 0 y[pos][row] (f32); EPI 1 tiles pair 16 gate rows with the
+// matching 16 up rows and write yh[pos][o] = f16(gelu(gate) * up) in fragment
+// order, ready to be the next GEMM's activations.
+constexpr int kTokC = 16;        // tokens per chunk (two 8-column MMA groups)
+constexpr int kMaxChunks = 512;  // chunk list capacity (shared memory)
+
+struct Chunk {
+  uint32_t e, p0, n;             // matrix, first position (sorted entry or token), tokens
+};
+
+struct QmmP {
+  const uint16_t* x;             // activation rows in fragment order, IN wide
+  const uint8_t* w;              // weights (MODE 1 addressing)
+  const uint32_t* offsets;       // [E+1] sorted-entry offsets; null: dense over n_dense tokens
+  const uint32_t* entries;       // non-null: x row of position p = entries[p] / K; null: x row = p
+  float* y;
+  uint16_t* yh;
+  uint32_t* status;
+  int IN, nb, rowbytes, ROWS, FF, K, E, n_dense;
+  int tiles;                     // tiles per matrix
+  int nq;                        // quanta per tile
+  int RR;                        // items per chunk = ceil(tiles / W)
+  int xpitch;                    // staged activation row pitch (halves)
+};
+
+E4B_DEV uint4 lds128(const uint16_t* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
+// Chunk list of this launch (warp 0; dense: arithmetic, grouped: a warp scan of
+// the experts' entry counts).  Returns the number of chunks.
+E4B_DEV int build_chunks(const QmmP& p, Chunk* ch, int lane) {
+  if (!p.offsets) {
+    const int n = (p.n_dense + kTokC - 1) / kTokC;
+    for (int c = lane; c < n && c < kMaxChunks; c += 32)
+      ch[c] = Chunk{0u, (uint32_t)(kTokC * c), (uint32_t)min(kTokC, p.n_dense - kTokC * c)};
+    return min(n, kMaxChunks);
   }
-  Lane L;
-  L.o_odd = 2 + 4 * t;
-  L.o_e1 = t < 3 ? 4 + 4 * t : 0;
-  L.sel = t < 3 ? 0x3210u : 0x5432u;
-  // B holds tokens as columns, so its element order follows the block's parity
-  // (the A nibble layout), not the column index
-  const XLane Xe = xlane(0, t), Xo = xlane(1, t);
-  for (uint32_t pass = 0; pass < ne; pass += kGroups * 8) {
-    const int ng = (int)min((uint32_t)kGroups, (ne - pass + 7) / 8);
-    // this lane's token (column g) of every group
-    const uint16_t* xr[kGroups];
+  int base = 0;
+  for (int e0 = 0; e0 < p.E; e0 += 32) {
+    const int e = e0 + lane;
+    const uint32_t a = e < p.E ? p.offsets[e] : 0u, b = e < p.E ? p.offsets[e + 1] : 0u;
+    const int n = (int)(b - a), c = (n + kTokC - 1) / kTokC;
+    int inc = c;
 #pragma unroll
-    for (int q = 0; q < kGroups; q++) {
-      const uint32_t j = pass + 8 * q + g;
-      xr[q] = nullptr;
-      if (q < ng && j < ne) xr[q] = x + (size_t)(XPOS ? p0 + j : entries[p0 + j] / (uint32_t)K) * IN;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
     }
-    float acc[kGroups][2][4];
+    const int ex = base + inc - c;
+    for (int j = 0; j < c; j++)
+      if (ex + j < kMaxChunks) ch[ex + j] = Chunk{(uint32_t)e, a + (uint32_t)(kTokC * j), (uint32_t)min(kTokC, n - kTokC * j)};
+    base += __shfl_sync(0xffffffffu, inc, 31);
+  }
+  if (base > kMaxChunks) {
+    if (lane == 0) set_status(p.status, E4B_ST_BADINDEX);
+    base = kMaxChunks;
+  }
+  return base;
+}
+
+// One staged quantum: NS 16-row subtiles (sub_bytes apart, row pitch `pitch`),
+// blocks [0, nblk) of the stage = global blocks kb0 + k (kb0 even).
+template <int NS>
+E4B_DEV void qmm_stage(const uint8_t* st, int pitch, int sub_bytes, int nblk, int kb0, const uint16_t* xr0,
+                       const uint16_t* xr1, bool two, const Lane& L, float (&acc)[2][2][4]) {
+  const uint8_t* r0 = st;
+  const uint8_t* r1 = st + 8 * pitch;
+  for (int k = 0; k < nblk; k += 2) {
 #pragma unroll
-    for (int q = 0; q < kGroups; q++)
+    for (int par = 0; par < 2; par++) {
+      const int kk = k + par;
+      uint32_t A[NS][8];
+      float d[NS][2];
 #pragma unroll
-      for (int s = 0; s < 2; s++)
+      for (int s = 0; s < NS; s++) {
+        const uint8_t* a = r0 + s * sub_bytes + 18 * kk;
+        const uint8_t* b = r1 + s * sub_bytes + 18 * kk;
+        const uint32_t va = par ? nib_odd(a, L) : nib_even(a, L);
+        const uint32_t vb = par ? nib_odd(b, L) : nib_even(b, L);
+        dq_row(va, A[s][0], A[s][1], A[s][2], A[s][3]);
+        dq_row(vb, A[s][4], A[s][5], A[s][6], A[s][7]);
+        d[s][0] = h2f(*reinterpret_cast<const uint16_t*>(a));
+        d[s][1] = h2f(*reinterpret_cast<const uint16_t*>(b));
+      }
+      const int kb = kb0 + kk;
 #pragma unroll
-        for (int r = 0; r < 4; r++) acc[q][s][r] = 0.f;
-    for (int b = warp; b < nb; b += kGW) {
-      uint32_t A[2][8];
-      float d[2][2];
+      for (int q = 0; q < 2; q++) {
+        if (q == 1 && !two) break;
+        const uint4 xb = lds128((q ? xr1 : xr0) + 32 * kb);
 #pragma unroll
-      for (int s = 0; s < 2; s++)
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const int row = rows[s][h];
-          if (row < ROWS) {   // rows beyond the matrix read as zero
-            const uint8_t* blk = we + (size_t)row * rowbytes + (size_t)b * 18;
-            dq_row(nib(blk, b, L), A[s][4 * h], A[s][4 * h + 1], A[s][4 * h + 2], A[s][4 * h + 3]);
-            d[s][h] = h2f(__ldg(reinterpret_cast<const uint16_t*>(we + (size_t)row * rowbytes + (size_t)b * 18)));
-          } else {
-            A[s][4 * h] = A[s][4 * h + 1] = A[s][4 * h + 2] = A[s][4 * h + 3] = 0u;
-            d[s][h] = 0.f;
-          }
-        }
-      // the block's scales of the rows this lane's C fragment holds (rows g, g+8)
-#pragma unroll
-      for (int q = 0; q < kGroups; q++) {
-        if (q >= ng) break;
-        const uint4 xb = xr[q] ? xfrag_f16(xr[q], b, (b & 1) ? Xo : Xe) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < NS; s++) {
           float c[4] = {0.f, 0.f, 0.f, 0.f};
-          // A regs: [row g: lo02, lo13, hi02, hi13 | row g+8: ...]
           mma16816(c, A[s][0], A[s][4], A[s][1], A[s][5], xb.x, xb.y);
           mma16816(c, A[s][2], A[s][6], A[s][3], A[s][7], xb.z, xb.w);
           acc[q][s][0] = fmaf(d[s][0], c[0], acc[q][s][0]);
@@ -148,43 +181,141 @@ __global__ void __launch_bounds__(32 * kGW) k_grp(const uint16_t* __restrict__ x
         }
       }
     }
-    // reduce the warps' block subsets (fixed order)
+  }
+}
+
+template <int MODE, int EPI, int W, int S>
+__global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_constant__ CUtensorMap map) {
+  constexpr int NS = MODE == 0 ? 2 : 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[W][S];
+  __shared__ __align__(8) uint64_t xbar;
+  __shared__ Chunk chunks[kMaxChunks];
+  __shared__ int s_nch;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t stage_bytes = MODE == 0 ? (uint32_t)kQuantumBytes : 16u * (uint32_t)p.rowbytes;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
+  uint8_t* stages = smem + (size_t)kTokC * p.xpitch * 2 + (size_t)warp * S * stage_bytes;
+
+  pdl_trigger();
+  if (lane == 0) {
+    if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map)) : "memory");
+    for (int s = 0; s < S; s++) mbar_init(&full[warp][s], 1);
+    if (warp == 0) mbar_init(&xbar, 1);
+    fence_barrier_init();
+  }
+  pdl_wait();
+  if (warp == 0) {
+    const int n = build_chunks(p, chunks, lane);
+    if (lane == 0) s_nch = n;
+  }
+  __syncthreads();
+  const int T = s_nch * p.RR;
+  const int i0 = (int)((int64_t)T * blockIdx.x / gridDim.x);
+  const int i1 = (int)((int64_t)T * (blockIdx.x + 1) / gridDim.x);
+
+  // producer cursor over (item, quantum) of this warp's tiles; every lane keeps it
+  auto has_tile = [&](int it) { return (it % p.RR) * W + warp < p.tiles; };
+  int pit = i0, pkq = 0;
+  while (pit < i1 && !has_tile(pit)) pit++;
+  auto issue = [&](int s) {
+    const Chunk c = chunks[pit / p.RR];
+    const int tile = (pit % p.RR) * W + warp;
+    uint8_t* st = stages + s * stage_bytes;
+    if (MODE == 0) {
+      if (lane == 0) mbar_expect_tx(&full[warp][s], (uint32_t)kQuantumBytes);
+      __syncwarp();
+      if (lane < 2) {
+        const int row = (int)c.e * p.ROWS + (EPI == 1 ? (lane == 0 ? 16 * tile : p.FF + 16 * tile) : 32 * tile + 16 * lane);
+        tma_load_2d(st + lane * kSubBytes, &map, pkq * 18, row, &full[warp][s]);
+      }
+    } else if (lane == 0) {
+      mbar_expect_tx(&full[warp][s], stage_bytes);
+      bulk_g2s(st, p.w + ((size_t)c.e * p.ROWS + 16 * (size_t)tile) * p.rowbytes, stage_bytes, &full[warp][s]);
+    }
+    if (++pkq == p.nq) {
+      pkq = 0;
+      do pit++; while (pit < i1 && !has_tile(pit));
+    }
+  };
 #pragma unroll
-    for (int q = 0; q < kGroups; q++)
+  for (int s = 0; s < S; s++)
+    if (pit < i1) issue(s);
+
+  Lane L;
+  L.o_odd = 2 + 4 * t;
+  L.o_e1 = t < 3 ? 4 + 4 * t : 0;
+  L.sel = t < 3 ? 0x3210u : 0x5432u;
+  bool ok = true;
+  int cur = -1, restage = 0, used = 0;
+  for (int it = i0; it < i1; it++) {
+    const int ci = it / p.RR;
+    const Chunk c = chunks[ci];
+    if (ci != cur) {
+      // every warp is done with the previous chunk's activations
+      __syncthreads();
+      if (warp == 0) {
+        if (lane == 0) mbar_expect_tx(&xbar, c.n * (uint32_t)p.IN * 2u);
+        __syncwarp();
+        if (lane < (int)c.n) {
+          const uint32_t pos = c.p0 + lane;
+          const uint32_t row = !p.offsets ? pos : (p.entries ? p.entries[pos] / (uint32_t)p.K : pos);
+          bulk_g2s(xs + (size_t)lane * p.xpitch, p.x + (size_t)row * p.IN, (uint32_t)p.IN * 2u, &xbar);
+        }
+      }
+      if (ok) ok = mbar_wait(&xbar, (uint32_t)(restage & 1), p.status);
+      restage++;
+      cur = ci;
+    }
+    if (!has_tile(it)) continue;
+    const int tile = (it % p.RR) * W + warp;
+    const bool two = c.n > 8;
+    const uint16_t* xr0 = xs + (size_t)g * p.xpitch + 8 * t;
+    const uint16_t* xr1 = xr0 + (size_t)8 * p.xpitch;
+    float acc[2][2][4];
+#pragma unroll
+    for (int q = 0; q < 2; q++)
 #pragma unroll
       for (int s = 0; s < 2; s++)
 #pragma unroll
-        for (int r = 0; r < 4; r++) red[warp][lane][q * 8 + s * 4 + r] = acc[q][s][r];
-    __syncthreads();
-    for (int i = threadIdx.x; i < 32 * ng * 8; i += blockDim.x) {
-      const int ln = i / (ng * 8), k = i % (ng * 8);
-      float v = 0.f;
-      for (int ww = 0; ww < kGW; ww++) v += red[ww][ln][k];
-      red[0][ln][k] = v;
+        for (int r = 0; r < 4; r++) acc[q][s][r] = 0.f;
+    for (int kq = 0; kq < p.nq; kq++, used++) {
+      const int s = used % S;
+      if (ok) ok = mbar_wait(&full[warp][s], (uint32_t)((used / S) & 1), p.status);
+      if (ok) {
+        const uint8_t* st = stages + s * stage_bytes + (size_t)g * (MODE == 0 ? kRowPitch : p.rowbytes);
+        if (MODE == 0)
+          qmm_stage<NS>(st, kRowPitch, kSubBytes, min(8, p.nb - 8 * kq), 8 * kq, xr0, xr1, two, L, acc);
+        else
+          qmm_stage<NS>(st, p.rowbytes, 0, p.nb, 0, xr0, xr1, two, L, acc);
+      }
+      // this lane's reads of the stage fed the MMAs above; refill it
+      __syncwarp();
+      if (ok && pit < i1) issue(s);
     }
-    __syncthreads();
-    // C layout: c0, c1 = row g, columns 2t, 2t+1; c2, c3 = row g+8
-    for (int i = threadIdx.x; i < 32 * ng; i += blockDim.x) {
-      const int ln = i % 32, q = i / 32, gg = ln >> 2, tt = ln & 3;
-      const float* v = red[0][ln] + q * 8;
+    if (!ok) continue;
+    // C fragment: [q][s][0..1] row g, tokens 8q+2t, +1; [2..3] row g+8
+#pragma unroll
+    for (int q = 0; q < 2; q++)
+#pragma unroll
       for (int col = 0; col < 2; col++) {
-        const uint32_t j = pass + 8 * q + 2 * tt + col;
-        if (j >= ne) continue;
-        const uint32_t pos = p0 + j;
+        const int j = 8 * q + 2 * t + col;
+        if (j >= (int)c.n) continue;
+        const size_t pos = c.p0 + j;
+#pragma unroll
         for (int h = 0; h < 2; h++) {
-          const float a0 = v[0 * 4 + 2 * h + col], a1 = v[1 * 4 + 2 * h + col];
           if (EPI == 1) {
-            const int o = 16 * tile + gg + 8 * h;
-            if (o < FF) yh[(size_t)pos * FF + o] = f2h(gelu_tanh(a0) * a1);
+            const int o = 16 * tile + g + 8 * h;
+            if (o < p.FF) p.yh[pos * p.FF + xfo_pos(o)] = f2h(gelu_tanh(acc[q][0][2 * h + col]) * acc[q][1][2 * h + col]);
           } else {
-            const int r0 = 32 * tile + gg + 8 * h, r1 = r0 + 16;
-            if (r0 < ROWS) y[(size_t)pos * ROWS + r0] = a0;
-            if (r1 < ROWS) y[(size_t)pos * ROWS + r1] = a1;
+#pragma unroll
+            for (int s = 0; s < NS; s++) {
+              const int r = (MODE == 0 ? 32 : 16) * tile + 16 * s + g + 8 * h;
+              if (r < p.ROWS) p.y[pos * p.ROWS + r] = acc[q][s][2 * h + col];
+            }
           }
         }
       }
-    }
-    __syncthreads();
   }
 }
 
@@ -198,6 +329,82 @@ __global__ void k_wacc(const float* __restrict__ y, const uint32_t* __restrict__
   float acc = 0.f;
   for (int k = 0; k < K; k++) acc += tkw[tok * K + k] * y[(size_t)inv[tok * K + k] * OUT + o];
   out[(size_t)tok * OUT + o] = acc;
+}
+
+template <int MODE, int EPI, int W, int S>
+int qmm_launch(e4b_ctx* c, const char* name, const QmmP& p, const CUtensorMap& map, size_t smem, int grid) {
+  auto kern = k_qmm<MODE, EPI, W, S>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "%s smem attr: %s", name, cudaGetErrorString(e));
+  return e4b_launch(c, name, kern, dim3((unsigned)grid), dim3(32 * W), smem, p, map);
+}
+
+// Shared memory a variant needs: staged activations + the warps' rings.
+size_t qmm_smem(const QmmP& p, int mode, int W, int S) {
+  const size_t stage = mode == 0 ? (size_t)kQuantumBytes : 16 * (size_t)p.rowbytes;
+  return (size_t)kTokC * p.xpitch * 2 + (size_t)W * S * stage;
+}
+constexpr size_t kQmmSmemCap = 227 * 1024 - 8 * 1024;   // dynamic budget beside the static chunk list
+
+// x: activations in fragment order; grouped when offsets != null.
+int qmm(e4b_ctx* c, const char* name, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
+        const uint32_t* entries, float* y, uint16_t* yh, int IN, int ROWS, int FF, int K, int E, int n_dense,
+        int epi) {
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0,
+              "%s: weights and activations must be 16-byte aligned", name);
+  E4B_REQUIRE(c, IN > 0 && IN % 64 == 0 && IN <= 16384, "%s: IN=%d must be a multiple of 64 (<= 16384)", name, IN);
+  QmmP p = {};
+  p.x = x; p.w = w; p.offsets = offsets; p.entries = entries; p.y = y; p.yh = yh; p.status = c->status;
+  p.IN = IN; p.nb = IN / 32; p.rowbytes = p.nb * 18; p.ROWS = ROWS; p.FF = FF; p.K = K; p.E = E;
+  p.n_dense = n_dense;
+  p.xpitch = IN + 32;
+  const int mode = (IN % 256 == 0 && tensor_map_encoder() != nullptr) ? 0 : 1;
+  E4B_REQUIRE(c, mode == 0 || epi == 0, "%s: the gate|up GEMM needs IN %% 256 == 0 (IN=%d)", name, IN);
+  E4B_REQUIRE(c, mode == 0 || ROWS % 16 == 0, "%s: ROWS=%d must be a multiple of 16 for IN=%d", name, ROWS, IN);
+  p.tiles = epi == 1 ? (FF + 15) / 16 : (mode == 0 ? (ROWS + 31) / 32 : ROWS / 16);
+  p.nq = mode == 0 ? (p.nb + 7) / 8 : 1;
+  CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  if (mode == 0) {
+    const cuuint64_t gdim[2] = {(cuuint64_t)(p.rowbytes / 8), (cuuint64_t)E * (cuuint64_t)ROWS};
+    const cuuint64_t gstride[1] = {(cuuint64_t)p.rowbytes};
+    const cuuint32_t box[2] = {kRowPitch / 8, 16};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(w), gdim, gstride,
+                                      box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    E4B_REQUIRE(c, r == CUDA_SUCCESS, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  }
+  // variants: (warps, stages) that fit the shared-memory budget
+  struct V { int W, S; };
+  const V cand[4] = {{8, 3}, {8, 2}, {4, 3}, {4, 2}};
+  int vi = -1;
+  for (int i = 0; i < 4 && vi < 0; i++)
+    if (qmm_smem(p, mode, cand[i].W, cand[i].S) <= kQmmSmemCap) vi = i;
+  E4B_REQUIRE(c, vi >= 0, "%s: IN=%d needs more shared memory than a CTA has", name, IN);
+  const V v = cand[vi];
+  p.RR = (p.tiles + v.W - 1) / v.W;
+  int grid = c->sm_count;
+  if (!offsets) {
+    const int items = (n_dense + kTokC - 1) / kTokC * p.RR;
+    if (grid > items) grid = items;
+  }
+  if (grid < 1) grid = 1;
+  const size_t sm = qmm_smem(p, mode, v.W, v.S);
+#define QMM_CASE(M, EP)                                                          \
+  if (mode == M && epi == EP) {                                                  \
+    switch (vi) {                                                                \
+      case 0: return qmm_launch<M, EP, 8, 3>(c, name, p, map, sm, grid);         \
+      case 1: return qmm_launch<M, EP, 8, 2>(c, name, p, map, sm, grid);         \
+      case 2: return qmm_launch<M, EP, 4, 3>(c, name, p, map, sm, grid);         \
+      default: return qmm_launch<M, EP, 4, 2>(c, name, p, map, sm, grid);        \
+    }                                                                            \
+  }
+  QMM_CASE(0, 0)
+  QMM_CASE(0, 1)
+  QMM_CASE(1, 0)
+#undef QMM_CASE
+  return e4b_fail(c, E4B_EINVAL, "%s: no kernel variant", name);
 }
 
 }  // namespace
@@ -218,40 +425,30 @@ E4B_API int e4b_q40gugrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const 
                          const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, x && w && offsets && entries && yh, "q40gugrp: null buffer");
-  E4B_REQUIRE(c, IN > 0 && IN % 32 == 0 && FF > 0 && E > 0 && K > 0, "q40gugrp: bad sizes IN=%d FF=%d", IN, FF);
-  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 4 == 0 && (IN / 32) % 2 == 0,
-              "q40gugrp: IN/32 must be even (rows on 4-byte boundaries, word reads inside each row)");
-  return e4b_launch(c, "q40gugrp", k_grp<1, 0>, dim3((FF + 15) / 16, E), dim3(32 * kGW), 0, x, w, offsets, entries,
-                    (float*)nullptr, yh, IN, 2 * FF, FF, K, 0);
+  E4B_REQUIRE(c, FF > 0 && FF % 32 == 0 && E > 0 && E <= 4096 && K > 0, "q40gugrp: bad sizes FF=%d E=%d", FF, E);
+  return qmm(c, "q40gugrp", x, w, offsets, entries, nullptr, yh, IN, 2 * FF, FF, K, E, 0, 1);
 }
 
 E4B_API int e4b_q40downgrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
                            const uint32_t* entries, float* y, int IN, int OUT, int E) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, x && w && offsets && entries && y, "q40downgrp: null buffer");
-  E4B_REQUIRE(c, IN > 0 && IN % 32 == 0 && OUT > 0 && E > 0, "q40downgrp: bad sizes IN=%d OUT=%d", IN, OUT);
-  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 4 == 0 && (IN / 32) % 2 == 0,
-              "q40downgrp: IN/32 must be even (rows on 4-byte boundaries, word reads inside each row)");
-  return e4b_launch(c, "q40downgrp", k_grp<0, 1>, dim3((OUT + 31) / 32, E), dim3(32 * kGW), 0, x, w, offsets,
-                    entries, y, (uint16_t*)nullptr, IN, OUT, 0, 1, 0);
+  E4B_REQUIRE(c, OUT > 0 && E > 0 && E <= 4096, "q40downgrp: bad sizes OUT=%d E=%d", OUT, E);
+  return qmm(c, "q40downgrp", x, w, offsets, nullptr, y, nullptr, IN, OUT, 0, 1, E, 0, 0);
 }
 
 E4B_API int e4b_q40mm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, float* y, int IN, int OUT, int n) {
   E4B_CHECK_CTX(c);
-  E4B_REQUIRE(c, x && w && y && n > 0, "q40mm: bad args");
-  E4B_REQUIRE(c, IN > 0 && IN % 64 == 0 && OUT > 0 && reinterpret_cast<uintptr_t>(w) % 4 == 0,
-              "q40mm: IN=%d must be a multiple of 64", IN);
-  return e4b_launch(c, "q40mm", k_grp<0, 1>, dim3((OUT + 31) / 32, 1), dim3(32 * kGW), 0, x, w,
-                    (const uint32_t*)nullptr, (const uint32_t*)nullptr, y, (uint16_t*)nullptr, IN, OUT, 0, 1, n);
+  E4B_REQUIRE(c, x && w && y && n > 0 && OUT > 0, "q40mm: bad args");
+  E4B_REQUIRE(c, (n + kTokC - 1) / kTokC <= kMaxChunks, "q40mm: n=%d tokens exceed %d", n, kTokC * kMaxChunks);
+  return qmm(c, "q40mm", x, w, nullptr, nullptr, y, nullptr, IN, OUT, 0, 1, 1, n, 0);
 }
 
 E4B_API int e4b_q40gumm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, uint16_t* yh, int IN, int FF, int n) {
   E4B_CHECK_CTX(c);
-  E4B_REQUIRE(c, x && w && yh && n > 0, "q40gumm: bad args");
-  E4B_REQUIRE(c, IN > 0 && IN % 64 == 0 && FF > 0 && reinterpret_cast<uintptr_t>(w) % 4 == 0,
-              "q40gumm: IN=%d must be a multiple of 64", IN);
-  return e4b_launch(c, "q40gumm", k_grp<1, 1>, dim3((FF + 15) / 16, 1), dim3(32 * kGW), 0, x, w,
-                    (const uint32_t*)nullptr, (const uint32_t*)nullptr, (float*)nullptr, yh, IN, 2 * FF, FF, 1, n);
+  E4B_REQUIRE(c, x && w && yh && n > 0 && FF > 0 && FF % 32 == 0, "q40gumm: bad args");
+  E4B_REQUIRE(c, (n + kTokC - 1) / kTokC <= kMaxChunks, "q40gumm: n=%d tokens exceed %d", n, kTokC * kMaxChunks);
+  return qmm(c, "q40gumm", x, w, nullptr, nullptr, nullptr, yh, IN, 2 * FF, FF, 1, 1, n, 1);
 }
 
 E4B_API int e4b_wacc(e4b_ctx* c, const float* y, const uint32_t* inv, const float* topk_w, float* out, int n_tok,

@@ -18,7 +18,7 @@ __global__ void k_rmsnorm(const float* __restrict__ x, const float* __restrict__
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
     float v = x[base + i] * inv;
     if (with_scale) v = v * w[i];
-    if (f16out) yh[base + i] = f2h(v);
+    if (f16out) yh[base + (f16out == 2 ? xfo_pos(i) : i)] = f2h(v);
     else y[base + i] = v;
     s2 += v;
   }
@@ -68,7 +68,7 @@ __global__ void k_rmsaccn(const float* __restrict__ t, const float* __restrict__
 __global__ void k_rmsacc3(const float* __restrict__ t, const float* __restrict__ w_acc, const float* __restrict__ w1,
                           const float* __restrict__ w2, const float* __restrict__ w3, const float* __restrict__ h_in,
                           uint16_t* __restrict__ y1, float* __restrict__ y2, uint16_t* __restrict__ y3,
-                          float* __restrict__ h_out, int dim, float eps) {
+                          float* __restrict__ h_out, int dim, float eps, int xfo) {
   pdl_wait();
   extern __shared__ float hs[];
   __shared__ float sh[32];
@@ -87,16 +87,17 @@ __global__ void k_rmsacc3(const float* __restrict__ t, const float* __restrict__
   __syncthreads();
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
     const float v = hs[i] * inv2;
-    y1[ob + i] = f2h(v * w1[i]);
+    const size_t oh = ob + (xfo ? xfo_pos(i) : i);
+    y1[oh] = f2h(v * w1[i]);
     y2[ob + i] = v * w2[i];
-    y3[ob + i] = f2h(v * w3[i]);
+    y3[oh] = f2h(v * w3[i]);
   }
 }
 
 __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict__ w1, const float* __restrict__ m,
                           const float* __restrict__ w2, const float* __restrict__ wp, const float* __restrict__ h_in,
                           const float* __restrict__ w_next, uint16_t* __restrict__ y_next, float* __restrict__ h_out,
-                          int H, float eps, float mul, int next) {
+                          int H, float eps, float mul, int next, int xfo) {
   pdl_wait();
   extern __shared__ float comb[];
   __shared__ float sh[32];
@@ -127,7 +128,7 @@ __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict_
   if (next) {
     const float inv4 = rms_scale(block_sum(s4, sh), H, eps);
     __syncthreads();
-    for (int i = threadIdx.x; i < H; i += blockDim.x) y_next[ob + i] = f2h(comb[i] * inv4 * w_next[i]);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) y_next[ob + (xfo ? xfo_pos(i) : i)] = f2h(comb[i] * inv4 * w_next[i]);
   }
 }
 
@@ -176,6 +177,7 @@ E4B_API int e4b_rmsnorm(e4b_ctx* c, const float* x, const float* w, float* y, fl
   E4B_REQUIRE(c, f16out ? yh != nullptr : y != nullptr, "rmsnorm: missing output");
   E4B_REQUIRE(c, !with_scale || w, "rmsnorm: missing weight");
   E4B_REQUIRE(c, !sumout || sums, "rmsnorm: missing sums");
+  E4B_REQUIRE(c, f16out >= 0 && f16out <= 2 && (f16out != 2 || dim % 32 == 0), "rmsnorm: bad f16out=%d", f16out);
   return e4b_launch(c, "rmsnorm", k_rmsnorm, dim3(rows), dim3(256), 0, x, w, y, sums, yh, dim, eps, with_scale,
                     sumout, f16out);
 }
@@ -197,27 +199,29 @@ E4B_API int e4b_rmsaccn(e4b_ctx* c, const float* t, const float* w1, float* hidd
 
 E4B_API int e4b_rmsacc3(e4b_ctx* c, const float* t, const float* w_acc, const float* w1, const float* w2,
                         const float* w3, const float* h_in, uint16_t* y1, float* y2, uint16_t* y3, float* h_out,
-                        int dim, float eps, int rows) {
+                        int dim, float eps, int rows, int xfo) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, t && w_acc && w1 && w2 && w3 && h_in && y1 && y2 && y3 && h_out && dim > 0, "rmsacc3: bad args");
+  E4B_REQUIRE(c, !xfo || dim % 32 == 0, "rmsacc3: fragment order needs dim %% 32 == 0");
   if (rows < 1) rows = 1;
   const size_t sm = (size_t)dim * 4;
   if (int r = set_smem(c, (const void*)k_rmsacc3, sm)) return r;
   return e4b_launch(c, "rmsacc3", k_rmsacc3, dim3(rows), dim3(256), sm, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
-                    h_out, dim, eps);
+                    h_out, dim, eps, xfo);
 }
 
 E4B_API int e4b_a4btail(e4b_ctx* c, const float* t1, const float* w1, const float* m, const float* w2,
                         const float* wp, const float* h_in, const float* w_next, uint16_t* y_next, float* h_out, int H,
-                        float eps, float mul, int next, int rows) {
+                        float eps, float mul, int next, int rows, int xfo) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, t1 && w1 && m && w2 && wp && h_in && h_out && H > 0, "a4btail: bad args");
   E4B_REQUIRE(c, !next || (w_next && y_next), "a4btail: next=1 needs w_next and y_next");
+  E4B_REQUIRE(c, !xfo || H % 32 == 0, "a4btail: fragment order needs H %% 32 == 0");
   if (rows < 1) rows = 1;
   const size_t sm = (size_t)H * 4;
   if (int r = set_smem(c, (const void*)k_a4btail, sm)) return r;
   return e4b_launch(c, "a4btail", k_a4btail, dim3(rows), dim3(256), sm, t1, w1, m, w2, wp, h_in, w_next, y_next,
-                    h_out, H, eps, mul, next);
+                    h_out, H, eps, mul, next, xfo);
 }
 
 E4B_API int e4b_geglumul(e4b_ctx* c, const float* a, const float* b, float* y, int N) {

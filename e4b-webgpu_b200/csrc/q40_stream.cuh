@@ -1,6 +1,9 @@
 // Internal interface of the streaming q4_0 GEMV (q40_stream.cu).
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace e4b {
@@ -17,6 +20,9 @@ bool q40_stream_supported(const void* w, const void* x, int IN, int rows);
 // 2: yh = f16(gelu(W x) * ple[off + o]).
 int q40_stream(e4b_ctx* c, const uint8_t* w, const void* x, int x_f32, float* y, uint16_t* yh, const float* ple,
                int IN, int OUT, int epi, int ff, int off);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (null if absent).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // Streaming q6_K LM head (q6k_stream.cu): batch 1, hidden a multiple of 2048.
 bool lmhead_stream_supported(const uint8_t* w, const float* x, int N);

@@ -241,6 +241,169 @@ __global__ void __launch_bounds__(256) k_q6k_mm(const uint8_t* __restrict__ w, c
   }
 }
 
+// ---- batched LM head, persistent and staged.  A unit is (block of 128 rows,
+// pass of up to 64 tokens); per q6_K superblock (256 k) a producer warp copies
+// the pass's activations (pre-split into f16 hi / lo and laid out as the MMA
+// B fragments: k_q6x_prep) with one bulk copy, and each row's 210-byte
+// superblock as its 16-byte-aligned 224-byte cover, into a 2-deep ring; four
+// MMA warps take 32 rows each (two 16-row subtiles share every B fragment).
+constexpr int kLmRows = 128;
+constexpr int kLmSlot = 224;
+constexpr int kLmXSlab = 8 * 16 * 32 * 16;        // 8 token groups x 16 k-steps x 32 lanes x 16 B
+constexpr int kLmWSlab = kLmRows * kLmSlot;
+
+// xp[s][q][j][lane] = {hi(x[k], x[k+1]), hi(x[k+8], x[k+9]), lo(..), lo(..)} for
+// token 8q + lane/4 and k = 256 s + 16 j + 2 (lane % 4); zero beyond n.
+__global__ void k_q6x_prep(const float* __restrict__ x, uint4* __restrict__ xp, int n, int N, int NG) {
+  pdl_wait();
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t total = (size_t)(N / 256) * NG * 16 * 32;
+  if (idx >= total) return;
+  const int lane = (int)(idx & 31), j = (int)((idx >> 5) & 15);
+  const size_t sq = idx >> 9;
+  const int q = (int)(sq % NG), sb = (int)(sq / NG);
+  const int tok = 8 * q + (lane >> 2), k = 256 * sb + 16 * j + 2 * (lane & 3);
+  uint16_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+  if (tok < n) {
+    const float* xr = x + (size_t)tok * N + k;
+    const float v[4] = {xr[0], xr[1], xr[8], xr[9]};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const __half hh = __float2half_rn(v[i]);
+      h[i] = __half_as_ushort(hh);
+      l[i] = f2h(v[i] - __half2float(hh));
+    }
+  }
+  xp[idx] = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+}
+
+__global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, const uint4* __restrict__ xp,
+                                                  float* __restrict__ y, int N, int OUT, int n, int NG, float softcap,
+                                                  uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[2], empty[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nsb = N >> 8, rowbytes = nsb * 210;
+  const int RB = (OUT + kLmRows - 1) / kLmRows, passes = (NG + 7) / 8, units = RB * passes;
+  uint8_t* xbuf = smem;
+  uint8_t* wbuf = smem + 2 * kLmXSlab;
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&full[b], 1);
+      mbar_init(&empty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+  if (warp == 4) {
+    // producer
+    int seq = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const int rb = u / passes, pass = u % passes, ng = min(8, NG - 8 * pass);
+      const int rows = min(kLmRows, OUT - kLmRows * rb);
+      for (int sb = 0; sb < nsb && ok; sb++, seq++) {
+        const int b = seq & 1;
+        if (seq >= 2) ok = mbar_wait(&empty[b], (uint32_t)(((seq >> 1) - 1) & 1), status);
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_expect_tx(&full[b], (uint32_t)(ng * (kLmXSlab / 8) + rows * kLmSlot));
+          bulk_g2s(xbuf + b * kLmXSlab, xp + ((size_t)sb * NG + 8 * pass) * 16 * 32, (uint32_t)(ng * (kLmXSlab / 8)),
+                   &full[b]);
+        }
+        __syncwarp();
+        for (int r = lane; r < rows; r += 32) {
+          const size_t start = (size_t)(kLmRows * rb + r) * rowbytes + 210 * sb;
+          bulk_g2s(wbuf + b * kLmWSlab + r * kLmSlot, w + (start & ~(size_t)15), kLmSlot, &full[b]);
+        }
+      }
+    }
+    return;
+  }
+  // MMA warps: rows 32 warp + {g, g+8} (subtile 0) and + 16 (subtile 1)
+  const int g = lane >> 2, t = lane & 3;
+  int seq = 0;
+  bool ok = true;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int rb = u / passes, pass = u % passes, ng = min(8, NG - 8 * pass);
+    float acc[8][2][4];
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+#pragma unroll
+      for (int s = 0; s < 2; s++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) acc[q][s][r] = 0.f;
+    int rr[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) rr[i] = 32 * warp + g + 8 * i;   // rows g, g+8, g+16, g+24 of the block
+    for (int sb = 0; sb < nsb; sb++, seq++) {
+      const int b = seq & 1;
+      if (ok) ok = mbar_wait(&full[b], (uint32_t)((seq >> 1) & 1), status);
+      if (ok) {
+        const uint8_t* blk[4];
+        float d[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const size_t start = (size_t)(kLmRows * rb + rr[i]) * rowbytes + 210 * sb;
+          blk[i] = wbuf + b * kLmWSlab + rr[i] * kLmSlot + (int)(start & 15);
+          d[i] = h2f(*reinterpret_cast<const uint16_t*>(blk[i] + 208));
+        }
+        const uint4* xs = reinterpret_cast<const uint4*>(xbuf + b * kLmXSlab);
+#pragma unroll 2
+        for (int j = 0; j < 16; j++) {
+          const int e0 = 16 * j + 2 * t;
+          uint32_t A[2][4];
+          float sc[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) sc[i] = d[i] * (float)(int8_t)blk[i][192 + j];
+#pragma unroll
+          for (int s = 0; s < 2; s++) {
+            A[s][0] = q6_pair(blk[2 * s], e0);
+            A[s][1] = q6_pair(blk[2 * s + 1], e0);
+            A[s][2] = q6_pair(blk[2 * s], e0 + 8);
+            A[s][3] = q6_pair(blk[2 * s + 1], e0 + 8);
+          }
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            if (q >= ng) break;
+            const uint4 xv = xs[(q * 16 + j) * 32 + lane];
+#pragma unroll
+            for (int s = 0; s < 2; s++) {
+              float c[4] = {0.f, 0.f, 0.f, 0.f};
+              mma16816(c, A[s][0], A[s][1], A[s][2], A[s][3], xv.x, xv.y);
+              mma16816(c, A[s][0], A[s][1], A[s][2], A[s][3], xv.z, xv.w);
+              acc[q][s][0] = fmaf(sc[2 * s], c[0], acc[q][s][0]);
+              acc[q][s][1] = fmaf(sc[2 * s], c[1], acc[q][s][1]);
+              acc[q][s][2] = fmaf(sc[2 * s + 1], c[2], acc[q][s][2]);
+              acc[q][s][3] = fmaf(sc[2 * s + 1], c[3], acc[q][s][3]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[b]);
+    }
+    if (!ok) continue;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      if (q >= ng) break;
+#pragma unroll
+      for (int s = 0; s < 2; s++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const int row = kLmRows * rb + rr[2 * s + (r >> 1)];
+          const int tok = 64 * pass + 8 * q + 2 * t + (r & 1);
+          if (row < OUT && tok < n) {
+            const float v = acc[q][s][r];
+            y[(size_t)tok * OUT + row] = softcap != 0.f ? softcap * tanhf(v / softcap) : v;
+          }
+        }
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -249,6 +412,22 @@ E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* c, const uint8_t* w, const float* x, ui
                                 int OUT, float softcap, int n) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, w && x && scratch && y && N > 0 && N % 256 == 0 && OUT > 0 && n > 0, "q6k_lmhead_rows: bad args");
+  if (OUT % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(scratch) % 16 == 0) {
+    // staged path: every superblock's aligned cover lies inside [w, w + OUT * rowbytes)
+    const int NG = (n + 7) / 8;
+    const size_t tot = (size_t)(N / 256) * NG * 16 * 32;
+    uint4* xp = reinterpret_cast<uint4*>(scratch);
+    if (int r = e4b_launch(c, "q6x_prep", k_q6x_prep, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, x, xp, n, N,
+                           NG))
+      return r;
+    const size_t smem = 2 * (size_t)kLmXSlab + 2 * (size_t)kLmWSlab;
+    cudaError_t e = cudaFuncSetAttribute(k_q6mm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q6mm smem attr: %s", cudaGetErrorString(e));
+    const int units = (OUT + kLmRows - 1) / kLmRows * ((NG + 7) / 8);
+    const int grid = units < c->sm_count ? units : c->sm_count;
+    return e4b_launch(c, "q6mm", k_q6mm, dim3((unsigned)grid), dim3(160), smem, w, (const uint4*)xp, y, N, OUT, n, NG,
+                      softcap, c->status);
+  }
   uint16_t* xh = scratch;
   uint16_t* xl = scratch + (size_t)n * N;
   const size_t tot = (size_t)n * N;

@@ -3,6 +3,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "q40_stream.cuh"
 
 namespace {
 
@@ -66,6 +67,63 @@ __global__ void __launch_bounds__(256) k_routertop(const float* __restrict__ x, 
   }
   __syncthreads();
   if (warp == 0) softmax_topk(p, E, K, pes, topk_idx + (size_t)b * K, topk_w + (size_t)b * K);
+}
+
+// Batched routing (many tokens): the scores are a small f32 GEMM
+// S[b][e] = x[b] . wr[e], split over kRtK-wide slices of H so that enough CTAs
+// run: CTA (token tile, expert tile, slice) stages its x and wr slices in
+// shared memory and writes part[slice][b][e]; then one warp per token sums the
+// slices in order and runs the softmax / top-K above.
+constexpr int kRtTok = 16, kRtExp = 32, kRtK = 128;
+
+__global__ void __launch_bounds__(256) k_router_part(const float* __restrict__ x, const float* __restrict__ wr,
+                                                     float* __restrict__ part, int B, int H, int E) {
+  pdl_wait();
+  __shared__ float xs[kRtTok][kRtK];
+  __shared__ float wsm[kRtExp][kRtK + 1];
+  const int b0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, k0 = blockIdx.z * kRtK;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < kRtTok * kRtK; i += 256) {
+    const int r = i / kRtK, k = i % kRtK;
+    xs[r][k] = (b0 + r < B && k0 + k < H) ? x[(size_t)(b0 + r) * H + k0 + k] : 0.f;
+  }
+  for (int i = tid; i < kRtExp * kRtK; i += 256) {
+    const int r = i / kRtK, k = i % kRtK;
+    wsm[r][k] = (e0 + r < E && k0 + k < H) ? wr[(size_t)(e0 + r) * H + k0 + k] : 0.f;
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll 8
+  for (int k = 0; k < kRtK; k++) {
+    const float w = wsm[lane][k];
+    a0 = fmaf(xs[2 * warp][k], w, a0);
+    a1 = fmaf(xs[2 * warp + 1][k], w, a1);
+  }
+  const int e = e0 + lane;
+  if (e < E) {
+    float* pp = part + (size_t)blockIdx.z * B * E;
+    if (b0 + 2 * warp < B) pp[(size_t)(b0 + 2 * warp) * E + e] = a0;
+    if (b0 + 2 * warp + 1 < B) pp[(size_t)(b0 + 2 * warp + 1) * E + e] = a1;
+  }
+}
+
+__global__ void __launch_bounds__(256) k_router_topk(const float* __restrict__ part, const float* __restrict__ pes,
+                                                     uint32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                                                     int B, int E, int K, int slices) {
+  pdl_wait();
+  extern __shared__ float pw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 8 + warp;
+  if (b >= B) return;
+  float* p = pw + (size_t)warp * E;
+  for (int e = lane; e < E; e += 32) {
+    float v = 0.f;
+    for (int s = 0; s < slices; s++) v += part[((size_t)s * B + b) * E + e];
+    p[e] = v;
+  }
+  __syncwarp();
+  softmax_topk(p, E, K, pes, topk_idx + (size_t)b * K, topk_w + (size_t)b * K);
 }
 
 // kernels/router.wgsl: scale-less RMS of h, x H^-0.5 x scale, then scores + top-K.
@@ -195,6 +253,18 @@ E4B_API int e4b_routertop(e4b_ctx* c, const float* x, const float* wr, const flo
   E4B_REQUIRE(c, H > 0 && E > 0 && E <= 4096 && K > 0 && K <= 32 && K <= E, "routertop: bad sizes H=%d E=%d K=%d", H,
               E, K);
   if (batch < 1) batch = 1;
+  const int slices = (H + kRtK - 1) / kRtK;
+  const size_t part_bytes = (size_t)slices * batch * E * 4;
+  if (batch > 1 && c->ws && c->ws_bytes >= e4b::kWsCounterBytes + part_bytes && (size_t)8 * E * 4 <= 48 * 1024) {
+    // the split-K partial area of the workspace (free between launches)
+    float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c->ws) + e4b::kWsCounterBytes);
+    if (int r = e4b_launch(c, "router_part", k_router_part,
+                           dim3((batch + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, slices), dim3(256), 0, x,
+                           wr, part, batch, H, E))
+      return r;
+    return e4b_launch(c, "router_topk", k_router_topk, dim3((batch + 7) / 8), dim3(256), (size_t)8 * E * 4,
+                      (const float*)part, pes, topk_idx, topk_w, batch, E, K, slices);
+  }
   return e4b_launch(c, "routertop", k_routertop, dim3(batch), dim3(256), (size_t)E * 4, x, wr, pes, topk_idx, topk_w,
                     H, E, K);
 }

@@ -72,7 +72,10 @@ class Device:
         if rc != 0:
             raise E4BError(name, rc, self.last_error())
         if name not in _RUNTIME:
-            self.kernel_launches += self.KERNELS.get(name, 1)
+            n = self.KERNELS.get(name, 1)
+            if name == "e4b_routertop" and args[-1] > 1:
+                n = 2          # split-K scores + per-token top-K
+            self.kernel_launches += n
         return rc
 
     def last_error(self) -> str:

@@ -112,8 +112,16 @@ E4B_API int e4b_q6k_lmhead(e4b_ctx* ctx, const uint8_t* w, const float* x, float
                            float softcap, int batch);
 
 /* ------------------------------------------------------------ norms / tails */
-/* kernels/rmsnorm.wgsl:13-51.  rows x dim; y (f32) or yh (f16) per f16out;
- * sums[row] = sum(y) if sumout. */
+/* Fragment order ("xfo"): the f16 activation rows that feed the multi-token
+ * q4_0 GEMMs below are stored permuted inside each 32-element block so one
+ * 16-byte load gives an MMA lane its 8 values: element j of a block sits at
+ * half 8t + slot with, for odd blocks, t = (j%16)/4; for even blocks
+ * t = ((j%16)-2)/4 for j%16 in [2,14) and t = 3 for j%16 in {0,1,14,15};
+ * slots [j0, j2, j1, j3] of t's four indices, +4 for j >= 16.  The python host
+ * gives the permutation as batch.xfo_perm(n). */
+
+/* kernels/rmsnorm.wgsl:13-51.  rows x dim; y (f32) or yh (f16) per f16out
+ * (2: f16 in fragment order); sums[row] = sum(y) if sumout. */
 E4B_API int e4b_rmsnorm(e4b_ctx* ctx, const float* x, const float* w, float* y, float* sums, uint16_t* yh,
                         int dim, int rows, float eps, int with_scale, int sumout, int f16out);
 /* kernels/rmsacc.wgsl:10-26: hidden = (hidden + rms(x)*w) * mul. */
@@ -124,14 +132,15 @@ E4B_API int e4b_rmsacc(e4b_ctx* ctx, const float* x, const float* w, float* hidd
  * f16(hidden) (norm2=0). */
 E4B_API int e4b_rmsaccn(e4b_ctx* ctx, const float* t, const float* w1, float* hidden, const float* w2,
                         uint16_t* yh, int dim, float eps, float mul, int norm2);
-/* kernels/rmsacc3.wgsl:27-53 (rows = batch). */
+/* kernels/rmsacc3.wgsl:27-53 (rows = batch); xfo=1: y1, y3 in fragment order. */
 E4B_API int e4b_rmsacc3(e4b_ctx* ctx, const float* t, const float* w_acc, const float* w1, const float* w2,
                         const float* w3, const float* h_in, uint16_t* y1, float* y2, uint16_t* y3,
-                        float* h_out, int dim, float eps, int rows);
-/* kernels/a4btail.wgsl:26-71 (rows = batch). */
+                        float* h_out, int dim, float eps, int rows, int xfo);
+/* kernels/a4btail.wgsl:26-71 (rows = batch); xfo=1: y_next in fragment order. */
 E4B_API int e4b_a4btail(e4b_ctx* ctx, const float* t1, const float* w1, const float* m, const float* w2,
                         const float* wp, const float* h_in, const float* w_next, uint16_t* y_next,
-                        float* h_out, int H, float eps, float mul, int next, int rows);
+                        float* h_out, int H, float eps, float mul, int next, int rows,
+                        int xfo);
 
 /* ------------------------------------------------------------ q4_0 GEMVs */
 /* kernels/q40mv.wgsl:56-89: y[z*OUT+o] = sum_b d_b sum_i (n_i-8) x_i.
@@ -157,19 +166,23 @@ E4B_API int e4b_q40moedown(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, co
  * expgroup: sort the n_tok*K entries of topk[n_tok][K] by expert (stable):
  *   offsets[E+1], entries[pos] = e, inv[e] = pos.
  * q40gugrp: per entry at sorted position pos, yh[pos][FF] = f16(gelu(gate)*up)
- *   with expert rows [gate FF | up FF] of w[E][2FF][IN] and x = x[token][IN] (f16).
- * q40downgrp: y[pos][OUT] = W_e x[pos] (x rows by position, f16; w[E][OUT][IN]).
+ *   with expert rows [gate FF | up FF] of w[E][2FF][IN] and x = x[token][IN];
+ *   IN % 256 == 0, FF % 32 == 0.
+ * q40downgrp: y[pos][OUT] = W_e x[pos] (x rows by position; w[E][OUT][IN]);
+ *   OUT % 16 == 0 when IN % 256 != 0.
  * wacc: out[t][o] = sum_k topk_w[t][k] * y[inv[t*K+k]][o], slots in order.
- * IN/32 must be even for the grouped GEMMs. */
+ * Every f16 x and yh of the multi-token GEMMs is in fragment order; IN % 64 == 0;
+ * weights and x 16-byte aligned.  An expert's tokens are processed 16 at a time. */
 E4B_API int e4b_expgroup(e4b_ctx* ctx, const uint32_t* topk, int n_tok, int K, int E, uint32_t* offsets,
                          uint32_t* entries, uint32_t* inv);
 E4B_API int e4b_q40gugrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
                          const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K);
 E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
                            const uint32_t* entries, float* y, int IN, int OUT, int E);
-/* Dense batched GEMMs on the same tensor-core path (n token rows, f16 x):
+/* Dense batched GEMMs on the same tensor-core path (n token rows, f16 x in
+ * fragment order):
  * q40mm: y[n][OUT] = W x[n] (f32); q40gumm: yh[n][FF] = f16(gelu(gate)*up) with
- * rows [gate FF | up FF] (kernels/q40gu.wgsl dense part, per token). */
+ * rows [gate FF | up FF] (kernels/q40gu.wgsl dense part, per token; yh in fragment order). */
 E4B_API int e4b_q40mm(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, float* y, int IN, int OUT, int n);
 E4B_API int e4b_q40gumm(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, uint16_t* yh, int IN, int FF, int n);
 E4B_API int e4b_wacc(e4b_ctx* ctx, const float* y, const uint32_t* inv, const float* topk_w, float* out, int n_tok,
@@ -180,7 +193,9 @@ E4B_API int e4b_moecomb(e4b_ctx* ctx, const float* slots, const float* topk_w, f
 /* ------------------------------------------------------------ router */
 /* kernels/routertop.wgsl:19-71: scores = Wr[E][H] . x (f32), softmax, K-way
  * iterative argmax (ties -> lowest index), renormalise, x pes[e].  One token
- * per row of x (batch rows). */
+ * per row of x (batch rows).  batch > 1 with a workspace attached: the scores
+ * are a split-K f32 GEMM into the workspace, then a per-token top-K pass (two
+ * launches). */
 E4B_API int e4b_routertop(e4b_ctx* ctx, const float* x, const float* wr, const float* pes, uint32_t* topk_idx,
                           float* topk_w, int H, int E, int K, int batch);
 /* kernels/router.wgsl:16-63: scale-less RMS of h, x scale x H^-0.5, then as routertop. */
@@ -232,7 +247,8 @@ E4B_API int e4b_geglub(e4b_ctx* ctx, const float* gu, uint16_t* yh, int N, int r
  * pleIn[b*PD+i] = (rms(proj_b*proj_scale)[i]*normW[i] + row_b[i]*mult) * sqrt(1/2),
  * row = q6_K row tok[0] (toksrc=1) or params[2] of the [LAYERS*PD]-wide table. */
 /* LM head for n token rows (batched decode): y[n][OUT] = softcap(W x[n][N]) on the
- * tensor cores; scratch: 2*n*N u16 (x split into f16 hi + lo). */
+ * tensor cores, x used as f16 hi + lo; scratch: 2*N*ceil8(n) u16, 16-byte aligned
+ * (the split activations, laid out as MMA fragments). */
 E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* ctx, const uint8_t* w, const float* x, uint16_t* scratch, float* y, int N,
                                 int OUT, float softcap, int n);
 E4B_API int e4b_pleprep(e4b_ctx* ctx, const uint8_t* table, const uint32_t* params, const uint32_t* tok,
@@ -247,7 +263,8 @@ E4B_API int e4b_plemul(e4b_ctx* ctx, const float* a, const float* ple, float* y,
 
 /* ---- batched decode of nseq sequences at one common position (params[0],
  * kvCount params[4]); sequence b's KV cache starts at cache + b * slots*KVH*HD,
- * its q / qkv / partial / output rows are row b of the per-sequence layouts. */
+ * its q / qkv / partial / output rows are row b of the per-sequence layouts.
+ * attcomb_seq xfo=1: out_h rows (QH*HD) in fragment order. */
 E4B_API int e4b_headprep_seq(e4b_ctx* ctx, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
                              uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
                              int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
@@ -257,7 +274,7 @@ E4B_API int e4b_attsplit_seq(e4b_ctx* ctx, const float* q, const uint16_t* kcach
                              int window, int cachemode, int ring, int chunk, int max_chunks, float scale,
                              int cache_slots, int nseq);
 E4B_API int e4b_attcomb_seq(e4b_ctx* ctx, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
-                            float* lse, int QH, int HD, int max_chunks, int nseq);
+                            float* lse, int QH, int HD, int max_chunks, int nseq, int xfo);
 
 /* ------------------------------------------------------------ argmax / feed */
 /* kernels/argmax2.wgsl:8-48 (both stages): out[0] = index of the largest x (ties

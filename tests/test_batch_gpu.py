@@ -35,14 +35,15 @@ def test_batched_moe_decode_matches_oracle(e4b, models, B):
             assert np.linalg.norm(h[b] - href) / np.linalg.norm(href) < 1e-2
 
 
-def test_batched_lmhead_rows(e4b, dev):
-    """e4b_q6k_lmhead_rows (tensor cores, x as f16 hi + lo) against the oracle q6_K matvec per row."""
+@pytest.mark.parametrize("V,N,n", [(3000, 512, 11), (1000, 768, 64), (520, 256, 70), (4, 256, 1)])
+def test_batched_lmhead_rows(e4b, dev, V, N, n):
+    """e4b_q6k_lmhead_rows (tensor cores, x as f16 hi + lo) against the oracle q6_K matvec per row;
+    V % 8 == 0 takes the staged kernel, other V the direct one."""
     from oracle import ops as O
-    V, N, n = 3000, 512, 11
-    w = e4b.synth.quant_q6_K(e4b.synth.normal_f32(V * N, 41, "lmrows", 0.02))
+    w = e4b.synth.quant_q6_K(e4b.synth.normal_f32(V * N, 41 + V, "lmrows", 0.02))
     x = np.random.default_rng(42).standard_normal((n, N)).astype(np.float32)
     y = dev.alloc(n * V * 4)
-    scr = dev.alloc(2 * n * N * 2)
+    scr = dev.alloc(2 * ((n + 7) // 8 * 8) * N * 2)
     dev.call("e4b_q6k_lmhead_rows", dev.upload(w).ptr, dev.upload(x).ptr, scr.ptr, y.ptr, N, V,
              np.float32(30.0), n)
     dev.sync()

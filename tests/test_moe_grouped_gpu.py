@@ -1,7 +1,9 @@
 """Grouped MoE for batched decode (expgroup -> q40gugrp -> q40downgrp -> wacc)
 against the per-token oracle: y_t = sum_k w_tk * W_down[e_tk] f16(gelu(gate) * up)
 with [gate | up] = W_gu[e_tk] x_t (kernels/q40gugrp.wgsl, q40downgrp.wgsl,
-wacc.wgsl semantics; src/engine-a4b.js:437-462 per token)."""
+wacc.wgsl semantics; src/engine-a4b.js:437-462 per token), plus the dense
+multi-token GEMMs (q40mm / q40gumm) and the fragment-order activation layout
+their producers write."""
 import numpy as np
 import pytest
 
@@ -37,7 +39,8 @@ def test_grouped_moe_matches_per_token_oracle(e4b, dev, n, hot):
     idx, w = _topk(rng, n, K, E, hot)
     # device
     d = dev
-    bx, bgu, bdn = d.upload(x.astype(np.float16)), d.upload(wgu), d.upload(wdn)
+    xfo = e4b.batch.to_xfo
+    bx, bgu, bdn = d.upload(xfo(x.astype(np.float16))), d.upload(wgu), d.upload(wdn)
     bidx, bw = d.upload(idx), d.upload(w)
     off, ent, inv = d.alloc((E + 1) * 4), d.alloc(n * K * 4), d.alloc(n * K * 4)
     g = d.alloc(n * K * EF * 2)
@@ -66,3 +69,90 @@ def test_grouped_moe_matches_per_token_oracle(e4b, dev, n, hot):
         ref = O.moe_down(slots, wdn, idx[t], w[t], EF, H)
         worst = max(worst, float(np.max(np.abs(got[t] - ref)) / np.max(np.abs(ref))))
     assert worst < 2e-3, worst     # f16 GeGLU intermediates may round one ulp apart
+
+
+@pytest.mark.parametrize("IN,OUT", [(512, 96), (256, 40), (192, 64), (704, 48)])
+@pytest.mark.parametrize("n", [1, 7, 16, 37, 64])
+def test_dense_q40mm(e4b, dev, IN, OUT, n):
+    """y[t] = W x[t] per token (kernels/q40mv.wgsl per row); IN % 256 == 0 takes the
+    TMA-box weight stream, other IN the whole-row bulk stream."""
+    rng = np.random.default_rng(IN + n)
+    w = q40(e4b, OUT, IN, 7 + IN)
+    x = O.f16r(rng.standard_normal((n, IN)).astype(F32))
+    y = dev.alloc(n * OUT * 4)
+    dev.call("e4b_q40mm", dev.upload(e4b.batch.to_xfo(x.astype(np.float16))).ptr, dev.upload(w).ptr, y.ptr, IN,
+             OUT, n)
+    dev.sync()
+    got = dev.read(y, F32, n * OUT).reshape(n, OUT)
+    assert dev.status() == 0
+    for t in range(n):
+        ref = O.q40mv(w, x[t], OUT, IN)
+        assert np.max(np.abs(got[t] - ref)) <= 1e-5 * np.max(np.abs(ref)), t
+
+
+@pytest.mark.parametrize("n", [1, 9, 64])
+def test_dense_q40gumm(e4b, dev, n):
+    IN, FF = 512, 96
+    rng = np.random.default_rng(n)
+    w = q40(e4b, 2 * FF, IN, 11)
+    x = O.f16r(rng.standard_normal((n, IN)).astype(F32))
+    yh = dev.alloc(n * FF * 2)
+    dev.call("e4b_q40gumm", dev.upload(e4b.batch.to_xfo(x.astype(np.float16))).ptr, dev.upload(w).ptr, yh.ptr, IN,
+             FF, n)
+    dev.sync()
+    got = e4b.batch.from_xfo(dev.read(yh, np.float16, n * FF).reshape(n, FF)).astype(F32)
+    for t in range(n):
+        ref = O.geglu_rows(O.q40mv(w, x[t], 2 * FF, IN), FF)
+        assert np.allclose(got[t], ref, rtol=2e-3, atol=1e-4), t
+
+
+def test_fragment_order_producers(e4b, dev):
+    """rmsnorm f16out=2 and rmsacc3 / a4btail / attcomb_seq with xfo=1 write the
+    same f16 values as the plain layout, permuted by xfo_perm."""
+    H, B = 256, 3
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((B, H)).astype(F32)
+    w = rng.uniform(0.5, 1.5, H).astype(F32)
+    bx, bw = dev.upload(x), dev.upload(w)
+    plain, perm = dev.alloc(B * H * 2), dev.alloc(B * H * 2)
+    for f16out, buf in ((1, plain), (2, perm)):
+        dev.call("e4b_rmsnorm", bx.ptr, bw.ptr, None, None, buf.ptr, H, B, np.float32(1e-6), 1, 0, f16out)
+    dev.sync()
+    a = dev.read(plain, np.uint16, B * H).reshape(B, H)
+    b = dev.read(perm, np.uint16, B * H).reshape(B, H)
+    assert np.array_equal(e4b.batch.to_xfo(a), b)
+    # rmsacc3: y1, y3 permuted, y2 / h_out untouched
+    t = rng.standard_normal((B, H)).astype(F32)
+    ws = [dev.upload(rng.uniform(0.5, 1.5, H).astype(F32)) for _ in range(4)]
+    outs = {}
+    for xfo in (0, 1):
+        bufs = [dev.alloc(B * H * 2), dev.alloc(B * H * 4), dev.alloc(B * H * 2), dev.alloc(B * H * 4)]
+        dev.call("e4b_rmsacc3", dev.upload(t).ptr, *[q.ptr for q in ws], bx.ptr, *[q.ptr for q in bufs], H,
+                 np.float32(1e-6), B, xfo)
+        dev.sync()
+        outs[xfo] = [dev.read(bufs[0], np.uint16, B * H).reshape(B, H), dev.read(bufs[1], F32, B * H),
+                     dev.read(bufs[2], np.uint16, B * H).reshape(B, H), dev.read(bufs[3], F32, B * H)]
+    assert np.array_equal(e4b.batch.to_xfo(outs[0][0]), outs[1][0])
+    assert np.array_equal(e4b.batch.to_xfo(outs[0][2]), outs[1][2])
+    assert np.array_equal(outs[0][1], outs[1][1]) and np.array_equal(outs[0][3], outs[1][3])
+    # a4btail
+    m = rng.standard_normal((B, H)).astype(F32)
+    tails = {}
+    for xfo in (0, 1):
+        yn, ho = dev.alloc(B * H * 2), dev.alloc(B * H * 4)
+        dev.call("e4b_a4btail", dev.upload(t).ptr, ws[0].ptr, dev.upload(m).ptr, ws[1].ptr, ws[2].ptr, bx.ptr,
+                 ws[3].ptr, yn.ptr, ho.ptr, H, np.float32(1e-6), np.float32(0.5), 1, B, xfo)
+        dev.sync()
+        tails[xfo] = dev.read(yn, np.uint16, B * H).reshape(B, H)
+    assert np.array_equal(e4b.batch.to_xfo(tails[0]), tails[1])
+    # attcomb_seq: QH heads x HD per sequence row
+    QH, HD, MC = 2, 128, 3
+    po = rng.standard_normal((B, QH, MC, HD)).astype(F32)
+    ml = np.stack([rng.standard_normal((B, QH, MC)), rng.uniform(0.5, 2.0, (B, QH, MC))], -1).astype(F32)
+    combs = {}
+    for xfo in (0, 1):
+        oh = dev.alloc(B * QH * HD * 2)
+        dev.call("e4b_attcomb_seq", dev.upload(po).ptr, dev.upload(ml).ptr, oh.ptr, None, None, QH, HD, MC, B, xfo)
+        dev.sync()
+        combs[xfo] = dev.read(oh, np.uint16, B * QH * HD).reshape(B, QH * HD)
+    assert np.array_equal(e4b.batch.to_xfo(combs[0]), combs[1])

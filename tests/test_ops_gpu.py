@@ -282,8 +282,9 @@ def test_geglu_elementwise(e4b, dev):
 
 
 # ------------------------------------------------------------------ router / argmax
-def test_routertop_batched(e4b, dev):
-    H, E, K, B = 2816, 128, 8, 4
+@pytest.mark.parametrize("H,E,K,B", [(2816, 128, 8, 4), (2816, 128, 8, 64), (512, 16, 4, 37), (200, 40, 3, 2)])
+def test_routertop_batched(e4b, dev, H, E, K, B):
+    """batch > 1 with the fixture's workspace: split-K score GEMM + per-token top-K."""
     x = rng(32).standard_normal((B, H)).astype(F32) * 0.05
     wr = (rng(33).standard_normal((E, H)) * 0.02).astype(F32)
     pes = rng(34).uniform(0.5, 1.5, E).astype(F32)
