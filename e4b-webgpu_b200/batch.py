@@ -8,7 +8,7 @@ src/engine-a4b.js:467-585 does for prefill):
 
   q|k|v        e4b_q40mm          (tensor-core GEMM, tokens as columns)
   head prep    e4b_headprep_seq   (per-sequence cache)
-  attention    e4b_attsplit_seq + e4b_attcomb_seq
+  attention    e4b_attdec_seq     (split-KV on the tensor cores + combine)
   o            e4b_q40mm
   norms        e4b_rmsacc3        (rows = B)
   router       e4b_routertop      (batch = B)
@@ -75,6 +75,8 @@ class BatchEngine(Engine):
         super().__init__(src, device, chunk=chunk, record=False, fused=False)
         if not self.cfg.moe:
             raise ValueError("BatchEngine drives the MoE (A4B) graph")
+        if self.chunk > 64:
+            raise ValueError("BatchEngine's attention partials are sized for 64-slot chunks (chunk <= 64)")
         H, IN = self.cfg.hidden, self.cfg.hidden
         for n, what in ((H, "hidden"), (self.cfg.q_dim, "q_dim"), (self.cfg.ff, "ff"), (self.cfg.expert_ff, "expert ff")):
             if n % 64:
@@ -136,11 +138,9 @@ class BatchEngine(Engine):
             d.call("e4b_headprep_seq", A.qkv, L.q_norm, L.k_norm, A.params, L.kc, L.vc, A.q, c.q_heads, c.kv_heads,
                    c.head_dim, L.angles, ctypes.c_float(L.theta), ctypes.c_float(c.eps), int(L.keqv), L.cachemode,
                    L.ring, L.slots, B)
-            d.call("e4b_attsplit_seq", A.q, L.kc, L.vc, A.params, A.part_o, A.part_ml, c.q_heads, c.kv_heads,
-                   c.head_dim, c.window if L.sliding else 0, L.cachemode, L.ring, self.chunk, L.max_chunks,
-                   ctypes.c_float(1.0), L.slots, B)
-            d.call("e4b_attcomb_seq", A.part_o, A.part_ml, A.attn, None, None, c.q_heads, c.head_dim, L.max_chunks, B,
-                   1)
+            d.call("e4b_attdec_seq", A.q, L.kc, L.vc, A.params, A.part_o, A.part_ml, A.attn, c.q_heads, c.kv_heads,
+                   c.head_dim, c.window if L.sliding else 0, L.cachemode, L.ring, L.max_chunks, ctypes.c_float(1.0),
+                   L.slots, B, 1)
             d.call("e4b_q40mm", A.attn, L.o, A.tmp, c.q_dim, H, B)
             d.call("e4b_rmsacc3", A.tmp, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
                    A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B, 1)

@@ -1,9 +1,10 @@
 // Decode attention: head prep (q/k RMSNorm + RoPE, v norm, f16 KV write),
 // RoPE, KV write, and split-KV flash-decode (phase A partials + phase B LSE merge)
 // over the f16 KV cache with GQA, sliding ring and global (linear) layers.
-#include "common.cuh"
+#include "attn.cuh"
 
 namespace {
+using e4b::SlotRule;
 
 E4B_DEV float rope_theta(uint32_t pos, int p, int HD, float theta) {
   // pos * THETA^(-2p/HD), in f32 (kernels/headprep.wgsl:55)
@@ -106,23 +107,7 @@ __global__ void k_kvwrite(const float* __restrict__ src, const uint32_t* __restr
 
 // Number of addressable slots and whether slot t is attended, for the query at
 // position qp (kernels/attnf32.wgsl:28-53, attsplit.wgsl:21-23).
-struct SlotRule {
-  int cachemode, ring, window;
-  uint32_t qp, len;
-  E4B_DEV uint32_t nslots() const {
-    if (cachemode == 1) return min(qp + 1, (uint32_t)ring);
-    return len;
-  }
-  E4B_DEV bool valid(uint32_t t) const {
-    if (cachemode == 1) {
-      const uint32_t ps = qp - ((qp + (uint32_t)ring - t) % (uint32_t)ring);  // slot t's true position
-      return ps <= qp && ps + (uint32_t)window > qp;
-    }
-    if (t >= len) return false;
-    if (cachemode == 0 && window > 0 && len > (uint32_t)window) return t >= len - (uint32_t)window;
-    return true;
-  }
-};
+
 
 // Phase A: CTA (head h, chunk c) scores `chunk` slots (one per thread), then
 // accumulates p_t * v_t over its dims.  Output unnormalised with local (m, l).

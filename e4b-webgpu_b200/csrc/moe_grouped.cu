@@ -60,7 +60,7 @@ __global__ void k_expgroup(const uint32_t* __restrict__ topk, int n, int E, uint
 
 // ---- multi-token q4_0 GEMM (grouped experts or one dense matrix).
 //
-// Work: a chunk is up to kTokC tokens of one matrix (an expert's sorted
+// Work: a chunk is up to TOKC (8 or 16) tokens of one matrix (an expert's sorted
 // entries, or consecutive tokens of the dense batch); an item is a chunk x W
 // consecutive row tiles, one tile per warp.  Every CTA of a persistent grid owns
 // a contiguous range of items (chunk-major, so consecutive items share their
@@ -78,7 +78,6 @@ __global__ void k_expgroup(const uint32_t* __restrict__ topk, int n, int E, uint
 // Epilogues: EPI 0 y[pos][row] (f32); EPI 1 tiles pair 16 gate rows with the
 // matching 16 up rows and write yh[pos][o] = f16(gelu(gate) * up) in fragment
 // order, ready to be the next GEMM's activations.
-constexpr int kTokC = 16;        // tokens per chunk (two 8-column MMA groups)
 constexpr int kMaxChunks = 512;  // chunk list capacity (shared memory)
 
 struct Chunk {
@@ -110,6 +109,7 @@ E4B_DEV uint4 lds128(const uint16_t* p) {
 
 // Chunk list of this launch (warp 0; dense: arithmetic, grouped: a warp scan of
 // the experts' entry counts).  Returns the number of chunks.
+template <int kTokC>
 E4B_DEV int build_chunks(const QmmP& p, Chunk* ch, int lane) {
   if (!p.offsets) {
     const int n = (p.n_dense + kTokC - 1) / kTokC;
@@ -140,51 +140,41 @@ E4B_DEV int build_chunks(const QmmP& p, Chunk* ch, int lane) {
   return base;
 }
 
-// One staged quantum: NS 16-row subtiles (sub_bytes apart, row pitch `pitch`),
-// blocks [0, nblk) of the stage = global blocks kb0 + k (kb0 even).
-template <int NS>
-E4B_DEV void qmm_stage(const uint8_t* st, int pitch, int sub_bytes, int nblk, int kb0, const uint16_t* xr0,
-                       const uint16_t* xr1, bool two, const Lane& L, float (&acc)[2][2][4]) {
-  const uint8_t* r0 = st;
-  const uint8_t* r1 = st + 8 * pitch;
-  for (int k = 0; k < nblk; k += 2) {
+// One block (32 k) of NS 16-row subtiles: a/b point at rows g and g+8 of
+// subtile 0 (subtile 1 sub_bytes further), xq at this lane's fragment of the
+// block for token group 0 (group 1 xstep halves further).
+template <int NS, int TWO, int PAR>
+E4B_DEV void qmm_block(const uint8_t* a, const uint8_t* b, int sub_bytes, const uint16_t* xq, int xstep, bool two,
+                       const Lane& L, float (&acc)[2][2][4]) {
+  uint32_t A[NS][8];
+  float d[NS][2];
 #pragma unroll
-    for (int par = 0; par < 2; par++) {
-      const int kk = k + par;
-      uint32_t A[NS][8];
-      float d[NS][2];
+  for (int s = 0; s < NS; s++) {
+    const uint8_t* ra = a + s * sub_bytes;
+    const uint8_t* rb = b + s * sub_bytes;
+    dq_row(PAR ? nib_odd(ra, L) : nib_even(ra, L), A[s][0], A[s][1], A[s][2], A[s][3]);
+    dq_row(PAR ? nib_odd(rb, L) : nib_even(rb, L), A[s][4], A[s][5], A[s][6], A[s][7]);
+    d[s][0] = h2f(*reinterpret_cast<const uint16_t*>(ra));
+    d[s][1] = h2f(*reinterpret_cast<const uint16_t*>(rb));
+  }
 #pragma unroll
-      for (int s = 0; s < NS; s++) {
-        const uint8_t* a = r0 + s * sub_bytes + 18 * kk;
-        const uint8_t* b = r1 + s * sub_bytes + 18 * kk;
-        const uint32_t va = par ? nib_odd(a, L) : nib_even(a, L);
-        const uint32_t vb = par ? nib_odd(b, L) : nib_even(b, L);
-        dq_row(va, A[s][0], A[s][1], A[s][2], A[s][3]);
-        dq_row(vb, A[s][4], A[s][5], A[s][6], A[s][7]);
-        d[s][0] = h2f(*reinterpret_cast<const uint16_t*>(a));
-        d[s][1] = h2f(*reinterpret_cast<const uint16_t*>(b));
-      }
-      const int kb = kb0 + kk;
+  for (int q = 0; q < (TWO ? 2 : 1); q++) {
+    if (q == 1 && !two) break;
+    const uint4 xb = lds128(xq + q * xstep);
 #pragma unroll
-      for (int q = 0; q < 2; q++) {
-        if (q == 1 && !two) break;
-        const uint4 xb = lds128((q ? xr1 : xr0) + 32 * kb);
-#pragma unroll
-        for (int s = 0; s < NS; s++) {
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
-          mma16816(c, A[s][0], A[s][4], A[s][1], A[s][5], xb.x, xb.y);
-          mma16816(c, A[s][2], A[s][6], A[s][3], A[s][7], xb.z, xb.w);
-          acc[q][s][0] = fmaf(d[s][0], c[0], acc[q][s][0]);
-          acc[q][s][1] = fmaf(d[s][0], c[1], acc[q][s][1]);
-          acc[q][s][2] = fmaf(d[s][1], c[2], acc[q][s][2]);
-          acc[q][s][3] = fmaf(d[s][1], c[3], acc[q][s][3]);
-        }
-      }
+    for (int s = 0; s < NS; s++) {
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      mma16816(c, A[s][0], A[s][4], A[s][1], A[s][5], xb.x, xb.y);
+      mma16816(c, A[s][2], A[s][6], A[s][3], A[s][7], xb.z, xb.w);
+      acc[q][s][0] = fmaf(d[s][0], c[0], acc[q][s][0]);
+      acc[q][s][1] = fmaf(d[s][0], c[1], acc[q][s][1]);
+      acc[q][s][2] = fmaf(d[s][1], c[2], acc[q][s][2]);
+      acc[q][s][3] = fmaf(d[s][1], c[3], acc[q][s][3]);
     }
   }
 }
 
-template <int MODE, int EPI, int W, int S>
+template <int MODE, int EPI, int W, int S, int TOKC>
 __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_constant__ CUtensorMap map) {
   constexpr int NS = MODE == 0 ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -195,7 +185,7 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const uint32_t stage_bytes = MODE == 0 ? (uint32_t)kQuantumBytes : 16u * (uint32_t)p.rowbytes;
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
-  uint8_t* stages = smem + (size_t)kTokC * p.xpitch * 2 + (size_t)warp * S * stage_bytes;
+  uint8_t* stages = smem + (size_t)TOKC * p.xpitch * 2 + (size_t)warp * S * stage_bytes;
 
   pdl_trigger();
   if (lane == 0) {
@@ -206,7 +196,7 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
   }
   pdl_wait();
   if (warp == 0) {
-    const int n = build_chunks(p, chunks, lane);
+    const int n = build_chunks<TOKC>(p, chunks, lane);
     if (lane == 0) s_nch = n;
   }
   __syncthreads();
@@ -269,9 +259,8 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
     }
     if (!has_tile(it)) continue;
     const int tile = (it % p.RR) * W + warp;
-    const bool two = c.n > 8;
+    const bool two = TOKC > 8 && c.n > 8;
     const uint16_t* xr0 = xs + (size_t)g * p.xpitch + 8 * t;
-    const uint16_t* xr1 = xr0 + (size_t)8 * p.xpitch;
     float acc[2][2][4];
 #pragma unroll
     for (int q = 0; q < 2; q++)
@@ -283,11 +272,31 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
       const int s = used % S;
       if (ok) ok = mbar_wait(&full[warp][s], (uint32_t)((used / S) & 1), p.status);
       if (ok) {
-        const uint8_t* st = stages + s * stage_bytes + (size_t)g * (MODE == 0 ? kRowPitch : p.rowbytes);
-        if (MODE == 0)
-          qmm_stage<NS>(st, kRowPitch, kSubBytes, min(8, p.nb - 8 * kq), 8 * kq, xr0, xr1, two, L, acc);
-        else
-          qmm_stage<NS>(st, p.rowbytes, 0, p.nb, 0, xr0, xr1, two, L, acc);
+        constexpr int TWO = TOKC > 8;
+        const int xstep = 8 * p.xpitch;
+        if (MODE == 0) {
+          // IN % 256 == 0: always 8 whole blocks, fully unrolled (immediate offsets)
+          const uint8_t* a = stages + s * stage_bytes + g * kRowPitch;
+          const uint16_t* xq = xr0 + 256 * kq;
+#pragma unroll
+          for (int k = 0; k < 8; k += 2) {
+            qmm_block<NS, TWO, 0>(a + 18 * k, a + 8 * kRowPitch + 18 * k, kSubBytes, xq + 32 * k, xstep, two, L, acc);
+            qmm_block<NS, TWO, 1>(a + 18 * k + 18, a + 8 * kRowPitch + 18 * k + 18, kSubBytes, xq + 32 * k + 32,
+                                  xstep, two, L, acc);
+          }
+        } else {
+          const uint8_t* a = stages + s * stage_bytes + (size_t)g * p.rowbytes;
+          const uint8_t* b = a + 8 * (size_t)p.rowbytes;
+          const uint16_t* xq = xr0;
+#pragma unroll 1
+          for (int k = 0; k < p.nb; k += 2) {
+            qmm_block<NS, TWO, 0>(a, b, 0, xq, xstep, two, L, acc);
+            qmm_block<NS, TWO, 1>(a + 18, b + 18, 0, xq + 32, xstep, two, L, acc);
+            a += 36;
+            b += 36;
+            xq += 64;
+          }
+        }
       }
       // this lane's reads of the stage fed the MMAs above; refill it
       __syncwarp();
@@ -331,18 +340,18 @@ __global__ void k_wacc(const float* __restrict__ y, const uint32_t* __restrict__
   out[(size_t)tok * OUT + o] = acc;
 }
 
-template <int MODE, int EPI, int W, int S>
+template <int MODE, int EPI, int W, int S, int TOKC>
 int qmm_launch(e4b_ctx* c, const char* name, const QmmP& p, const CUtensorMap& map, size_t smem, int grid) {
-  auto kern = k_qmm<MODE, EPI, W, S>;
+  auto kern = k_qmm<MODE, EPI, W, S, TOKC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "%s smem attr: %s", name, cudaGetErrorString(e));
   return e4b_launch(c, name, kern, dim3((unsigned)grid), dim3(32 * W), smem, p, map);
 }
 
 // Shared memory a variant needs: staged activations + the warps' rings.
-size_t qmm_smem(const QmmP& p, int mode, int W, int S) {
+size_t qmm_smem(const QmmP& p, int mode, int W, int S, int tokc) {
   const size_t stage = mode == 0 ? (size_t)kQuantumBytes : 16 * (size_t)p.rowbytes;
-  return (size_t)kTokC * p.xpitch * 2 + (size_t)W * S * stage;
+  return (size_t)tokc * p.xpitch * 2 + (size_t)W * S * stage;
 }
 constexpr size_t kQmmSmemCap = 227 * 1024 - 8 * 1024;   // dynamic budget beside the static chunk list
 
@@ -375,29 +384,36 @@ int qmm(e4b_ctx* c, const char* name, const uint16_t* x, const uint8_t* w, const
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     E4B_REQUIRE(c, r == CUDA_SUCCESS, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
   }
-  // variants: (warps, stages) that fit the shared-memory budget
-  struct V { int W, S; };
-  const V cand[4] = {{8, 3}, {8, 2}, {4, 3}, {4, 2}};
+  // variants (warps, stages, tokens per chunk), first that fits the shared
+  // memory: grouped experts hold few tokens each, so 8-token chunks and 16
+  // warps (more warps hide the dequant's latencies); a dense batch reuses each
+  // dequantised weight for 16 tokens.
+  struct V { int W, S, T; };
+  static const V cand[6] = {{16, 2, 8}, {8, 3, 16}, {8, 2, 16}, {4, 3, 16}, {4, 2, 16}, {4, 2, 8}};
   int vi = -1;
-  for (int i = 0; i < 4 && vi < 0; i++)
-    if (qmm_smem(p, mode, cand[i].W, cand[i].S) <= kQmmSmemCap) vi = i;
+  for (int i = offsets ? 0 : 1; i < 6 && vi < 0; i++)
+    if (qmm_smem(p, mode, cand[i].W, cand[i].S, cand[i].T) <= kQmmSmemCap) vi = i;
   E4B_REQUIRE(c, vi >= 0, "%s: IN=%d needs more shared memory than a CTA has", name, IN);
   const V v = cand[vi];
   p.RR = (p.tiles + v.W - 1) / v.W;
   int grid = c->sm_count;
   if (!offsets) {
-    const int items = (n_dense + kTokC - 1) / kTokC * p.RR;
+    E4B_REQUIRE(c, (n_dense + v.T - 1) / v.T <= kMaxChunks, "%s: n=%d tokens exceed %d", name, n_dense,
+                v.T * kMaxChunks);
+    const int items = (n_dense + v.T - 1) / v.T * p.RR;
     if (grid > items) grid = items;
   }
   if (grid < 1) grid = 1;
-  const size_t sm = qmm_smem(p, mode, v.W, v.S);
+  const size_t sm = qmm_smem(p, mode, v.W, v.S, v.T);
 #define QMM_CASE(M, EP)                                                          \
   if (mode == M && epi == EP) {                                                  \
     switch (vi) {                                                                \
-      case 0: return qmm_launch<M, EP, 8, 3>(c, name, p, map, sm, grid);         \
-      case 1: return qmm_launch<M, EP, 8, 2>(c, name, p, map, sm, grid);         \
-      case 2: return qmm_launch<M, EP, 4, 3>(c, name, p, map, sm, grid);         \
-      default: return qmm_launch<M, EP, 4, 2>(c, name, p, map, sm, grid);        \
+      case 0: return qmm_launch<M, EP, 16, 2, 8>(c, name, p, map, sm, grid);     \
+      case 1: return qmm_launch<M, EP, 8, 3, 16>(c, name, p, map, sm, grid);     \
+      case 2: return qmm_launch<M, EP, 8, 2, 16>(c, name, p, map, sm, grid);     \
+      case 3: return qmm_launch<M, EP, 4, 3, 16>(c, name, p, map, sm, grid);     \
+      case 4: return qmm_launch<M, EP, 4, 2, 16>(c, name, p, map, sm, grid);     \
+      default: return qmm_launch<M, EP, 4, 2, 8>(c, name, p, map, sm, grid);     \
     }                                                                            \
   }
   QMM_CASE(0, 0)
@@ -440,14 +456,12 @@ E4B_API int e4b_q40downgrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, cons
 E4B_API int e4b_q40mm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, float* y, int IN, int OUT, int n) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, x && w && y && n > 0 && OUT > 0, "q40mm: bad args");
-  E4B_REQUIRE(c, (n + kTokC - 1) / kTokC <= kMaxChunks, "q40mm: n=%d tokens exceed %d", n, kTokC * kMaxChunks);
   return qmm(c, "q40mm", x, w, nullptr, nullptr, y, nullptr, IN, OUT, 0, 1, 1, n, 0);
 }
 
 E4B_API int e4b_q40gumm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, uint16_t* yh, int IN, int FF, int n) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, x && w && yh && n > 0 && FF > 0 && FF % 32 == 0, "q40gumm: bad args");
-  E4B_REQUIRE(c, (n + kTokC - 1) / kTokC <= kMaxChunks, "q40gumm: n=%d tokens exceed %d", n, kTokC * kMaxChunks);
   return qmm(c, "q40gumm", x, w, nullptr, nullptr, nullptr, yh, IN, 2 * FF, FF, 1, 1, n, 1);
 }
 

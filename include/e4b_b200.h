@@ -275,6 +275,16 @@ E4B_API int e4b_attsplit_seq(e4b_ctx* ctx, const float* q, const uint16_t* kcach
                              int cache_slots, int nseq);
 E4B_API int e4b_attcomb_seq(e4b_ctx* ctx, const float* part_o, const float* part_ml, uint16_t* out_h, float* out_f,
                             float* lse, int QH, int HD, int max_chunks, int nseq, int xfo);
+/* attsplit_seq + attcomb_seq in one call for the batched decode, on the tensor
+ * cores: work items are (sequence, KV head, 64-slot chunk) over the live chunks
+ * only, each KV row is read once for its QH/KVH (<= 8) query heads, and
+ * kcache == vcache (keqv layers) loads the shared rows once.  Writes out_h
+ * (f16; fragment order when xfo) via part_o / part_ml [nseq][QH][max_chunks]
+ * (max_chunks * 64 >= the scanned slots).  HD % 64 == 0, HD <= 256; two launches. */
+E4B_API int e4b_attdec_seq(e4b_ctx* ctx, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                           const uint32_t* params, float* part_o, float* part_ml, uint16_t* out_h, int QH, int KVH,
+                           int HD, int window, int cachemode, int ring, int max_chunks, float scale, int cache_slots,
+                           int nseq, int xfo);
 
 /* ------------------------------------------------------------ argmax / feed */
 /* kernels/argmax2.wgsl:8-48 (both stages): out[0] = index of the largest x (ties
