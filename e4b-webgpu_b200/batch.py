@@ -13,8 +13,8 @@ src/engine-a4b.js:467-585 does for prefill):
   norms        e4b_rmsacc3        (rows = B)
   router       e4b_routertop      (batch = B)
   dense FFN    e4b_q40gumm + e4b_q40mm
-  experts      e4b_expgroup -> e4b_q40gugrp -> e4b_q40downgrp -> e4b_wacc
-  tail         e4b_a4btail        (rows = B)
+  experts      e4b_expgroup -> e4b_q40gugrp -> e4b_q40downgrp
+  tail         e4b_a4btail_wacc   (expert combine + a4btail, rows = B)
 
 Every f16 activation that feeds a q4_0 GEMM (normed rows, attention output,
 MoE input, GeGLU outputs) is kept in fragment order (xfo_perm), written so
@@ -150,9 +150,8 @@ class BatchEngine(Engine):
             d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
             d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
             d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
-            d.call("e4b_wacc", A.yo, A.inv, A.topk_w, A.moe_out, B, K, H)
-            d.call("e4b_a4btail", A.tmp, L.post_ffw1, A.moe_out, L.post_ffw2, L.post_ffw, A.hidden_b,
-                   nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
+            d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, A.yo, A.inv, A.topk_w, K, L.post_ffw2, L.post_ffw,
+                   A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
                    ctypes.c_float(L.scale), int(nxt is not None), B, 1)
         d.call("e4b_rmsnorm", A.hidden, self.out_norm, A.xf, None, None, H, B, ctypes.c_float(c.eps), 1, 0, 0)
         d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)

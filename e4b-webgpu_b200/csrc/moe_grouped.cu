@@ -58,6 +58,74 @@ __global__ void k_expgroup(const uint32_t* __restrict__ topk, int n, int E, uint
   }
 }
 
+// Stable counting sort for small E (<= kSortE): one entry per thread per round
+// of 1024; equal experts inside a warp found with match.any, warps ordered by a
+// per-round count table, rounds in order -> positions ascend with the entry
+// index inside every expert, exactly as the ballot version above.
+constexpr int kSortE = 256;
+__global__ void __launch_bounds__(1024) k_expsort(const uint32_t* __restrict__ topk, int n, int E,
+                                                  uint32_t* __restrict__ offsets, uint32_t* __restrict__ entries,
+                                                  uint32_t* __restrict__ inv, uint32_t* status) {
+  pdl_wait();
+  __shared__ uint32_t base[kSortE + 1];
+  __shared__ uint16_t wcnt[32][kSortE];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e <= E; e += 1024) base[e] = 0;
+  __syncthreads();
+  bool bad = false;
+  for (int i = tid; i < n; i += 1024) {
+    const uint32_t e = topk[i];
+    if (e < (uint32_t)E) atomicAdd(&base[e], 1u);
+    else bad = true;
+  }
+  if (bad) set_status(status, E4B_ST_BADINDEX);
+  __syncthreads();
+  if (warp == 0) {      // exclusive scan of the counts -> offsets and running bases
+    uint32_t run = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const uint32_t c = e < E ? base[e] : 0u;
+      uint32_t inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+      }
+      if (e < E) {
+        base[e] = run + inc - c;
+        offsets[e] = run + inc - c;
+      }
+      run += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) offsets[E] = run;
+  }
+  __syncthreads();
+  for (int r0 = 0; r0 < n; r0 += 1024) {
+    const int i = r0 + tid;
+    const uint32_t e = i < n ? topk[i] : 0xffffffffu;
+    const bool live = e < (uint32_t)E;
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+    for (int k = tid; k < 32 * E; k += 1024) wcnt[k / E][k % E] = 0;
+    __syncthreads();
+    if (live && rank == 0) wcnt[warp][e] = (uint16_t)__popc(peers);
+    __syncthreads();
+    if (live) {
+      uint32_t pos = base[e] + rank;
+      for (int w = 0; w < warp; w++) pos += wcnt[w][e];
+      entries[pos] = (uint32_t)i;
+      inv[i] = pos;
+    }
+    __syncthreads();
+    for (int e2 = tid; e2 < E; e2 += 1024) {
+      uint32_t add = 0;
+      for (int w = 0; w < 32; w++) add += wcnt[w][e2];
+      base[e2] += add;
+    }
+    __syncthreads();
+  }
+}
+
 // ---- multi-token q4_0 GEMM (grouped experts or one dense matrix).
 //
 // Work: a chunk is up to TOKC (8 or 16) tokens of one matrix (an expert's sorted
@@ -174,9 +242,13 @@ E4B_DEV void qmm_block(const uint8_t* a, const uint8_t* b, int sub_bytes, const 
   }
 }
 
-template <int MODE, int EPI, int W, int S, int TOKC>
+// KS > 1 (dense batches): the KS warps of a tile group split its quanta and sum
+// their partials through shared memory in a fixed order (deterministic), so a
+// small matrix still spreads over every SM.
+template <int MODE, int EPI, int W, int S, int TOKC, int KS>
 __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_constant__ CUtensorMap map) {
   constexpr int NS = MODE == 0 ? 2 : 1;
+  constexpr int TPI = W / KS;            // tiles per item
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[W][S];
   __shared__ __align__(8) uint64_t xbar;
@@ -186,6 +258,10 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
   const uint32_t stage_bytes = MODE == 0 ? (uint32_t)kQuantumBytes : 16u * (uint32_t)p.rowbytes;
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
   uint8_t* stages = smem + (size_t)TOKC * p.xpitch * 2 + (size_t)warp * S * stage_bytes;
+  float* red = reinterpret_cast<float*>(smem + (size_t)TOKC * p.xpitch * 2 + (size_t)W * S * stage_bytes);
+  // this warp's tile slot and quantum range
+  const int wt = warp / KS, kp = warp % KS;
+  const int kq0 = p.nq * kp / KS, kq1 = p.nq * (kp + 1) / KS;
 
   pdl_trigger();
   if (lane == 0) {
@@ -205,12 +281,12 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
   const int i1 = (int)((int64_t)T * (blockIdx.x + 1) / gridDim.x);
 
   // producer cursor over (item, quantum) of this warp's tiles; every lane keeps it
-  auto has_tile = [&](int it) { return (it % p.RR) * W + warp < p.tiles; };
-  int pit = i0, pkq = 0;
+  auto has_tile = [&](int it) { return (it % p.RR) * TPI + wt < p.tiles && kq0 < kq1; };
+  int pit = i0, pkq = kq0;
   while (pit < i1 && !has_tile(pit)) pit++;
   auto issue = [&](int s) {
     const Chunk c = chunks[pit / p.RR];
-    const int tile = (pit % p.RR) * W + warp;
+    const int tile = (pit % p.RR) * TPI + wt;
     uint8_t* st = stages + s * stage_bytes;
     if (MODE == 0) {
       if (lane == 0) mbar_expect_tx(&full[warp][s], (uint32_t)kQuantumBytes);
@@ -223,8 +299,8 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
       mbar_expect_tx(&full[warp][s], stage_bytes);
       bulk_g2s(st, p.w + ((size_t)c.e * p.ROWS + 16 * (size_t)tile) * p.rowbytes, stage_bytes, &full[warp][s]);
     }
-    if (++pkq == p.nq) {
-      pkq = 0;
+    if (++pkq == kq1) {
+      pkq = kq0;
       do pit++; while (pit < i1 && !has_tile(pit));
     }
   };
@@ -257,8 +333,9 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
       restage++;
       cur = ci;
     }
-    if (!has_tile(it)) continue;
-    const int tile = (it % p.RR) * W + warp;
+    const bool mine = has_tile(it);
+    if (KS == 1 && !mine) continue;
+    const int tile = (it % p.RR) * TPI + wt;
     const bool two = TOKC > 8 && c.n > 8;
     const uint16_t* xr0 = xs + (size_t)g * p.xpitch + 8 * t;
     float acc[2][2][4];
@@ -268,7 +345,7 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
       for (int s = 0; s < 2; s++)
 #pragma unroll
         for (int r = 0; r < 4; r++) acc[q][s][r] = 0.f;
-    for (int kq = 0; kq < p.nq; kq++, used++) {
+    for (int kq = kq0; kq < (mine ? kq1 : kq0); kq++, used++) {
       const int s = used % S;
       if (ok) ok = mbar_wait(&full[warp][s], (uint32_t)((used / S) & 1), p.status);
       if (ok) {
@@ -301,6 +378,31 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
       // this lane's reads of the stage fed the MMAs above; refill it
       __syncwarp();
       if (ok && pit < i1) issue(s);
+    }
+    if (KS > 1) {
+      // partials of the KS warps of each tile, summed in k order by its first warp
+      float* mine_red = red + ((size_t)warp * 32 + lane) * 16;
+#pragma unroll
+      for (int q = 0; q < 2; q++)
+#pragma unroll
+        for (int s2 = 0; s2 < 2; s2++)
+#pragma unroll
+          for (int r = 0; r < 4; r++) mine_red[q * 8 + s2 * 4 + r] = acc[q][s2][r];
+      __syncthreads();
+      if (kp == 0 && mine) {
+#pragma unroll
+        for (int q = 0; q < 2; q++)
+#pragma unroll
+          for (int s2 = 0; s2 < 2; s2++)
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+              float v = 0.f;
+              for (int k = 0; k < KS; k++) v += red[((size_t)(warp + k) * 32 + lane) * 16 + q * 8 + s2 * 4 + r];
+              acc[q][s2][r] = v;
+            }
+      }
+      __syncthreads();
+      if (kp != 0 || !mine) continue;
     }
     if (!ok) continue;
     // C fragment: [q][s][0..1] row g, tokens 8q+2t, +1; [2..3] row g+8
@@ -340,18 +442,18 @@ __global__ void k_wacc(const float* __restrict__ y, const uint32_t* __restrict__
   out[(size_t)tok * OUT + o] = acc;
 }
 
-template <int MODE, int EPI, int W, int S, int TOKC>
+template <int MODE, int EPI, int W, int S, int TOKC, int KS>
 int qmm_launch(e4b_ctx* c, const char* name, const QmmP& p, const CUtensorMap& map, size_t smem, int grid) {
-  auto kern = k_qmm<MODE, EPI, W, S, TOKC>;
+  auto kern = k_qmm<MODE, EPI, W, S, TOKC, KS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "%s smem attr: %s", name, cudaGetErrorString(e));
   return e4b_launch(c, name, kern, dim3((unsigned)grid), dim3(32 * W), smem, p, map);
 }
 
 // Shared memory a variant needs: staged activations + the warps' rings.
-size_t qmm_smem(const QmmP& p, int mode, int W, int S, int tokc) {
+size_t qmm_smem(const QmmP& p, int mode, int W, int S, int tokc, int ks) {
   const size_t stage = mode == 0 ? (size_t)kQuantumBytes : 16 * (size_t)p.rowbytes;
-  return (size_t)tokc * p.xpitch * 2 + (size_t)W * S * stage;
+  return (size_t)tokc * p.xpitch * 2 + (size_t)W * S * stage + (ks > 1 ? (size_t)W * 32 * 16 * 4 : 0);
 }
 constexpr size_t kQmmSmemCap = 227 * 1024 - 8 * 1024;   // dynamic budget beside the static chunk list
 
@@ -388,14 +490,18 @@ int qmm(e4b_ctx* c, const char* name, const uint16_t* x, const uint8_t* w, const
   // memory: grouped experts hold few tokens each, so 8-token chunks and 16
   // warps (more warps hide the dequant's latencies); a dense batch reuses each
   // dequantised weight for 16 tokens.
-  struct V { int W, S, T; };
-  static const V cand[6] = {{16, 2, 8}, {8, 3, 16}, {8, 2, 16}, {4, 3, 16}, {4, 2, 16}, {4, 2, 8}};
+  struct V { int W, S, T, KS; };
+  static const V cand[7] = {{16, 2, 8, 1}, {8, 3, 16, 4}, {8, 2, 16, 4}, {8, 3, 16, 1}, {8, 2, 16, 1},
+                            {4, 2, 16, 1}, {4, 2, 8, 1}};
   int vi = -1;
-  for (int i = offsets ? 0 : 1; i < 6 && vi < 0; i++)
-    if (qmm_smem(p, mode, cand[i].W, cand[i].S, cand[i].T) <= kQmmSmemCap) vi = i;
+  for (int i = offsets ? 0 : 1; i < 7 && vi < 0; i++) {
+    if (cand[i].KS > 1 && p.nq < cand[i].KS) continue;      // nothing to split (whole-row stages)
+    if (qmm_smem(p, mode, cand[i].W, cand[i].S, cand[i].T, cand[i].KS) <= kQmmSmemCap) vi = i;
+  }
   E4B_REQUIRE(c, vi >= 0, "%s: IN=%d needs more shared memory than a CTA has", name, IN);
   const V v = cand[vi];
-  p.RR = (p.tiles + v.W - 1) / v.W;
+  const int tpi = v.W / v.KS;
+  p.RR = (p.tiles + tpi - 1) / tpi;
   int grid = c->sm_count;
   if (!offsets) {
     E4B_REQUIRE(c, (n_dense + v.T - 1) / v.T <= kMaxChunks, "%s: n=%d tokens exceed %d", name, n_dense,
@@ -404,16 +510,17 @@ int qmm(e4b_ctx* c, const char* name, const uint16_t* x, const uint8_t* w, const
     if (grid > items) grid = items;
   }
   if (grid < 1) grid = 1;
-  const size_t sm = qmm_smem(p, mode, v.W, v.S, v.T);
+  const size_t sm = qmm_smem(p, mode, v.W, v.S, v.T, v.KS);
 #define QMM_CASE(M, EP)                                                          \
   if (mode == M && epi == EP) {                                                  \
     switch (vi) {                                                                \
-      case 0: return qmm_launch<M, EP, 16, 2, 8>(c, name, p, map, sm, grid);     \
-      case 1: return qmm_launch<M, EP, 8, 3, 16>(c, name, p, map, sm, grid);     \
-      case 2: return qmm_launch<M, EP, 8, 2, 16>(c, name, p, map, sm, grid);     \
-      case 3: return qmm_launch<M, EP, 4, 3, 16>(c, name, p, map, sm, grid);     \
-      case 4: return qmm_launch<M, EP, 4, 2, 16>(c, name, p, map, sm, grid);     \
-      default: return qmm_launch<M, EP, 4, 2, 8>(c, name, p, map, sm, grid);     \
+      case 0: return qmm_launch<M, EP, 16, 2, 8, 1>(c, name, p, map, sm, grid);  \
+      case 1: return qmm_launch<M, EP, 8, 3, 16, 4>(c, name, p, map, sm, grid);  \
+      case 2: return qmm_launch<M, EP, 8, 2, 16, 4>(c, name, p, map, sm, grid);  \
+      case 3: return qmm_launch<M, EP, 8, 3, 16, 1>(c, name, p, map, sm, grid);  \
+      case 4: return qmm_launch<M, EP, 8, 2, 16, 1>(c, name, p, map, sm, grid);  \
+      case 5: return qmm_launch<M, EP, 4, 2, 16, 1>(c, name, p, map, sm, grid);  \
+      default: return qmm_launch<M, EP, 4, 2, 8, 1>(c, name, p, map, sm, grid);  \
     }                                                                            \
   }
   QMM_CASE(0, 0)
@@ -433,6 +540,9 @@ E4B_API int e4b_expgroup(e4b_ctx* c, const uint32_t* topk, int n_tok, int K, int
   E4B_REQUIRE(c, topk && offsets && entries && inv, "expgroup: null buffer");
   E4B_REQUIRE(c, n_tok > 0 && K > 0 && E > 0 && E <= 4096 && (long long)n_tok * K < (1ll << 24),
               "expgroup: bad sizes n=%d K=%d E=%d", n_tok, K, E);
+  if (E <= kSortE)
+    return e4b_launch(c, "expgroup", k_expsort, dim3(1), dim3(1024), 0, topk, n_tok * K, E, offsets, entries, inv,
+                      c->status);
   return e4b_launch(c, "expgroup", k_expgroup, dim3(1), dim3(1024), (size_t)(E + 1) * 4, topk, n_tok * K, E, offsets,
                     entries, inv, c->status);
 }

@@ -70,15 +70,21 @@ __global__ void k_rmsacc3(const float* __restrict__ t, const float* __restrict__
                           uint16_t* __restrict__ y1, float* __restrict__ y2, uint16_t* __restrict__ y3,
                           float* __restrict__ h_out, int dim, float eps, int xfo) {
   pdl_wait();
-  extern __shared__ float hs[];
+  extern __shared__ float hs[];           // [dim] h, [dim] t
   __shared__ float sh[32];
+  float* ts = hs + dim;
   const size_t ob = (size_t)blockIdx.x * dim;
   float s = 0.f;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) s = fmaf(t[ob + i], t[ob + i], s);
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = t[ob + i];
+    ts[i] = v;
+    hs[i] = h_in[ob + i];
+    s = fmaf(v, v, s);
+  }
   const float inv1 = rms_scale(block_sum(s, sh), dim, eps);
   float s2 = 0.f;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-    const float h = h_in[ob + i] + t[ob + i] * inv1 * w_acc[i];
+    const float h = hs[i] + ts[i] * inv1 * w_acc[i];
     h_out[ob + i] = h;
     hs[i] = h;
     s2 = fmaf(h, h, s2);
@@ -94,17 +100,32 @@ __global__ void k_rmsacc3(const float* __restrict__ t, const float* __restrict__
   }
 }
 
+// m = the MoE output row; with y != null it is first formed here as the
+// slot-ordered combine sum_k w[row][k] * y[inv[row K + k]] (kernels/wacc.wgsl).
 __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict__ w1, const float* __restrict__ m,
                           const float* __restrict__ w2, const float* __restrict__ wp, const float* __restrict__ h_in,
                           const float* __restrict__ w_next, uint16_t* __restrict__ y_next, float* __restrict__ h_out,
-                          int H, float eps, float mul, int next, int xfo) {
+                          int H, float eps, float mul, int next, int xfo, const float* __restrict__ y,
+                          const uint32_t* __restrict__ inv, const float* __restrict__ tkw, int K) {
   pdl_wait();
-  extern __shared__ float comb[];
+  extern __shared__ float comb[];          // [H] comb, [H] t1, [H] h_in
   __shared__ float sh[32];
+  float* ts = comb + H;
+  float* hs = comb + 2 * H;
   const size_t ob = (size_t)blockIdx.x * H;
   float s1 = 0.f, s2 = 0.f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float a = t1[ob + i], mv = m[ob + i];
+    const float a = t1[ob + i];
+    float mv;
+    if (y) {
+      mv = 0.f;
+      for (int k = 0; k < K; k++)
+        mv += tkw[(size_t)blockIdx.x * K + k] * y[(size_t)inv[(size_t)blockIdx.x * K + k] * H + i];
+    } else {
+      mv = m[ob + i];
+    }
+    ts[i] = a;
+    hs[i] = h_in[ob + i];
     s1 = fmaf(a, a, s1);
     s2 = fmaf(mv, mv, s2);
     comb[i] = mv;
@@ -113,14 +134,14 @@ __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict_
   const float inv2 = rms_scale(block_sum(s2, sh), H, eps);
   float s3 = 0.f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float cc = t1[ob + i] * inv1 * w1[i] + comb[i] * inv2 * w2[i];
+    const float cc = ts[i] * inv1 * w1[i] + comb[i] * inv2 * w2[i];
     comb[i] = cc;
     s3 = fmaf(cc, cc, s3);
   }
   const float inv3 = rms_scale(block_sum(s3, sh), H, eps);
   float s4 = 0.f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float hn = (h_in[ob + i] + comb[i] * inv3 * wp[i]) * mul;
+    const float hn = (hs[i] + comb[i] * inv3 * wp[i]) * mul;
     h_out[ob + i] = hn;
     comb[i] = hn;
     s4 = fmaf(hn, hn, s4);
@@ -204,9 +225,9 @@ E4B_API int e4b_rmsacc3(e4b_ctx* c, const float* t, const float* w_acc, const fl
   E4B_REQUIRE(c, t && w_acc && w1 && w2 && w3 && h_in && y1 && y2 && y3 && h_out && dim > 0, "rmsacc3: bad args");
   E4B_REQUIRE(c, !xfo || dim % 32 == 0, "rmsacc3: fragment order needs dim %% 32 == 0");
   if (rows < 1) rows = 1;
-  const size_t sm = (size_t)dim * 4;
+  const size_t sm = (size_t)dim * 8;
   if (int r = set_smem(c, (const void*)k_rmsacc3, sm)) return r;
-  return e4b_launch(c, "rmsacc3", k_rmsacc3, dim3(rows), dim3(256), sm, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
+  return e4b_launch(c, "rmsacc3", k_rmsacc3, dim3(rows), dim3(512), sm, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
                     h_out, dim, eps, xfo);
 }
 
@@ -218,10 +239,26 @@ E4B_API int e4b_a4btail(e4b_ctx* c, const float* t1, const float* w1, const floa
   E4B_REQUIRE(c, !next || (w_next && y_next), "a4btail: next=1 needs w_next and y_next");
   E4B_REQUIRE(c, !xfo || H % 32 == 0, "a4btail: fragment order needs H %% 32 == 0");
   if (rows < 1) rows = 1;
-  const size_t sm = (size_t)H * 4;
+  const size_t sm = (size_t)H * 12;
   if (int r = set_smem(c, (const void*)k_a4btail, sm)) return r;
-  return e4b_launch(c, "a4btail", k_a4btail, dim3(rows), dim3(256), sm, t1, w1, m, w2, wp, h_in, w_next, y_next,
-                    h_out, H, eps, mul, next, xfo);
+  return e4b_launch(c, "a4btail", k_a4btail, dim3(rows), dim3(512), sm, t1, w1, m, w2, wp, h_in, w_next, y_next,
+                    h_out, H, eps, mul, next, xfo, (const float*)nullptr, (const uint32_t*)nullptr,
+                    (const float*)nullptr, 0);
+}
+
+E4B_API int e4b_a4btail_wacc(e4b_ctx* c, const float* t1, const float* w1, const float* y, const uint32_t* inv,
+                             const float* topk_w, int K, const float* w2, const float* wp, const float* h_in,
+                             const float* w_next, uint16_t* y_next, float* h_out, int H, float eps, float mul, int next,
+                             int rows, int xfo) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, t1 && w1 && y && inv && topk_w && K > 0 && w2 && wp && h_in && h_out && H > 0 && rows > 0,
+              "a4btail_wacc: bad args");
+  E4B_REQUIRE(c, !next || (w_next && y_next), "a4btail_wacc: next=1 needs w_next and y_next");
+  E4B_REQUIRE(c, !xfo || H % 32 == 0, "a4btail_wacc: fragment order needs H %% 32 == 0");
+  const size_t sm = (size_t)H * 12;
+  if (int r = set_smem(c, (const void*)k_a4btail, sm)) return r;
+  return e4b_launch(c, "a4btail_wacc", k_a4btail, dim3(rows), dim3(512), sm, t1, w1, (const float*)nullptr, w2, wp,
+                    h_in, w_next, y_next, h_out, H, eps, mul, next, xfo, y, inv, topk_w, K);
 }
 
 E4B_API int e4b_geglumul(e4b_ctx* c, const float* a, const float* b, float* y, int N) {

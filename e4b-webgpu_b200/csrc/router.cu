@@ -19,8 +19,18 @@ E4B_DEV void softmax_topk(float* p, int E, int K, const float* __restrict__ pes,
   for (int i = lane; i < E; i += 32) p[i] = expf(p[i] - mx);
   __syncwarp();
   float sum = 0.f;
-  if (lane == 0)
-    for (int i = 0; i < E; i++) sum += p[i];  // sequential, as the reference's single-thread epilogue
+  if (lane == 0) {   // sequential, as the reference's single-thread epilogue (vector loads, same order)
+    int i = 0;
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0)
+      for (; i + 4 <= E; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(p + i);
+        sum += v.x;
+        sum += v.y;
+        sum += v.z;
+        sum += v.w;
+      }
+    for (; i < E; i++) sum += p[i];
+  }
   sum = __shfl_sync(0xffffffffu, sum, 0);
   float wsum = 0.f;
   float wk[32];

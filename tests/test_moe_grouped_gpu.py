@@ -156,3 +156,48 @@ def test_fragment_order_producers(e4b, dev):
         dev.sync()
         combs[xfo] = dev.read(oh, np.uint16, B * QH * HD).reshape(B, QH * HD)
     assert np.array_equal(e4b.batch.to_xfo(combs[0]), combs[1])
+
+
+@pytest.mark.parametrize("n,K,E", [(64, 8, 128), (1, 8, 128), (700, 2, 16), (37, 4, 300), (2000, 3, 256)])
+def test_expgroup_stable_sort(e4b, dev, n, K, E):
+    """Entries sorted by expert, stable in the entry index (both sort kernels)."""
+    rng = np.random.default_rng(n + E)
+    idx = np.stack([rng.choice(E, K, replace=False) for _ in range(n)]).astype(np.uint32)
+    off, ent, inv = dev.alloc((E + 1) * 4), dev.alloc(n * K * 4), dev.alloc(n * K * 4)
+    dev.call("e4b_expgroup", dev.upload(idx).ptr, n, K, E, off.ptr, ent.ptr, inv.ptr)
+    dev.sync()
+    flat = idx.reshape(-1)
+    want = np.argsort(flat, kind="stable").astype(np.uint32)
+    entries = dev.read(ent, np.uint32, n * K)
+    assert np.array_equal(entries, want)
+    assert np.array_equal(dev.read(inv, np.uint32, n * K)[want], np.arange(n * K, dtype=np.uint32))
+    assert np.array_equal(dev.read(off, np.uint32, E + 1),
+                          np.concatenate([[0], np.cumsum(np.bincount(flat, minlength=E))]).astype(np.uint32))
+    assert dev.status() == 0
+
+
+def test_a4btail_wacc_equals_wacc_then_a4btail(e4b, dev):
+    """The fused expert combine + tail is bit-identical to e4b_wacc followed by e4b_a4btail."""
+    H, B, K = 512, 5, 4
+    rng = np.random.default_rng(9)
+    y = rng.standard_normal((B * K, H)).astype(F32)
+    inv = rng.permutation(B * K).astype(np.uint32)
+    tw = rng.uniform(0.1, 0.5, (B, K)).astype(F32)
+    t1 = rng.standard_normal((B, H)).astype(F32)
+    hin = rng.standard_normal((B, H)).astype(F32)
+    ws = [dev.upload(rng.uniform(0.5, 1.5, H).astype(F32)) for _ in range(4)]
+    by, binv, btw, bt, bh = (dev.upload(a) for a in (y, inv, tw, t1, hin))
+    m = dev.alloc(B * H * 4)
+    outs = []
+    for fused in (0, 1):
+        yn, ho = dev.alloc(B * H * 2), dev.alloc(B * H * 4)
+        if fused:
+            dev.call("e4b_a4btail_wacc", bt.ptr, ws[0].ptr, by.ptr, binv.ptr, btw.ptr, K, ws[1].ptr, ws[2].ptr, bh.ptr,
+                     ws[3].ptr, yn.ptr, ho.ptr, H, np.float32(1e-6), np.float32(0.7), 1, B, 1)
+        else:
+            dev.call("e4b_wacc", by.ptr, binv.ptr, btw.ptr, m.ptr, B, K, H)
+            dev.call("e4b_a4btail", bt.ptr, ws[0].ptr, m.ptr, ws[1].ptr, ws[2].ptr, bh.ptr, ws[3].ptr, yn.ptr, ho.ptr,
+                     H, np.float32(1e-6), np.float32(0.7), 1, B, 1)
+        dev.sync()
+        outs.append((dev.read(yn, np.uint16, B * H), dev.read(ho, F32, B * H)))
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
