@@ -2,9 +2,11 @@
 // + attcomb.wgsl semantics for nseq sequences at one common position).
 //
 // Work item = (sequence, KV head, chunk of 64 cache slots); only chunks that
-// hold live slots are visited, by a persistent grid.  Per item the CTA
-// bulk-copies the chunk's K and V rows (one 512-byte copy per row, into a
-// padded shared-memory layout) two items ahead of use, and does both products
+// hold live slots are visited, by a persistent grid.  Per item the CTA loads
+// the chunk's K and V tiles with 4-D TMA boxes (and the group's q rows with
+// one bulk copy) of [64 slots x 64 dims] (the
+// cache viewed as [nseq][slots][KVH][HD], 128-byte swizzle, so the MMA reads
+// are bank-conflict free) up to two items ahead of use, and does both products
 // on mma.sync m16n8k16 with the G query heads of the KV head as the 8 MMA
 // columns, so each KV row is read once for the whole GQA group:
 //   S^T[slot][head] = K[slot][:] . q[head][:]   (A = K rows, B = q as f16 hi + lo)
@@ -15,14 +17,17 @@
 // the unnormalised sum_t p_t v_t with its (max, sum p) as the reference's
 // phase A does; the combine kernel merges the live chunks (phase B).
 #include "attn.cuh"
-#include "stream.cuh"
+#include "q40_frag.cuh"
+#include "q40_stream.cuh"
 
 namespace {
 using namespace e4b;
 
 constexpr int kAC = 64;            // slots per chunk
 constexpr int kAW = 4;             // warps per CTA
+constexpr int kAS = 3;             // stages (items in flight)
 constexpr int kPP = kAC + 8;       // padded p row (halves)
+constexpr int kSub = kAC * 128;    // bytes of one [64 slots x 64 dims] swizzled box
 
 struct AttP {
   const float* q;                  // [nseq][QH][HD]
@@ -35,8 +40,17 @@ struct AttP {
   int QH, KVH, HD, G, window, cachemode, ring, max_chunks, nseq, keqv;
   float scale;
   size_t seq_stride;               // halves between sequences' caches
-  int kpitch;                      // halves per staged K / V row (HD + 8)
 };
+
+// Tiles are HD/64 boxes of [64 slots x 128 bytes] under the 128-byte swizzle:
+// the 16-byte chunk c of slot row r sits at chunk c ^ (r & 7) of its row.
+E4B_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
 
 E4B_DEV void ldsm_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* ptr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -45,6 +59,20 @@ E4B_DEV void ldsm_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r
 }
 E4B_DEV uint32_t lds32(const uint16_t* ptr) { return *reinterpret_cast<const uint32_t*>(ptr); }
 
+// The cache as a 4-D f16 tensor [nseq][slots][KVH][HD] for TMA boxes of
+// [64 dims x 1 head x 64 slots x 1 sequence] with the 128-byte swizzle.
+bool cache_map(CUtensorMap* m, const uint16_t* base, int HD, int KVH, int slots, int nseq) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dim[4] = {(cuuint64_t)HD, (cuuint64_t)KVH, (cuuint64_t)slots, (cuuint64_t)nseq};
+  const cuuint64_t stride[3] = {(cuuint64_t)HD * 2, (cuuint64_t)KVH * HD * 2, (cuuint64_t)slots * KVH * HD * 2};
+  const cuuint32_t box[4] = {64, 1, kAC, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<uint16_t*>(base), dim, stride, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 E4B_DEV SlotRule att_rule(const AttP& p) {
   SlotRule r{p.cachemode, p.ring, p.window, 0, 0};
   r.qp = p.params[0];
@@ -52,25 +80,27 @@ E4B_DEV SlotRule att_rule(const AttP& p) {
   return r;
 }
 
-__global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[2];
+__global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __grid_constant__ CUtensorMap kmap,
+                                                      const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kAS];
   __shared__ float red_m[kAW][8], red_l[kAW][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tile = kAC * p.kpitch;                                 // halves per K or V tile
-  uint16_t* kv = reinterpret_cast<uint16_t*>(smem);                // [2 stages][K tile | V tile]
-  uint4* qf = reinterpret_cast<uint4*>(smem + (size_t)4 * tile * 2);   // [HD/16][32 lanes]
-  uint16_t* ph = reinterpret_cast<uint16_t*>(qf + (p.HD / 16) * 32);   // [8 heads][kPP] p hi
+  const int tile = (p.HD / 64) * kSub;                             // bytes per K or V tile
+  const int qbytes = p.G * p.HD * 4;                               // the group's q rows (f32)
+  // swizzled boxes need 1024-byte aligned destinations
+  uint8_t* kv = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);   // [kAS stages][K tile | V tile]
+  float* qst = reinterpret_cast<float*>(kv + (size_t)kAS * 2 * tile);    // [kAS stages][G][HD]
+  uint4* qf = reinterpret_cast<uint4*>(qst + (size_t)kAS * p.G * p.HD);  // [HD/16][32 lanes]
+  uint16_t* ph = reinterpret_cast<uint16_t*>(qf + (p.HD / 16) * 32);     // [8 heads][kPP] p hi
   uint16_t* pl = ph + 8 * kPP;                                     // p lo
-  // stale rows only ever meet p = 0; start them at zero so 0 * x stays 0
-  for (int i = threadIdx.x; i < 4 * tile / 8; i += blockDim.x) reinterpret_cast<uint4*>(kv)[i] = make_uint4(0, 0, 0, 0);
   for (int i = threadIdx.x; i < 2 * 8 * kPP; i += blockDim.x) ph[i] = 0;
   if (threadIdx.x == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
+    if (!p.keqv) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
+    for (int s = 0; s < kAS; s++) mbar_init(&full[s], 1);
     fence_barrier_init();
   }
-  fence_proxy_async();
   __syncthreads();
   pdl_trigger();
   pdl_wait();
@@ -82,67 +112,106 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p) {
     return;
   }
   const int per_seq = p.KVH * nch, items = p.nseq * per_seq;
+  // a contiguous run of items per CTA: consecutive chunks of one (sequence, KV head)
+  const int i0 = (int)((long long)items * blockIdx.x / gridDim.x);
+  const int i1 = (int)((long long)items * (blockIdx.x + 1) / gridDim.x);
 
+  // one thread issues an item's boxes: HD/64 for K (+ HD/64 for V); slots
+  // past the cache's end read as zeros, slots past the live ones are finite
+  // cache contents that only meet p = 0
   auto issue = [&](int it, int s) {
     const int b = it / per_seq, rem = it % per_seq, kvh = rem / nch, c = rem % nch;
-    const uint32_t t0 = (uint32_t)c * kAC;
-    const int rows = (int)min((uint32_t)kAC, n - t0);
-    const uint32_t row_bytes = (uint32_t)p.HD * 2;
-    if (lane == 0) mbar_expect_tx(&full[s], (uint32_t)rows * row_bytes * (p.keqv ? 1u : 2u));
-    __syncwarp();
-    uint16_t* dk = kv + (size_t)s * 2 * tile;
-    for (int r = lane; r < rows; r += 32) {
-      const size_t off = (size_t)b * p.seq_stride + ((size_t)(t0 + r) * p.KVH + kvh) * p.HD;
-      bulk_g2s(dk + r * p.kpitch, p.kc + off, row_bytes, &full[s]);
-      if (!p.keqv) bulk_g2s(dk + tile + r * p.kpitch, p.vc + off, row_bytes, &full[s]);
+    uint8_t* dk = kv + (size_t)s * 2 * tile;
+    const bool newq = it == i0 || c == 0;       // the q rows change with the (sequence, KV head)
+    mbar_expect_tx(&full[s], (uint32_t)tile * (p.keqv ? 1u : 2u) + (newq ? (uint32_t)qbytes : 0u));
+    if (newq)
+      bulk_g2s(qst + (size_t)s * p.G * p.HD, p.q + ((size_t)b * p.QH + kvh * p.G) * p.HD, (uint32_t)qbytes, &full[s]);
+    for (int j = 0; j < p.HD / 64; j++) {
+      tma_load_4d(dk + j * kSub, &kmap, 64 * j, kvh, c * kAC, b, &full[s]);
+      if (!p.keqv) tma_load_4d(dk + tile + j * kSub, &vmap, 64 * j, kvh, c * kAC, b, &full[s]);
     }
   };
-  if (warp == 0) {
-    if ((int)blockIdx.x < items) issue(blockIdx.x, 0);
-    if ((int)(blockIdx.x + gridDim.x) < items) issue(blockIdx.x + gridDim.x, 1);
-  }
+  if (threadIdx.x == 0)
+    for (int k = 0; k < kAS; k++)
+      if (i0 + k < i1) issue(i0 + k, k);
 
+  // lane-constant shared-memory offsets of the swizzled tiles:
+  //   scores A: rows r0 = 16 warp + g (+8), chunk 2u (+1) of box j/4 -> xor with r0 & 7 = g
+  //   P.V A (ldmatrix.trans): row 16 ks + lrow, chunk 2 (dt & 3) + hbit of box dt / 4, xor with lane & 7
+  const int r0 = 16 * warp + g;
+  uint32_t koff[8];
+#pragma unroll
+  for (int u = 0; u < 8; u++) koff[u] = (uint32_t)(r0 * 128 + ((u ^ g) << 4) + 4 * t);
+  const int dtiles = p.HD / 16 / kAW;           // 1..4
+  const int lrow = (lane & 7) + ((lane >> 4) << 3), hbit = (lane >> 3) & 1;
+  uint32_t voff[4];
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    const int dt = warp * dtiles + u;
+    voff[u] = (uint32_t)((dt >> 2) * kSub + lrow * 128 + (((2 * (dt & 3) + hbit) ^ (lane & 7)) << 4));
+  }
   bool ok = true;
   int local = 0;
-  for (int it = blockIdx.x; it < items; it += gridDim.x, local++) {
-    const int s = local & 1;
-    const int b = it / per_seq, rem = it % per_seq, kvh = rem / nch, c = rem % nch;
-    const uint32_t t0 = (uint32_t)c * kAC;
-    // q fragments of the group's heads: (q[k], q[k+1]) and (q[k+8], q[k+9]), k = 16 j + 2 t, hi and lo
-    for (int i = threadIdx.x; i < (p.HD / 16) * 32; i += blockDim.x) {
-      const int j = i >> 5, gg = (i & 31) >> 2, tt = i & 3;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (gg < p.G) {
-        const float* qr = p.q + ((size_t)b * p.QH + kvh * p.G + gg) * p.HD + 16 * j + 2 * tt;
-        const float x[4] = {qr[0], qr[1], qr[8], qr[9]};
-        uint16_t h[4], l[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-          const __half hh = __float2half_rn(x[k]);
-          h[k] = __half_as_ushort(hh);
-          l[k] = f2h(x[k] - __half2float(hh));
-        }
-        v = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+  int b = i0 / per_seq, kvh = (i0 % per_seq) / nch, c = (i0 % per_seq) % nch;
+  for (int it = i0; it < i1; it++, local++) {
+    if (it != i0 && ++c == nch) {
+      c = 0;
+      if (++kvh == p.KVH) {
+        kvh = 0;
+        b++;
       }
-      qf[i] = v;
     }
-    __syncthreads();
-    if (ok) ok = mbar_wait(&full[s], (uint32_t)((local >> 1) & 1), p.status);
-    const uint16_t* Kt = kv + (size_t)s * 2 * tile;
-    const uint16_t* Vt = p.keqv ? Kt : Kt + tile;
+    const int s = local % kAS;
+    const uint32_t t0 = (uint32_t)c * kAC;
+    if (ok) ok = mbar_wait(&full[s], (uint32_t)((local / kAS) & 1), p.status);
+    // q fragments of the group's heads: (q[k], q[k+1]) and (q[k+8], q[k+9]), k = 16 j + 2 t, hi and lo;
+    // rebuilt only when the run moves to another (sequence, KV head)
+    if (it == i0 || c == 0) {
+      const float* qs = qst + (size_t)s * p.G * p.HD;
+      for (int i = threadIdx.x; i < (p.HD / 16) * 32; i += blockDim.x) {
+        const int j = i >> 5, gg = (i & 31) >> 2, tt = i & 3;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (gg < p.G) {
+          const float* qr = qs + gg * p.HD + 16 * j + 2 * tt;
+          const float x[4] = {qr[0], qr[1], qr[8], qr[9]};
+          uint16_t h[4], l[4];
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const __half hh = __float2half_rn(x[k]);
+            h[k] = __half_as_ushort(hh);
+            l[k] = f2h(x[k] - __half2float(hh));
+          }
+          v = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+        }
+        qf[i] = v;
+      }
+      __syncthreads();
+    }
+    const uint8_t* Kt = kv + (size_t)s * 2 * tile;
+    const uint8_t* Vt = p.keqv ? Kt : Kt + tile;
     // ---- scores of this warp's 16 slots x the group's heads
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
     if (ok) {
-      const uint16_t* k0 = Kt + (16 * warp + g) * p.kpitch + 2 * t;
-      const uint16_t* k1 = k0 + 8 * p.kpitch;
-#pragma unroll 4
-      for (int j = 0; j < p.HD / 16; j++) {
-        const uint32_t a0 = lds32(k0 + 16 * j), a1 = lds32(k1 + 16 * j);
-        const uint32_t a2 = lds32(k0 + 16 * j + 8), a3 = lds32(k1 + 16 * j + 8);
-        const uint4 qv = qf[j * 32 + lane];
-        mma16816(sc, a0, a1, a2, a3, qv.x, qv.y);
-        mma16816(sc, a0, a1, a2, a3, qv.z, qv.w);
+      // four independent accumulation chains over the dims, summed in a fixed order
+      float sp[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) sp[u][0] = sp[u][1] = sp[u][2] = sp[u][3] = 0.f;
+      for (int j0 = 0; j0 < p.HD / 16; j0 += 4) {
+        const uint8_t* kb = Kt + (j0 >> 2) * kSub;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int j = j0 + u;
+          const uint32_t a0 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u]);
+          const uint32_t a1 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u] + 1024);
+          const uint32_t a2 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u + 1]);
+          const uint32_t a3 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u + 1] + 1024);
+          const uint4 qv = qf[j * 32 + lane];
+          mma16816(sp[u], a0, a1, a2, a3, qv.x, qv.y);
+          mma16816(sp[u], a0, a1, a2, a3, qv.z, qv.w);
+        }
       }
+#pragma unroll
+      for (int r = 0; r < 4; r++) sc[r] = (sp[0][r] + sp[1][r]) + (sp[2][r] + sp[3][r]);
     }
     // sc: [0] (slot g, head 2t) [1] (slot g, head 2t+1) [2] (slot g+8, head 2t) [3] (slot g+8, head 2t+1)
     const uint32_t sa = t0 + 16 * warp + g, sb = sa + 8;
@@ -196,25 +265,40 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p) {
     }
     __syncthreads();
     // ---- O^T[d][head] for this warp's d tiles
-    const int dtiles = p.HD / 16 / kAW;
     const size_t part_row = (size_t)b * p.QH + kvh * p.G;
-    for (int dt = warp * dtiles; dt < (warp + 1) * dtiles && ok; dt++) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      // this warp's d tiles interleaved: independent accumulators
+      float acc[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < kAC / 16; ks++) {
-        uint32_t a0, a1, a2, a3;
-        const int row = 16 * ks + (lane & 7) + ((lane >> 4) << 3), col = 16 * dt + ((lane >> 3) & 1) * 8;
-        ldsm_x4_trans(a0, a1, a2, a3, Vt + row * p.kpitch + col);
         const uint16_t* bh = ph + g * kPP + 16 * ks + 2 * t;
         const uint16_t* bl = pl + g * kPP + 16 * ks + 2 * t;
-        mma16816(acc, a0, a1, a2, a3, lds32(bh), lds32(bh + 8));
-        mma16816(acc, a0, a1, a2, a3, lds32(bl), lds32(bl + 8));
-      }
-      // acc: [0] (d g, head 2t) [1] (d g, head 2t+1) [2] (d g+8, head 2t) [3] (d g+8, head 2t+1)
+        const uint32_t h0 = lds32(bh), h1 = lds32(bh + 8), l0 = lds32(bl), l1 = lds32(bl + 8);
 #pragma unroll
-      for (int k = 0; k < 4; k++) {
-        const int head = 2 * t + (k & 1), d = 16 * dt + g + ((k & 2) ? 8 : 0);
-        if (head < p.G) p.part_o[((part_row + head) * p.max_chunks + c) * p.HD + d] = acc[k];
+        for (int u = 0; u < 4; u++) {
+          if (u >= dtiles) break;
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_trans(a0, a1, a2, a3, Vt + voff[u] + ks * 16 * 128);
+          mma16816(acc[u], a0, a1, a2, a3, h0, h1);
+          mma16816(acc[u], a0, a1, a2, a3, l0, l1);
+        }
+      }
+      // acc[u]: [0] (d g, head 2t) [1] (d g, head 2t+1) [2] (d g+8, head 2t) [3] (d g+8, head 2t+1)
+      const size_t hstride = (size_t)p.max_chunks * p.HD;
+      float* o0 = p.part_o + ((part_row + 2 * t) * p.max_chunks + c) * p.HD + 16 * warp * dtiles + g;
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        if (u >= dtiles) break;
+        if (2 * t < p.G) {
+          o0[16 * u] = acc[u][0];
+          o0[16 * u + 8] = acc[u][2];
+        }
+        if (2 * t + 1 < p.G) {
+          o0[hstride + 16 * u] = acc[u][1];
+          o0[hstride + 16 * u + 8] = acc[u][3];
+        }
       }
     }
     if (warp == 0 && g == 0 && ok) {
@@ -237,7 +321,7 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p) {
     }
     // every warp is done with this stage, the p rows and the q fragments
     __syncthreads();
-    if (warp == 0 && ok && it + 2 * (int)gridDim.x < items) issue(it + 2 * gridDim.x, s);
+    if (threadIdx.x == 0 && ok && it + kAS < i1) issue(it + kAS, s);
   }
 }
 
@@ -294,13 +378,17 @@ E4B_API int e4b_attdec_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, c
   p.QH = QH; p.KVH = KVH; p.HD = HD; p.G = QH / KVH; p.window = window; p.cachemode = cachemode; p.ring = ring;
   p.max_chunks = max_chunks; p.nseq = nseq; p.keqv = kcache == vcache; p.scale = scale;
   p.seq_stride = (size_t)cache_slots * KVH * HD;
-  p.kpitch = HD + 8;
-  const size_t smem = (size_t)4 * kAC * p.kpitch * 2 + (size_t)(HD / 16) * 32 * 16 + (size_t)2 * 8 * kPP * 2;
+  CUtensorMap kmap, vmap;
+  E4B_REQUIRE(c, cache_map(&kmap, kcache, HD, KVH, cache_slots, nseq), "attdec_seq: K cache tensor map failed");
+  if (p.keqv) vmap = kmap;
+  else E4B_REQUIRE(c, cache_map(&vmap, vcache, HD, KVH, cache_slots, nseq), "attdec_seq: V cache tensor map failed");
+  const size_t smem = (size_t)kAS * 2 * (HD / 64) * kSub + (size_t)kAS * p.G * HD * 4 + (size_t)(HD / 16) * 32 * 16 +
+                      (size_t)2 * 8 * kPP * 2 + 1024;
   cudaError_t e = cudaFuncSetAttribute(k_attdec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "attdec smem attr: %s", cudaGetErrorString(e));
   const long long most = (long long)nseq * KVH * max_chunks;
   const int grid = (int)(most < c->sm_count ? most : c->sm_count);
-  if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW), smem, p)) return r;
+  if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW), smem, p, kmap, vmap)) return r;
   return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(128), 0, p, out_h, xfo);
 }
 

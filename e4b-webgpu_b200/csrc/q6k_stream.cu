@@ -244,13 +244,15 @@ __global__ void __launch_bounds__(256) k_q6k_mm(const uint8_t* __restrict__ w, c
 // ---- batched LM head, persistent and staged.  A unit is (block of 128 rows,
 // pass of up to 64 tokens); per q6_K superblock (256 k) a producer warp copies
 // the pass's activations (pre-split into f16 hi / lo and laid out as the MMA
-// B fragments: k_q6x_prep) with one bulk copy, and each row's 210-byte
-// superblock as its 16-byte-aligned 224-byte cover, into a 2-deep ring; four
-// MMA warps take 32 rows each (two 16-row subtiles share every B fragment).
+// B fragments: k_q6x_prep) with one bulk copy into a 2-deep ring shared by the
+// CTA, and each of the four MMA warps stages its own 32 rows' superblocks
+// (the 16-byte-aligned 224-byte cover of each 210-byte block, 16-byte
+// cp.async per piece, 3 deep); two 16-row subtiles share every B fragment.
 constexpr int kLmRows = 128;
-constexpr int kLmSlot = 224;
+constexpr int kLmSlot = 240;                      // the 224-byte cover + 16 (row pitch off the bank period)
 constexpr int kLmXSlab = 8 * 16 * 32 * 16;        // 8 token groups x 16 k-steps x 32 lanes x 16 B
-constexpr int kLmWSlab = kLmRows * kLmSlot;
+constexpr int kLmWS = 3;                          // weight stages per warp
+constexpr int kLmWWarp = 32 * kLmSlot;            // one warp's rows of one superblock
 
 // xp[s][q][j][lane] = {hi(x[k], x[k+1]), hi(x[k+8], x[k+9]), lo(..), lo(..)} for
 // token 8q + lane/4 and k = 256 s + 16 j + 2 (lane % 4); zero beyond n.
@@ -277,6 +279,13 @@ __global__ void k_q6x_prep(const float* __restrict__ x, uint4* __restrict__ xp, 
   xp[idx] = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
 }
 
+E4B_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+E4B_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+E4B_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, const uint4* __restrict__ xp,
                                                   float* __restrict__ y, int N, int OUT, int n, int NG, float softcap,
                                                   uint32_t* status) {
@@ -286,7 +295,7 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
   const int nsb = N >> 8, rowbytes = nsb * 210;
   const int RB = (OUT + kLmRows - 1) / kLmRows, passes = (NG + 7) / 8, units = RB * passes;
   uint8_t* xbuf = smem;
-  uint8_t* wbuf = smem + 2 * kLmXSlab;
+  uint8_t* wbuf = smem + 2 * kLmXSlab + (size_t)(warp < 4 ? warp : 0) * kLmWS * kLmWWarp;
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; b++) {
       mbar_init(&full[b], 1);
@@ -298,32 +307,44 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
   pdl_trigger();
   pdl_wait();
   if (warp == 4) {
-    // producer
+    // producer of the activation slabs
     int seq = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const int rb = u / passes, pass = u % passes, ng = min(8, NG - 8 * pass);
-      const int rows = min(kLmRows, OUT - kLmRows * rb);
+      const int pass = u % passes, ng = min(8, NG - 8 * pass);
       for (int sb = 0; sb < nsb && ok; sb++, seq++) {
         const int b = seq & 1;
         if (seq >= 2) ok = mbar_wait(&empty[b], (uint32_t)(((seq >> 1) - 1) & 1), status);
-        if (!ok) break;
-        if (lane == 0) {
-          mbar_expect_tx(&full[b], (uint32_t)(ng * (kLmXSlab / 8) + rows * kLmSlot));
+        if (ok && lane == 0) {
+          mbar_expect_tx(&full[b], (uint32_t)(ng * (kLmXSlab / 8)));
           bulk_g2s(xbuf + b * kLmXSlab, xp + ((size_t)sb * NG + 8 * pass) * 16 * 32, (uint32_t)(ng * (kLmXSlab / 8)),
                    &full[b]);
         }
         __syncwarp();
-        for (int r = lane; r < rows; r += 32) {
-          const size_t start = (size_t)(kLmRows * rb + r) * rowbytes + 210 * sb;
-          bulk_g2s(wbuf + b * kLmWSlab + r * kLmSlot, w + (start & ~(size_t)15), kLmSlot, &full[b]);
-        }
       }
     }
     return;
   }
   // MMA warps: rows 32 warp + {g, g+8} (subtile 0) and + 16 (subtile 1)
   const int g = lane >> 2, t = lane & 3;
+  const int steps = ((units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * nsb;   // this CTA's steps
+  // stage step k's superblock of this lane's row (row 32 warp + lane of the block)
+  auto stage_w = [&](int k) {
+    const int u = blockIdx.x + (k / nsb) * gridDim.x, sb = k % nsb;
+    const int row = kLmRows * (u / passes) + 32 * warp + lane;
+    if (row < OUT) {
+      const size_t start = (size_t)row * rowbytes + 210 * sb;
+      const uint8_t* src = w + (start & ~(size_t)15);
+      uint8_t* dst = wbuf + (k % kLmWS) * kLmWWarp + lane * kLmSlot;
+#pragma unroll
+      for (int c = 0; c < 14; c++) cp_async16(dst + 16 * c, src + 16 * c);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int k = 0; k < kLmWS - 1; k++)
+    if (k < steps) stage_w(k);
+    else cp_async_commit();
   int seq = 0;
   bool ok = true;
   for (int u = blockIdx.x; u < units; u += gridDim.x) {
@@ -340,17 +361,25 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
     for (int i = 0; i < 4; i++) rr[i] = 32 * warp + g + 8 * i;   // rows g, g+8, g+16, g+24 of the block
     for (int sb = 0; sb < nsb; sb++, seq++) {
       const int b = seq & 1;
+      // keep kLmWS - 1 weight stages in flight; this step's has landed after the wait
+      if (seq + kLmWS - 1 < steps) stage_w(seq + kLmWS - 1);
+      else cp_async_commit();
+      cp_async_wait<kLmWS - 1>();
+      __syncwarp();
       if (ok) ok = mbar_wait(&full[b], (uint32_t)((seq >> 1) & 1), status);
       if (ok) {
+        const uint8_t* wst = wbuf + (seq % kLmWS) * kLmWWarp;
         const uint8_t* blk[4];
         float d[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
           const size_t start = (size_t)(kLmRows * rb + rr[i]) * rowbytes + 210 * sb;
-          blk[i] = wbuf + b * kLmWSlab + rr[i] * kLmSlot + (int)(start & 15);
+          blk[i] = wst + (g + 8 * i) * kLmSlot + (int)(start & 15);
           d[i] = h2f(*reinterpret_cast<const uint16_t*>(blk[i] + 208));
         }
         const uint4* xs = reinterpret_cast<const uint4*>(xbuf + b * kLmXSlab);
+        // all 8 token groups every step (a short last pass computes unused
+        // columns that are not stored), 16 independent MMA chains per step
 #pragma unroll 2
         for (int j = 0; j < 16; j++) {
           const int e0 = 16 * j + 2 * t;
@@ -366,19 +395,32 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
             A[s][3] = q6_pair(blk[2 * s + 1], e0 + 8);
           }
 #pragma unroll
-          for (int q = 0; q < 8; q++) {
-            if (q >= ng) break;
-            const uint4 xv = xs[(q * 16 + j) * 32 + lane];
+          for (int hq = 0; hq < 8; hq += 4) {
+            // 4 token groups x 2 subtiles: 8 independent MMA chains
+            uint4 xv[4];
 #pragma unroll
-            for (int s = 0; s < 2; s++) {
-              float c[4] = {0.f, 0.f, 0.f, 0.f};
-              mma16816(c, A[s][0], A[s][1], A[s][2], A[s][3], xv.x, xv.y);
-              mma16816(c, A[s][0], A[s][1], A[s][2], A[s][3], xv.z, xv.w);
-              acc[q][s][0] = fmaf(sc[2 * s], c[0], acc[q][s][0]);
-              acc[q][s][1] = fmaf(sc[2 * s], c[1], acc[q][s][1]);
-              acc[q][s][2] = fmaf(sc[2 * s + 1], c[2], acc[q][s][2]);
-              acc[q][s][3] = fmaf(sc[2 * s + 1], c[3], acc[q][s][3]);
-            }
+            for (int q = 0; q < 4; q++) xv[q] = xs[((hq + q) * 16 + j) * 32 + lane];
+            float c[4][2][4];
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+              for (int s = 0; s < 2; s++) {
+                c[q][s][0] = c[q][s][1] = c[q][s][2] = c[q][s][3] = 0.f;
+                mma16816(c[q][s], A[s][0], A[s][1], A[s][2], A[s][3], xv[q].x, xv[q].y);
+              }
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+              for (int s = 0; s < 2; s++) mma16816(c[q][s], A[s][0], A[s][1], A[s][2], A[s][3], xv[q].z, xv[q].w);
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+              for (int s = 0; s < 2; s++) {
+                acc[hq + q][s][0] = fmaf(sc[2 * s], c[q][s][0], acc[hq + q][s][0]);
+                acc[hq + q][s][1] = fmaf(sc[2 * s], c[q][s][1], acc[hq + q][s][1]);
+                acc[hq + q][s][2] = fmaf(sc[2 * s + 1], c[q][s][2], acc[hq + q][s][2]);
+                acc[hq + q][s][3] = fmaf(sc[2 * s + 1], c[q][s][3], acc[hq + q][s][3]);
+              }
           }
         }
       }
@@ -402,6 +444,7 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
         }
     }
   }
+  cp_async_wait<0>();
 }
 
 }  // namespace
@@ -420,7 +463,7 @@ E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* c, const uint8_t* w, const float* x, ui
     if (int r = e4b_launch(c, "q6x_prep", k_q6x_prep, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, x, xp, n, N,
                            NG))
       return r;
-    const size_t smem = 2 * (size_t)kLmXSlab + 2 * (size_t)kLmWSlab;
+    const size_t smem = 2 * (size_t)kLmXSlab + 4 * (size_t)kLmWS * kLmWWarp;
     cudaError_t e = cudaFuncSetAttribute(k_q6mm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q6mm smem attr: %s", cudaGetErrorString(e));
     const int units = (OUT + kLmRows - 1) / kLmRows * ((NG + 7) / 8);
