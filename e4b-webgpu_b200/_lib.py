@@ -60,10 +60,28 @@ _LIB = None
 PROTOS = None
 
 
+def _nccl_path():
+    """The NCCL build the expert-parallel exchange opens: E4B_NCCL_LIB, else the
+    nvidia-nccl wheel's (the one a CUDA-enabled framework in this process would
+    load, so both share one copy), else the loader's libnccl.so.2."""
+    if os.environ.get("E4B_NCCL_LIB"):
+        return os.environ["E4B_NCCL_LIB"]
+    import importlib.util
+    spec = importlib.util.find_spec("nvidia")
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        cand = os.path.join(base, "nccl", "lib", "libnccl.so.2")
+        if os.path.exists(cand):
+            return cand
+    return ""
+
+
 def lib():
     """Load libe4b_b200.so and type every function the header declares."""
     global _LIB, PROTOS
     if _LIB is None:
+        path = _nccl_path()
+        if path:
+            os.environ.setdefault("E4B_NCCL_LIB", path)
         if not os.path.exists(LIBPATH):
             raise RuntimeError(f"{LIBPATH} is missing: build it with __graft_entry__.build() "
                                "(the decode path has no CPU fallback)")

@@ -58,6 +58,15 @@ def xfo_perm(n: int) -> np.ndarray:
     return pos
 
 
+def nccl_unique_id(dev) -> bytes:
+    """A fresh NCCL unique id (128 bytes) for an expert-parallel group."""
+    buf = (ctypes.c_uint8 * 128)()
+    rc = dev.L.e4b_nccl_unique_id(ctypes.cast(buf, ctypes.c_void_p))
+    if rc != 0:
+        raise RuntimeError(f"e4b_nccl_unique_id failed ({rc})")
+    return bytes(buf)
+
+
 def to_xfo(x: np.ndarray) -> np.ndarray:
     """Rows of x (last axis) permuted into fragment order."""
     out = np.empty_like(x)
@@ -70,8 +79,17 @@ def from_xfo(x: np.ndarray) -> np.ndarray:
 
 
 class BatchEngine(Engine):
-    def __init__(self, src, nseq: int, device=0, *, chunk: int = 64):
+    def __init__(self, src, nseq: int, device=0, *, chunk: int = 64, ep=None):
+        """nseq sequences decoded in lockstep on this GPU.  ep = (nranks, rank,
+        nccl_id): expert parallelism -- this rank decodes its nseq sequences and
+        owns experts [rank*E/nranks, (rank+1)*E/nranks); every rank of the
+        communicator must build its engine with the same nccl_id (from
+        e4b_nccl_unique_id on one rank)."""
         self.nseq = int(nseq)
+        self.ep = None
+        if ep is not None:
+            nranks, rank, nid = ep
+            self.ep = (int(nranks), int(rank), bytes(nid))
         super().__init__(src, device, chunk=chunk, record=False, fused=False)
         if not self.cfg.moe:
             raise ValueError("BatchEngine drives the MoE (A4B) graph")
@@ -116,6 +134,8 @@ class BatchEngine(Engine):
         A.amax_part = d.alloc(B * ARGMAX_PARTS * 8, "amaxPart")
         A.amax = d.alloc(B * 8, "amax")
         A.ring = d.alloc(B * RING_CAP * 4, "tokRing")
+        if self.ep is not None:
+            self._alloc_ep(A)
         self.A = A
         ws = int(d.L.e4b_workspace_bytes())
         A.ws = d.alloc(ws, "workspace")
@@ -124,6 +144,52 @@ class BatchEngine(Engine):
         d.call("e4b_host_alloc", ctypes.c_size_t(32), ctypes.byref(p))
         self.host_params = np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint32)), shape=(8,))
         self._host_params_ptr = p.value
+
+    def _alloc_ep(self, A):
+        c, d, B = self.cfg, self.dev, self.nseq
+        N, rank, nid = self.ep
+        H, E, K, EF = c.hidden, c.experts, c.topk, c.expert_ff
+        if E % N:
+            raise ValueError(f"{E} experts do not split over {N} ranks")
+        self.e_loc = E // N
+        self.cap = B * K                       # every entry of this rank could go to one peer
+        rows = N * self.cap
+        A.ep_sx = d.alloc(rows * H * 2, "epSendX")
+        A.ep_rx = d.alloc(rows * H * 2, "epRecvX")
+        A.ep_sid = d.alloc(rows * 4, "epSendIds")
+        A.ep_rid = d.alloc(rows * 4, "epRecvIds")
+        A.ep_slot = d.alloc(B * K * 4, "epSlot")
+        A.ep_off = d.alloc((self.e_loc + 1) * 4, "epOffsets")
+        A.ep_ent = d.alloc(rows * 4, "epEntries")
+        A.ep_inv = d.alloc(rows * 4, "epInv")
+        A.ep_gl = d.alloc(rows * EF * 2, "epGeglu")
+        A.ep_y = d.alloc(rows * H * 4, "epY")
+        A.ep_sy = d.alloc(rows * H * 4, "epSendY")
+        A.ep_ry = d.alloc(rows * H * 4, "epRecvY")
+        idbuf = (ctypes.c_uint8 * 128).from_buffer_copy(nid)
+        d.call("e4b_nccl_init", N, rank, ctypes.cast(idbuf, ctypes.c_void_p))
+        # this rank's experts inside the full expert tensors
+        per_gu = 2 * EF * (H // 32) * 18
+        per_dn = H * (EF // 32) * 18
+        for L in self.layers:
+            L.gu_loc = ctypes.c_void_p(L.gu_exps.ptr + rank * self.e_loc * per_gu)
+            L.dn_loc = ctypes.c_void_p(L.down_exps.ptr + rank * self.e_loc * per_dn)
+
+    def _moe_ep(self, L):
+        """Routed experts across the ranks (dispatch -> local experts -> return)."""
+        c, d, A, B = self.cfg, self.dev, self.A, self.nseq
+        N = self.ep[0]
+        H, E, K, EF = c.hidden, c.experts, c.topk, c.expert_ff
+        rows = N * self.cap
+        d.call("e4b_ep_dispatch", A.topk_idx, B, K, E, N, self.cap, A.moe_in, H, A.ep_sx, A.ep_sid, A.ep_slot)
+        d.call("e4b_ep_exchange", A.ep_sx, A.ep_rx, ctypes.c_size_t(self.cap * H * 2))
+        d.call("e4b_ep_exchange", A.ep_sid, A.ep_rid, ctypes.c_size_t(self.cap * 4))
+        d.call("e4b_expgroup", A.ep_rid, rows, 1, self.e_loc, A.ep_off, A.ep_ent, A.ep_inv)
+        d.call("e4b_q40gugrp", A.ep_rx, L.gu_loc, A.ep_off, A.ep_ent, A.ep_gl, H, EF, self.e_loc, 1)
+        d.call("e4b_q40downgrp", A.ep_gl, L.dn_loc, A.ep_off, A.ep_ent, A.ep_y, EF, H, self.e_loc)
+        d.call("e4b_ep_return", A.ep_rid, A.ep_inv, A.ep_y, rows, H, A.ep_sy)
+        d.call("e4b_ep_exchange", A.ep_sy, A.ep_ry, ctypes.c_size_t(self.cap * H * 4))
+        return A.ep_ry, A.ep_slot
 
     # ------------------------------------------------------------ one step (B tokens)
     def encode_forward(self):
@@ -147,10 +213,14 @@ class BatchEngine(Engine):
             d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
             d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
             d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
-            d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
-            d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
-            d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
-            d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, A.yo, A.inv, A.topk_w, K, L.post_ffw2, L.post_ffw,
+            if self.ep is None:
+                d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
+                d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
+                d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
+                y_rows, y_map = A.yo, A.inv
+            else:
+                y_rows, y_map = self._moe_ep(L)
+            d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, y_rows, y_map, A.topk_w, K, L.post_ffw2, L.post_ffw,
                    A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
                    ctypes.c_float(L.scale), int(nxt is not None), B, 1)
         d.call("e4b_rmsnorm", A.hidden, self.out_norm, A.xf, None, None, H, B, ctypes.c_float(c.eps), 1, 0, 0)

@@ -60,8 +60,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> dict:
             if verbose:
                 print(" ".join(cmd[-3:]))
     if _newer(LIB, objs):
-        _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static",
-              "-L/usr/lib/x86_64-linux-gnu", "-lnccl"])
+        _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static", "-ldl"])
     synth_src = os.path.join(CSRC, "synth.c")
     if _newer(SYNTH, [synth_src]):
         # -ffp-contract=off: the q4_0 rule x*id + 8.5 must round like the

@@ -35,6 +35,7 @@ struct e4b_ctx {
 int e4b_fail(e4b_ctx* c, int code, const char* fmt, ...);
 namespace e4b {
 void dense_plans_release(e4b_ctx* c);   // frees a context's fused token plans
+void nccl_release(e4b_ctx* c);          // destroys a context's NCCL communicator
 }
 
 #define E4B_CHECK_CTX(c) \

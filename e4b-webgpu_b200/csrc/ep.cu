@@ -1,0 +1,249 @@
+// Expert parallelism for the batched MoE decode: experts
+// sharded in contiguous blocks over the ranks of one node, every rank decoding
+// its own sequences (attention and dense layers replicated).  Per MoE layer:
+//   dispatch   each (token, slot) entry's f16 activation row and local expert
+//              id go to the expert's owner, packed per peer in arrival order
+//              into fixed-capacity slabs (no host round trip for counts);
+//   exchange   grouped ncclSend / ncclRecv with every rank (NVLink / NVSwitch);
+//   experts    the owner groups what it received by local expert and runs the
+//              grouped GEMMs on those rows;
+//   return     each result row goes back into the slab slot it came from, so
+//              the source finds entry (t, k) at slot[t*K+k] and combines in
+//              slot order exactly as the single-GPU path does.
+// The reference's engine-a4b.js has no multi-GPU path; the per-entry math is
+// the single-GPU kernels', so results are bit-identical for any rank count.
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdlib.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+// NCCL is opened at run time (E4B_NCCL_LIB, else libnccl.so.2) with local
+// symbols, so the process can also hold another framework's NCCL build.
+struct Nccl {
+  bool tried = false;
+  void* h = nullptr;
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*groupStart)() = nullptr;
+  ncclResult_t (*groupEnd)() = nullptr;
+  ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*errorString)(ncclResult_t) = nullptr;
+};
+Nccl g_nccl;
+
+template <class F>
+bool sym(void* h, const char* name, F& f) {
+  f = reinterpret_cast<F>(dlsym(h, name));
+  return f != nullptr;
+}
+// Under g_mu.
+Nccl* nccl() {
+  if (!g_nccl.tried) {
+    g_nccl.tried = true;
+    const char* path = getenv("E4B_NCCL_LIB");
+    void* h = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (h && sym(h, "ncclGetUniqueId", g_nccl.getUniqueId) && sym(h, "ncclCommInitRank", g_nccl.commInitRank) &&
+        sym(h, "ncclCommDestroy", g_nccl.commDestroy) && sym(h, "ncclGroupStart", g_nccl.groupStart) &&
+        sym(h, "ncclGroupEnd", g_nccl.groupEnd) && sym(h, "ncclSend", g_nccl.send) &&
+        sym(h, "ncclRecv", g_nccl.recv) && sym(h, "ncclGetErrorString", g_nccl.errorString))
+      g_nccl.h = h;
+  }
+  return g_nccl.h ? &g_nccl : nullptr;
+}
+
+constexpr uint32_t kNone = 0xffffffffu;
+
+struct NcclState {
+  ncclComm_t comm = nullptr;
+  int nranks = 0, rank = 0;
+};
+std::mutex g_mu;
+std::vector<std::pair<e4b_ctx*, NcclState>> g_comms;
+
+NcclState* state_of(e4b_ctx* c) {
+  for (auto& kv : g_comms)
+    if (kv.first == c) return &kv.second;
+  return nullptr;
+}
+
+// One CTA: entry i = t*K + k in order; its destination rank is the owner of
+// expert topk[i]; its position among the entries bound there is the number of
+// earlier entries with the same destination (stable, deterministic).
+__global__ void __launch_bounds__(1024) k_ep_dispatch(const uint32_t* __restrict__ topk, int n, int per_rank,
+                                                      int nranks, int cap, const uint16_t* __restrict__ x, int K,
+                                                      int H, uint16_t* __restrict__ send_x,
+                                                      uint32_t* __restrict__ send_ids, uint32_t* __restrict__ slot,
+                                                      uint32_t* status) {
+  pdl_wait();
+  __shared__ uint32_t base[64];
+  __shared__ uint32_t wcnt[32][64];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < nranks * cap; i += 1024) send_ids[i] = kNone;
+  if (tid < 64) base[tid] = 0;
+  __syncthreads();
+  for (int r0 = 0; r0 < n; r0 += 1024) {
+    const int i = r0 + tid;
+    uint32_t d = kNone;
+    if (i < n) {
+      const uint32_t e = topk[i];
+      d = e / (uint32_t)per_rank;
+      if (d >= (uint32_t)nranks) {
+        set_status(status, E4B_ST_BADINDEX);
+        slot[i] = kNone;
+        d = kNone;
+      }
+    }
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    const uint32_t rank_in = __popc(peers & ((1u << lane) - 1u));
+    for (int k = tid; k < 32 * 64; k += 1024) wcnt[k >> 6][k & 63] = 0;
+    __syncthreads();
+    if (d != kNone && rank_in == 0) wcnt[warp][d] = __popc(peers);
+    __syncthreads();
+    if (d != kNone) {
+      uint32_t pos = base[d] + rank_in;
+      for (int w = 0; w < warp; w++) pos += wcnt[w][d];
+      if (pos < (uint32_t)cap) {
+        slot[i] = d * cap + pos;
+        send_ids[d * cap + pos] = topk[i] - d * (uint32_t)per_rank;
+      } else {
+        slot[i] = kNone;
+        set_status(status, E4B_ST_BADINDEX);    // capacity exceeded
+      }
+    }
+    __syncthreads();
+    if (tid < nranks) {
+      uint32_t add = 0;
+      for (int w = 0; w < 32; w++) add += wcnt[w][tid];
+      base[tid] += add;
+    }
+    __syncthreads();
+  }
+  // copy the rows: warp per entry, 16-byte pieces
+  for (int i = warp; i < n; i += 32) {
+    const uint32_t sl = slot[i];
+    if (sl == kNone) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(i / K) * H);
+    uint4* dst = reinterpret_cast<uint4*>(send_x + (size_t)sl * H);
+    for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
+  }
+}
+
+// send_y[i] = y[inv[i]] for every received row i that holds an entry.
+__global__ void k_ep_return(const uint32_t* __restrict__ ids, const uint32_t* __restrict__ inv,
+                            const float* __restrict__ y, int rows, int H, float* __restrict__ send_y) {
+  pdl_wait();
+  const int i = blockIdx.x;
+  if (i >= rows || ids[i] == kNone) return;
+  const float4* src = reinterpret_cast<const float4*>(y + (size_t)inv[i] * H);
+  float4* dst = reinterpret_cast<float4*>(send_y + (size_t)i * H);
+  for (int j = threadIdx.x; j < H / 4; j += blockDim.x) dst[j] = src[j];
+}
+
+}  // namespace
+
+namespace e4b {
+void nccl_release(e4b_ctx* c) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (size_t i = 0; i < g_comms.size(); i++)
+    if (g_comms[i].first == c) {
+      if (g_comms[i].second.comm && nccl()) nccl()->commDestroy(g_comms[i].second.comm);
+      g_comms.erase(g_comms.begin() + i);
+      return;
+    }
+}
+}  // namespace e4b
+
+extern "C" {
+
+E4B_API int e4b_nccl_unique_id(uint8_t* out) {
+  if (!out) return E4B_EINVAL;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Nccl* n = nccl();
+  if (!n) return E4B_ENCCL;
+  ncclUniqueId id;
+  if (n->getUniqueId(&id) != ncclSuccess) return E4B_ENCCL;
+  static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+  memcpy(out, &id, sizeof(id));
+  return E4B_OK;
+}
+
+E4B_API int e4b_nccl_init(e4b_ctx* c, int nranks, int rank, const uint8_t* id) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, id && nranks > 0 && nranks <= 64 && rank >= 0 && rank < nranks, "nccl_init: bad args");
+  e4b::nccl_release(c);
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  E4B_CUDA(c, cudaSetDevice(c->device));
+  Nccl* n;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    n = nccl();
+  }
+  E4B_REQUIRE(c, n, "nccl_init: cannot open NCCL (%s)", getenv("E4B_NCCL_LIB") ? getenv("E4B_NCCL_LIB") : "libnccl.so.2");
+  // collective over the ranks: not under the lock (ranks may share a process)
+  ncclComm_t comm;
+  ncclResult_t r = n->commInitRank(&comm, nranks, uid, rank);
+  E4B_REQUIRE(c, r == ncclSuccess, "ncclCommInitRank: %s", n->errorString(r));
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_comms.push_back({c, NcclState{comm, nranks, rank}});
+  return E4B_OK;
+}
+
+E4B_API int e4b_nccl_destroy(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  e4b::nccl_release(c);
+  return E4B_OK;
+}
+
+E4B_API int e4b_ep_dispatch(e4b_ctx* c, const uint32_t* topk, int n_tok, int K, int E, int nranks, int cap,
+                            const uint16_t* x, int H, uint16_t* send_x, uint32_t* send_ids, uint32_t* slot) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, topk && x && send_x && send_ids && slot && n_tok > 0 && K > 0 && cap > 0,
+              "ep_dispatch: bad args");
+  E4B_REQUIRE(c, nranks > 0 && nranks <= 64 && E % nranks == 0, "ep_dispatch: E=%d over %d ranks", E, nranks);
+  E4B_REQUIRE(c, H % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(send_x) % 16 == 0,
+              "ep_dispatch: rows must be 16-byte aligned");
+  return e4b_launch(c, "ep_dispatch", k_ep_dispatch, dim3(1), dim3(1024), 0, topk, n_tok * K, E / nranks, nranks, cap,
+                    x, K, H, send_x, send_ids, slot, c->status);
+}
+
+E4B_API int e4b_ep_exchange(e4b_ctx* c, const void* send, void* recv, size_t bytes_per_peer) {
+  E4B_CHECK_CTX(c);
+  NcclState* st;
+  Nccl* n;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    st = state_of(c);
+    n = nccl();
+  }
+  E4B_REQUIRE(c, st && st->comm && n, "ep_exchange: no NCCL communicator (e4b_nccl_init)");
+  E4B_REQUIRE(c, send && recv && bytes_per_peer > 0, "ep_exchange: bad args");
+  ncclResult_t r = n->groupStart();
+  for (int p = 0; p < st->nranks && r == ncclSuccess; p++) {
+    r = n->send(static_cast<const uint8_t*>(send) + p * bytes_per_peer, bytes_per_peer, ncclUint8, p, st->comm,
+                c->stream);
+    if (r == ncclSuccess)
+      r = n->recv(static_cast<uint8_t*>(recv) + p * bytes_per_peer, bytes_per_peer, ncclUint8, p, st->comm,
+                  c->stream);
+  }
+  const ncclResult_t r2 = n->groupEnd();
+  E4B_REQUIRE(c, r == ncclSuccess && r2 == ncclSuccess, "ep_exchange: %s",
+              n->errorString(r != ncclSuccess ? r : r2));
+  return E4B_OK;
+}
+
+E4B_API int e4b_ep_return(e4b_ctx* c, const uint32_t* recv_ids, const uint32_t* inv, const float* y, int rows, int H,
+                          float* send_y) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, recv_ids && inv && y && send_y && rows > 0 && H % 4 == 0, "ep_return: bad args");
+  return e4b_launch(c, "ep_return", k_ep_return, dim3(rows), dim3(256), 0, recv_ids, inv, y, rows, H, send_y);
+}
+
+}  // extern "C"

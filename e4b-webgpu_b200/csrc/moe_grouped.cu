@@ -41,7 +41,8 @@ __global__ void k_expgroup(const uint32_t* __restrict__ topk, int n, int E, uint
     cnt[E] = s;
   }
   __syncthreads();
-  if (threadIdx.x == 0 && cnt[E] != (uint32_t)n) set_status(status, E4B_ST_BADINDEX);   // expert id out of range
+  for (int i = threadIdx.x; i < n; i += blockDim.x)   // expert id out of range (0xffffffff: an empty slot)
+    if (topk[i] >= (uint32_t)E && topk[i] != 0xffffffffu) set_status(status, E4B_ST_BADINDEX);
   for (int e = warp; e < E; e += nw) {
     uint32_t base = cnt[e];
     for (int i0 = 0; i0 < n; i0 += 32) {
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(1024) k_expsort(const uint32_t* __restrict__ t
   for (int i = tid; i < n; i += 1024) {
     const uint32_t e = topk[i];
     if (e < (uint32_t)E) atomicAdd(&base[e], 1u);
-    else bad = true;
+    else if (e != 0xffffffffu) bad = true;        // 0xffffffff: an empty slot, skipped
   }
   if (bad) set_status(status, E4B_ST_BADINDEX);
   __syncthreads();

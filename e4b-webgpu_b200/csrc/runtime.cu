@@ -42,6 +42,7 @@ E4B_API int e4b_destroy(e4b_ctx* c) {
   for (auto& g : c->plans)
     if (g) cudaGraphExecDestroy(g);
   e4b::dense_plans_release(c);
+  e4b::nccl_release(c);
   for (auto& e : c->ev) cudaEventDestroy(e);
   cudaFree(c->status);
   cudaStreamDestroy(c->stream);

@@ -36,7 +36,8 @@ _RUNTIME = {"e4b_create", "e4b_destroy", "e4b_device_info", "e4b_alloc", "e4b_fr
             "e4b_copy", "e4b_sync", "e4b_event_record", "e4b_event_elapsed", "e4b_set_pdl", "e4b_device_status",
             "e4b_plan_begin", "e4b_plan_end", "e4b_plan_launch", "e4b_plan_destroy", "e4b_set_workspace",
             "e4b_set_option", "e4b_dense_plan_create", "e4b_dense_plan_destroy",
-            "e4b_dense_plan_trace", "e4b_dense_plan_phases"}
+            "e4b_dense_plan_trace", "e4b_dense_plan_phases", "e4b_nccl_init", "e4b_nccl_destroy",
+            "e4b_ep_exchange"}
 
 
 def _ptr(x):

@@ -171,7 +171,8 @@ E4B_API int e4b_q40moedown(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, co
 /* ---- grouped MoE for batched decode (kernels/expgroup.wgsl, q40gugrp.wgsl,
  * q40downgrp.wgsl, wacc.wgsl).  Entries are (token, slot) pairs e = token*K + slot.
  * expgroup: sort the n_tok*K entries of topk[n_tok][K] by expert (stable):
- *   offsets[E+1], entries[pos] = e, inv[e] = pos.
+ *   offsets[E+1], entries[pos] = e, inv[e] = pos; an id of 0xffffffff is an
+ *   empty slot and is left out (its inv is not written).
  * q40gugrp: per entry at sorted position pos, yh[pos][FF] = f16(gelu(gate)*up)
  *   with expert rows [gate FF | up FF] of w[E][2FF][IN] and x = x[token][IN];
  *   IN % 256 == 0, FF % 32 == 0.
@@ -196,6 +197,29 @@ E4B_API int e4b_wacc(e4b_ctx* ctx, const float* y, const uint32_t* inv, const fl
                      int K, int OUT);
 /* kernels/moecomb.wgsl:6-15: y[i] = sum_k topkW[k] * slots[k*H+i]. */
 E4B_API int e4b_moecomb(e4b_ctx* ctx, const float* slots, const float* topk_w, float* y, int H, int K);
+
+/* ------------------------------------------------------- expert parallelism
+ * Experts in contiguous blocks of E/nranks per rank; every rank decodes its own
+ * sequences.  nccl_unique_id on one rank, shared by the caller (any transport),
+ * then nccl_init on every rank (one communicator per context).
+ * ep_dispatch: entry i = t*K+k of topk[n_tok][K] goes to rank e/(E/nranks):
+ *   send_x[rank][pos] = x[t] (H halves), send_ids[rank][pos] = e - rank*E/nranks,
+ *   slot[i] = rank*cap + pos, pos in entry order; unused rows get id 0xffffffff.
+ *   cap entries per peer (n_tok*K is always enough); overflow sets the status word.
+ * ep_exchange: grouped ncclSend/ncclRecv of bytes_per_peer with every rank
+ *   (recv block p = what rank p sent here).
+ * ep_return: send_y[i] = y[inv[i]] for the rows i < rows whose id is not
+ *   0xffffffff (y rows of H floats, inv from expgroup over the received ids).
+ * After the results come back, e4b_a4btail_wacc(y = received rows, inv = slot)
+ * combines in slot order. */
+E4B_API int e4b_nccl_unique_id(uint8_t* out128);
+E4B_API int e4b_nccl_init(e4b_ctx* ctx, int nranks, int rank, const uint8_t* id128);
+E4B_API int e4b_nccl_destroy(e4b_ctx* ctx);
+E4B_API int e4b_ep_dispatch(e4b_ctx* ctx, const uint32_t* topk, int n_tok, int K, int E, int nranks, int cap,
+                            const uint16_t* x, int H, uint16_t* send_x, uint32_t* send_ids, uint32_t* slot);
+E4B_API int e4b_ep_exchange(e4b_ctx* ctx, const void* send, void* recv, size_t bytes_per_peer);
+E4B_API int e4b_ep_return(e4b_ctx* ctx, const uint32_t* recv_ids, const uint32_t* inv, const float* y, int rows,
+                          int H, float* send_y);
 
 /* ------------------------------------------------------------ router */
 /* kernels/routertop.wgsl:19-71: scores = Wr[E][H] . x (f32), softmax, K-way
