@@ -80,6 +80,13 @@ class Dist:
         self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
         return float(t.item())
 
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        if self.world == 1:
+            return b
+        obj = [b]
+        self.td.broadcast_object_list(obj, src=0)
+        return obj[0]
+
     def close(self):
         if self.world > 1:
             self.td.destroy_process_group()
@@ -169,49 +176,109 @@ def bench_config(e4b, args):
     return cfg
 
 
-def moe_step_bytes(cfg, B: int, ctx_len: int) -> dict:
+def moe_metric(B: int, world: int) -> str:
+    return f"MoE decode tok/s bs{B} A4B-shaped (batched, grouped experts" + (", expert parallel)" if world > 1 else ")")
+
+
+def expected_unique_experts(E: int, K: int, B: int, zipf: float | None, trials: int = 200) -> float:
+    """Expected distinct experts one step's B x K routing touches: uniform
+    top-K without replacement, or the Zipf(s) benchmark routing (simulated)."""
+    if not zipf:
+        return E * (1.0 - (1.0 - K / E) ** B)
+    rng = np.random.default_rng(0)
+    p = np.arange(1, E + 1, dtype=np.float64) ** (-zipf)
+    p /= p.sum()
+    tot = 0
+    for _ in range(trials):
+        seen = set()
+        for _ in range(B):
+            seen.update(rng.choice(E, K, replace=False, p=p).tolist())
+        tot += len(seen)
+    return tot / trials
+
+
+def moe_step_bytes(cfg, B: int, ctx_len: int, zipf: float | None = None) -> dict:
     """Algorithmic HBM bytes of one batched MoE decode step (B tokens): every dense
     / attention / router weight once, the experts the step touches (expected
-    unique experts of B tokens x top-K without replacement: E (1 - (1 - K/E)^B)),
+    distinct experts of B tokens x top-K: E (1 - (1 - K/E)^B) for uniform
+    routing, simulated for the Zipf benchmark routing),
     the q6_K LM head, the B embedding rows and every sequence's KV over its
     attended positions plus the new K/V."""
     H, L, E, K = cfg.hidden, cfg.layers, cfg.experts, cfg.topk
     q4 = lambda rows, n_in: rows * n_in // 32 * 18
-    uniq = E * (1.0 - (1.0 - K / E) ** B)
+    uniq = expected_unique_experts(E, K, B, zipf)
     expert = q4(2 * cfg.expert_ff, H) + q4(H, cfg.expert_ff)
     w = 0
+    ew = 0
     for l in range(L):
         w += q4(cfg.qkv_rows(l), H) + q4(H, cfg.q_dim) + q4(2 * cfg.ff, H) + q4(H, cfg.ff) + E * H * 4
-        w += int(uniq * expert)
+        ew += int(uniq * expert)
+    w += ew
     head = cfg.vocab * H // 256 * 210
-    per_pos = cfg.kv_heads * cfg.head_dim * 2 * 2
     kv = 0
     for l in range(L):
-        att = min(ctx_len, cfg.window) if cfg.is_sliding(l) else ctx_len
-        kv += B * (att + 1) * per_pos
+        sliding = cfg.is_sliding(l)
+        att = min(ctx_len, cfg.window) if sliding else ctx_len
+        shared = cfg.keqv_global and not sliding          # K and V are one cache on those layers
+        kv += B * (att + 1) * cfg.kv_heads * cfg.head_dim * 2 * (1 if shared else 2)
     emb = B * (H // 256 * 210)
-    return {"weights": w, "lm_head": head, "embed": emb, "kv": kv, "unique_experts_per_layer": round(uniq, 1),
-            "total": w + head + emb + kv}
+    return {"weights": w, "expert_weights": ew, "lm_head": head, "embed": emb, "kv": kv,
+            "unique_experts_per_layer": round(uniq, 1), "total": w + head + emb + kv}
 
 
 def run_moe_batch(args, rank, world, local_rank):
     """BASELINE configs 4/5: B sequences decoded in lockstep through the grouped
-    MoE path; value = tokens of all sequences / device time."""
+    MoE path; on N > 1 GPUs expert parallelism (B/N sequences and E/N experts
+    per rank, NCCL exchange per MoE layer).  value = tokens of all sequences /
+    the slowest rank's device time."""
     import ctypes
     e4b = importlib.import_module("e4b-webgpu_b200")
     import __graft_entry__
     __graft_entry__.build()
-    dist = Dist(world, local_rank, "nccl" if world > 1 else None)
-    if world > 1:
-        raise SystemExit("--batch on more than one GPU needs expert parallelism (not in this build)")
+    dist = Dist(world, local_rank, "gloo" if world > 1 else None)
     cfg = bench_config(e4b, args)
     B = args.batch
+    if B % world:
+        raise SystemExit(f"--batch {B} does not split over {world} GPUs")
+    nloc = B // world
+    zipf = args.zipf if args.zipf > 0 else None
     t0 = time.time()
-    img = e4b.synth.build_model(cfg, seed=0)
+    if world > 1:
+        # one rank synthesises the image into a shared file, the others map it
+        import shutil
+        import tempfile
+        d = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > (48 << 30) \
+            else tempfile.gettempdir()
+        path = os.path.join(d, f"e4b_bench_{cfg.name}_seed0_{os.getenv('MASTER_PORT', '0')}.gguf")
+        if rank == 0:
+            img0 = e4b.synth.build_model(cfg, seed=0)
+            img0.tofile(path + ".part")
+            del img0
+            os.replace(path + ".part", path)       # appears whole or not at all
+        else:
+            # bounded wait for rank 0's file (the process group's own timeout stays short)
+            t_wait = time.time()
+            while not os.path.exists(path):
+                if time.time() - t_wait > 1800:
+                    raise SystemExit(f"rank {rank}: model image {path} not written within 30 min")
+                time.sleep(1.0)
+        dist.barrier()
+        img = path
+    else:
+        img = e4b.synth.build_model(cfg, seed=0)
     t_build = time.time() - t0
-    eng = e4b.BatchEngine(img, B, local_rank)
+    ep = None
+    if world > 1:
+        nid = None
+        if rank == 0:
+            probe = e4b.Device(local_rank)
+            nid = e4b.batch.nccl_unique_id(probe)
+            probe.close()
+        ep = (world, rank, dist.bcast_bytes(nid))
+    eng = e4b.BatchEngine(img, nloc, local_rank, ep=ep, zipf=zipf, tok0=rank * nloc)
     dev = eng.dev
-    prompts = np.stack([e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=1000 + b) for b in range(B)])
+    prompts = np.stack([e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=1000 + b)
+                        for b in range(rank * nloc, (rank + 1) * nloc)])
     t1 = time.time()
     eng.prefill(prompts)
     dev.sync()
@@ -224,53 +291,72 @@ def run_moe_batch(args, rank, world, local_rank):
     clocks = ClockSampler(local_rank)
     clocks.start()
     time.sleep(0.3)
+    dist.barrier()
     dev.sync()
     dev.call("e4b_event_record", 0)
     eng.decode_chunk(args.steps)
     dev.call("e4b_event_record", 1)
     dev.sync()
+    dist.barrier()
     ms = ctypes.c_float()
     dev.call("e4b_event_elapsed", 0, 1, ctypes.byref(ms))
-    t_dev = ms.value / 1000.0
+    t_dev = dist.max(ms.value / 1000.0)
     pos += args.steps
     clk = clocks.stop()
-    # end to end: per step the B tokens go host -> device and the B results come back
-    toks = eng.dev.read(eng.A.tok, np.uint32, B)
-    host = np.empty(B, np.uint32)
+    # end to end: per step this rank's tokens go host -> device and its results come back
+    toks = eng.dev.read(eng.A.tok, np.uint32, nloc)
+    host = np.empty(nloc, np.uint32)
+    dist.barrier()
     dev.sync()
     dev.call("e4b_event_record", 2)
     for i in range(args.steps):
         eng.step(toks, pos)
-        dev.call("e4b_download", host.ctypes.data_as(ctypes.c_void_p), eng.A.tok.ptr, ctypes.c_size_t(4 * B))
+        dev.call("e4b_download", host.ctypes.data_as(ctypes.c_void_p), eng.A.tok.ptr, ctypes.c_size_t(4 * nloc))
         toks = host.copy()
         pos += 1
     dev.call("e4b_event_record", 3)
     dev.sync()
+    dist.barrier()
     dev.call("e4b_event_elapsed", 2, 3, ctypes.byref(ms))
-    t_e2e = ms.value / 1000.0
+    t_e2e = dist.max(ms.value / 1000.0)
+    a2a = eng.exchange_time(pos) if world > 1 else 0.0
+    a2a = dist.max(a2a)
     status = dev.status()
     kpt = eng.kernels_per_token
     eng.close()
+    if world > 1:
+        dist.barrier()
+        if rank == 0:
+            os.unlink(img)
     if status:
         raise RuntimeError(f"device status word {status:#x} after the run")
     peak, peak_kind = peaks()
-    sb = moe_step_bytes(cfg, B, ctx_mid)
+    sb = moe_step_bytes(cfg, B, ctx_mid, zipf)
+    # per-GPU algorithmic bytes: replicated dense / attention weights and LM head,
+    # this rank's share of the expert bytes and of the KV
+    rank_bytes = sb["weights"] - sb["expert_weights"] + sb["expert_weights"] / world + sb["lm_head"] + \
+        (sb["embed"] + sb["kv"]) / world
     value = B * args.steps / t_dev
-    ach = sb["total"] * args.steps / t_dev / 1e9
+    ach = rank_bytes * args.steps / t_dev / 1e9
     out = {
-        "metric": f"MoE decode tok/s bs{B} A4B-shaped (batched, grouped experts)", "value": round(value, 2),
-        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000 * t_dev / args.steps, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_0/q6_K weights, f32 accumulate, f16 activations",
-        "data": "synthetic: seeded N(0,0.02) weights quantised to q4_0/q6_K, uniform prompt ids",
-        "config": {"workload": f"{cfg.name}: {B} sequences in lockstep after a {args.prefill}-token prefill",
-                   "model": cfg.name, "global_batch": B, "seq_len": ctx_mid, "parallelism": "single",
+        "metric": moe_metric(B, world),
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * t_dev / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "q4_0/q6_K weights, f32 accumulate, f16 activations",
+        "data": "synthetic: seeded N(0,0.02) weights quantised to q4_0/q6_K, uniform prompt ids"
+                + (f", seeded Zipf({zipf}) expert routing" if zipf else ""),
+        "config": {"workload": f"{cfg.name}: {B} sequences in lockstep after a {args.prefill}-token prefill"
+                               + (f", {nloc} per GPU, {cfg.experts // world} experts per GPU" if world > 1 else ""),
+                   "model": cfg.name, "global_batch": B, "seq_len": ctx_mid,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "routing": f"zipf{zipf}" if zipf else "router top-8",
                    "l2": "weights (%.1f GB/step) >> 126 MB L2: no flush needed" % (sb["total"] / 1e9)},
-        "e2e": {"value": round(B * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B + 32,
+        "e2e": {"value": round(B * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B + 32 * world,
                 "d2h_bytes_per_step": 4 * B},
-        "roofline": {"bound": "hbm", "kernel": "whole step (all kernels)", "achieved": round(ach, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(ach / peak, 4), "peak_source": peak_kind,
-                     "bytes_per_step": sb, "traffic": None},
+        "roofline": {"bound": "hbm", "kernel": "whole step (all kernels), per GPU", "achieved": round(ach, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_source": peak_kind,
+                     "bytes_per_step": sb, "bytes_per_gpu_step": int(rank_bytes), "traffic": None},
+        "exposed_all_to_all_us_per_step": round(a2a, 1) if world > 1 else None,
         "clocks": clk, "gpu_launches": int(kpt * args.steps), "kernels_per_step": kpt,
         "prefill_s": round(t_prefill, 1), "model_build_s": round(t_build, 1),
     }
@@ -445,11 +531,19 @@ def run_reference(args, rank, world):
     warm = min(args.warmup, 1)
     base = cpu_baseline(img, cfg, budget_s=60.0, max_steps=steps + warm)
     v = base["value"]
-    return {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
-            "ms_per_step": round(1000.0 / v, 2) if v else None, "higher_is_better": True, "scaling": "weak",
+    if args.batch > 1:
+        # the reference path decodes one token at a time; a batch of independent
+        # sequences runs at its per-token rate (the sample is sequence 0's decode)
+        metric = moe_metric(args.batch, world)
+        workload = f"{cfg.name}: {args.batch} sequences, CPU reference decoding them one token at a time"
+    else:
+        metric, workload = METRIC, f"{cfg.name}: bs1 greedy decode"
+    return {"metric": metric, "value": v, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": round(1000.0 / v, 2) if v else None, "higher_is_better": True,
+            "scaling": "strong" if args.batch > 1 else "weak",
             "vs_baseline": None, "dtype": "q4_0/q6_K weights, f32 accumulate, f16 activations",
             "data": "synthetic (same seeded model as the ours arm)", "impl": "reference",
-            "config": {"workload": f"{cfg.name}: bs1 greedy decode", "model": cfg.name},
+            "config": {"workload": workload, "model": cfg.name},
             "cpu_baseline": base,
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -606,10 +700,14 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="e4b")
-    ap.add_argument("--prefill", type=int, default=512)
+    ap.add_argument("--config", default=None,
+                    help="model config (default: e4b on 1 GPU -- BASELINE config 2; a4b on N > 1 -- config 5)")
+    ap.add_argument("--prefill", type=int, default=None, help="prompt tokens (default 512 for e4b, 1024 for a4b)")
     ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling cases)")
-    ap.add_argument("--batch", type=int, default=1, help="sequences decoded in lockstep (MoE configs)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences decoded in lockstep (default 1 on 1 GPU, 64 -- expert parallel -- on N > 1)")
+    ap.add_argument("--zipf", type=float, default=1.1,
+                    help="batched MoE: Zipf(s) expert routing of BASELINE config 5 (0 = the router's top-8)")
     ap.add_argument("--fused", type=int, default=1, help="1: fused token kernel where the model allows it; "
                                                           "0: one kernel per operator")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
@@ -622,6 +720,18 @@ def main():
     ap.add_argument("--stages", type=int, default=4)
     ap.add_argument("--variant", type=int, default=0, help="GEMV variant (warps x piece blocks): 0=8x32 1=16x16 2=16x8")
     args = ap.parse_args()
+    rank, world, local_rank = dist_env()
+    if args.config is None:
+        args.config = "e4b" if world == 1 else "a4b"
+    if args.batch is None:
+        args.batch = 64 if (world > 1 and args.config == "a4b") else 1
+    if args.prefill is None:
+        args.prefill = 1024 if args.config == "a4b" else 512
+    if world > 1:
+        # torchrun starts every worker with OMP_NUM_THREADS=1; the host-side weight
+        # synthesis (OpenMP, loaded lazily) gets its share of the cores back
+        share = rank == 0 and args.batch > 1
+        os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // (1 if share else world)))
     if args.kernel:
         run_kernel(args)
         return
@@ -630,7 +740,6 @@ def main():
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    rank, world, local_rank = dist_env()
     if args.impl == "reference":
         out = run_reference(args, rank, world)
     elif args.batch > 1:

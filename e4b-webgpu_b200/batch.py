@@ -79,13 +79,18 @@ def from_xfo(x: np.ndarray) -> np.ndarray:
 
 
 class BatchEngine(Engine):
-    def __init__(self, src, nseq: int, device=0, *, chunk: int = 64, ep=None):
+    def __init__(self, src, nseq: int, device=0, *, chunk: int = 64, ep=None, zipf: float | None = None,
+                 tok0: int = 0, route_seed: int = 1234):
         """nseq sequences decoded in lockstep on this GPU.  ep = (nranks, rank,
         nccl_id): expert parallelism -- this rank decodes its nseq sequences and
         owns experts [rank*E/nranks, (rank+1)*E/nranks); every rank of the
         communicator must build its engine with the same nccl_id (from
-        e4b_nccl_unique_id on one rank)."""
+        e4b_nccl_unique_id on one rank).  zipf = s: benchmark routing -- each
+        layer's experts are drawn from a seeded Zipf(s) popularity instead of
+        the router's top-K; tok0 = this rank's first global
+        sequence, so any rank count routes identically."""
         self.nseq = int(nseq)
+        self.zipf, self.tok0, self.route_seed = zipf, int(tok0), int(route_seed)
         self.ep = None
         if ep is not None:
             nranks, rank, nid = ep
@@ -175,21 +180,64 @@ class BatchEngine(Engine):
             L.gu_loc = ctypes.c_void_p(L.gu_exps.ptr + rank * self.e_loc * per_gu)
             L.dn_loc = ctypes.c_void_p(L.down_exps.ptr + rank * self.e_loc * per_dn)
 
-    def _moe_ep(self, L):
-        """Routed experts across the ranks (dispatch -> local experts -> return)."""
+    def _timed(self, what, *args):
+        """Queue a call; inside exchange_time() bracket it with events."""
+        d, xev = self.dev, getattr(self, "_xev", None)
+        timed = xev is not None and len(xev) < 29
+        if timed:
+            a = 4 + 2 * len(xev)
+            d.call("e4b_event_record", a)
+        d.call(what, *args)
+        if timed:
+            d.call("e4b_event_record", a + 1)
+            xev.append((a, a + 1))
+
+    def _moe_ep_send(self):
+        """Dispatch this layer's entries and start the exchange of rows + expert
+        ids (one NCCL group on the side stream)."""
         c, d, A, B = self.cfg, self.dev, self.A, self.nseq
         N = self.ep[0]
-        H, E, K, EF = c.hidden, c.experts, c.topk, c.expert_ff
-        rows = N * self.cap
+        H, E, K = c.hidden, c.experts, c.topk
         d.call("e4b_ep_dispatch", A.topk_idx, B, K, E, N, self.cap, A.moe_in, H, A.ep_sx, A.ep_sid, A.ep_slot)
-        d.call("e4b_ep_exchange", A.ep_sx, A.ep_rx, ctypes.c_size_t(self.cap * H * 2))
-        d.call("e4b_ep_exchange", A.ep_sid, A.ep_rid, ctypes.c_size_t(self.cap * 4))
+        d.call("e4b_ep_exchange2_async", A.ep_sx, A.ep_rx, ctypes.c_size_t(self.cap * H * 2), A.ep_sid, A.ep_rid,
+               ctypes.c_size_t(self.cap * 4))
+
+    def _moe_ep_finish(self, L):
+        """Wait for the rows, run this rank's experts on them, send each result
+        back to its slab slot; returns (result rows, entry -> row map)."""
+        c, d, A = self.cfg, self.dev, self.A
+        N = self.ep[0]
+        H, EF = c.hidden, c.expert_ff
+        rows = N * self.cap
+        self._timed("e4b_ep_join")
         d.call("e4b_expgroup", A.ep_rid, rows, 1, self.e_loc, A.ep_off, A.ep_ent, A.ep_inv)
         d.call("e4b_q40gugrp", A.ep_rx, L.gu_loc, A.ep_off, A.ep_ent, A.ep_gl, H, EF, self.e_loc, 1)
         d.call("e4b_q40downgrp", A.ep_gl, L.dn_loc, A.ep_off, A.ep_ent, A.ep_y, EF, H, self.e_loc)
         d.call("e4b_ep_return", A.ep_rid, A.ep_inv, A.ep_y, rows, H, A.ep_sy)
-        d.call("e4b_ep_exchange", A.ep_sy, A.ep_ry, ctypes.c_size_t(self.cap * H * 4))
+        self._timed("e4b_ep_exchange", A.ep_sy, A.ep_ry, ctypes.c_size_t(self.cap * H * 4))
         return A.ep_ry, A.ep_slot
+
+    def exchange_time(self, pos: int) -> float:
+        """Exposed exchange time (us) of one step: what the main stream waits at
+        each join for the overlapped row exchange, plus the result exchange (as
+        the stream sees them, waits for peers included); one eager step with
+        events around them for the first layers, scaled to all layers."""
+        d = self.dev
+        toks = d.read(self.A.tok, np.uint32, self.nseq)
+        self.set_step(toks, pos)
+        self._xev = []
+        try:
+            self.encode_forward()
+            d.sync()
+            ms = ctypes.c_float()
+            tot = 0.0
+            for a, b in self._xev:
+                d.call("e4b_event_elapsed", a, b, ctypes.byref(ms))
+                tot += ms.value
+            n = len(self._xev)
+        finally:
+            self._xev = None
+        return 1000.0 * tot * (2 * self.cfg.layers) / max(n, 1)
 
     # ------------------------------------------------------------ one step (B tokens)
     def encode_forward(self):
@@ -211,6 +259,11 @@ class BatchEngine(Engine):
             d.call("e4b_rmsacc3", A.tmp, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
                    A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B, 1)
             d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
+            if self.zipf:
+                d.call("e4b_route_zipf", A.params, A.topk_idx, A.topk_w, B, K, E, ctypes.c_float(self.zipf),
+                       ctypes.c_uint32(self.route_seed), L.i, self.tok0)
+            if self.ep is not None:
+                self._moe_ep_send()           # the rows travel while the dense FFN runs
             d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
             d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
             if self.ep is None:
@@ -219,7 +272,7 @@ class BatchEngine(Engine):
                 d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
                 y_rows, y_map = A.yo, A.inv
             else:
-                y_rows, y_map = self._moe_ep(L)
+                y_rows, y_map = self._moe_ep_finish(L)
             d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, y_rows, y_map, A.topk_w, K, L.post_ffw2, L.post_ffw,
                    A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
                    ctypes.c_float(L.scale), int(nxt is not None), B, 1)

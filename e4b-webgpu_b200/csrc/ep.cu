@@ -63,6 +63,8 @@ constexpr uint32_t kNone = 0xffffffffu;
 struct NcclState {
   ncclComm_t comm = nullptr;
   int nranks = 0, rank = 0;
+  cudaStream_t side = nullptr;          // exchanges that overlap the main stream's work
+  cudaEvent_t fork = nullptr, done = nullptr;
 };
 std::mutex g_mu;
 std::vector<std::pair<e4b_ctx*, NcclState>> g_comms;
@@ -153,7 +155,12 @@ void nccl_release(e4b_ctx* c) {
   std::lock_guard<std::mutex> lk(g_mu);
   for (size_t i = 0; i < g_comms.size(); i++)
     if (g_comms[i].first == c) {
-      if (g_comms[i].second.comm && nccl()) nccl()->commDestroy(g_comms[i].second.comm);
+      NcclState& st = g_comms[i].second;
+      if (st.side) cudaStreamSynchronize(st.side);
+      if (st.comm && nccl()) nccl()->commDestroy(st.comm);
+      if (st.fork) cudaEventDestroy(st.fork);
+      if (st.done) cudaEventDestroy(st.done);
+      if (st.side) cudaStreamDestroy(st.side);
       g_comms.erase(g_comms.begin() + i);
       return;
     }
@@ -191,8 +198,15 @@ E4B_API int e4b_nccl_init(e4b_ctx* c, int nranks, int rank, const uint8_t* id) {
   ncclComm_t comm;
   ncclResult_t r = n->commInitRank(&comm, nranks, uid, rank);
   E4B_REQUIRE(c, r == ncclSuccess, "ncclCommInitRank: %s", n->errorString(r));
+  NcclState st{comm, nranks, rank};
+  if (cudaStreamCreateWithFlags(&st.side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&st.fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&st.done, cudaEventDisableTiming) != cudaSuccess) {
+    n->commDestroy(comm);
+    return e4b_fail(c, E4B_ECUDA, "nccl_init: side stream / events");
+  }
   std::lock_guard<std::mutex> lk(g_mu);
-  g_comms.push_back({c, NcclState{comm, nranks, rank}});
+  g_comms.push_back({c, st});
   return E4B_OK;
 }
 
@@ -214,28 +228,65 @@ E4B_API int e4b_ep_dispatch(e4b_ctx* c, const uint32_t* topk, int n_tok, int K, 
                     x, K, H, send_x, send_ids, slot, c->status);
 }
 
+namespace {
+// One NCCL group: every buffer pair (send_i, recv_i, bytes_i per peer) with every rank.
+int exchange(e4b_ctx* c, NcclState* st, Nccl* n, cudaStream_t stream, int nbuf, const void* const* send,
+             void* const* recv, const size_t* bytes) {
+  ncclResult_t r = n->groupStart();
+  for (int b = 0; b < nbuf && r == ncclSuccess; b++)
+    for (int p = 0; p < st->nranks && r == ncclSuccess; p++) {
+      r = n->send(static_cast<const uint8_t*>(send[b]) + p * bytes[b], bytes[b], ncclUint8, p, st->comm, stream);
+      if (r == ncclSuccess)
+        r = n->recv(static_cast<uint8_t*>(recv[b]) + p * bytes[b], bytes[b], ncclUint8, p, st->comm, stream);
+    }
+  const ncclResult_t r2 = n->groupEnd();
+  E4B_REQUIRE(c, r == ncclSuccess && r2 == ncclSuccess, "ep_exchange: %s",
+              n->errorString(r != ncclSuccess ? r : r2));
+  return E4B_OK;
+}
+int comm_of(e4b_ctx* c, NcclState** st, Nccl** n) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    *st = state_of(c);
+    *n = nccl();
+  }
+  E4B_REQUIRE(c, *st && (*st)->comm && *n, "ep_exchange: no NCCL communicator (e4b_nccl_init)");
+  return E4B_OK;
+}
+}  // namespace
+
 E4B_API int e4b_ep_exchange(e4b_ctx* c, const void* send, void* recv, size_t bytes_per_peer) {
   E4B_CHECK_CTX(c);
   NcclState* st;
   Nccl* n;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    st = state_of(c);
-    n = nccl();
-  }
-  E4B_REQUIRE(c, st && st->comm && n, "ep_exchange: no NCCL communicator (e4b_nccl_init)");
+  if (int r = comm_of(c, &st, &n)) return r;
   E4B_REQUIRE(c, send && recv && bytes_per_peer > 0, "ep_exchange: bad args");
-  ncclResult_t r = n->groupStart();
-  for (int p = 0; p < st->nranks && r == ncclSuccess; p++) {
-    r = n->send(static_cast<const uint8_t*>(send) + p * bytes_per_peer, bytes_per_peer, ncclUint8, p, st->comm,
-                c->stream);
-    if (r == ncclSuccess)
-      r = n->recv(static_cast<uint8_t*>(recv) + p * bytes_per_peer, bytes_per_peer, ncclUint8, p, st->comm,
-                  c->stream);
-  }
-  const ncclResult_t r2 = n->groupEnd();
-  E4B_REQUIRE(c, r == ncclSuccess && r2 == ncclSuccess, "ep_exchange: %s",
-              n->errorString(r != ncclSuccess ? r : r2));
+  return exchange(c, st, n, c->stream, 1, &send, &recv, &bytes_per_peer);
+}
+
+E4B_API int e4b_ep_exchange2_async(e4b_ctx* c, const void* send_a, void* recv_a, size_t bytes_a, const void* send_b,
+                                   void* recv_b, size_t bytes_b) {
+  E4B_CHECK_CTX(c);
+  NcclState* st;
+  Nccl* n;
+  if (int r = comm_of(c, &st, &n)) return r;
+  E4B_REQUIRE(c, send_a && recv_a && bytes_a > 0 && send_b && recv_b && bytes_b > 0, "ep_exchange2_async: bad args");
+  E4B_CUDA(c, cudaEventRecord(st->fork, c->stream));
+  E4B_CUDA(c, cudaStreamWaitEvent(st->side, st->fork, 0));
+  const void* send[2] = {send_a, send_b};
+  void* recv[2] = {recv_a, recv_b};
+  const size_t bytes[2] = {bytes_a, bytes_b};
+  if (int r = exchange(c, st, n, st->side, 2, send, recv, bytes)) return r;
+  E4B_CUDA(c, cudaEventRecord(st->done, st->side));
+  return E4B_OK;
+}
+
+E4B_API int e4b_ep_join(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  NcclState* st;
+  Nccl* n;
+  if (int r = comm_of(c, &st, &n)) return r;
+  E4B_CUDA(c, cudaStreamWaitEvent(c->stream, st->done, 0));
   return E4B_OK;
 }
 

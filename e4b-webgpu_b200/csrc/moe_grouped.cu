@@ -271,7 +271,9 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
     if (warp == 0) mbar_init(&xbar, 1);
     fence_barrier_init();
   }
-  pdl_wait();
+  // a dense batch's chunk list needs no device data: its first weight quanta
+  // are requested before the wait on the previous kernel
+  if (p.offsets) pdl_wait();
   if (warp == 0) {
     const int n = build_chunks<TOKC>(p, chunks, lane);
     if (lane == 0) s_nch = n;
@@ -308,6 +310,7 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
 #pragma unroll
   for (int s = 0; s < S; s++)
     if (pit < i1) issue(s);
+  if (!p.offsets) pdl_wait();        // before the activations (produced by the previous kernel) are read
 
   Lane L;
   L.o_odd = 2 + 4 * t;

@@ -136,6 +136,74 @@ __global__ void __launch_bounds__(256) k_router_topk(const float* __restrict__ p
   softmax_topk(p, E, K, pes, topk_idx + (size_t)b * K, topk_w + (size_t)b * K);
 }
 
+// Skewed routing for the expert-parallel benchmark (a seeded
+// Zipf(s) load over the experts): token i (global index tok0 + i) at position
+// params[0] of layer `salt` draws K distinct experts by inverse-CDF sampling of
+// Zipf(s) over popularity ranks, mapped to expert ids by a seeded permutation,
+// each with weight 1/K.  A counter-based hash makes the draw a pure function of
+// (seed, salt, position, token), so every rank count routes the same way.
+E4B_DEV uint32_t mix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+__global__ void k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __restrict__ topk_idx,
+                             float* __restrict__ topk_w, int n_tok, int K, int E, float s, uint32_t seed, int salt,
+                             int tok0) {
+  pdl_wait();
+  extern __shared__ float cdf[];          // [E] cumulative popularity, then [E] rank -> expert (as bits)
+  uint32_t* perm = reinterpret_cast<uint32_t*>(cdf + E);
+  if (threadIdx.x == 0) {
+    float acc = 0.f;
+    for (int r = 0; r < E; r++) {
+      acc += powf((float)(r + 1), -s);
+      cdf[r] = acc;
+      perm[r] = (uint32_t)r;
+    }
+    for (int r = 0; r < E; r++) cdf[r] /= acc;
+    for (int r = E - 1; r > 0; r--) {     // seeded Fisher-Yates: which experts are popular
+      const uint32_t j = mix32(seed ^ (0x9e3779b9u * (uint32_t)r)) % (uint32_t)(r + 1);
+      const uint32_t t = perm[r];
+      perm[r] = perm[j];
+      perm[j] = t;
+    }
+  }
+  __syncthreads();
+  const uint32_t pos = params[0];
+  for (int i = threadIdx.x; i < n_tok; i += blockDim.x) {
+    uint32_t chosen[32];
+    int got = 0;
+    for (uint32_t attempt = 0; got < K && attempt < 4096u; attempt++) {
+      const uint32_t h = mix32(seed ^ mix32((uint32_t)salt * 0x85ebca6bu ^ mix32(pos ^ mix32((uint32_t)(tok0 + i) ^
+                                                                                              (attempt << 20)))));
+      const float u = (float)(h >> 8) * (1.0f / 16777216.0f);
+      int lo = 0, hi = E - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (cdf[mid] > u) hi = mid;
+        else lo = mid + 1;
+      }
+      const uint32_t e = perm[lo];
+      bool dup = false;
+      for (int k = 0; k < got; k++) dup |= chosen[k] == e;
+      if (!dup) chosen[got++] = e;
+    }
+    for (int r = 0; got < K && r < E; r++) {   // (never needed in practice) fill by popularity
+      const uint32_t e = perm[r];
+      bool dup = false;
+      for (int k = 0; k < got; k++) dup |= chosen[k] == e;
+      if (!dup) chosen[got++] = e;
+    }
+    for (int k = 0; k < K; k++) {
+      topk_idx[(size_t)i * K + k] = chosen[k];
+      topk_w[(size_t)i * K + k] = 1.0f / (float)K;
+    }
+  }
+}
+
 // kernels/router.wgsl: scale-less RMS of h, x H^-0.5 x scale, then scores + top-K.
 __global__ void __launch_bounds__(256) k_router(const float* __restrict__ h, const float* __restrict__ scale,
                                                 const float* __restrict__ wr, const float* __restrict__ pes,
@@ -277,6 +345,15 @@ E4B_API int e4b_routertop(e4b_ctx* c, const float* x, const float* wr, const flo
   }
   return e4b_launch(c, "routertop", k_routertop, dim3(batch), dim3(256), (size_t)E * 4, x, wr, pes, topk_idx, topk_w,
                     H, E, K);
+}
+
+E4B_API int e4b_route_zipf(e4b_ctx* c, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int n_tok, int K,
+                           int E, float s, uint32_t seed, int salt, int tok0) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, params && topk_idx && topk_w && n_tok > 0 && K > 0 && K <= 32 && K <= E && E <= 4096 && s > 0.f,
+              "route_zipf: bad args");
+  return e4b_launch(c, "route_zipf", k_route_zipf, dim3(1), dim3(256), (size_t)E * 8, params, topk_idx, topk_w, n_tok,
+                    K, E, s, seed, salt, tok0);
 }
 
 E4B_API int e4b_router(e4b_ctx* c, const float* h, const float* scale, const float* wr, const float* pes,

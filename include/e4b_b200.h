@@ -218,6 +218,12 @@ E4B_API int e4b_nccl_destroy(e4b_ctx* ctx);
 E4B_API int e4b_ep_dispatch(e4b_ctx* ctx, const uint32_t* topk, int n_tok, int K, int E, int nranks, int cap,
                             const uint16_t* x, int H, uint16_t* send_x, uint32_t* send_ids, uint32_t* slot);
 E4B_API int e4b_ep_exchange(e4b_ctx* ctx, const void* send, void* recv, size_t bytes_per_peer);
+/* Two exchanges in one NCCL group on the communicator's side stream, after the
+ * work queued so far; e4b_ep_join makes later work wait for them (work queued
+ * in between overlaps the transfer). */
+E4B_API int e4b_ep_exchange2_async(e4b_ctx* ctx, const void* send_a, void* recv_a, size_t bytes_a,
+                                   const void* send_b, void* recv_b, size_t bytes_b);
+E4B_API int e4b_ep_join(e4b_ctx* ctx);
 E4B_API int e4b_ep_return(e4b_ctx* ctx, const uint32_t* recv_ids, const uint32_t* inv, const float* y, int rows,
                           int H, float* send_y);
 
@@ -229,6 +235,12 @@ E4B_API int e4b_ep_return(e4b_ctx* ctx, const uint32_t* recv_ids, const uint32_t
  * launches). */
 E4B_API int e4b_routertop(e4b_ctx* ctx, const float* x, const float* wr, const float* pes, uint32_t* topk_idx,
                           float* topk_w, int H, int E, int K, int batch);
+/* Benchmark routing (not a reference kernel): replaces the
+ * router's choice for n_tok tokens with K distinct experts drawn from a seeded
+ * Zipf(s) popularity over the E experts (weights 1/K); a pure function of
+ * (seed, salt, position params[0], token tok0 + i). */
+E4B_API int e4b_route_zipf(e4b_ctx* ctx, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int n_tok,
+                           int K, int E, float s, uint32_t seed, int salt, int tok0);
 /* kernels/router.wgsl:16-63: scale-less RMS of h, x scale x H^-0.5, then as routertop. */
 E4B_API int e4b_router(e4b_ctx* ctx, const float* h, const float* scale, const float* wr, const float* pes,
                        uint32_t* topk_idx, float* topk_w, int H, int E, int K, float eps);

@@ -33,8 +33,8 @@ def test_ep_dispatch_matches_oracle(e4b, dev):
                 assert np.array_equal(gx[d, p], x[src[d, p] // K])
 
 
-def _run_batch(e4b, buf, prompts, n_new, device, ep=None):
-    eng = e4b.BatchEngine(buf, prompts.shape[0], device, ep=ep)
+def _run_batch(e4b, buf, prompts, n_new, device, ep=None, zipf=None, tok0=0):
+    eng = e4b.BatchEngine(buf, prompts.shape[0], device, ep=ep, zipf=zipf, tok0=tok0)
     try:
         ids = eng.generate(prompts, n_new)
         h = eng.read_hidden()
@@ -89,7 +89,7 @@ def _ep_rank(rank, N, port, B, P, n_new, q):
             obj[0] = e4b.batch.nccl_unique_id(dev)
             dev.close()
         dist.broadcast_object_list(obj, src=0)
-        ids, h = _run_batch(e4b, buf, mine, n_new, rank, ep=(N, rank, obj[0]))
+        ids, h = _run_batch(e4b, buf, mine, n_new, rank, ep=(N, rank, obj[0]), zipf=1.1, tok0=rank * (B // N))
         q.put((rank, ids, h))
         dist.barrier()
     finally:
@@ -105,7 +105,7 @@ def test_ep_two_ranks_match_single_gpu(e4b, models):
     cfg = e4b.config.get("tiny_moe")
     B, P, n_new, N = 6, 6, 5, 2
     prompts = np.stack([e4b.synth.prompt_ids(P, cfg.vocab, seed=300 + b) for b in range(B)])
-    ids0, h0 = _run_batch(e4b, buf, prompts, n_new, 0)
+    ids0, h0 = _run_batch(e4b, buf, prompts, n_new, 0, zipf=1.1)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -123,3 +123,24 @@ def test_ep_two_ranks_match_single_gpu(e4b, models):
     h = np.concatenate([got[r][1] for r in range(N)])
     assert np.array_equal(ids, ids0)
     assert np.array_equal(h, h0)
+
+
+def test_route_zipf(e4b, dev):
+    """Benchmark routing: K distinct experts per token, a pure function of
+    (seed, layer, position, global token), skewed towards few experts."""
+    n, K, E = 512, 8, 128
+    params = np.zeros(8, np.uint32)
+    params[0] = 77
+    bp = dev.upload(params)
+    out = []
+    for tok0, cnt in ((0, n), (100, n - 100)):
+        idx, w = dev.alloc(cnt * K * 4), dev.alloc(cnt * K * 4)
+        dev.call("e4b_route_zipf", bp.ptr, idx.ptr, w.ptr, cnt, K, E, np.float32(1.1), np.uint32(5), 3, tok0)
+        dev.sync()
+        out.append((dev.read(idx, np.uint32, cnt * K).reshape(cnt, K), dev.read(w, np.float32, cnt * K)))
+    a, wa = out[0]
+    assert all(len(set(r)) == K for r in a) and a.max() < E
+    assert np.allclose(wa, 1.0 / K)
+    assert np.array_equal(a[100:], out[1][0])            # same draw for the same global token
+    counts = np.bincount(a.reshape(-1), minlength=E)
+    assert counts.max() > 4 * counts.mean()               # skewed load
