@@ -179,6 +179,19 @@ class BatchEngine(Engine):
         for L in self.layers:
             L.gu_loc = ctypes.c_void_p(L.gu_exps.ptr + rank * self.e_loc * per_gu)
             L.dn_loc = ctypes.c_void_p(L.down_exps.ptr + rank * self.e_loc * per_dn)
+        # vocabulary-sharded LM head: this rank's V/N rows for every rank's tokens
+        V = c.vocab
+        self.v_shard = V % N == 0 and (V // N) % 8 == 0
+        if self.v_shard:
+            Bt, Vs = N * B, V // N
+            self.vs = Vs
+            A.xf_all = d.alloc(Bt * H * 4, "xfAll")
+            A.xsplit_all = d.alloc(2 * ((Bt + 7) // 8 * 8) * H * 2, "xSplitAll")
+            A.logits_s = d.alloc(Bt * Vs * 4, "logitsShard")
+            A.amax_part_s = d.alloc(Bt * ARGMAX_PARTS * 8, "amaxPartShard")
+            A.amax_s = d.alloc(Bt * 8, "amaxShard")
+            A.amax_all = d.alloc(N * Bt * 8, "amaxAll")
+            self.emb_shard = ctypes.c_void_p(self.emb.ptr + rank * Vs * (H // 256) * 210)
 
     def _timed(self, what, *args):
         """Queue a call; inside exchange_time() bracket it with events."""
@@ -277,8 +290,19 @@ class BatchEngine(Engine):
                    A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
                    ctypes.c_float(L.scale), int(nxt is not None), B, 1)
         d.call("e4b_rmsnorm", A.hidden, self.out_norm, A.xf, None, None, H, B, ctypes.c_float(c.eps), 1, 0, 0)
-        d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)
-        d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
+        if self.ep is not None and self.v_shard:
+            # every rank: its V/N LM-head rows for all ranks' tokens, then the argmax merge
+            N, rank = self.ep[0], self.ep[1]
+            Bt = N * B
+            d.call("e4b_ep_allgather", A.xf, A.xf_all, ctypes.c_size_t(B * H * 4))
+            d.call("e4b_q6k_lmhead_rows", self.emb_shard, A.xf_all, A.xsplit_all, A.logits_s, H, self.vs,
+                   ctypes.c_float(c.softcap), Bt)
+            d.call("e4b_argmax_rows", A.logits_s, A.amax_part_s, A.amax_s, self.vs, ARGMAX_PARTS, Bt)
+            d.call("e4b_ep_allgather", A.amax_s, A.amax_all, ctypes.c_size_t(Bt * 8))
+            d.call("e4b_argmax_merge", A.amax_all, N, Bt, self.vs, rank * B, B, A.amax)
+        else:
+            d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)
+            d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
         d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
 
     # ------------------------------------------------------------ host API

@@ -34,6 +34,7 @@ struct Nccl {
   ncclResult_t (*groupEnd)() = nullptr;
   ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*errorString)(ncclResult_t) = nullptr;
 };
 Nccl g_nccl;
@@ -52,7 +53,8 @@ Nccl* nccl() {
     if (h && sym(h, "ncclGetUniqueId", g_nccl.getUniqueId) && sym(h, "ncclCommInitRank", g_nccl.commInitRank) &&
         sym(h, "ncclCommDestroy", g_nccl.commDestroy) && sym(h, "ncclGroupStart", g_nccl.groupStart) &&
         sym(h, "ncclGroupEnd", g_nccl.groupEnd) && sym(h, "ncclSend", g_nccl.send) &&
-        sym(h, "ncclRecv", g_nccl.recv) && sym(h, "ncclGetErrorString", g_nccl.errorString))
+        sym(h, "ncclRecv", g_nccl.recv) && sym(h, "ncclAllGather", g_nccl.allGather) &&
+        sym(h, "ncclGetErrorString", g_nccl.errorString))
       g_nccl.h = h;
   }
   return g_nccl.h ? &g_nccl : nullptr;
@@ -134,6 +136,29 @@ __global__ void __launch_bounds__(1024) k_ep_dispatch(const uint32_t* __restrict
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(i / K) * H);
     uint4* dst = reinterpret_cast<uint4*>(send_x + (size_t)sl * H);
     for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
+  }
+}
+
+// Vocabulary-sharded LM head: rank r holds the argmax (index within its slice,
+// value) of rows [r*Vs, (r+1)*Vs) for every token; token row0 + b takes the best
+// over the ranks, ties to the lowest global index (the single-GPU argmax rule).
+__global__ void k_argmax_merge(const uint32_t* __restrict__ all, int nranks, int ntok, uint32_t vs, int row0,
+                               int nrows, uint32_t* __restrict__ out) {
+  pdl_wait();
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < nrows; b += gridDim.x * blockDim.x) {
+    float bv = -3.0e38f;
+    uint32_t bi = kNone;
+    for (int r = 0; r < nranks; r++) {
+      const uint32_t* e = all + ((size_t)r * ntok + row0 + b) * 2;
+      const float v = __uint_as_float(e[1]);
+      const uint32_t i = e[0] == kNone ? kNone : (uint32_t)r * vs + e[0];
+      if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+    out[2 * b] = bi;
+    out[2 * b + 1] = __float_as_uint(bv);
   }
 }
 
@@ -288,6 +313,26 @@ E4B_API int e4b_ep_join(e4b_ctx* c) {
   if (int r = comm_of(c, &st, &n)) return r;
   E4B_CUDA(c, cudaStreamWaitEvent(c->stream, st->done, 0));
   return E4B_OK;
+}
+
+E4B_API int e4b_ep_allgather(e4b_ctx* c, const void* send, void* recv, size_t bytes_per_rank) {
+  E4B_CHECK_CTX(c);
+  NcclState* st;
+  Nccl* n;
+  if (int r = comm_of(c, &st, &n)) return r;
+  E4B_REQUIRE(c, send && recv && bytes_per_rank > 0, "ep_allgather: bad args");
+  const ncclResult_t r = n->allGather(send, recv, bytes_per_rank, ncclUint8, st->comm, c->stream);
+  E4B_REQUIRE(c, r == ncclSuccess, "ep_allgather: %s", n->errorString(r));
+  return E4B_OK;
+}
+
+E4B_API int e4b_argmax_merge(e4b_ctx* c, const uint32_t* all, int nranks, int ntok, int slice, int row0, int nrows,
+                             uint32_t* out) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, all && out && nranks > 0 && ntok > 0 && slice > 0 && row0 >= 0 && nrows > 0 && row0 + nrows <= ntok,
+              "argmax_merge: bad args");
+  return e4b_launch(c, "argmax_merge", k_argmax_merge, dim3((nrows + 255) / 256), dim3(256), 0, all, nranks, ntok,
+                    (uint32_t)slice, row0, nrows, out);
 }
 
 E4B_API int e4b_ep_return(e4b_ctx* c, const uint32_t* recv_ids, const uint32_t* inv, const float* y, int rows, int H,

@@ -227,7 +227,7 @@ E4B_API int e4b_rmsacc3(e4b_ctx* c, const float* t, const float* w_acc, const fl
   if (rows < 1) rows = 1;
   const size_t sm = (size_t)dim * 8;
   if (int r = set_smem(c, (const void*)k_rmsacc3, sm)) return r;
-  return e4b_launch(c, "rmsacc3", k_rmsacc3, dim3(rows), dim3(512), sm, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
+  return e4b_launch(c, "rmsacc3", k_rmsacc3, dim3(rows), dim3(1024), sm, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
                     h_out, dim, eps, xfo);
 }
 
@@ -241,7 +241,7 @@ E4B_API int e4b_a4btail(e4b_ctx* c, const float* t1, const float* w1, const floa
   if (rows < 1) rows = 1;
   const size_t sm = (size_t)H * 12;
   if (int r = set_smem(c, (const void*)k_a4btail, sm)) return r;
-  return e4b_launch(c, "a4btail", k_a4btail, dim3(rows), dim3(512), sm, t1, w1, m, w2, wp, h_in, w_next, y_next,
+  return e4b_launch(c, "a4btail", k_a4btail, dim3(rows), dim3(1024), sm, t1, w1, m, w2, wp, h_in, w_next, y_next,
                     h_out, H, eps, mul, next, xfo, (const float*)nullptr, (const uint32_t*)nullptr,
                     (const float*)nullptr, 0);
 }
@@ -257,7 +257,7 @@ E4B_API int e4b_a4btail_wacc(e4b_ctx* c, const float* t1, const float* w1, const
   E4B_REQUIRE(c, !xfo || H % 32 == 0, "a4btail_wacc: fragment order needs H %% 32 == 0");
   const size_t sm = (size_t)H * 12;
   if (int r = set_smem(c, (const void*)k_a4btail, sm)) return r;
-  return e4b_launch(c, "a4btail_wacc", k_a4btail, dim3(rows), dim3(512), sm, t1, w1, (const float*)nullptr, w2, wp,
+  return e4b_launch(c, "a4btail_wacc", k_a4btail, dim3(rows), dim3(1024), sm, t1, w1, (const float*)nullptr, w2, wp,
                     h_in, w_next, y_next, h_out, H, eps, mul, next, xfo, y, inv, topk_w, K);
 }
 

@@ -128,8 +128,19 @@ __global__ void __launch_bounds__(256) k_router_topk(const float* __restrict__ p
   if (b >= B) return;
   float* p = pw + (size_t)warp * E;
   for (int e = lane; e < E; e += 32) {
+    // slices summed in order; the loads are independent and issued together
+    const float* src = part + (size_t)b * E + e;
+    const size_t step = (size_t)B * E;
     float v = 0.f;
-    for (int s = 0; s < slices; s++) v += part[((size_t)s * B + b) * E + e];
+    int s = 0;
+    for (; s + 8 <= slices; s += 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) t[u] = src[(s + u) * step];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v += t[u];
+    }
+    for (; s < slices; s++) v += src[s * step];
     p[e] = v;
   }
   __syncwarp();

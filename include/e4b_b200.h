@@ -226,6 +226,14 @@ E4B_API int e4b_ep_exchange2_async(e4b_ctx* ctx, const void* send_a, void* recv_
 E4B_API int e4b_ep_join(e4b_ctx* ctx);
 E4B_API int e4b_ep_return(e4b_ctx* ctx, const uint32_t* recv_ids, const uint32_t* inv, const float* y, int rows,
                           int H, float* send_y);
+/* Vocabulary-sharded LM head for N > 1: ep_allgather = ncclAllGather of
+ * bytes_per_rank (rank-major); argmax_merge: all[r][t] = (index within rank r's
+ * slice of `slice` rows, f32 value bits) from e4b_argmax_rows -> out[b] for
+ * tokens row0 + b = the best over ranks with global index r*slice + index, ties
+ * to the lowest global index. */
+E4B_API int e4b_ep_allgather(e4b_ctx* ctx, const void* send, void* recv, size_t bytes_per_rank);
+E4B_API int e4b_argmax_merge(e4b_ctx* ctx, const uint32_t* all, int nranks, int ntok, int slice, int row0,
+                             int nrows, uint32_t* out);
 
 /* ------------------------------------------------------------ router */
 /* kernels/routertop.wgsl:19-71: scores = Wr[E][H] . x (f32), softmax, K-way
