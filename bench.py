@@ -646,6 +646,52 @@ def run_trace(args):
     print(json.dumps(out))
 
 
+def run_attn(e4b, dev, args):
+    """BASELINE config 3 on the batched tensor-core attention (e4b_attdec_seq):
+    GQA 8q / 2kv x 256, f16 K/V N(0,1), KV 4096 / 8192 / 32768, batch 1 and 16,
+    global and sliding-window (512) masks.  Bytes = the K/V rows of the live
+    chunks; K/V > L2 for the large cases, smaller ones rotate over copies."""
+    import ctypes
+    QH, KVH, HD = 8, 2, 256
+    peak, kind_p = peaks()
+    rows = []
+    rng = np.random.default_rng(0)
+    for kv in (4096, 8192, 32768):
+        for nseq in (1, 16):
+            cache = nseq * kv * KVH * HD * 2
+            copies = max(1, int(math.ceil(256e6 / cache)))
+            q = dev.upload(rng.standard_normal((nseq, QH, HD)).astype(np.float32))
+            kvs = [(dev.upload(rng.standard_normal(cache // 2, dtype=np.float32).astype(np.float16)),
+                    dev.upload(rng.standard_normal(cache // 2, dtype=np.float32).astype(np.float16)))
+                   for _ in range(copies)]
+            maxch = kv // 64
+            po, pm = dev.alloc(nseq * QH * maxch * HD * 4), dev.alloc(nseq * QH * maxch * 8)
+            out = dev.alloc(nseq * QH * HD * 2)
+            for window in (0, 512):
+                params = np.zeros(8, np.uint32)
+                params[0], params[1], params[5] = kv - 1, kv, kv
+                bp = dev.upload(params)
+                mode = 0 if window else 2
+
+                def loop(kvs=kvs, bp=bp, mode=mode, window=window):
+                    for i in range(args.launches):
+                        kb, vb = kvs[i % len(kvs)]
+                        dev.call("e4b_attdec_seq", q, kb, vb, bp, po, pm, out, QH, KVH, HD, window, mode, 0, maxch,
+                                 ctypes.c_float(1.0 / 16), kv, nseq, 0)
+                us = graph_time(dev, loop) / args.launches
+                live = min(kv, (kv - (kv - window) // 64 * 64) if window else kv)
+                nbytes = nseq * live * KVH * HD * 2 * 2
+                rows.append({"kv": kv, "batch": nseq, "mask": f"sliding{window}" if window else "global",
+                             "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                             "frac": round(nbytes / us / 1e3 / peak, 4)})
+    st = dev.status()
+    dev.close()
+    print(json.dumps({"kernel": "attn", "desc": "e4b_attdec_seq (split-KV + combine), config 3 shapes",
+                      "peak": peak, "peak_source": kind_p, "launches": args.launches, "cases": rows, "status": st}))
+    if st:
+        raise SystemExit(f"device status {st:#x}")
+
+
 def run_kernel(args):
     """Time one streaming kernel alone: `launches` launches cycling over enough
     distinct weight copies that the working set exceeds L2."""
@@ -656,6 +702,8 @@ def run_kernel(args):
     dev = e4b.Device(0)
     if args.kernel == "rmschain":
         return run_rmschain(e4b, dev, args)
+    if args.kernel == "attn":
+        return run_attn(e4b, dev, args)
     desc, rows, n_in, kind = KERNELS[args.kernel]
     ws = int(dev.L.e4b_workspace_bytes())
     wsb = dev.alloc(ws, "workspace")
@@ -712,7 +760,7 @@ def main():
                                                           "0: one kernel per operator")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain"], help="time one kernel alone instead of the decode")
+    ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain", "attn"], help="time one kernel alone instead of the decode")
     ap.add_argument("--trace", action="store_true", help="per-phase timing of the fused token kernel")
     ap.add_argument("--launches", type=int, default=200)
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1/0)")

@@ -79,6 +79,12 @@ E4B_DEV SlotRule att_rule(const AttP& p) {
   r.len = p.cachemode == 2 ? p.params[5] : p.params[1];
   return r;
 }
+// First chunk holding a valid slot: a windowed linear cache skips the slots
+// before its window; rings and unwindowed caches start at 0.
+E4B_DEV int first_chunk(const SlotRule& r) {
+  if (r.cachemode == 0 && r.window > 0 && r.len > (uint32_t)r.window) return (int)((r.len - r.window) / kAC);
+  return 0;
+}
 
 __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __grid_constant__ CUtensorMap kmap,
                                                       const __grid_constant__ CUtensorMap vmap) {
@@ -106,11 +112,12 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
   pdl_wait();
   const SlotRule rule = att_rule(p);
   const uint32_t n = rule.nslots();
-  const int nch = (int)((n + kAC - 1) / kAC);
-  if (nch > p.max_chunks) {
+  const int nch_all = (int)((n + kAC - 1) / kAC);
+  if (nch_all > p.max_chunks) {
     if (threadIdx.x == 0) set_status(p.status, E4B_ST_BADINDEX);
     return;
   }
+  const int c_lo = first_chunk(rule), nch = nch_all - c_lo;       // live chunks [c_lo, nch_all)
   const int per_seq = p.KVH * nch, items = p.nseq * per_seq;
   // a contiguous run of items per CTA: consecutive chunks of one (sequence, KV head)
   const int i0 = (int)((long long)items * blockIdx.x / gridDim.x);
@@ -120,9 +127,9 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
   // past the cache's end read as zeros, slots past the live ones are finite
   // cache contents that only meet p = 0
   auto issue = [&](int it, int s) {
-    const int b = it / per_seq, rem = it % per_seq, kvh = rem / nch, c = rem % nch;
+    const int b = it / per_seq, rem = it % per_seq, kvh = rem / nch, c = c_lo + rem % nch;
     uint8_t* dk = kv + (size_t)s * 2 * tile;
-    const bool newq = it == i0 || c == 0;       // the q rows change with the (sequence, KV head)
+    const bool newq = it == i0 || c == c_lo;    // the q rows change with the (sequence, KV head)
     mbar_expect_tx(&full[s], (uint32_t)tile * (p.keqv ? 1u : 2u) + (newq ? (uint32_t)qbytes : 0u));
     if (newq)
       bulk_g2s(qst + (size_t)s * p.G * p.HD, p.q + ((size_t)b * p.QH + kvh * p.G) * p.HD, (uint32_t)qbytes, &full[s]);
@@ -152,10 +159,10 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
   }
   bool ok = true;
   int local = 0;
-  int b = i0 / per_seq, kvh = (i0 % per_seq) / nch, c = (i0 % per_seq) % nch;
+  int b = i0 / per_seq, kvh = (i0 % per_seq) / nch, c = c_lo + (i0 % per_seq) % nch;
   for (int it = i0; it < i1; it++, local++) {
-    if (it != i0 && ++c == nch) {
-      c = 0;
+    if (it != i0 && ++c == nch_all) {
+      c = c_lo;
       if (++kvh == p.KVH) {
         kvh = 0;
         b++;
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
     if (ok) ok = mbar_wait(&full[s], (uint32_t)((local / kAS) & 1), p.status);
     // q fragments of the group's heads: (q[k], q[k+1]) and (q[k+8], q[k+9]), k = 16 j + 2 t, hi and lo;
     // rebuilt only when the run moves to another (sequence, KV head)
-    if (it == i0 || c == 0) {
+    if (it == i0 || c == c_lo) {
       const float* qs = qst + (size_t)s * p.G * p.HD;
       for (int i = threadIdx.x; i < (p.HD / 16) * 32; i += blockDim.x) {
         const int j = i >> 5, gg = (i & 31) >> 2, tt = i & 3;
@@ -326,24 +333,43 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
 }
 
 // Phase B over the live chunks: out[h][d] = sum_c o_c e^(m_c - M) / sum_c l_c e^(m_c - M).
+// The chunk weights e^(m_c - M) are formed once per head in shared memory; the
+// sums over chunks then issue independent loads (same order and arithmetic).
 __global__ void k_attcomb_dec(const AttP p, uint16_t* __restrict__ out_h, int xfo) {
   pdl_wait();
+  extern __shared__ float wc[];            // [max_chunks]
+  __shared__ float sh[32];
   const SlotRule rule = att_rule(p);
   const int nch = min((int)((rule.nslots() + kAC - 1) / kAC), p.max_chunks);
+  const int c_lo = min(first_chunk(rule), nch);
   const int h = blockIdx.x, b = blockIdx.y;
   const size_t row = (size_t)b * p.QH + h;
   const float* ml = p.part_ml + row * p.max_chunks * 2;
-  float M = -INFINITY;
-  for (int c = 0; c < nch; c++)
-    if (ml[2 * c + 1] > 0.f) M = fmaxf(M, ml[2 * c]);
-  float den = 0.f;
-  for (int c = 0; c < nch; c++)
-    if (ml[2 * c + 1] > 0.f) den += ml[2 * c + 1] * expf(ml[2 * c] - M);
+  float m = -INFINITY;
+  for (int c = c_lo + threadIdx.x; c < nch; c += blockDim.x)
+    if (ml[2 * c + 1] > 0.f) m = fmaxf(m, ml[2 * c]);
+  const float M = block_max(m, sh);
+  for (int c = c_lo + threadIdx.x; c < nch; c += blockDim.x)
+    wc[c] = ml[2 * c + 1] > 0.f ? expf(ml[2 * c] - M) : 0.f;
+  __syncthreads();
+  float den = 0.f;                          // in chunk order, as a single thread would
+  for (int c = c_lo; c < nch; c++)
+    if (ml[2 * c + 1] > 0.f) den += ml[2 * c + 1] * wc[c];
   uint16_t* out = out_h + (size_t)b * p.QH * p.HD;
+  const float* po = p.part_o + row * p.max_chunks * p.HD;
   for (int d = threadIdx.x; d < p.HD; d += blockDim.x) {
     float acc = 0.f;
-    for (int c = 0; c < nch; c++)
-      if (ml[2 * c + 1] > 0.f) acc = fmaf(p.part_o[(row * p.max_chunks + c) * p.HD + d], expf(ml[2 * c] - M), acc);
+    int c = c_lo;
+    for (; c + 8 <= nch; c += 8) {
+      float o[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) o[u] = wc[c + u] != 0.f ? po[(size_t)(c + u) * p.HD + d] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (wc[c + u] != 0.f) acc = fmaf(o[u], wc[c + u], acc);
+    }
+    for (; c < nch; c++)
+      if (wc[c] != 0.f) acc = fmaf(po[(size_t)c * p.HD + d], wc[c], acc);
     const float v = den > 0.f ? acc / den : 0.f;
     const int i = h * p.HD + d;
     out[xfo ? xfo_pos(i) : i] = f2h(v);
@@ -389,7 +415,8 @@ E4B_API int e4b_attdec_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, c
   const long long most = (long long)nseq * KVH * max_chunks;
   const int grid = (int)(most < c->sm_count ? most : c->sm_count);
   if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW), smem, p, kmap, vmap)) return r;
-  return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(128), 0, p, out_h, xfo);
+  return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(128), (size_t)max_chunks * 4, p, out_h,
+                    xfo);
 }
 
 }  // extern "C"
