@@ -338,4 +338,8 @@ class BatchEngine(Engine):
         return self.dev.read(self.A.hidden, F32, self.nseq * self.cfg.hidden).reshape(self.nseq, -1)
 
     def read_logits(self) -> np.ndarray:
+        """Logits of the last step, [nseq][vocab] (one GPU; an expert-parallel
+        rank holds only its vocabulary slice for every rank's tokens)."""
+        if self.ep is not None and getattr(self, "v_shard", False):
+            raise RuntimeError("expert-parallel ranks keep vocabulary slices, not full logit rows")
         return self.dev.read(self.A.logits, F32, self.nseq * self.cfg.vocab).reshape(self.nseq, -1)

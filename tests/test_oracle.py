@@ -172,3 +172,29 @@ def test_oracle_decode_runs_all_graphs(models):
         ids, margins, recs = m.generate([1, 2, 3, 4], 3, record=True)
         assert len(ids) == 3 and all(0 <= t < 4096 for t in ids)
         assert np.isfinite(recs[-1]["hidden"]).all()
+
+
+def test_fragment_order_permutation():
+    """batch.xfo_perm is a permutation within every 32-element block and puts
+    MMA lane t's B-fragment values -- the k indices its q4_0 A fragment uses
+    (odd blocks 4t..4t+3, even blocks 2+4t..5+4t or {0, 1, 14, 15} for t = 3,
+    and the same + 16) -- at halves 8t..8t+7 as [j0, j2, j1, j3, +16 ...]."""
+    import importlib
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    n = 128
+    pos = e4b.batch.xfo_perm(n)
+    assert sorted(pos.tolist()) == list(range(n))
+    for b in range(n // 32):
+        assert set(pos[32 * b:32 * b + 32].tolist()) == set(range(32 * b, 32 * b + 32))
+        for t in range(4):
+            if b & 1:
+                j = [4 * t, 4 * t + 1, 4 * t + 2, 4 * t + 3]
+            elif t < 3:
+                j = [2 + 4 * t, 3 + 4 * t, 4 + 4 * t, 5 + 4 * t]
+            else:
+                j = [0, 1, 14, 15]
+            order = [j[0], j[2], j[1], j[3], j[0] + 16, j[2] + 16, j[1] + 16, j[3] + 16]
+            for slot, jj in enumerate(order):
+                assert pos[32 * b + jj] == 32 * b + 8 * t + slot
+    x = np.arange(n, dtype=np.float32)
+    assert np.array_equal(e4b.batch.from_xfo(e4b.batch.to_xfo(x)), x)
