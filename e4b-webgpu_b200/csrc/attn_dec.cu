@@ -3,8 +3,7 @@
 //
 // Work item = (sequence, KV head, chunk of 64 cache slots); only chunks that
 // hold live slots are visited, by a persistent grid.  Per item the CTA loads
-// the chunk's K and V tiles with 4-D TMA boxes (and the group's q rows with
-// one bulk copy) of [64 slots x 64 dims] (the
+// the chunk's K and V tiles with 4-D TMA boxes of [64 slots x 64 dims] (the
 // cache viewed as [nseq][slots][KVH][HD], 128-byte swizzle, so the MMA reads
 // are bank-conflict free) up to two items ahead of use, and does both products
 // on mma.sync m16n8k16 with the G query heads of the KV head as the 8 MMA
@@ -86,21 +85,29 @@ E4B_DEV int first_chunk(const SlotRule& r) {
   return 0;
 }
 
-__global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __grid_constant__ CUtensorMap kmap,
-                                                      const __grid_constant__ CUtensorMap vmap) {
+// Two groups of kAW warps per CTA take alternate items of the CTA's run (named
+// barriers per group), so one group's MMAs and softmax overlap the other's
+// waits; both draw from one kAS-deep ring of K/V stages.
+constexpr int kAG = 2;             // warp groups per CTA
+
+E4B_DEV void group_sync(int grp) { asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * kAW) : "memory"); }
+
+__global__ void __launch_bounds__(32 * kAW * kAG, 1) k_attdec(const AttP p, const __grid_constant__ CUtensorMap kmap,
+                                                              const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kAS];
-  __shared__ float red_m[kAW][8], red_l[kAW][8];
+  __shared__ float red_m[kAG][kAW][8], red_l[kAG][kAW][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tile = (p.HD / 64) * kSub;                             // bytes per K or V tile
-  const int qbytes = p.G * p.HD * 4;                               // the group's q rows (f32)
+  const int grp = warp / kAW, wg = warp % kAW;          // warp group, warp within the group
+  const int gtid = threadIdx.x - grp * 32 * kAW;        // thread within the group
+  const int tile = (p.HD / 64) * kSub;                  // bytes per K or V tile
   // swizzled boxes need 1024-byte aligned destinations
-  uint8_t* kv = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);   // [kAS stages][K tile | V tile]
-  float* qst = reinterpret_cast<float*>(kv + (size_t)kAS * 2 * tile);    // [kAS stages][G][HD]
-  uint4* qf = reinterpret_cast<uint4*>(qst + (size_t)kAS * p.G * p.HD);  // [HD/16][32 lanes]
-  uint16_t* ph = reinterpret_cast<uint16_t*>(qf + (p.HD / 16) * 32);     // [8 heads][kPP] p hi
-  uint16_t* pl = ph + 8 * kPP;                                     // p lo
-  for (int i = threadIdx.x; i < 2 * 8 * kPP; i += blockDim.x) ph[i] = 0;
+  uint8_t* kv = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);          // [kAS stages][K tile | V tile]
+  uint4* qf = reinterpret_cast<uint4*>(kv + (size_t)kAS * 2 * tile) + (size_t)grp * (p.HD / 16) * 32;
+  uint16_t* ph = reinterpret_cast<uint16_t*>(reinterpret_cast<uint4*>(kv + (size_t)kAS * 2 * tile) +
+                                             (size_t)kAG * (p.HD / 16) * 32) + (size_t)grp * 2 * 8 * kPP;
+  uint16_t* pl = ph + 8 * kPP;                          // this group's p rows: hi, lo [8 heads][kPP]
+  for (int i = gtid; i < 2 * 8 * kPP; i += 32 * kAW) ph[i] = 0;
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
     if (!p.keqv) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
@@ -123,16 +130,14 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
   const int i0 = (int)((long long)items * blockIdx.x / gridDim.x);
   const int i1 = (int)((long long)items * (blockIdx.x + 1) / gridDim.x);
 
-  // one thread issues an item's boxes: HD/64 for K (+ HD/64 for V); slots
-  // past the cache's end read as zeros, slots past the live ones are finite
-  // cache contents that only meet p = 0
-  auto issue = [&](int it, int s) {
+  // one thread issues an item's boxes into stage (item - i0) % kAS: HD/64 for
+  // K (+ HD/64 for V); slots past the cache's end read as zeros, slots past the
+  // live ones are finite cache contents that only meet p = 0
+  auto issue = [&](int it) {
+    const int s = (it - i0) % kAS;
     const int b = it / per_seq, rem = it % per_seq, kvh = rem / nch, c = c_lo + rem % nch;
     uint8_t* dk = kv + (size_t)s * 2 * tile;
-    const bool newq = it == i0 || c == c_lo;    // the q rows change with the (sequence, KV head)
-    mbar_expect_tx(&full[s], (uint32_t)tile * (p.keqv ? 1u : 2u) + (newq ? (uint32_t)qbytes : 0u));
-    if (newq)
-      bulk_g2s(qst + (size_t)s * p.G * p.HD, p.q + ((size_t)b * p.QH + kvh * p.G) * p.HD, (uint32_t)qbytes, &full[s]);
+    mbar_expect_tx(&full[s], (uint32_t)tile * (p.keqv ? 1u : 2u));
     for (int j = 0; j < p.HD / 64; j++) {
       tma_load_4d(dk + j * kSub, &kmap, 64 * j, kvh, c * kAC, b, &full[s]);
       if (!p.keqv) tma_load_4d(dk + tile + j * kSub, &vmap, 64 * j, kvh, c * kAC, b, &full[s]);
@@ -140,12 +145,12 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
   };
   if (threadIdx.x == 0)
     for (int k = 0; k < kAS; k++)
-      if (i0 + k < i1) issue(i0 + k, k);
+      if (i0 + k < i1) issue(i0 + k);
 
   // lane-constant shared-memory offsets of the swizzled tiles:
-  //   scores A: rows r0 = 16 warp + g (+8), chunk 2u (+1) of box j/4 -> xor with r0 & 7 = g
+  //   scores A: rows r0 = 16 wg + g (+8), chunk 2u (+1) of box j/4 -> xor with r0 & 7 = g
   //   P.V A (ldmatrix.trans): row 16 ks + lrow, chunk 2 (dt & 3) + hbit of box dt / 4, xor with lane & 7
-  const int r0 = 16 * warp + g;
+  const int r0 = 16 * wg + g;
   uint32_t koff[8];
 #pragma unroll
   for (int u = 0; u < 8; u++) koff[u] = (uint32_t)(r0 * 128 + ((u ^ g) << 4) + 4 * t);
@@ -154,32 +159,23 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
   uint32_t voff[4];
 #pragma unroll
   for (int u = 0; u < 4; u++) {
-    const int dt = warp * dtiles + u;
+    const int dt = wg * dtiles + u;
     voff[u] = (uint32_t)((dt >> 2) * kSub + lrow * 128 + (((2 * (dt & 3) + hbit) ^ (lane & 7)) << 4));
   }
   bool ok = true;
-  int local = 0;
-  int b = i0 / per_seq, kvh = (i0 % per_seq) / nch, c = c_lo + (i0 % per_seq) % nch;
-  for (int it = i0; it < i1; it++, local++) {
-    if (it != i0 && ++c == nch_all) {
-      c = c_lo;
-      if (++kvh == p.KVH) {
-        kvh = 0;
-        b++;
-      }
-    }
-    const int s = local % kAS;
+  int qb = -1, qk = -1;                          // (sequence, KV head) whose q fragments qf holds
+  for (int it = i0 + grp; it < i1; it += kAG) {
+    const int local = it - i0, s = local % kAS;
+    const int b = it / per_seq, rem = it % per_seq, kvh = rem / nch, c = c_lo + rem % nch;
     const uint32_t t0 = (uint32_t)c * kAC;
-    if (ok) ok = mbar_wait(&full[s], (uint32_t)((local / kAS) & 1), p.status);
     // q fragments of the group's heads: (q[k], q[k+1]) and (q[k+8], q[k+9]), k = 16 j + 2 t, hi and lo;
-    // rebuilt only when the run moves to another (sequence, KV head)
-    if (it == i0 || c == c_lo) {
-      const float* qs = qst + (size_t)s * p.G * p.HD;
-      for (int i = threadIdx.x; i < (p.HD / 16) * 32; i += blockDim.x) {
+    // rebuilt when this group moves to another (sequence, KV head)
+    if (b != qb || kvh != qk) {
+      for (int i = gtid; i < (p.HD / 16) * 32; i += 32 * kAW) {
         const int j = i >> 5, gg = (i & 31) >> 2, tt = i & 3;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (gg < p.G) {
-          const float* qr = qs + gg * p.HD + 16 * j + 2 * tt;
+          const float* qr = p.q + ((size_t)b * p.QH + kvh * p.G + gg) * p.HD + 16 * j + 2 * tt;
           const float x[4] = {qr[0], qr[1], qr[8], qr[9]};
           uint16_t h[4], l[4];
 #pragma unroll
@@ -192,8 +188,11 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
         }
         qf[i] = v;
       }
-      __syncthreads();
+      qb = b;
+      qk = kvh;
+      group_sync(grp);
     }
+    if (ok) ok = mbar_wait(&full[s], (uint32_t)((local / kAS) & 1), p.status);
     const uint8_t* Kt = kv + (size_t)s * 2 * tile;
     const uint8_t* Vt = p.keqv ? Kt : Kt + tile;
     // ---- scores of this warp's 16 slots x the group's heads
@@ -221,7 +220,7 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
       for (int r = 0; r < 4; r++) sc[r] = (sp[0][r] + sp[1][r]) + (sp[2][r] + sp[3][r]);
     }
     // sc: [0] (slot g, head 2t) [1] (slot g, head 2t+1) [2] (slot g+8, head 2t) [3] (slot g+8, head 2t+1)
-    const uint32_t sa = t0 + 16 * warp + g, sb = sa + 8;
+    const uint32_t sa = t0 + 16 * wg + g, sb = sa + 8;
     const bool va = sa < n && rule.valid(sa), vb = sb < n && rule.valid(sb);
     float s0 = va ? sc[0] * p.scale : -INFINITY, s1 = va ? sc[1] * p.scale : -INFINITY;
     float s2 = vb ? sc[2] * p.scale : -INFINITY, s3 = vb ? sc[3] * p.scale : -INFINITY;
@@ -232,15 +231,15 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
     }
     if (g == 0) {
-      red_m[warp][2 * t] = m0;
-      red_m[warp][2 * t + 1] = m1;
+      red_m[grp][wg][2 * t] = m0;
+      red_m[grp][wg][2 * t + 1] = m1;
     }
-    __syncthreads();
-    float M0 = red_m[0][2 * t], M1 = red_m[0][2 * t + 1];
+    group_sync(grp);
+    float M0 = red_m[grp][0][2 * t], M1 = red_m[grp][0][2 * t + 1];
 #pragma unroll
     for (int w = 1; w < kAW; w++) {
-      M0 = fmaxf(M0, red_m[w][2 * t]);
-      M1 = fmaxf(M1, red_m[w][2 * t + 1]);
+      M0 = fmaxf(M0, red_m[grp][w][2 * t]);
+      M1 = fmaxf(M1, red_m[grp][w][2 * t + 1]);
     }
     const float p0 = (va && M0 != -INFINITY) ? expf(s0 - M0) : 0.f;
     const float p1 = (va && M1 != -INFINITY) ? expf(s1 - M1) : 0.f;
@@ -253,12 +252,12 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
       l1 += __shfl_xor_sync(0xffffffffu, l1, o);
     }
     if (g == 0) {
-      red_l[warp][2 * t] = l0;
-      red_l[warp][2 * t + 1] = l1;
+      red_l[grp][wg][2 * t] = l0;
+      red_l[grp][wg][2 * t + 1] = l1;
     }
     // p as f16 hi + lo, [head][slot] (heads >= G keep their zeros)
     {
-      const int la = 16 * warp + g, lb = la + 8;
+      const int la = 16 * wg + g, lb = la + 8;
       const float pv[4] = {p0, p1, p2, p3};
 #pragma unroll
       for (int k = 0; k < 4; k++) {
@@ -270,7 +269,7 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
         }
       }
     }
-    __syncthreads();
+    group_sync(grp);
     // ---- O^T[d][head] for this warp's d tiles
     const size_t part_row = (size_t)b * p.QH + kvh * p.G;
     if (ok) {
@@ -294,7 +293,7 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
       }
       // acc[u]: [0] (d g, head 2t) [1] (d g, head 2t+1) [2] (d g+8, head 2t) [3] (d g+8, head 2t+1)
       const size_t hstride = (size_t)p.max_chunks * p.HD;
-      float* o0 = p.part_o + ((part_row + 2 * t) * p.max_chunks + c) * p.HD + 16 * warp * dtiles + g;
+      float* o0 = p.part_o + ((part_row + 2 * t) * p.max_chunks + c) * p.HD + 16 * wg * dtiles + g;
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         if (u >= dtiles) break;
@@ -308,12 +307,12 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
         }
       }
     }
-    if (warp == 0 && g == 0 && ok) {
+    if (wg == 0 && g == 0 && ok) {
       float L0 = 0.f, L1 = 0.f;
 #pragma unroll
       for (int w = 0; w < kAW; w++) {
-        L0 += red_l[w][2 * t];
-        L1 += red_l[w][2 * t + 1];
+        L0 += red_l[grp][w][2 * t];
+        L1 += red_l[grp][w][2 * t + 1];
       }
       if (2 * t < p.G) {
         float* ml = p.part_ml + ((part_row + 2 * t) * p.max_chunks + c) * 2;
@@ -326,9 +325,9 @@ __global__ void __launch_bounds__(32 * kAW, 1) k_attdec(const AttP p, const __gr
         ml[1] = L1;
       }
     }
-    // every warp is done with this stage, the p rows and the q fragments
-    __syncthreads();
-    if (threadIdx.x == 0 && ok && it + kAS < i1) issue(it + kAS, s);
+    // every warp of the group is done with this stage, its p rows and q fragments
+    group_sync(grp);
+    if (gtid == 0 && ok && it + kAS < i1) issue(it + kAS);
   }
 }
 
@@ -408,13 +407,13 @@ E4B_API int e4b_attdec_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, c
   E4B_REQUIRE(c, cache_map(&kmap, kcache, HD, KVH, cache_slots, nseq), "attdec_seq: K cache tensor map failed");
   if (p.keqv) vmap = kmap;
   else E4B_REQUIRE(c, cache_map(&vmap, vcache, HD, KVH, cache_slots, nseq), "attdec_seq: V cache tensor map failed");
-  const size_t smem = (size_t)kAS * 2 * (HD / 64) * kSub + (size_t)kAS * p.G * HD * 4 + (size_t)(HD / 16) * 32 * 16 +
-                      (size_t)2 * 8 * kPP * 2 + 1024;
+  const size_t smem = (size_t)kAS * 2 * (HD / 64) * kSub + (size_t)kAG * ((size_t)(HD / 16) * 32 * 16 + 2 * 8 * kPP * 2) +
+                      1024;
   cudaError_t e = cudaFuncSetAttribute(k_attdec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "attdec smem attr: %s", cudaGetErrorString(e));
   const long long most = (long long)nseq * KVH * max_chunks;
   const int grid = (int)(most < c->sm_count ? most : c->sm_count);
-  if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW), smem, p, kmap, vmap)) return r;
+  if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW * kAG), smem, p, kmap, vmap)) return r;
   return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(128), (size_t)max_chunks * 4, p, out_h,
                     xfo);
 }
