@@ -116,7 +116,18 @@ class BatchEngine(Engine):
         A.hidden = d.alloc(B * H * 4, "hidden")
         A.hidden_b = d.alloc(B * H * 4, "hiddenB")
         A.normed = d.alloc(B * H * 2, "normed")
-        A.qkv = d.alloc(B * maxrows * 4, "qkv")
+        # the dense q|k|v and o GEMMs split K over CTA groups when the batch is
+        # large enough to share each weight decode (partials summed by the consumer)
+        def kparts(n_in, rows):
+            # as many K-parts as keep (K-part x 8-tile group) items within one wave of CTAs
+            if not (8 <= B <= 64 and n_in % 256 == 0):
+                return 1
+            groups = -(-rows // 256)
+            return max(1, min(n_in // 256, d.sm_count // groups))
+        self.kp_qkv = kparts(H, maxrows)
+        self.kp_o = kparts(c.q_dim, H)
+        A.qkv = d.alloc(self.kp_qkv * B * maxrows * 4, "qkv")
+        A.oparts = d.alloc(self.kp_o * B * H * 4, "oParts")
         A.q = d.alloc(B * QD * 4, "qPrep")
         A.attn = d.alloc(B * QD * 2, "attnOut")
         A.part_o = d.alloc(B * c.q_heads * maxch * c.head_dim * 4, "partO")
@@ -261,16 +272,22 @@ class BatchEngine(Engine):
                1, 0, 2)
         for L in self.layers:
             nxt = self.layers[L.i + 1].attn_norm if L.i + 1 < c.layers else None
-            d.call("e4b_q40mm", A.normed, L.qkv, A.qkv, H, L.qkv_rows, B)
+            if self.kp_qkv > 1:
+                d.call("e4b_q40mm_kparts", A.normed, L.qkv, A.qkv, H, L.qkv_rows, B, self.kp_qkv)
+            else:
+                d.call("e4b_q40mm", A.normed, L.qkv, A.qkv, H, L.qkv_rows, B)
             d.call("e4b_headprep_seq", A.qkv, L.q_norm, L.k_norm, A.params, L.kc, L.vc, A.q, c.q_heads, c.kv_heads,
                    c.head_dim, L.angles, ctypes.c_float(L.theta), ctypes.c_float(c.eps), int(L.keqv), L.cachemode,
-                   L.ring, L.slots, B)
+                   L.ring, L.slots, B, self.kp_qkv)
             d.call("e4b_attdec_seq", A.q, L.kc, L.vc, A.params, A.part_o, A.part_ml, A.attn, c.q_heads, c.kv_heads,
                    c.head_dim, c.window if L.sliding else 0, L.cachemode, L.ring, L.max_chunks, ctypes.c_float(1.0),
                    L.slots, B, 1)
-            d.call("e4b_q40mm", A.attn, L.o, A.tmp, c.q_dim, H, B)
-            d.call("e4b_rmsacc3", A.tmp, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
-                   A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B, 1)
+            if self.kp_o > 1:
+                d.call("e4b_q40mm_kparts", A.attn, L.o, A.oparts, c.q_dim, H, B, self.kp_o)
+            else:
+                d.call("e4b_q40mm", A.attn, L.o, A.oparts, c.q_dim, H, B)
+            d.call("e4b_rmsacc3", A.oparts, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
+                   A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B, 1, self.kp_o)
             d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
             if self.zipf:
                 d.call("e4b_route_zipf", A.params, A.topk_idx, A.topk_w, B, K, E, ctypes.c_float(self.zipf),

@@ -16,9 +16,10 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
                            const uint32_t* __restrict__ params, uint16_t* __restrict__ kcache,
                            uint16_t* __restrict__ vcache, float* __restrict__ q_out, int QH, int KVH, int HD,
                            int angles, float theta, float eps, int keqv, int cachemode, int ring, int cache_slots,
-                           uint32_t* status, size_t seq_stride) {
+                           uint32_t* status, size_t seq_stride, int nparts, size_t part_stride) {
   pdl_wait();
   __shared__ float sh[32];
+  __shared__ float xv[512];                      // this head's qkv row (the sum of nparts K-part partials)
   const int head = blockIdx.x, b = blockIdx.y;
   // seq_stride > 0: row b is sequence b at the common position params[0], with
   // its own cache at kcache / vcache + b * seq_stride; else rows are consecutive
@@ -33,7 +34,12 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
   const size_t qkvS = (size_t)(QH + KVH * (2 - keqv)) * HD;
   const size_t base = (size_t)b * qkvS + (size_t)src * HD;
   float s = 0.f;
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) s = fmaf(qkv[base + d], qkv[base + d], s);
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float v = qkv[base + d];
+    for (int k = 1; k < nparts; k++) v += qkv[(size_t)k * part_stride + base + d];
+    xv[d] = v;
+    s = fmaf(v, v, s);
+  }
   const float inv = rms_scale(block_sum(s, sh), HD, eps);
   const int half = HD / 2;
   const uint32_t pos = params[0] + pb;
@@ -47,8 +53,8 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
   if (head < QH) {
     float* qo = q_out + ((size_t)b * QH + head) * HD;
     for (int p = threadIdx.x; p < half; p += blockDim.x) {
-      const float x0 = qkv[base + p] * inv * qw[p];
-      const float x1 = qkv[base + p + half] * inv * qw[p + half];
+      const float x0 = xv[p] * inv * qw[p];
+      const float x1 = xv[p + half] * inv * qw[p + half];
       if (p < angles) {
         float sn, cs;
         sincosf(rope_theta(pos, p, HD, theta), &sn, &cs);
@@ -63,8 +69,8 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
     const int h = head - QH;
     uint16_t* kc = kcache + ((size_t)slot * KVH + h) * HD;
     for (int p = threadIdx.x; p < half; p += blockDim.x) {
-      const float x0 = qkv[base + p] * inv * kw[p];
-      const float x1 = qkv[base + p + half] * inv * kw[p + half];
+      const float x0 = xv[p] * inv * kw[p];
+      const float x1 = xv[p + half] * inv * kw[p + half];
       if (p < angles) {
         float sn, cs;
         sincosf(rope_theta(pos, p, HD, theta), &sn, &cs);
@@ -78,7 +84,7 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
   } else {
     const int h = head - QH - KVH;
     uint16_t* vc = vcache + ((size_t)slot * KVH + h) * HD;
-    for (int d = threadIdx.x; d < HD; d += blockDim.x) vc[d] = f2h(qkv[base + d] * inv);
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) vc[d] = f2h(xv[d] * inv);
   }
 }
 
@@ -211,7 +217,7 @@ E4B_API int e4b_headprep(e4b_ctx* c, const float* qkv, const float* qw, const fl
                          float theta, float eps, int keqv, int cachemode, int ring, int cache_slots, int batch) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, qkv && qw && kw && params && kcache && vcache && q_out, "headprep: null buffer");
-  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD % 2 == 0 && rope_angles >= 0 &&
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD <= 512 && HD % 2 == 0 && rope_angles >= 0 &&
                      rope_angles <= HD / 2 && cache_slots > 0,
               "headprep: bad geometry QH=%d KVH=%d HD=%d angles=%d", QH, KVH, HD, rope_angles);
   E4B_REQUIRE(c, cachemode >= 0 && cachemode <= 2 && (cachemode != 1 || (ring > 0 && ring <= cache_slots)),
@@ -219,15 +225,16 @@ E4B_API int e4b_headprep(e4b_ctx* c, const float* qkv, const float* qw, const fl
   if (batch < 1) batch = 1;
   return e4b_launch(c, "headprep", k_headprep, dim3(QH + 2 * KVH, batch), dim3(128), 0, qkv, qw, kw, params, kcache,
                     vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring, cache_slots,
-                    c->status, (size_t)0);
+                    c->status, (size_t)0, 1, (size_t)0);
 }
 
 E4B_API int e4b_headprep_seq(e4b_ctx* c, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
                              uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
                              int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
-                             int cache_slots, int nseq) {
+                             int cache_slots, int nseq, int nparts) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, qkv && qw && kw && params && kcache && vcache && q_out && nseq > 0, "headprep_seq: bad args");
+  E4B_REQUIRE(c, nparts >= 1 && HD <= 512, "headprep_seq: nparts=%d, HD=%d (<= 512)", nparts, HD);
   E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD % 2 == 0 && rope_angles >= 0 &&
                      rope_angles <= HD / 2 && cache_slots > 0,
               "headprep_seq: bad geometry QH=%d KVH=%d HD=%d angles=%d", QH, KVH, HD, rope_angles);
@@ -236,7 +243,8 @@ E4B_API int e4b_headprep_seq(e4b_ctx* c, const float* qkv, const float* qw, cons
   const size_t stride = (size_t)cache_slots * KVH * HD;
   return e4b_launch(c, "headprep_seq", k_headprep, dim3(QH + 2 * KVH, nseq), dim3(128), 0, qkv, qw, kw, params,
                     kcache, vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring,
-                    cache_slots, c->status, stride);
+                    cache_slots, c->status, stride, nparts,
+                    (size_t)nseq * (QH + KVH * (2 - (keqv ? 1 : 0))) * HD);
 }
 
 E4B_API int e4b_rope(e4b_ctx* c, float* x, const uint32_t* params, int heads, int HD, int rope_angles, float theta) {

@@ -446,6 +446,159 @@ __global__ void k_wacc(const float* __restrict__ y, const uint32_t* __restrict__
   out[(size_t)tok * OUT + o] = acc;
 }
 
+// ---- dense batch, K split across CTAs: y_parts[kp][t][row] = W[row][K-part kp] x_t.
+// Item = (K-part, group of kKW 32-row tiles, one per warp); items are K-part
+// major, so a CTA restages its activations (all <= 64 tokens, only the part's
+// k-range) once per part it visits, as 2-D TMA boxes of [64 tokens x 64 halves]
+// under the 128-byte swizzle (four per 256-k quantum; conflict-free reads).  Every weight is decoded once for all the
+// tokens (8 MMA column groups); the consumer sums the parts in order.
+constexpr int kKW = 8, kKS = 3;
+
+struct QkpP {
+  const uint16_t* x;             // [n][IN] fragment order
+  float* y;                      // [kparts][n][ROWS]
+  uint32_t* status;
+  int IN, nb, ROWS, n, tiles, nq, kparts, groups, xpitch;   // groups = tile groups; xpitch = staged quanta
+};
+
+E4B_DEV int kq_begin(const QkpP& p, int kp) { return p.nq * kp / p.kparts; }
+
+__global__ void __launch_bounds__(32 * kKW, 1) k_qkp(const QkpP p, const __grid_constant__ CUtensorMap map,
+                                                     const __grid_constant__ CUtensorMap xmap) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kKW][kKS];
+  __shared__ __align__(8) uint64_t xbar;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  // xpitch: staged quanta per part; each quantum is 4 swizzled boxes of 8 KB
+  uint8_t* xs = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);
+  uint8_t* stages = xs + (size_t)p.xpitch * 32768 + (size_t)warp * kKS * kQuantumBytes;
+  const int T = p.kparts * p.groups;
+  const int i0 = (int)((int64_t)T * blockIdx.x / gridDim.x), i1 = (int)((int64_t)T * (blockIdx.x + 1) / gridDim.x);
+  pdl_trigger();
+  if (lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map)) : "memory");
+    if (warp == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+    for (int s = 0; s < kKS; s++) mbar_init(&full[warp][s], 1);
+    if (warp == 0) mbar_init(&xbar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // producer cursor over this warp's (item, quantum) sequence; weights only, so
+  // the first quanta are requested before the wait on the previous kernel
+  auto has_tile = [&](int it) { return (it % p.groups) * kKW + warp < p.tiles; };
+  int pit = i0;
+  while (pit < i1 && !has_tile(pit)) pit++;
+  int pkq = pit < i1 ? kq_begin(p, pit / p.groups) : 0;
+  auto issue = [&](int s) {
+    const int tile = (pit % p.groups) * kKW + warp, kp = pit / p.groups;
+    if (lane == 0) mbar_expect_tx(&full[warp][s], (uint32_t)kQuantumBytes);
+    __syncwarp();
+    if (lane < 2) tma_load_2d(stages + s * kQuantumBytes + lane * kSubBytes, &map, pkq * 18, 32 * tile + 16 * lane,
+                              &full[warp][s]);
+    if (++pkq == kq_begin(p, kp + 1)) {
+      do pit++; while (pit < i1 && !has_tile(pit));
+      if (pit < i1) pkq = kq_begin(p, pit / p.groups);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < kKS; s++)
+    if (pit < i1) issue(s);
+  pdl_wait();
+
+  Lane L;
+  L.o_odd = 2 + 4 * t;
+  L.o_e1 = t < 3 ? 4 + 4 * t : 0;
+  L.sel = t < 3 ? 0x3210u : 0x5432u;
+  const int ng = (p.n + 7) >> 3;
+  bool ok = true;
+  int cur = -1, restage = 0, used = 0;
+  for (int it = i0; it < i1; it++) {
+    const int kp = it / p.groups, q0 = kq_begin(p, kp), q1 = kq_begin(p, kp + 1);
+    if (kp != cur) {
+      __syncthreads();          // every warp is done with the previous part's activations
+      if (threadIdx.x == 0) {
+        mbar_expect_tx(&xbar, (uint32_t)(q1 - q0) * 32768u);
+        for (int b = 0; b < 4 * (q1 - q0); b++) tma_load_2d(xs + (size_t)b * 8192, &xmap, 256 * q0 + 64 * b, 0, &xbar);
+      }
+      if (ok) ok = mbar_wait(&xbar, (uint32_t)(restage & 1), p.status);
+      restage++;
+      cur = kp;
+    }
+    if (!has_tile(it)) continue;
+    const int tile = (it % p.groups) * kKW + warp;
+    float acc[8][2][4];
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+#pragma unroll
+      for (int s = 0; s < 2; s++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) acc[q][s][r] = 0.f;
+    // token 8q + g, block k of quantum kq: box 4 (kq - q0) + k / 2, row 8q + g,
+    // 16-byte chunk (4 (k & 1) + t) ^ g
+    uint32_t xoff[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) xoff[h] = (uint32_t)(g * 128 + (((4 * h + t) ^ g) << 4));
+    for (int kq = q0; kq < q1; kq++, used++) {
+      const int s = used % kKS;
+      if (ok) ok = mbar_wait(&full[warp][s], (uint32_t)((used / kKS) & 1), p.status);
+      if (ok) {
+        const uint8_t* a = stages + s * kQuantumBytes + g * kRowPitch;
+        const uint8_t* xq = xs + (size_t)(kq - q0) * 32768;
+#pragma unroll 2
+        for (int k = 0; k < 8; k++) {
+          const int par = k & 1;
+          uint32_t A[2][8];
+          float d[2][2];
+#pragma unroll
+          for (int sb = 0; sb < 2; sb++) {
+            const uint8_t* ra = a + sb * kSubBytes + 18 * k;
+            const uint8_t* rb = ra + 8 * kRowPitch;
+            dq_row(par ? nib_odd(ra, L) : nib_even(ra, L), A[sb][0], A[sb][1], A[sb][2], A[sb][3]);
+            dq_row(par ? nib_odd(rb, L) : nib_even(rb, L), A[sb][4], A[sb][5], A[sb][6], A[sb][7]);
+            d[sb][0] = h2f(*reinterpret_cast<const uint16_t*>(ra));
+            d[sb][1] = h2f(*reinterpret_cast<const uint16_t*>(rb));
+          }
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            if (q >= ng) break;
+            const uint4 xb = *reinterpret_cast<const uint4*>(xq + (k >> 1) * 8192 + q * 1024 + xoff[k & 1]);
+#pragma unroll
+            for (int sb = 0; sb < 2; sb++) {
+              float c[4] = {0.f, 0.f, 0.f, 0.f};
+              mma16816(c, A[sb][0], A[sb][4], A[sb][1], A[sb][5], xb.x, xb.y);
+              mma16816(c, A[sb][2], A[sb][6], A[sb][3], A[sb][7], xb.z, xb.w);
+              acc[q][sb][0] = fmaf(d[sb][0], c[0], acc[q][sb][0]);
+              acc[q][sb][1] = fmaf(d[sb][0], c[1], acc[q][sb][1]);
+              acc[q][sb][2] = fmaf(d[sb][1], c[2], acc[q][sb][2]);
+              acc[q][sb][3] = fmaf(d[sb][1], c[3], acc[q][sb][3]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (ok && pit < i1) issue(s);
+    }
+    if (!ok) continue;
+    float* yp = p.y + (size_t)kp * p.n * p.ROWS;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      if (q >= ng) break;
+#pragma unroll
+      for (int col = 0; col < 2; col++) {
+        const int j = 8 * q + 2 * t + col;
+        if (j >= p.n) continue;
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+          for (int sb = 0; sb < 2; sb++) {
+            const int r = 32 * tile + 16 * sb + g + 8 * h;
+            if (r < p.ROWS) yp[(size_t)j * p.ROWS + r] = acc[q][sb][2 * h + col];
+          }
+      }
+    }
+  }
+}
+
 template <int MODE, int EPI, int W, int S, int TOKC, int KS>
 int qmm_launch(e4b_ctx* c, const char* name, const QmmP& p, const CUtensorMap& map, size_t smem, int grid) {
   auto kern = k_qmm<MODE, EPI, W, S, TOKC, KS>;
@@ -571,6 +724,53 @@ E4B_API int e4b_q40mm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, float* y,
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, x && w && y && n > 0 && OUT > 0, "q40mm: bad args");
   return qmm(c, "q40mm", x, w, nullptr, nullptr, y, nullptr, IN, OUT, 0, 1, 1, n, 0);
+}
+
+E4B_API int e4b_q40mm_kparts(e4b_ctx* c, const uint16_t* x, const uint8_t* w, float* y_parts, int IN, int OUT, int n,
+                             int kparts) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && w && y_parts && n > 0 && n <= 64 && OUT > 0, "q40mm_kparts: bad args (n <= 64)");
+  E4B_REQUIRE(c, IN > 0 && IN % 256 == 0 && IN <= 16384 && tensor_map_encoder(), "q40mm_kparts: IN=%d must be a multiple of 256", IN);
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0,
+              "q40mm_kparts: weights and activations must be 16-byte aligned");
+  QkpP p = {};
+  p.x = x; p.y = y_parts; p.status = c->status;
+  p.IN = IN; p.nb = IN / 32; p.ROWS = OUT; p.n = n;
+  p.nq = p.nb / 8;
+  E4B_REQUIRE(c, kparts >= 1 && kparts <= p.nq, "q40mm_kparts: kparts=%d must be in [1, %d]", kparts, p.nq);
+  p.kparts = kparts;
+  p.tiles = (OUT + 31) / 32;
+  p.groups = (p.tiles + kKW - 1) / kKW;
+  const int max_q = (p.nq + kparts - 1) / kparts;
+  p.xpitch = max_q;
+  const size_t smem = (size_t)max_q * 32768 + (size_t)kKW * kKS * kQuantumBytes + 1024;
+  E4B_REQUIRE(c, smem <= kQmmSmemCap, "q40mm_kparts: %d quanta per part need too much shared memory", max_q);
+  const int rowbytes = p.nb * 18;
+  CUtensorMap map;
+  const cuuint64_t gdim[2] = {(cuuint64_t)(rowbytes / 8), (cuuint64_t)OUT};
+  const cuuint64_t gstride[1] = {(cuuint64_t)rowbytes};
+  const cuuint32_t box[2] = {kRowPitch / 8, 16};
+  const cuuint32_t estride[2] = {1, 1};
+  CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(w), gdim, gstride,
+                                    box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  E4B_REQUIRE(c, r == CUDA_SUCCESS, "q40mm_kparts: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  // the activations [n][IN] f16 as boxes of 64 halves x 64 rows (rows past n read as zeros)
+  CUtensorMap xmap;
+  {
+    const cuuint64_t xd[2] = {(cuuint64_t)IN, (cuuint64_t)n};
+    const cuuint64_t xs[1] = {(cuuint64_t)IN * 2};
+    const cuuint32_t xb[2] = {64, 64};
+    CUresult rx = tensor_map_encoder()(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(x), xd, xs, xb,
+                                       estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    E4B_REQUIRE(c, rx == CUDA_SUCCESS, "q40mm_kparts: activation tensor map failed (%d)", (int)rx);
+  }
+  cudaError_t e = cudaFuncSetAttribute(k_qkp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q40mm_kparts smem attr: %s", cudaGetErrorString(e));
+  const int items = kparts * p.groups;
+  const int grid = items < c->sm_count ? items : c->sm_count;
+  return e4b_launch(c, "q40mm_kparts", k_qkp, dim3((unsigned)grid), dim3(32 * kKW), smem, p, map, xmap);
 }
 
 E4B_API int e4b_q40gumm(e4b_ctx* c, const uint16_t* x, const uint8_t* w, uint16_t* yh, int IN, int FF, int n) {

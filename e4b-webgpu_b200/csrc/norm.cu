@@ -68,7 +68,7 @@ __global__ void k_rmsaccn(const float* __restrict__ t, const float* __restrict__
 __global__ void k_rmsacc3(const float* __restrict__ t, const float* __restrict__ w_acc, const float* __restrict__ w1,
                           const float* __restrict__ w2, const float* __restrict__ w3, const float* __restrict__ h_in,
                           uint16_t* __restrict__ y1, float* __restrict__ y2, uint16_t* __restrict__ y3,
-                          float* __restrict__ h_out, int dim, float eps, int xfo) {
+                          float* __restrict__ h_out, int dim, float eps, int xfo, int nparts, size_t part_stride) {
   pdl_wait();
   extern __shared__ float hs[];           // [dim] h, [dim] t
   __shared__ float sh[32];
@@ -76,7 +76,8 @@ __global__ void k_rmsacc3(const float* __restrict__ t, const float* __restrict__
   const size_t ob = (size_t)blockIdx.x * dim;
   float s = 0.f;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-    const float v = t[ob + i];
+    float v = t[ob + i];
+    for (int k = 1; k < nparts; k++) v += t[(size_t)k * part_stride + ob + i];   // K-part partials, in order
     ts[i] = v;
     hs[i] = h_in[ob + i];
     s = fmaf(v, v, s);
@@ -220,15 +221,16 @@ E4B_API int e4b_rmsaccn(e4b_ctx* c, const float* t, const float* w1, float* hidd
 
 E4B_API int e4b_rmsacc3(e4b_ctx* c, const float* t, const float* w_acc, const float* w1, const float* w2,
                         const float* w3, const float* h_in, uint16_t* y1, float* y2, uint16_t* y3, float* h_out,
-                        int dim, float eps, int rows, int xfo) {
+                        int dim, float eps, int rows, int xfo, int nparts) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, t && w_acc && w1 && w2 && w3 && h_in && y1 && y2 && y3 && h_out && dim > 0, "rmsacc3: bad args");
   E4B_REQUIRE(c, !xfo || dim % 32 == 0, "rmsacc3: fragment order needs dim %% 32 == 0");
+  E4B_REQUIRE(c, nparts >= 1, "rmsacc3: nparts=%d", nparts);
   if (rows < 1) rows = 1;
   const size_t sm = (size_t)dim * 8;
   if (int r = set_smem(c, (const void*)k_rmsacc3, sm)) return r;
   return e4b_launch(c, "rmsacc3", k_rmsacc3, dim3(rows), dim3(1024), sm, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
-                    h_out, dim, eps, xfo);
+                    h_out, dim, eps, xfo, nparts, (size_t)rows * dim);
 }
 
 E4B_API int e4b_a4btail(e4b_ctx* c, const float* t1, const float* w1, const float* m, const float* w2,

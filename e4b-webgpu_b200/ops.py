@@ -64,10 +64,10 @@ def rmsaccn(dev: Device, t, w1, hidden, w2, yh, *, DIM, EPS=1e-6, MUL=1.0, NORM2
     dev.call("e4b_rmsaccn", _p(t), _p(w1), _p(hidden), _p(w2), _p(yh), DIM, float(EPS), float(MUL), NORM2)
 
 
-def rmsacc3(dev: Device, t, w_acc, w1, w2, w3, h_in, y1, y2, y3, h_out, *, DIM, EPS=1e-6, BATCH=1, XFO=0):
+def rmsacc3(dev: Device, t, w_acc, w1, w2, w3, h_in, y1, y2, y3, h_out, *, DIM, EPS=1e-6, BATCH=1, XFO=0, NPARTS=1):
     """kernels/rmsacc3.wgsl"""
     dev.call("e4b_rmsacc3", _p(t), _p(w_acc), _p(w1), _p(w2), _p(w3), _p(h_in), _p(y1), _p(y2), _p(y3), _p(h_out),
-             DIM, float(EPS), BATCH, XFO)
+             DIM, float(EPS), BATCH, XFO, NPARTS)
 
 
 def a4btail(dev: Device, t1, w1, m, w2, wp, h_in, w_next, y_next, h_out, *, H, EPS=1e-6, MUL=1.0, NEXT=1, BATCH=1,

@@ -132,10 +132,11 @@ E4B_API int e4b_rmsacc(e4b_ctx* ctx, const float* x, const float* w, float* hidd
  * f16(hidden) (norm2=0). */
 E4B_API int e4b_rmsaccn(e4b_ctx* ctx, const float* t, const float* w1, float* hidden, const float* w2,
                         uint16_t* yh, int dim, float eps, float mul, int norm2);
-/* kernels/rmsacc3.wgsl:27-53 (rows = batch); xfo=1: y1, y3 in fragment order. */
+/* kernels/rmsacc3.wgsl:27-53 (rows = batch); xfo=1: y1, y3 in fragment order;
+ * nparts > 1: t is the sum of nparts [rows][dim] partials (e4b_q40mm_kparts), in order. */
 E4B_API int e4b_rmsacc3(e4b_ctx* ctx, const float* t, const float* w_acc, const float* w1, const float* w2,
                         const float* w3, const float* h_in, uint16_t* y1, float* y2, uint16_t* y3,
-                        float* h_out, int dim, float eps, int rows, int xfo);
+                        float* h_out, int dim, float eps, int rows, int xfo, int nparts);
 /* kernels/a4btail.wgsl:26-71 (rows = batch); xfo=1: y_next in fragment order. */
 E4B_API int e4b_a4btail(e4b_ctx* ctx, const float* t1, const float* w1, const float* m, const float* w2,
                         const float* wp, const float* h_in, const float* w_next, uint16_t* y_next,
@@ -192,6 +193,11 @@ E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, co
  * q40mm: y[n][OUT] = W x[n] (f32); q40gumm: yh[n][FF] = f16(gelu(gate)*up) with
  * rows [gate FF | up FF] (kernels/q40gu.wgsl dense part, per token; yh in fragment order). */
 E4B_API int e4b_q40mm(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, float* y, int IN, int OUT, int n);
+/* q40mm with K split over kparts CTA groups, all n <= 64 tokens per weight
+ * decode: y_parts[kp][n][OUT] = the kp-th K-range's share (quanta of 256 k,
+ * split evenly); the consumer sums the parts in order.  IN % 256 == 0. */
+E4B_API int e4b_q40mm_kparts(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, float* y_parts, int IN, int OUT,
+                             int n, int kparts);
 E4B_API int e4b_q40gumm(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, uint16_t* yh, int IN, int FF, int n);
 E4B_API int e4b_wacc(e4b_ctx* ctx, const float* y, const uint32_t* inv, const float* topk_w, float* out, int n_tok,
                      int K, int OUT);
@@ -315,11 +321,12 @@ E4B_API int e4b_plemul(e4b_ctx* ctx, const float* a, const float* ple, float* y,
 /* ---- batched decode of nseq sequences at one common position (params[0],
  * kvCount params[4]); sequence b's KV cache starts at cache + b * slots*KVH*HD,
  * its q / qkv / partial / output rows are row b of the per-sequence layouts.
- * attcomb_seq xfo=1: out_h rows (QH*HD) in fragment order. */
+ * attcomb_seq xfo=1: out_h rows (QH*HD) in fragment order.  headprep_seq
+ * nparts > 1: qkv is the sum of nparts [nseq][rows] partials (e4b_q40mm_kparts). */
 E4B_API int e4b_headprep_seq(e4b_ctx* ctx, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
                              uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
                              int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
-                             int cache_slots, int nseq);
+                             int cache_slots, int nseq, int nparts);
 E4B_API int e4b_attsplit_seq(e4b_ctx* ctx, const float* q, const uint16_t* kcache, const uint16_t* vcache,
                              const uint32_t* params, float* part_o, float* part_ml, int QH, int KVH, int HD,
                              int window, int cachemode, int ring, int chunk, int max_chunks, float scale,

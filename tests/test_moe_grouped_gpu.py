@@ -128,7 +128,7 @@ def test_fragment_order_producers(e4b, dev):
     for xfo in (0, 1):
         bufs = [dev.alloc(B * H * 2), dev.alloc(B * H * 4), dev.alloc(B * H * 2), dev.alloc(B * H * 4)]
         dev.call("e4b_rmsacc3", dev.upload(t).ptr, *[q.ptr for q in ws], bx.ptr, *[q.ptr for q in bufs], H,
-                 np.float32(1e-6), B, xfo)
+                 np.float32(1e-6), B, xfo, 1)
         dev.sync()
         outs[xfo] = [dev.read(bufs[0], np.uint16, B * H).reshape(B, H), dev.read(bufs[1], F32, B * H),
                      dev.read(bufs[2], np.uint16, B * H).reshape(B, H), dev.read(bufs[3], F32, B * H)]
@@ -201,3 +201,47 @@ def test_a4btail_wacc_equals_wacc_then_a4btail(e4b, dev):
         dev.sync()
         outs.append((dev.read(yn, np.uint16, B * H), dev.read(ho, F32, B * H)))
     assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("IN,OUT,n,kparts", [(2816, 6144, 64, 8), (4096, 2816, 64, 16), (512, 96, 37, 2),
+                                             (256, 40, 5, 1), (768, 200, 64, 3)])
+def test_q40mm_kparts(e4b, dev, IN, OUT, n, kparts):
+    """K split over CTA groups, all tokens per weight decode: the parts sum (in
+    order) to W x per token, within the oracle's f32 tolerance."""
+    rng = np.random.default_rng(IN + OUT)
+    w = q40(e4b, OUT, IN, 3 + IN)
+    x = O.f16r(rng.standard_normal((n, IN)).astype(F32))
+    y = dev.alloc(kparts * n * OUT * 4)
+    dev.call("e4b_q40mm_kparts", dev.upload(e4b.batch.to_xfo(x.astype(np.float16))).ptr, dev.upload(w).ptr, y.ptr,
+             IN, OUT, n, kparts)
+    dev.sync()
+    assert dev.status() == 0
+    parts = dev.read(y, F32, kparts * n * OUT).reshape(kparts, n, OUT)
+    got = parts[0].copy()
+    for k in range(1, kparts):
+        got += parts[k]
+    for t in range(0, n, 7):
+        ref = O.q40mv(w, x[t], OUT, IN)
+        assert np.max(np.abs(got[t] - ref)) <= 1e-5 * np.max(np.abs(ref)), t
+
+
+def test_kpart_consumers(e4b, dev):
+    """headprep_seq and rmsacc3 with nparts > 1 equal the single-part call on
+    the summed input (sums in part order)."""
+    rng = np.random.default_rng(8)
+    H, B, P = 256, 3, 4
+    parts = rng.standard_normal((P, B, H)).astype(F32)
+    total = parts[0].copy()
+    for k in range(1, P):
+        total += parts[k]
+    ws = [dev.upload(rng.uniform(0.5, 1.5, H).astype(F32)) for _ in range(4)]
+    hin = dev.upload(rng.standard_normal((B, H)).astype(F32))
+    res = []
+    for src, npart in ((parts, P), (total, 1)):
+        bufs = [dev.alloc(B * H * 2), dev.alloc(B * H * 4), dev.alloc(B * H * 2), dev.alloc(B * H * 4)]
+        dev.call("e4b_rmsacc3", dev.upload(src).ptr, *[q.ptr for q in ws], hin.ptr, *[q.ptr for q in bufs], H,
+                 np.float32(1e-6), B, 1, npart)
+        dev.sync()
+        res.append([dev.read(bufs[i], np.uint8, B * H * (2 if i % 2 == 0 else 4)) for i in range(4)])
+    for a, b in zip(*res):
+        assert np.array_equal(a, b)
