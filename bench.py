@@ -792,12 +792,12 @@ def main():
         out = run_reference(args, rank, world)
     elif args.batch > 1:
         out, img, cfg = run_moe_batch(args, rank, world, local_rank)
-        if rank == 0:
-            out["cpu_baseline"] = None if args.no_cpu else cpu_baseline(img, cfg, args.cpu_budget, 8)
+        if rank == 0:   # the CPU baseline is an N = 1 measurement
+            out["cpu_baseline"] = None if (args.no_cpu or world > 1) else cpu_baseline(img, cfg, args.cpu_budget, 8)
     else:
         out, img, cfg = run_ours(args, rank, world, local_rank)
         if rank == 0:
-            out["cpu_baseline"] = None if args.no_cpu else cpu_baseline(img, cfg, args.cpu_budget, 64)
+            out["cpu_baseline"] = None if (args.no_cpu or world > 1) else cpu_baseline(img, cfg, args.cpu_budget, 64)
     if rank == 0 and out is not None:
         print(json.dumps(out), flush=True)
 
