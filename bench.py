@@ -275,7 +275,7 @@ def run_moe_batch(args, rank, world, local_rank):
             nid = e4b.batch.nccl_unique_id(probe)
             probe.close()
         ep = (world, rank, dist.bcast_bytes(nid))
-    eng = e4b.BatchEngine(img, nloc, local_rank, ep=ep, zipf=zipf, tok0=rank * nloc)
+    eng = e4b.BatchEngine(img, nloc, local_rank, ep=ep, zipf=zipf, tok0=rank * nloc, ep_overlap=bool(args.ep_overlap))
     dev = eng.dev
     prompts = np.stack([e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=1000 + b)
                         for b in range(rank * nloc, (rank + 1) * nloc)])
@@ -754,6 +754,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling cases)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences decoded in lockstep (default 1 on 1 GPU, 64 -- expert parallel -- on N > 1)")
+    ap.add_argument("--ep-overlap", type=int, default=1,
+                    help="expert parallel: exchange the rows on a side stream beside the dense FFN (1) or in line (0)")
     ap.add_argument("--zipf", type=float, default=1.1,
                     help="batched MoE: Zipf(s) expert routing of BASELINE config 5 (0 = the router's top-8)")
     ap.add_argument("--fused", type=int, default=1, help="1: fused token kernel where the model allows it; "

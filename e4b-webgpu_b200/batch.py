@@ -80,7 +80,7 @@ def from_xfo(x: np.ndarray) -> np.ndarray:
 
 class BatchEngine(Engine):
     def __init__(self, src, nseq: int, device=0, *, chunk: int = 64, ep=None, zipf: float | None = None,
-                 tok0: int = 0, route_seed: int = 1234):
+                 tok0: int = 0, route_seed: int = 1234, ep_overlap: bool = True):
         """nseq sequences decoded in lockstep on this GPU.  ep = (nranks, rank,
         nccl_id): expert parallelism -- this rank decodes its nseq sequences and
         owns experts [rank*E/nranks, (rank+1)*E/nranks); every rank of the
@@ -91,6 +91,7 @@ class BatchEngine(Engine):
         sequence, so any rank count routes identically."""
         self.nseq = int(nseq)
         self.zipf, self.tok0, self.route_seed = zipf, int(tok0), int(route_seed)
+        self.ep_overlap = bool(ep_overlap)     # row exchange on a side stream beside the dense FFN
         self.ep = None
         if ep is not None:
             nranks, rank, nid = ep
@@ -292,7 +293,7 @@ class BatchEngine(Engine):
             if self.zipf:
                 d.call("e4b_route_zipf", A.params, A.topk_idx, A.topk_w, B, K, E, ctypes.c_float(self.zipf),
                        ctypes.c_uint32(self.route_seed), L.i, self.tok0)
-            if self.ep is not None:
+            if self.ep is not None and self.ep_overlap:
                 self._moe_ep_send()           # the rows travel while the dense FFN runs
             d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
             d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
@@ -302,6 +303,8 @@ class BatchEngine(Engine):
                 d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
                 y_rows, y_map = A.yo, A.inv
             else:
+                if not self.ep_overlap:
+                    self._moe_ep_send()
                 y_rows, y_map = self._moe_ep_finish(L)
             d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, y_rows, y_map, A.topk_w, K, L.post_ffw2, L.post_ffw,
                    A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),

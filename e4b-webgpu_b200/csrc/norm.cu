@@ -120,8 +120,10 @@ __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict_
     float mv;
     if (y) {
       mv = 0.f;
-      for (int k = 0; k < K; k++)
-        mv += tkw[(size_t)blockIdx.x * K + k] * y[(size_t)inv[(size_t)blockIdx.x * K + k] * H + i];
+      for (int k = 0; k < K; k++) {
+        const uint32_t r = inv[(size_t)blockIdx.x * K + k];
+        if (r != 0xffffffffu) mv += tkw[(size_t)blockIdx.x * K + k] * y[(size_t)r * H + i];   // 0xffffffff: dropped entry
+      }
     } else {
       mv = m[ob + i];
     }
