@@ -531,7 +531,7 @@ def run_reference(args, rank, world):
     warm = min(args.warmup, 1)
     base = cpu_baseline(img, cfg, budget_s=60.0, max_steps=steps + warm)
     v = base["value"]
-    if args.batch > 1:
+    if args.batch > 1 or cfg.moe:
         # the reference path decodes one token at a time; a batch of independent
         # sequences runs at its per-token rate (the sample is sequence 0's decode)
         metric = moe_metric(args.batch, world)
@@ -792,7 +792,8 @@ def main():
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         out = run_reference(args, rank, world)
-    elif args.batch > 1:
+    elif args.batch > 1 or importlib.import_module("e4b-webgpu_b200").config.get(args.config).moe:
+        # MoE configs (any batch, including 1) run the batched engine
         out, img, cfg = run_moe_batch(args, rank, world, local_rank)
         if rank == 0:   # the CPU baseline is an N = 1 measurement
             out["cpu_baseline"] = None if (args.no_cpu or world > 1) else cpu_baseline(img, cfg, args.cpu_budget, 8)

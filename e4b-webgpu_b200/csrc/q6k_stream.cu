@@ -286,6 +286,7 @@ E4B_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memo
 template <int N>
 E4B_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+template <int NGT>   // token groups computed per step: 1, 2, 4 or 8 (>= the pass's groups)
 __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, const uint4* __restrict__ xp,
                                                   float* __restrict__ y, int N, int OUT, int n, int NG, float softcap,
                                                   uint32_t* status) {
@@ -349,9 +350,9 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
   bool ok = true;
   for (int u = blockIdx.x; u < units; u += gridDim.x) {
     const int rb = u / passes, pass = u % passes, ng = min(8, NG - 8 * pass);
-    float acc[8][2][4];
+    float acc[NGT][2][4];
 #pragma unroll
-    for (int q = 0; q < 8; q++)
+    for (int q = 0; q < NGT; q++)
 #pragma unroll
       for (int s = 0; s < 2; s++)
 #pragma unroll
@@ -378,8 +379,8 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
           d[i] = h2f(*reinterpret_cast<const uint16_t*>(blk[i] + 208));
         }
         const uint4* xs = reinterpret_cast<const uint4*>(xbuf + b * kLmXSlab);
-        // all 8 token groups every step (a short last pass computes unused
-        // columns that are not stored), 16 independent MMA chains per step
+        // NGT token groups every step (a short last pass computes unused
+        // columns that are not stored), up to 16 independent MMA chains per step
 #pragma unroll 2
         for (int j = 0; j < 16; j++) {
           const int e0 = 16 * j + 2 * t;
@@ -394,26 +395,27 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
             A[s][2] = q6_pair(blk[2 * s], e0 + 8);
             A[s][3] = q6_pair(blk[2 * s + 1], e0 + 8);
           }
+          constexpr int HQ = NGT < 4 ? NGT : 4;
 #pragma unroll
-          for (int hq = 0; hq < 8; hq += 4) {
-            // 4 token groups x 2 subtiles: 8 independent MMA chains
-            uint4 xv[4];
+          for (int hq = 0; hq < NGT; hq += HQ) {
+            // HQ token groups x 2 subtiles: independent MMA chains
+            uint4 xv[HQ];
 #pragma unroll
-            for (int q = 0; q < 4; q++) xv[q] = xs[((hq + q) * 16 + j) * 32 + lane];
-            float c[4][2][4];
+            for (int q = 0; q < HQ; q++) xv[q] = xs[((hq + q) * 16 + j) * 32 + lane];
+            float c[HQ][2][4];
 #pragma unroll
-            for (int q = 0; q < 4; q++)
+            for (int q = 0; q < HQ; q++)
 #pragma unroll
               for (int s = 0; s < 2; s++) {
                 c[q][s][0] = c[q][s][1] = c[q][s][2] = c[q][s][3] = 0.f;
                 mma16816(c[q][s], A[s][0], A[s][1], A[s][2], A[s][3], xv[q].x, xv[q].y);
               }
 #pragma unroll
-            for (int q = 0; q < 4; q++)
+            for (int q = 0; q < HQ; q++)
 #pragma unroll
               for (int s = 0; s < 2; s++) mma16816(c[q][s], A[s][0], A[s][1], A[s][2], A[s][3], xv[q].z, xv[q].w);
 #pragma unroll
-            for (int q = 0; q < 4; q++)
+            for (int q = 0; q < HQ; q++)
 #pragma unroll
               for (int s = 0; s < 2; s++) {
                 acc[hq + q][s][0] = fmaf(sc[2 * s], c[q][s][0], acc[hq + q][s][0]);
@@ -429,7 +431,7 @@ __global__ void __launch_bounds__(160, 1) k_q6mm(const uint8_t* __restrict__ w, 
     }
     if (!ok) continue;
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
+    for (int q = 0; q < NGT; q++) {
       if (q >= ng) break;
 #pragma unroll
       for (int s = 0; s < 2; s++)
@@ -464,12 +466,19 @@ E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* c, const uint8_t* w, const float* x, ui
                            NG))
       return r;
     const size_t smem = 2 * (size_t)kLmXSlab + 4 * (size_t)kLmWS * kLmWWarp;
-    cudaError_t e = cudaFuncSetAttribute(k_q6mm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q6mm smem attr: %s", cudaGetErrorString(e));
     const int units = (OUT + kLmRows - 1) / kLmRows * ((NG + 7) / 8);
     const int grid = units < c->sm_count ? units : c->sm_count;
-    return e4b_launch(c, "q6mm", k_q6mm, dim3((unsigned)grid), dim3(160), smem, w, (const uint4*)xp, y, N, OUT, n, NG,
-                      softcap, c->status);
+    // groups computed per step: enough for the widest pass
+    auto launch = [&](auto kern) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q6mm smem attr: %s", cudaGetErrorString(e));
+      return e4b_launch(c, "q6mm", kern, dim3((unsigned)grid), dim3(160), smem, w, (const uint4*)xp, y, N, OUT, n, NG,
+                        softcap, c->status);
+    };
+    if (NG == 1) return launch(k_q6mm<1>);
+    if (NG == 2) return launch(k_q6mm<2>);
+    if (NG <= 4) return launch(k_q6mm<4>);
+    return launch(k_q6mm<8>);
   }
   uint16_t* xh = scratch;
   uint16_t* xl = scratch + (size_t)n * N;

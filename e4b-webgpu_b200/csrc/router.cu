@@ -344,7 +344,7 @@ E4B_API int e4b_routertop(e4b_ctx* c, const float* x, const float* wr, const flo
   if (batch < 1) batch = 1;
   const int slices = (H + kRtK - 1) / kRtK;
   const size_t part_bytes = (size_t)slices * batch * E * 4;
-  if (batch > 1 && c->ws && c->ws_bytes >= e4b::kWsCounterBytes + part_bytes && (size_t)8 * E * 4 <= 48 * 1024) {
+  if (c->ws && c->ws_bytes >= e4b::kWsCounterBytes + part_bytes && (size_t)8 * E * 4 <= 48 * 1024) {
     // the split-K partial area of the workspace (free between launches)
     float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c->ws) + e4b::kWsCounterBytes);
     if (int r = e4b_launch(c, "router_part", k_router_part,

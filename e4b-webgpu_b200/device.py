@@ -72,9 +72,11 @@ class Device:
         rc = getattr(self.L, name)(self.ctx, *conv)
         if rc != 0:
             raise E4BError(name, rc, self.last_error())
+        if name == "e4b_set_workspace":
+            self.has_workspace = bool(conv[0])
         if name not in _RUNTIME:
             n = self.KERNELS.get(name, 1)
-            if name == "e4b_routertop" and args[-1] > 1:
+            if name == "e4b_routertop" and getattr(self, "has_workspace", False):
                 n = 2          # split-K scores + per-token top-K
             self.kernel_launches += n
         return rc

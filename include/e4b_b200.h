@@ -245,8 +245,8 @@ E4B_API int e4b_argmax_merge(e4b_ctx* ctx, const uint32_t* all, int nranks, int 
 /* ------------------------------------------------------------ router */
 /* kernels/routertop.wgsl:19-71: scores = Wr[E][H] . x (f32), softmax, K-way
  * iterative argmax (ties -> lowest index), renormalise, x pes[e].  One token
- * per row of x (batch rows).  batch > 1 with a workspace attached: the scores
- * are a split-K f32 GEMM into the workspace, then a per-token top-K pass (two
+ * per row of x (batch rows).  With a workspace attached the scores are a
+ * split-K f32 GEMM into the workspace, then a per-token top-K pass (two
  * launches). */
 E4B_API int e4b_routertop(e4b_ctx* ctx, const float* x, const float* wr, const float* pes, uint32_t* topk_idx,
                           float* topk_w, int H, int E, int K, int batch);

@@ -35,7 +35,8 @@ def test_batched_moe_decode_matches_oracle(e4b, models, B):
             assert np.linalg.norm(h[b] - href) / np.linalg.norm(href) < 1e-2
 
 
-@pytest.mark.parametrize("V,N,n", [(3000, 512, 11), (1000, 768, 64), (520, 256, 70), (4, 256, 1)])
+@pytest.mark.parametrize("V,N,n", [(3000, 512, 11), (1000, 768, 64), (520, 256, 70), (4, 256, 1), (1000, 768, 1),
+                                   (520, 256, 30)])
 def test_batched_lmhead_rows(e4b, dev, V, N, n):
     """e4b_q6k_lmhead_rows (tensor cores, x as f16 hi + lo) against the oracle q6_K matvec per row;
     V % 8 == 0 takes the staged kernel, other V the direct one."""
