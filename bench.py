@@ -1,6 +1,6 @@
 #!/usr/bin/env python
 """Decode benchmark: bs1 greedy decode tok/s of the E4B-shaped q4_0 model
-(35 layers, H=2048, 8q/2kv x 256, FF 16384, V 262144, PLE
+(benchmark config 2: 35 layers, H=2048, 8q/2kv x 256, FF 16384, V 262144, PLE
 256/layer, 4 sliding (W=512) : 1 global), as a fraction of the HBM roofline.
 
 A step is one decoded token (one pass of the per-token plan).  Flow:
@@ -165,7 +165,7 @@ def token_bytes(cfg, ctx_len: int) -> dict:
 
 
 def bench_config(e4b, args):
-    """BASELINE's config by name; --layers keeps its layer shapes with fewer
+    """The benchmark config by name; --layers keeps its layer shapes with fewer
     layers (small cases for ncu captures)."""
     import dataclasses
     cfg = e4b.config.get(args.config)
@@ -227,7 +227,7 @@ def moe_step_bytes(cfg, B: int, ctx_len: int, zipf: float | None = None) -> dict
 
 
 def run_moe_batch(args, rank, world, local_rank):
-    """BASELINE configs 4/5: B sequences decoded in lockstep through the grouped
+    """benchmark configs 4/5: B sequences decoded in lockstep through the grouped
     MoE path; on N > 1 GPUs expert parallelism (B/N sequences and E/N experts
     per rank, NCCL exchange per MoE layer).  value = tokens of all sequences /
     the slowest rank's device time."""
@@ -647,7 +647,7 @@ def run_trace(args):
 
 
 def run_attn(e4b, dev, args):
-    """BASELINE config 3 on the batched tensor-core attention (e4b_attdec_seq):
+    """benchmark config 3 on the batched tensor-core attention (e4b_attdec_seq):
     GQA 8q / 2kv x 256, f16 K/V N(0,1), KV 4096 / 8192 / 32768, batch 1 and 16,
     global and sliding-window (512) masks.  Bytes = the K/V rows of the live
     chunks; K/V > L2 for the large cases, smaller ones rotate over copies."""
@@ -749,7 +749,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default=None,
-                    help="model config (default: e4b on 1 GPU -- BASELINE config 2; a4b on N > 1 -- config 5)")
+                    help="model config (default: e4b on 1 GPU -- benchmark config 2; a4b on N > 1 -- config 5)")
     ap.add_argument("--prefill", type=int, default=None, help="prompt tokens (default 512 for e4b, 1024 for a4b)")
     ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling cases)")
     ap.add_argument("--batch", type=int, default=None,
@@ -757,7 +757,7 @@ def main():
     ap.add_argument("--ep-overlap", type=int, default=1,
                     help="expert parallel: exchange the rows on a side stream beside the dense FFN (1) or in line (0)")
     ap.add_argument("--zipf", type=float, default=1.1,
-                    help="batched MoE: Zipf(s) expert routing of BASELINE config 5 (0 = the router's top-8)")
+                    help="batched MoE: Zipf(s) expert routing of benchmark config 5 (0 = the router's top-8)")
     ap.add_argument("--fused", type=int, default=1, help="1: fused token kernel where the model allows it; "
                                                           "0: one kernel per operator")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")

@@ -1,4 +1,4 @@
-"""Batched decode of B sequences in lockstep (BASELINE configs 4/5: A4B-shaped
+"""Batched decode of B sequences in lockstep (benchmark configs 4/5: A4B-shaped
 MoE at batch 1/16/64).
 
 All B sequences share the position block (same prompt length, one token per
@@ -87,7 +87,7 @@ class BatchEngine(Engine):
         communicator must build its engine with the same nccl_id (from
         e4b_nccl_unique_id on one rank).  zipf = s: benchmark routing -- each
         layer's experts are drawn from a seeded Zipf(s) popularity instead of
-        the router's top-K; tok0 = this rank's first global
+        the router's top-K (benchmark config 5); tok0 = this rank's first global
         sequence, so any rank count routes identically."""
         self.nseq = int(nseq)
         self.zipf, self.tok0, self.route_seed = zipf, int(tok0), int(route_seed)

@@ -7,7 +7,7 @@ a ring KV cache of `window + ring_slack` slots with full RoPE at theta 10k, glob
 layers use a linear cache with partial RoPE (a quarter of the pairs rotate) at
 theta 1M (src/engine-a4b.js:328-347).
 
-Named shapes:
+Named shapes (benchmark configs):
   tiny      2L, H=512, 4q/1kv x 128, FF 2048, V 4096, all layers global
   e4b       35L, H=2048, 8q/2kv x 256, FF 16384, V 262144, PLE 256/layer,
             4 sliding (W=512) : 1 global
@@ -150,7 +150,7 @@ def _pattern(L: int, period: int) -> list:
 
 
 def tiny() -> ModelConfig:
-    # all-global layers, RoPE theta 10000 with every pair rotating.
+    # benchmark config 1: all-global layers, RoPE theta 10000 with every pair rotating.
     return ModelConfig(name="tiny", arch="dense", hidden=512, layers=2, q_heads=4, kv_heads=1,
                        head_dim=128, ff=2048, vocab=4096, window=0, sliding=[False, False],
                        theta_global=10000.0, rope_frac_global=1.0, max_ctx=1024)

@@ -1,4 +1,4 @@
-// Expert parallelism for the batched MoE decode: experts
+// Expert parallelism for the batched MoE decode (benchmark config 5): experts
 // sharded in contiguous blocks over the ranks of one node, every rank decoding
 // its own sequences (attention and dense layers replicated).  Per MoE layer:
 //   dispatch   each (token, slot) entry's f16 activation row and local expert

@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(256) k_router_topk(const float* __restrict__ p
   softmax_topk(p, E, K, pes, topk_idx + (size_t)b * K, topk_w + (size_t)b * K);
 }
 
-// Skewed routing for the expert-parallel benchmark (a seeded
+// Skewed routing for the expert-parallel benchmark (benchmark config 5: a seeded
 // Zipf(s) load over the experts): token i (global index tok0 + i) at position
 // params[0] of layer `salt` draws K distinct experts by inverse-CDF sampling of
 // Zipf(s) over popularity ranks, mapped to expert ids by a seeded permutation,

@@ -250,7 +250,7 @@ E4B_API int e4b_argmax_merge(e4b_ctx* ctx, const uint32_t* all, int nranks, int 
  * launches). */
 E4B_API int e4b_routertop(e4b_ctx* ctx, const float* x, const float* wr, const float* pes, uint32_t* topk_idx,
                           float* topk_w, int H, int E, int K, int batch);
-/* Benchmark routing (not a reference kernel): replaces the
+/* Benchmark routing (benchmark config 5, not a reference kernel): replaces the
  * router's choice for n_tok tokens with K distinct experts drawn from a seeded
  * Zipf(s) popularity over the E experts (weights 1/K); a pure function of
  * (seed, salt, position params[0], token tok0 + i). */

@@ -5,7 +5,7 @@ Contents:
   * q40_raw / q40_deq, q6k_raw / q6k_deq: seeded q4_0 and q6_K blocks and their
     f32 dequantisation by the python `gguf` package (an independent decoder of
     the GGML block formats), including edge blocks (all-zero, extreme scales);
-  * for the `tiny` (32-token prompt from seed 0, 32 greedy
+  * for the `tiny` (benchmark config 1: 32-token prompt from seed 0, 32 greedy
     tokens) and `tiny_ple` models built by e4b-webgpu_b200/synth.py: the sha256
     of the GGUF image, the prompt, the oracle's greedy ids and top-2 margins, the
     per-step per-layer hidden-state norms of the prompt steps, and the final

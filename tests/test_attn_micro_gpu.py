@@ -1,4 +1,4 @@
-"""split-KV decode attention microbenchmark shapes -- GQA 8
+"""benchmark config 3: split-KV decode attention microbenchmark shapes -- GQA 8
 query / 2 KV heads, head_dim 256, f16 K/V/q drawn N(0,1), one planted key per
 sequence with q.k scaled x8 (a sharp softmax peak), KV lengths 4096 / 8192 /
 32768 at batch 1 and 16, sliding-window (512) and global masking.  The fp32

@@ -63,7 +63,7 @@ def test_teacher_forced_layers(e4b, models, name, fused):
                                             ("tiny_ple", 20, 24, False), ("tiny_ple", 20, 24, True),
                                             ("tiny_moe", 16, 24, False)])
 def test_greedy_ids_match(e4b, models, name, P, N, fused):
-    """BASELINE config 1 shape for tiny: 32-token prompt (seed 0), 32 greedy tokens."""
+    """benchmark config 1 shape for tiny: 32-token prompt (seed 0), 32 greedy tokens."""
     buf = models(name)
     prompt = e4b.synth.prompt_ids(P, e4b.config.get(name).vocab, seed=0)
     eng = e4b.Engine(buf, 0, fused=fused)

@@ -1,4 +1,4 @@
-"""Expert-parallel batched MoE decode on the GPU: the
+"""Expert-parallel batched MoE decode (benchmark config 5) on the GPU: the
 dispatch kernel against the oracle's slab layout, a one-rank NCCL group (the
 full dispatch / exchange / return path on one GPU) and, where the box has two
 GPUs, two ranks -- each must reproduce the single-GPU BatchEngine exactly."""
