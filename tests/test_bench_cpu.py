@@ -1,0 +1,46 @@
+"""The algorithmic byte counts behind bench.py's roofline fields (no GPU)."""
+import importlib
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def bench():
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    return importlib.import_module("bench")
+
+
+def test_expected_unique_experts(bench):
+    # uniform top-K without replacement: E (1 - (1 - K/E)^B)
+    assert bench.expected_unique_experts(128, 8, 1, None) == pytest.approx(8.0)
+    assert bench.expected_unique_experts(128, 8, 64, None) == pytest.approx(125.9, abs=0.1)
+    # the Zipf(1.1) benchmark routing concentrates the load on fewer experts
+    z = bench.expected_unique_experts(128, 8, 64, 1.1, trials=20)
+    assert 60 < z < 125
+
+
+def test_moe_step_bytes_a4b(bench):
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    cfg = e4b.config.get("a4b")
+    b = bench.moe_step_bytes(cfg, 64, 1043)
+    # per layer: q|k|v, o, dense gate|up and down, router in f32; experts by unique count
+    assert b["lm_head"] == 262144 * 2816 // 256 * 210
+    assert b["embed"] == 64 * 2816 // 256 * 210
+    assert 12.4e9 < b["expert_weights"] < 12.8e9
+    assert 7.0e9 < b["kv"] < 8.0e9         # K and V per sliding layer, one shared cache per global layer
+    assert b["total"] == b["weights"] + b["lm_head"] + b["embed"] + b["kv"]
+    assert 21.0e9 < b["total"] < 22.5e9
+    # batch 1 touches 8 experts per layer
+    b1 = bench.moe_step_bytes(cfg, 1, 1043)
+    assert b1["unique_experts_per_layer"] == pytest.approx(8.0)
+    assert b1["total"] < 3.0e9
+
+
+def test_moe_metric_names(bench):
+    assert bench.moe_metric(64, 1).startswith("MoE decode tok/s bs64")
+    assert "expert parallel" in bench.moe_metric(64, 8)
