@@ -242,6 +242,10 @@ def run_moe_batch(args, rank, world, local_rank):
         raise SystemExit(f"--batch {B} does not split over {world} GPUs")
     nloc = B // world
     zipf = args.zipf if args.zipf > 0 else None
+    need = args.prefill + args.warmup + 2 * args.steps      # prefill, warm-up, timed and end-to-end tokens
+    if need > cfg.max_ctx:
+        raise SystemExit(f"{need} positions exceed the {cfg.max_ctx}-slot global-layer KV cache of {cfg.name}; "
+                         f"use fewer --steps / --warmup / --prefill")
     t0 = time.time()
     if world > 1:
         # one rank synthesises the image into a shared file, the others map it
@@ -362,6 +366,35 @@ def run_moe_batch(args, rank, world, local_rank):
     }
     dist.close()
     return out, img, cfg
+
+
+def wants_moe_point(args, world: int, config_given: bool, prefill_given: bool) -> bool:
+    """The default one-GPU run (no --config / --prefill / --layers) also
+    measures the N = 1 point of the batch-64 expert-parallel series, so a
+    scaling sweep over --gpus 1, 2, 4, 8 carries both ends of its ratio."""
+    return (world == 1 and args.impl == "ours" and not config_given and not prefill_given and not args.layers
+            and not args.no_moe_point)
+
+
+def moe_point(args, local_rank) -> dict:
+    """Benchmark config 5's workload (A4B, 64 sequences, 1024-token prefill,
+    Zipf(1.1) routing) on this one GPU: what `--gpus N` reports for N > 1.
+    Scaling efficiency at N GPUs = value(N) / (N x this value)."""
+    import copy
+    a = copy.copy(args)
+    a.config, a.batch, a.prefill, a.layers, a.zipf = "a4b", 64, 1024, 0, 1.1
+    cap = importlib.import_module("e4b-webgpu_b200").config.get("a4b").max_ctx
+    a.steps = max(1, min(args.steps, (cap - a.prefill - args.warmup) // 2))
+    try:
+        out, _, _ = run_moe_batch(a, 0, 1, local_rank)
+    except Exception as e:  # the headline line still prints; the failure is recorded beside it
+        return {"error": f"{type(e).__name__}: {e}"}
+    keep = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "config", "e2e", "clocks",
+            "gpu_launches", "prefill_s", "model_build_s")
+    pt = {k: out[k] for k in keep}
+    pt["roofline"] = {k: out["roofline"][k] for k in ("bound", "achieved", "peak", "unit", "frac")}
+    pt["note"] = "N = 1 point of the expert-parallel series (bench.py --gpus N); efficiency(N) = value(N) / (N x value)"
+    return pt
 
 
 def run_ours(args, rank, world, local_rank):
@@ -762,6 +795,8 @@ def main():
                                                           "0: one kernel per operator")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-moe-point", action="store_true",
+                    help="default one-GPU run: skip the batch-64 expert-parallel series' N = 1 point")
     ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain", "attn"], help="time one kernel alone instead of the decode")
     ap.add_argument("--trace", action="store_true", help="per-phase timing of the fused token kernel")
     ap.add_argument("--launches", type=int, default=200)
@@ -771,6 +806,7 @@ def main():
     ap.add_argument("--variant", type=int, default=0, help="GEMV variant (warps x piece blocks): 0=8x32 1=16x16 2=16x8")
     args = ap.parse_args()
     rank, world, local_rank = dist_env()
+    config_given, prefill_given = args.config is not None, args.prefill is not None
     if args.config is None:
         args.config = "e4b" if world == 1 else "a4b"
     if args.batch is None:
@@ -801,6 +837,9 @@ def main():
         out, img, cfg = run_ours(args, rank, world, local_rank)
         if rank == 0:
             out["cpu_baseline"] = None if (args.no_cpu or world > 1) else cpu_baseline(img, cfg, args.cpu_budget, 64)
+        if wants_moe_point(args, world, config_given, prefill_given):
+            del img
+            out["moe_ep_series_1gpu"] = moe_point(args, local_rank)
     if rank == 0 and out is not None:
         print(json.dumps(out), flush=True)
 

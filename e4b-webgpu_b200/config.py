@@ -165,7 +165,7 @@ def e4b() -> ModelConfig:
 def a4b() -> ModelConfig:
     return ModelConfig(name="a4b", arch="moe", hidden=2816, layers=30, q_heads=16, kv_heads=4,
                        head_dim=256, ff=2112, vocab=262144, window=1024, sliding=_pattern(30, 6),
-                       experts=128, topk=8, expert_ff=704, keqv_global=True, max_ctx=2048)
+                       experts=128, topk=8, expert_ff=704, keqv_global=True, max_ctx=4096)
 
 
 def tiny_ple() -> ModelConfig:

@@ -44,3 +44,15 @@ def test_moe_step_bytes_a4b(bench):
 def test_moe_metric_names(bench):
     assert bench.moe_metric(64, 1).startswith("MoE decode tok/s bs64")
     assert "expert parallel" in bench.moe_metric(64, 8)
+
+
+def test_moe_point_only_on_the_default_one_gpu_run(bench):
+    import argparse
+    a = argparse.Namespace(impl="ours", layers=0, no_moe_point=False)
+    assert bench.wants_moe_point(a, 1, False, False)
+    assert not bench.wants_moe_point(a, 2, False, False)          # N > 1 lines are the series itself
+    assert not bench.wants_moe_point(a, 1, True, False)           # an explicit --config
+    assert not bench.wants_moe_point(a, 1, False, True)           # profiling cases pass --prefill
+    assert not bench.wants_moe_point(argparse.Namespace(impl="ours", layers=4, no_moe_point=False), 1, False, False)
+    assert not bench.wants_moe_point(argparse.Namespace(impl="reference", layers=0, no_moe_point=False), 1, False, False)
+    assert not bench.wants_moe_point(argparse.Namespace(impl="ours", layers=0, no_moe_point=True), 1, False, False)
