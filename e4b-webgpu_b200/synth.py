@@ -107,8 +107,22 @@ def _fill_normal(seed, name, std):
     return f
 
 
-def build_model(cfg: ModelConfig, seed: int = 0, std: float = 0.02, path: str | None = None) -> np.ndarray:
-    """Build a synthetic GGUF image for `cfg` (in memory, or at `path`); returns the uint8 buffer."""
+def _fill_shifted(seed, name, val, std):
+    def f(out):
+        o = out.view(np.float32)
+        synth_lib().e4b_synth_normal_f32(_f32p(o), o.size, seed, stream_of(name), std)
+        o += np.float32(val)
+    return f
+
+
+def build_model(cfg: ModelConfig, seed: int = 0, std: float = 0.02, path: str | None = None,
+                vec_std: float = 0.0, router_std: float | None = None) -> np.ndarray:
+    """Build a synthetic GGUF image for `cfg` (in memory, or at `path`); returns the uint8 buffer.
+    vec_std > 0 draws every f32 vector (norm weights, router / expert / layer
+    scales) as its constant + N(0, vec_std) instead of the constant, so a test
+    can tell the vectors apart; router_std (default: std) is the router
+    weights' deviation -- larger values give peaked routing with fewer near-tied
+    expert choices.  The benchmark models keep the defaults."""
     w = gguf.GGUFWriter()
     for k, v in cfg.to_kv().items():
         w.add_kv(k, v)
@@ -119,7 +133,7 @@ def build_model(cfg: ModelConfig, seed: int = 0, std: float = 0.02, path: str | 
         w.add_tensor(name, [n_in, n_out], Q4, _fill_q40(seed, name, std))
 
     def vec(name, n, val=1.0):
-        w.add_tensor(name, [n], F32, _fill_const(val))
+        w.add_tensor(name, [n], F32, _fill_const(val) if vec_std <= 0 else _fill_shifted(seed, name, val, vec_std))
 
     w.add_tensor("token_embd.weight", [H, V], Q6, _fill_q6k(seed, "token_embd.weight", std))
     vec("output_norm.weight", H)
@@ -159,7 +173,7 @@ def build_model(cfg: ModelConfig, seed: int = 0, std: float = 0.02, path: str | 
             vec(p + "ffn_gate_inp.scale", H)
             vec(p + "ffn_down_exps.scale", E)
             w.add_tensor(p + "ffn_gate_inp.weight", [H, E], F32,
-                         _fill_normal(seed, p + "ffn_gate_inp.weight", std))
+                         _fill_normal(seed, p + "ffn_gate_inp.weight", std if router_std is None else router_std))
             w.add_tensor(p + "ffn_gate_up_exps.weight", [H, 2 * EF, E], Q4,
                          _fill_q40(seed, p + "ffn_gate_up_exps.weight", std))
             w.add_tensor(p + "ffn_down_exps.weight", [EF, H, E], Q4,

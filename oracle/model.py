@@ -93,8 +93,9 @@ class OracleModel:
         self.kc, self.vc = [], []
         for l in range(self.L):
             n = self.ring(l) if self.sliding[l] else self.max_ctx
-            self.kc.append(np.zeros((n, self.KVH, self.HD), np.float16))
-            self.vc.append(np.zeros((n, self.KVH, self.HD), np.float16))
+            dt = np.float16 if ops.STORE_F16 else F32
+            self.kc.append(np.zeros((n, self.KVH, self.HD), dt))
+            self.vc.append(np.zeros((n, self.KVH, self.HD), dt))
         self.kv_count = 0
 
     # ---- one token
@@ -122,8 +123,8 @@ class OracleModel:
                 slot, cm = pos % self.ring(l), 1
             else:
                 slot, cm = slot_g, 2
-            self.kc[l][slot] = k.astype(np.float16)
-            self.vc[l][slot] = v.astype(np.float16)
+            self.kc[l][slot] = k
+            self.vc[l][slot] = v
             att = ops.decode_attention(q, self.kc[l], self.vc[l], pos, KVH, self.W, self.ring(l), cm, slot_g + 1)
             t = ops.q40mv(self.t(b + "attn_output.weight"), att.reshape(-1), H, QH * HD)
             nxt = self.f(p.format(l + 1) + "attn_norm.weight") if l + 1 < self.L else None
