@@ -131,7 +131,7 @@ def run_case(name: str) -> dict:
         for h in hooks:
             h.remove()
     P, T = len(prompt), len(seq)
-    pos = np.array(sorted({0, P // 2, P - 1, T - 1}), np.int64)
+    pos = np.array(sorted({0, T - 1} if name in pin_cases.FEW_POSITIONS else {0, P // 2, P - 1, T - 1}), np.int64)
     hidden = np.stack([np.stack([hs[l][0, p].numpy() for l in range(cfg.layers)]) for p in pos]).astype(np.float32)
     top_i = np.argsort(-logits, axis=1, kind="stable")[:, :TOPN]
     top_v = np.take_along_axis(logits, top_i, axis=1)
