@@ -56,3 +56,17 @@ def test_moe_point_only_on_the_default_one_gpu_run(bench):
     assert not bench.wants_moe_point(argparse.Namespace(impl="ours", layers=4, no_moe_point=False), 1, False, False)
     assert not bench.wants_moe_point(argparse.Namespace(impl="reference", layers=0, no_moe_point=False), 1, False, False)
     assert not bench.wants_moe_point(argparse.Namespace(impl="ours", layers=0, no_moe_point=True), 1, False, False)
+
+
+def test_reference_arm_prints_its_line():
+    """`bench.py --impl reference` (the CPU restatement timed on the host) on the
+    small config: one JSON line with the contract's keys, no GPU needed."""
+    import json
+    import subprocess
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", "tiny",
+                        "--steps", "2", "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "tok/s" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
