@@ -76,6 +76,21 @@ def test_q40mv(e4b, dev, n_in, rows, xf16):
     assert rel_err(get(dev, y, F32, rows), O.q40mv(raw, x, rows, n_in)) < RTOL
 
 
+def test_q40mv_reference_kat(e4b, dev):
+    """The reference's synthetic q40mv known-answer test (resident-a4b.html:421-456,
+    "mvtest") on the CUDA GEMV: f16 x[i] = ((13 i + 5) mod 17 - 8) / 8 through the
+    A4B down projection shape (2112 -> 2816); every row within f32 accumulation
+    error of the exact per-block sum."""
+    from test_oracle import mvtest_exact, mvtest_x
+    rows, n_in = 2816, 2112
+    raw = q40(e4b, rows, n_in, 41)
+    x = mvtest_x(n_in)
+    y = dev.alloc(rows * 4)
+    e4b.ops.q40mv(dev, up(dev, x.astype(np.float16)), up(dev, raw), None, y, IN=n_in, OUT=rows, XF16=1)
+    exact, mag = mvtest_exact(raw, x, rows, n_in)
+    assert np.all(np.abs(get(dev, y, F32, rows) - exact) <= 1e-5 * mag)
+
+
 def test_q40mv_stream_matches_simple_kernel(e4b, dev):
     """The streaming tensor-core GEMV and the one-warp-per-row kernel agree to
     fp32 summation order on a split-K shape, with the f32-input path too."""

@@ -198,3 +198,35 @@ def test_fragment_order_permutation():
                 assert pos[32 * b + jj] == 32 * b + 8 * t + slot
     x = np.arange(n, dtype=np.float32)
     assert np.array_equal(e4b.batch.from_xfo(e4b.batch.to_xfo(x)), x)
+
+
+def mvtest_x(n):
+    """The reference's synthetic q40mv known-answer input (resident-a4b.html:421-456,
+    "mvtest"): x[i] = ((13 i + 5) mod 17 - 8) / 8, exact in f16."""
+    i = np.arange(n)
+    return (((i * 13 + 5) % 17 - 8) / 8).astype(np.float32)
+
+
+def mvtest_exact(raw, x, rows, n_in):
+    """Row results by the KAT's own rule: per 32-weight block, d x sum((lo - 8) x_j +
+    (hi - 8) x_{j+16}) over the 16 bytes, in float64."""
+    b = raw.reshape(rows, n_in // 32, 18)
+    d = b[:, :, :2].copy().view(np.float16).astype(np.float64)[..., 0]
+    nib = b[:, :, 2:].astype(np.int64)
+    xb = x.astype(np.float64).reshape(n_in // 32, 32)
+    blk = (((nib & 15) - 8) * xb[None, :, :16]).sum(-1) + (((nib >> 4) - 8) * xb[None, :, 16:]).sum(-1)
+    terms = d * blk
+    return terms.sum(-1), np.abs(terms).sum(-1)
+
+
+def test_oracle_q40mv_reference_kat(e4b):
+    """The reference's mvtest at its shape (2112-wide down projection, x as
+    above): the oracle's q4_0 matvec equals the exact per-block sum to f32
+    accumulation error."""
+    rows, n_in = 64, 2112
+    raw = e4b.synth.quant_q4_0(e4b.synth.normal_f32(rows * n_in, 5, "mvtest", 0.02))
+    x = mvtest_x(n_in)
+    assert np.array_equal(x.astype(np.float16).astype(np.float32), x)
+    exact, mag = mvtest_exact(raw, x, rows, n_in)
+    got = O.q40mv(raw, x, rows, n_in)
+    assert np.all(np.abs(got - exact) <= 1e-6 * mag)
