@@ -192,6 +192,10 @@ __global__ void __launch_bounds__(32 * kAW * kAG, 1) k_attdec(const AttP p, cons
       qk = kvh;
       group_sync(grp);
     }
+    // A parity names the barrier's current or immediately preceding phase, so
+    // this item's wait is only meaningful once the stage's previous item (kAS
+    // back, the other group's) has landed: wait for that phase first.
+    if (ok && local >= kAS) ok = mbar_wait(&full[s], (uint32_t)(((local - kAS) / kAS) & 1), p.status);
     if (ok) ok = mbar_wait(&full[s], (uint32_t)((local / kAS) & 1), p.status);
     const uint8_t* Kt = kv + (size_t)s * 2 * tile;
     const uint8_t* Vt = p.keqv ? Kt : Kt + tile;
