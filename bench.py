@@ -279,7 +279,9 @@ def run_moe_batch(args, rank, world, local_rank):
             nid = e4b.batch.nccl_unique_id(probe)
             probe.close()
         ep = (world, rank, dist.bcast_bytes(nid))
-    eng = e4b.BatchEngine(img, nloc, local_rank, ep=ep, zipf=zipf, tok0=rank * nloc, ep_overlap=bool(args.ep_overlap))
+    transport = args.ep_transport if world > 1 else "nccl"
+    eng = e4b.BatchEngine(img, nloc, local_rank, ep=ep, zipf=zipf, tok0=rank * nloc, ep_overlap=bool(args.ep_overlap),
+                          ep_transport=transport)
     dev = eng.dev
     prompts = np.stack([e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=1000 + b)
                         for b in range(rank * nloc, (rank + 1) * nloc)])
@@ -353,6 +355,8 @@ def run_moe_batch(args, rank, world, local_rank):
                                + (f", {nloc} per GPU, {cfg.experts // world} experts per GPU" if world > 1 else ""),
                    "model": cfg.name, "global_batch": B, "seq_len": ctx_mid,
                    "parallelism": f"ep{world}" if world > 1 else "single",
+                   "exchange": ("peer memory (CUDA IPC)" if transport == "p2p" else "NCCL send/recv") if world > 1
+                   else None,
                    "routing": f"zipf{zipf}" if zipf else "router top-8",
                    "l2": "weights (%.1f GB/step) >> 126 MB L2: no flush needed" % (sb["total"] / 1e9)},
         "e2e": {"value": round(B * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B + 32 * world,
@@ -789,6 +793,8 @@ def main():
                     help="sequences decoded in lockstep (default 1 on 1 GPU, 64 -- expert parallel -- on N > 1)")
     ap.add_argument("--ep-overlap", type=int, default=1,
                     help="expert parallel: exchange the rows on a side stream beside the dense FFN (1) or in line (0)")
+    ap.add_argument("--ep-transport", choices=["nccl", "p2p"], default="nccl",
+                    help="expert parallel: slabs by NCCL send/recv, or stored into the peers' memory (CUDA IPC)")
     ap.add_argument("--zipf", type=float, default=1.1,
                     help="batched MoE: Zipf(s) expert routing of benchmark config 5 (0 = the router's top-8)")
     ap.add_argument("--fused", type=int, default=1, help="1: fused token kernel where the model allows it; "

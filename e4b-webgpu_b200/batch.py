@@ -80,7 +80,7 @@ def from_xfo(x: np.ndarray) -> np.ndarray:
 
 class BatchEngine(Engine):
     def __init__(self, src, nseq: int, device=0, *, chunk: int = 64, ep=None, zipf: float | None = None,
-                 tok0: int = 0, route_seed: int = 1234, ep_overlap: bool = True):
+                 tok0: int = 0, route_seed: int = 1234, ep_overlap: bool = True, ep_transport: str = "nccl"):
         """nseq sequences decoded in lockstep on this GPU.  ep = (nranks, rank,
         nccl_id): expert parallelism -- this rank decodes its nseq sequences and
         owns experts [rank*E/nranks, (rank+1)*E/nranks); every rank of the
@@ -88,7 +88,14 @@ class BatchEngine(Engine):
         e4b_nccl_unique_id on one rank).  zipf = s: benchmark routing -- each
         layer's experts are drawn from a seeded Zipf(s) popularity instead of
         the router's top-K (benchmark config 5); tok0 = this rank's first global
-        sequence, so any rank count routes identically."""
+        sequence, so any rank count routes identically.  ep_transport: "nccl"
+        (grouped send/recv of the slabs) or "p2p" (rows and results stored
+        straight into the peers' slabs through CUDA IPC mappings, device-side
+        epoch flags; 2 or more ranks, one process per GPU)."""
+        if ep_transport not in ("nccl", "p2p"):
+            raise ValueError(f"ep_transport {ep_transport!r}: 'nccl' or 'p2p'")
+        self.ep_transport = ep_transport
+        self._ipc_open = []
         self.nseq = int(nseq)
         self.zipf, self.tok0, self.route_seed = zipf, int(tok0), int(route_seed)
         self.ep_overlap = bool(ep_overlap)     # row exchange on a side stream beside the dense FFN
@@ -171,7 +178,9 @@ class BatchEngine(Engine):
         self.e_loc = E // N
         self.cap = B * K                       # every entry of this rank could go to one peer
         rows = N * self.cap
-        A.ep_sx = d.alloc(rows * H * 2, "epSendX")
+        if self.ep_transport == "nccl":          # the peer-memory transport stores rows and results directly
+            A.ep_sx = d.alloc(rows * H * 2, "epSendX")
+            A.ep_sy = d.alloc(rows * H * 4, "epSendY")
         A.ep_rx = d.alloc(rows * H * 2, "epRecvX")
         A.ep_sid = d.alloc(rows * 4, "epSendIds")
         A.ep_rid = d.alloc(rows * 4, "epRecvIds")
@@ -181,10 +190,11 @@ class BatchEngine(Engine):
         A.ep_inv = d.alloc(rows * 4, "epInv")
         A.ep_gl = d.alloc(rows * EF * 2, "epGeglu")
         A.ep_y = d.alloc(rows * H * 4, "epY")
-        A.ep_sy = d.alloc(rows * H * 4, "epSendY")
         A.ep_ry = d.alloc(rows * H * 4, "epRecvY")
         idbuf = (ctypes.c_uint8 * 128).from_buffer_copy(nid)
         d.call("e4b_nccl_init", N, rank, ctypes.cast(idbuf, ctypes.c_void_p))
+        if self.ep_transport == "p2p":
+            self._map_peers(A, N, rank)
         # this rank's experts inside the full expert tensors
         per_gu = 2 * EF * (H // 32) * 18
         per_dn = H * (EF // 32) * 18
@@ -205,6 +215,50 @@ class BatchEngine(Engine):
             A.amax_all = d.alloc(N * Bt * 8, "amaxAll")
             self.emb_shard = ctypes.c_void_p(self.emb.ptr + rank * Vs * (H // 256) * 210)
 
+    def _map_peers(self, A, N: int, rank: int):
+        """Peer-memory transport: export this rank's receive slabs and flag
+        arrays, gather every rank's handles (NCCL), map the peers' buffers and
+        upload the address tables (rows, ids, results, dispatch flags, return
+        flags: nranks addresses each)."""
+        if N < 2:
+            raise ValueError("the peer-memory transport needs 2 or more ranks")
+        d = self.dev
+        A.ep_flag_d = d.alloc(N * 4, "epFlagDispatch")
+        A.ep_flag_r = d.alloc(N * 4, "epFlagReturn")
+        A.ep_ctr = d.alloc(16, "epCounters")         # [dispatch epoch, arrivals, return epoch, arrivals]
+        mine = [A.ep_rx, A.ep_rid, A.ep_ry, A.ep_flag_d, A.ep_flag_r]
+        hs = np.zeros((len(mine), 64), np.uint8)
+        for k, b in enumerate(mine):
+            d.call("e4b_ipc_handle", b.ptr, hs[k].ctypes.data_as(ctypes.c_void_p))
+        sbuf, rbuf = d.upload(hs.reshape(-1), "ipcHandles"), d.alloc(N * hs.size, "ipcHandlesAll")
+        d.call("e4b_ep_allgather", sbuf, rbuf, ctypes.c_size_t(hs.size))
+        d.sync()
+        allh = np.ascontiguousarray(d.read(rbuf, np.uint8, N * hs.size).reshape(N, len(mine), 64))
+        table = np.zeros((len(mine), N), np.uint64)
+        for r in range(N):
+            for k, b in enumerate(mine):
+                if r == rank:
+                    table[k, r] = b.ptr
+                    continue
+                p = ctypes.c_void_p()
+                d.call("e4b_ipc_open", allh[r, k].ctypes.data_as(ctypes.c_void_p), ctypes.byref(p))
+                self._ipc_open.append(p.value)
+                table[k, r] = p.value
+        A.ep_tab = [d.upload(table[k], f"epPeers{k}") for k in range(len(mine))]
+
+    def close(self):
+        if self._ipc_open:
+            # every rank has finished its stores into peer memory before a mapping goes away
+            d = self.dev
+            d.sync()
+            one, all_ = d.alloc(4, "closeBarrier"), d.alloc(4 * self.ep[0], "closeBarrierAll")
+            d.call("e4b_ep_allgather", one, all_, ctypes.c_size_t(4))
+            d.sync()
+            for p in self._ipc_open:
+                d.call("e4b_ipc_close", ctypes.c_void_p(p))
+            self._ipc_open = []
+        super().close()
+
     def _timed(self, what, *args):
         """Queue a call; inside exchange_time() bracket it with events."""
         d, xev = self.dev, getattr(self, "_xev", None)
@@ -221,8 +275,13 @@ class BatchEngine(Engine):
         """Dispatch this layer's entries and start the exchange of rows + expert
         ids (one NCCL group on the side stream)."""
         c, d, A, B = self.cfg, self.dev, self.A, self.nseq
-        N = self.ep[0]
+        N, rank = self.ep[0], self.ep[1]
         H, E, K = c.hidden, c.experts, c.topk
+        if self.ep_transport == "p2p":
+            d.call("e4b_ep_dispatch", A.topk_idx, B, K, E, N, self.cap, A.moe_in, H, None, A.ep_sid, A.ep_slot)
+            d.call("e4b_ep_push", A.ep_slot, B, K, A.moe_in, H, A.ep_sid, N, rank, self.cap, A.ep_tab[0], A.ep_tab[1],
+                   A.ep_tab[3], A.ep_ctr)
+            return
         d.call("e4b_ep_dispatch", A.topk_idx, B, K, E, N, self.cap, A.moe_in, H, A.ep_sx, A.ep_sid, A.ep_slot)
         d.call("e4b_ep_exchange2_async", A.ep_sx, A.ep_rx, ctypes.c_size_t(self.cap * H * 2), A.ep_sid, A.ep_rid,
                ctypes.c_size_t(self.cap * 4))
@@ -231,13 +290,22 @@ class BatchEngine(Engine):
         """Wait for the rows, run this rank's experts on them, send each result
         back to its slab slot; returns (result rows, entry -> row map)."""
         c, d, A = self.cfg, self.dev, self.A
-        N = self.ep[0]
+        N, rank = self.ep[0], self.ep[1]
         H, EF = c.hidden, c.expert_ff
         rows = N * self.cap
-        self._timed("e4b_ep_join")
+        p2p = self.ep_transport == "p2p"
+        if p2p:
+            self._timed("e4b_ep_wait", A.ep_flag_d, A.ep_ctr, N)
+        else:
+            self._timed("e4b_ep_join")
         d.call("e4b_expgroup", A.ep_rid, rows, 1, self.e_loc, A.ep_off, A.ep_ent, A.ep_inv)
         d.call("e4b_q40gugrp", A.ep_rx, L.gu_loc, A.ep_off, A.ep_ent, A.ep_gl, H, EF, self.e_loc, 1)
         d.call("e4b_q40downgrp", A.ep_gl, L.dn_loc, A.ep_off, A.ep_ent, A.ep_y, EF, H, self.e_loc)
+        if p2p:
+            d.call("e4b_ep_push_back", A.ep_rid, A.ep_inv, A.ep_y, H, N, rank, self.cap, A.ep_tab[2], A.ep_tab[4],
+                   A.ep_ctr.at(8))
+            self._timed("e4b_ep_wait", A.ep_flag_r, A.ep_ctr.at(8), N)
+            return A.ep_ry, A.ep_slot
         d.call("e4b_ep_return", A.ep_rid, A.ep_inv, A.ep_y, rows, H, A.ep_sy)
         self._timed("e4b_ep_exchange", A.ep_sy, A.ep_ry, ctypes.c_size_t(self.cap * H * 4))
         return A.ep_ry, A.ep_slot

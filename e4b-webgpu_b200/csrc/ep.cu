@@ -12,13 +12,24 @@
 //              slot order exactly as the single-GPU path does.
 // The reference's engine-a4b.js has no multi-GPU path; the per-entry math is
 // the single-GPU kernels', so results are bit-identical for any rank count.
+//
+// Two transports move the slabs.  NCCL: grouped send/recv of the whole slabs.
+// Peer memory: every rank's receive slabs are mapped into the other ranks'
+// address spaces (CUDA IPC), ep_push stores each row straight into its owner's
+// slab (same layout: source rank x cap rows) and publishes an epoch flag in
+// every peer; ep_wait holds the stream until every peer's flag for this rank
+// has reached the same epoch (bounded, status word on time-out).  Epochs count
+// the pushes of each direction on every rank, which all ranks issue in the same
+// order, so no host value is needed and CUDA-graph replays stay valid.
 #include <dlfcn.h>
 #include <nccl.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
+#include "stream.cuh"
 
 namespace {
 
@@ -129,7 +140,8 @@ __global__ void __launch_bounds__(1024) k_ep_dispatch(const uint32_t* __restrict
     }
     __syncthreads();
   }
-  // copy the rows: warp per entry, 16-byte pieces
+  // copy the rows: warp per entry, 16-byte pieces (peer-memory transport: ep_push does it)
+  if (!send_x) return;
   for (int i = warp; i < n; i += 32) {
     const uint32_t sl = slot[i];
     if (sl == kNone) continue;
@@ -159,6 +171,93 @@ __global__ void k_argmax_merge(const uint32_t* __restrict__ all, int nranks, int
     }
     out[2 * b] = bi;
     out[2 * b + 1] = __float_as_uint(bv);
+  }
+}
+
+// ---- peer-memory transport
+E4B_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+E4B_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// After this CTA's stores into peer memory: the last CTA of the grid to get
+// here publishes epoch = ctr[0] + 1 to flag[rank] of every rank's flag array
+// and keeps it in ctr[0] (ctr[1] counts arrivals, zero at rest).
+E4B_DEV void publish_epoch(uint32_t* const* flag, int nranks, int rank, uint32_t* ctr) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t done = atomicAdd(ctr + 1, 1u);
+    if (done == gridDim.x - 1) {
+      __threadfence_system();
+      const uint32_t e = __ldcg(ctr) + 1u;
+      for (int d = 0; d < nranks; d++) st_release_sys(flag[d] + rank, e);
+      ctr[0] = e;
+      ctr[1] = 0u;
+    }
+  }
+}
+
+// Rows of the dispatched entries into their owners' receive slabs: entry i with
+// slot d*cap + pos -> rx[d] row rank*cap + pos; block 0 also writes this rank's
+// id rows send_ids[d*cap, (d+1)*cap) into rid[d] rows rank*cap ... rank*cap + cap.
+__global__ void __launch_bounds__(256) k_ep_push(const uint32_t* __restrict__ slot, int n, int K, int H,
+                                                 const uint16_t* __restrict__ x, const uint32_t* __restrict__ send_ids,
+                                                 int nranks, int rank, int cap, uint16_t* const* rx,
+                                                 uint32_t* const* rid, uint32_t* const* flag, uint32_t* ctr) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int i = blockIdx.x * nw + warp; i < n; i += gridDim.x * nw) {
+    const uint32_t sl = slot[i];
+    if (sl == kNone) continue;
+    const uint32_t d = sl / (uint32_t)cap, pos = sl % (uint32_t)cap;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(i / K) * H);
+    uint4* dst = reinterpret_cast<uint4*>(rx[d] + ((size_t)rank * cap + pos) * H);
+    for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
+  }
+  if (blockIdx.x == 0)
+    for (int j = threadIdx.x; j < nranks * cap; j += blockDim.x)
+      rid[j / cap][(size_t)rank * cap + j % cap] = send_ids[j];
+  publish_epoch(flag, nranks, rank, ctr);
+}
+
+// Result rows back to their sources: received row i = p*cap + pos (from rank p)
+// holding an entry -> ry[p] row rank*cap + pos = y[inv[i]].
+__global__ void __launch_bounds__(256) k_ep_push_back(const uint32_t* __restrict__ ids,
+                                                      const uint32_t* __restrict__ inv, const float* __restrict__ y,
+                                                      int nranks, int rank, int cap, int H, float* const* ry,
+                                                      uint32_t* const* flag, uint32_t* ctr) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int i = blockIdx.x * nw + warp; i < nranks * cap; i += gridDim.x * nw) {
+    if (ids[i] == kNone) continue;
+    const int p = i / cap, pos = i % cap;
+    const float4* src = reinterpret_cast<const float4*>(y + (size_t)inv[i] * H);
+    float4* dst = reinterpret_cast<float4*>(ry[p] + ((size_t)rank * cap + pos) * H);
+    for (int j = lane; j < H / 4; j += 32) dst[j] = src[j];
+  }
+  publish_epoch(flag, nranks, rank, ctr);
+}
+
+// One thread per peer: wait until flag[p] has reached this rank's own epoch
+// ctr[0] (wrap-safe), giving up after ~1 s with E4B_ST_TIMEOUT.
+__global__ void k_ep_wait(const uint32_t* flag, const uint32_t* ctr, int nranks, uint32_t* status) {
+  pdl_wait();
+  const int p = threadIdx.x;
+  if (p >= nranks) return;
+  const uint32_t e = __ldcg(ctr);
+  const uint64_t t0 = e4b::globaltimer_ns();
+  for (uint32_t it = 0;; it++) {
+    if ((int32_t)(ld_acquire_sys(flag + p) - e) >= 0) return;
+    if ((it & 63u) == 63u && e4b::globaltimer_ns() - t0 > 1000000000ull) {
+      set_status(status, E4B_ST_TIMEOUT);
+      return;
+    }
+    __nanosleep(100);
   }
 }
 
@@ -244,8 +343,7 @@ E4B_API int e4b_nccl_destroy(e4b_ctx* c) {
 E4B_API int e4b_ep_dispatch(e4b_ctx* c, const uint32_t* topk, int n_tok, int K, int E, int nranks, int cap,
                             const uint16_t* x, int H, uint16_t* send_x, uint32_t* send_ids, uint32_t* slot) {
   E4B_CHECK_CTX(c);
-  E4B_REQUIRE(c, topk && x && send_x && send_ids && slot && n_tok > 0 && K > 0 && cap > 0,
-              "ep_dispatch: bad args");
+  E4B_REQUIRE(c, topk && x && send_ids && slot && n_tok > 0 && K > 0 && cap > 0, "ep_dispatch: bad args");
   E4B_REQUIRE(c, nranks > 0 && nranks <= 64 && E % nranks == 0, "ep_dispatch: E=%d over %d ranks", E, nranks);
   E4B_REQUIRE(c, H % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(send_x) % 16 == 0,
               "ep_dispatch: rows must be 16-byte aligned");
@@ -340,6 +438,69 @@ E4B_API int e4b_ep_return(e4b_ctx* c, const uint32_t* recv_ids, const uint32_t* 
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, recv_ids && inv && y && send_y && rows > 0 && H % 4 == 0, "ep_return: bad args");
   return e4b_launch(c, "ep_return", k_ep_return, dim3(rows), dim3(256), 0, recv_ids, inv, y, rows, H, send_y);
+}
+
+E4B_API int e4b_ipc_handle(e4b_ctx* c, const void* ptr, uint8_t* out64) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, ptr && out64, "ipc_handle: bad args");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  cudaIpcMemHandle_t h;
+  E4B_CUDA(c, cudaSetDevice(c->device));
+  E4B_CUDA(c, cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)));
+  memcpy(out64, &h, sizeof(h));
+  return E4B_OK;
+}
+
+E4B_API int e4b_ipc_open(e4b_ctx* c, const uint8_t* handle64, void** out) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, handle64 && out, "ipc_open: bad args");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  *out = nullptr;
+  E4B_CUDA(c, cudaSetDevice(c->device));
+  E4B_CUDA(c, cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess));
+  return E4B_OK;
+}
+
+E4B_API int e4b_ipc_close(e4b_ctx* c, void* ptr) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, ptr, "ipc_close: null pointer");
+  E4B_CUDA(c, cudaSetDevice(c->device));
+  E4B_CUDA(c, cudaIpcCloseMemHandle(ptr));
+  return E4B_OK;
+}
+
+E4B_API int e4b_ep_push(e4b_ctx* c, const uint32_t* slot, int n_tok, int K, const uint16_t* x, int H,
+                        const uint32_t* send_ids, int nranks, int rank, int cap, const uint64_t* rx_ptrs,
+                        const uint64_t* rid_ptrs, const uint64_t* flag_ptrs, uint32_t* ctr) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, slot && x && send_ids && rx_ptrs && rid_ptrs && flag_ptrs && ctr && n_tok > 0 && K > 0 && cap > 0,
+              "ep_push: bad args");
+  E4B_REQUIRE(c, nranks > 1 && nranks <= 64 && rank >= 0 && rank < nranks, "ep_push: rank %d of %d", rank, nranks);
+  E4B_REQUIRE(c, H % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0, "ep_push: rows must be 16-byte aligned");
+  const int n = n_tok * K, grid = std::min(std::max((n + 7) / 8, 1), 4 * c->sm_count);
+  return e4b_launch(c, "ep_push", k_ep_push, dim3(grid), dim3(256), 0, slot, n, K, H, x, send_ids, nranks, rank, cap,
+                    reinterpret_cast<uint16_t* const*>(rx_ptrs), reinterpret_cast<uint32_t* const*>(rid_ptrs),
+                    reinterpret_cast<uint32_t* const*>(flag_ptrs), ctr);
+}
+
+E4B_API int e4b_ep_push_back(e4b_ctx* c, const uint32_t* recv_ids, const uint32_t* inv, const float* y, int H,
+                             int nranks, int rank, int cap, const uint64_t* ry_ptrs, const uint64_t* flag_ptrs,
+                             uint32_t* ctr) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, recv_ids && inv && y && ry_ptrs && flag_ptrs && ctr && cap > 0 && H % 4 == 0,
+              "ep_push_back: bad args");
+  E4B_REQUIRE(c, nranks > 1 && nranks <= 64 && rank >= 0 && rank < nranks, "ep_push_back: rank %d of %d", rank,
+              nranks);
+  const int rows = nranks * cap, grid = std::min(std::max((rows + 7) / 8, 1), 4 * c->sm_count);
+  return e4b_launch(c, "ep_push_back", k_ep_push_back, dim3(grid), dim3(256), 0, recv_ids, inv, y, nranks, rank, cap,
+                    H, reinterpret_cast<float* const*>(ry_ptrs), reinterpret_cast<uint32_t* const*>(flag_ptrs), ctr);
+}
+
+E4B_API int e4b_ep_wait(e4b_ctx* c, const uint32_t* flag, const uint32_t* ctr, int nranks) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, flag && ctr && nranks > 1 && nranks <= 64, "ep_wait: bad args");
+  return e4b_launch(c, "ep_wait", k_ep_wait, dim3(1), dim3(64), 0, flag, ctr, nranks, c->status);
 }
 
 }  // extern "C"

@@ -37,7 +37,8 @@ _RUNTIME = {"e4b_create", "e4b_destroy", "e4b_device_info", "e4b_alloc", "e4b_fr
             "e4b_plan_begin", "e4b_plan_end", "e4b_plan_launch", "e4b_plan_destroy", "e4b_set_workspace",
             "e4b_set_option", "e4b_dense_plan_create", "e4b_dense_plan_destroy",
             "e4b_dense_plan_trace", "e4b_dense_plan_phases", "e4b_nccl_init", "e4b_nccl_destroy",
-            "e4b_ep_exchange", "e4b_ep_exchange2_async", "e4b_ep_join", "e4b_ep_allgather"}
+            "e4b_ep_exchange", "e4b_ep_exchange2_async", "e4b_ep_join", "e4b_ep_allgather", "e4b_ipc_handle",
+            "e4b_ipc_open", "e4b_ipc_close"}
 
 
 def _ptr(x):

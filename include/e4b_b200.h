@@ -241,6 +241,33 @@ E4B_API int e4b_ep_return(e4b_ctx* ctx, const uint32_t* recv_ids, const uint32_t
 E4B_API int e4b_ep_allgather(e4b_ctx* ctx, const void* send, void* recv, size_t bytes_per_rank);
 E4B_API int e4b_argmax_merge(e4b_ctx* ctx, const uint32_t* all, int nranks, int ntok, int slice, int row0,
                              int nrows, uint32_t* out);
+/* Peer-memory transport (N >= 2 ranks, one process per GPU, in place of
+ * ep_exchange*): each rank exports its receive slabs (rows, ids, results) and
+ * two flag arrays of nranks u32 with ipc_handle (64 bytes each), the handles
+ * travel by any means (ep_allgather), and every rank opens its peers' with
+ * ipc_open; *_ptrs are device arrays of nranks addresses (this rank's own
+ * buffer at index rank).
+ * ep_dispatch with send_x = NULL fills only send_ids / slot; ep_push then
+ *   stores x[t] of every entry straight into rx_ptrs[d] row rank*cap + pos and
+ *   this rank's ids into rid_ptrs[d] rows rank*cap.., and publishes epoch
+ *   ctr[0] + 1 into flag_ptrs[d][rank] of every rank (ctr: 2 u32 of this rank,
+ *   zero-initialised, one pair per direction).
+ * ep_wait: the stream waits (device side, ~1 s bound, then the TIMEOUT status)
+ *   until flag[p] has reached ctr[0] for every p.
+ * ep_push_back: received row i = p*cap + pos holding an entry -> ry_ptrs[p] row
+ *   rank*cap + pos = y[inv[i]], then the same publication.
+ * Slabs keep the NCCL path's layout, so expgroup / a4btail_wacc read them
+ * unchanged. */
+E4B_API int e4b_ipc_handle(e4b_ctx* ctx, const void* ptr, uint8_t* out64);
+E4B_API int e4b_ipc_open(e4b_ctx* ctx, const uint8_t* handle64, void** out);
+E4B_API int e4b_ipc_close(e4b_ctx* ctx, void* ptr);
+E4B_API int e4b_ep_push(e4b_ctx* ctx, const uint32_t* slot, int n_tok, int K, const uint16_t* x, int H,
+                        const uint32_t* send_ids, int nranks, int rank, int cap, const uint64_t* rx_ptrs,
+                        const uint64_t* rid_ptrs, const uint64_t* flag_ptrs, uint32_t* ctr);
+E4B_API int e4b_ep_push_back(e4b_ctx* ctx, const uint32_t* recv_ids, const uint32_t* inv, const float* y, int H,
+                             int nranks, int rank, int cap, const uint64_t* ry_ptrs, const uint64_t* flag_ptrs,
+                             uint32_t* ctr);
+E4B_API int e4b_ep_wait(e4b_ctx* ctx, const uint32_t* flag, const uint32_t* ctr, int nranks);
 
 /* ------------------------------------------------------------ router */
 /* kernels/routertop.wgsl:19-71: scores = Wr[E][H] . x (f32), softmax, K-way

@@ -76,3 +76,26 @@ def combine(recv_y: np.ndarray, slot: np.ndarray, topk_w: np.ndarray) -> np.ndar
             acc = (acc + F32(topk_w[t, k]) * ys[slot[t * K + k]]).astype(F32)
         m[t] = acc
     return m
+
+
+def exchange(send: list) -> list:
+    """The NCCL all-to-all of fixed slabs: recv[d][p*cap + j] = send[p][d*cap + j]
+    (send[p] of N*cap rows on rank p)."""
+    N = len(send)
+    cap = send[0].shape[0] // N
+    return [np.concatenate([send[p][d * cap:(d + 1) * cap] for p in range(N)]) for d in range(N)]
+
+
+def push(rows_by_entry: list, slots: list, cap: int, template) -> list:
+    """The peer-memory transport (ep_push / ep_push_back): rank p stores the row
+    of each entry with slot d*cap + pos straight into rank d's receive slab at
+    row p*cap + pos; rows not stored keep `template` (unused slots)."""
+    N = len(slots)
+    recv = [np.array(template, copy=True) for _ in range(N)]
+    for p in range(N):
+        for i, sl in enumerate(np.asarray(slots[p]).reshape(-1)):
+            if sl < 0:
+                continue
+            d, pos = divmod(int(sl), cap)
+            recv[d][p * cap + pos] = rows_by_entry[p][i]
+    return recv

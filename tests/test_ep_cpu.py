@@ -104,3 +104,47 @@ def test_ep_exchange_matches_single_process_moe(N):
     for r in range(N):
         # same products and slot order; numpy's f32 dot inside q40mv may sum in another order
         assert np.allclose(got[r], ref[r], rtol=1e-5, atol=1e-6), r
+
+
+@pytest.mark.parametrize("N", [2, 4])
+def test_peer_stores_land_where_the_nccl_exchange_puts_rows(N):
+    """Rows stored by the peer-memory transport (entry with slot d*cap + pos of
+    rank p -> rank d's slab row p*cap + pos) fill the same receive slab as the
+    NCCL exchange of the dispatched send slabs, ids included; the results go back
+    the same way (owner row p*cap + pos -> source p's row owner*cap + pos)."""
+    rng = np.random.default_rng(N)
+    T, K, E, H = 5, 3, 4 * N, 8
+    cap = T * K
+    topks = [np.stack([rng.choice(E, K, replace=False) for _ in range(T)]) for _ in range(N)]
+    xs = [rng.standard_normal((T, H)).astype(np.float32) for _ in range(N)]
+    disp = [EP.dispatch(tk, E, N, cap) for tk in topks]
+    send_x, send_id = [], []
+    for p in range(N):
+        ids, src, slot = disp[p]
+        sx = np.zeros((N * cap, H), np.float32)
+        for d in range(N):
+            for j in range(cap):
+                if src[d, j] >= 0:
+                    sx[d * cap + j] = xs[p][src[d, j] // K]
+        send_x.append(sx)
+        send_id.append(ids.reshape(-1, 1).astype(np.int64))
+    via_nccl = EP.exchange(send_x)
+    ids_nccl = EP.exchange(send_id)
+    rows = [np.repeat(xs[p], K, axis=0) for p in range(N)]
+    via_push = EP.push(rows, [disp[p][2] for p in range(N)], cap, np.zeros((N * cap, H), np.float32))
+    # id rows: every slot of a peer's cap region is written (NONE where unused)
+    ids_push = [np.concatenate([disp[p][0][d].reshape(-1, 1) for p in range(N)]).astype(np.int64) for d in range(N)]
+    for d in range(N):
+        assert np.array_equal(ids_push[d], ids_nccl[d])
+        used = ids_nccl[d][:, 0] != EP.NONE
+        assert np.array_equal(via_push[d][used], via_nccl[d][used])
+    # results: owner d's row p*cap + pos back to source p's row d*cap + pos
+    ys = [rng.standard_normal((N * cap, H)).astype(np.float32) for _ in range(N)]
+    back_nccl = EP.exchange(ys)
+    back_push = [np.zeros((N * cap, H), np.float32) for _ in range(N)]
+    for d in range(N):
+        for i in range(N * cap):
+            p, pos = divmod(i, cap)
+            back_push[p][d * cap + pos] = ys[d][i]
+    for p in range(N):
+        assert np.array_equal(back_push[p], back_nccl[p])

@@ -1,7 +1,10 @@
 """Expert-parallel batched MoE decode (benchmark config 5) on the GPU: the
 dispatch kernel against the oracle's slab layout, a one-rank NCCL group (the
 full dispatch / exchange / return path on one GPU) and, where the box has two
-GPUs, two ranks -- each must reproduce the single-GPU BatchEngine exactly."""
+GPUs, two ranks over each transport (NCCL send/recv; rows and results stored
+into the peers' memory through CUDA IPC) -- each must reproduce the single-GPU
+BatchEngine exactly.  The peer-memory transport needs a process per GPU, so it
+has no one-GPU case."""
 import os
 import socket
 
@@ -33,8 +36,8 @@ def test_ep_dispatch_matches_oracle(e4b, dev):
                 assert np.array_equal(gx[d, p], x[src[d, p] // K])
 
 
-def _run_batch(e4b, buf, prompts, n_new, device, ep=None, zipf=None, tok0=0):
-    eng = e4b.BatchEngine(buf, prompts.shape[0], device, ep=ep, zipf=zipf, tok0=tok0)
+def _run_batch(e4b, buf, prompts, n_new, device, ep=None, zipf=None, tok0=0, transport="nccl"):
+    eng = e4b.BatchEngine(buf, prompts.shape[0], device, ep=ep, zipf=zipf, tok0=tok0, ep_transport=transport)
     try:
         ids = eng.generate(prompts, n_new)
         h = eng.read_hidden()
@@ -68,7 +71,7 @@ def _free_port():
     return port
 
 
-def _ep_rank(rank, N, port, B, P, n_new, q):
+def _ep_rank(rank, N, port, B, P, n_new, q, transport):
     import importlib
     import sys
     import torch.distributed as dist
@@ -89,14 +92,16 @@ def _ep_rank(rank, N, port, B, P, n_new, q):
             obj[0] = e4b.batch.nccl_unique_id(dev)
             dev.close()
         dist.broadcast_object_list(obj, src=0)
-        ids, h = _run_batch(e4b, buf, mine, n_new, rank, ep=(N, rank, obj[0]), zipf=1.1, tok0=rank * (B // N))
+        ids, h = _run_batch(e4b, buf, mine, n_new, rank, ep=(N, rank, obj[0]), zipf=1.1, tok0=rank * (B // N),
+                            transport=transport)
         q.put((rank, ids, h))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_ep_two_ranks_match_single_gpu(e4b, models):
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_ep_two_ranks_match_single_gpu(e4b, models, transport):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -109,7 +114,7 @@ def test_ep_two_ranks_match_single_gpu(e4b, models):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, N, port, B, P, n_new, q)) for r in range(N)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, N, port, B, P, n_new, q, transport)) for r in range(N)]
     for p in procs:
         p.start()
     got = {}
