@@ -245,7 +245,7 @@ class BatchEngine(Engine):
                 self._ipc_open.append(p.value)
                 table[k, r] = p.value
         A.ep_tab = [d.upload(table[k], f"epPeers{k}") for k in range(len(mine))]
-        A.ep_bar, A.ep_bar_all = d.alloc(4, "epBarrier"), d.alloc(4 * N, "epBarrierAll")
+        self._bar = (d.alloc(4, "epBarrier"), d.alloc(4 * N, "epBarrierAll"))
 
     def run_token(self, count: int = 1):
         """As Engine.run_token; with the peer-memory transport every rank first
@@ -254,8 +254,7 @@ class BatchEngine(Engine):
         still preparing its run."""
         self.build_plan()
         if self._ipc_open:
-            A = self.A
-            self.dev.call("e4b_ep_allgather", A.ep_bar, A.ep_bar_all, ctypes.c_size_t(4))
+            self.dev.call("e4b_ep_allgather", self._bar[0], self._bar[1], ctypes.c_size_t(4))
         super().run_token(count)
 
     def close(self):
@@ -263,7 +262,7 @@ class BatchEngine(Engine):
             # every rank has finished its stores into peer memory before a mapping goes away
             d = self.dev
             d.sync()
-            d.call("e4b_ep_allgather", self.A.ep_bar, self.A.ep_bar_all, ctypes.c_size_t(4))
+            d.call("e4b_ep_allgather", self._bar[0], self._bar[1], ctypes.c_size_t(4))
             d.sync()
             for p in self._ipc_open:
                 d.call("e4b_ipc_close", ctypes.c_void_p(p))
