@@ -223,6 +223,7 @@ class BatchEngine(Engine):
         if N < 2:
             raise ValueError("the peer-memory transport needs 2 or more ranks")
         d = self.dev
+        self._bar = (d.alloc(4, "epBarrier"), d.alloc(4 * N, "epBarrierAll"))
         A.ep_flag_d = d.alloc(N * 4, "epFlagDispatch")
         A.ep_flag_r = d.alloc(N * 4, "epFlagReturn")
         A.ep_ctr = d.alloc(16, "epCounters")         # [dispatch epoch, arrivals, return epoch, arrivals]
@@ -245,7 +246,6 @@ class BatchEngine(Engine):
                 self._ipc_open.append(p.value)
                 table[k, r] = p.value
         A.ep_tab = [d.upload(table[k], f"epPeers{k}") for k in range(len(mine))]
-        self._bar = (d.alloc(4, "epBarrier"), d.alloc(4 * N, "epBarrierAll"))
 
     def run_token(self, count: int = 1):
         """As Engine.run_token; with the peer-memory transport every rank first
