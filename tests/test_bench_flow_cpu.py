@@ -1,0 +1,141 @@
+"""bench.py's default flow end to end on the CPU, with the engines replaced by
+stand-ins that answer the calls the timed regions make (events, copies, status):
+the one-GPU line with its batch-64 expert-parallel point, and the MoE line, come
+out as JSON with the contract's keys.  This exercises the host code of the GPU
+paths; the numbers are the stand-ins' and mean nothing."""
+import importlib
+import json
+import os
+import sys
+import types
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+class _Dev:
+    def __init__(self):
+        self.calls = []
+
+    def call(self, name, *args):
+        self.calls.append(name)
+        if name == "e4b_event_elapsed":
+            args[2]._obj.value = 4.0            # ms between the two events
+        return 0
+
+    def sync(self):
+        pass
+
+    def status(self):
+        return 0
+
+    def read(self, buf, dtype, n, offset=0):
+        return np.zeros(n, dtype)
+
+
+def _ptr():
+    return types.SimpleNamespace(ptr=0)
+
+
+class _Engine:
+    """Engine: prefill / decode_chunk / set_params / run_token / read_ring."""
+    def __init__(self, img, device=0, fused=None, **kw):
+        self.dev = _Dev()
+        self.fused, self.plan_mode, self.dense_plan = True, "graph", 0
+        self.kernels_per_token = 5
+        self.A = types.SimpleNamespace(amax=_ptr(), tok=_ptr())
+        self._host_tok_ptr = 0
+        self.host_tok = np.zeros(1, np.uint32)
+
+    def prefill(self, prompt):
+        pass
+
+    def decode_chunk(self, n):
+        pass
+
+    def set_params(self, tok, pos):
+        pass
+
+    def run_token(self, n=1):
+        pass
+
+    def read_ring(self, start, n):
+        return np.zeros(n, np.uint32)
+
+    def close(self):
+        pass
+
+
+class _Batch(_Engine):
+    made = []
+
+    def __init__(self, img, nseq, device=0, **kw):
+        super().__init__(img, device)
+        self.kw = kw
+        self.kernels_per_token = 400
+        _Batch.made.append(kw)
+
+    def step(self, toks, pos):
+        pass
+
+    def exchange_time(self, pos):
+        return 0.0
+
+
+@pytest.fixture
+def bench(monkeypatch):
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    b = importlib.import_module("bench")
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    monkeypatch.setattr(e4b, "Engine", _Engine)
+    monkeypatch.setattr(e4b, "BatchEngine", _Batch)
+    monkeypatch.setattr(e4b.synth, "build_model", lambda cfg, seed=0, **kw: np.zeros(16, np.uint8))
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+        monkeypatch.delenv(k, raising=False)
+    _Batch.made.clear()
+    return b
+
+
+def _run(bench, monkeypatch, capsys, argv):
+    monkeypatch.setattr(sys, "argv", ["bench.py"] + argv)
+    bench.main()
+    return json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+
+
+def test_default_line_with_the_expert_parallel_point(bench, monkeypatch, capsys):
+    line = _run(bench, monkeypatch, capsys, ["--steps", "4", "--warmup", "3", "--no-cpu"])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "e2e", "roofline", "clocks", "gpu_launches"):
+        assert k in line, k
+    assert line["metric"].startswith("decode tok/s bs1 E4B") and line["n_gpus"] == 1
+    assert line["value"] == pytest.approx(4 / 0.004)
+    assert {"bound", "achieved", "peak", "unit", "frac", "traffic"} <= set(line["roofline"])
+    assert line["e2e"]["h2d_bytes_per_step"] == 32 and line["gpu_launches"] == 5 * 4
+    pt = line["moe_ep_series_1gpu"]
+    assert "error" not in pt, pt
+    assert pt["config"]["global_batch"] == 64 and pt["config"]["routing"] == "zipf1.1"
+    assert pt["value"] == pytest.approx(64 * 4 / 0.004)
+    assert _Batch.made[-1]["ep"] is None and _Batch.made[-1]["ep_transport"] == "nccl"
+
+
+def test_profiling_cases_skip_the_point(bench, monkeypatch, capsys):
+    line = _run(bench, monkeypatch, capsys, ["--prefill", "16", "--steps", "4", "--warmup", "3", "--no-cpu"])
+    assert "moe_ep_series_1gpu" not in line and not _Batch.made
+
+
+def test_moe_line(bench, monkeypatch, capsys):
+    line = _run(bench, monkeypatch, capsys, ["--config", "a4b", "--batch", "16", "--zipf", "0", "--steps", "4",
+                                             "--warmup", "3", "--no-cpu"])
+    assert line["metric"].startswith("MoE decode tok/s bs16") and line["config"]["routing"] == "router top-8"
+    assert line["roofline"]["bytes_per_step"]["unique_experts_per_layer"] > 8
+    assert line["e2e"]["h2d_bytes_per_step"] == 4 * 16 + 32 and line["gpu_launches"] == 400 * 4
+
+
+def test_moe_line_refuses_more_positions_than_the_cache(bench, monkeypatch, capsys):
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--config", "a4b", "--batch", "16", "--steps", "2000",
+                                      "--warmup", "3", "--no-cpu"])
+    with pytest.raises(SystemExit):
+        bench.main()
