@@ -1,7 +1,8 @@
-"""bench.py's default flow end to end on the CPU, with the engines replaced by
+"""bench.py's flows end to end on the CPU, with the engines replaced by
 stand-ins that answer the calls the timed regions make (events, copies, status):
-the one-GPU line with its batch-64 expert-parallel point, and the MoE line, come
-out as JSON with the contract's keys.  This exercises the host code of the GPU
+the one-GPU line with its batch-64 expert-parallel point, the MoE line, and the
+two-rank expert-parallel line (gloo plumbing, rank 0 prints) come out as JSON
+with the contract's keys.  This exercises the host code of the GPU
 paths; the numbers are the stand-ins' and mean nothing."""
 import importlib
 import json
@@ -139,3 +140,49 @@ def test_moe_line_refuses_more_positions_than_the_cache(bench, monkeypatch, caps
                                       "--warmup", "3", "--no-cpu"])
     with pytest.raises(SystemExit):
         bench.main()
+
+
+def _rank_main(rank, world, port, q):
+    """One rank of `bench.py --gpus 2` (gloo plumbing, stand-in engines)."""
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    import contextlib
+    import io
+    b = importlib.import_module("bench")
+    e4b = importlib.import_module("e4b-webgpu_b200")
+    e4b.Engine, e4b.BatchEngine = _Engine, _Batch
+    e4b.synth.build_model = lambda cfg, seed=0, **kw: np.zeros(16, np.uint8)
+    e4b.Device = lambda i: types.SimpleNamespace(close=lambda: None)
+    e4b.batch.nccl_unique_id = lambda dev: bytes(128)
+    sys.argv = ["bench.py", "--gpus", str(world), "--steps", "4", "--warmup", "3", "--prefill", "8",
+                "--ep-transport", "p2p"]
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out):
+        b.main()
+    q.put((rank, out.getvalue(), [m["ep"][:2] + (m["ep_transport"],) for m in _Batch.made]))
+
+
+def test_two_rank_moe_line():
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict((r, (o, m)) for r, o, m in (q.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    line = json.loads(got[0][0].strip().splitlines()[-1])
+    assert got[1][0].strip() == ""                      # only rank 0 prints
+    assert line["n_gpus"] == 2 and line["config"]["parallelism"] == "ep2"
+    assert line["config"]["exchange"] == "peer memory (CUDA IPC)"
+    assert line["metric"].startswith("MoE decode tok/s bs64") and "exposed_all_to_all_us_per_step" in line
+    assert got[0][1] == [(2, 0, "p2p")] and got[1][1] == [(2, 1, "p2p")]
