@@ -53,6 +53,11 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
+def under_torchrun() -> bool:
+    """Launched by torch.distributed.run (any --nproc-per-node, 1 included)."""
+    return "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+
+
 class Dist:
     """Barrier and max-over-ranks for N > 1 (torch.distributed is plumbing only)."""
 
@@ -374,30 +379,38 @@ def run_moe_batch(args, rank, world, local_rank):
 
 def wants_moe_point(args, world: int, config_given: bool, prefill_given: bool) -> bool:
     """The default one-GPU run (no --config / --prefill / --layers) also
-    measures the N = 1 point of the batch-64 expert-parallel series, so a
-    scaling sweep over --gpus 1, 2, 4, 8 carries both ends of its ratio."""
+    measures benchmark config 5's workload on this GPU and reports it inside
+    its line, so the BENCH record carries the MoE bs64 single-GPU number too."""
     return (world == 1 and args.impl == "ours" and not config_given and not prefill_given and not args.layers
-            and not args.no_moe_point)
+            and not args.no_moe_point and not under_torchrun())
 
 
-def moe_point(args, local_rank) -> dict:
+def moe_point(args, budget_s: float) -> dict:
     """Benchmark config 5's workload (A4B, 64 sequences, 1024-token prefill,
-    Zipf(1.1) routing) on this one GPU: what `--gpus N` reports for N > 1.
-    Scaling efficiency at N GPUs = value(N) / (N x this value)."""
-    import copy
-    a = copy.copy(args)
-    a.config, a.batch, a.prefill, a.layers, a.zipf = "a4b", 64, 1024, 0, 1.1
+    Zipf(1.1) routing) on this one GPU, run as a child process under a
+    wall-clock budget: a failure or an overrun is recorded beside the headline
+    instead of taking it down."""
     cap = importlib.import_module("e4b-webgpu_b200").config.get("a4b").max_ctx
-    a.steps = max(1, min(args.steps, (cap - a.prefill - args.warmup) // 2))
+    steps = max(1, min(args.steps, (cap - 1024 - args.warmup) // 2))
+    cmd = [sys.executable, os.path.abspath(__file__), "--config", "a4b", "--batch", "64", "--prefill", "1024",
+           "--zipf", "1.1", "--steps", str(steps), "--warmup", str(args.warmup), "--no-cpu"]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "TORCHELASTIC_RUN_ID",
+                                                             "LOCAL_WORLD_SIZE")}
     try:
-        out, _, _ = run_moe_batch(a, 0, 1, local_rank)
-    except Exception as e:  # the headline line still prints; the failure is recorded beside it
-        return {"error": f"{type(e).__name__}: {e}"}
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=budget_s, env=env)
+    except subprocess.TimeoutExpired:
+        return {"error": f"not finished within its {budget_s:.0f} s budget"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        tail = (r.stderr or r.stdout).strip().splitlines()[-3:]
+        return {"error": f"rc {r.returncode}: " + " | ".join(tail)}
+    out = json.loads(lines[-1])
     keep = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "config", "e2e", "clocks",
             "gpu_launches", "prefill_s", "model_build_s")
-    pt = {k: out[k] for k in keep}
+    pt = {k: out[k] for k in keep if k in out}
     pt["roofline"] = {k: out["roofline"][k] for k in ("bound", "achieved", "peak", "unit", "frac")}
-    pt["note"] = "N = 1 point of the expert-parallel series (bench.py --gpus N); efficiency(N) = value(N) / (N x value)"
+    pt["note"] = ("config 5 on one GPU (bench.py --config a4b --batch 64); the scaling series runs the same "
+                  "workload under torchrun at every N, N = 1 included")
     return pt
 
 
@@ -530,57 +543,86 @@ def run_ours(args, rank, world, local_rank):
     return out, img, cfg
 
 
-def cpu_baseline(img, cfg, budget_s: float, max_steps: int):
-    """The oracle (CPU restatement of the reference path) on this host's cores:
-    a short prompt, then timed greedy decode steps (bounded by budget_s)."""
-    from oracle import ops as O
+def oracle_at_context(img, ctx0: int, seed: int = 7):
+    """The oracle model with its KV caches holding `ctx0` positions of seeded
+    N(0, 1) f16 keys / values (the attention work of a decode step at context
+    ctx0, as after a ctx0-token prefill, without spending minutes on a CPU
+    prefill)."""
     from oracle.model import OracleModel
     m = OracleModel(img)
-    lib = O.qlib()
-    cores = int(lib.oracle_threads())
-    prompt = [1, 2, 3, 4]
-    tok = None
-    for p, t in enumerate(prompt):
-        tok, _ = m.step(t, p)
-    pos = len(prompt)
+    rng = np.random.default_rng(seed)
+    for l in range(m.L):
+        n = min(ctx0, m.kc[l].shape[0])
+        m.kc[l][:n] = rng.standard_normal(m.kc[l][:n].shape, dtype=np.float32).astype(m.kc[l].dtype)
+        m.vc[l][:n] = rng.standard_normal(m.vc[l][:n].shape, dtype=np.float32).astype(m.vc[l].dtype)
+    m.kv_count = ctx0
+    return m
+
+
+def cpu_decode(img, ctx0: int, warmup: int, steps: int, budget_s: float):
+    """Greedy decode steps of the oracle (the CPU restatement of the reference
+    path) from context ctx0: `warmup` untimed, then up to `steps` timed ones,
+    stopping early once budget_s of timed work is spent.  Returns (steps done,
+    seconds, cores, last position)."""
+    from oracle import ops as O
+    m = oracle_at_context(img, ctx0)
+    cores = int(O.qlib().oracle_threads())
+    tok, pos = 1, ctx0
+    for _ in range(warmup):
+        tok, _ = m.step(tok, pos)
+        pos += 1
     n, t0 = 0, time.time()
-    while n < max_steps and (time.time() - t0) < budget_s:
+    while n < steps and (n == 0 or time.time() - t0 < budget_s):
         tok, _ = m.step(tok, pos)
         pos += 1
         n += 1
-    dt = time.time() - t0
+    return n, time.time() - t0, cores, pos
+
+
+def cpu_baseline(img, cfg, ctx0: int, budget_s: float, max_steps: int):
+    """The oracle on this host's cores, at the GPU arm's context (bounded sample)."""
+    n, dt, cores, pos = cpu_decode(img, ctx0, 1, max_steps, budget_s)
     return {"value": round(n / dt, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{n} greedy decode steps of {cfg.name} after a {len(prompt)}-token prompt "
-                      f"(context {len(prompt)}..{pos}; attention is <2% of a token's bytes), oracle C q4_0/q6_K "
+            "sample": f"{n} greedy decode steps of {cfg.name} (one sequence) at context {ctx0}..{pos} "
+                      f"(KV caches pre-filled with seeded values), after 1 untimed step; oracle C q4_0/q6_K "
                       f"matvecs on {cores} OpenMP threads + numpy"}
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the reference path's CPU restatement (the oracle; the
+    reference itself is JavaScript + WGSL on WebGPU and cannot run here), on
+    rank 0 only, with every host thread.  One step = one greedy decode token of
+    one sequence at the GPU arm's context; W untimed steps, then K timed ones
+    (capped by a time budget so the arm ends within minutes).  Loads only the
+    host libraries (synthetic weights, oracle), not the CUDA library."""
     if rank != 0:
         return None
     e4b = importlib.import_module("e4b-webgpu_b200")
-    import __graft_entry__
-    __graft_entry__.build()
+    importlib.import_module("e4b-webgpu_b200.build").build_host()
+    from oracle import build as ob
+    ob.build()
     cfg = bench_config(e4b, args)
     img = e4b.synth.build_model(cfg, seed=0)
-    # each "step" of the reference arm is a bounded sample of CPU decode steps
-    steps = max(1, min(args.steps, 16))
-    warm = min(args.warmup, 1)
-    base = cpu_baseline(img, cfg, budget_s=60.0, max_steps=steps + warm)
-    v = base["value"]
+    n, dt, cores, pos = cpu_decode(img, args.prefill, args.warmup, args.steps, budget_s=args.cpu_budget * 6)
+    v = round(n / dt, 4)
+    sample = (f"{n} timed greedy decode steps of {cfg.name} (one sequence) at context "
+              f"{args.prefill + args.warmup}..{pos} after {args.warmup} untimed ones; KV caches pre-filled with "
+              f"seeded values for the {args.prefill}-token prompt; oracle C q4_0/q6_K matvecs on {cores} "
+              f"OpenMP threads + numpy")
     if args.batch > 1 or cfg.moe:
-        # the reference path decodes one token at a time; a batch of independent
-        # sequences runs at its per-token rate (the sample is sequence 0's decode)
+        # the reference path decodes one token of one sequence at a time; a
+        # batch of independent sequences runs at its per-token rate
         metric = moe_metric(args.batch, world)
         workload = f"{cfg.name}: {args.batch} sequences, CPU reference decoding them one token at a time"
     else:
-        metric, workload = METRIC, f"{cfg.name}: bs1 greedy decode"
-    return {"metric": metric, "value": v, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
-            "ms_per_step": round(1000.0 / v, 2) if v else None, "higher_is_better": True,
+        metric, workload = METRIC, f"{cfg.name}: bs1 greedy decode after a {args.prefill}-token prefill"
+    base = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+    return {"metric": metric, "value": v, "unit": "tok/s", "n_gpus": world, "steps": n, "warmup": args.warmup,
+            "ms_per_step": round(1000.0 * dt / n, 2) if n else None, "higher_is_better": True,
             "scaling": "strong" if args.batch > 1 else "weak",
             "vs_baseline": None, "dtype": "q4_0/q6_K weights, f32 accumulate, f16 activations",
             "data": "synthetic (same seeded model as the ours arm)", "impl": "reference",
-            "config": {"workload": workload, "model": cfg.name},
+            "config": {"workload": workload, "model": cfg.name, "seq_len": args.prefill + args.warmup + n // 2},
             "cpu_baseline": base,
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -802,7 +844,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-moe-point", action="store_true",
-                    help="default one-GPU run: skip the batch-64 expert-parallel series' N = 1 point")
+                    help="default one-GPU run: skip the nested config-5 (A4B bs64) measurement")
+    ap.add_argument("--moe-budget", type=float, default=600.0,
+                    help="wall-clock budget (s) of the nested config-5 measurement")
     ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain", "attn"], help="time one kernel alone instead of the decode")
     ap.add_argument("--trace", action="store_true", help="per-phase timing of the fused token kernel")
     ap.add_argument("--launches", type=int, default=200)
@@ -813,10 +857,14 @@ def main():
     args = ap.parse_args()
     rank, world, local_rank = dist_env()
     config_given, prefill_given = args.config is not None, args.prefill is not None
+    # Plain `bench.py --gpus 1`: benchmark config 2 (E4B bs1).  Under torchrun,
+    # at every N including 1: benchmark config 5 (A4B bs64, expert parallel), so
+    # a scaling series compares one workload across N.
+    scale_series = world > 1 or under_torchrun()
     if args.config is None:
-        args.config = "e4b" if world == 1 else "a4b"
+        args.config = "a4b" if scale_series else "e4b"
     if args.batch is None:
-        args.batch = 64 if (world > 1 and args.config == "a4b") else 1
+        args.batch = 64 if (scale_series and args.config == "a4b") else 1
     if args.prefill is None:
         args.prefill = 1024 if args.config == "a4b" else 512
     if world > 1:
@@ -838,14 +886,16 @@ def main():
         # MoE configs (any batch, including 1) run the batched engine
         out, img, cfg = run_moe_batch(args, rank, world, local_rank)
         if rank == 0:   # the CPU baseline is an N = 1 measurement
-            out["cpu_baseline"] = None if (args.no_cpu or world > 1) else cpu_baseline(img, cfg, args.cpu_budget, 8)
+            out["cpu_baseline"] = None if (args.no_cpu or world > 1) else \
+                cpu_baseline(img, cfg, args.prefill, args.cpu_budget, 8)
     else:
         out, img, cfg = run_ours(args, rank, world, local_rank)
         if rank == 0:
-            out["cpu_baseline"] = None if (args.no_cpu or world > 1) else cpu_baseline(img, cfg, args.cpu_budget, 64)
+            out["cpu_baseline"] = None if (args.no_cpu or world > 1) else \
+                cpu_baseline(img, cfg, args.prefill, args.cpu_budget, 64)
         if wants_moe_point(args, world, config_given, prefill_given):
             del img
-            out["moe_ep_series_1gpu"] = moe_point(args, local_rank)
+            out["moe_bs64_1gpu"] = moe_point(args, args.moe_budget)
     if rank == 0 and out is not None:
         print(json.dumps(out), flush=True)
 

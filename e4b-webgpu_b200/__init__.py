@@ -11,7 +11,7 @@ from . import config, gguf, ops, synth  # noqa: F401
 from ._lib import E4BError, lib  # noqa: F401
 from .config import ModelConfig  # noqa: F401
 from .device import Buffer, Device  # noqa: F401
-from .engine import Engine  # noqa: F401
+from .engine import DeviceStatusError, Engine  # noqa: F401
 from .batch import BatchEngine  # noqa: F401
 
-__all__ = ["Engine", "BatchEngine", "Device", "Buffer", "ModelConfig", "E4BError", "config", "gguf", "ops", "synth", "lib"]
+__all__ = ["Engine", "DeviceStatusError", "BatchEngine", "Device", "Buffer", "ModelConfig", "E4BError", "config", "gguf", "ops", "synth", "lib"]

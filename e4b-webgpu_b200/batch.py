@@ -31,7 +31,7 @@ import math
 import numpy as np
 
 from . import ops
-from .engine import Engine, RING_CAP, ARGMAX_PARTS, F32
+from .engine import Engine, RING_CAP, ARGMAX_PARTS, F32, STATUS_EVERY
 
 C = ctypes.c_void_p
 
@@ -417,8 +417,11 @@ class BatchEngine(Engine):
 
     def prefill(self, prompts):
         prompts = np.asarray(prompts)
-        for pos in range(prompts.shape[1]):
+        P = prompts.shape[1]
+        for pos in range(P):
             self.step(prompts[:, pos], pos)
+            if (pos + 1) % STATUS_EVERY == 0 or pos + 1 == P:
+                self.check_status(f"prefill (position {pos})")
 
     def generate(self, prompts, n_new: int):
         """prompts [B][P] (same length) -> [B][n_new] greedy ids."""

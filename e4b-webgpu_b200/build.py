@@ -41,6 +41,17 @@ def _run(cmd):
     return r.stdout + r.stderr
 
 
+def build_host() -> None:
+    """Only the host C library (synthetic weights), for processes that never
+    touch the GPU (the benchmark's CPU reference arm)."""
+    synth_src = os.path.join(CSRC, "synth.c")
+    if _newer(SYNTH, [synth_src]):
+        # -ffp-contract=off: the q4_0 rule x*id + 8.5 must round like the
+        # unfused reference quantiser, so no FMA contraction on the host.
+        _run(["gcc", "-O3", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off", "-std=c11",
+              synth_src, "-o", SYNTH, "-lm"])
+
+
 def build(verbose: bool = False, ptxas_info: bool = False) -> dict:
     os.makedirs(BUILD, exist_ok=True)
     headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) \
@@ -61,12 +72,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> dict:
                 print(" ".join(cmd[-3:]))
     if _newer(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static", "-ldl"])
-    synth_src = os.path.join(CSRC, "synth.c")
-    if _newer(SYNTH, [synth_src]):
-        # -ffp-contract=off: the q4_0 rule x*id + 8.5 must round like the
-        # unfused reference quantiser, so no FMA contraction on the host.
-        _run(["gcc", "-O3", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off", "-std=c11",
-              synth_src, "-o", SYNTH, "-lm"])
+    build_host()
     return logs
 
 

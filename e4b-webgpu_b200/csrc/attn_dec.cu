@@ -39,6 +39,7 @@ struct AttP {
   int QH, KVH, HD, G, window, cachemode, ring, max_chunks, nseq, keqv;
   float scale;
   size_t seq_stride;               // halves between sequences' caches
+  uint64_t wait_ns;                // bound of every wait (time-out -> E4B_ST_TIMEOUT)
 };
 
 // Tiles are HD/64 boxes of [64 slots x 128 bytes] under the 128-byte swizzle:
@@ -92,10 +93,53 @@ constexpr int kAG = 2;             // warp groups per CTA
 
 E4B_DEV void group_sync(int grp) { asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * kAW) : "memory"); }
 
+// Stage ring protocol.  Item `local` of a CTA's run uses stage local % kAS and
+// is that stage's (local / kAS)-th load, i.e. barrier phase local / kAS.  The
+// two groups alternate items and kAS is odd, so consecutive uses of a stage
+// belong to different groups, and a parity wait alone cannot tell phase k from
+// phase k - 2 (a consumer that runs ahead would pass on the stage's previous
+// load).  So the issuing thread publishes, per stage, the item it issued last
+// (release), and a consumer first waits until its own item is the one issued
+// (acquire): the stage's previous item has then been consumed, and the next one
+// cannot be issued before this consumer is done, so the parity of phase
+// local / kAS is unambiguous.  Every wait is bounded and also ends when another
+// CTA has recorded a time-out in the status word.
+E4B_DEV void st_release_cta(int* a, int v) {
+  asm volatile("st.release.cta.shared::cta.s32 [%0], %1;" ::"r"(smem_u32(a)), "r"(v) : "memory");
+}
+E4B_DEV int ld_acquire_cta(const int* a) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.s32 %0, [%1];" : "=r"(v) : "r"(smem_u32(a)) : "memory");
+  return v;
+}
+E4B_DEV bool aborted(const uint32_t* status) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(status) : "memory");
+  return (v & E4B_ST_TIMEOUT) != 0;
+}
+// Spin until `pred()`; false after `limit_ns` (recording E4B_ST_TIMEOUT) or as
+// soon as another CTA has recorded one.
+template <class Pred>
+E4B_DEV bool bounded_spin(Pred pred, uint32_t* status, uint64_t limit_ns) {
+  if (pred()) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; i++) {
+    if (pred()) return true;
+    if ((i & 63u) == 63u) {
+      if (aborted(status)) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        set_status(status, E4B_ST_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(32 * kAW * kAG, 1) k_attdec(const AttP p, const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kAS];
+  __shared__ int issued[kAS];                           // per stage: the item issued into it last
   __shared__ float red_m[kAG][kAW][8], red_l[kAG][kAW][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int grp = warp / kAW, wg = warp % kAW;          // warp group, warp within the group
@@ -111,7 +155,10 @@ __global__ void __launch_bounds__(32 * kAW * kAG, 1) k_attdec(const AttP p, cons
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
     if (!p.keqv) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
-    for (int s = 0; s < kAS; s++) mbar_init(&full[s], 1);
+    for (int s = 0; s < kAS; s++) {
+      mbar_init(&full[s], 1);
+      issued[s] = -1;
+    }
     fence_barrier_init();
   }
   __syncthreads();
@@ -142,6 +189,7 @@ __global__ void __launch_bounds__(32 * kAW * kAG, 1) k_attdec(const AttP p, cons
       tma_load_4d(dk + j * kSub, &kmap, 64 * j, kvh, c * kAC, b, &full[s]);
       if (!p.keqv) tma_load_4d(dk + tile + j * kSub, &vmap, 64 * j, kvh, c * kAC, b, &full[s]);
     }
+    st_release_cta(&issued[s], it);
   };
   if (threadIdx.x == 0)
     for (int k = 0; k < kAS; k++)
@@ -192,11 +240,13 @@ __global__ void __launch_bounds__(32 * kAW * kAG, 1) k_attdec(const AttP p, cons
       qk = kvh;
       group_sync(grp);
     }
-    // A parity names the barrier's current or immediately preceding phase, so
-    // this item's wait is only meaningful once the stage's previous item (kAS
-    // back, the other group's) has landed: wait for that phase first.
-    if (ok && local >= kAS) ok = mbar_wait(&full[s], (uint32_t)(((local - kAS) / kAS) & 1), p.status);
-    if (ok) ok = mbar_wait(&full[s], (uint32_t)((local / kAS) & 1), p.status);
+    // this item issued into its stage (so the stage's previous load is consumed),
+    // then the stage's phase local / kAS complete
+    if (ok) ok = bounded_spin([&] { return ld_acquire_cta(&issued[s]) >= it; }, p.status, p.wait_ns);
+    if (ok) {
+      const uint32_t par = (uint32_t)((local / kAS) & 1);
+      ok = bounded_spin([&] { return mbar_try_wait(&full[s], par); }, p.status, p.wait_ns);
+    }
     const uint8_t* Kt = kv + (size_t)s * 2 * tile;
     const uint8_t* Vt = p.keqv ? Kt : Kt + tile;
     // ---- scores of this warp's 16 slots x the group's heads
@@ -333,6 +383,19 @@ __global__ void __launch_bounds__(32 * kAW * kAG, 1) k_attdec(const AttP p, cons
     group_sync(grp);
     if (gtid == 0 && ok && it + kAS < i1) issue(it + kAS);
   }
+  // After a time-out some issued loads may not have been consumed: let them land
+  // (bounded) before the CTA's shared memory is released.  On the normal path
+  // every issued item was consumed and these waits pass at once.
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int s = 0; s < kAS; s++) {
+      const int last = issued[s];
+      if (last < 0) continue;
+      const uint32_t par = (uint32_t)(((last - i0) / kAS) & 1);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full[s], par) && globaltimer_ns() - t0 < p.wait_ns) {
+      }
+    }
 }
 
 // Phase B over the live chunks: out[h][d] = sum_c o_c e^(m_c - M) / sum_c l_c e^(m_c - M).
@@ -407,6 +470,7 @@ E4B_API int e4b_attdec_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, c
   p.QH = QH; p.KVH = KVH; p.HD = HD; p.G = QH / KVH; p.window = window; p.cachemode = cachemode; p.ring = ring;
   p.max_chunks = max_chunks; p.nseq = nseq; p.keqv = kcache == vcache; p.scale = scale;
   p.seq_stride = (size_t)cache_slots * KVH * HD;
+  p.wait_ns = c->wait_ns;
   CUtensorMap kmap, vmap;
   E4B_REQUIRE(c, cache_map(&kmap, kcache, HD, KVH, cache_slots, nseq), "attdec_seq: K cache tensor map failed");
   if (p.keqv) vmap = kmap;
@@ -416,7 +480,8 @@ E4B_API int e4b_attdec_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, c
   cudaError_t e = cudaFuncSetAttribute(k_attdec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "attdec smem attr: %s", cudaGetErrorString(e));
   const long long most = (long long)nseq * KVH * max_chunks;
-  const int grid = (int)(most < c->sm_count ? most : c->sm_count);
+  const int cap = c->attn_grid_cap > 0 ? c->attn_grid_cap : c->sm_count;
+  const int grid = (int)(most < cap ? most : cap);
   if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW * kAG), smem, p, kmap, vmap)) return r;
   return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(128), (size_t)max_chunks * 4, p, out_h,
                     xfo);

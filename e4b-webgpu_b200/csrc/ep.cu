@@ -244,8 +244,9 @@ __global__ void __launch_bounds__(256) k_ep_push_back(const uint32_t* __restrict
 }
 
 // One thread per peer: wait until flag[p] has reached this rank's own epoch
-// ctr[0] (wrap-safe), giving up after ~1 s with E4B_ST_TIMEOUT.
-__global__ void k_ep_wait(const uint32_t* flag, const uint32_t* ctr, int nranks, uint32_t* status) {
+// ctr[0] (wrap-safe), giving up after limit_ns (the context's "wait_limit_us",
+// default 1 s) with E4B_ST_TIMEOUT.
+__global__ void k_ep_wait(const uint32_t* flag, const uint32_t* ctr, int nranks, uint32_t* status, uint64_t limit_ns) {
   pdl_wait();
   const int p = threadIdx.x;
   if (p >= nranks) return;
@@ -253,7 +254,7 @@ __global__ void k_ep_wait(const uint32_t* flag, const uint32_t* ctr, int nranks,
   const uint64_t t0 = e4b::globaltimer_ns();
   for (uint32_t it = 0;; it++) {
     if ((int32_t)(ld_acquire_sys(flag + p) - e) >= 0) return;
-    if ((it & 63u) == 63u && e4b::globaltimer_ns() - t0 > 1000000000ull) {
+    if ((it & 63u) == 63u && e4b::globaltimer_ns() - t0 > limit_ns) {
       set_status(status, E4B_ST_TIMEOUT);
       return;
     }
@@ -500,7 +501,7 @@ E4B_API int e4b_ep_push_back(e4b_ctx* c, const uint32_t* recv_ids, const uint32_
 E4B_API int e4b_ep_wait(e4b_ctx* c, const uint32_t* flag, const uint32_t* ctr, int nranks) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, flag && ctr && nranks > 1 && nranks <= 64, "ep_wait: bad args");
-  return e4b_launch(c, "ep_wait", k_ep_wait, dim3(1), dim3(64), 0, flag, ctr, nranks, c->status);
+  return e4b_launch(c, "ep_wait", k_ep_wait, dim3(1), dim3(64), 0, flag, ctr, nranks, c->status, c->wait_ns);
 }
 
 }  // extern "C"

@@ -156,6 +156,12 @@ E4B_API int e4b_set_option(e4b_ctx* c, const char* name, int value) {
   } else if (!strcmp(name, "stream_stages")) {
     E4B_REQUIRE(c, value >= 2 && value <= 4, "stream_stages must be 2..4");
     c->stream_stages = value;
+  } else if (!strcmp(name, "attn_grid_cap")) {
+    E4B_REQUIRE(c, value >= 0, "attn_grid_cap must be >= 0 (0 = one CTA per SM)");
+    c->attn_grid_cap = value;
+  } else if (!strcmp(name, "wait_limit_us")) {
+    E4B_REQUIRE(c, value >= 1000 && value <= 10000000, "wait_limit_us must be 1000..10000000");
+    c->wait_ns = (uint64_t)value * 1000ull;
   } else {
     return e4b_fail(c, E4B_EINVAL, "unknown option %s", name);
   }

@@ -30,6 +30,11 @@ from .device import Device
 F32 = np.float32
 RING_CAP = 16384        # greedy-token ring (src/engine-a4b.js:250 uses 1024)
 ARGMAX_PARTS = 256
+STATUS_EVERY = 32       # tokens between reads of the device status word in prefill / decode_chunk
+
+
+class DeviceStatusError(RuntimeError):
+    """A device-side check or bounded wait failed (the status word is nonzero)."""
 
 
 class DenseLayer(ctypes.Structure):
@@ -380,10 +385,27 @@ class Engine:
         """src/engine-a4b.js:781-784"""
         return int(self.dev.read(self.A.amax, np.uint32, 1)[0])
 
-    def decode_chunk(self, count: int):
+    def check_status(self, where: str):
+        """Read (and clear) the device status word; raise if a device-side check
+        or a bounded wait failed since the last read, so a failing kernel stops
+        the run at once instead of being relaunched for every later token."""
+        st = self.dev.status()
+        if st:
+            raise DeviceStatusError(f"{where}: device status word {st:#x} "
+                                    "(1 = index out of range, 2 = a bounded device wait timed out)")
+
+    def decode_chunk(self, count: int, check_every: int = STATUS_EVERY):
         """`count` greedy tokens continuing from the device-side parameters
-        (src/engine-a4b.js:786-823)."""
-        self.run_token(count)
+        (src/engine-a4b.js:786-823); the status word is read every
+        `check_every` tokens (0: only by the caller)."""
+        step = count if check_every <= 0 else check_every
+        done = 0
+        while done < count:
+            n = min(step, count - done)
+            self.run_token(n)
+            done += n
+            if check_every > 0:
+                self.check_status(f"decode_chunk (token {done} of {count})")
 
     def read_ring(self, start: int, n: int) -> np.ndarray:
         return self.dev.read(self.A.ring, np.uint32, n, offset=start * 4)
@@ -406,6 +428,8 @@ class Engine:
             self._hp_next = 0
         for pos, t in enumerate(prompt):
             self.step(int(t), pos)
+            if (pos + 1) % STATUS_EVERY == 0 or pos + 1 == len(prompt):
+                self.check_status(f"prefill (position {pos})")
 
     def generate(self, prompt, n_new: int, eos=None):
         """generateFast (src/engine-a4b.js:826-847): prefill, then greedy decode

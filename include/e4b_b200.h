@@ -81,7 +81,12 @@ E4B_API int e4b_set_workspace(e4b_ctx* ctx, void* ws, size_t bytes); /* ws = NUL
 E4B_API size_t e4b_workspace_bytes(void);
 /* Tuning knobs of the streaming kernels: "stream_ctas_per_sm" (1..2, default 1),
  * "stream_stages" (2..4, default 4), "stream_variant" (GEMV warps per CTA x
- * blocks per staged piece: 0 = 8 x 32, 1 = 16 x 16, 2 = 16 x 8). */
+ * blocks per staged piece: 0 = 8 x 32, 1 = 16 x 16, 2 = 16 x 8).
+ * "attn_grid_cap" (>= 0, default 0 = one CTA per SM): at most this many CTAs for
+ * e4b_attdec_seq, so each CTA runs more items (the stage ring's wrap-around).
+ * "wait_limit_us" (1000..10000000, default 1000000): the bound of the batched
+ * attention's and e4b_ep_wait's device waits, after which the call records
+ * E4B_ST_TIMEOUT in the status word and returns. */
 E4B_API int e4b_set_option(e4b_ctx* ctx, const char* name, int value);
 /* Device status word: nonzero after a device-side check or bounded wait failed;
  * reading it resets it to zero. */

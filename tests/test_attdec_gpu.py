@@ -104,3 +104,35 @@ def test_attdec_fragment_order(e4b, dev):
         dev.sync()
         res[xfo] = dev.read(out, np.uint16, nseq * QH * HD).reshape(nseq, QH * HD)
     assert np.array_equal(e4b.batch.to_xfo(res[0]), res[1])
+
+
+@pytest.mark.parametrize("grid_cap", [1, 2, 3])
+@pytest.mark.parametrize("keqv", [False, True])
+def test_attdec_many_items_per_cta(e4b, dev, grid_cap, keqv):
+    """The stage ring wraps many times: nseq 4 x 4 KV heads x 32 chunks = 512
+    items on 1..3 CTAs (>= 170 items per CTA), so every stage is reused by
+    both warp groups in turn."""
+    QH, KVH, HD, nseq, slots_n = 16, 4, 256, 4, 2048
+    G = QH // KVH
+    rng = np.random.default_rng(11 + grid_cap)
+    q = rng.standard_normal((nseq, QH, HD)).astype(F32) * 0.2
+    kc = rng.standard_normal((nseq, slots_n, KVH, HD)).astype(np.float16)
+    vc = kc if keqv else rng.standard_normal((nseq, slots_n, KVH, HD)).astype(np.float16)
+    params = np.zeros(8, np.uint32)
+    params[0], params[1], params[5] = slots_n - 1, slots_n, slots_n
+    maxch = slots_n // 64
+    bk = dev.upload(kc)
+    bv = bk if keqv else dev.upload(vc)
+    po, pm = dev.alloc(nseq * QH * maxch * HD * 4), dev.alloc(nseq * QH * maxch * 8)
+    out = dev.alloc(nseq * QH * HD * 2)
+    dev.call("e4b_set_option", b"attn_grid_cap", grid_cap)
+    try:
+        dev.call("e4b_attdec_seq", dev.upload(q).ptr, bk.ptr, bv.ptr, dev.upload(params).ptr, po.ptr, pm.ptr, out.ptr,
+                 QH, KVH, HD, 0, 2, 0, maxch, np.float32(1.0), slots_n, nseq, 0)
+        dev.sync()
+    finally:
+        dev.call("e4b_set_option", b"attn_grid_cap", 0)
+    assert dev.status() == 0
+    got = dev.read(out, np.float16, nseq * QH * HD).reshape(nseq, QH, HD).astype(np.float64)
+    ref = reference(q, kc, vc, list(range(slots_n)), G)
+    assert np.max(np.abs(got - ref)) <= 2e-3 * max(1.0, np.max(np.abs(ref)))

@@ -70,3 +70,18 @@ def test_reference_arm_prints_its_line():
     assert line["impl"] == "reference" and line["unit"] == "tok/s" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
+    assert line["steps"] == 2 and line["warmup"] == 3            # the driver's --steps / --warmup
+
+
+def test_reference_arm_does_not_load_the_cuda_library():
+    """The reference arm runs the CPU restatement only: the process maps the
+    host libraries (synthetic weights, oracle) but not libe4b_b200.so."""
+    import subprocess
+    code = ("import sys, runpy; sys.argv = ['bench.py', '--impl', 'reference', '--config', 'tiny', '--steps', '1', "
+            "'--warmup', '3', '--prefill', '8']; runpy.run_path('bench.py', run_name='__main__'); "
+            "maps = open('/proc/self/maps').read(); "
+            "print('CUDA_LIB_MAPPED' if 'libe4b_b200.so' in maps else 'HOST_ONLY'); "
+            "assert 'liboracle_q.so' in maps")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip().splitlines()[-1] == "HOST_ONLY"

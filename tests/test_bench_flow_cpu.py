@@ -94,7 +94,7 @@ def bench(monkeypatch):
     monkeypatch.setattr(e4b, "Engine", _Engine)
     monkeypatch.setattr(e4b, "BatchEngine", _Batch)
     monkeypatch.setattr(e4b.synth, "build_model", lambda cfg, seed=0, **kw: np.zeros(16, np.uint8))
-    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "TORCHELASTIC_RUN_ID", "LOCAL_WORLD_SIZE"):
         monkeypatch.delenv(k, raising=False)
     _Batch.made.clear()
     return b
@@ -106,7 +106,32 @@ def _run(bench, monkeypatch, capsys, argv):
     return json.loads(capsys.readouterr().out.strip().splitlines()[-1])
 
 
+def _child_in_process(bench, monkeypatch, fail=None):
+    """The nested config-5 point runs bench.py as a child process; here the
+    child is bench.main() in this process (same stand-ins), or a failure."""
+    import contextlib
+    import io
+    import subprocess
+
+    def run(cmd, capture_output, text, timeout, env):
+        if fail == "timeout":
+            raise subprocess.TimeoutExpired(cmd, timeout)
+        if fail == "rc":
+            return subprocess.CompletedProcess(cmd, 1, "", "RuntimeError: device status word 0x2 after the run")
+        argv = sys.argv
+        out = io.StringIO()
+        try:
+            sys.argv = ["bench.py"] + cmd[2:]
+            with contextlib.redirect_stdout(out):
+                bench.main()
+        finally:
+            sys.argv = argv
+        return subprocess.CompletedProcess(cmd, 0, out.getvalue(), "")
+    monkeypatch.setattr(bench.subprocess, "run", run)
+
+
 def test_default_line_with_the_expert_parallel_point(bench, monkeypatch, capsys):
+    _child_in_process(bench, monkeypatch)
     line = _run(bench, monkeypatch, capsys, ["--steps", "4", "--warmup", "3", "--no-cpu"])
     for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
               "vs_baseline", "dtype", "data", "config", "e2e", "roofline", "clocks", "gpu_launches"):
@@ -115,16 +140,34 @@ def test_default_line_with_the_expert_parallel_point(bench, monkeypatch, capsys)
     assert line["value"] == pytest.approx(4 / 0.004)
     assert {"bound", "achieved", "peak", "unit", "frac", "traffic"} <= set(line["roofline"])
     assert line["e2e"]["h2d_bytes_per_step"] == 32 and line["gpu_launches"] == 5 * 4
-    pt = line["moe_ep_series_1gpu"]
+    pt = line["moe_bs64_1gpu"]
     assert "error" not in pt, pt
     assert pt["config"]["global_batch"] == 64 and pt["config"]["routing"] == "zipf1.1"
     assert pt["value"] == pytest.approx(64 * 4 / 0.004)
     assert _Batch.made[-1]["ep"] is None and _Batch.made[-1]["ep_transport"] == "nccl"
 
 
+@pytest.mark.parametrize("fail", ["timeout", "rc"])
+def test_failed_point_keeps_the_headline(bench, monkeypatch, capsys, fail):
+    _child_in_process(bench, monkeypatch, fail)
+    line = _run(bench, monkeypatch, capsys, ["--steps", "4", "--warmup", "3", "--no-cpu"])
+    assert line["metric"].startswith("decode tok/s bs1 E4B") and line["value"] == pytest.approx(4 / 0.004)
+    assert "error" in line["moe_bs64_1gpu"]
+
+
+def test_torchrun_one_rank_runs_the_scaling_workload(bench, monkeypatch, capsys):
+    """Under torchrun the N = 1 point of the scaling series is config 5 (A4B
+    bs64, Zipf routing), the same workload as N > 1."""
+    monkeypatch.setenv("TORCHELASTIC_RUN_ID", "x")
+    line = _run(bench, monkeypatch, capsys, ["--gpus", "1", "--steps", "4", "--warmup", "3", "--no-cpu"])
+    assert line["metric"].startswith("MoE decode tok/s bs64") and line["n_gpus"] == 1
+    assert line["config"]["global_batch"] == 64 and line["config"]["routing"] == "zipf1.1"
+    assert line["scaling"] == "strong" and "moe_bs64_1gpu" not in line
+
+
 def test_profiling_cases_skip_the_point(bench, monkeypatch, capsys):
     line = _run(bench, monkeypatch, capsys, ["--prefill", "16", "--steps", "4", "--warmup", "3", "--no-cpu"])
-    assert "moe_ep_series_1gpu" not in line and not _Batch.made
+    assert "moe_bs64_1gpu" not in line and not _Batch.made
 
 
 def test_moe_line(bench, monkeypatch, capsys):
