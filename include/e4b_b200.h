@@ -194,6 +194,17 @@ E4B_API int e4b_q40gugrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, cons
                          const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K);
 E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
                            const uint32_t* entries, float* y, int IN, int OUT, int E);
+/* Batched-prefill q4_0 GEMM on the tcgen05 tensor cores: kernels/q40sg.wgsl:30-124
+ * (TPREC=f32) and, grouped, kernels/q40grpsg32.wgsl:31-129.  x: f16 [M][IN]
+ * row-major (plain order), IN a multiple of 64, 16-byte aligned.  w: q4_0
+ * [groups][rows][IN] with rows = OUT (epi 0) or 2*OUT ([gate OUT | up OUT],
+ * epi 1).  groups == 1: one matrix over rows [0, M) (offsets may be NULL);
+ * groups > 1 (<= 256): rows [offsets[g], offsets[g+1]) of x use matrix g
+ * (offsets: device u32 [groups+1], e.g. from e4b_expgroup).  epi 0: y f32
+ * [M][OUT] = W x; epi 1: yh f16 [M][OUT] = f16(gelu(gate) * up).  Weights are
+ * dequantised exactly (f16 hi + lo), products summed in f32. */
+E4B_API int e4b_q40gemm(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, float* y, uint16_t* yh,
+                        const uint32_t* offsets, int IN, int OUT, int M, int groups, int epi);
 /* Dense batched GEMMs on the same tensor-core path (n token rows, f16 x in
  * fragment order):
  * q40mm: y[n][OUT] = W x[n] (f32); q40gumm: yh[n][FF] = f16(gelu(gate)*up) with
