@@ -771,6 +771,64 @@ def run_attn(e4b, dev, args):
         raise SystemExit(f"device status {st:#x}")
 
 
+def tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_tcgemm(e4b, dev, args):
+    """The prefill GEMM (e4b_q40gemm, tcgen05) on one A4B prefill chunk of
+    `--tokens` rows (default 64 sequences x 64 positions): the dense q|k|v, o,
+    gate|up + GeGLU and down projections, and the grouped expert gate|up +
+    GeGLU and down over the chunk's tokens x top-8 entries sorted by expert
+    (uniform routing).  FLOPs = 2 M N K of the useful product; the tensor pipe
+    runs twice that (f16 hi + lo weight halves)."""
+    import ctypes
+    cfg = e4b.config.get("a4b")
+    H, QD, FF, E, K, EF = cfg.hidden, cfg.q_dim, cfg.ff, cfg.experts, cfg.topk, cfg.expert_ff
+    R = args.tokens
+    rng = np.random.default_rng(0)
+    ent = R * K
+    counts = np.bincount(np.stack([rng.choice(E, K, replace=False) for _ in range(R)]).ravel(), minlength=E)
+    offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.uint32)
+    boffs = dev.upload(offs)
+    def q40(rows, n_in, name):
+        return dev.upload(e4b.synth.quant_q4_0(e4b.synth.normal_f32(rows * n_in, 0, name, 0.02)), name)
+    cases = [  # name, IN, OUT, M, groups, epi, weights (rows)
+        ("qkv", H, cfg.qkv_rows(0), R, 1, 0), ("o", QD, H, R, 1, 0), ("dense_gu", H, FF, R, 1, 1),
+        ("dense_down", FF, H, R, 1, 0), ("expert_gu", H, EF, ent, E, 1), ("expert_down", EF, H, ent, E, 0)]
+    peak, kind_p = tensor_peak()
+    rows_out = []
+    for name, IN, OUT, M, groups, epi in cases:
+        wrows = 2 * OUT if epi == 1 else OUT
+        w = q40(groups * wrows, IN, name)
+        x = dev.upload(rng.standard_normal((M, IN), dtype=np.float32).astype(np.float16))
+        y = dev.alloc(M * OUT * (2 if epi else 4))
+        def loop(w=w, x=x, y=y, IN=IN, OUT=OUT, M=M, groups=groups, epi=epi):
+            for _ in range(args.launches):
+                dev.call("e4b_q40gemm", x, w, None if epi else y, y if epi else None,
+                         boffs if groups > 1 else None, IN, OUT, M, groups, epi)
+        us = graph_time(dev, loop) / args.launches
+        flops = 2.0 * M * wrows * IN
+        tf = flops / us / 1e6
+        rows_out.append({"gemm": name, "M": M, "N": wrows, "K": IN, "groups": groups, "us": round(us, 1),
+                         "tflops": round(tf, 1), "frac": round(tf / peak, 4), "tensor_pipe_frac": round(2 * tf / peak, 4)})
+        dev.free(w), dev.free(x), dev.free(y)
+    tot_us = sum(r["us"] for r in rows_out)
+    tot_f = sum(2.0 * r["M"] * r["N"] * r["K"] for r in rows_out)
+    st = dev.status()
+    dev.close()
+    print(json.dumps({"kernel": "tcgemm", "desc": "e4b_q40gemm on one A4B prefill chunk", "tokens": R,
+                      "peak_tflops": peak, "peak_source": kind_p, "cases": rows_out,
+                      "layer_us": round(tot_us, 1), "layer_tflops": round(tot_f / tot_us / 1e6, 1), "status": st}))
+    if st:
+        raise SystemExit(f"device status {st:#x}")
+
+
 def run_kernel(args):
     """Time one streaming kernel alone: `launches` launches cycling over enough
     distinct weight copies that the working set exceeds L2."""
@@ -783,6 +841,8 @@ def run_kernel(args):
         return run_rmschain(e4b, dev, args)
     if args.kernel == "attn":
         return run_attn(e4b, dev, args)
+    if args.kernel == "tcgemm":
+        return run_tcgemm(e4b, dev, args)
     desc, rows, n_in, kind = KERNELS[args.kernel]
     ws = int(dev.L.e4b_workspace_bytes())
     wsb = dev.alloc(ws, "workspace")
@@ -847,7 +907,9 @@ def main():
                     help="default one-GPU run: skip the nested config-5 (A4B bs64) measurement")
     ap.add_argument("--moe-budget", type=float, default=600.0,
                     help="wall-clock budget (s) of the nested config-5 measurement")
-    ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain", "attn"], help="time one kernel alone instead of the decode")
+    ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain", "attn", "tcgemm"],
+                    help="time one kernel alone instead of the decode")
+    ap.add_argument("--tokens", type=int, default=4096, help="--kernel tcgemm: token rows of the prefill chunk")
     ap.add_argument("--trace", action="store_true", help="per-phase timing of the fused token kernel")
     ap.add_argument("--launches", type=int, default=200)
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1/0)")

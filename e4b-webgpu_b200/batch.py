@@ -415,13 +415,119 @@ class BatchEngine(Engine):
         self.set_step(tokens, pos)
         self.run_token(1)
 
-    def prefill(self, prompts):
+    def prefill(self, prompts, chunk: int | None = None):
+        """Fill the KV caches for prompts [B][P] and leave the last position's
+        greedy tokens on the device, ready for decode_chunk at position P
+        (src/engine-a4b.js:549-585).  One GPU: chunked batched prefill (B x C
+        token rows per step, tensor-core GEMMs); expert parallel, or chunk=0:
+        token by token (src/engine-a4b.js:828)."""
         prompts = np.asarray(prompts)
         P = prompts.shape[1]
+        if self.ep is None and chunk != 0:
+            return self.prefill_chunked(prompts, chunk)
         for pos in range(P):
             self.step(prompts[:, pos], pos)
             if (pos + 1) % STATUS_EVERY == 0 or pos + 1 == P:
                 self.check_status(f"prefill (position {pos})")
+
+    def prefill_chunk_len(self) -> int:
+        """Positions per prefill chunk: about 4096 token rows, at most 512
+        positions (the sliding rings hold window + 512 slots, so a chunk never
+        overwrites a slot one of its own queries still needs)."""
+        c = self.cfg
+        lim = 512
+        if any(L.sliding for L in self.layers):
+            lim = min(lim, min(L.ring for L in self.layers if L.sliding) - c.window + 1)
+        return max(1, min(lim, 4096 // self.nseq))
+
+    def _alloc_prefill(self, R: int):
+        c, d, B = self.cfg, self.dev, self.nseq
+        H, QD, FF, E, K, EF = c.hidden, c.q_dim, c.ff, c.experts, c.topk, c.expert_ff
+        if getattr(self, "PA", None) is not None and self.PA.R >= R:
+            return self.PA
+        if getattr(self, "PA", None) is not None:
+            for b in self.PA.bufs:
+                d.free(b)
+        PA = type("PrefillActs", (), {})()
+        PA.R = R
+        maxrows = max(L.qkv_rows for L in self.layers)
+        sizes = dict(tok=R * 4, hidden=R * H * 4, hidden_b=R * H * 4, normed=R * H * 2, qkv=R * maxrows * 4,
+                     q=R * QD * 4, attn=R * QD * 2, o=R * H * 4, router_in=R * H * 4, moe_in=R * H * 2,
+                     topk_idx=R * K * 4, topk_w=R * K * 4, geglu=R * FF * 2, tmp=R * H * 4,
+                     offsets=(E + 1) * 4, entries=R * K * 4, inv=R * K * 4, xs=R * K * H * 2,
+                     gl=R * K * EF * 2, yo=R * K * H * 4, params=32)
+        PA.bufs = []
+        for name, n in sizes.items():
+            b = d.alloc(n, f"pre_{name}", zero=False)
+            setattr(PA, name, b)
+            PA.bufs.append(b)
+        self.PA = PA
+        return PA
+
+    def prefill_chunked(self, prompts, chunk: int | None = None):
+        """Batched prefill (src/engine-a4b.js:467-585): chunks of C positions of
+        all B sequences as B x C position-major token rows (row = p * B + b).
+        Per layer: q|k|v, o, dense gate|up + GeGLU and down as tcgen05 GEMMs over
+        all rows (e4b_q40gemm); head prep writes every row's K/V into its
+        sequence's cache (e4b_headprep_rows); causal attention of the chunk
+        (e4b_attn_prefill); router per row; the rows' B x C x K expert entries
+        sorted by expert, their activation rows gathered contiguously, and the
+        grouped expert GEMMs; the combine fused into the layer tail.  After the
+        last chunk, the last position's rows go through the final norm, LM head,
+        argmax and token feedback, so decoding continues at position P."""
+        c, d, B = self.cfg, self.dev, self.nseq
+        H, QD, FF, E, K, EF, V = c.hidden, c.q_dim, c.ff, c.experts, c.topk, c.expert_ff, c.vocab
+        prompts = np.asarray(prompts, np.uint32)
+        assert prompts.shape[0] == B
+        P = prompts.shape[1]
+        C = min(chunk or self.prefill_chunk_len(), P)
+        PA = self._alloc_prefill(B * C)
+        eps = ctypes.c_float(c.eps)
+        hp = np.zeros(8, np.uint32)
+        for p0 in range(0, P, C):
+            n = min(C, P - p0)
+            R = B * n
+            d.write(PA.tok, np.ascontiguousarray(prompts[:, p0:p0 + n].T).reshape(-1))
+            hp[:] = (p0, p0 + 1, 0, 0, p0, p0 + 1, 0, 0)
+            d.write(PA.params, hp)
+            d.call("e4b_q6k_embed", self.emb, PA.params, PA.tok, PA.hidden, H, V, ctypes.c_float(F32(math.sqrt(H))),
+                   1, R)
+            d.call("e4b_rmsnorm", PA.hidden, self.layers[0].attn_norm, None, None, PA.normed, H, R, eps, 1, 0, 1)
+            for L in self.layers:
+                nxt = self.layers[L.i + 1].attn_norm if L.i + 1 < c.layers else None
+                d.call("e4b_q40gemm", PA.normed, L.qkv, PA.qkv, None, None, H, L.qkv_rows, R, 1, 0)
+                d.call("e4b_headprep_rows", PA.qkv, L.q_norm, L.k_norm, PA.params, L.kc, L.vc, PA.q, c.q_heads,
+                       c.kv_heads, c.head_dim, L.angles, ctypes.c_float(L.theta), eps, int(L.keqv), L.cachemode,
+                       L.ring, L.slots, B, n)
+                d.call("e4b_attn_prefill", PA.q, L.kc, L.vc, PA.params, PA.attn, c.q_heads, c.kv_heads, c.head_dim,
+                       c.window if L.sliding else 0, L.cachemode, L.ring, ctypes.c_float(1.0), L.slots, B, n)
+                d.call("e4b_q40gemm", PA.attn, L.o, PA.o, None, None, QD, H, R, 1, 0)
+                d.call("e4b_rmsacc3", PA.o, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, PA.hidden, PA.normed,
+                       PA.router_in, PA.moe_in, PA.hidden_b, H, eps, R, 0, 1)
+                d.call("e4b_routertop", PA.router_in, L.wr, L.pes, PA.topk_idx, PA.topk_w, H, E, K, R)
+                if self.zipf:
+                    d.call("e4b_route_zipf_rows", PA.params, PA.topk_idx, PA.topk_w, B, n, K, E,
+                           ctypes.c_float(self.zipf), ctypes.c_uint32(self.route_seed), L.i, self.tok0)
+                d.call("e4b_q40gemm", PA.normed, L.gu, None, PA.geglu, None, H, FF, R, 1, 1)
+                d.call("e4b_q40gemm", PA.geglu, L.down, PA.tmp, None, None, FF, H, R, 1, 0)
+                d.call("e4b_expgroup", PA.topk_idx, R, K, E, PA.offsets, PA.entries, PA.inv)
+                d.call("e4b_gather_rows", PA.moe_in, PA.entries, K, PA.xs, H, R * K, R)
+                d.call("e4b_q40gemm", PA.xs, L.gu_exps, None, PA.gl, PA.offsets, H, EF, R * K, E, 1)
+                d.call("e4b_q40gemm", PA.gl, L.down_exps, PA.yo, None, PA.offsets, EF, H, R * K, E, 0)
+                d.call("e4b_a4btail_wacc", PA.tmp, L.post_ffw1, PA.yo, PA.inv, PA.topk_w, K, L.post_ffw2, L.post_ffw,
+                       PA.hidden_b, nxt if nxt is not None else L.attn_norm, PA.normed, PA.hidden, H, eps,
+                       ctypes.c_float(L.scale), int(nxt is not None), R, 0)
+            self.check_status(f"prefill chunk at position {p0}")
+        # the last position's B rows: final norm, LM head, argmax, token feedback
+        A = self.A
+        last = ctypes.c_void_p(PA.hidden.ptr + (n - 1) * B * H * 4)
+        self.host_params[:] = (P - 1, P, 0, 0, P - 1, P, P - 1, 0)
+        d.write(A.params, self.host_params)
+        d.call("e4b_rmsnorm", last, self.out_norm, A.xf, None, None, H, B, eps, 1, 0, 0)
+        d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)
+        d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
+        d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
+        self.check_status("prefill (last position)")
 
     def generate(self, prompts, n_new: int):
         """prompts [B][P] (same length) -> [B][n_new] greedy ids."""

@@ -16,19 +16,20 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
                            const uint32_t* __restrict__ params, uint16_t* __restrict__ kcache,
                            uint16_t* __restrict__ vcache, float* __restrict__ q_out, int QH, int KVH, int HD,
                            int angles, float theta, float eps, int keqv, int cachemode, int ring, int cache_slots,
-                           uint32_t* status, size_t seq_stride, int nparts, size_t part_stride) {
+                           uint32_t* status, size_t seq_stride, int nparts, size_t part_stride, int nseq) {
   pdl_wait();
   __shared__ float sh[32];
   __shared__ float xv[512];                      // this head's qkv row (the sum of nparts K-part partials)
   const int head = blockIdx.x, b = blockIdx.y;
-  // seq_stride > 0: row b is sequence b at the common position params[0], with
-  // its own cache at kcache / vcache + b * seq_stride; else rows are consecutive
-  // positions of one sequence
+  // seq_stride > 0: row b is sequence b % nseq at position params[0] + b / nseq
+  // (position-major rows of nseq sequences; one position when there are nseq
+  // rows), with its own cache at kcache / vcache + (b % nseq) * seq_stride; else
+  // rows are consecutive positions of one sequence
   if (seq_stride) {
-    kcache += (size_t)b * seq_stride;
-    vcache += (size_t)b * seq_stride;
+    kcache += (size_t)(b % nseq) * seq_stride;
+    vcache += (size_t)(b % nseq) * seq_stride;
   }
-  const uint32_t pb = seq_stride ? 0u : (uint32_t)b;
+  const uint32_t pb = seq_stride ? (uint32_t)(b / nseq) : (uint32_t)b;
   int src = head;
   if (keqv && head >= QH + KVH) src = head - KVH;  // v reads the k slice
   const size_t qkvS = (size_t)(QH + KVH * (2 - keqv)) * HD;
@@ -225,7 +226,7 @@ E4B_API int e4b_headprep(e4b_ctx* c, const float* qkv, const float* qw, const fl
   if (batch < 1) batch = 1;
   return e4b_launch(c, "headprep", k_headprep, dim3(QH + 2 * KVH, batch), dim3(128), 0, qkv, qw, kw, params, kcache,
                     vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring, cache_slots,
-                    c->status, (size_t)0, 1, (size_t)0);
+                    c->status, (size_t)0, 1, (size_t)0, 1);
 }
 
 E4B_API int e4b_headprep_seq(e4b_ctx* c, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
@@ -244,7 +245,27 @@ E4B_API int e4b_headprep_seq(e4b_ctx* c, const float* qkv, const float* qw, cons
   return e4b_launch(c, "headprep_seq", k_headprep, dim3(QH + 2 * KVH, nseq), dim3(128), 0, qkv, qw, kw, params,
                     kcache, vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring,
                     cache_slots, c->status, stride, nparts,
-                    (size_t)nseq * (QH + KVH * (2 - (keqv ? 1 : 0))) * HD);
+                    (size_t)nseq * (QH + KVH * (2 - (keqv ? 1 : 0))) * HD, nseq);
+}
+
+E4B_API int e4b_headprep_rows(e4b_ctx* c, const float* qkv, const float* qw, const float* kw, const uint32_t* params,
+                              uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
+                              int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
+                              int cache_slots, int nseq, int npos) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, qkv && qw && kw && params && kcache && vcache && q_out && nseq > 0 && npos > 0,
+              "headprep_rows: bad args");
+  E4B_REQUIRE(c, HD <= 512 && (long long)nseq * npos <= 65535, "headprep_rows: HD=%d (<= 512), %d rows (<= 65535)",
+              HD, nseq * npos);
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && HD > 0 && HD % 2 == 0 && rope_angles >= 0 &&
+                     rope_angles <= HD / 2 && cache_slots > 0,
+              "headprep_rows: bad geometry QH=%d KVH=%d HD=%d angles=%d", QH, KVH, HD, rope_angles);
+  E4B_REQUIRE(c, cachemode >= 0 && cachemode <= 2 && (cachemode != 1 || (ring > 0 && ring <= cache_slots)),
+              "headprep_rows: bad cache mode %d / ring %d", cachemode, ring);
+  const size_t stride = (size_t)cache_slots * KVH * HD;
+  return e4b_launch(c, "headprep_rows", k_headprep, dim3(QH + 2 * KVH, nseq * npos), dim3(128), 0, qkv, qw, kw,
+                    params, kcache, vcache, q_out, QH, KVH, HD, rope_angles, theta, eps, keqv ? 1 : 0, cachemode, ring,
+                    cache_slots, c->status, stride, 1, (size_t)0, nseq);
 }
 
 E4B_API int e4b_rope(e4b_ctx* c, float* x, const uint32_t* params, int heads, int HD, int rope_angles, float theta) {

@@ -442,6 +442,333 @@ __global__ void k_attcomb_dec(const AttP p, uint16_t* __restrict__ out_h, int xf
   }
 }
 
+// ---------------------------------------------------------------- prefill
+// Causal attention of a batched-prefill chunk: npos consecutive positions of
+// nseq sequences (rows position-major, row = p * nseq + b) whose K/V rows are
+// already in the caches (e4b_headprep_rows), as the reference's prefill runs
+// its attention per prompt token (src/engine-a4b.js:478-479).  Work item =
+// (sequence, KV head, block of kPC / G positions): the block's G heads x
+// positions are the 64 MMA columns, so every K/V tile is read once per block
+// instead of once per query.  Online softmax over the live 64-slot chunks
+// with f32 running (max, sum) per column; the products are k_attdec's (f16
+// K/V x f16 hi + lo q and p, f32 sums).
+constexpr int kPC = 64;                  // query columns per item
+constexpr int kPW = 4;                   // warps per CTA
+
+struct PreP {
+  const float* q;                        // [npos * nseq][QH][HD]
+  const uint32_t* params;                // the chunk's first position (src/engine-a4b.js:697 layout)
+  uint16_t* out;                         // [npos * nseq][QH * HD] f16
+  uint32_t* status;
+  int QH, KVH, HD, G, window, cachemode, ring, nseq, npos, keqv, pb;
+  float scale;
+  uint64_t wait_ns;
+};
+
+struct PreItem {
+  int b, kvh, p0, np, c0, c1;
+};
+E4B_DEV PreItem pre_item(const PreP& p, int it) {
+  const int nqb = (p.npos + p.pb - 1) / p.pb;
+  PreItem I;
+  I.b = it / (p.KVH * nqb);
+  const int rem = it % (p.KVH * nqb);
+  I.kvh = rem / nqb;
+  const int qb = rem % nqb;
+  I.p0 = qb * p.pb;
+  I.np = min(p.pb, p.npos - I.p0);
+  const uint32_t qp_last = p.params[0] + (uint32_t)(I.p0 + I.np - 1);
+  const uint32_t len0 = p.cachemode == 2 ? p.params[5] : p.params[1];
+  if (p.cachemode == 1) {
+    I.c0 = 0;
+    I.c1 = (int)((min(qp_last + 1, (uint32_t)p.ring) + kAC - 1) / kAC);
+  } else {
+    const uint32_t len_first = len0 + (uint32_t)I.p0, len_last = len0 + (uint32_t)(I.p0 + I.np - 1);
+    I.c0 = (p.cachemode == 0 && p.window > 0 && len_first > (uint32_t)p.window)
+               ? (int)((len_first - (uint32_t)p.window) / kAC) : 0;
+    I.c1 = (int)((len_last + kAC - 1) / kAC);
+  }
+  I.c1 = max(I.c1, I.c0 + 1);         // every item consumes at least one load (issuer and consumers agree)
+  return I;
+}
+
+__global__ void __launch_bounds__(32 * kPW, 1) k_attpre(const PreP p, const __grid_constant__ CUtensorMap kmap,
+                                                        const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ float red_m[kPW][kPC], red_l[kPW][kPC], m_run[kPC], l_run[kPC];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tile = (p.HD / 64) * kSub;
+  uint8_t* kv = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);          // [2 stages][K tile | V tile]
+  uint4* qf = reinterpret_cast<uint4*>(kv + (size_t)2 * 2 * tile);            // [(HD/16) * 8 n-tiles][32 lanes]
+  uint16_t* ph = reinterpret_cast<uint16_t*>(qf + (size_t)(p.HD / 16) * 8 * 32);   // [kPC][kPP] hi
+  uint16_t* pl = ph + kPC * kPP;                                                    // lo
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
+    if (!p.keqv) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+  const int nqb = (p.npos + p.pb - 1) / p.pb;
+  const int items = p.nseq * p.KVH * nqb;
+  const uint32_t len0 = p.cachemode == 2 ? p.params[5] : p.params[1];
+  const uint32_t qp0 = p.params[0];
+
+  // thread 0 issues the K/V loads of this CTA's (item, chunk) sequence, two ahead
+  int is_it = blockIdx.x, is_c = 0, is_c1 = 0;
+  uint32_t n_issued = 0;
+  if (threadIdx.x == 0 && is_it < items) {
+    const PreItem I = pre_item(p, is_it);
+    is_c = I.c0;
+    is_c1 = I.c1;
+  }
+  auto issue_next = [&]() {
+    if (is_it >= items) return;
+    const PreItem I = pre_item(p, is_it);
+    const int st = n_issued & 1;
+    uint8_t* dk = kv + (size_t)st * 2 * tile;
+    mbar_expect_tx(&full[st], (uint32_t)tile * (p.keqv ? 1u : 2u));
+    for (int j = 0; j < p.HD / 64; j++) {
+      tma_load_4d(dk + j * kSub, &kmap, 64 * j, I.kvh, is_c * kAC, I.b, &full[st]);
+      if (!p.keqv) tma_load_4d(dk + tile + j * kSub, &vmap, 64 * j, I.kvh, is_c * kAC, I.b, &full[st]);
+    }
+    n_issued++;
+    if (++is_c >= is_c1) {
+      is_it += gridDim.x;
+      if (is_it < items) {
+        const PreItem J = pre_item(p, is_it);
+        is_c = J.c0;
+        is_c1 = J.c1;
+      }
+    }
+  };
+  if (threadIdx.x == 0) {
+    issue_next();
+    issue_next();
+  }
+
+  const int r0 = 16 * warp + g;
+  uint32_t koff[8];
+#pragma unroll
+  for (int u = 0; u < 8; u++) koff[u] = (uint32_t)(r0 * 128 + ((u ^ g) << 4) + 4 * t);
+  const int dtiles = p.HD / 16 / kPW;           // 1..4
+  const int lrow = (lane & 7) + ((lane >> 4) << 3), hbit = (lane >> 3) & 1;
+  uint32_t voff[4];
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    const int dt = warp * dtiles + u;
+    voff[u] = (uint32_t)((dt >> 2) * kSub + lrow * 128 + (((2 * (dt & 3) + hbit) ^ (lane & 7)) << 4));
+  }
+  bool ok = true;
+  uint32_t L = 0;                                 // loads consumed
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const PreItem I = pre_item(p, it);
+    // q fragments of the 64 columns (col = position-in-block * G + head-in-group), hi and lo
+    for (int i = threadIdx.x; i < (p.HD / 16) * 8 * 32; i += 32 * kPW) {
+      const int j = i >> 8, nt = (i >> 5) & 7, gg = (i & 31) >> 2, tt = i & 3;
+      const int col = 8 * nt + gg, pp = col / p.G, gi = col % p.G;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (pp < I.np) {
+        const size_t row = (size_t)(I.p0 + pp) * p.nseq + I.b;
+        const float* qr = p.q + (row * p.QH + I.kvh * p.G + gi) * p.HD + 16 * j + 2 * tt;
+        const float x[4] = {qr[0], qr[1], qr[8], qr[9]};
+        uint16_t h[4], l[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const __half hh = __float2half_rn(x[k]);
+          h[k] = __half_as_ushort(hh);
+          l[k] = f2h(x[k] - __half2float(hh));
+        }
+        v = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+      }
+      qf[i] = v;
+    }
+    if (threadIdx.x < kPC) {
+      m_run[threadIdx.x] = -INFINITY;
+      l_run[threadIdx.x] = 0.f;
+    }
+    float acc[4][8][4];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++) acc[u][nt][0] = acc[u][nt][1] = acc[u][nt][2] = acc[u][nt][3] = 0.f;
+    // per column of this lane (n-tile nt, column 8 nt + 2 t + e): the query's slot rule
+    __syncthreads();
+    for (int c = I.c0; c < I.c1; c++, L++) {
+      const int st = L & 1;
+      if (ok) ok = bounded_spin([&] { return mbar_try_wait(&full[st], (L >> 1) & 1u); }, p.status, p.wait_ns);
+      const uint8_t* Kt = kv + (size_t)st * 2 * tile;
+      const uint8_t* Vt = p.keqv ? Kt : Kt + tile;
+      // ---- S^T[slot][col] for this warp's 16 slots
+      float sc[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      if (ok) {
+        for (int j0 = 0; j0 < p.HD / 16; j0 += 4) {
+          const uint8_t* kb = Kt + (j0 >> 2) * kSub;
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int j = j0 + u;
+            const uint32_t a0 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u]);
+            const uint32_t a1 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u] + 1024);
+            const uint32_t a2 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u + 1]);
+            const uint32_t a3 = *reinterpret_cast<const uint32_t*>(kb + koff[2 * u + 1] + 1024);
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+              const uint4 qv = qf[(j * 8 + nt) * 32 + lane];
+              mma16816(sc[nt], a0, a1, a2, a3, qv.x, qv.y);
+              mma16816(sc[nt], a0, a1, a2, a3, qv.z, qv.w);
+            }
+          }
+        }
+      }
+      // ---- mask, column maxima
+      const uint32_t sa = (uint32_t)c * kAC + 16 * warp + g, sb = sa + 8;
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++) {
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int col = 8 * nt + 2 * t + e, pp = col / p.G;
+          SlotRule r{p.cachemode, p.ring, p.window, qp0 + (uint32_t)(I.p0 + pp), len0 + (uint32_t)(I.p0 + pp)};
+          const uint32_t n = r.nslots();
+          const bool live = pp < I.np && ok;
+          const bool va = live && sa < n && r.valid(sa), vb = live && sb < n && r.valid(sb);
+          sc[nt][e] = va ? sc[nt][e] * p.scale : -INFINITY;
+          sc[nt][2 + e] = vb ? sc[nt][2 + e] * p.scale : -INFINITY;
+        }
+        float m0 = fmaxf(sc[nt][0], sc[nt][2]), m1 = fmaxf(sc[nt][1], sc[nt][3]);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+          m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+        }
+        if (g == 0) {
+          red_m[warp][8 * nt + 2 * t] = m0;
+          red_m[warp][8 * nt + 2 * t + 1] = m1;
+        }
+      }
+      __syncthreads();
+      // ---- new running max, p = e^(s - M), rescale factors
+      float alpha[8][2];
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++) {
+        float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int col = 8 * nt + 2 * t + e;
+          float M = red_m[0][col];
+#pragma unroll
+          for (int w = 1; w < kPW; w++) M = fmaxf(M, red_m[w][col]);
+          const float mo = m_run[col];
+          const float Mn = fmaxf(mo, M);
+          alpha[nt][e] = (mo == -INFINITY) ? 0.f : expf(mo - Mn);
+          const float pa = (sc[nt][e] == -INFINITY) ? 0.f : expf(sc[nt][e] - Mn);
+          const float pb2 = (sc[nt][2 + e] == -INFINITY) ? 0.f : expf(sc[nt][2 + e] - Mn);
+          const int la = 16 * warp + g, lb = la + 8;
+          const __half ha = __float2half_rn(pa), hb = __float2half_rn(pb2);
+          ph[col * kPP + la] = __half_as_ushort(ha);
+          pl[col * kPP + la] = f2h(pa - __half2float(ha));
+          ph[col * kPP + lb] = __half_as_ushort(hb);
+          pl[col * kPP + lb] = f2h(pb2 - __half2float(hb));
+          if (e == 0) l0 = pa + pb2;
+          else l1 = pa + pb2;
+        }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+          l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        }
+        if (g == 0) {
+          red_l[warp][8 * nt + 2 * t] = l0;
+          red_l[warp][8 * nt + 2 * t + 1] = l1;
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x < kPC) {
+        const int col = threadIdx.x;
+        float M = red_m[0][col];
+        for (int w = 1; w < kPW; w++) M = fmaxf(M, red_m[w][col]);
+        const float mo = m_run[col], Mn = fmaxf(mo, M);
+        const float al = (mo == -INFINITY) ? 0.f : expf(mo - Mn);
+        float ls = 0.f;
+        for (int w = 0; w < kPW; w++) ls += red_l[w][col];
+        l_run[col] = l_run[col] * al + ls;
+        m_run[col] = Mn;
+      }
+      // ---- O^T[d][col] = alpha O^T + V^T P^T for this warp's d tiles
+      if (ok) {
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+          for (int nt = 0; nt < 8; nt++) {
+            acc[u][nt][0] *= alpha[nt][0];
+            acc[u][nt][1] *= alpha[nt][1];
+            acc[u][nt][2] *= alpha[nt][0];
+            acc[u][nt][3] *= alpha[nt][1];
+          }
+#pragma unroll
+        for (int ks = 0; ks < kAC / 16; ks++) {
+          uint32_t bh[8][2], bl[8][2];
+#pragma unroll
+          for (int nt = 0; nt < 8; nt++) {
+            const uint16_t* rh = ph + (8 * nt + g) * kPP + 16 * ks + 2 * t;
+            const uint16_t* rl = pl + (8 * nt + g) * kPP + 16 * ks + 2 * t;
+            bh[nt][0] = lds32(rh);
+            bh[nt][1] = lds32(rh + 8);
+            bl[nt][0] = lds32(rl);
+            bl[nt][1] = lds32(rl + 8);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            if (u >= dtiles) break;
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_trans(a0, a1, a2, a3, Vt + voff[u] + ks * 16 * 128);
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+              mma16816(acc[u][nt], a0, a1, a2, a3, bh[nt][0], bh[nt][1]);
+              mma16816(acc[u][nt], a0, a1, a2, a3, bl[nt][0], bl[nt][1]);
+            }
+          }
+        }
+      }
+      __syncthreads();                          // stage and p rows free
+      if (threadIdx.x == 0 && ok) issue_next();
+    }
+    // ---- out = O / l (f16), rows (position, sequence), head kvh * G + head-in-group
+    if (ok) {
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int col = 8 * nt + 2 * t + e, pp = col / p.G, gi = col % p.G;
+          if (pp >= I.np) continue;
+          const float l = l_run[col];
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          uint16_t* o = p.out + ((size_t)(I.p0 + pp) * p.nseq + I.b) * (size_t)p.QH * p.HD +
+                        (size_t)(I.kvh * p.G + gi) * p.HD + 16 * warp * dtiles + g;
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            if (u >= dtiles) break;
+            o[16 * u] = f2h(acc[u][nt][e] * inv);
+            o[16 * u + 8] = f2h(acc[u][nt][2 + e] * inv);
+          }
+        }
+    }
+    __syncthreads();                            // m_run / l_run / qf reused by the next item
+  }
+  // loads issued but not consumed (only after a time-out) land before the CTA ends
+  if (threadIdx.x == 0)
+    for (uint32_t k = L; k < n_issued; k++) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full[k & 1], (k >> 1) & 1u) && globaltimer_ns() - t0 < p.wait_ns) {
+      }
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -485,6 +812,38 @@ E4B_API int e4b_attdec_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, c
   if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW * kAG), smem, p, kmap, vmap)) return r;
   return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(128), (size_t)max_chunks * 4, p, out_h,
                     xfo);
+}
+
+E4B_API int e4b_attn_prefill(e4b_ctx* c, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                             const uint32_t* params, uint16_t* out, int QH, int KVH, int HD, int window, int cachemode,
+                             int ring, float scale, int cache_slots, int nseq, int npos) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, q && kcache && vcache && params && out && nseq > 0 && npos > 0 && cache_slots > 0,
+              "attn_prefill: bad args");
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && (QH / KVH) <= kPC && kPC % (QH / KVH) == 0,
+              "attn_prefill: %d query heads per KV head (must divide %d)", KVH > 0 ? QH / KVH : 0, kPC);
+  E4B_REQUIRE(c, HD % 64 == 0 && HD <= 256, "attn_prefill: HD=%d must be a multiple of 64 up to 256", HD);
+  E4B_REQUIRE(c, cachemode >= 0 && cachemode <= 2 && (cachemode != 1 || (ring > 0 && window > 0 && ring <= cache_slots)),
+              "attn_prefill: bad cache mode");
+  E4B_REQUIRE(c, cachemode != 1 || npos + window <= ring + 1,
+              "attn_prefill: %d positions per chunk overwrite ring slots still in a window (ring %d, window %d)", npos,
+              ring, window);
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(kcache) % 16 == 0 && reinterpret_cast<uintptr_t>(vcache) % 16 == 0,
+              "attn_prefill: caches must be 16-byte aligned");
+  PreP p = {};
+  p.q = q; p.params = params; p.out = out; p.status = c->status;
+  p.QH = QH; p.KVH = KVH; p.HD = HD; p.G = QH / KVH; p.window = window; p.cachemode = cachemode; p.ring = ring;
+  p.nseq = nseq; p.npos = npos; p.keqv = kcache == vcache; p.pb = kPC / p.G; p.scale = scale; p.wait_ns = c->wait_ns;
+  CUtensorMap kmap, vmap;
+  E4B_REQUIRE(c, cache_map(&kmap, kcache, HD, KVH, cache_slots, nseq), "attn_prefill: K cache tensor map failed");
+  if (p.keqv) vmap = kmap;
+  else E4B_REQUIRE(c, cache_map(&vmap, vcache, HD, KVH, cache_slots, nseq), "attn_prefill: V cache tensor map failed");
+  const size_t smem = 1024 + (size_t)2 * 2 * (HD / 64) * kSub + (size_t)(HD / 16) * 8 * 32 * 16 + (size_t)2 * kPC * kPP * 2;
+  cudaError_t e = cudaFuncSetAttribute(k_attpre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "attn_prefill smem attr: %s", cudaGetErrorString(e));
+  const long long items = (long long)nseq * KVH * ((npos + p.pb - 1) / p.pb);
+  const int grid = (int)(items < c->sm_count ? items : c->sm_count);
+  return e4b_launch(c, "attn_prefill", k_attpre, dim3(grid), dim3(32 * kPW), smem, p, kmap, vmap);
 }
 
 }  // extern "C"

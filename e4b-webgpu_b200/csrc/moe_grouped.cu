@@ -691,6 +691,35 @@ int qmm(e4b_ctx* c, const char* name, const uint16_t* x, const uint8_t* w, const
 
 extern "C" {
 
+// dst[i] = src[idx[i] / div] (f16 rows of H), a zero row where idx[i] is the
+// empty marker: the activation rows of expert-sorted entries, contiguous per
+// expert, for the grouped prefill GEMM.
+__global__ void k_gather_rows(const uint16_t* __restrict__ src, const uint32_t* __restrict__ idx, int div,
+                              uint16_t* __restrict__ dst, int H, int n, int n_src) {
+  pdl_wait();
+  const int i = blockIdx.x;
+  if (i >= n) return;
+  const uint32_t e = idx[i];
+  const uint32_t r = e == 0xffffffffu ? 0xffffffffu : e / (uint32_t)div;
+  uint4* d = reinterpret_cast<uint4*>(dst + (size_t)i * H);
+  if (r >= (uint32_t)n_src) {
+    for (int j = threadIdx.x; j < H / 8; j += blockDim.x) d[j] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)r * H);
+  for (int j = threadIdx.x; j < H / 8; j += blockDim.x) d[j] = s[j];
+}
+
+E4B_API int e4b_gather_rows(e4b_ctx* c, const uint16_t* src, const uint32_t* idx, int div, uint16_t* dst, int H,
+                            int n, int n_src) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, src && idx && dst && div > 0 && n > 0 && n_src > 0 && H > 0 && H % 8 == 0,
+              "gather_rows: bad args (H=%d must be a multiple of 8)", H);
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(src) % 16 == 0 && reinterpret_cast<uintptr_t>(dst) % 16 == 0,
+              "gather_rows: rows must be 16-byte aligned");
+  return e4b_launch(c, "gather_rows", k_gather_rows, dim3(n), dim3(128), 0, src, idx, div, dst, H, n, n_src);
+}
+
 E4B_API int e4b_expgroup(e4b_ctx* c, const uint32_t* topk, int n_tok, int K, int E, uint32_t* offsets,
                          uint32_t* entries, uint32_t* inv) {
   E4B_CHECK_CTX(c);

@@ -163,7 +163,7 @@ E4B_DEV uint32_t mix32(uint32_t x) {
 }
 __global__ void k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __restrict__ topk_idx,
                              float* __restrict__ topk_w, int n_tok, int K, int E, float s, uint32_t seed, int salt,
-                             int tok0) {
+                             int tok0, int nseq) {
   pdl_wait();
   extern __shared__ float cdf[];          // [E] cumulative popularity, then [E] rank -> expert (as bits)
   uint32_t* perm = reinterpret_cast<uint32_t*>(cdf + E);
@@ -183,13 +183,14 @@ __global__ void k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __re
     }
   }
   __syncthreads();
-  const uint32_t pos = params[0];
   for (int i = threadIdx.x; i < n_tok; i += blockDim.x) {
+    // row i: sequence tok0 + i % nseq at position params[0] + i / nseq
+    const uint32_t pos = params[0] + (uint32_t)(i / nseq);
+    const uint32_t tk = (uint32_t)(tok0 + i % nseq);
     uint32_t chosen[32];
     int got = 0;
     for (uint32_t attempt = 0; got < K && attempt < 4096u; attempt++) {
-      const uint32_t h = mix32(seed ^ mix32((uint32_t)salt * 0x85ebca6bu ^ mix32(pos ^ mix32((uint32_t)(tok0 + i) ^
-                                                                                              (attempt << 20)))));
+      const uint32_t h = mix32(seed ^ mix32((uint32_t)salt * 0x85ebca6bu ^ mix32(pos ^ mix32(tk ^ (attempt << 20)))));
       const float u = (float)(h >> 8) * (1.0f / 16777216.0f);
       int lo = 0, hi = E - 1;
       while (lo < hi) {
@@ -364,7 +365,17 @@ E4B_API int e4b_route_zipf(e4b_ctx* c, const uint32_t* params, uint32_t* topk_id
   E4B_REQUIRE(c, params && topk_idx && topk_w && n_tok > 0 && K > 0 && K <= 32 && K <= E && E <= 4096 && s > 0.f,
               "route_zipf: bad args");
   return e4b_launch(c, "route_zipf", k_route_zipf, dim3(1), dim3(256), (size_t)E * 8, params, topk_idx, topk_w, n_tok,
-                    K, E, s, seed, salt, tok0);
+                    K, E, s, seed, salt, tok0, n_tok);
+}
+
+E4B_API int e4b_route_zipf_rows(e4b_ctx* c, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int nseq,
+                                int npos, int K, int E, float s, uint32_t seed, int salt, int tok0) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, params && topk_idx && topk_w && nseq > 0 && npos > 0 && K > 0 && K <= 32 && K <= E && E <= 4096 &&
+                     s > 0.f,
+              "route_zipf_rows: bad args");
+  return e4b_launch(c, "route_zipf", k_route_zipf, dim3(1), dim3(256), (size_t)E * 8, params, topk_idx, topk_w,
+                    nseq * npos, K, E, s, seed, salt, tok0, nseq);
 }
 
 E4B_API int e4b_router(e4b_ctx* c, const float* h, const float* scale, const float* wr, const float* pes,

@@ -143,7 +143,7 @@ E4B_API int e4b_set_pdl(e4b_ctx* c, int enable) {
   c->pdl = enable != 0;
   return E4B_OK;
 }
-E4B_API size_t e4b_workspace_bytes(void) { return (size_t)32 << 20; }
+E4B_API size_t e4b_workspace_bytes(void) { return (size_t)96 << 20; }
 E4B_API int e4b_set_option(e4b_ctx* c, const char* name, int value) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, name, "null option name");

@@ -194,6 +194,13 @@ E4B_API int e4b_q40gugrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, cons
                          const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K);
 E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
                            const uint32_t* entries, float* y, int IN, int OUT, int E);
+/* dst[i] = src[idx[i] / div] for n f16 rows of H (a zero row where idx[i] is
+ * 0xffffffff or out of range): the expert-sorted activation rows of a prefill
+ * chunk (entries from e4b_expgroup, div = K), contiguous per expert as the
+ * grouped GEMM reads them (the row gather of kernels/q40grpsg32.wgsl:51-58,
+ * done once per layer instead of per tile). */
+E4B_API int e4b_gather_rows(e4b_ctx* ctx, const uint16_t* src, const uint32_t* idx, int div, uint16_t* dst, int H,
+                            int n, int n_src);
 /* Batched-prefill q4_0 GEMM on the tcgen05 tensor cores: kernels/q40sg.wgsl:30-124
  * (TPREC=f32) and, grouped, kernels/q40grpsg32.wgsl:31-129.  x: f16 [M][IN]
  * row-major (plain order), IN a multiple of 64, 16-byte aligned.  w: q4_0
@@ -299,6 +306,11 @@ E4B_API int e4b_routertop(e4b_ctx* ctx, const float* x, const float* wr, const f
  * (seed, salt, position params[0], token tok0 + i). */
 E4B_API int e4b_route_zipf(e4b_ctx* ctx, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int n_tok,
                            int K, int E, float s, uint32_t seed, int salt, int tok0);
+/* e4b_route_zipf for nseq x npos position-major rows (a batched-prefill chunk):
+ * row i is token tok0 + i % nseq at position params[0] + i / nseq, routed as the
+ * token-by-token calls route it. */
+E4B_API int e4b_route_zipf_rows(e4b_ctx* ctx, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int nseq,
+                                int npos, int K, int E, float s, uint32_t seed, int salt, int tok0);
 /* kernels/router.wgsl:16-63: scale-less RMS of h, x scale x H^-0.5, then as routertop. */
 E4B_API int e4b_router(e4b_ctx* ctx, const float* h, const float* scale, const float* wr, const float* pes,
                        uint32_t* topk_idx, float* topk_w, int H, int E, int K, float eps);
@@ -371,6 +383,26 @@ E4B_API int e4b_headprep_seq(e4b_ctx* ctx, const float* qkv, const float* qw, co
                              uint16_t* kcache, uint16_t* vcache, float* q_out, int QH, int KVH, int HD,
                              int rope_angles, float theta, float eps, int keqv, int cachemode, int ring,
                              int cache_slots, int nseq, int nparts);
+/* e4b_headprep_seq for a batched-prefill chunk: nseq x npos position-major
+ * rows (row r = sequence r % nseq at position params[0] + r / nseq, linear
+ * cache slot params[4] + r / nseq); K/V of every row land in its sequence's
+ * cache (kernels/headprep.wgsl:19-87 per row, as encodeLayerPre runs it,
+ * src/engine-a4b.js:476-477). */
+E4B_API int e4b_headprep_rows(e4b_ctx* ctx, const float* qkv, const float* qw, const float* kw,
+                              const uint32_t* params, uint16_t* kcache, uint16_t* vcache, float* q_out, int QH,
+                              int KVH, int HD, int rope_angles, float theta, float eps, int keqv, int cachemode,
+                              int ring, int cache_slots, int nseq, int npos);
+/* Causal attention of a batched-prefill chunk (the reference's per-token
+ * attention over a prompt chunk, src/engine-a4b.js:478-479 with attnos.wgsl /
+ * attnf32.wgsl semantics): q f32 [npos*nseq][QH][HD] position-major rows (row =
+ * p * nseq + b), whose K/V rows are already in the caches; params = the chunk's
+ * first position (src/engine-a4b.js:697 layout); query p attends with position
+ * params[0] + p and length params[1] + p (params[5] + p for cachemode 2).
+ * out f16 [npos*nseq][QH*HD].  QH/KVH must divide 64; for a ring, npos + window
+ * <= ring + 1 (no slot a query still needs is overwritten within the chunk). */
+E4B_API int e4b_attn_prefill(e4b_ctx* ctx, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                             const uint32_t* params, uint16_t* out, int QH, int KVH, int HD, int window,
+                             int cachemode, int ring, float scale, int cache_slots, int nseq, int npos);
 E4B_API int e4b_attsplit_seq(e4b_ctx* ctx, const float* q, const uint16_t* kcache, const uint16_t* vcache,
                              const uint32_t* params, float* part_o, float* part_ml, int QH, int KVH, int HD,
                              int window, int cachemode, int ring, int chunk, int max_chunks, float scale,
