@@ -291,9 +291,15 @@ def run_moe_batch(args, rank, world, local_rank):
     prompts = np.stack([e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=1000 + b)
                         for b in range(rank * nloc, (rank + 1) * nloc)])
     t1 = time.time()
+    dev.sync()
+    dev.call("e4b_event_record", 6)
     eng.prefill(prompts)
+    dev.call("e4b_event_record", 7)
     dev.sync()
     t_prefill = time.time() - t1
+    pms = ctypes.c_float()
+    dev.call("e4b_event_elapsed", 6, 7, ctypes.byref(pms))
+    t_prefill_dev = dist.max(pms.value / 1000.0)
     pos = args.prefill
     eng.decode_chunk(args.warmup)
     dev.sync()
@@ -372,6 +378,9 @@ def run_moe_batch(args, rank, world, local_rank):
         "exposed_all_to_all_us_per_step": round(a2a, 1) if world > 1 else None,
         "clocks": clk, "gpu_launches": int(kpt * args.steps), "kernels_per_step": kpt,
         "prefill_s": round(t_prefill, 1), "model_build_s": round(t_build, 1),
+        "prefill": {"positions": args.prefill, "sequences": B,
+                    "mode": "chunked batched (tcgen05 GEMMs)" if world == 1 else "token by token (expert parallel)",
+                    "device_s": round(t_prefill_dev, 3), "tok_s": round(B * args.prefill / t_prefill_dev, 1)},
     }
     dist.close()
     return out, img, cfg
@@ -406,7 +415,7 @@ def moe_point(args, budget_s: float) -> dict:
         return {"error": f"rc {r.returncode}: " + " | ".join(tail)}
     out = json.loads(lines[-1])
     keep = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "config", "e2e", "clocks",
-            "gpu_launches", "prefill_s", "model_build_s")
+            "gpu_launches", "prefill_s", "model_build_s", "prefill")
     pt = {k: out[k] for k in keep if k in out}
     pt["roofline"] = {k: out["roofline"][k] for k in ("bound", "achieved", "peak", "unit", "frac")}
     pt["note"] = ("config 5 on one GPU (bench.py --config a4b --batch 64); the scaling series runs the same "

@@ -183,7 +183,7 @@ __global__ void k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __re
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < n_tok; i += blockDim.x) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_tok; i += gridDim.x * blockDim.x) {
     // row i: sequence tok0 + i % nseq at position params[0] + i / nseq
     const uint32_t pos = params[0] + (uint32_t)(i / nseq);
     const uint32_t tk = (uint32_t)(tok0 + i % nseq);
@@ -374,8 +374,9 @@ E4B_API int e4b_route_zipf_rows(e4b_ctx* c, const uint32_t* params, uint32_t* to
   E4B_REQUIRE(c, params && topk_idx && topk_w && nseq > 0 && npos > 0 && K > 0 && K <= 32 && K <= E && E <= 4096 &&
                      s > 0.f,
               "route_zipf_rows: bad args");
-  return e4b_launch(c, "route_zipf", k_route_zipf, dim3(1), dim3(256), (size_t)E * 8, params, topk_idx, topk_w,
-                    nseq * npos, K, E, s, seed, salt, tok0, nseq);
+  // every CTA builds the popularity table itself, then routes its rows
+  return e4b_launch(c, "route_zipf", k_route_zipf, dim3((nseq * npos + 255) / 256), dim3(256), (size_t)E * 8, params,
+                    topk_idx, topk_w, nseq * npos, K, E, s, seed, salt, tok0, nseq);
 }
 
 E4B_API int e4b_router(e4b_ctx* c, const float* h, const float* scale, const float* wr, const float* pes,
