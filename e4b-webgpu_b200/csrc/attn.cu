@@ -209,6 +209,68 @@ __global__ void k_attcomb(const float* __restrict__ part_o, const float* __restr
   if (lse && threadIdx.x == 0) lse[h] = den > 0.f ? M + logf(den) : -INFINITY;
 }
 
+
+// Attention-mass score pass of a counted (linear) cache (the SCORE=1 pass of
+// kernels/attnos.wgsl:82-97): for every live slot t < len (len = params[5]) and
+// query head h, score[h][t] += exp(scale * q_h . k_t - lse_h), the head's
+// normalised attention probability of slot t, accumulated across decode steps.
+// One thread per slot; the G query heads of its KV head share the K row.
+__global__ void k_attn_score(const float* __restrict__ q, const uint16_t* __restrict__ kcache,
+                             const float* __restrict__ lse, const uint32_t* __restrict__ params,
+                             float* __restrict__ score, int QH, int KVH, int HD, float scale, int scap) {
+  pdl_wait();
+  extern __shared__ float qs[];                 // [G][HD]
+  const int kvh = blockIdx.y, G = QH / KVH;
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i] = q[(size_t)kvh * G * HD + i];
+  __syncthreads();
+  const uint32_t len = params[5];
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if ((uint32_t)t >= len || t >= scap) return;
+  const uint16_t* k = kcache + ((size_t)t * KVH + kvh) * HD;
+  float acc[8];
+#pragma unroll
+  for (int g = 0; g < 8; g++) acc[g] = 0.f;
+  for (int d = 0; d < HD; d += 8) {
+    const uint4 kv = *reinterpret_cast<const uint4*>(k + d);
+    const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+    float kf[8];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      kf[2 * e] = h2f((uint16_t)(w[e] & 0xFFFFu));
+      kf[2 * e + 1] = h2f((uint16_t)(w[e] >> 16));
+    }
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+      if (g >= G) break;
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[g] = fmaf(qs[g * HD + d + e], kf[e], acc[g]);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < 8; g++) {
+    if (g >= G) break;
+    const int h = kvh * G + g;
+    score[(size_t)h * scap + t] += expf(acc[g] * scale - lse[h]);
+  }
+}
+
+// kernels/kvgather.wgsl:9-18: dst slot i <- src slot keep[i], K and V.
+__global__ void k_kvgather(const uint32_t* __restrict__ keep, const uint16_t* __restrict__ src_k,
+                           const uint16_t* __restrict__ src_v, uint16_t* __restrict__ dst_k,
+                           uint16_t* __restrict__ dst_v, int row, int src_slots) {
+  pdl_wait();
+  const int i = blockIdx.x;
+  const uint32_t s = keep[i];
+  if (s >= (uint32_t)src_slots) return;
+  const uint4* sk = reinterpret_cast<const uint4*>(src_k + (size_t)s * row);
+  const uint4* sv = reinterpret_cast<const uint4*>(src_v + (size_t)s * row);
+  uint4* dk = reinterpret_cast<uint4*>(dst_k + (size_t)i * row);
+  uint4* dv = reinterpret_cast<uint4*>(dst_v + (size_t)i * row);
+  for (int e = threadIdx.x; e < row / 8; e += blockDim.x) {
+    dk[e] = sk[e];
+    dv[e] = sv[e];
+  }
+}
 }  // namespace
 
 extern "C" {
@@ -332,6 +394,27 @@ E4B_API int e4b_attcomb_seq(e4b_ctx* c, const float* part_o, const float* part_m
   E4B_REQUIRE(c, !xfo || (QH * HD) % 32 == 0, "attcomb_seq: fragment order needs QH*HD %% 32 == 0");
   return e4b_launch(c, "attcomb_seq", k_attcomb, dim3(QH, nseq), dim3(128), 0, part_o, part_ml, out_h, out_f, lse,
                     HD, max_chunks, xfo);
+}
+
+
+E4B_API int e4b_attn_score(e4b_ctx* c, const float* q, const uint16_t* kcache, const float* lse,
+                           const uint32_t* params, float* score, int QH, int KVH, int HD, float scale, int scap) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, q && kcache && lse && params && score && scap > 0, "attn_score: bad args");
+  E4B_REQUIRE(c, QH > 0 && KVH > 0 && QH % KVH == 0 && QH / KVH <= 8 && HD > 0 && HD % 8 == 0,
+              "attn_score: QH=%d KVH=%d HD=%d (<= 8 query heads per KV head, HD %% 8 == 0)", QH, KVH, HD);
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(kcache) % 16 == 0, "attn_score: cache must be 16-byte aligned");
+  return e4b_launch(c, "attn_score", k_attn_score, dim3((scap + 127) / 128, KVH), dim3(128),
+                    (size_t)(QH / KVH) * HD * 4, q, kcache, lse, params, score, QH, KVH, HD, scale, scap);
+}
+
+E4B_API int e4b_kvgather(e4b_ctx* c, const uint32_t* keep, int n, const uint16_t* src_k, const uint16_t* src_v,
+                         uint16_t* dst_k, uint16_t* dst_v, int KVH, int HD, int src_slots) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, keep && src_k && src_v && dst_k && dst_v && n > 0 && src_slots > 0, "kvgather: bad args");
+  E4B_REQUIRE(c, KVH > 0 && HD > 0 && (KVH * HD) % 8 == 0, "kvgather: KVH*HD must be a multiple of 8");
+  return e4b_launch(c, "kvgather", k_kvgather, dim3(n), dim3(128), 0, keep, src_k, src_v, dst_k, dst_v, KVH * HD,
+                    src_slots);
 }
 
 }  // extern "C"

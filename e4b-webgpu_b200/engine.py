@@ -65,9 +65,31 @@ def fused_supported(c: ModelConfig) -> bool:
 
 class Engine:
     def __init__(self, src, device: int | Device = 0, *, chunk: int = 64, record: bool = False,
-                 fused: bool | None = None):
+                 fused: bool | None = None, kv_budget: int | None = None, kv_decap: int | None = None,
+                 kv_protect: int = 64, ternary: dict | None = None):
         """fused: run each token's layers as one persistent kernel (dense graph
-        only; None = whenever the model's shapes allow it)."""
+        only; None = whenever the model's shapes allow it).  kv_budget: long
+        context with budget compaction of the counted (global) caches
+        (src/engine-a4b.js:16-21, 589-657): every decode step accumulates the
+        attention mass of their slots, compact_all() keeps kv_budget of them
+        (the kv_protect most recent plus the highest mass), generate_long()
+        recompacts whenever the count would pass kv_decap (default kv_budget +
+        128).  Runs on the per-operator path.  ternary: the expert tensors in the
+        ternary format ({layer: {"gu" | "down": (planes, scales)}}, from
+        ternary.ternarize_model) decoded by e4b_t2gu / e4b_t2moedown
+        (src/engine-a4b.js:338-340, 442-454)."""
+        self.ternary = ternary
+        self.kv_budget = kv_budget
+        self.kv_decap = kv_decap if kv_decap is not None else (kv_budget + 128 if kv_budget else None)
+        self.kv_protect = kv_protect
+        self.kv_count = 0
+        if kv_budget is not None:
+            if fused:
+                raise ValueError("budget compaction runs on the per-operator path (fused=False)")
+            fused = False
+            if not (0 < kv_protect <= kv_budget < self.kv_decap):
+                raise ValueError(f"need 0 < kv_protect <= kv_budget < kv_decap ({kv_protect}, {kv_budget}, "
+                                 f"{self.kv_decap})")
         self.g = gguf.open_gguf(src)
         self.cfg = ModelConfig.from_kv(self.g.kv)
         self.dev = device if isinstance(device, Device) else Device(device)
@@ -148,6 +170,12 @@ class Engine:
                 L.pes = self._f32(p + "ffn_down_exps.scale")
                 L.gu_exps = self._raw(p + "ffn_gate_up_exps.weight")
                 L.down_exps = self._raw(p + "ffn_down_exps.weight")
+                t2 = (getattr(self, "ternary", None) or {}).get(l)
+                if t2 is not None:
+                    L.gu_t2 = self.dev.upload(np.ascontiguousarray(t2["gu"][0]), f"guT2_{l}")
+                    L.gu_t2s = self.dev.upload(np.ascontiguousarray(t2["gu"][1]), f"guT2s_{l}")
+                    L.down_t2 = self.dev.upload(np.ascontiguousarray(t2["down"][0]), f"downT2_{l}")
+                    L.down_t2s = self.dev.upload(np.ascontiguousarray(t2["down"][1]), f"downT2s_{l}")
             L.angles = c.rope_angles(l)
             L.theta = c.theta(l)
             L.ring = c.ring(l)
@@ -195,6 +223,15 @@ class Engine:
             A.moe_out = d.alloc(H * 4, "moeOut")
         if self.record:
             A.dump = d.alloc(c.layers * H * 4, "hiddenDump")
+        if self.kv_budget is not None:
+            A.lse = d.alloc(c.q_heads * 4, "lse")
+            glob = [L for L in self.layers if L.cachemode == 2]
+            smax = max([L.slots for L in glob], default=1)
+            A.keep = d.alloc(smax * 4, "kvKeep")
+            A.kscr = d.alloc(smax * c.kv_heads * c.head_dim * 2, "kvScratchK")
+            A.vscr = d.alloc(smax * c.kv_heads * c.head_dim * 2, "kvScratchV")
+            for L in glob:
+                L.score = d.alloc(c.q_heads * L.slots * 4, f"score{L.i}")
         self.A = A
         ws = int(d.L.e4b_workspace_bytes())
         A.ws = d.alloc(ws, "workspace")
@@ -282,8 +319,12 @@ class Engine:
         ops.attsplit(d, A.q, L.kc, L.vc, A.params, A.part_o, A.part_ml, Q_HEADS=c.q_heads, KV_HEADS=c.kv_heads,
                      HEAD_DIM=c.head_dim, WINDOW=c.window if L.sliding else 0, CACHEMODE=L.cachemode, RING=L.ring,
                      CS=self.chunk, CHUNKS=L.max_chunks)
-        ops.attcomb(d, A.part_o, A.part_ml, A.attn, None, None, Q_HEADS=c.q_heads, HEAD_DIM=c.head_dim,
-                    CHUNKS=L.max_chunks)
+        scoring = self.kv_budget is not None and L.cachemode == 2
+        ops.attcomb(d, A.part_o, A.part_ml, A.attn, None, A.lse if scoring else None, Q_HEADS=c.q_heads,
+                    HEAD_DIM=c.head_dim, CHUNKS=L.max_chunks)
+        if scoring:      # the mass pass of kernels/attnos.wgsl:82-97 (SCORE=1 on global layers)
+            d.call("e4b_attn_score", A.q, L.kc, A.lse, A.params, L.score, c.q_heads, c.kv_heads, c.head_dim,
+                   ctypes.c_float(1.0), L.slots)
         ops.q40mv(d, A.attn, L.o, None, A.tmp, IN=c.q_dim, OUT=H, XF16=1)
 
     def _next_norm(self, L):
@@ -317,10 +358,18 @@ class Engine:
         ops.rmsacc3(d, A.tmp, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed, A.router_in,
                     A.moe_in, A.hidden_b, DIM=H, EPS=c.eps)
         ops.routertop(d, A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H=H, E=c.experts, K=K)
-        ops.q40gu(d, A.moe_in, L.gu_exps, A.topk_idx, A.geglu_slots, A.normed, L.gu, A.geglu, IN=H, FF=EF, FF2=FF,
-                  K=K)
-        ops.q40mv(d, A.geglu, L.down, None, A.tmp, IN=FF, OUT=H, XF16=1)
-        ops.q40moedown(d, A.geglu_slots, L.down_exps, A.topk_idx, A.topk_w, A.moe_out, IN=EF, OUT=H, K=K)
+        if getattr(L, "gu_t2", None) is not None:
+            # ternary experts (src/engine-a4b.js:442-454): dense branch q4_0, expert slots t2
+            ops.q40gu(d, None, None, None, None, A.normed, L.gu, A.geglu, IN=H, FF=0, FF2=FF, K=0)
+            d.call("e4b_t2gu", A.moe_in, L.gu_t2, L.gu_t2s, A.topk_idx, A.geglu_slots, H, EF, K, c.experts)
+            ops.q40mv(d, A.geglu, L.down, None, A.tmp, IN=FF, OUT=H, XF16=1)
+            d.call("e4b_t2moedown", A.geglu_slots, L.down_t2, L.down_t2s, A.topk_idx, A.topk_w, A.moe_out, EF, H, K,
+                   c.experts)
+        else:
+            ops.q40gu(d, A.moe_in, L.gu_exps, A.topk_idx, A.geglu_slots, A.normed, L.gu, A.geglu, IN=H, FF=EF,
+                      FF2=FF, K=K)
+            ops.q40mv(d, A.geglu, L.down, None, A.tmp, IN=FF, OUT=H, XF16=1)
+            ops.q40moedown(d, A.geglu_slots, L.down_exps, A.topk_idx, A.topk_w, A.moe_out, IN=EF, OUT=H, K=K)
         nxt = self._next_norm(L)
         ops.a4btail(d, A.tmp, L.post_ffw1, A.moe_out, L.post_ffw2, L.post_ffw, A.hidden_b,
                     nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H=H, EPS=c.eps, MUL=L.scale,
@@ -364,21 +413,28 @@ class Engine:
                 self.encode_forward()
 
     # ------------------------------------------------------------ host API
-    def set_params(self, token: int, pos: int, ring_index: int | None = None, sync_slot: bool = False):
-        """Queue [pos, pos+1, token, 0, kvCount, kvCount+1, ringIndex, 0] (src/engine-a4b.js:697-698)."""
+    def set_params(self, token: int, pos: int, ring_index: int | None = None, sync_slot: bool = False,
+                   kv: int | None = None):
+        """Queue [pos, pos+1, token, 0, kvCount, kvCount+1, ringIndex, 0] (src/engine-a4b.js:697-698);
+        kvCount = pos unless given (budget compaction decouples the two)."""
         if self._hp_next >= self.host_params_n:
             self.dev.sync()
             self._hp_next = 0
         i = self._hp_next
         self._hp_next += 1
         ri = pos if ring_index is None else ring_index
-        self.host_params[i] = (pos, pos + 1, token, 0, pos, pos + 1, ri, 0)
+        kc = pos if kv is None else kv
+        self.host_params[i] = (pos, pos + 1, token, 0, kc, kc + 1, ri, 0)
         self.dev.call("e4b_upload_async", self.A.params.ptr, ctypes.c_void_p(self._host_params_ptr + i * 32),
                       ctypes.c_size_t(32))
 
     def step(self, token: int, pos: int):
         """One token at `pos` (src/engine-a4b.js:695-705); the result stays on the device."""
-        self.set_params(token, pos)
+        if self.kv_budget is not None:
+            self.set_params(token, pos, kv=self.kv_count)
+            self.kv_count += 1
+        else:
+            self.set_params(token, pos)
         self.run_token(1)
 
     def argmax_fast(self) -> int:
@@ -393,6 +449,80 @@ class Engine:
         if st:
             raise DeviceStatusError(f"{where}: device status word {st:#x} "
                                     "(1 = index out of range, 2 = a bounded device wait timed out)")
+
+    # ------------------------------------------------------------ long context
+    def reset_scores(self):
+        for L in self.layers:
+            if getattr(L, "score", None) is not None:
+                self.dev.memset(L.score, 0)
+
+    def compact_all(self):
+        """compactAll (src/engine-a4b.js:589-617): per counted (global) cache,
+        mass[t] = sum over heads of the accumulated scores; keep the kv_protect
+        most recent slots and the highest-mass others up to kv_budget (ties:
+        lower slot), ascending; gather them to the front (e4b_kvgather through
+        scratch, kernels/kvgather.wgsl); reset the scores; the count and the
+        device parameters' kvCount become the kept length."""
+        if self.kv_budget is None:
+            raise RuntimeError("compact_all needs an Engine built with kv_budget")
+        c, d, A = self.cfg, self.dev, self.A
+        d.sync()
+        n = self.kv_count
+        kept = n
+        row = c.kv_heads * c.head_dim * 2
+        for L in self.layers:
+            if getattr(L, "score", None) is None:
+                continue
+            sc = d.read(L.score, F32, c.q_heads * L.slots).reshape(c.q_heads, L.slots)
+            mass = sc[:, :n].astype(np.float64).sum(axis=0)
+            prot = min(self.kv_protect, n)
+            cand = np.argsort(-mass[:n - prot], kind="stable")
+            keep = np.sort(np.concatenate([cand[:max(self.kv_budget - prot, 0)],
+                                           np.arange(n - prot, n)])).astype(np.uint32)
+            d.write(A.keep, keep)
+            d.call("e4b_kvgather", A.keep, len(keep), L.kc, L.vc, A.kscr, A.vscr, c.kv_heads, c.head_dim, L.slots)
+            d.call("e4b_copy", ctypes.c_void_p(L.kc.ptr), ctypes.c_void_p(A.kscr.ptr), ctypes.c_size_t(len(keep) * row))
+            d.call("e4b_copy", ctypes.c_void_p(L.vc.ptr), ctypes.c_void_p(A.vscr.ptr), ctypes.c_size_t(len(keep) * row))
+            d.memset(L.score, 0)
+            kept = len(keep)
+        self.kv_count = kept
+        p = d.read(A.params, np.uint32, 8)
+        p[4], p[5] = kept, kept + 1
+        d.write(A.params, p)
+        self.check_status("compact_all")
+
+    def generate_long(self, prompt, n_new: int, eos=None):
+        """generateLong (src/engine-a4b.js:622-657): prefill; if the prompt
+        exceeds kv_decap, one scored probe step then a compaction; then greedy
+        decode in runs of 8 tokens with scores accumulating, recompacting when
+        the count would pass kv_decap.  Returns n_new ids (cut at eos)."""
+        if self.kv_budget is None:
+            raise RuntimeError("generate_long needs an Engine built with kv_budget")
+        self.kv_count = 0
+        P = len(prompt)
+        assert P >= 1 and P + n_new <= RING_CAP
+        self.prefill(prompt)
+        self.reset_scores()                 # the reference's prefill does not score
+        done = 1
+        if self.kv_count > self.kv_decap:
+            self.decode_chunk(1)            # probe: scored step on the full cache
+            self.kv_count += 1
+            done = 2
+            self.compact_all()
+        while done < n_new:
+            if self.kv_count + 8 > self.kv_decap:
+                self.compact_all()
+            n = min(8, n_new - done)
+            self.decode_chunk(n)
+            self.kv_count += n
+            done += n
+        self.dev.sync()
+        ids = [int(x) for x in self.read_ring(P - 1, n_new)]
+        if eos:
+            for i, t in enumerate(ids):
+                if t in eos:
+                    return ids[:i + 1]
+        return ids
 
     def decode_chunk(self, count: int, check_every: int = STATUS_EVERY):
         """`count` greedy tokens continuing from the device-side parameters

@@ -201,6 +201,17 @@ E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, co
  * done once per layer instead of per tile). */
 E4B_API int e4b_gather_rows(e4b_ctx* ctx, const uint16_t* src, const uint32_t* idx, int div, uint16_t* dst, int H,
                             int n, int n_src);
+/* Ternary experts (kernels/t2gu.wgsl, kernels/t2moedown.wgsl; format of
+ * scripts/ternarize_a4b.py): w = 2-bit planes, 16 values of t + 1 per u32 in the
+ * shift-group layout (element 4g + j at bits 2g + 8j), rows of IN/16 words;
+ * scale = one f16 per row.  t2gu: expert slots of the fused gate|up + GeGLU,
+ * rows [e][gate FF | up FF] -> yh[k][FF] (f16); t2moedown: y[o] = sum_k topk_w[k] *
+ * scale[e_k][o] * t[e_k][o] . x[k] (slot-combined).  Expert ids >= E set the
+ * BADINDEX status. */
+E4B_API int e4b_t2gu(e4b_ctx* ctx, const uint16_t* x, const uint32_t* w, const uint16_t* scale, const uint32_t* topk,
+                     uint16_t* yh, int IN, int FF, int K, int E);
+E4B_API int e4b_t2moedown(e4b_ctx* ctx, const uint16_t* x, const uint32_t* w, const uint16_t* scale,
+                          const uint32_t* topk, const float* topk_w, float* y, int IN, int OUT, int K, int E);
 /* Batched-prefill q4_0 GEMM on the tcgen05 tensor cores: kernels/q40sg.wgsl:30-124
  * (TPREC=f32) and, grouped, kernels/q40grpsg32.wgsl:31-129.  x: f16 [M][IN]
  * row-major (plain order), IN a multiple of 64, 16-byte aligned.  w: q4_0
@@ -331,6 +342,16 @@ E4B_API int e4b_headprep(e4b_ctx* ctx, const float* qkv, const float* qw, const 
 /* kernels/rope.wgsl:8-27 (in place, pos = params[0]). */
 E4B_API int e4b_rope(e4b_ctx* ctx, float* x, const uint32_t* params, int heads, int HD, int rope_angles,
                      float theta);
+/* The SCORE=1 mass pass of kernels/attnos.wgsl:82-97 for a counted (linear)
+ * cache: score[h][t] += exp(scale * q_h . k_t - lse[h]) for t < params[5]; lse
+ * from e4b_attcomb.  score: [QH][scap] f32, accumulated over decode steps and
+ * read by the host's budget compaction (src/engine-a4b.js:589-617). */
+E4B_API int e4b_attn_score(e4b_ctx* ctx, const float* q, const uint16_t* kcache, const float* lse,
+                           const uint32_t* params, float* score, int QH, int KVH, int HD, float scale, int scap);
+/* kernels/kvgather.wgsl:9-18: dst slot i <- src slot keep[i] (K and V rows of
+ * KVH*HD f16) for i < n; keep entries >= src_slots are skipped. */
+E4B_API int e4b_kvgather(e4b_ctx* ctx, const uint32_t* keep, int n, const uint16_t* src_k, const uint16_t* src_v,
+                         uint16_t* dst_k, uint16_t* dst_v, int KVH, int HD, int src_slots);
 /* kernels/kvwrite.wgsl:5-10: dst[params[0]*N + i] = src[i] (f32). */
 E4B_API int e4b_kvwrite(e4b_ctx* ctx, const float* src, const uint32_t* params, float* dst, int N);
 /* kernels/attsplit.wgsl:16-76 (flash-decode phase A) over the f16 cache.

@@ -33,7 +33,10 @@ F32 = np.float32
 
 
 class OracleModel:
-    def __init__(self, src):
+    def __init__(self, src, ternary=None):
+        """ternary: {layer: {"gu" | "down": (planes, scales)}}: those layers' experts
+        in the ternary format (kernels/t2gu.wgsl, kernels/t2moedown.wgsl)."""
+        self.ternary = ternary or {}
         self.g = gguf_min.open_gguf(src)
         kv = self.g.kv
         a = "gemma4."
@@ -60,6 +63,7 @@ class OracleModel:
         self.keqv_g = bool(kv.get(a + "attention.k_eq_v_global", False))
         self.max_ctx = int(kv.get("e4b.max_ctx", 8192))
         self.moe = self.E > 0
+        self.scoring = False        # accumulate attention mass of the counted (global) caches
         self.reset()
 
     # ---- per-layer geometry (same rules as the reference: src/engine-a4b.js:328-347)
@@ -97,6 +101,10 @@ class OracleModel:
             self.kc.append(np.zeros((n, self.KVH, self.HD), dt))
             self.vc.append(np.zeros((n, self.KVH, self.HD), dt))
         self.kv_count = 0
+        self.reset_scores()
+
+    def reset_scores(self):
+        self.scores = {l: np.zeros((self.QH, self.max_ctx), F32) for l in range(self.L) if not self.sliding[l]}
 
     # ---- one token
     def step(self, tok: int, pos: int, record: bool = False):
@@ -126,6 +134,8 @@ class OracleModel:
             self.kc[l][slot] = k
             self.vc[l][slot] = v
             att = ops.decode_attention(q, self.kc[l], self.vc[l], pos, KVH, self.W, self.ring(l), cm, slot_g + 1)
+            if self.scoring and cm == 2:
+                self.scores[l][:, :slot_g + 1] += ops.attention_mass(q, self.kc[l], slot_g + 1, KVH)
             t = ops.q40mv(self.t(b + "attn_output.weight"), att.reshape(-1), H, QH * HD)
             nxt = self.f(p.format(l + 1) + "attn_norm.weight") if l + 1 < self.L else None
             mul = float(self.f(b + "layer_output_scale.weight")[0])
@@ -183,17 +193,66 @@ class OracleModel:
         idx, w = ops.router_topk(router_in, wr, self.f(b + "ffn_down_exps.scale"), K)
         wgu = self.cat(b + "ffn_gate.weight", b + "ffn_up.weight")
         gd = ops.geglu_rows(ops.q40mv(wgu, normed, 2 * FF, H), FF)
-        gue = self.t(b + "ffn_gate_up_exps.weight")
-        per = 2 * EF * H // 32 * 18
-        slots = np.stack([ops.geglu_rows(ops.q40mv(gue[int(e) * per:(int(e) + 1) * per], moe_in, 2 * EF, H), EF)
-                          for e in idx])
-        t1 = ops.q40mv(self.t(b + "ffn_down.weight"), gd, H, FF)
-        m = ops.moe_down(slots, self.t(b + "ffn_down_exps.weight"), idx, w, EF, H)
+        t2 = self.ternary.get(int(b.split(".")[1]))
+        if t2 is not None:
+            slots = ops.t2gu(moe_in, t2["gu"][0].reshape(-1), t2["gu"][1], idx, H, EF)
+            t1 = ops.q40mv(self.t(b + "ffn_down.weight"), gd, H, FF)
+            m = ops.t2moedown(slots, t2["down"][0].reshape(-1), t2["down"][1], idx, w, EF, H)
+        else:
+            gue = self.t(b + "ffn_gate_up_exps.weight")
+            per = 2 * EF * H // 32 * 18
+            slots = np.stack([ops.geglu_rows(ops.q40mv(gue[int(e) * per:(int(e) + 1) * per], moe_in, 2 * EF, H), EF)
+                              for e in idx])
+            t1 = ops.q40mv(self.t(b + "ffn_down.weight"), gd, H, FF)
+            m = ops.moe_down(slots, self.t(b + "ffn_down_exps.weight"), idx, w, EF, H)
         wn = nxt if nxt is not None else self.f(b + "attn_norm.weight")
         h, xn = ops.a4btail(t1, self.f(b + "post_ffw_norm_1.weight"), m, self.f(b + "post_ffw_norm_2.weight"),
                             self.f(b + "post_ffw_norm.weight"), hB, wn, eps, mul, nxt is not None)
         self.last_topk = (idx, w)
         return h, xn
+
+    # ---- long context (src/engine-a4b.js:589-657)
+    def compact(self, budget, protect):
+        """compactAll: every counted (global) cache keeps the slots
+        ops.budget_keep picks from its accumulated scores, gathered to the front
+        (kernels/kvgather.wgsl); scores reset; the count becomes the kept length."""
+        n = self.kv_count
+        kept = n
+        for l, sc in self.scores.items():
+            keep = ops.budget_keep(sc, n, budget, protect)
+            self.kc[l][:len(keep)] = self.kc[l][keep]
+            self.vc[l][:len(keep)] = self.vc[l][keep]
+            kept = len(keep)
+        self.reset_scores()
+        self.kv_count = kept
+
+    def generate_long(self, prompt, n_new, budget, decap, protect):
+        """generateLong: prefill (no scores), a scored probe step and a
+        compaction when the prompt exceeds `decap`, then decode in runs of 8
+        with scores accumulating, recompacting whenever the count would pass
+        `decap`.  Returns the greedy ids."""
+        self.reset()
+        self.scoring = False
+        tok = None
+        for pos, t in enumerate(prompt):
+            tok, _ = self.step(int(t), pos)
+        pos = len(prompt)
+        ids = [tok]
+        self.scoring = True
+        if self.kv_count > decap:
+            tok, _ = self.step(int(ids[-1]), pos)
+            pos += 1
+            ids.append(tok)
+            self.compact(budget, protect)
+        while len(ids) < n_new:
+            if self.kv_count + 8 > decap:
+                self.compact(budget, protect)
+            for _ in range(min(8, n_new - len(ids))):
+                tok, _ = self.step(int(ids[-1]), pos)
+                pos += 1
+                ids.append(tok)
+        self.scoring = False
+        return ids[:n_new]
 
     # ---- driver (src/engine-a4b.js:826-847 generateFast semantics)
     def generate(self, prompt, n_new, record=False):

@@ -239,6 +239,33 @@ def attend(q, kc, vc, valid, scale=1.0):
     return o.astype(F32), F32(m + np.log(den))
 
 
+def attention_mass(q, kcache, length, kvh, scale=1.0):
+    """Per-slot normalised attention probability of every q head over the first
+    `length` slots of a counted cache, [qh][length] f32: the SCORE=1 pass of
+    kernels/attnos.wgsl:82-97 (exp(s - gm) / denom)."""
+    qh, hd = q.shape
+    grp = qh // kvh
+    out = np.empty((qh, length), F32)
+    for h in range(qh):
+        k = kcache[:length, h // grp].astype(F32)
+        s = (k @ np.asarray(q[h], F32)) * F32(scale)
+        e = np.exp(s - s.max())
+        out[h] = e / e.sum(dtype=F32)
+    return out
+
+
+def budget_keep(scores, n, budget, protect):
+    """The slots a budget compaction keeps (src/engine-a4b.js:589-603): mass[t] =
+    sum over heads of the accumulated scores (f64), the `protect` most recent
+    slots always, plus the top (budget - protect) others by mass (ties: lower
+    slot first, the stable sort), ascending."""
+    mass = np.asarray(scores, np.float64)[:, :n].sum(axis=0)
+    prot = min(protect, n)
+    cand = np.argsort(-mass[:n - prot], kind="stable")
+    keep = np.concatenate([cand[:max(budget - prot, 0)], np.arange(n - prot, n)])
+    return np.sort(keep).astype(np.uint32)
+
+
 def decode_attention(q, kcache, vcache, qp, kvh, window, ring, cachemode, length):
     """Decode attention for all q heads (GQA kvh = h / (QH/KVH)); output f16-rounded
     like the reference's attnOut buffer.  cachemode 1 = sliding ring, 2 = linear."""
@@ -255,6 +282,43 @@ def decode_attention(q, kcache, vcache, qp, kvh, window, ring, cachemode, length
         o, _ = attend(q[h], kcache[:, h // grp], vcache[:, h // grp], valid)
         out[h] = o
     return f16r(out)
+
+
+# ------------------------------------------------------------ ternary experts
+
+def t2_unpack(w, cols):
+    """2-bit shift-group planes -> t in {-1, 0, 1} [rows][cols]: element 4g + j of a
+    word at bits 2g + 8j, stored t + 1 (scripts/ternarize_a4b.py pack_t2,
+    kernels/t2gu.wgsl t2dot16)."""
+    w = np.asarray(w, np.uint32).reshape(-1, cols // 16)
+    out = np.empty((w.shape[0], cols // 16, 16), np.int8)
+    for g in range(4):
+        for j in range(4):
+            out[:, :, 4 * g + j] = ((w >> np.uint32(2 * g + 8 * j)) & np.uint32(3)).astype(np.int8) - 1
+    return out.reshape(w.shape[0], cols)
+
+
+def t2gu(x, w, scale, topk, n_in, ff):
+    """Expert slots of the fused gate|up + GeGLU on ternary rows [e][gate ff | up ff]
+    (kernels/t2gu.wgsl expert branch): f16(gelu(a_g t_g.x) * a_u t_u.x) per slot."""
+    xs = np.asarray(x, F32)
+    out = np.empty((len(topk), ff), F32)
+    for k, e in enumerate(topk):
+        rows = t2_unpack(w[int(e) * 2 * ff * (n_in // 16):(int(e) + 1) * 2 * ff * (n_in // 16)], n_in).astype(F32)
+        sc = np.asarray(scale[int(e) * 2 * ff:(int(e) + 1) * 2 * ff]).astype(F32)
+        acc = (rows @ xs).astype(F32) * sc
+        out[k] = gelu_tanh(acc[:ff]) * acc[ff:]
+    return f16r(out)
+
+
+def t2moedown(x_slots, w, scale, topk, topk_w, n_in, n_out):
+    """y = sum_k w_k * a[e_k] * t[e_k] . x_k  (kernels/t2moedown.wgsl)."""
+    y = np.zeros(n_out, F32)
+    for k, e in enumerate(topk):
+        rows = t2_unpack(w[int(e) * n_out * (n_in // 16):(int(e) + 1) * n_out * (n_in // 16)], n_in).astype(F32)
+        sc = np.asarray(scale[int(e) * n_out:(int(e) + 1) * n_out]).astype(F32)
+        y = y + F32(topk_w[k]) * ((rows @ np.asarray(x_slots[k], F32)).astype(F32) * sc)
+    return y.astype(F32)
 
 
 # ------------------------------------------------------------ MoE

@@ -230,3 +230,16 @@ def test_oracle_q40mv_reference_kat(e4b):
     exact, mag = mvtest_exact(raw, x, rows, n_in)
     got = O.q40mv(raw, x, rows, n_in)
     assert np.all(np.abs(got - exact) <= 1e-6 * mag)
+
+
+def test_budget_keep_rule():
+    """compactAll's choice (src/engine-a4b.js:589-603): the protected most recent
+    slots always, the rest by accumulated mass summed over heads, ties to the
+    lower slot, result ascending."""
+    from oracle import ops as O
+    sc = np.zeros((2, 12), np.float32)
+    sc[0, :10] = [0.5, 0.1, 0.9, 0.1, 0.3, 0.9, 0.0, 0.2, 0.4, 0.1]
+    sc[1, :10] = [0.0, 0.0, 0.0, 0.0, 0.6, 0.0, 0.0, 0.0, 0.0, 0.0]
+    keep = O.budget_keep(sc, 10, 5, 2)          # slots 8, 9 protected; 3 of 0..7 by mass
+    assert keep.tolist() == [2, 4, 5, 8, 9]     # masses 0.9 (2), 0.9 (4), 0.9 (5): ties keep the lower slots
+    assert O.budget_keep(sc, 10, 12, 2).tolist() == list(range(10))
