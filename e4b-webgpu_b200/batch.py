@@ -529,12 +529,12 @@ class BatchEngine(Engine):
         d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
         self.check_status("prefill (last position)")
 
-    def generate(self, prompts, n_new: int):
-        """prompts [B][P] (same length) -> [B][n_new] greedy ids."""
+    def generate(self, prompts, n_new: int, chunk: int | None = None):
+        """prompts [B][P] (same length) -> [B][n_new] greedy ids; chunk as prefill's."""
         prompts = np.asarray(prompts)
         P = prompts.shape[1]
         assert P + n_new <= RING_CAP
-        self.prefill(prompts)
+        self.prefill(prompts, chunk=chunk)
         if n_new > 1:
             self.decode_chunk(n_new - 1)
         self.dev.sync()

@@ -37,9 +37,11 @@ def test_ep_dispatch_matches_oracle(e4b, dev):
 
 
 def _run_batch(e4b, buf, prompts, n_new, device, ep=None, zipf=None, tok0=0, transport="nccl"):
+    """Token-by-token prefill on every path, so that one GPU and the expert-
+    parallel ranks (which prefill token by token) run the same arithmetic."""
     eng = e4b.BatchEngine(buf, prompts.shape[0], device, ep=ep, zipf=zipf, tok0=tok0, ep_transport=transport)
     try:
-        ids = eng.generate(prompts, n_new)
+        ids = eng.generate(prompts, n_new, chunk=0)
         h = eng.read_hidden()
         assert eng.dev.status() == 0
     finally:
