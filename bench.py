@@ -938,6 +938,9 @@ def main():
         args.batch = 64 if (scale_series and args.config == "a4b") else 1
     if args.prefill is None:
         args.prefill = 1024 if args.config == "a4b" else 512
+    if world > 1 and os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        # NCCL's version banner goes to stdout; rank 0's stdout is the one JSON line
+        os.environ["NCCL_DEBUG"] = "WARN"
     if world > 1:
         # torchrun starts every worker with OMP_NUM_THREADS=1; the host-side weight
         # synthesis (OpenMP, loaded lazily) gets its share of the cores back
