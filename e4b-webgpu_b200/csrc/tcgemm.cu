@@ -10,10 +10,11 @@
 //   warp 0      TMA: token tiles [256 rows x 64 halves] of x (128-byte swizzle)
 //   warp 1      TMEM owner + MMA issuer (one thread): per K-step 8 x
 //               tcgen05.mma 128x256x16 into a double-buffered f32 accumulator
-//   warps 2-5   dequant: one weight row per thread; raw q4_0 bytes fetched with
-//               cp.async, decoded into an f16 "hi" tile and an f16 "lo" tile in
-//               the swizzled K-major layout the MMA reads (see below)
-//   warps 6-9   epilogue: tcgen05.ld of the accumulator, y (f32) or, for the
+//   warps 2-9   dequant: two threads per weight row (one q4_0 block of each
+//               K-step each); raw q4_0 bytes fetched with cp.async, decoded
+//               into an f16 "hi" tile and an f16 "lo" tile in the swizzled
+//               K-major layout the MMA reads (see below)
+//   warps 10-13 epilogue: tcgen05.ld of the accumulator, y (f32) or, for the
 //               fused gate|up, f16(gelu(gate) * up)
 // Exactness: a weight d*(n-8) needs up to 15 significant bits, more than f16
 // holds, so it is split as hi = f16(d*(n-8)) and lo = d*(n-8) - hi (exact in
@@ -32,11 +33,11 @@ constexpr int kTM = 128;                 // weight rows per tile
 constexpr int kTN = 256;                 // tokens per tile
 constexpr int kTK = 64;                  // K per step
 constexpr int kRawBlk = 8;               // q4_0 blocks per raw stage (4 K-steps)
-constexpr int kSA = 2, kSB = 3, kSR = 2; // stages: dequantised weights, tokens, raw bytes
+constexpr int kSA = 3, kSB = 2, kSR = 2; // stages: dequantised weights, tokens, raw bytes
 constexpr int kRawStride = 176;          // bytes per row of a raw stage (16-byte writes conflict free)
 constexpr int kTileA = kTM * 128;        // 16 KB: one f16 tile (hi or lo) of a K-step
 constexpr int kTileB = kTN * 128;        // 32 KB: the token tile of a K-step
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;           // 14 warps: TMA, MMA, 8 dequant, 4 epilogue
 constexpr int kMaxGroups = 256;
 constexpr uint32_t kTmemCols = 512;      // two 256-column f32 accumulators
 
@@ -133,10 +134,14 @@ E4B_DEV void tc_ld32(uint32_t taddr, float (&v)[32]) {
 E4B_DEV uint64_t sw128_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = 256,
+// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N <= 256,
 // optionally negating A.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
-constexpr uint32_t kIdescNegA = kIdesc | (1u << 13);
+// N = the tile's token rows rounded up to 16 (a group's last tile is usually
+// partial: its MMAs shrink with it).
+E4B_DEV uint32_t idesc_for(int nrows, bool neg_a) {
+  const uint32_t n = (uint32_t)min(kTN, max(16, (nrows + 15) & ~15));
+  return (1u << 4) | ((n >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24) | (neg_a ? (1u << 13) : 0u);
+}
 
 // ---------------------------------------------------------------- tiles
 // Tile order: per group, weight tile major, token tile minor (consecutive CTAs
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSA; i++) {
-      mbar_init(&S.a_full[i], kTM);
+      mbar_init(&S.a_full[i], 2 * kTM);     // two dequant threads per weight row
       mbar_init(&S.a_empty[i], 1);
     }
     for (int i = 0; i < kSB; i++) {
@@ -292,6 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
         if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + buf * (uint32_t)kTN;
+        const Tile T = tile_of(S, p, t);
+        const uint32_t idp = idesc_for(T.nrows, false), idn = idesc_for(T.nrows, true);
         for (int s = 0; s < p.nk; s++, ca++, cb++) {
           const int sa = ca % kSA, sb = cb % kSB;
           ok = wait_bar(&S.a_full[sa], (ca / kSA) & 1u, p.status, p.wait_ns) &&
@@ -303,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
 #pragma unroll
           for (int ks = 0; ks < kTK / 16; ks++) {
             const uint64_t bd = sw128_desc(b0 + 32 * ks);
-            tc_mma(d_tmem, sw128_desc(a_hi + 32 * ks), bd, kIdesc, (s | ks) != 0);
-            tc_mma(d_tmem, sw128_desc(a_lo + 32 * ks), bd, kIdescNegA, 1u);
+            tc_mma(d_tmem, sw128_desc(a_hi + 32 * ks), bd, idp, (s | ks) != 0);
+            tc_mma(d_tmem, sw128_desc(a_lo + 32 * ks), bd, idn, 1u);
           }
           tc_commit(&S.a_empty[sa]);
           tc_commit(&S.b_empty[sb]);
@@ -318,10 +325,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
       }
     }
     __syncwarp();
-  } else if (warp < 6) {
-    // ---------------- dequant: thread m owns weight row m of each tile
-    const int m = threadIdx.x - 64;
-    uint8_t* raw = sR + (size_t)m * kRawStride;                 // + stage * kTM * kRawStride
+  } else if (warp < 10) {
+    // ---------------- dequant: threads 2m, 2m+1 own weight row m of each tile;
+    // thread h decodes block h of every K-step (two q4_0 blocks per K-step)
+    const int dt = threadIdx.x - 64, m = dt >> 1, hh = dt & 1;
+    uint8_t* raw = sR + (size_t)m * kRawStride;                 // + stage * kTM * kRawStride, shared by the pair
     uint32_t ca = 0;
     bool ok = true;
     const int nraw = (p.nb + kRawBlk - 1) / kRawBlk;
@@ -338,7 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
         valid = wrow < p.OUT;
       }
       const uint8_t* src = p.w + ((size_t)T.g * p.wrows + (valid ? wrow : 0)) * p.rowbytes;
-      // raw stage r: blocks [8r, 8r + nblk) of this row: the 16-byte aligned cover
+      // raw stage r: blocks [8r, 8r + nblk) of this row: the 16-byte aligned
+      // cover, its chunks split between the row's two threads
       auto fetch = [&](int r) {
         if (!valid) return;
         const uint8_t* s0 = src + (size_t)r * kRawBlk * 18;
@@ -346,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
         const uint8_t* a0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(s0) & ~(uintptr_t)15);
         const uint8_t* a1 = s0 + nblk * 18;
         uint8_t* dst = raw + (size_t)(r % kSR) * kTM * kRawStride;
-        for (int i = 0; i < 10 && a0 + 16 * i < a1; i++) {
+        for (int i = hh; i < 10 && a0 + 16 * i < a1; i += 2) {
           const uint8_t* q = a0 + 16 * i;
           const long long left = p.w_end - q;
           cp_async16(dst + 16 * i, q, left >= 16 ? 16u : (uint32_t)left);
@@ -355,23 +364,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
       fetch(0);
       cp_async_commit();
       for (int r = 0; r < nraw && ok; r++) {
+        __syncwarp();                       // the pair is done reading the buffer about to be refilled
         if (r + 1 < nraw) fetch(r + 1);
         cp_async_commit();
         cp_async_wait<1>();
-        // this row's raw bytes of stage r as 36 aligned words
+        __syncwarp();                       // the partner's chunks of stage r are visible
         uint32_t wd[36];
         {
+          // the 16-byte aligned cover as ten 16-byte reads (row stride 176 = 11
+          // chunks: the 8 rows of a quarter warp hit 8 distinct bank groups; a
+          // row's two threads read the same addresses), then the row's bytes
+          // from word offset (sh / 4), shifted by (sh % 4)
           const uint8_t* s0 = src + (size_t)r * kRawBlk * 18;
           const int sh = (int)(reinterpret_cast<uintptr_t>(s0) & 15);
-          const uint8_t* rb = raw + (size_t)(r % kSR) * kTM * kRawStride + (sh & ~3);
+          const uint4* rb = reinterpret_cast<const uint4*>(raw + (size_t)(r % kSR) * kTM * kRawStride);
           const uint32_t fs = (uint32_t)(sh & 2) * 8;
-          uint32_t prev = *reinterpret_cast<const uint32_t*>(rb);
+          uint32_t cw[40];
 #pragma unroll
-          for (int j = 0; j < 36; j++) {
-            const uint32_t nx = *reinterpret_cast<const uint32_t*>(rb + 4 * j + 4);
-            wd[j] = valid ? __funnelshift_r(prev, nx, fs) : 0u;
-            prev = nx;
+          for (int i = 0; i < 10; i++) {
+            const uint4 v = rb[i];
+            cw[4 * i] = v.x;
+            cw[4 * i + 1] = v.y;
+            cw[4 * i + 2] = v.z;
+            cw[4 * i + 3] = v.w;
           }
+          switch (sh >> 2) {     // compile-time register indices in every branch
+#define E4B_WD(O)                                                                          \
+  case O:                                                                                  \
+    _Pragma("unroll") for (int j = 0; j < 36; j++) wd[j] = __funnelshift_r(cw[j + O], cw[j + O + 1], fs); \
+    break;
+            E4B_WD(0) E4B_WD(1) E4B_WD(2)
+            default:
+#pragma unroll
+              for (int j = 0; j < 36; j++) wd[j] = __funnelshift_r(cw[j + 3], cw[j + 4], fs);
+#undef E4B_WD
+          }
+          if (!valid)
+#pragma unroll
+            for (int j = 0; j < 36; j++) wd[j] = 0u;
         }
         const int nblk = min(kRawBlk, p.nb - r * kRawBlk);
 #pragma unroll
@@ -379,34 +409,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
           if (2 * k2 >= nblk || !ok) break;
           const int sa = ca % kSA;
           ok = wait_bar(&S.a_empty[sa], ((ca / kSA) & 1u) ^ 1u, p.status, p.wait_ns);
+          ok = __all_sync(0xffffffffu, ok);  // the pair's __syncwarp()s need the whole warp on one path
           if (!ok) break;
           uint8_t* th = sA + (size_t)sa * 2 * kTileA + (size_t)m * 128;
           uint8_t* tl = th + kTileA;
+          // block 2 k2 + hh: d at byte 18 b, nibbles at 18 b + 2; even b is
+          // word aligned, odd b two bytes past a word (both selected, no branch)
+          const int we = (18 * (2 * k2)) / 4, wo = (18 * (2 * k2 + 1) - 2) / 4;
+          const uint32_t d16 = hh ? (wd[wo] >> 16) : (wd[we] & 0xFFFFu);
+          uint32_t q[4];
 #pragma unroll
-          for (int bb = 0; bb < 2; bb++) {
-            const int b = 2 * k2 + bb;               // block within the raw stage (compile-time)
-            // block b starts at byte 18b: d at 18b, nibbles at 18b + 2
-            uint32_t d16, q[4];
-            if ((b & 1) == 0) {
-              const int w0 = (18 * b) / 4;
-              d16 = wd[w0] & 0xFFFFu;
+          for (int i = 0; i < 4; i++) q[i] = hh ? wd[wo + 1 + i] : __funnelshift_r(wd[we + i], wd[we + i + 1], 16);
+          uint4 hi[4], nlo[4];
+          decode_block(d16, q, hi, nlo);
 #pragma unroll
-              for (int i = 0; i < 4; i++) q[i] = __funnelshift_r(wd[w0 + i], wd[w0 + i + 1], 16);
-            } else {
-              const int w0 = (18 * b - 2) / 4;
-              d16 = wd[w0] >> 16;
-#pragma unroll
-              for (int i = 0; i < 4; i++) q[i] = wd[w0 + 1 + i];
-            }
-            uint4 hi[4], nlo[4];
-            decode_block(d16, q, hi, nlo);
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-              const int chunk = 4 * bb + c;
-              const uint32_t off = (uint32_t)((chunk ^ (m & 7)) << 4);
-              *reinterpret_cast<uint4*>(th + off) = hi[c];
-              *reinterpret_cast<uint4*>(tl + off) = nlo[c];
-            }
+          for (int c = 0; c < 4; c++) {
+            const int chunk = 4 * hh + c;
+            const uint32_t off = (uint32_t)((chunk ^ (m & 7)) << 4);
+            *reinterpret_cast<uint4*>(th + off) = hi[c];
+            *reinterpret_cast<uint4*>(tl + off) = nlo[c];
           }
           fence_proxy_async();              // generic-proxy writes -> the tensor core's reads
           mbar_arrive(&S.a_full[sa]);
