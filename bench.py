@@ -61,7 +61,9 @@ def under_torchrun() -> bool:
 class Dist:
     """Barrier and max-over-ranks for N > 1 (torch.distributed is plumbing only)."""
 
-    def __init__(self, world, local_rank, backend):
+    def __init__(self, world, local_rank, backend, timeout_s: float = 120.0):
+        """timeout_s bounds every collective: a rank that died or never joined
+        ends the others' next barrier / max with an error instead of a hang."""
         self.world = world
         self.pg = None
         if world > 1:
@@ -70,7 +72,7 @@ class Dist:
             import torch.distributed as td
             if backend == "nccl":
                 torch.cuda.set_device(local_rank)
-            td.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            td.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
             self.td, self.torch = td, torch
             self.dev = f"cuda:{local_rank}" if backend == "nccl" else "cpu"
 

@@ -200,3 +200,91 @@ def test_e4b_fused_matches_oracle(e4b):
         if a != b:
             assert margins[i] < TIE, (i, a, b, margins[i])
             break
+
+
+def _window_check(got_ids, ref_ids, margins, dlog, max_flips=2):
+    """Per-step greedy agreement over a window where both sides consumed the
+    same tokens: a step may disagree only where the oracle's top-2 logit margin
+    is a tie (< TIE) or is within twice that step's measured logit difference
+    (the numerical error the step itself shows), and at most `max_flips` steps
+    may disagree at all."""
+    flips = [i for i, (a, b) in enumerate(zip(got_ids, ref_ids)) if a != b]
+    for i in flips:
+        assert margins[i] < max(TIE, 2 * dlog[i]), (i, got_ids[i], ref_ids[i], margins[i], dlog[i])
+    assert len(flips) <= max_flips, flips
+
+
+def test_e4b_greedy_window_64(e4b):
+    """Full E4B shapes through the fused token kernel: a 16-token prompt then 64
+    greedy steps, the GPU engine and the oracle each on their own state but both
+    fed the oracle's greedy token every step (so one tie does not end the
+    comparison); the greedy id is checked at every step."""
+    buf = e4b.synth.build_model(e4b.config.e4b())
+    eng = e4b.Engine(buf, 0)
+    assert eng.fused
+    ref = OracleModel(buf)
+    prompt = [int(t) for t in e4b.synth.prompt_ids(16, eng.cfg.vocab, seed=3)]
+    got, want, margins, dlog = [], [], [], []
+    try:
+        tok = None
+        for pos in range(len(prompt) + 64):
+            t = prompt[pos] if pos < len(prompt) else tok
+            eng.step(int(t), pos)
+            rid, rec = ref.step(int(t), pos, record=True)
+            if pos >= len(prompt) - 1:
+                eng.dev.sync()
+                lg = eng.read_logits()
+                top2 = np.sort(rec["logits"])[-2:]
+                got.append(int(np.argmax(lg)))
+                want.append(rid)
+                margins.append(float(top2[1] - top2[0]))
+                dlog.append(float(np.max(np.abs(lg - rec["logits"]))))
+            tok = rid
+        assert eng.dev.status() == 0
+    finally:
+        eng.close()
+    assert len(got) == 65
+    _window_check(got, want, margins, dlog)
+
+
+def test_a4b_batch_engine_full_size(e4b):
+    """Benchmark config 4 at full size (30 layers, hidden 2816, 128 experts top-8,
+    vocabulary 262144) through the batched engine: two sequences, an 8-token
+    prompt and 16 greedy steps each, both sides fed the oracle's greedy tokens;
+    the greedy ids checked at every step of both sequences."""
+    buf = e4b.synth.build_model(e4b.config.a4b())
+    B, P, N = 2, 8, 16
+    prompts = np.stack([e4b.synth.prompt_ids(P, 262144, seed=50 + b) for b in range(B)])
+    eng = e4b.BatchEngine(buf, B, 0)
+    refs = [OracleModel(buf) for _ in range(B)]
+    got = [[] for _ in range(B)]
+    want = [[] for _ in range(B)]
+    margins = [[] for _ in range(B)]
+    dlog = [[] for _ in range(B)]
+    try:
+        toks = prompts[:, 0].copy()
+        for pos in range(P + N):
+            if pos < P:
+                toks = prompts[:, pos].copy()
+            eng.step(toks, pos)
+            nxt = np.empty(B, np.uint32)
+            recs = []
+            for b in range(B):
+                rid, rec = refs[b].step(int(toks[b]), pos, record=True)
+                nxt[b] = rid
+                recs.append(rec)
+            if pos >= P - 1:
+                eng.dev.sync()
+                lg = eng.read_logits()
+                for b in range(B):
+                    top2 = np.sort(recs[b]["logits"])[-2:]
+                    got[b].append(int(np.argmax(lg[b])))
+                    want[b].append(int(nxt[b]))
+                    margins[b].append(float(top2[1] - top2[0]))
+                    dlog[b].append(float(np.max(np.abs(lg[b] - recs[b]["logits"]))))
+            toks = nxt
+        assert eng.dev.status() == 0
+    finally:
+        eng.close()
+    for b in range(B):
+        _window_check(got[b], want[b], margins[b], dlog[b])
