@@ -214,37 +214,78 @@ def _window_check(got_ids, ref_ids, margins, dlog, max_flips=2):
     assert len(flips) <= max_flips, flips
 
 
+class _NoisyF16:
+    """Within the block, every f16 rounding of the oracle first scales its input
+    by (1 + 1e-6 N(0,1)): the oracle's own sensitivity to f32 summation order."""
+
+    def __init__(self, seed):
+        self.rng = np.random.default_rng(seed)
+
+    def __enter__(self):
+        from oracle import ops as O
+        self.O, self.orig = O, O.f16r
+        rng, orig = self.rng, self.orig
+
+        def noisy(x):
+            x = np.asarray(x, np.float32)
+            return orig((x * (1 + 1e-6 * rng.standard_normal(x.shape))).astype(np.float32))
+        O.f16r = noisy
+        return self
+
+    def __exit__(self, *a):
+        self.O.f16r = self.orig
+
+
 def test_e4b_greedy_window_64(e4b):
     """Full E4B shapes through the fused token kernel: a 16-token prompt then 64
-    greedy steps, the GPU engine and the oracle each on their own state but both
-    fed the oracle's greedy token every step (so one tie does not end the
-    comparison); the greedy id is checked at every step."""
+    greedy steps, with the GPU engine, the oracle and a second oracle whose f16
+    roundings see 1e-6 relative noise each on their own state, all fed the
+    oracle's greedy token every step (so a disagreement does not end the
+    comparison).  This 35-layer random-weight model amplifies rounding
+    differences chaotically over positions (measured: logit differences of
+    ~0.5 after 16 positions between the oracle and its own 1e-6 perturbation),
+    so greedy identity over the window is not a property any two f32
+    summation orders share.  Checked instead, per step: the GPU's logits are
+    no further from the oracle than 3x the perturbed oracle's (or 1e-2 of the
+    logit scale), every greedy disagreement lies within twice that step's
+    measured logit difference, and the GPU disagrees with the oracle at most
+    as often as the perturbed oracle does, plus 2."""
     buf = e4b.synth.build_model(e4b.config.e4b())
     eng = e4b.Engine(buf, 0)
     assert eng.fused
-    ref = OracleModel(buf)
+    ref, pert = OracleModel(buf), OracleModel(buf)
     prompt = [int(t) for t in e4b.synth.prompt_ids(16, eng.cfg.vocab, seed=3)]
-    got, want, margins, dlog = [], [], [], []
+    rows = []          # (step, gpu id, oracle id, perturbed id, margin, |dlog| gpu, |dlog| perturbed)
     try:
         tok = None
         for pos in range(len(prompt) + 64):
             t = prompt[pos] if pos < len(prompt) else tok
             eng.step(int(t), pos)
             rid, rec = ref.step(int(t), pos, record=True)
+            with _NoisyF16(1000 + pos):
+                pid, prec = pert.step(int(t), pos, record=True)
             if pos >= len(prompt) - 1:
                 eng.dev.sync()
                 lg = eng.read_logits()
                 top2 = np.sort(rec["logits"])[-2:]
-                got.append(int(np.argmax(lg)))
-                want.append(rid)
-                margins.append(float(top2[1] - top2[0]))
-                dlog.append(float(np.max(np.abs(lg - rec["logits"]))))
+                rows.append((pos, int(np.argmax(lg)), rid, pid, float(top2[1] - top2[0]),
+                             float(np.max(np.abs(lg - rec["logits"]))),
+                             float(np.max(np.abs(prec["logits"] - rec["logits"])))))
             tok = rid
         assert eng.dev.status() == 0
     finally:
         eng.close()
-    assert len(got) == 65
-    _window_check(got, want, margins, dlog)
+    assert len(rows) == 65
+    scale = 1e-2 * max(np.max(np.abs(rec["logits"])), 1.0)
+    for r in rows:
+        assert r[5] <= max(3 * r[6], scale), r
+        if r[1] != r[2]:
+            assert r[4] < max(TIE, 2 * r[5]), r
+    flips_gpu = sum(r[1] != r[2] for r in rows)
+    flips_pert = sum(r[3] != r[2] for r in rows)
+    print(f"e4b window: {flips_gpu} GPU / {flips_pert} perturbed-oracle disagreements in {len(rows)} steps; "
+          f"median |dlogits| {np.median([r[5] for r in rows]):.3f} GPU vs {np.median([r[6] for r in rows]):.3f}")
+    assert flips_gpu <= flips_pert + 2, (flips_gpu, flips_pert)
 
 
 def test_a4b_batch_engine_full_size(e4b):
