@@ -161,35 +161,52 @@ E4B_DEV uint32_t mix32(uint32_t x) {
   x ^= x >> 16;
   return x;
 }
-__global__ void k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __restrict__ topk_idx,
-                             float* __restrict__ topk_w, int n_tok, int K, int E, float s, uint32_t seed, int salt,
-                             int tok0, int nseq) {
+// Benchmark routing.  Per CTA: the Zipf(s) popularity table (cumulative, by a
+// fixed-order inclusive scan) and a seeded permutation saying which experts are
+// popular; then one warp per token: the token draws from its own hash stream,
+// 32 attempts at a time across the lanes, and keeps the first K distinct
+// experts in attempt order (exactly what drawing one attempt after another
+// would keep).
+__global__ void __launch_bounds__(256) k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __restrict__ topk_idx,
+                                                    float* __restrict__ topk_w, int n_tok, int K, int E, float s,
+                                                    uint32_t seed, int salt, int tok0, int nseq) {
   pdl_wait();
   extern __shared__ float cdf[];          // [E] cumulative popularity, then [E] rank -> expert (as bits)
   uint32_t* perm = reinterpret_cast<uint32_t*>(cdf + E);
-  if (threadIdx.x == 0) {
-    float acc = 0.f;
-    for (int r = 0; r < E; r++) {
-      acc += powf((float)(r + 1), -s);
-      cdf[r] = acc;
-      perm[r] = (uint32_t)r;
-    }
-    for (int r = 0; r < E; r++) cdf[r] /= acc;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = threadIdx.x; r < E; r += blockDim.x) {
+    cdf[r] = powf((float)(r + 1), -s);
+    perm[r] = (uint32_t)r;
+  }
+  __syncthreads();
+  for (int off = 1; off < E; off <<= 1) {          // Hillis-Steele inclusive scan, fixed order
+    float v[16];
+    int n = 0;
+    for (int r = threadIdx.x; r < E; r += blockDim.x, n++) v[n & 15] = r >= off ? cdf[r - off] : 0.f;
+    __syncthreads();
+    n = 0;
+    for (int r = threadIdx.x; r < E; r += blockDim.x, n++) cdf[r] += v[n & 15];
+    __syncthreads();
+  }
+  const float tot = cdf[E - 1];
+  __syncthreads();
+  for (int r = threadIdx.x; r < E; r += blockDim.x) cdf[r] /= tot;
+  if (threadIdx.x == 0)
     for (int r = E - 1; r > 0; r--) {     // seeded Fisher-Yates: which experts are popular
       const uint32_t j = mix32(seed ^ (0x9e3779b9u * (uint32_t)r)) % (uint32_t)(r + 1);
       const uint32_t t = perm[r];
       perm[r] = perm[j];
       perm[j] = t;
     }
-  }
   __syncthreads();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_tok; i += gridDim.x * blockDim.x) {
+  for (int i = blockIdx.x * nw + warp; i < n_tok; i += gridDim.x * nw) {
     // row i: sequence tok0 + i % nseq at position params[0] + i / nseq
     const uint32_t pos = params[0] + (uint32_t)(i / nseq);
     const uint32_t tk = (uint32_t)(tok0 + i % nseq);
-    uint32_t chosen[32];
+    uint32_t chosen = 0xffffffffu;        // lane k < K holds the k-th expert kept
     int got = 0;
-    for (uint32_t attempt = 0; got < K && attempt < 4096u; attempt++) {
+    for (uint32_t a0 = 0; got < K && a0 < 4096u; a0 += 32) {
+      const uint32_t attempt = a0 + (uint32_t)lane;
       const uint32_t h = mix32(seed ^ mix32((uint32_t)salt * 0x85ebca6bu ^ mix32(pos ^ mix32(tk ^ (attempt << 20)))));
       const float u = (float)(h >> 8) * (1.0f / 16777216.0f);
       int lo = 0, hi = E - 1;
@@ -199,19 +216,26 @@ __global__ void k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __re
         else lo = mid + 1;
       }
       const uint32_t e = perm[lo];
-      bool dup = false;
-      for (int k = 0; k < got; k++) dup |= chosen[k] == e;
-      if (!dup) chosen[got++] = e;
+      for (int j = 0; j < 32 && got < K; j++) {      // attempts in order
+        const uint32_t ej = __shfl_sync(0xffffffffu, e, j);
+        const bool dup = __any_sync(0xffffffffu, lane < got && chosen == ej);
+        if (!dup) {
+          if (lane == got) chosen = ej;
+          got++;
+        }
+      }
     }
     for (int r = 0; got < K && r < E; r++) {   // (never needed in practice) fill by popularity
       const uint32_t e = perm[r];
-      bool dup = false;
-      for (int k = 0; k < got; k++) dup |= chosen[k] == e;
-      if (!dup) chosen[got++] = e;
+      const bool dup = __any_sync(0xffffffffu, lane < got && chosen == e);
+      if (!dup) {
+        if (lane == got) chosen = e;
+        got++;
+      }
     }
-    for (int k = 0; k < K; k++) {
-      topk_idx[(size_t)i * K + k] = chosen[k];
-      topk_w[(size_t)i * K + k] = 1.0f / (float)K;
+    if (lane < K) {
+      topk_idx[(size_t)i * K + lane] = chosen;
+      topk_w[(size_t)i * K + lane] = 1.0f / (float)K;
     }
   }
 }
@@ -364,8 +388,8 @@ E4B_API int e4b_route_zipf(e4b_ctx* c, const uint32_t* params, uint32_t* topk_id
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, params && topk_idx && topk_w && n_tok > 0 && K > 0 && K <= 32 && K <= E && E <= 4096 && s > 0.f,
               "route_zipf: bad args");
-  return e4b_launch(c, "route_zipf", k_route_zipf, dim3(1), dim3(256), (size_t)E * 8, params, topk_idx, topk_w, n_tok,
-                    K, E, s, seed, salt, tok0, n_tok);
+  return e4b_launch(c, "route_zipf", k_route_zipf, dim3((n_tok + 7) / 8), dim3(256), (size_t)E * 8, params, topk_idx,
+                    topk_w, n_tok, K, E, s, seed, salt, tok0, n_tok);
 }
 
 E4B_API int e4b_route_zipf_rows(e4b_ctx* c, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int nseq,
@@ -374,8 +398,8 @@ E4B_API int e4b_route_zipf_rows(e4b_ctx* c, const uint32_t* params, uint32_t* to
   E4B_REQUIRE(c, params && topk_idx && topk_w && nseq > 0 && npos > 0 && K > 0 && K <= 32 && K <= E && E <= 4096 &&
                      s > 0.f,
               "route_zipf_rows: bad args");
-  // every CTA builds the popularity table itself, then routes its rows
-  return e4b_launch(c, "route_zipf", k_route_zipf, dim3((nseq * npos + 255) / 256), dim3(256), (size_t)E * 8, params,
+  // every CTA builds the popularity table itself, then routes its rows (a warp per row)
+  return e4b_launch(c, "route_zipf", k_route_zipf, dim3((nseq * npos + 7) / 8), dim3(256), (size_t)E * 8, params,
                     topk_idx, topk_w, nseq * npos, K, E, s, seed, salt, tok0, nseq);
 }
 
