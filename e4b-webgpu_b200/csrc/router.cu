@@ -118,19 +118,18 @@ __global__ void __launch_bounds__(256) k_router_part(const float* __restrict__ x
   }
 }
 
+// One CTA per token: every thread sums one expert's slices (in slice order,
+// loads issued together), then warp 0 runs the softmax / top-K.
 __global__ void __launch_bounds__(256) k_router_topk(const float* __restrict__ part, const float* __restrict__ pes,
                                                      uint32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
                                                      int B, int E, int K, int slices) {
   pdl_wait();
-  extern __shared__ float pw[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x * 8 + warp;
+  extern __shared__ __align__(16) float pw[];
+  const int b = blockIdx.x;
   if (b >= B) return;
-  float* p = pw + (size_t)warp * E;
-  for (int e = lane; e < E; e += 32) {
-    // slices summed in order; the loads are independent and issued together
+  const size_t step = (size_t)B * E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const float* src = part + (size_t)b * E + e;
-    const size_t step = (size_t)B * E;
     float v = 0.f;
     int s = 0;
     for (; s + 8 <= slices; s += 8) {
@@ -141,10 +140,10 @@ __global__ void __launch_bounds__(256) k_router_topk(const float* __restrict__ p
       for (int u = 0; u < 8; u++) v += t[u];
     }
     for (; s < slices; s++) v += src[s * step];
-    p[e] = v;
+    pw[e] = v;
   }
-  __syncwarp();
-  softmax_topk(p, E, K, pes, topk_idx + (size_t)b * K, topk_w + (size_t)b * K);
+  __syncthreads();
+  if (threadIdx.x < 32) softmax_topk(pw, E, K, pes, topk_idx + (size_t)b * K, topk_w + (size_t)b * K);
 }
 
 // Skewed routing for the expert-parallel benchmark (benchmark config 5: a seeded
@@ -369,15 +368,15 @@ E4B_API int e4b_routertop(e4b_ctx* c, const float* x, const float* wr, const flo
   if (batch < 1) batch = 1;
   const int slices = (H + kRtK - 1) / kRtK;
   const size_t part_bytes = (size_t)slices * batch * E * 4;
-  if (c->ws && c->ws_bytes >= e4b::kWsCounterBytes + part_bytes && (size_t)8 * E * 4 <= 48 * 1024) {
+  if (c->ws && c->ws_bytes >= e4b::kWsCounterBytes + part_bytes && (size_t)E * 4 <= 48 * 1024) {
     // the split-K partial area of the workspace (free between launches)
     float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c->ws) + e4b::kWsCounterBytes);
     if (int r = e4b_launch(c, "router_part", k_router_part,
                            dim3((batch + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, slices), dim3(256), 0, x,
                            wr, part, batch, H, E))
       return r;
-    return e4b_launch(c, "router_topk", k_router_topk, dim3((batch + 7) / 8), dim3(256), (size_t)8 * E * 4,
-                      (const float*)part, pes, topk_idx, topk_w, batch, E, K, slices);
+    return e4b_launch(c, "router_topk", k_router_topk, dim3(batch), dim3(E < 256 ? ((E + 31) / 32) * 32 : 256),
+                      (size_t)E * 4, (const float*)part, pes, topk_idx, topk_w, batch, E, K, slices);
   }
   return e4b_launch(c, "routertop", k_routertop, dim3(batch), dim3(256), (size_t)E * 4, x, wr, pes, topk_idx, topk_w,
                     H, E, K);
