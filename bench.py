@@ -840,6 +840,55 @@ def run_tcgemm(e4b, dev, args):
         raise SystemExit(f"device status {st:#x}")
 
 
+def run_lmhead(e4b, dev, args):
+    """The batched LM head at the A4B shape: 262144 x 2816 q6_K (605 MB, above L2,
+    so every launch streams the weights from HBM) for n token rows, each n on
+    the tile-packed copy (e4b_q6k_lmhead_tiles), and through
+    e4b_q6k_lmhead_rows on the tcgen05 kernel and on the mma.sync one
+    ("lmhead_tc_min" 1 / 65).  Weights are random q6_K bytes with a fixed
+    superblock scale (timing only).  Algorithmic bytes = weights + x (f32) +
+    logits (f32)."""
+    cfg = e4b.config.get("a4b")
+    V, H = cfg.vocab, cfg.hidden
+    nsb = H // 256
+    rng = np.random.default_rng(0)
+    raw = rng.integers(0, 256, size=(V * nsb, 210), dtype=np.uint8)
+    raw[:, 208:210] = np.frombuffer(np.float16(1e-3).tobytes(), np.uint8)
+    w = dev.upload(raw.reshape(-1), "lm_w")
+    del raw
+    wt = dev.alloc(int(dev.L.e4b_q6k_packed_bytes(H, V)), "lm_wt")
+    dev.call("e4b_q6k_pack_tiles", w, wt, H, V)
+    hbm, kind_h = peaks()
+    out = []
+    for n in args.rows:
+        x = dev.upload(rng.standard_normal((n, H), dtype=np.float32), "x")
+        y = dev.alloc(n * V * 4, "y")
+        scr = dev.alloc(2 * max(64, (n + 7) // 8 * 8) * H * 2, "scr")
+        row = {"n": n}
+        for label, tc in (("tiles", 0), ("tc", 1), ("mma_sync", 65)):
+            if tc:
+                dev.call("e4b_set_option", b"lmhead_tc_min", tc)
+            def loop(x=x, y=y, scr=scr, n=n, tc=tc):
+                for _ in range(args.launches):
+                    if tc == 0:
+                        dev.call("e4b_q6k_lmhead_tiles", wt, x, scr, y, H, V, np.float32(cfg.softcap), n)
+                    else:
+                        dev.call("e4b_q6k_lmhead_rows", w, x, scr, y, H, V, np.float32(cfg.softcap), n)
+            us = graph_time(dev, loop) / args.launches
+            byts = V * nsb * 210 + n * H * 4 + n * V * 4
+            row[label] = {"us": round(us, 1), "gbs": round(byts / us / 1e3, 1), "frac": round(byts / us / 1e3 / hbm, 4),
+                          "useful_tflops": round(2.0 * n * V * H / us / 1e6, 1)}
+        dev.call("e4b_set_option", b"lmhead_tc_min", 1)
+        out.append(row)
+        dev.free(x), dev.free(y), dev.free(scr)
+    st = dev.status()
+    dev.close()
+    print(json.dumps({"kernel": "lmhead", "desc": "e4b_q6k_lmhead_rows, A4B LM head 262144 x 2816 q6_K",
+                      "peak_gbs": hbm, "peak_source": kind_h, "rows": out, "status": st}))
+    if st:
+        raise SystemExit(f"device status {st:#x}")
+
+
 def run_kernel(args):
     """Time one streaming kernel alone: `launches` launches cycling over enough
     distinct weight copies that the working set exceeds L2."""
@@ -854,6 +903,8 @@ def run_kernel(args):
         return run_attn(e4b, dev, args)
     if args.kernel == "tcgemm":
         return run_tcgemm(e4b, dev, args)
+    if args.kernel == "lmhead":
+        return run_lmhead(e4b, dev, args)
     desc, rows, n_in, kind = KERNELS[args.kernel]
     ws = int(dev.L.e4b_workspace_bytes())
     wsb = dev.alloc(ws, "workspace")
@@ -918,11 +969,13 @@ def main():
                     help="default one-GPU run: skip the nested config-5 (A4B bs64) measurement")
     ap.add_argument("--moe-budget", type=float, default=600.0,
                     help="wall-clock budget (s) of the nested config-5 measurement")
-    ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain", "attn", "tcgemm"],
+    ap.add_argument("--kernel", choices=sorted(KERNELS) + ["rmschain", "attn", "tcgemm", "lmhead"],
                     help="time one kernel alone instead of the decode")
     ap.add_argument("--tokens", type=int, default=4096, help="--kernel tcgemm: token rows of the prefill chunk")
     ap.add_argument("--trace", action="store_true", help="per-phase timing of the fused token kernel")
     ap.add_argument("--launches", type=int, default=200)
+    ap.add_argument("--rows", type=int, nargs="+", default=[1, 8, 16, 32, 64],
+                    help="--kernel lmhead: token rows per launch")
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1/0)")
     ap.add_argument("--ctas-per-sm", type=int, default=1)
     ap.add_argument("--stages", type=int, default=4)

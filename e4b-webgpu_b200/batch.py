@@ -20,7 +20,8 @@ Every f16 activation that feeds a q4_0 GEMM (normed rows, attention output,
 MoE input, GeGLU outputs) is kept in fragment order (xfo_perm), written so
 by its producer.
 
-then the final norm, e4b_q6k_lmhead_rows, e4b_argmax_rows and
+then the final norm, e4b_q6k_lmhead_tiles (on a tile-packed copy of the
+q6_K embedding), e4b_argmax_rows and
 e4b_feedtok_rows (each sequence's greedy token fed back on the device).
 """
 from __future__ import annotations
@@ -153,11 +154,15 @@ class BatchEngine(Engine):
         A.yo = d.alloc(B * K * H * 4, "expOut")
         A.moe_out = d.alloc(B * H * 4, "moeOut")
         A.xf = d.alloc(B * H * 4, "xfinal")
-        A.xsplit = d.alloc(2 * ((B + 7) // 8 * 8) * H * 2, "xSplit")
+        A.xsplit = d.alloc(2 * max(64, (B + 7) // 8 * 8) * H * 2, "xSplit")
         A.logits = d.alloc(B * c.vocab * 4, "logits")
         A.amax_part = d.alloc(B * ARGMAX_PARTS * 8, "amaxPart")
         A.amax = d.alloc(B * 8, "amax")
         A.ring = d.alloc(B * RING_CAP * 4, "tokRing")
+        # the LM head streams a tile-packed copy of the (tied) q6_K embedding: one
+        # contiguous TMA copy per 128 rows x superblock (e4b_q6k_lmhead_tiles)
+        self.emb_tiles = self._pack_lm_head(self.emb, c.vocab) if B <= 64 else None
+        self.emb_shard_tiles = None
         if self.ep is not None:
             self._alloc_ep(A)
         self.A = A
@@ -208,12 +213,28 @@ class BatchEngine(Engine):
             Bt, Vs = N * B, V // N
             self.vs = Vs
             A.xf_all = d.alloc(Bt * H * 4, "xfAll")
-            A.xsplit_all = d.alloc(2 * ((Bt + 7) // 8 * 8) * H * 2, "xSplitAll")
+            A.xsplit_all = d.alloc(2 * max(64, (Bt + 7) // 8 * 8) * H * 2, "xSplitAll")
             A.logits_s = d.alloc(Bt * Vs * 4, "logitsShard")
             A.amax_part_s = d.alloc(Bt * ARGMAX_PARTS * 8, "amaxPartShard")
             A.amax_s = d.alloc(Bt * 8, "amaxShard")
             A.amax_all = d.alloc(N * Bt * 8, "amaxAll")
             self.emb_shard = ctypes.c_void_p(self.emb.ptr + rank * Vs * (H // 256) * 210)
+            if Bt <= 64:
+                self.emb_shard_tiles = self._pack_lm_head(self.emb_shard, Vs)
+
+    def _pack_lm_head(self, w, rows):
+        d, H = self.dev, self.cfg.hidden
+        buf = d.alloc(int(d.L.e4b_q6k_packed_bytes(H, rows)), "lmHeadTiles")
+        d.call("e4b_q6k_pack_tiles", w, buf, H, rows)
+        return buf
+
+    def _lm_head(self, w, wt, x, xsplit, logits, rows, n):
+        """softcap(W x) for n rows of x: the tile-packed copy when there is one."""
+        c, d = self.cfg, self.dev
+        if wt is not None and n <= 64:
+            d.call("e4b_q6k_lmhead_tiles", wt, x, xsplit, logits, c.hidden, rows, ctypes.c_float(c.softcap), n)
+        else:
+            d.call("e4b_q6k_lmhead_rows", w, x, xsplit, logits, c.hidden, rows, ctypes.c_float(c.softcap), n)
 
     def _map_peers(self, A, N: int, rank: int):
         """Peer-memory transport: export this rank's receive slabs and flag
@@ -393,13 +414,12 @@ class BatchEngine(Engine):
             N, rank = self.ep[0], self.ep[1]
             Bt = N * B
             d.call("e4b_ep_allgather", A.xf, A.xf_all, ctypes.c_size_t(B * H * 4))
-            d.call("e4b_q6k_lmhead_rows", self.emb_shard, A.xf_all, A.xsplit_all, A.logits_s, H, self.vs,
-                   ctypes.c_float(c.softcap), Bt)
+            self._lm_head(self.emb_shard, self.emb_shard_tiles, A.xf_all, A.xsplit_all, A.logits_s, self.vs, Bt)
             d.call("e4b_argmax_rows", A.logits_s, A.amax_part_s, A.amax_s, self.vs, ARGMAX_PARTS, Bt)
             d.call("e4b_ep_allgather", A.amax_s, A.amax_all, ctypes.c_size_t(Bt * 8))
             d.call("e4b_argmax_merge", A.amax_all, N, Bt, self.vs, rank * B, B, A.amax)
         else:
-            d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)
+            self._lm_head(self.emb, self.emb_tiles, A.xf, A.xsplit, A.logits, V, B)
             d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
         d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
 
@@ -524,7 +544,7 @@ class BatchEngine(Engine):
         self.host_params[:] = (P - 1, P, 0, 0, P - 1, P, P - 1, 0)
         d.write(A.params, self.host_params)
         d.call("e4b_rmsnorm", last, self.out_norm, A.xf, None, None, H, B, eps, 1, 0, 0)
-        d.call("e4b_q6k_lmhead_rows", self.emb, A.xf, A.xsplit, A.logits, H, V, ctypes.c_float(c.softcap), B)
+        self._lm_head(self.emb, self.emb_tiles, A.xf, A.xsplit, A.logits, V, B)
         d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
         d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
         self.check_status("prefill (last position)")

@@ -28,6 +28,7 @@ struct e4b_ctx {
   int stream_variant = 0;           // GEMV warps x piece size: 0 = 8x32, 1 = 16x16, 2 = 16x8
   int attn_grid_cap = 0;            // batched attention: at most this many CTAs (0 = one per SM)
   uint64_t wait_ns = 1000000000ull; // bound of the batched attention's and ep_wait's device waits
+  int lmhead_tc_min = 1;             // batched LM head: tcgen05 kernel for n >= this (<= 64)
   cudaEvent_t ev[64] = {};
   std::vector<cudaGraphExec_t> plans;
   cudaGraph_t cap_graph = nullptr;

@@ -28,4 +28,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 bool lmhead_stream_supported(const uint8_t* w, const float* x, int N);
 int lmhead_stream(e4b_ctx* c, const uint8_t* w, const float* x, float* y, int N, int OUT, float softcap);
 
+// Batched q6_K LM head on tcgen05 (q6tc.cu): n <= 64 token rows; scratch holds
+// 2 * 64 * N halves.
+bool q6tc_supported(const uint8_t* w, const void* scratch, int N, int OUT, int n);
+int q6tc_lmhead(e4b_ctx* c, const uint8_t* w, bool packed, const float* x, uint16_t* scratch, float* y, int N,
+                int OUT, float softcap, int n);
+
 }  // namespace e4b

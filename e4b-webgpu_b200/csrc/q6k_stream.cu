@@ -17,6 +17,7 @@
 // The 6-bit values are assembled four at a time with byte-parallel masks,
 // turned into exact f32 (q - 32) with the 2^23 magic-number trick, multiplied
 // by x in f32, and scaled per sub-block by sc * d (kernels/q6k.wgsl:44-68).
+#include "q40_stream.cuh"
 #include "stream.cuh"
 
 namespace {
@@ -457,6 +458,8 @@ E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* c, const uint8_t* w, const float* x, ui
                                 int OUT, float softcap, int n) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, w && x && scratch && y && N > 0 && N % 256 == 0 && OUT > 0 && n > 0, "q6k_lmhead_rows: bad args");
+  if (n >= c->lmhead_tc_min && e4b::q6tc_supported(w, scratch, N, OUT, n))
+    return e4b::q6tc_lmhead(c, w, false, x, scratch, y, N, OUT, softcap, n);
   if (OUT % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(scratch) % 16 == 0) {
     // staged path: every superblock's aligned cover lies inside [w, w + OUT * rowbytes)
     const int NG = (n + 7) / 8;

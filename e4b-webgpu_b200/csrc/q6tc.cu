@@ -1,0 +1,517 @@
+// Batched q6_K LM head on the 5th-generation tensor cores (sm_100a):
+//   y[t][o] = softcap( sum_b d[o][b] * sum_{j<16} sc[o][b][j] * sum_{i in j} (q[o][i] - 32) * x[t][i] )
+// for up to 64 token rows t -- the reference's LM head (kernels/q6kmv.wgsl,
+// f32 dequantisation and accumulation; its batched-decode form runs it once
+// per sequence) for a whole decode batch at once.
+//
+// Tile = 128 vocabulary rows (UMMA M, TMEM lanes); the batch's tokens are the
+// UMMA N side: B = [x_hi (NP rows); x_lo (NP rows)], x = x_hi + x_lo split into
+// two f16 halves by k_q6tc_prep, NP = 32 or 64.  K in steps of 64 (one
+// 128-byte swizzle row of f16).  Per CTA (one per SM, persistent over tiles),
+// warp-specialised:
+//   warp 0      TMA: the [2 NP x 64] slab of B for each K-step
+//   warp 1      TMEM owner + MMA issuer (one thread)
+//   warps 2-17  dequant: four threads per vocabulary row, one q6_K
+//               superblock (256 k = 4 K-steps) per raw stage
+//   warps 18-21 epilogue: per superblock, tcgen05.ld of its accumulator,
+//               times d, added to the tile's running sum (kept in TMEM);
+//               softcap and store at the tile's end
+//   warp 22     raw weights: per superblock one 1-D TMA bulk copy per row (the
+//               16-byte aligned 224-byte cover of its 210 bytes), three
+//               superblocks in flight
+//
+// Exactness.  The superblock scale d (f16) is applied in f32 by the epilogue;
+// inside a superblock the weight is the integer m = sc * (q - 32), |m| <= 4096,
+// which f16 holds exactly only up to 2048.  So A is split like the q4_0 GEMM
+// does: hi = f16(m) (one f16 multiply) and lo = m - hi in {-1, 0, 1} (one f16
+// FMA, exact), lo stored negated and the MMA negating it back.  Per K = 16:
+//   MMA 1: hi x [x_hi; x_lo]  (N = 2 NP: columns [0, NP) and [NP, 2 NP))
+//   MMA 2: lo x  x_hi         (N = NP, into columns [0, NP))
+// Every product is exact in the f32 accumulator; the dropped lo * x_lo term is
+// below 2^-23 of the hi * x terms it sits beside (|lo| <= 1 where |m| > 2048,
+// |x_lo| <= 2^-11 |x|).  Each superblock accumulates into its own 2 NP
+// TMEM columns (three buffers rotate), which the epilogue folds into the
+// running sum as y += d * (C[t] + C[NP + t]).
+#include "q40_stream.cuh"
+#include "tc.cuh"
+
+namespace {
+using namespace e4b;
+
+constexpr int kQM = 128;                   // vocabulary rows per tile
+constexpr int kQK = 64;                    // K per step
+constexpr int kQSA = 3, kQSB = 2, kQSR = 3;  // stages: dequantised A, token slabs, raw superblocks
+constexpr int kQCover = 224;               // 16-byte aligned cover of a 210-byte superblock
+constexpr int kQRawStride = 240;           // bytes per row of a raw stage (15 x 16: odd chunk count)
+constexpr int kQTileA = kQM * 128;         // 16 KB: one f16 tile (hi or -lo) of a K-step
+constexpr int kQMaxNP = 64;
+constexpr int kQTileB = 2 * kQMaxNP * 128; // 16 KB: [x_hi; x_lo] slab of a K-step
+constexpr int kQBufs = 3;                  // superblock accumulators in TMEM
+constexpr int kQBufCols = 2 * kQMaxNP;
+constexpr int kQTotal = kQBufs * kQBufCols;  // TMEM columns of the tile's running sum (NP of them)
+constexpr uint32_t kQTmemCols = 512;
+constexpr int kQDeqWarps = 16;             // four threads per vocabulary row
+constexpr int kQEpiWarp0 = 2 + kQDeqWarps;  // four epilogue warps, then the raw-weight producer
+constexpr int kQRawWarp = kQEpiWarp0 + 4;
+constexpr int kQThreads = 32 * (kQRawWarp + 1);
+
+struct Q6P {
+  const uint8_t* w;
+  const uint8_t* w_end;
+  float* y;                 // [n][OUT]
+  uint32_t* status;
+  int N, OUT, n, NP, nsb, rowbytes, ntiles;
+  float softcap;
+  uint64_t wait_ns;
+};
+
+struct Q6Smem {
+  uint64_t a_full[kQSA], a_empty[kQSA], b_full[kQSB], b_empty[kQSB], acc_full[kQBufs], acc_empty[kQBufs], drain;
+  uint64_t r_full[kQSR], r_empty[kQSR];
+  uint32_t tmem_base;
+};
+
+// xs[r][k]: r < NP: f16(x[r][k]); NP <= r < 2 NP: f16(x[r-NP][k] - that); 0 for tokens >= n.
+__global__ void k_q6tc_prep(const float* __restrict__ x, uint16_t* __restrict__ xs, int n, int N, int NP) {
+  pdl_wait();
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)NP * N) return;
+  const int t = (int)(idx / N);
+  const size_t k = idx - (size_t)t * N;
+  uint16_t h = 0, l = 0;
+  if (t < n) {
+    const float v = x[(size_t)t * N + k];
+    const __half hh = __float2half_rn(v);
+    h = __half_as_ushort(hh);
+    l = f2h(v - __half2float(hh));
+  }
+  xs[(size_t)t * N + k] = h;
+  xs[(size_t)(NP + t) * N + k] = l;
+}
+
+// four 6-bit values (one per byte) -> f16 pairs (v0 - 32, v1 - 32), (v2 - 32, v3 - 32)
+E4B_DEV void q6_quad(uint32_t v, uint32_t& p01, uint32_t& p23) {
+  p01 = hsub2(__byte_perm(v, 0x64646464u, 0x5140u), 0x64206420u);
+  p23 = hsub2(__byte_perm(v, 0x64646464u, 0x5342u), 0x64206420u);
+}
+E4B_DEV uint32_t sc_pair(uint32_t scw, int byte) {
+  const int s = (int)(int8_t)((scw >> (8 * byte)) & 0xFFu);
+  const uint32_t h = __half_as_ushort(__int2half_rn(s));
+  return h | (h << 16);
+}
+
+// Tile-packed copy of a row-major q6_K matrix: dst superblock (t, sb, m) =
+// row 128 t + m's superblock sb, zero for rows >= OUT (one thread per 2 bytes).
+__global__ void k_q6_pack(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int OUT, int nsb,
+                          size_t total) {
+  pdl_wait();
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const size_t blk = i / 105;
+  const int hw = (int)(i - blk * 105);
+  const int m = (int)(blk % kQM);
+  const size_t ts = blk / kQM;
+  const int sb = (int)(ts % nsb);
+  const size_t t = ts / nsb;
+  const size_t row = t * kQM + m;
+  dst[i] = row < (size_t)OUT ? src[(row * nsb + sb) * 105 + hw] : (uint16_t)0;
+}
+
+// PACKED: w is the tile-packed copy (k_q6_pack): superblock sb of row 128 t + m
+// at byte ((t * nsb + sb) * 128 + m) * 210, so a raw stage is one contiguous
+// 26880-byte TMA bulk copy.  Otherwise w is row-major q6_K and the dequant
+// threads fetch their rows' 224-byte covers with cp.async.
+template <bool PACKED>
+__global__ void __launch_bounds__(kQThreads, 1) k_q6tc(const Q6P p, const __grid_constant__ CUtensorMap xmap) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ Q6Smem S;
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sA = base;                                            // [kQSA][hi 16 KB | -lo 16 KB]
+  uint8_t* sB = sA + (size_t)kQSA * 2 * kQTileA;                 // [kQSB][16 KB]
+  uint8_t* sR = sB + (size_t)kQSB * kQTileB;                     // [kQSR][128 rows][240 B]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kQSA; i++) {
+      mbar_init(&S.a_full[i], kQDeqWarps);
+      mbar_init(&S.a_empty[i], 1);
+    }
+    for (int i = 0; i < kQSB; i++) {
+      mbar_init(&S.b_full[i], 1);
+      mbar_init(&S.b_empty[i], 1);
+    }
+    for (int i = 0; i < kQBufs; i++) {
+      mbar_init(&S.acc_full[i], 1);
+      mbar_init(&S.acc_empty[i], kQM);
+    }
+    for (int i = 0; i < kQSR; i++) {
+      mbar_init(&S.r_full[i], 1);
+      mbar_init(&S.r_empty[i], kQDeqWarps);
+    }
+    mbar_init(&S.drain, 1);
+    fence_barrier_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+  }
+  if (warp == 1) tc_alloc(&S.tmem_base, kQTmemCols);
+  pdl_wait();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+  const int nk = 4 * p.nsb;
+
+  if (warp == 0) {
+    // ---------------- TMA producer: the token slab of every K-step
+    if (lane == 0) {
+      const uint32_t bbytes = (uint32_t)(2 * p.NP * 128);
+      uint32_t cb = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+        for (int s = 0; s < nk; s++, cb++) {
+          const int st = cb % kQSB;
+          ok = wait_bar(&S.b_empty[st], ((cb / kQSB) & 1u) ^ 1u, p.status, p.wait_ns);
+          if (!ok) break;
+          mbar_expect_tx(&S.b_full[st], bbytes);
+          tma_load_2d(sB + (size_t)st * kQTileB, &xmap, s * kQK, 0, &S.b_full[st]);
+        }
+      }
+      for (uint32_t k = 0; k < kQSB && k < cb; k++) {
+        const uint32_t c = cb - 1 - k;
+        drain_bar(&S.b_full[c % kQSB], (c / kQSB) & 1u, p.wait_ns);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_hi = idesc_m128((uint32_t)(2 * p.NP), false), id_lo = idesc_m128((uint32_t)p.NP, true);
+      uint32_t ca = 0, cb = 0, j = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+        for (int sb = 0; sb < p.nsb && ok; sb++, j++) {
+          const uint32_t buf = j % kQBufs;
+          ok = wait_bar(&S.acc_empty[buf], ((j / kQBufs) & 1u) ^ 1u, p.status, p.wait_ns);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem + buf * (uint32_t)kQBufCols;
+          for (int s = 0; s < 4; s++, ca++, cb++) {
+            const int sa = ca % kQSA, sbb = cb % kQSB;
+            ok = wait_bar(&S.a_full[sa], (ca / kQSA) & 1u, p.status, p.wait_ns) &&
+                 wait_bar(&S.b_full[sbb], (cb / kQSB) & 1u, p.status, p.wait_ns);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a_hi = smem_u32(sA + (size_t)sa * 2 * kQTileA), a_lo = a_hi + kQTileA;
+            const uint32_t b0 = smem_u32(sB + (size_t)sbb * kQTileB);
+#pragma unroll
+            for (int ks = 0; ks < kQK / 16; ks++) {
+              const uint64_t bd = sw128_desc(b0 + 32 * ks);
+              tc_mma(d_tmem, sw128_desc(a_hi + 32 * ks), bd, id_hi, (s | ks) != 0);
+              tc_mma(d_tmem, sw128_desc(a_lo + 32 * ks), bd, id_lo, 1u);
+            }
+            tc_commit(&S.a_empty[sa]);
+            tc_commit(&S.b_empty[sbb]);
+          }
+          if (ok) tc_commit(&S.acc_full[buf]);
+        }
+      }
+      // every MMA this thread issued has completed before TMEM is released
+      tc_commit(&S.drain);
+      drain_bar(&S.drain, 0, p.wait_ns);
+    }
+    __syncwarp();
+  } else if (warp < 2 + kQDeqWarps) {
+    // ---------------- dequant: threads 4m .. 4m+3 own vocabulary row m of each
+    // tile.  For K-step s = 2 h + odd (half h of the superblock) thread qq
+    // produces elements 16 qq .. 16 qq + 15 of the step (one sub-block):
+    // 6-bit values from ql[64 h + 16 qq + i] (low nibble for even steps, high
+    // for odd) and bits (2 (qq / 2) + 4 odd) of qh[32 h + 16 (qq % 2) + i],
+    // scale sc[8 h + 4 odd + qq].
+    const int dt = threadIdx.x - 64, m = dt >> 2, qq = dt & 3;
+    uint32_t ca = 0, cr = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+      const int row = t * kQM + m;
+      const bool valid = row < p.OUT;
+      const uint8_t* src = p.w + (size_t)(valid ? row : 0) * p.rowbytes;
+      auto fetch = [&](int sb) {              // row-major layout: this thread's chunks of the row's cover
+        if (!valid) return;
+        const uint8_t* a0 =
+            reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src + (size_t)sb * 210) & ~(uintptr_t)15);
+        uint8_t* dst = sR + ((size_t)(sb % kQSR) * kQM + m) * kQRawStride;
+        for (int i = qq; i < kQCover / 16; i += 4) {
+          const uint8_t* q = a0 + 16 * i;
+          const long long left = p.w_end - q;
+          if (left > 0) cp_async16z(dst + 16 * i, q, left >= 16 ? 16u : (uint32_t)left);
+        }
+      };
+      if constexpr (!PACKED) {                // raw superblocks two ahead of the one being decoded
+        fetch(0);
+        cp_async_commit_group();
+        if (p.nsb > 1) fetch(1);
+        cp_async_commit_group();
+      }
+      for (int sb = 0; sb < p.nsb && ok; sb++, cr++) {
+        int st, sh;
+        const uint8_t* slot;
+        if constexpr (PACKED) {
+          st = cr % kQSR;
+          ok = wait_bar(&S.r_full[st], (cr / kQSR) & 1u, p.status, p.wait_ns);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          sh = (m * 210) & 15;
+          slot = sR + (size_t)st * kQM * kQRawStride + ((m * 210) & ~15);
+        } else {
+          st = sb % kQSR;
+          __syncwarp();                       // the row's threads are done reading the stage about to be refilled
+          if (sb + 2 < p.nsb) fetch(sb + 2);
+          cp_async_commit_group();
+          cp_async_wait_group<2>();
+          __syncwarp();                       // the other threads' chunks of this stage are visible
+          sh = (int)(reinterpret_cast<uintptr_t>(src + (size_t)sb * 210) & 15);
+          slot = sR + ((size_t)st * kQM + m) * kQRawStride;
+        }
+        const uint32_t* rw = reinterpret_cast<const uint32_t*>(slot);   // sh is even
+        const uint32_t fs = (uint32_t)(sh & 2) * 8;
+        const int w0 = sh >> 2;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          uint32_t ql[4], qh[4], scw[2];
+          {
+            uint32_t a[5], b[5], c[3];
+            const int oq = w0 + 16 * h + 4 * qq, oh = w0 + 32 + 8 * h + 4 * (qq & 1), os = w0 + 48 + 2 * h;
+#pragma unroll
+            for (int i = 0; i < 5; i++) {
+              a[i] = rw[oq + i];
+              b[i] = rw[oh + i];
+            }
+#pragma unroll
+            for (int i = 0; i < 3; i++) c[i] = rw[os + i];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              ql[i] = __funnelshift_r(a[i], a[i + 1], fs);
+              qh[i] = __funnelshift_r(b[i], b[i + 1], fs);
+            }
+            scw[0] = __funnelshift_r(c[0], c[1], fs);
+            scw[1] = __funnelshift_r(c[1], c[2], fs);
+            if (!valid) scw[0] = scw[1] = 0u;    // rows past OUT: zero weights (never stored)
+          }
+          if (PACKED && h == 1) {                  // this warp's reads of the raw stage are done
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.r_empty[st]);
+          }
+#pragma unroll
+          for (int odd = 0; odd < 2; odd++) {
+            const int sa = ca % kQSA;
+            ok = wait_bar(&S.a_empty[sa], ((ca / kQSA) & 1u) ^ 1u, p.status, p.wait_ns);
+            ok = __all_sync(0xffffffffu, ok);  // the __syncwarp()s above need the whole warp on one path
+            if (!ok) break;
+            uint8_t* th = sA + (size_t)sa * 2 * kQTileA + (size_t)m * 128;
+            uint8_t* tl = th + kQTileA;
+            const uint32_t sc2 = sc_pair(scw[odd], qq), nsc2 = sc2 ^ 0x80008000u;
+            const int qhs = 2 * (qq >> 1) + 4 * odd;   // qh bits of this thread's elements
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+              uint32_t hi[4], nlo[4];
+#pragma unroll
+              for (int wq = 0; wq < 2; wq++) {
+                const uint32_t lo4 = (odd ? (ql[2 * c + wq] >> 4) : ql[2 * c + wq]) & 0x0F0F0F0Fu;
+                const uint32_t hb = ((qh[2 * c + wq] >> qhs) & 0x03030303u) << 4;
+                uint32_t p01, p23;
+                q6_quad(lo4 | hb, p01, p23);
+                hi[2 * wq] = hmul2(p01, sc2);
+                hi[2 * wq + 1] = hmul2(p23, sc2);
+                nlo[2 * wq] = hfma2(p01, nsc2, hi[2 * wq]);          // hi - m = -lo, exact
+                nlo[2 * wq + 1] = hfma2(p23, nsc2, hi[2 * wq + 1]);
+              }
+              const uint32_t off = (uint32_t)(((2 * qq + c) ^ (m & 7)) << 4);
+              *reinterpret_cast<uint4*>(th + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+              *reinterpret_cast<uint4*>(tl + off) = make_uint4(nlo[0], nlo[1], nlo[2], nlo[3]);
+            }
+            fence_proxy_async();              // generic-proxy writes -> the tensor core's reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.a_full[sa]);   // one arrival per warp
+            ca++;
+          }
+          if (!ok) break;
+        }
+      }
+    }
+    if constexpr (!PACKED) cp_async_wait_group<0>();
+  } else if (warp < kQRawWarp) {
+    // ---------------- epilogue: warp w reads TMEM lanes 32 (w % 4) .. ; the
+    // tile's running sum over superblocks lives in TMEM columns [kQTotal, + NP)
+    const int q = warp & 3, m = 32 * q + lane;
+    const int NP = p.NP;
+    const uint32_t lanes = (uint32_t)(32 * q) << 16, ttot = tmem + (uint32_t)kQTotal + lanes;
+    uint32_t j = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+      const int row = t * kQM + m;
+      const bool valid = row < p.OUT;
+      for (int sb = 0; sb < p.nsb; sb++, j++) {
+        const size_t doff = PACKED ? (((size_t)t * p.nsb + sb) * kQM + m) * 210 + 208
+                                   : (size_t)(valid ? row : 0) * p.rowbytes + (size_t)sb * 210 + 208;
+        const float d = valid ? h2f(*reinterpret_cast<const uint16_t*>(p.w + doff)) : 0.f;
+        const uint32_t buf = j % kQBufs;
+        ok = wait_bar(&S.acc_full[buf], (j / kQBufs) & 1u, p.status, p.wait_ns);
+        ok = __all_sync(0xffffffffu, ok);     // the warp-collective TMEM accesses below need every lane
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem + buf * (uint32_t)kQBufCols + lanes;
+        for (int cc = 0; 32 * cc < NP; cc++) {
+          uint32_t hi[32], lo[32];
+          tc_ld32_nowait(taddr + 32 * cc, hi);
+          tc_ld32_nowait(taddr + NP + 32 * cc, lo);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i++) hi[i] = __float_as_uint(d * (__uint_as_float(hi[i]) + __uint_as_float(lo[i])));
+          if (sb > 0) {
+            tc_ld32_nowait(ttot + 32 * cc, lo);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i++) hi[i] = __float_as_uint(__uint_as_float(hi[i]) + __uint_as_float(lo[i]));
+          }
+          tc_st32(ttot + 32 * cc, hi);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&S.acc_empty[buf]);
+      }
+      if (!ok) break;
+      // the whole warp reads its lanes' sums (tcgen05.ld is warp-collective);
+      // only rows inside the vocabulary are stored
+      for (int cc = 0; 32 * cc < NP; cc++) {
+        uint32_t v[32];
+        tc_ld32_nowait(ttot + 32 * cc, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const int tok = 32 * cc + i;
+          if (valid && tok < p.n) {
+            const float x = __uint_as_float(v[i]);
+            p.y[(size_t)tok * p.OUT + row] = p.softcap != 0.f ? p.softcap * tanhf(x / p.softcap) : x;
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- raw-weight producer (tile-packed layout): per superblock
+    // one 1-D TMA bulk copy of the tile's 128 x 210 contiguous bytes
+    if (PACKED && lane == 0) {
+      constexpr uint32_t kStage = (uint32_t)kQM * 210;
+      uint32_t cr = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+        for (int sb = 0; sb < p.nsb; sb++, cr++) {
+          const int st = cr % kQSR;
+          ok = wait_bar(&S.r_empty[st], ((cr / kQSR) & 1u) ^ 1u, p.status, p.wait_ns);
+          if (!ok) break;
+          mbar_expect_tx(&S.r_full[st], kStage);
+          bulk_g2s(sR + (size_t)st * kQM * kQRawStride, p.w + ((size_t)t * p.nsb + sb) * kStage, kStage,
+                   &S.r_full[st]);
+        }
+      }
+      // let copies still in flight land before the CTA ends (bounded)
+      for (uint32_t k = 0; k < kQSR && k < cr; k++) {
+        const uint32_t c = cr - 1 - k;
+        drain_bar(&S.r_full[c % kQSR], (c / kQSR) & 1u, p.wait_ns);
+      }
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tc_dealloc(tmem, kQTmemCols);
+  }
+}
+
+constexpr size_t kQSmemBytes =
+    1024 + (size_t)kQSA * 2 * kQTileA + (size_t)kQSB * kQTileB + (size_t)kQSR * kQM * kQRawStride;
+
+}  // namespace
+
+namespace e4b {
+
+bool q6tc_supported(const uint8_t* w, const void* scratch, int N, int OUT, int n) {
+  return n >= 1 && n <= kQMaxNP && N % 256 == 0 && OUT % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(scratch) % 16 == 0;
+}
+
+size_t q6_packed_bytes(int N, int OUT) { return (size_t)((OUT + kQM - 1) / kQM) * (N / 256) * kQM * 210; }
+
+// scratch: 2 * NP * N halves (NP = 32 for n <= 32, else 64).
+int q6tc_lmhead(e4b_ctx* c, const uint8_t* w, bool packed, const float* x, uint16_t* scratch, float* y, int N,
+                int OUT, float softcap, int n) {
+  const int NP = n <= 32 ? 32 : 64;
+  const size_t tot = (size_t)NP * N;
+  if (int r = e4b_launch(c, "q6tc_prep", k_q6tc_prep, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, x, scratch,
+                         n, N, NP))
+    return r;
+  auto enc = tensor_map_encoder();
+  if (!enc) return e4b_fail(c, E4B_ECUDA, "q6tc: cuTensorMapEncodeTiled unavailable");
+  CUtensorMap xmap;
+  const cuuint64_t dim[2] = {(cuuint64_t)N, (cuuint64_t)(2 * NP)};
+  const cuuint64_t stride[1] = {(cuuint64_t)N * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kQK, (cuuint32_t)(2 * NP)};
+  const cuuint32_t es[2] = {1, 1};
+  if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, scratch, dim, stride, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return e4b_fail(c, E4B_ECUDA, "q6tc: tensor map encode failed (N=%d)", N);
+  Q6P p;
+  p.w = w;
+  p.rowbytes = (N / 256) * 210;
+  p.w_end = w + (packed ? q6_packed_bytes(N, OUT) : (size_t)OUT * p.rowbytes);
+  p.y = y;
+  p.status = c->status;
+  p.N = N;
+  p.OUT = OUT;
+  p.n = n;
+  p.NP = NP;
+  p.nsb = N / 256;
+  p.ntiles = (OUT + kQM - 1) / kQM;
+  p.softcap = softcap;
+  p.wait_ns = c->wait_ns;
+  auto launch = [&](auto kern) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kQSmemBytes);
+    if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q6tc smem attr: %s", cudaGetErrorString(e));
+    const int grid = p.ntiles < c->sm_count ? p.ntiles : c->sm_count;
+    return e4b_launch(c, "q6tc", kern, dim3((unsigned)grid), dim3(kQThreads), kQSmemBytes, p, xmap);
+  };
+  return packed ? launch(k_q6tc<true>) : launch(k_q6tc<false>);
+}
+
+int q6_pack(e4b_ctx* c, const uint8_t* w, uint8_t* wt, int N, int OUT) {
+  const size_t total = q6_packed_bytes(N, OUT) / 2;
+  return e4b_launch(c, "q6_pack", k_q6_pack, dim3((unsigned)((total + 255) / 256)), dim3(256), 0,
+                    reinterpret_cast<const uint16_t*>(w), reinterpret_cast<uint16_t*>(wt), OUT, N / 256, total);
+}
+
+}  // namespace e4b
+
+extern "C" {
+
+E4B_API size_t e4b_q6k_packed_bytes(int N, int OUT) {
+  return N > 0 && N % 256 == 0 && OUT > 0 ? e4b::q6_packed_bytes(N, OUT) : 0;
+}
+
+E4B_API int e4b_q6k_pack_tiles(e4b_ctx* c, const uint8_t* w, uint8_t* wt, int N, int OUT) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, w && wt && N > 0 && N % 256 == 0 && OUT > 0, "q6k_pack_tiles: bad args (N=%d OUT=%d)", N, OUT);
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 2 == 0 && reinterpret_cast<uintptr_t>(wt) % 16 == 0,
+              "q6k_pack_tiles: w must be 2-byte and wt 16-byte aligned");
+  return e4b::q6_pack(c, w, wt, N, OUT);
+}
+
+E4B_API int e4b_q6k_lmhead_tiles(e4b_ctx* c, const uint8_t* wt, const float* x, uint16_t* scratch, float* y, int N,
+                                 int OUT, float softcap, int n) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, wt && x && scratch && y && N > 0 && N % 256 == 0 && OUT > 0, "q6k_lmhead_tiles: bad args");
+  E4B_REQUIRE(c, n >= 1 && n <= kQMaxNP, "q6k_lmhead_tiles: n=%d must be 1..%d", n, kQMaxNP);
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(wt) % 16 == 0 && reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
+              "q6k_lmhead_tiles: wt and scratch must be 16-byte aligned");
+  return e4b::q6tc_lmhead(c, wt, true, x, scratch, y, N, OUT, softcap, n);
+}
+
+}  // extern "C"

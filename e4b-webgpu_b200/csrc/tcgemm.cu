@@ -24,7 +24,7 @@
 // reference's own q40sg vs q40mv).  lo is stored negated (the FMA gives
 // hi - d*(n-8)) and the second MMA negates A in its instruction descriptor.
 #include "q40_stream.cuh"
-#include "stream.cuh"
+#include "tc.cuh"
 
 namespace {
 using namespace e4b;
@@ -63,84 +63,10 @@ struct Smem {
   int row_end[kMaxGroups];
 };
 
-// ---------------------------------------------------------------- PTX helpers
-E4B_DEV bool aborted(const uint32_t* status) {
-  uint32_t v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(status) : "memory");
-  return (v & E4B_ST_TIMEOUT) != 0;
-}
-// Bounded mbarrier wait; false after limit_ns (recording E4B_ST_TIMEOUT) or once
-// any CTA has recorded a time-out.
-E4B_DEV bool wait_bar(uint64_t* b, uint32_t parity, uint32_t* status, uint64_t limit_ns) {
-  if (mbar_try_wait(b, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 0;; i++) {
-    if (mbar_try_wait(b, parity)) return true;
-    if ((i & 63u) == 63u) {
-      if (aborted(status)) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
-        set_status(status, E4B_ST_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-E4B_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
-}
-E4B_DEV void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-E4B_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-E4B_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-E4B_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-E4B_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-E4B_DEV void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-E4B_DEV void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// 32 consecutive accumulator columns of this thread's TMEM lane.
-E4B_DEV void tc_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle
-// layout (8-row x 128-byte atoms, 1024 bytes apart), version 1 (sm_100).
-E4B_DEV uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N <= 256,
-// optionally negating A.
-// N = the tile's token rows rounded up to 16 (a group's last tile is usually
-// partial: its MMAs shrink with it).
+// Instruction descriptor for a tile: N = the tile's token rows rounded up to
+// 16 (a group's last tile is usually partial: its MMAs shrink with it).
 E4B_DEV uint32_t idesc_for(int nrows, bool neg_a) {
-  const uint32_t n = (uint32_t)min(kTN, max(16, (nrows + 15) & ~15));
-  return (1u << 4) | ((n >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24) | (neg_a ? (1u << 13) : 0u);
+  return idesc_m128((uint32_t)min(kTN, max(16, (nrows + 15) & ~15)), neg_a);
 }
 
 // ---------------------------------------------------------------- tiles
@@ -167,11 +93,6 @@ E4B_DEV Tile tile_of(const Smem& S, const GemmP& p, int t) {
 }
 
 // ---------------------------------------------------------------- dequant
-E4B_DEV uint32_t hmul2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
 // f16 pairs (n_a - 8, n_b - 8) from two nibble bytes, via 0x6400 | n = 1024 + n.
 E4B_DEV uint32_t nib_pair(uint32_t nibbles, uint32_t sel) {
   return hsub2(__byte_perm(nibbles, 0x64u, sel), 0x64086408u);
@@ -358,16 +279,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
         for (int i = hh; i < 10 && a0 + 16 * i < a1; i += 2) {
           const uint8_t* q = a0 + 16 * i;
           const long long left = p.w_end - q;
-          cp_async16(dst + 16 * i, q, left >= 16 ? 16u : (uint32_t)left);
+          cp_async16z(dst + 16 * i, q, left >= 16 ? 16u : (uint32_t)left);
         }
       };
       fetch(0);
-      cp_async_commit();
+      cp_async_commit_group();
       for (int r = 0; r < nraw && ok; r++) {
         __syncwarp();                       // the pair is done reading the buffer about to be refilled
         if (r + 1 < nraw) fetch(r + 1);
-        cp_async_commit();
-        cp_async_wait<1>();
+        cp_async_commit_group();
+        cp_async_wait_group<1>();
         __syncwarp();                       // the partner's chunks of stage r are visible
         uint32_t wd[36];
         {
@@ -435,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
         }
       }
     }
-    cp_async_wait<0>();
+    cp_async_wait_group<0>();
   } else {
     // ---------------- epilogue: warp w reads TMEM lanes 32 (w % 4) ..
     const int q = warp & 3, m = 32 * q + lane;
@@ -445,6 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tcgemm(const GemmP p, const __g
       const Tile T = tile_of(S, p, t);
       const uint32_t buf = lt & 1u;
       ok = wait_bar(&S.acc_full[buf], (lt >> 1) & 1u, p.status, p.wait_ns);
+      ok = __all_sync(0xffffffffu, ok);     // the warp-collective TMEM loads below need every lane
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem + buf * (uint32_t)kTN + ((uint32_t)(32 * q) << 16);

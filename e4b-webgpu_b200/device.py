@@ -51,7 +51,8 @@ def _ptr(x):
 
 class Device:
     # C-ABI functions that enqueue kernels, with the number of kernels each launches
-    KERNELS = {"e4b_argmax": 2, "e4b_argmax_static": 2, "e4b_argmax_rows": 2, "e4b_q6k_lmhead_rows": 2, "e4b_attdec_seq": 2}
+    KERNELS = {"e4b_argmax": 2, "e4b_argmax_static": 2, "e4b_argmax_rows": 2, "e4b_q6k_lmhead_rows": 2,
+               "e4b_q6k_lmhead_tiles": 2, "e4b_attdec_seq": 2}
 
     def __init__(self, device: int = 0):
         self.kernel_launches = 0

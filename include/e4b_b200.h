@@ -84,6 +84,8 @@ E4B_API size_t e4b_workspace_bytes(void);
  * blocks per staged piece: 0 = 8 x 32, 1 = 16 x 16, 2 = 16 x 8).
  * "attn_grid_cap" (>= 0, default 0 = one CTA per SM): at most this many CTAs for
  * e4b_attdec_seq, so each CTA runs more items (the stage ring's wrap-around).
+ * "lmhead_tc_min" (1..65, default 1): e4b_q6k_lmhead_rows uses its tcgen05
+ * kernel for n >= this many rows (65: never).
  * "wait_limit_us" (1000..10000000, default 1000000): the bound of the batched
  * attention's and e4b_ep_wait's device waits, after which the call records
  * E4B_ST_TIMEOUT in the status word and returns. */
@@ -381,10 +383,24 @@ E4B_API int e4b_geglub(e4b_ctx* ctx, const float* gu, uint16_t* yh, int N, int r
  * pleIn[b*PD+i] = (rms(proj_b*proj_scale)[i]*normW[i] + row_b[i]*mult) * sqrt(1/2),
  * row = q6_K row tok[0] (toksrc=1) or params[2] of the [LAYERS*PD]-wide table. */
 /* LM head for n token rows (batched decode): y[n][OUT] = softcap(W x[n][N]) on the
- * tensor cores, x used as f16 hi + lo; scratch: 2*N*ceil8(n) u16, 16-byte aligned
- * (the split activations, laid out as MMA fragments). */
+ * tensor cores, x used as f16 hi + lo; scratch: 2*N*max(64, ceil8(n)) u16, 16-byte
+ * aligned (the split activations).  For n <= 64 (and n >= the "lmhead_tc_min"
+ * option) and OUT % 8 == 0 the tcgen05 kernel runs, else the mma.sync ones.
+ * kernels/q6k.wgsl:75-127 per row. */
 E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* ctx, const uint8_t* w, const float* x, uint16_t* scratch, float* y, int N,
                                 int OUT, float softcap, int n);
+/* Tile-packed copy of a row-major q6_K matrix for e4b_q6k_lmhead_tiles: for
+ * tile t = row / 128, superblock sb, row m = row % 128 the 210-byte superblock
+ * sits at ((t * N/256 + sb) * 128 + m) * 210; rows past OUT are zero.  Size:
+ * e4b_q6k_packed_bytes(N, OUT) = ceil(OUT/128) * N/256 * 26880.  Same bytes as
+ * the reference's q6_K table (kernels/q6k.wgsl), reordered so that each
+ * (tile, superblock) is one contiguous TMA bulk copy. */
+E4B_API size_t e4b_q6k_packed_bytes(int N, int OUT);
+E4B_API int e4b_q6k_pack_tiles(e4b_ctx* ctx, const uint8_t* w, uint8_t* wt, int N, int OUT);
+/* e4b_q6k_lmhead_rows on the tile-packed copy (1 <= n <= 64): the tcgen05 kernel
+ * with the weights streamed by TMA; scratch: 2*N*64 u16, 16-byte aligned. */
+E4B_API int e4b_q6k_lmhead_tiles(e4b_ctx* ctx, const uint8_t* wt, const float* x, uint16_t* scratch, float* y, int N,
+                                 int OUT, float softcap, int n);
 E4B_API int e4b_pleprep(e4b_ctx* ctx, const uint8_t* table, const uint32_t* params, const uint32_t* tok,
                         const float* proj, const float* norm_w, float* ple_in, int PD, int LAYERS, int rows,
                         float mult, float proj_scale, float eps, int toksrc);

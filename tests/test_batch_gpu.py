@@ -35,19 +35,67 @@ def test_batched_moe_decode_matches_oracle(e4b, models, B):
             assert np.linalg.norm(h[b] - href) / np.linalg.norm(href) < 1e-2
 
 
+def _pack_tiles_ref(w, V, N):
+    """numpy restatement of the tile-packed layout: superblock sb of row 128 t + m at
+    ((t * nsb + sb) * 128 + m) * 210, zero rows past V."""
+    nsb, T = N // 256, (V + 127) // 128
+    blocks = np.zeros((T * 128, nsb, 210), np.uint8)
+    blocks[:V] = np.frombuffer(bytes(w), np.uint8).reshape(V, nsb, 210)
+    return blocks.reshape(T, 128, nsb, 210).transpose(0, 2, 1, 3).reshape(-1)
+
+
+@pytest.mark.parametrize("V,N,n", [(3000, 512, 11), (1000, 768, 64), (1000, 768, 1), (40000, 1024, 64),
+                                   (40000, 512, 33), (4096, 2816, 64)])
+def test_lmhead_tiles(e4b, dev, V, N, n):
+    """e4b_q6k_pack_tiles lays the bytes out as the numpy restatement says, and
+    e4b_q6k_lmhead_tiles on the packed copy matches the oracle q6_K matvec per row
+    and the row-major e4b_q6k_lmhead_rows to the last bit of either (same
+    per-superblock accumulation order)."""
+    from oracle import ops as O
+    w = e4b.synth.quant_q6_K(e4b.synth.normal_f32(V * N, 43 + V, "lmtiles", 0.02))
+    nbytes = int(dev.L.e4b_q6k_packed_bytes(N, V))
+    assert nbytes == (V + 127) // 128 * (N // 256) * 128 * 210
+    bw, wt = dev.upload(w), dev.alloc(nbytes)
+    dev.call("e4b_q6k_pack_tiles", bw.ptr, wt.ptr, N, V)
+    dev.sync()
+    assert np.array_equal(dev.read(wt, np.uint8, nbytes), _pack_tiles_ref(w, V, N))
+    x = np.random.default_rng(44).standard_normal((n, N)).astype(np.float32)
+    bx, y, y2, scr = dev.upload(x), dev.alloc(n * V * 4), dev.alloc(n * V * 4), dev.alloc(2 * 64 * N * 2)
+    dev.call("e4b_q6k_lmhead_tiles", wt.ptr, bx.ptr, scr.ptr, y.ptr, N, V, np.float32(30.0), n)
+    dev.call("e4b_q6k_lmhead_rows", bw.ptr, bx.ptr, scr.ptr, y2.ptr, N, V, np.float32(30.0), n)
+    dev.sync()
+    assert dev.status() == 0
+    got = dev.read(y, np.float32, n * V).reshape(n, V)
+    assert np.array_equal(got, dev.read(y2, np.float32, n * V).reshape(n, V))
+    for r in range(n):
+        ref = O.softcap(O.q6k_matvec(w, x[r], V, N), 30.0)
+        assert np.max(np.abs(got[r] - ref)) / np.max(np.abs(ref)) < 2e-5
+
+
+@pytest.mark.parametrize("tc", [1, 65])
 @pytest.mark.parametrize("V,N,n", [(3000, 512, 11), (1000, 768, 64), (520, 256, 70), (4, 256, 1), (1000, 768, 1),
-                                   (520, 256, 30)])
-def test_batched_lmhead_rows(e4b, dev, V, N, n):
-    """e4b_q6k_lmhead_rows (tensor cores, x as f16 hi + lo) against the oracle q6_K matvec per row;
-    V % 8 == 0 takes the staged kernel, other V the direct one."""
+                                   (520, 256, 30), (40000, 1024, 64), (40000, 512, 33)])
+def test_batched_lmhead_rows(e4b, dev, V, N, n, tc):
+    """e4b_q6k_lmhead_rows against the oracle q6_K matvec per row.  With
+    lmhead_tc_min = 1, n <= 64 and V % 8 == 0 take the tcgen05 kernel (weights
+    split exactly into f16 hi + lo, x as f16 hi + lo); with 65 (and for n > 64)
+    the mma.sync kernels: V % 8 == 0 the staged one, other V the direct one.
+    V = 40000 spans more 128-row tiles than a B200 has SMs (the persistent
+    grid's second round); the synthetic scales reach +-127, so ~2 % of the
+    weights have a non-zero lo part."""
     from oracle import ops as O
     w = e4b.synth.quant_q6_K(e4b.synth.normal_f32(V * N, 41 + V, "lmrows", 0.02))
     x = np.random.default_rng(42).standard_normal((n, N)).astype(np.float32)
     y = dev.alloc(n * V * 4)
-    scr = dev.alloc(2 * ((n + 7) // 8 * 8) * N * 2)
-    dev.call("e4b_q6k_lmhead_rows", dev.upload(w).ptr, dev.upload(x).ptr, scr.ptr, y.ptr, N, V,
-             np.float32(30.0), n)
-    dev.sync()
+    scr = dev.alloc(2 * max(64, (n + 7) // 8 * 8) * N * 2)
+    dev.call("e4b_set_option", b"lmhead_tc_min", tc)
+    try:
+        dev.call("e4b_q6k_lmhead_rows", dev.upload(w).ptr, dev.upload(x).ptr, scr.ptr, y.ptr, N, V,
+                 np.float32(30.0), n)
+        dev.sync()
+    finally:
+        dev.call("e4b_set_option", b"lmhead_tc_min", 1)
+    assert dev.status() == 0
     got = dev.read(y, np.float32, n * V).reshape(n, V)
     for r in range(n):
         ref = O.softcap(O.q6k_matvec(w, x[r], V, N), 30.0)
