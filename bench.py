@@ -288,6 +288,7 @@ def run_moe_batch(args, rank, world, local_rank):
         ep = (world, rank, dist.bcast_bytes(nid))
     transport = args.ep_transport if world > 1 else "nccl"
     eng = e4b.BatchEngine(img, nloc, local_rank, ep=ep, zipf=zipf, tok0=rank * nloc, ep_overlap=bool(args.ep_overlap),
+                          overlap_route=bool(args.overlap_route),
                           ep_transport=transport)
     dev = eng.dev
     prompts = np.stack([e4b.synth.prompt_ids(args.prefill, cfg.vocab, seed=1000 + b)
@@ -955,6 +956,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling cases)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences decoded in lockstep (default 1 on 1 GPU, 64 -- expert parallel -- on N > 1)")
+    ap.add_argument("--overlap-route", type=int, default=1,
+                    help="one GPU: each layer's routing chain on a side stream beside the dense FFN (1) or in line (0)")
     ap.add_argument("--ep-overlap", type=int, default=1,
                     help="expert parallel: exchange the rows on a side stream beside the dense FFN (1) or in line (0)")
     ap.add_argument("--ep-transport", choices=["nccl", "p2p"], default="nccl",

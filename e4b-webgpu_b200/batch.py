@@ -81,7 +81,8 @@ def from_xfo(x: np.ndarray) -> np.ndarray:
 
 class BatchEngine(Engine):
     def __init__(self, src, nseq: int, device=0, *, chunk: int = 64, ep=None, zipf: float | None = None,
-                 tok0: int = 0, route_seed: int = 1234, ep_overlap: bool = True, ep_transport: str = "nccl"):
+                 tok0: int = 0, route_seed: int = 1234, ep_overlap: bool = True, ep_transport: str = "nccl",
+                 overlap_route: bool = True):
         """nseq sequences decoded in lockstep on this GPU.  ep = (nranks, rank,
         nccl_id): expert parallelism -- this rank decodes its nseq sequences and
         owns experts [rank*E/nranks, (rank+1)*E/nranks); every rank of the
@@ -92,7 +93,9 @@ class BatchEngine(Engine):
         sequence, so any rank count routes identically.  ep_transport: "nccl"
         (grouped send/recv of the slabs) or "p2p" (rows and results stored
         straight into the peers' slabs through CUDA IPC mappings, device-side
-        epoch flags; 2 or more ranks, one process per GPU)."""
+        epoch flags; 2 or more ranks, one process per GPU).  overlap_route (one
+        GPU): each layer's routing chain (router, Zipf draw, expert sort) runs
+        on a side stream concurrently with the dense FFN."""
         if ep_transport not in ("nccl", "p2p"):
             raise ValueError(f"ep_transport {ep_transport!r}: 'nccl' or 'p2p'")
         self.ep_transport = ep_transport
@@ -100,6 +103,7 @@ class BatchEngine(Engine):
         self.nseq = int(nseq)
         self.zipf, self.tok0, self.route_seed = zipf, int(tok0), int(route_seed)
         self.ep_overlap = bool(ep_overlap)     # row exchange on a side stream beside the dense FFN
+        self.overlap_route = bool(overlap_route)   # routing chain on a side stream beside the dense FFN
         self.ep = None
         if ep is not None:
             nranks, rank, nid = ep
@@ -163,6 +167,14 @@ class BatchEngine(Engine):
         # contiguous TMA copy per 128 rows x superblock (e4b_q6k_lmhead_tiles)
         self.emb_tiles = self._pack_lm_head(self.emb, c.vocab) if B <= 64 else None
         self.emb_shard_tiles = None
+        self.zipf_all = bool(self.zipf) and self.ep is None
+        if self.zipf_all:
+            # benchmark routing of every layer drawn in one launch per step from a
+            # popularity table built once
+            A.zipf_table = d.alloc(2 * E * 4, "zipfTable")
+            d.call("e4b_zipf_table", A.zipf_table, E, ctypes.c_float(self.zipf), ctypes.c_uint32(self.route_seed))
+            A.ztop_idx = d.alloc(c.layers * B * K * 4, "zipfTopkAll")
+            A.ztop_w = d.alloc(c.layers * B * K * 4, "zipfWAll")
         if self.ep is not None:
             self._alloc_ep(A)
         self.A = A
@@ -370,8 +382,15 @@ class BatchEngine(Engine):
         d.call("e4b_q6k_embed", self.emb, A.params, A.tok, A.hidden, H, V, ctypes.c_float(F32(math.sqrt(H))), 1, B)
         d.call("e4b_rmsnorm", A.hidden, self.layers[0].attn_norm, None, None, A.normed, H, B, ctypes.c_float(c.eps),
                1, 0, 2)
+        if self.zipf_all:
+            d.call("e4b_route_zipf_layers", A.params, A.zipf_table, A.ztop_idx, A.ztop_w, B, c.layers, K, E,
+                   ctypes.c_uint32(self.route_seed), 0, self.tok0)
         for L in self.layers:
             nxt = self.layers[L.i + 1].attn_norm if L.i + 1 < c.layers else None
+            topk_idx, topk_w = A.topk_idx, A.topk_w
+            if self.zipf_all:
+                topk_idx = ctypes.c_void_p(A.ztop_idx.ptr + L.i * B * K * 4)
+                topk_w = ctypes.c_void_p(A.ztop_w.ptr + L.i * B * K * 4)
             if self.kp_qkv > 1:
                 d.call("e4b_q40mm_kparts", A.normed, L.qkv, A.qkv, H, L.qkv_rows, B, self.kp_qkv)
             else:
@@ -388,16 +407,27 @@ class BatchEngine(Engine):
                 d.call("e4b_q40mm", A.attn, L.o, A.oparts, c.q_dim, H, B)
             d.call("e4b_rmsacc3", A.oparts, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
                    A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B, 1, self.kp_o)
+            side = self.ep is None and self.overlap_route
+            if side:
+                # the routing chain (router, Zipf draw, expert sort) on the side stream,
+                # concurrent with the dense FFN on the main stream
+                d.call("e4b_side_begin")
             d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
-            if self.zipf:
+            if self.zipf and not self.zipf_all:
                 d.call("e4b_route_zipf", A.params, A.topk_idx, A.topk_w, B, K, E, ctypes.c_float(self.zipf),
                        ctypes.c_uint32(self.route_seed), L.i, self.tok0)
             if self.ep is not None and self.ep_overlap:
                 self._moe_ep_send()           # the rows travel while the dense FFN runs
+            if side:
+                d.call("e4b_expgroup", topk_idx, B, K, E, A.offsets, A.entries, A.inv)
+                d.call("e4b_side_end")
             d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
             d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
             if self.ep is None:
-                d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
+                if side:
+                    d.call("e4b_join")
+                else:
+                    d.call("e4b_expgroup", topk_idx, B, K, E, A.offsets, A.entries, A.inv)
                 d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
                 d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
                 y_rows, y_map = A.yo, A.inv
@@ -405,7 +435,7 @@ class BatchEngine(Engine):
                 if not self.ep_overlap:
                     self._moe_ep_send()
                 y_rows, y_map = self._moe_ep_finish(L)
-            d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, y_rows, y_map, A.topk_w, K, L.post_ffw2, L.post_ffw,
+            d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, y_rows, y_map, topk_w, K, L.post_ffw2, L.post_ffw,
                    A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
                    ctypes.c_float(L.scale), int(nxt is not None), B, 1)
         d.call("e4b_rmsnorm", A.hidden, self.out_norm, A.xf, None, None, H, B, ctypes.c_float(c.eps), 1, 0, 0)

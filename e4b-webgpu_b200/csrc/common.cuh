@@ -29,6 +29,10 @@ struct e4b_ctx {
   int attn_grid_cap = 0;            // batched attention: at most this many CTAs (0 = one per SM)
   uint64_t wait_ns = 1000000000ull; // bound of the batched attention's and ep_wait's device waits
   int lmhead_tc_min = 1;             // batched LM head: tcgen05 kernel for n >= this (<= 64)
+  cudaStream_t main_stream = nullptr;  // e4b_side_begin .. e4b_side_end: launches go to `side`
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  bool forked = false, side_pending = false;
   cudaEvent_t ev[64] = {};
   std::vector<cudaGraphExec_t> plans;
   cudaGraph_t cap_graph = nullptr;

@@ -160,19 +160,12 @@ E4B_DEV uint32_t mix32(uint32_t x) {
   x ^= x >> 16;
   return x;
 }
-// Benchmark routing.  Per CTA: the Zipf(s) popularity table (cumulative, by a
-// fixed-order inclusive scan) and a seeded permutation saying which experts are
-// popular; then one warp per token: the token draws from its own hash stream,
-// 32 attempts at a time across the lanes, and keeps the first K distinct
-// experts in attempt order (exactly what drawing one attempt after another
-// would keep).
-__global__ void __launch_bounds__(256) k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __restrict__ topk_idx,
-                                                    float* __restrict__ topk_w, int n_tok, int K, int E, float s,
-                                                    uint32_t seed, int salt, int tok0, int nseq) {
-  pdl_wait();
-  extern __shared__ float cdf[];          // [E] cumulative popularity, then [E] rank -> expert (as bits)
-  uint32_t* perm = reinterpret_cast<uint32_t*>(cdf + E);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+// Benchmark routing.  The Zipf(s) popularity table: cumulative popularity of
+// each rank (a fixed-order inclusive scan, normalised) and a seeded
+// permutation saying which experts are popular, built by one CTA into shared
+// memory.  It depends on (s, seed, E) only, so an engine builds it once
+// (k_zipf_table) and the per-step routing reloads it.
+E4B_DEV void zipf_table_build(float* cdf, uint32_t* perm, int E, float s, uint32_t seed) {
   for (int r = threadIdx.x; r < E; r += blockDim.x) {
     cdf[r] = powf((float)(r + 1), -s);
     perm[r] = (uint32_t)r;
@@ -198,44 +191,93 @@ __global__ void __launch_bounds__(256) k_route_zipf(const uint32_t* __restrict__
       perm[j] = t;
     }
   __syncthreads();
-  for (int i = blockIdx.x * nw + warp; i < n_tok; i += gridDim.x * nw) {
-    // row i: sequence tok0 + i % nseq at position params[0] + i / nseq
-    const uint32_t pos = params[0] + (uint32_t)(i / nseq);
-    const uint32_t tk = (uint32_t)(tok0 + i % nseq);
-    uint32_t chosen = 0xffffffffu;        // lane k < K holds the k-th expert kept
-    int got = 0;
-    for (uint32_t a0 = 0; got < K && a0 < 4096u; a0 += 32) {
-      const uint32_t attempt = a0 + (uint32_t)lane;
-      const uint32_t h = mix32(seed ^ mix32((uint32_t)salt * 0x85ebca6bu ^ mix32(pos ^ mix32(tk ^ (attempt << 20)))));
-      const float u = (float)(h >> 8) * (1.0f / 16777216.0f);
-      int lo = 0, hi = E - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (cdf[mid] > u) hi = mid;
-        else lo = mid + 1;
-      }
-      const uint32_t e = perm[lo];
-      for (int j = 0; j < 32 && got < K; j++) {      // attempts in order
-        const uint32_t ej = __shfl_sync(0xffffffffu, e, j);
-        const bool dup = __any_sync(0xffffffffu, lane < got && chosen == ej);
-        if (!dup) {
-          if (lane == got) chosen = ej;
-          got++;
-        }
-      }
+}
+// One warp routes one token: the token draws from its own hash stream, 32
+// attempts at a time across the lanes, and keeps the first K distinct experts
+// in attempt order (exactly what drawing one attempt after another would keep).
+E4B_DEV void zipf_route_token(const float* cdf, const uint32_t* perm, int E, int K, uint32_t seed, int salt,
+                              uint32_t pos, uint32_t tk, uint32_t* idx_out, float* w_out, int lane) {
+  uint32_t chosen = 0xffffffffu;        // lane k < K holds the k-th expert kept
+  int got = 0;
+  for (uint32_t a0 = 0; got < K && a0 < 4096u; a0 += 32) {
+    const uint32_t attempt = a0 + (uint32_t)lane;
+    const uint32_t h = mix32(seed ^ mix32((uint32_t)salt * 0x85ebca6bu ^ mix32(pos ^ mix32(tk ^ (attempt << 20)))));
+    const float u = (float)(h >> 8) * (1.0f / 16777216.0f);
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (cdf[mid] > u) hi = mid;
+      else lo = mid + 1;
     }
-    for (int r = 0; got < K && r < E; r++) {   // (never needed in practice) fill by popularity
-      const uint32_t e = perm[r];
-      const bool dup = __any_sync(0xffffffffu, lane < got && chosen == e);
+    const uint32_t e = perm[lo];
+    for (int j = 0; j < 32 && got < K; j++) {      // attempts in order
+      const uint32_t ej = __shfl_sync(0xffffffffu, e, j);
+      const bool dup = __any_sync(0xffffffffu, lane < got && chosen == ej);
       if (!dup) {
-        if (lane == got) chosen = e;
+        if (lane == got) chosen = ej;
         got++;
       }
     }
-    if (lane < K) {
-      topk_idx[(size_t)i * K + lane] = chosen;
-      topk_w[(size_t)i * K + lane] = 1.0f / (float)K;
+  }
+  for (int r = 0; got < K && r < E; r++) {   // (never needed in practice) fill by popularity
+    const uint32_t e = perm[r];
+    const bool dup = __any_sync(0xffffffffu, lane < got && chosen == e);
+    if (!dup) {
+      if (lane == got) chosen = e;
+      got++;
     }
+  }
+  if (lane < K) {
+    idx_out[lane] = chosen;
+    w_out[lane] = 1.0f / (float)K;
+  }
+}
+
+// Per CTA: the table, then one warp per row i (sequence tok0 + i % nseq at
+// position params[0] + i / nseq).
+__global__ void __launch_bounds__(256) k_route_zipf(const uint32_t* __restrict__ params, uint32_t* __restrict__ topk_idx,
+                                                    float* __restrict__ topk_w, int n_tok, int K, int E, float s,
+                                                    uint32_t seed, int salt, int tok0, int nseq) {
+  pdl_wait();
+  extern __shared__ float cdf[];          // [E] cumulative popularity, then [E] rank -> expert (as bits)
+  uint32_t* perm = reinterpret_cast<uint32_t*>(cdf + E);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  zipf_table_build(cdf, perm, E, s, seed);
+  for (int i = blockIdx.x * nw + warp; i < n_tok; i += gridDim.x * nw) {
+    const uint32_t pos = params[0] + (uint32_t)(i / nseq);
+    const uint32_t tk = (uint32_t)(tok0 + i % nseq);
+    zipf_route_token(cdf, perm, E, K, seed, salt, pos, tk, topk_idx + (size_t)i * K, topk_w + (size_t)i * K, lane);
+  }
+}
+
+// The table into global memory: [E] cdf, then [E] permutation.
+__global__ void __launch_bounds__(256) k_zipf_table(float* __restrict__ table, int E, float s, uint32_t seed) {
+  pdl_wait();
+  extern __shared__ float cdf[];
+  uint32_t* perm = reinterpret_cast<uint32_t*>(cdf + E);
+  zipf_table_build(cdf, perm, E, s, seed);
+  for (int r = threadIdx.x; r < 2 * E; r += blockDim.x) table[r] = cdf[r];
+}
+
+// Every layer of one decode step at once: row (layer l, token i) of
+// n_layers x n_tok, layer salt salt0 + l, sequence tok0 + i at position
+// params[0]; outputs [n_layers][n_tok][K].  The table comes from k_zipf_table.
+__global__ void __launch_bounds__(256) k_route_zipf_layers(const uint32_t* __restrict__ params,
+                                                           const float* __restrict__ table,
+                                                           uint32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                                                           int n_tok, int n_layers, int K, int E, uint32_t seed,
+                                                           int salt0, int tok0) {
+  pdl_wait();
+  extern __shared__ float cdf[];
+  uint32_t* perm = reinterpret_cast<uint32_t*>(cdf + E);
+  for (int r = threadIdx.x; r < 2 * E; r += blockDim.x) cdf[r] = table[r];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const uint32_t pos = params[0];
+  for (int i = blockIdx.x * nw + warp; i < n_tok * n_layers; i += gridDim.x * nw) {
+    const int l = i / n_tok, t = i - l * n_tok;
+    zipf_route_token(cdf, perm, E, K, seed, salt0 + l, pos, (uint32_t)(tok0 + t), topk_idx + (size_t)i * K,
+                     topk_w + (size_t)i * K, lane);
   }
 }
 
@@ -389,6 +431,24 @@ E4B_API int e4b_route_zipf(e4b_ctx* c, const uint32_t* params, uint32_t* topk_id
               "route_zipf: bad args");
   return e4b_launch(c, "route_zipf", k_route_zipf, dim3((n_tok + 7) / 8), dim3(256), (size_t)E * 8, params, topk_idx,
                     topk_w, n_tok, K, E, s, seed, salt, tok0, n_tok);
+}
+
+E4B_API int e4b_zipf_table(e4b_ctx* c, float* table, int E, float s, uint32_t seed) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, table && E > 0 && E <= 4096 && s > 0.f, "zipf_table: bad args");
+  return e4b_launch(c, "zipf_table", k_zipf_table, dim3(1), dim3(256), (size_t)E * 8, table, E, s, seed);
+}
+
+E4B_API int e4b_route_zipf_layers(e4b_ctx* c, const uint32_t* params, const float* table, uint32_t* topk_idx,
+                                  float* topk_w, int n_tok, int n_layers, int K, int E, uint32_t seed, int salt0,
+                                  int tok0) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, params && table && topk_idx && topk_w && n_tok > 0 && n_layers > 0 && K > 0 && K <= 32 && K <= E &&
+                     E <= 4096,
+              "route_zipf_layers: bad args");
+  const long long rows = (long long)n_tok * n_layers;
+  return e4b_launch(c, "route_zipf_layers", k_route_zipf_layers, dim3((unsigned)((rows + 7) / 8)), dim3(256),
+                    (size_t)E * 8, params, table, topk_idx, topk_w, n_tok, n_layers, K, E, seed, salt0, tok0);
 }
 
 E4B_API int e4b_route_zipf_rows(e4b_ctx* c, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int nseq,

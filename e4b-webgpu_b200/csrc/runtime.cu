@@ -43,6 +43,13 @@ E4B_API int e4b_destroy(e4b_ctx* c) {
     if (g) cudaGraphExecDestroy(g);
   e4b::dense_plans_release(c);
   e4b::nccl_release(c);
+  if (c->forked) c->stream = c->main_stream;
+  if (c->side) {
+    cudaStreamSynchronize(c->side);
+    cudaStreamDestroy(c->side);
+  }
+  if (c->fork_ev) cudaEventDestroy(c->fork_ev);
+  if (c->join_ev) cudaEventDestroy(c->join_ev);
   for (auto& e : c->ev) cudaEventDestroy(e);
   cudaFree(c->status);
   cudaStreamDestroy(c->stream);
@@ -193,9 +200,42 @@ E4B_API int e4b_device_status(e4b_ctx* c, uint32_t* st) {
   return E4B_OK;
 }
 
+E4B_API int e4b_side_begin(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, !c->forked && !c->side_pending, "side_begin: side work already open or not joined");
+  if (!c->side) {
+    E4B_CUDA(c, cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+    E4B_CUDA(c, cudaEventCreateWithFlags(&c->fork_ev, cudaEventDisableTiming));
+    E4B_CUDA(c, cudaEventCreateWithFlags(&c->join_ev, cudaEventDisableTiming));
+  }
+  E4B_CUDA(c, cudaEventRecord(c->fork_ev, c->stream));
+  E4B_CUDA(c, cudaStreamWaitEvent(c->side, c->fork_ev, 0));
+  c->main_stream = c->stream;
+  c->stream = c->side;
+  c->forked = true;
+  return E4B_OK;
+}
+E4B_API int e4b_side_end(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, c->forked, "side_end without side_begin");
+  E4B_CUDA(c, cudaEventRecord(c->join_ev, c->side));
+  c->stream = c->main_stream;
+  c->forked = false;
+  c->side_pending = true;
+  return E4B_OK;
+}
+E4B_API int e4b_join(e4b_ctx* c) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, !c->forked && c->side_pending, "join without side_begin / side_end");
+  E4B_CUDA(c, cudaStreamWaitEvent(c->stream, c->join_ev, 0));
+  c->side_pending = false;
+  return E4B_OK;
+}
+
 E4B_API int e4b_plan_begin(e4b_ctx* c) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, !c->capturing, "plan already being recorded");
+  E4B_REQUIRE(c, !c->forked && !c->side_pending, "plan_begin with side work open");
   E4B_CUDA(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
   c->capturing = true;
   return E4B_OK;
@@ -203,6 +243,7 @@ E4B_API int e4b_plan_begin(e4b_ctx* c) {
 E4B_API int e4b_plan_end(e4b_ctx* c, int* plan) {
   E4B_CHECK_CTX(c);
   E4B_REQUIRE(c, c->capturing && plan, "no plan being recorded");
+  E4B_REQUIRE(c, !c->forked && !c->side_pending, "plan_end before e4b_join");
   c->capturing = false;
   cudaGraph_t g = nullptr;
   E4B_CUDA(c, cudaStreamEndCapture(c->stream, &g));

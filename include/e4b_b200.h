@@ -100,6 +100,17 @@ E4B_API int e4b_plan_begin(e4b_ctx* ctx);
 E4B_API int e4b_plan_end(e4b_ctx* ctx, int* plan);
 E4B_API int e4b_plan_launch(e4b_ctx* ctx, int plan, int count);
 E4B_API int e4b_plan_destroy(e4b_ctx* ctx, int plan);
+/* Two concurrent chains on one context: after e4b_side_begin the launches go
+ * to a second stream that starts after the work queued so far; e4b_side_end
+ * sends later launches to the main stream again (which does not wait for the
+ * side chain); e4b_join makes the main stream's later work wait for the side
+ * chain.  So "side_begin, A, side_end, B, join, C" runs A and B concurrently
+ * and C after both.  Plans (graph capture) may contain such pairs; they do
+ * not nest.  No counterpart in the reference, whose WebGPU queue runs its
+ * dispatches in submission order. */
+E4B_API int e4b_side_begin(e4b_ctx* ctx);
+E4B_API int e4b_side_end(e4b_ctx* ctx);
+E4B_API int e4b_join(e4b_ctx* ctx);
 
 /* ----------------------------------------------------------- dequantisation */
 /* Bit-exact block decoders (for parity checks of the in-kernel decode).
@@ -324,6 +335,17 @@ E4B_API int e4b_route_zipf(e4b_ctx* ctx, const uint32_t* params, uint32_t* topk_
  * token-by-token calls route it. */
 E4B_API int e4b_route_zipf_rows(e4b_ctx* ctx, const uint32_t* params, uint32_t* topk_idx, float* topk_w, int nseq,
                                 int npos, int K, int E, float s, uint32_t seed, int salt, int tok0);
+/* The Zipf(s) popularity table e4b_route_zipf builds per CTA, once into device
+ * memory: table[0..E) cumulative popularity by rank, table[E..2E) the seeded
+ * rank -> expert permutation (as u32 bits).  It depends on (s, seed, E) only. */
+E4B_API int e4b_zipf_table(e4b_ctx* ctx, float* table, int E, float s, uint32_t seed);
+/* e4b_route_zipf for every layer of one decode step in one launch: rows
+ * (layer l, token i), layer salt salt0 + l, sequence tok0 + i at position
+ * params[0]; topk_idx / topk_w [n_layers][n_tok][K]; same draws as
+ * e4b_route_zipf with salt = salt0 + l. */
+E4B_API int e4b_route_zipf_layers(e4b_ctx* ctx, const uint32_t* params, const float* table, uint32_t* topk_idx,
+                                  float* topk_w, int n_tok, int n_layers, int K, int E, uint32_t seed, int salt0,
+                                  int tok0);
 /* kernels/router.wgsl:16-63: scale-less RMS of h, x scale x H^-0.5, then as routertop. */
 E4B_API int e4b_router(e4b_ctx* ctx, const float* h, const float* scale, const float* wr, const float* pes,
                        uint32_t* topk_idx, float* topk_w, int H, int E, int K, float eps);

@@ -151,3 +151,28 @@ def test_route_zipf(e4b, dev):
     assert np.array_equal(a[100:], out[1][0])            # same draw for the same global token
     counts = np.bincount(a.reshape(-1), minlength=E)
     assert counts.max() > 4 * counts.mean()               # skewed load
+
+
+def test_route_zipf_layers_matches_per_layer(e4b, dev):
+    """The one-launch-per-step form (a table built once by e4b_zipf_table, every
+    layer's rows in one grid) draws exactly what e4b_route_zipf draws layer by
+    layer."""
+    n, K, E, layers, s, seed, tok0 = 64, 8, 128, 5, 1.1, 1234, 3
+    params = np.zeros(8, np.uint32)
+    params[0] = 517
+    bp = dev.upload(params)
+    table = dev.alloc(2 * E * 4)
+    dev.call("e4b_zipf_table", table.ptr, E, np.float32(s), np.uint32(seed))
+    idx_all, w_all = dev.alloc(layers * n * K * 4), dev.alloc(layers * n * K * 4)
+    dev.call("e4b_route_zipf_layers", bp.ptr, table.ptr, idx_all.ptr, w_all.ptr, n, layers, K, E, np.uint32(seed), 0,
+             tok0)
+    dev.sync()
+    got = dev.read(idx_all, np.uint32, layers * n * K).reshape(layers, n, K)
+    gw = dev.read(w_all, np.float32, layers * n * K)
+    assert np.allclose(gw, 1.0 / K)
+    for layer in range(layers):
+        idx, w = dev.alloc(n * K * 4), dev.alloc(n * K * 4)
+        dev.call("e4b_route_zipf", bp.ptr, idx.ptr, w.ptr, n, K, E, np.float32(s), np.uint32(seed), layer, tok0)
+        dev.sync()
+        assert np.array_equal(got[layer], dev.read(idx, np.uint32, n * K).reshape(n, K)), layer
+    assert dev.status() == 0
