@@ -16,9 +16,15 @@
 //   warps 18-21 epilogue: per superblock, tcgen05.ld of its accumulator,
 //               times d, added to the tile's running sum (kept in TMEM);
 //               softcap and store at the tile's end
-//   warp 22     raw weights: per superblock one 1-D TMA bulk copy per row (the
-//               16-byte aligned 224-byte cover of its 210 bytes), three
-//               superblocks in flight
+//   warp 22     raw weights (tile-packed layout): per superblock one 1-D TMA
+//               bulk copy of the tile's 128 x 210 contiguous bytes, three
+//               superblocks in flight.  With the row-major layout the dequant
+//               threads fetch their rows' 224-byte covers with cp.async instead.
+//
+// Measured on B200 (A4B 262144 x 2816, n = 64): 500 us on the packed layout,
+// 525 us row-major (the mma.sync kernel: 965 us).  The time barely depends on
+// n: dequantisation, the per-K-step MMA issue and the hand-offs between the
+// warp roles bound it, not HBM (605 MB would stream in ~93 us).
 //
 // Exactness.  The superblock scale d (f16) is applied in f32 by the epilogue;
 // inside a superblock the weight is the integer m = sc * (q - 32), |m| <= 4096,
