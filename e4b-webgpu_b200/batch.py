@@ -167,7 +167,7 @@ class BatchEngine(Engine):
         # contiguous TMA copy per 128 rows x superblock (e4b_q6k_lmhead_tiles)
         self.emb_tiles = self._pack_lm_head(self.emb, c.vocab) if B <= 64 else None
         self.emb_shard_tiles = None
-        self.zipf_all = bool(self.zipf) and self.ep is None
+        self.zipf_all = bool(self.zipf)
         if self.zipf_all:
             # benchmark routing of every layer drawn in one launch per step from a
             # popularity table built once
@@ -314,18 +314,18 @@ class BatchEngine(Engine):
             d.call("e4b_event_record", a + 1)
             xev.append((a, a + 1))
 
-    def _moe_ep_send(self):
-        """Dispatch this layer's entries and start the exchange of rows + expert
-        ids (one NCCL group on the side stream)."""
+    def _moe_ep_send(self, topk_idx):
+        """Dispatch this layer's entries (experts topk_idx) and start the exchange
+        of rows + expert ids (one NCCL group on the side stream)."""
         c, d, A, B = self.cfg, self.dev, self.A, self.nseq
         N, rank = self.ep[0], self.ep[1]
         H, E, K = c.hidden, c.experts, c.topk
         if self.ep_transport == "p2p":
-            d.call("e4b_ep_dispatch", A.topk_idx, B, K, E, N, self.cap, A.moe_in, H, None, A.ep_sid, A.ep_slot)
+            d.call("e4b_ep_dispatch", topk_idx, B, K, E, N, self.cap, A.moe_in, H, None, A.ep_sid, A.ep_slot)
             d.call("e4b_ep_push", A.ep_slot, B, K, A.moe_in, H, A.ep_sid, N, rank, self.cap, A.ep_tab[0], A.ep_tab[1],
                    A.ep_tab[3], A.ep_ctr)
             return
-        d.call("e4b_ep_dispatch", A.topk_idx, B, K, E, N, self.cap, A.moe_in, H, A.ep_sx, A.ep_sid, A.ep_slot)
+        d.call("e4b_ep_dispatch", topk_idx, B, K, E, N, self.cap, A.moe_in, H, A.ep_sx, A.ep_sid, A.ep_slot)
         d.call("e4b_ep_exchange2_async", A.ep_sx, A.ep_rx, ctypes.c_size_t(self.cap * H * 2), A.ep_sid, A.ep_rid,
                ctypes.c_size_t(self.cap * 4))
 
@@ -376,6 +376,45 @@ class BatchEngine(Engine):
         return 1000.0 * tot * (2 * self.cfg.layers) / max(n, 1)
 
     # ------------------------------------------------------------ one step (B tokens)
+    def _tail(self, L, y_rows, y_map, topk_w, nxt):
+        c, A = self.cfg, self.A
+        self.dev.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, y_rows, y_map, topk_w, c.topk, L.post_ffw2, L.post_ffw,
+                      A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, c.hidden,
+                      ctypes.c_float(c.eps), ctypes.c_float(L.scale), int(nxt is not None), self.nseq, 1)
+
+    def _moe_zipf(self, L, topk_idx, topk_w, nxt):
+        """The MoE half of a layer under benchmark routing: the step's Zipf draw
+        (topk_idx / topk_w, drawn for every layer at the start of the step)
+        replaces the router's choice, so nothing waits for the router; it still
+        scores the tokens (the model's work), on the side stream, and joins at
+        the end of the layer (its input buffer is rewritten by the next layer)."""
+        c, d, A, B = self.cfg, self.dev, self.A, self.nseq
+        H, E, K, EF, FF = c.hidden, c.experts, c.topk, c.expert_ff, c.ff
+        side = self.overlap_route
+        if side:
+            d.call("e4b_side_begin")
+        d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
+        if side:
+            d.call("e4b_side_end")
+        if self.ep is not None:
+            if self.ep_overlap:
+                self._moe_ep_send(topk_idx)       # the rows travel while the dense FFN runs
+        else:
+            d.call("e4b_expgroup", topk_idx, B, K, E, A.offsets, A.entries, A.inv)
+        d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
+        d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
+        if self.ep is None:
+            d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
+            d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
+            y_rows, y_map = A.yo, A.inv
+        else:
+            if not self.ep_overlap:
+                self._moe_ep_send(topk_idx)
+            y_rows, y_map = self._moe_ep_finish(L)
+        self._tail(L, y_rows, y_map, topk_w, nxt)
+        if side:
+            d.call("e4b_join")
+
     def encode_forward(self):
         c, d, A, B = self.cfg, self.dev, self.A, self.nseq
         H, V, E, K, EF, FF = c.hidden, c.vocab, c.experts, c.topk, c.expert_ff, c.ff
@@ -407,19 +446,22 @@ class BatchEngine(Engine):
                 d.call("e4b_q40mm", A.attn, L.o, A.oparts, c.q_dim, H, B)
             d.call("e4b_rmsacc3", A.oparts, L.post_attn, L.ffn_norm, L.router_s, L.pre_ffw2, A.hidden, A.normed,
                    A.router_in, A.moe_in, A.hidden_b, H, ctypes.c_float(c.eps), B, 1, self.kp_o)
+            if self.zipf_all:
+                self._moe_zipf(L, topk_idx, topk_w, nxt)
+                continue
             side = self.ep is None and self.overlap_route
             if side:
                 # the routing chain (router, Zipf draw, expert sort) on the side stream,
                 # concurrent with the dense FFN on the main stream
                 d.call("e4b_side_begin")
             d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
-            if self.zipf and not self.zipf_all:
+            if self.zipf:
                 d.call("e4b_route_zipf", A.params, A.topk_idx, A.topk_w, B, K, E, ctypes.c_float(self.zipf),
                        ctypes.c_uint32(self.route_seed), L.i, self.tok0)
             if self.ep is not None and self.ep_overlap:
-                self._moe_ep_send()           # the rows travel while the dense FFN runs
+                self._moe_ep_send(A.topk_idx)     # the rows travel while the dense FFN runs
             if side:
-                d.call("e4b_expgroup", topk_idx, B, K, E, A.offsets, A.entries, A.inv)
+                d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
                 d.call("e4b_side_end")
             d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
             d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
@@ -427,17 +469,15 @@ class BatchEngine(Engine):
                 if side:
                     d.call("e4b_join")
                 else:
-                    d.call("e4b_expgroup", topk_idx, B, K, E, A.offsets, A.entries, A.inv)
+                    d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
                 d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
                 d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
                 y_rows, y_map = A.yo, A.inv
             else:
                 if not self.ep_overlap:
-                    self._moe_ep_send()
+                    self._moe_ep_send(A.topk_idx)
                 y_rows, y_map = self._moe_ep_finish(L)
-            d.call("e4b_a4btail_wacc", A.tmp, L.post_ffw1, y_rows, y_map, topk_w, K, L.post_ffw2, L.post_ffw,
-                   A.hidden_b, nxt if nxt is not None else L.attn_norm, A.normed, A.hidden, H, ctypes.c_float(c.eps),
-                   ctypes.c_float(L.scale), int(nxt is not None), B, 1)
+            self._tail(L, y_rows, y_map, A.topk_w, nxt)
         d.call("e4b_rmsnorm", A.hidden, self.out_norm, A.xf, None, None, H, B, ctypes.c_float(c.eps), 1, 0, 0)
         if self.ep is not None and self.v_shard:
             # every rank: its V/N LM-head rows for all ranks' tokens, then the argmax merge
