@@ -36,8 +36,7 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
   const size_t base = (size_t)b * qkvS + (size_t)src * HD;
   float s = 0.f;
   for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float v = qkv[base + d];
-    for (int k = 1; k < nparts; k++) v += qkv[(size_t)k * part_stride + base + d];
+    const float v = sum_parts(qkv + base + d, part_stride, nparts);
     xv[d] = v;
     s = fmaf(v, v, s);
   }

@@ -93,6 +93,21 @@ E4B_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::
 E4B_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 E4B_DEV uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
 
+// p[0] + p[stride] + ... + p[(n - 1) stride], added in that order (the K-split
+// GEMMs' partials); the loads are issued eight at a time, not one per add.
+E4B_DEV float sum_parts(const float* __restrict__ p, size_t stride, int n) {
+  float v = 0.f;
+  for (int k0 = 0; k0 < n; k0 += 8) {
+    float x[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) x[k] = k0 + k < n ? p[(size_t)(k0 + k) * stride] : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (k0 + k < n) v = (k0 + k == 0) ? x[k] : v + x[k];
+  }
+  return v;
+}
+
 E4B_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -76,8 +76,7 @@ __global__ void k_rmsacc3(const float* __restrict__ t, const float* __restrict__
   const size_t ob = (size_t)blockIdx.x * dim;
   float s = 0.f;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-    float v = t[ob + i];
-    for (int k = 1; k < nparts; k++) v += t[(size_t)k * part_stride + ob + i];   // K-part partials, in order
+    const float v = sum_parts(t + ob + i, part_stride, nparts);   // K-part partials, in order
     ts[i] = v;
     hs[i] = h_in[ob + i];
     s = fmaf(v, v, s);
@@ -111,18 +110,33 @@ __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict_
   pdl_wait();
   extern __shared__ float comb[];          // [H] comb, [H] t1, [H] h_in
   __shared__ float sh[32];
+  __shared__ uint32_t s_inv[32];           // this row's K slots (K <= 32) and their weights
+  __shared__ float s_w[32];
   float* ts = comb + H;
   float* hs = comb + 2 * H;
   const size_t ob = (size_t)blockIdx.x * H;
+  if (y && threadIdx.x < K) {
+    s_inv[threadIdx.x] = inv[(size_t)blockIdx.x * K + threadIdx.x];
+    s_w[threadIdx.x] = tkw[(size_t)blockIdx.x * K + threadIdx.x];
+  }
+  __syncthreads();
   float s1 = 0.f, s2 = 0.f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     const float a = t1[ob + i];
     float mv;
     if (y) {
+      // the slots' rows loaded eight at a time, then added in slot order
       mv = 0.f;
-      for (int k = 0; k < K; k++) {
-        const uint32_t r = inv[(size_t)blockIdx.x * K + k];
-        if (r != 0xffffffffu) mv += tkw[(size_t)blockIdx.x * K + k] * y[(size_t)r * H + i];   // 0xffffffff: dropped entry
+      for (int k0 = 0; k0 < K; k0 += 8) {
+        float yv[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const uint32_t r = k0 + k < K ? s_inv[k0 + k] : 0xffffffffu;   // 0xffffffff: dropped entry
+          yv[k] = r != 0xffffffffu ? y[(size_t)r * H + i] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+          if (k0 + k < K && s_inv[k0 + k] != 0xffffffffu) mv += s_w[k0 + k] * yv[k];
       }
     } else {
       mv = m[ob + i];
@@ -255,8 +269,8 @@ E4B_API int e4b_a4btail_wacc(e4b_ctx* c, const float* t1, const float* w1, const
                              const float* w_next, uint16_t* y_next, float* h_out, int H, float eps, float mul, int next,
                              int rows, int xfo) {
   E4B_CHECK_CTX(c);
-  E4B_REQUIRE(c, t1 && w1 && y && inv && topk_w && K > 0 && w2 && wp && h_in && h_out && H > 0 && rows > 0,
-              "a4btail_wacc: bad args");
+  E4B_REQUIRE(c, t1 && w1 && y && inv && topk_w && K > 0 && K <= 32 && w2 && wp && h_in && h_out && H > 0 && rows > 0,
+              "a4btail_wacc: bad args (K <= 32)");
   E4B_REQUIRE(c, !next || (w_next && y_next), "a4btail_wacc: next=1 needs w_next and y_next");
   E4B_REQUIRE(c, !xfo || H % 32 == 0, "a4btail_wacc: fragment order needs H %% 32 == 0");
   const size_t sm = (size_t)H * 12;

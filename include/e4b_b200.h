@@ -163,7 +163,7 @@ E4B_API int e4b_a4btail(e4b_ctx* ctx, const float* t1, const float* w1, const fl
 /* kernels/wacc.wgsl + a4btail.wgsl in one pass (batched MoE tail): the MoE
  * output row m[row] = sum_k topk_w[row][k] * y[inv[row*K+k]] (slot order) is
  * formed in place of reading m; an inv of 0xffffffff (an entry an expert-parallel
- * slab had no room for, flagged in the status word) contributes nothing. */
+ * slab had no room for, flagged in the status word) contributes nothing.  K <= 32. */
 E4B_API int e4b_a4btail_wacc(e4b_ctx* ctx, const float* t1, const float* w1, const float* y, const uint32_t* inv,
                              const float* topk_w, int K, const float* w2, const float* wp, const float* h_in,
                              const float* w_next, uint16_t* y_next, float* h_out, int H, float eps, float mul,
