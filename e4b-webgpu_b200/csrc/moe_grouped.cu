@@ -283,13 +283,22 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
   const int i0 = (int)((int64_t)T * blockIdx.x / gridDim.x);
   const int i1 = (int)((int64_t)T * (blockIdx.x + 1) / gridDim.x);
 
-  // producer cursor over (item, quantum) of this warp's tiles; every lane keeps it
-  auto has_tile = [&](int it) { return (it % p.RR) * TPI + wt < p.tiles && kq0 < kq1; };
-  int pit = i0, pkq = kq0;
-  while (pit < i1 && !has_tile(pit)) pit++;
+  // producer cursor over (item, quantum) of this warp's tiles; every lane keeps
+  // it.  Item it = chunk pci, tile slot prr (it = pci * RR + prr), advanced
+  // incrementally (no division per quantum).
+  int pit = i0, pkq = kq0, pci = i0 / p.RR, prr = i0 - pci * p.RR;
+  auto has_slot = [&](int rr) { return rr * TPI + wt < p.tiles && kq0 < kq1; };
+  auto next_item = [&]() {
+    pit++;
+    if (++prr == p.RR) {
+      prr = 0;
+      pci++;
+    }
+  };
+  while (pit < i1 && !has_slot(prr)) next_item();
   auto issue = [&](int s) {
-    const Chunk c = chunks[pit / p.RR];
-    const int tile = (pit % p.RR) * TPI + wt;
+    const Chunk c = chunks[pci];
+    const int tile = prr * TPI + wt;
     uint8_t* st = stages + s * stage_bytes;
     if (MODE == 0) {
       if (lane == 0) mbar_expect_tx(&full[warp][s], (uint32_t)kQuantumBytes);
@@ -304,7 +313,7 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
     }
     if (++pkq == kq1) {
       pkq = kq0;
-      do pit++; while (pit < i1 && !has_tile(pit));
+      do next_item(); while (pit < i1 && !has_slot(prr));
     }
   };
 #pragma unroll
@@ -318,8 +327,8 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
   L.sel = t < 3 ? 0x3210u : 0x5432u;
   bool ok = true;
   int cur = -1, restage = 0, used = 0;
-  for (int it = i0; it < i1; it++) {
-    const int ci = it / p.RR;
+  int ci = i0 / p.RR, rr = i0 - ci * p.RR;          // item it = ci * RR + rr
+  for (int it = i0; it < i1; it++, rr = rr + 1 == p.RR ? 0 : rr + 1, ci = rr == 0 ? ci + 1 : ci) {
     const Chunk c = chunks[ci];
     if (ci != cur) {
       // every warp is done with the previous chunk's activations
@@ -337,9 +346,9 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
       restage++;
       cur = ci;
     }
-    const bool mine = has_tile(it);
+    const bool mine = has_slot(rr);
     if (KS == 1 && !mine) continue;
-    const int tile = (it % p.RR) * TPI + wt;
+    const int tile = rr * TPI + wt;
     const bool two = TOKC > 8 && c.n > 8;
     const uint16_t* xr0 = xs + (size_t)g * p.xpitch + 8 * t;
     float acc[2][2][4];
