@@ -36,13 +36,20 @@ E4B_DEV uint32_t nib(const uint8_t* blk, int k, const Lane& L) {
 //   low k-half: (B0, B2) -> k = 2t, 2t+1 ; (B1, B3) -> k = 2t+8, 2t+9
 //   high k-half: the same with the high nibbles (elements 16 + j).
 // f16 magic: 0x6400|n = 1024+n, minus 1032 -> n-8 ; 0x6400|n<<4 = 1024+16n, /16 - 72 -> n-8.
+// (a & m) | c in one LOP3 (truth table 0xEA), whatever the compiler would make
+// of the two constants.
+E4B_DEV uint32_t and_or(uint32_t a, uint32_t m, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(m), "r"(c));
+  return d;
+}
 E4B_DEV void dq_row(uint32_t v, uint32_t& lo02, uint32_t& lo13, uint32_t& hi02, uint32_t& hi13) {
   const uint32_t v8 = v >> 8;
-  const uint32_t k1032 = 0x64086408u, kSixteenth = 0x2C002C00u, kM72 = 0xD480D480u;
-  lo02 = hsub2((v & 0x000F000Fu) | 0x64006400u, k1032);
-  lo13 = hsub2((v8 & 0x000F000Fu) | 0x64006400u, k1032);
-  hi02 = hfma2((v & 0x00F000F0u) | 0x64006400u, kSixteenth, kM72);
-  hi13 = hfma2((v8 & 0x00F000F0u) | 0x64006400u, kSixteenth, kM72);
+  const uint32_t k1032 = 0x64086408u, kSixteenth = 0x2C002C00u, kM72 = 0xD480D480u, kMag = 0x64006400u;
+  lo02 = hsub2(and_or(v, 0x000F000Fu, kMag), k1032);
+  lo13 = hsub2(and_or(v8, 0x000F000Fu, kMag), k1032);
+  hi02 = hfma2(and_or(v, 0x00F000F0u, kMag), kSixteenth, kM72);
+  hi13 = hfma2(and_or(v8, 0x00F000F0u, kMag), kSixteenth, kM72);
 }
 
 // ---- B operand: lane (g, t) supplies column g of B, i.e. the activations of
