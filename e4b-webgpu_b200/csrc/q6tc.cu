@@ -17,7 +17,7 @@
 //               times d, added to the tile's running sum (kept in TMEM);
 //               softcap and store at the tile's end
 //   warp 22     raw weights (tile-packed layout): per superblock one 1-D TMA
-//               bulk copy of the tile's 128 x 210 contiguous bytes, three
+//               bulk copy of the tile's 128 x 212 contiguous bytes, three
 //               superblocks in flight.  With the row-major layout the dequant
 //               threads fetch their rows' 224-byte covers with cp.async instead.
 //
@@ -48,6 +48,7 @@ constexpr int kQM = 128;                   // vocabulary rows per tile
 constexpr int kQK = 64;                    // K per step
 constexpr int kQSA = 3, kQSB = 2, kQSR = 3;  // stages: dequantised A, token slabs, raw superblocks
 constexpr int kQCover = 224;               // 16-byte aligned cover of a 210-byte superblock
+constexpr int kPk = 212;                   // packed superblock entry: the 210 bytes + 2 zero bytes (4-byte aligned rows)
 constexpr int kQRawStride = 240;           // bytes per row of a raw stage (15 x 16: odd chunk count)
 constexpr int kQTileA = kQM * 128;         // 16 KB: one f16 tile (hi or -lo) of a K-step
 constexpr int kQMaxNP = 64;
@@ -106,26 +107,27 @@ E4B_DEV uint32_t sc_pair(uint32_t scw, int byte) {
   return h | (h << 16);
 }
 
-// Tile-packed copy of a row-major q6_K matrix: dst superblock (t, sb, m) =
-// row 128 t + m's superblock sb, zero for rows >= OUT (one thread per 2 bytes).
+// Tile-packed copy of a row-major q6_K matrix: dst entry (t, sb, m) = row
+// 128 t + m's superblock sb (210 bytes, then 2 zero bytes so every entry is
+// 4-byte aligned), zero for rows >= OUT (one thread per 2 bytes).
 __global__ void k_q6_pack(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int OUT, int nsb,
                           size_t total) {
   pdl_wait();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
-  const size_t blk = i / 105;
-  const int hw = (int)(i - blk * 105);
+  const size_t blk = i / (kPk / 2);
+  const int hw = (int)(i - blk * (kPk / 2));
   const int m = (int)(blk % kQM);
   const size_t ts = blk / kQM;
   const int sb = (int)(ts % nsb);
   const size_t t = ts / nsb;
   const size_t row = t * kQM + m;
-  dst[i] = row < (size_t)OUT ? src[(row * nsb + sb) * 105 + hw] : (uint16_t)0;
+  dst[i] = row < (size_t)OUT && hw < 105 ? src[(row * nsb + sb) * 105 + hw] : (uint16_t)0;
 }
 
 // PACKED: w is the tile-packed copy (k_q6_pack): superblock sb of row 128 t + m
-// at byte ((t * nsb + sb) * 128 + m) * 210, so a raw stage is one contiguous
-// 26880-byte TMA bulk copy.  Otherwise w is row-major q6_K and the dequant
+// at byte ((t * nsb + sb) * 128 + m) * 212, so a raw stage is one contiguous
+// 27136-byte TMA bulk copy.  Otherwise w is row-major q6_K and the dequant
 // threads fetch their rows' 224-byte covers with cp.async.
 template <bool PACKED>
 __global__ void __launch_bounds__(kQThreads, 1) k_q6tc(const Q6P p, const __grid_constant__ CUtensorMap xmap) {
@@ -264,8 +266,8 @@ __global__ void __launch_bounds__(kQThreads, 1) k_q6tc(const Q6P p, const __grid
           ok = wait_bar(&S.r_full[st], (cr / kQSR) & 1u, p.status, p.wait_ns);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
-          sh = (m * 210) & 15;
-          slot = sR + (size_t)st * kQM * kQRawStride + ((m * 210) & ~15);
+          sh = (m * kPk) & 15;
+          slot = sR + (size_t)st * kQM * kQRawStride + ((m * kPk) & ~15);
         } else {
           st = sb % kQSR;
           __syncwarp();                       // the row's threads are done reading the stage about to be refilled
@@ -355,7 +357,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_q6tc(const Q6P p, const __grid
       const int row = t * kQM + m;
       const bool valid = row < p.OUT;
       for (int sb = 0; sb < p.nsb; sb++, j++) {
-        const size_t doff = PACKED ? (((size_t)t * p.nsb + sb) * kQM + m) * 210 + 208
+        const size_t doff = PACKED ? (((size_t)t * p.nsb + sb) * kQM + m) * kPk + 208
                                    : (size_t)(valid ? row : 0) * p.rowbytes + (size_t)sb * 210 + 208;
         const float d = valid ? h2f(*reinterpret_cast<const uint16_t*>(p.w + doff)) : 0.f;
         const uint32_t buf = j % kQBufs;
@@ -402,9 +404,9 @@ __global__ void __launch_bounds__(kQThreads, 1) k_q6tc(const Q6P p, const __grid
     }
   } else {
     // ---------------- raw-weight producer (tile-packed layout): per superblock
-    // one 1-D TMA bulk copy of the tile's 128 x 210 contiguous bytes
+    // one 1-D TMA bulk copy of the tile's 128 x 212 contiguous bytes
     if (PACKED && lane == 0) {
-      constexpr uint32_t kStage = (uint32_t)kQM * 210;
+      constexpr uint32_t kStage = (uint32_t)kQM * kPk;
       uint32_t cr = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
@@ -435,6 +437,157 @@ __global__ void __launch_bounds__(kQThreads, 1) k_q6tc(const Q6P p, const __grid
 constexpr size_t kQSmemBytes =
     1024 + (size_t)kQSA * 2 * kQTileA + (size_t)kQSB * kQTileB + (size_t)kQSR * kQM * kQRawStride;
 
+// ---------------------------------------------------------------- one token
+// LM head for ONE token row on the tile-packed copy (decode at batch 1), on
+// the warp-level tensor cores.  Work unit = 16 consecutive rows (8 per
+// 128-row tile); a unit's superblock sb is one contiguous 16 x 212-byte
+// stretch of the packed copy, which the warp's lane 0 brings into the warp's
+// ring with one bulk copy, three stages ahead.  Per superblock half (128 k,
+// 8 sub-blocks of 16) the lanes run 16 m16n8k16 MMAs (x as f16 hi + lo) with
+// the block-diagonal B of the q4_0 GEMV: sub-block j's x sits in column j, so
+// column j of the accumulator is sub-block j's dot product and gets its own
+// scale d * sc[j] in f32 afterwards.  A = q - 32, exact in f16; within a
+// sub-block the k order is permuted (lane t's MMA slots 2t, 2t+1, 2t+8, 2t+9
+// hold elements 4t .. 4t+3, the 4 bytes of one word) on both A and B.  The
+// products are exact in the f32 accumulator; only the summation order
+// differs from kernels/q6k.wgsl.
+constexpr int kGW = 16;                    // warps per CTA
+constexpr int kGS = 3;                     // ring stages per warp
+constexpr int kGStage = 16 * kPk;          // one unit's superblock: 3392 bytes
+
+// xs[s][t] for sub-block s (16 elements) and lane slot t: {hi(x[16s+4t], +1),
+// hi(+2, +3), lo(..), lo(..)} with x = hi + lo split into f16.
+E4B_DEV uint4 x_slot(const float* __restrict__ x, int s, int t) {
+  const float4 v = *reinterpret_cast<const float4*>(x + 16 * s + 4 * t);
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  uint16_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const __half hh = __float2half_rn(f[i]);
+    h[i] = __half_as_ushort(hh);
+    l[i] = f2h(f[i] - __half2float(hh));
+  }
+  return make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+}
+// (a & m) | c as one LOP3 (truth table 0xEA)
+E4B_DEV uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(m), "r"(c));
+  return d;
+}
+// 4 six-bit values of one word of a sub-block: nibbles of ql (hi4: the high
+// ones) with bits `qsh` of each qh byte above them, as f16 pairs of (q - 32).
+E4B_DEV void q6_word(uint32_t ql, uint32_t qh, bool hi4, int qsh, uint32_t& p01, uint32_t& p23) {
+  const uint32_t lo4 = hi4 ? (ql >> 4) : ql;
+  const uint32_t hb = ((qh >> qsh) << 4) & 0x30303030u;
+  q6_quad(lop_and_or(lo4, 0x0F0F0F0Fu, hb), p01, p23);
+}
+
+__global__ void __launch_bounds__(32 * kGW, 1) k_q6gv(const uint8_t* __restrict__ wt, const float* __restrict__ x,
+                                                    float* __restrict__ y, int N, int OUT, float softcap,
+                                                    uint32_t* status, uint64_t wait_ns) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __shared__ __align__(8) uint64_t full[kGW][kGS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int nsb = N >> 8, nsub = N >> 4;
+  uint4* xs = reinterpret_cast<uint4*>(gsm);                                   // [nsub][4]
+  uint8_t* ring = gsm + (size_t)nsub * 4 * 16 + (size_t)warp * kGS * kGStage;  // this warp's stages
+  if (lane == 0) {
+    for (int s = 0; s < kGS; s++) mbar_init(&full[warp][s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  const int units = ((OUT + 127) / 128) * 8;                 // 16-row units of whole tiles
+  const int w0 = blockIdx.x * kGW + warp, wstep = gridDim.x * kGW;
+  const int nmine = w0 < units ? (units - w0 + wstep - 1) / wstep : 0;
+  const int steps = nmine * nsb;                             // (unit, superblock) stages of this warp
+  auto issue = [&](int k) {                                  // lane 0: stage k into ring slot k % kGS
+    const int u = w0 + (k / nsb) * wstep, sb = k % nsb;
+    const int tile = u >> 3, rg = u & 7;
+    const uint8_t* src = wt + (((size_t)tile * nsb + sb) * 8 + rg) * (size_t)kGStage;
+    mbar_expect_tx(&full[warp][k % kGS], (uint32_t)kGStage);
+    bulk_g2s(ring + (size_t)(k % kGS) * kGStage, src, (uint32_t)kGStage, &full[warp][k % kGS]);
+  };
+  // the weights do not depend on the previous kernel: request them first
+  if (lane == 0)
+    for (int k = 0; k < kGS && k < steps; k++) issue(k);
+  pdl_wait();
+  for (int i = threadIdx.x; i < nsub * 4; i += blockDim.x) xs[i] = x_slot(x, i >> 2, i & 3);
+  __syncthreads();
+
+  const int ra = g * kPk, rb = (g + 8) * kPk;                // this lane's rows in a stage
+  bool ok = true;
+  int k = 0;
+  for (int j = 0; j < nmine; j++) {
+    const int u = w0 + j * wstep;
+    float acc_a = 0.f, acc_b = 0.f;
+    for (int sb = 0; sb < nsb; sb++, k++) {
+      const int st = k % kGS;
+      if (ok) ok = mbar_wait(&full[warp][st], (uint32_t)((k / kGS) & 1), status);
+      ok = __all_sync(0xffffffffu, ok);      // the MMAs below need the whole warp on one path
+      const uint8_t* sg = ring + (size_t)st * kGStage;
+      if (ok) {
+        const float da = h2f(*reinterpret_cast<const uint16_t*>(sg + ra + 208));
+        const float db = h2f(*reinterpret_cast<const uint16_t*>(sg + rb + 208));
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          // this lane's B: x of sub-block g of the half (column g), hi and lo
+          const uint4 xv = xs[(16 * sb + 8 * h + g) * 4 + t];
+          uint32_t qla[4], qlb[4], qha[2], qhb[2];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {      // ql words (jj & 1, lh) = (q >> 1, q & 1)
+            const int o = 64 * h + 32 * (q >> 1) + 16 * (q & 1) + 4 * t;
+            qla[q] = *reinterpret_cast<const uint32_t*>(sg + ra + o);
+            qlb[q] = *reinterpret_cast<const uint32_t*>(sg + rb + o);
+          }
+#pragma unroll
+          for (int lh = 0; lh < 2; lh++) {
+            const int o = 128 + 32 * h + 16 * lh + 4 * t;
+            qha[lh] = *reinterpret_cast<const uint32_t*>(sg + ra + o);
+            qhb[lh] = *reinterpret_cast<const uint32_t*>(sg + rb + o);
+          }
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int jb = 0; jb < 8; jb++) {   // sub-block jb = 2 jj + lh of the half
+            const int jj = jb >> 1, lh = jb & 1, q = 2 * (jj & 1) + lh;
+            uint32_t a01, a23, b01, b23;
+            q6_word(qla[q], qha[lh], jj >= 2, 2 * jj, a01, a23);
+            q6_word(qlb[q], qhb[lh], jj >= 2, 2 * jj, b01, b23);
+            const bool mine = g == jb;
+            mma16816(c, a01, b01, a23, b23, mine ? xv.x : 0u, mine ? xv.y : 0u);
+            mma16816(c, a01, b01, a23, b23, mine ? xv.z : 0u, mine ? xv.w : 0u);
+          }
+          // c[0], c[1]: row g, sub-blocks 2t, 2t+1 of the half; c[2], c[3]: row g + 8
+          const int so = 192 + 8 * h + 2 * t;
+          const uint32_t sa = *reinterpret_cast<const uint16_t*>(sg + ra + so);
+          const uint32_t sbv = *reinterpret_cast<const uint16_t*>(sg + rb + so);
+          acc_a = fmaf(da, fmaf((float)(int8_t)(sa & 0xFFu), c[0], (float)(int8_t)(sa >> 8) * c[1]), acc_a);
+          acc_b = fmaf(db, fmaf((float)(int8_t)(sbv & 0xFFu), c[2], (float)(int8_t)(sbv >> 8) * c[3]), acc_b);
+        }
+      }
+      __syncwarp();                  // every lane's reads of the stage are done before it is refilled
+      if (lane == 0 && ok && k + kGS < steps) issue(k + kGS);
+    }
+    // the 4 lanes of a row group hold its sub-block columns: sum them
+    acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
+    acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 2);
+    acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
+    acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 2);
+    const int r0 = 16 * u + g;
+    if (t == 0 && ok) {
+      if (r0 < OUT) y[r0] = softcap != 0.f ? softcap * tanhf(acc_a / softcap) : acc_a;
+      if (r0 + 8 < OUT) y[r0 + 8] = softcap != 0.f ? softcap * tanhf(acc_b / softcap) : acc_b;
+    }
+  }
+  // copies still in flight after a time-out land (bounded) before the CTA ends
+  if (lane == 0 && !ok)
+    for (int q = k; q < k + kGS && q < steps; q++) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full[warp][q % kGS], (uint32_t)((q / kGS) & 1)) && globaltimer_ns() - t0 < wait_ns) {
+      }
+    }
+}
+
 }  // namespace
 
 namespace e4b {
@@ -444,7 +597,7 @@ bool q6tc_supported(const uint8_t* w, const void* scratch, int N, int OUT, int n
          reinterpret_cast<uintptr_t>(scratch) % 16 == 0;
 }
 
-size_t q6_packed_bytes(int N, int OUT) { return (size_t)((OUT + kQM - 1) / kQM) * (N / 256) * kQM * 210; }
+size_t q6_packed_bytes(int N, int OUT) { return (size_t)((OUT + kQM - 1) / kQM) * (N / 256) * kQM * kPk; }
 
 // scratch: 2 * NP * N halves (NP = 32 for n <= 32, else 64).
 int q6tc_lmhead(e4b_ctx* c, const uint8_t* w, bool packed, const float* x, uint16_t* scratch, float* y, int N,
@@ -513,10 +666,21 @@ E4B_API int e4b_q6k_pack_tiles(e4b_ctx* c, const uint8_t* w, uint8_t* wt, int N,
 E4B_API int e4b_q6k_lmhead_tiles(e4b_ctx* c, const uint8_t* wt, const float* x, uint16_t* scratch, float* y, int N,
                                  int OUT, float softcap, int n) {
   E4B_CHECK_CTX(c);
-  E4B_REQUIRE(c, wt && x && scratch && y && N > 0 && N % 256 == 0 && OUT > 0, "q6k_lmhead_tiles: bad args");
+  E4B_REQUIRE(c, wt && x && y && N > 0 && N % 256 == 0 && OUT > 0, "q6k_lmhead_tiles: bad args");
   E4B_REQUIRE(c, n >= 1 && n <= kQMaxNP, "q6k_lmhead_tiles: n=%d must be 1..%d", n, kQMaxNP);
-  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(wt) % 16 == 0 && reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
-              "q6k_lmhead_tiles: wt and scratch must be 16-byte aligned");
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(wt) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0,
+              "q6k_lmhead_tiles: wt and x must be 16-byte aligned");
+  if (n == 1) {
+    // one token: the warp-level GEMV (k_q6gv), no scratch
+    const size_t smem = (size_t)N * 4 + (size_t)kGW * kGS * kGStage;
+    E4B_REQUIRE(c, smem <= 227 * 1024, "q6k_lmhead_tiles: N=%d too large for one token's staged x", N);
+    cudaError_t e = cudaFuncSetAttribute(k_q6gv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q6gv smem attr: %s", cudaGetErrorString(e));
+    return e4b_launch(c, "q6gv", k_q6gv, dim3((unsigned)c->sm_count), dim3(32 * kGW), smem, wt, x, y, N, OUT, softcap,
+                      c->status, c->wait_ns);
+  }
+  E4B_REQUIRE(c, scratch && reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
+              "q6k_lmhead_tiles: scratch must be 16-byte aligned");
   return e4b::q6tc_lmhead(c, wt, true, x, scratch, y, N, OUT, softcap, n);
 }
 

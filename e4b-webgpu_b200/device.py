@@ -38,7 +38,7 @@ _RUNTIME = {"e4b_create", "e4b_destroy", "e4b_device_info", "e4b_alloc", "e4b_fr
             "e4b_set_option", "e4b_dense_plan_create", "e4b_dense_plan_destroy",
             "e4b_dense_plan_trace", "e4b_dense_plan_phases", "e4b_nccl_init", "e4b_nccl_destroy",
             "e4b_ep_exchange", "e4b_ep_exchange2_async", "e4b_ep_join", "e4b_ep_allgather", "e4b_ipc_handle",
-            "e4b_ipc_open", "e4b_ipc_close"}
+            "e4b_ipc_open", "e4b_ipc_close", "e4b_side_begin", "e4b_side_end", "e4b_join"}
 
 
 def _ptr(x):
@@ -80,6 +80,8 @@ class Device:
             n = self.KERNELS.get(name, 1)
             if name == "e4b_routertop" and getattr(self, "has_workspace", False):
                 n = 2          # split-K scores + per-token top-K
+            if name == "e4b_q6k_lmhead_tiles" and args[-1] == 1:
+                n = 1          # one token: the GEMV alone, no activation split
             self.kernel_launches += n
         return rc
 

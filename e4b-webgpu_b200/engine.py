@@ -107,6 +107,13 @@ class Engine:
         self._load_weights()
         self._alloc_activations()
         self.dense_plan = self._create_dense_plan() if self.fused else None
+        # the fused path's LM head streams a tile-packed copy of the q6_K table
+        # (one contiguous bulk copy per 16 rows x superblock; the warp-MMA GEMV)
+        self.emb_tiles = None
+        if self.fused:
+            H, V = self.cfg.hidden, self.cfg.vocab
+            self.emb_tiles = self.dev.alloc(int(self.dev.L.e4b_q6k_packed_bytes(H, V)), "lmHeadTiles")
+            self.dev.call("e4b_q6k_pack_tiles", self.emb, self.emb_tiles, H, V)
 
     # ------------------------------------------------------------ loading
     def _raw(self, name: str):
@@ -285,7 +292,7 @@ class Engine:
         H, V = c.hidden, c.vocab
         if self.fused:
             d.call("e4b_dense_plan_run", self.dense_plan)
-            ops.q6k_lmhead(d, self.emb, A.xf, A.logits, N=H, OUT=V, SOFTCAP=c.softcap)
+            d.call("e4b_q6k_lmhead_tiles", self.emb_tiles, A.xf, None, A.logits, H, V, ctypes.c_float(c.softcap), 1)
             ops.argmax(d, A.logits, A.amax_part, A.amax, N=V, PARTS=ARGMAX_PARTS)
             ops.feedtok(d, A.amax, A.params, A.ring, RING_CAP=RING_CAP)
             return

@@ -413,8 +413,9 @@ E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* ctx, const uint8_t* w, const float* x, 
                                 int OUT, float softcap, int n);
 /* Tile-packed copy of a row-major q6_K matrix for e4b_q6k_lmhead_tiles: for
  * tile t = row / 128, superblock sb, row m = row % 128 the 210-byte superblock
- * sits at ((t * N/256 + sb) * 128 + m) * 210; rows past OUT are zero.  Size:
- * e4b_q6k_packed_bytes(N, OUT) = ceil(OUT/128) * N/256 * 26880.  Same bytes as
+ * sits at ((t * N/256 + sb) * 128 + m) * 212, followed by 2 zero bytes (so
+ * every entry is 4-byte aligned); rows past OUT are zero.  Size:
+ * e4b_q6k_packed_bytes(N, OUT) = ceil(OUT/128) * N/256 * 27136.  Same bytes as
  * the reference's q6_K table (kernels/q6k.wgsl), reordered so that each
  * (tile, superblock) is one contiguous TMA bulk copy. */
 E4B_API size_t e4b_q6k_packed_bytes(int N, int OUT);

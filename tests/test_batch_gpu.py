@@ -37,24 +37,25 @@ def test_batched_moe_decode_matches_oracle(e4b, models, B):
 
 def _pack_tiles_ref(w, V, N):
     """numpy restatement of the tile-packed layout: superblock sb of row 128 t + m at
-    ((t * nsb + sb) * 128 + m) * 210, zero rows past V."""
+    ((t * nsb + sb) * 128 + m) * 212 (210 bytes + 2 zero bytes), zero rows past V."""
     nsb, T = N // 256, (V + 127) // 128
-    blocks = np.zeros((T * 128, nsb, 210), np.uint8)
-    blocks[:V] = np.frombuffer(bytes(w), np.uint8).reshape(V, nsb, 210)
-    return blocks.reshape(T, 128, nsb, 210).transpose(0, 2, 1, 3).reshape(-1)
+    blocks = np.zeros((T * 128, nsb, 212), np.uint8)
+    blocks[:V, :, :210] = np.frombuffer(bytes(w), np.uint8).reshape(V, nsb, 210)
+    return blocks.reshape(T, 128, nsb, 212).transpose(0, 2, 1, 3).reshape(-1)
 
 
 @pytest.mark.parametrize("V,N,n", [(3000, 512, 11), (1000, 768, 64), (1000, 768, 1), (40000, 1024, 64),
-                                   (40000, 512, 33), (4096, 2816, 64)])
+                                   (40000, 512, 33), (4096, 2816, 64), (40000, 2048, 1), (3000, 256, 1)])
 def test_lmhead_tiles(e4b, dev, V, N, n):
     """e4b_q6k_pack_tiles lays the bytes out as the numpy restatement says, and
-    e4b_q6k_lmhead_tiles on the packed copy matches the oracle q6_K matvec per row
-    and the row-major e4b_q6k_lmhead_rows to the last bit of either (same
-    per-superblock accumulation order)."""
+    e4b_q6k_lmhead_tiles on the packed copy matches the oracle q6_K matvec per row;
+    for n > 1 also the row-major e4b_q6k_lmhead_rows to the last bit (the same
+    tcgen05 kernel and per-superblock accumulation order).  n = 1 runs the
+    one-token warp-MMA GEMV (k_q6gv); V = 40000 gives its warps several units."""
     from oracle import ops as O
     w = e4b.synth.quant_q6_K(e4b.synth.normal_f32(V * N, 43 + V, "lmtiles", 0.02))
     nbytes = int(dev.L.e4b_q6k_packed_bytes(N, V))
-    assert nbytes == (V + 127) // 128 * (N // 256) * 128 * 210
+    assert nbytes == (V + 127) // 128 * (N // 256) * 128 * 212
     bw, wt = dev.upload(w), dev.alloc(nbytes)
     dev.call("e4b_q6k_pack_tiles", bw.ptr, wt.ptr, N, V)
     dev.sync()
@@ -66,7 +67,8 @@ def test_lmhead_tiles(e4b, dev, V, N, n):
     dev.sync()
     assert dev.status() == 0
     got = dev.read(y, np.float32, n * V).reshape(n, V)
-    assert np.array_equal(got, dev.read(y2, np.float32, n * V).reshape(n, V))
+    if n > 1:
+        assert np.array_equal(got, dev.read(y2, np.float32, n * V).reshape(n, V))
     for r in range(n):
         ref = O.softcap(O.q6k_matvec(w, x[r], V, N), 30.0)
         assert np.max(np.abs(got[r] - ref)) / np.max(np.abs(ref)) < 2e-5
