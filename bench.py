@@ -866,12 +866,13 @@ def run_lmhead(e4b, dev, args):
         y = dev.alloc(n * V * 4, "y")
         scr = dev.alloc(2 * max(64, (n + 7) // 8 * 8) * H * 2, "scr")
         row = {"n": n}
-        for label, tc in (("tiles", 0), ("tc", 1), ("mma_sync", 65)):
-            if tc:
+        for label, tc in (("tiles", 0), ("tiles_mma", -2), ("tiles_tc", -1), ("tc", 1), ("mma_sync", 65)):
+            if tc > 0:
                 dev.call("e4b_set_option", b"lmhead_tc_min", tc)
+            dev.call("e4b_set_option", b"lmhead_tiles_tc", -tc if tc < 0 else 0)
             def loop(x=x, y=y, scr=scr, n=n, tc=tc):
                 for _ in range(args.launches):
-                    if tc == 0:
+                    if tc <= 0:
                         dev.call("e4b_q6k_lmhead_tiles", wt, x, scr, y, H, V, np.float32(cfg.softcap), n)
                     else:
                         dev.call("e4b_q6k_lmhead_rows", w, x, scr, y, H, V, np.float32(cfg.softcap), n)
@@ -880,6 +881,7 @@ def run_lmhead(e4b, dev, args):
             row[label] = {"us": round(us, 1), "gbs": round(byts / us / 1e3, 1), "frac": round(byts / us / 1e3 / hbm, 4),
                           "useful_tflops": round(2.0 * n * V * H / us / 1e6, 1)}
         dev.call("e4b_set_option", b"lmhead_tc_min", 1)
+        dev.call("e4b_set_option", b"lmhead_tiles_tc", 0)
         out.append(row)
         dev.free(x), dev.free(y), dev.free(scr)
     st = dev.status()

@@ -29,6 +29,7 @@ struct e4b_ctx {
   int attn_grid_cap = 0;            // batched attention: at most this many CTAs (0 = one per SM)
   uint64_t wait_ns = 1000000000ull; // bound of the batched attention's and ep_wait's device waits
   int lmhead_tc_min = 1;             // batched LM head: tcgen05 kernel for n >= this (<= 64)
+  int lmhead_tiles_tc = 0;           // packed LM head, 2..64 rows: 0 = by row count, 1 = tcgen05, 2 = warp-MMA
   cudaStream_t main_stream = nullptr;  // e4b_side_begin .. e4b_side_end: launches go to `side`
   cudaStream_t side = nullptr;
   cudaEvent_t fork_ev = nullptr, join_ev = nullptr;

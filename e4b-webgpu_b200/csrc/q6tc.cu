@@ -588,6 +588,179 @@ __global__ void __launch_bounds__(32 * kGW, 1) k_q6gv(const uint8_t* __restrict_
     }
 }
 
+// ---------------------------------------------------------------- a few tokens
+// LM head for 2..64 token rows on the tile-packed copy, on the warp-level
+// tensor cores.  A CTA takes whole 128-row tiles; per superblock its producer
+// warp brings in the tile's 128 x 212 bytes (one bulk copy) and the
+// superblock's activation slab (x as f16 hi + lo in B-fragment order, built
+// once by k_q6gm_prep, NG x 8 KB), and each of 8 MMA warps runs its 16 rows
+// against every token group: per sub-block of 16 elements, for each group of 8
+// tokens, two m16n8k16 MMAs (x hi, x lo) and the sub-block's scale d * sc
+// applied to the four results in f32.  A = q - 32 (exact in f16), the k order
+// inside a sub-block permuted on A and B alike as in k_q6gv.
+constexpr int kMW = 8;                      // MMA warps (16 rows each)
+constexpr int kMWS = 3;                     // weight stages
+constexpr int kMXS = 2;                     // activation stages
+constexpr int kMStage = kQM * kPk;          // 27136 bytes
+constexpr int kMXSlab = 16 * 8 * 32 * 16;   // one superblock, 8 groups: 64 KB
+
+// xp[sb][s16][q][lane] = {hi(x[8q + g][k], x[..][k + 1]), hi(+2, +3), lo(..), lo(..)},
+// k = 256 sb + 16 s16 + 4 t, lane = 4 g + t; zero for tokens >= n.
+__global__ void k_q6gm_prep(const float* __restrict__ x, uint4* __restrict__ xp, int n, int N, int NG) {
+  pdl_wait();
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t total = (size_t)(N / 16) * NG * 32;
+  if (idx >= total) return;
+  const int lane = (int)(idx & 31);
+  const size_t sq = idx >> 5;
+  const int q = (int)(sq % NG);
+  const int s = (int)(sq / NG);                   // global sub-block: 16 sb + s16
+  const int tok = 8 * q + (lane >> 2), k = 16 * s + 4 * (lane & 3);
+  uint16_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+  if (tok < n) {
+    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)tok * N + k);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const __half hh = __float2half_rn(f[i]);
+      h[i] = __half_as_ushort(hh);
+      l[i] = f2h(f[i] - __half2float(hh));
+    }
+  }
+  xp[idx] = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(l[0], l[1]), pack_h2(l[2], l[3]));
+}
+
+template <int NG>   // token groups of 8 (n <= 8 NG)
+__global__ void __launch_bounds__(32 * (kMW + 1), 1) k_q6gm(const uint8_t* __restrict__ wt, const uint4* __restrict__ xp,
+                                                          float* __restrict__ y, int N, int OUT, int n, float softcap,
+                                                          uint32_t* status) {
+  extern __shared__ __align__(16) uint8_t msm[];
+  __shared__ __align__(8) uint64_t wfull[kMWS], wempty[kMWS], xfull[kMXS], xempty[kMXS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int nsb = N >> 8, ntiles = (OUT + kQM - 1) / kQM;
+  const uint32_t xbytes = (uint32_t)NG * (kMXSlab / 8);
+  uint8_t* wring = msm;                                       // [kMWS][27136]
+  uint8_t* xring = msm + (size_t)kMWS * kMStage;              // [kMXS][xbytes = NG x 8 KB]
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kMWS; i++) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wempty[i], kMW);
+    }
+    for (int i = 0; i < kMXS; i++) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], kMW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int mytiles = (int)blockIdx.x < ntiles ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  const int steps = mytiles * nsb;
+  if (warp == kMW) {
+    // ---------------- producer: weights (which need nothing from the previous kernel) and activation slabs
+    if (lane == 0) {
+      bool ok = true;
+      for (int k = 0; k < steps && ok; k++) {
+        const int tile = (int)blockIdx.x + (k / nsb) * (int)gridDim.x, sb = k % nsb;
+        const int ws = k % kMWS, xs = k % kMXS;
+        if (k >= kMWS) ok = mbar_wait(&wempty[ws], (uint32_t)(((k / kMWS) - 1) & 1), status);
+        if (!ok) break;
+        mbar_expect_tx(&wfull[ws], (uint32_t)kMStage);
+        bulk_g2s(wring + (size_t)ws * kMStage, wt + ((size_t)tile * nsb + sb) * kMStage, (uint32_t)kMStage, &wfull[ws]);
+        if (k == 0) pdl_wait();          // the activation slabs come from the previous kernel
+        if (k >= kMXS) ok = mbar_wait(&xempty[xs], (uint32_t)(((k / kMXS) - 1) & 1), status);
+        if (!ok) break;
+        mbar_expect_tx(&xfull[xs], xbytes);
+        bulk_g2s(xring + (size_t)xs * xbytes, xp + (size_t)sb * 16 * NG * 32, xbytes, &xfull[xs]);
+      }
+      if (steps == 0) pdl_wait();
+    }
+    return;
+  }
+  // ---------------- MMA warps: rows 16 warp + g and + 8 of the tile
+  const int ra = (16 * warp + g) * kPk, rb = ra + 8 * kPk;
+  bool ok = true;
+  int k = 0;
+  for (int j = 0; j < mytiles; j++) {
+    const int tile = (int)blockIdx.x + j * (int)gridDim.x;
+    float acc[NG][4];
+#pragma unroll
+    for (int q = 0; q < NG; q++) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+    for (int sb = 0; sb < nsb; sb++, k++) {
+      const int ws = k % kMWS, xs = k % kMXS;
+      if (ok) ok = mbar_wait(&wfull[ws], (uint32_t)((k / kMWS) & 1), status);
+      if (ok) ok = mbar_wait(&xfull[xs], (uint32_t)((k / kMXS) & 1), status);
+      ok = __all_sync(0xffffffffu, ok);      // the MMAs below need the whole warp on one path
+      if (ok) {
+        const uint8_t* sg = wring + (size_t)ws * kMStage;
+        const uint4* xsl = reinterpret_cast<const uint4*>(xring + (size_t)xs * xbytes);
+        const float da = h2f(*reinterpret_cast<const uint16_t*>(sg + ra + 208));
+        const float db = h2f(*reinterpret_cast<const uint16_t*>(sg + rb + 208));
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          uint32_t qla[4], qlb[4], qha[2], qhb[2];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const int o = 64 * h + 32 * (q >> 1) + 16 * (q & 1) + 4 * t;
+            qla[q] = *reinterpret_cast<const uint32_t*>(sg + ra + o);
+            qlb[q] = *reinterpret_cast<const uint32_t*>(sg + rb + o);
+          }
+#pragma unroll
+          for (int lh = 0; lh < 2; lh++) {
+            const int o = 128 + 32 * h + 16 * lh + 4 * t;
+            qha[lh] = *reinterpret_cast<const uint32_t*>(sg + ra + o);
+            qhb[lh] = *reinterpret_cast<const uint32_t*>(sg + rb + o);
+          }
+          // the half's 8 scales of rows g and g + 8
+          const uint2 sca = make_uint2(*reinterpret_cast<const uint32_t*>(sg + ra + 192 + 8 * h),
+                                       *reinterpret_cast<const uint32_t*>(sg + ra + 196 + 8 * h));
+          const uint2 scb = make_uint2(*reinterpret_cast<const uint32_t*>(sg + rb + 192 + 8 * h),
+                                       *reinterpret_cast<const uint32_t*>(sg + rb + 196 + 8 * h));
+#pragma unroll
+          for (int jb = 0; jb < 8; jb++) {
+            const int jj = jb >> 1, lh = jb & 1, q = 2 * (jj & 1) + lh;
+            uint32_t a01, a23, b01, b23;
+            q6_word(qla[q], qha[lh], jj >= 2, 2 * jj, a01, a23);
+            q6_word(qlb[q], qhb[lh], jj >= 2, 2 * jj, b01, b23);
+            const uint32_t wa = jb < 4 ? sca.x : sca.y, wb = jb < 4 ? scb.x : scb.y;
+            const float sa = da * (float)(int8_t)((wa >> (8 * (jb & 3))) & 0xFFu);
+            const float sbb = db * (float)(int8_t)((wb >> (8 * (jb & 3))) & 0xFFu);
+            const uint4* xq = xsl + (size_t)(8 * h + jb) * NG * 32 + lane;
+#pragma unroll
+            for (int q2 = 0; q2 < NG; q2++) {
+              const uint4 xv = xq[q2 * 32];
+              float c[4] = {0.f, 0.f, 0.f, 0.f};
+              mma16816(c, a01, b01, a23, b23, xv.x, xv.y);
+              mma16816(c, a01, b01, a23, b23, xv.z, xv.w);
+              acc[q2][0] = fmaf(sa, c[0], acc[q2][0]);
+              acc[q2][1] = fmaf(sa, c[1], acc[q2][1]);
+              acc[q2][2] = fmaf(sbb, c[2], acc[q2][2]);
+              acc[q2][3] = fmaf(sbb, c[3], acc[q2][3]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&wempty[ws]);
+        mbar_arrive(&xempty[xs]);
+      }
+    }
+    if (!ok) continue;
+    // c[0], c[1]: row g, tokens 8 q + 2 t, + 1; c[2], c[3]: row g + 8
+    const int row = tile * kQM + 16 * warp + g;
+#pragma unroll
+    for (int q2 = 0; q2 < NG; q2++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const int rr = row + 8 * (r >> 1), tok = 8 * q2 + 2 * t + (r & 1);
+        if (rr < OUT && tok < n) {
+          const float v = acc[q2][r];
+          y[(size_t)tok * OUT + rr] = softcap != 0.f ? softcap * tanhf(v / softcap) : v;
+        }
+      }
+  }
+}
+
 }  // namespace
 
 namespace e4b {
@@ -681,7 +854,29 @@ E4B_API int e4b_q6k_lmhead_tiles(e4b_ctx* c, const uint8_t* wt, const float* x, 
   }
   E4B_REQUIRE(c, scratch && reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
               "q6k_lmhead_tiles: scratch must be 16-byte aligned");
-  return e4b::q6tc_lmhead(c, wt, true, x, scratch, y, N, OUT, softcap, n);
+  // measured (A4B shape): the warp-MMA kernel wins up to 32 rows, the tcgen05 one above
+  const bool tc = c->lmhead_tiles_tc == 1 || (c->lmhead_tiles_tc == 0 && n > 32);
+  if (tc) return e4b::q6tc_lmhead(c, wt, true, x, scratch, y, N, OUT, softcap, n);
+  // a few tokens: the warp-MMA kernel over activation slabs built once into scratch
+  const int NG = n <= 8 ? 1 : (n <= 16 ? 2 : (n <= 32 ? 4 : 8));
+  const size_t tot = (size_t)(N / 16) * NG * 32;
+  uint4* xp = reinterpret_cast<uint4*>(scratch);
+  if (int r = e4b_launch(c, "q6gm_prep", k_q6gm_prep, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, x, xp, n, N,
+                         NG))
+    return r;
+  const size_t smem = (size_t)kMWS * kMStage + (size_t)kMXS * NG * (kMXSlab / 8);
+  const int ntiles = (OUT + kQM - 1) / kQM;
+  const int grid = ntiles < c->sm_count ? ntiles : c->sm_count;
+  auto launch = [&](auto kern) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "q6gm smem attr: %s", cudaGetErrorString(e));
+    return e4b_launch(c, "q6gm", kern, dim3((unsigned)grid), dim3(32 * (kMW + 1)), smem, wt, (const uint4*)xp, y, N,
+                      OUT, n, softcap, c->status);
+  };
+  if (NG == 1) return launch(k_q6gm<1>);
+  if (NG == 2) return launch(k_q6gm<2>);
+  if (NG == 4) return launch(k_q6gm<4>);
+  return launch(k_q6gm<8>);
 }
 
 }  // extern "C"

@@ -166,6 +166,9 @@ E4B_API int e4b_set_option(e4b_ctx* c, const char* name, int value) {
   } else if (!strcmp(name, "attn_grid_cap")) {
     E4B_REQUIRE(c, value >= 0, "attn_grid_cap must be >= 0 (0 = one CTA per SM)");
     c->attn_grid_cap = value;
+  } else if (!strcmp(name, "lmhead_tiles_tc")) {
+    E4B_REQUIRE(c, value >= 0 && value <= 2, "lmhead_tiles_tc must be 0, 1 or 2");
+    c->lmhead_tiles_tc = value;
   } else if (!strcmp(name, "lmhead_tc_min")) {
     E4B_REQUIRE(c, value >= 1 && value <= 65, "lmhead_tc_min must be 1..65 (65 = never)");
     c->lmhead_tc_min = value;

@@ -86,6 +86,9 @@ E4B_API size_t e4b_workspace_bytes(void);
  * e4b_attdec_seq, so each CTA runs more items (the stage ring's wrap-around).
  * "lmhead_tc_min" (1..65, default 1): e4b_q6k_lmhead_rows uses its tcgen05
  * kernel for n >= this many rows (65: never).
+ * "lmhead_tiles_tc" (0..2, default 0): how e4b_q6k_lmhead_tiles runs 2..64
+ * rows: 0 = the warp-MMA kernel up to 32 rows, the tcgen05 one above; 1 = always
+ * tcgen05; 2 = always warp-MMA.
  * "wait_limit_us" (1000..10000000, default 1000000): the bound of the batched
  * attention's and e4b_ep_wait's device waits, after which the call records
  * E4B_ST_TIMEOUT in the status word and returns. */
@@ -420,8 +423,11 @@ E4B_API int e4b_q6k_lmhead_rows(e4b_ctx* ctx, const uint8_t* w, const float* x, 
  * (tile, superblock) is one contiguous TMA bulk copy. */
 E4B_API size_t e4b_q6k_packed_bytes(int N, int OUT);
 E4B_API int e4b_q6k_pack_tiles(e4b_ctx* ctx, const uint8_t* w, uint8_t* wt, int N, int OUT);
-/* e4b_q6k_lmhead_rows on the tile-packed copy (1 <= n <= 64): the tcgen05 kernel
- * with the weights streamed by TMA; scratch: 2*N*64 u16, 16-byte aligned. */
+/* e4b_q6k_lmhead_rows on the tile-packed copy (1 <= n <= 64), weights streamed
+ * by bulk copies: n = 1 the warp-MMA GEMV (scratch unused, may be null); n >= 2
+ * the warp-MMA kernel over activation slabs built in scratch, or the tcgen05
+ * kernel (above 32 rows; option "lmhead_tiles_tc"); scratch: 2*N*64 u16,
+ * 16-byte aligned; x 16-byte aligned. */
 E4B_API int e4b_q6k_lmhead_tiles(e4b_ctx* ctx, const uint8_t* wt, const float* x, uint16_t* scratch, float* y, int N,
                                  int OUT, float softcap, int n);
 E4B_API int e4b_pleprep(e4b_ctx* ctx, const uint8_t* table, const uint32_t* params, const uint32_t* tok,

@@ -46,12 +46,14 @@ def _pack_tiles_ref(w, V, N):
 
 @pytest.mark.parametrize("V,N,n", [(3000, 512, 11), (1000, 768, 64), (1000, 768, 1), (40000, 1024, 64),
                                    (40000, 512, 33), (4096, 2816, 64), (40000, 2048, 1), (3000, 256, 1)])
-def test_lmhead_tiles(e4b, dev, V, N, n):
+@pytest.mark.parametrize("tc", [2, 1])
+def test_lmhead_tiles(e4b, dev, V, N, n, tc):
     """e4b_q6k_pack_tiles lays the bytes out as the numpy restatement says, and
-    e4b_q6k_lmhead_tiles on the packed copy matches the oracle q6_K matvec per row;
-    for n > 1 also the row-major e4b_q6k_lmhead_rows to the last bit (the same
-    tcgen05 kernel and per-superblock accumulation order).  n = 1 runs the
-    one-token warp-MMA GEMV (k_q6gv); V = 40000 gives its warps several units."""
+    e4b_q6k_lmhead_tiles on the packed copy matches the oracle q6_K matvec per row.
+    n = 1 runs the one-token warp-MMA GEMV (k_q6gv); n > 1 the warp-MMA kernel
+    over activation slabs (tc = 2) or the tcgen05 kernel (tc = 1), which then
+    also equals the row-major e4b_q6k_lmhead_rows to the last bit (the same
+    per-superblock accumulation order).  V = 40000 gives the warps several units."""
     from oracle import ops as O
     w = e4b.synth.quant_q6_K(e4b.synth.normal_f32(V * N, 43 + V, "lmtiles", 0.02))
     nbytes = int(dev.L.e4b_q6k_packed_bytes(N, V))
@@ -62,12 +64,16 @@ def test_lmhead_tiles(e4b, dev, V, N, n):
     assert np.array_equal(dev.read(wt, np.uint8, nbytes), _pack_tiles_ref(w, V, N))
     x = np.random.default_rng(44).standard_normal((n, N)).astype(np.float32)
     bx, y, y2, scr = dev.upload(x), dev.alloc(n * V * 4), dev.alloc(n * V * 4), dev.alloc(2 * 64 * N * 2)
-    dev.call("e4b_q6k_lmhead_tiles", wt.ptr, bx.ptr, scr.ptr, y.ptr, N, V, np.float32(30.0), n)
-    dev.call("e4b_q6k_lmhead_rows", bw.ptr, bx.ptr, scr.ptr, y2.ptr, N, V, np.float32(30.0), n)
-    dev.sync()
+    dev.call("e4b_set_option", b"lmhead_tiles_tc", tc)
+    try:
+        dev.call("e4b_q6k_lmhead_tiles", wt.ptr, bx.ptr, scr.ptr, y.ptr, N, V, np.float32(30.0), n)
+        dev.call("e4b_q6k_lmhead_rows", bw.ptr, bx.ptr, scr.ptr, y2.ptr, N, V, np.float32(30.0), n)
+        dev.sync()
+    finally:
+        dev.call("e4b_set_option", b"lmhead_tiles_tc", 0)
     assert dev.status() == 0
     got = dev.read(y, np.float32, n * V).reshape(n, V)
-    if n > 1:
+    if n > 1 and tc == 1:
         assert np.array_equal(got, dev.read(y2, np.float32, n * V).reshape(n, V))
     for r in range(n):
         ref = O.softcap(O.q6k_matvec(w, x[r], V, N), 30.0)
