@@ -22,7 +22,8 @@
 //               threads fetch their rows' 224-byte covers with cp.async instead.
 //
 // Measured on B200 (A4B 262144 x 2816, n = 64): 500 us on the packed layout,
-// 525 us row-major (the mma.sync kernel: 965 us).  The time barely depends on
+// 525 us row-major (the mma.sync kernel: 965 us).  For 1..32 rows the packed
+// copy goes to the warp-MMA kernels below instead (k_q6gv, k_q6gm).  The time barely depends on
 // n: dequantisation, the per-K-step MMA issue and the hand-offs between the
 // warp roles bound it, not HBM (605 MB would stream in ~93 us).
 //
