@@ -104,12 +104,12 @@ class Engine:
         if fused and not fused_supported(self.cfg):
             raise ValueError(f"model {self.cfg.name!r} has shapes the fused token kernel does not take")
         self.fused = bool(fused)
+        self.emb_tiles = None                # tile-packed LM head table (the batched engine makes its own)
         self._load_weights()
         self._alloc_activations()
         self.dense_plan = self._create_dense_plan() if self.fused else None
         # the fused path's LM head streams a tile-packed copy of the q6_K table
         # (one contiguous bulk copy per 16 rows x superblock; the warp-MMA GEMV)
-        self.emb_tiles = None
         if self.fused:
             H, V = self.cfg.hidden, self.cfg.vocab
             self.emb_tiles = self.dev.alloc(int(self.dev.L.e4b_q6k_packed_bytes(H, V)), "lmHeadTiles")
