@@ -859,6 +859,7 @@ def run_lmhead(e4b, dev, args):
     del raw
     wt = dev.alloc(int(dev.L.e4b_q6k_packed_bytes(H, V)), "lm_wt")
     dev.call("e4b_q6k_pack_tiles", w, wt, H, V)
+    dev.sync()           # the packing is not part of any timed launch
     hbm, kind_h = peaks()
     out = []
     for n in args.rows:
