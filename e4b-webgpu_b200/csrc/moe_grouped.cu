@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
           const uint8_t* a = stages + s * stage_bytes + (size_t)g * p.rowbytes;
           const uint8_t* b = a + 8 * (size_t)p.rowbytes;
           const uint16_t* xq = xr0;
-#pragma unroll 1
+#pragma unroll 2
           for (int k = 0; k < p.nb; k += 2) {
             qmm_block<NS, TWO, 0>(a, b, 0, xq, xstep, two, L, acc);
             qmm_block<NS, TWO, 1>(a + 18, b + 18, 0, xq + 32, xstep, two, L, acc);
