@@ -1,6 +1,8 @@
 // RMSNorm family and element-wise GeGLU / PLE products.  One CTA per row for the
 // reductions (rows = batch tokens); f32 math, f16 stores where the reference
 // stores f16.
+#include <initializer_list>
+
 #include "common.cuh"
 
 namespace {
@@ -170,6 +172,169 @@ __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict_
   }
 }
 
+// ---- float4 forms of rmsacc3 / a4btail: one float4 column per thread
+// (dim % 4 == 0, dim <= 4 * blockDim, 16-byte aligned rows).  Every global
+// load is issued before the first reduction and the row stays in registers
+// between the reductions, so a CTA waits on memory once instead of once per
+// strided element.  Per element the arithmetic is the scalar kernels'; the
+// sums of squares add each thread's four elements first.
+E4B_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+E4B_DEV void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+E4B_DEV float sq4(float4 v) { return fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, v.x * v.x))); }
+// p[0] + p[stride4] + ... in that order, per component (sum_parts on float4s)
+E4B_DEV float4 sum_parts4(const float4* __restrict__ p, size_t stride4, int n) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = 0; k0 < n; k0 += 8) {
+    float4 x[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) x[k] = k0 + k < n ? p[(size_t)(k0 + k) * stride4] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      if (k0 + k >= n) break;
+      if (k0 + k == 0) {
+        v = x[k];
+      } else {
+        v.x += x[k].x;
+        v.y += x[k].y;
+        v.z += x[k].z;
+        v.w += x[k].w;
+      }
+    }
+  }
+  return v;
+}
+// Two block sums with one pair of barriers (sh >= 64 floats); each adds the
+// warp results in warp order, as block_sum does.
+E4B_DEV float2 block_sum2(float a, float b, float* sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  __syncthreads();
+  if (lane == 0) {
+    sh[wid] = a;
+    sh[32 + wid] = b;
+  }
+  __syncthreads();
+  float ta = 0.f, tb = 0.f;
+  for (int i = 0; i < nw; i++) {
+    ta += sh[i];
+    tb += sh[32 + i];
+  }
+  return make_float2(ta, tb);
+}
+// four f16 values of elements i..i+3 (fragment order: scattered positions)
+E4B_DEV void st_h4(uint16_t* __restrict__ y, size_t ob, int i, int xfo, float a, float b, float c, float d) {
+  if (xfo) {
+    y[ob + xfo_pos(i)] = f2h(a);
+    y[ob + xfo_pos(i + 1)] = f2h(b);
+    y[ob + xfo_pos(i + 2)] = f2h(c);
+    y[ob + xfo_pos(i + 3)] = f2h(d);
+  } else {
+    *reinterpret_cast<uint2*>(y + ob + i) = make_uint2((uint32_t)f2h(a) | ((uint32_t)f2h(b) << 16),
+                                                       (uint32_t)f2h(c) | ((uint32_t)f2h(d) << 16));
+  }
+}
+
+__global__ void __launch_bounds__(1024, 1)
+    k_rmsacc3v(const float* __restrict__ t, const float* __restrict__ w_acc, const float* __restrict__ w1,
+               const float* __restrict__ w2, const float* __restrict__ w3, const float* __restrict__ h_in,
+               uint16_t* __restrict__ y1, float* __restrict__ y2, uint16_t* __restrict__ y3, float* __restrict__ h_out,
+               int dim, float eps, int xfo, int nparts, size_t part_stride) {
+  __shared__ float sh[64];
+  const int i = 4 * (int)threadIdx.x;
+  const bool on = i < dim;
+  const size_t ob = (size_t)blockIdx.x * dim;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  // the norm vectors do not depend on the previous kernel
+  const float4 wa = on ? ld4(w_acc + i) : z, a1 = on ? ld4(w1 + i) : z, a2 = on ? ld4(w2 + i) : z,
+               a3 = on ? ld4(w3 + i) : z;
+  pdl_wait();
+  float4 tv = z, hv = z;
+  if (on) {
+    tv = sum_parts4(reinterpret_cast<const float4*>(t + ob + i), part_stride / 4, nparts);
+    hv = ld4(h_in + ob + i);
+  }
+  const float inv1 = rms_scale(block_sum(on ? sq4(tv) : 0.f, sh), dim, eps);
+  float4 h;
+  h.x = hv.x + tv.x * inv1 * wa.x;
+  h.y = hv.y + tv.y * inv1 * wa.y;
+  h.z = hv.z + tv.z * inv1 * wa.z;
+  h.w = hv.w + tv.w * inv1 * wa.w;
+  if (on) st4(h_out + ob + i, h);
+  const float inv2 = rms_scale(block_sum(on ? sq4(h) : 0.f, sh), dim, eps);
+  if (!on) return;
+  const float4 v = make_float4(h.x * inv2, h.y * inv2, h.z * inv2, h.w * inv2);
+  st_h4(y1, ob, i, xfo, v.x * a1.x, v.y * a1.y, v.z * a1.z, v.w * a1.w);
+  st4(y2 + ob + i, make_float4(v.x * a2.x, v.y * a2.y, v.z * a2.z, v.w * a2.w));
+  st_h4(y3, ob, i, xfo, v.x * a3.x, v.y * a3.y, v.z * a3.z, v.w * a3.w);
+}
+
+__global__ void __launch_bounds__(1024, 1)
+    k_a4btailv(const float* __restrict__ t1, const float* __restrict__ w1, const float* __restrict__ m,
+               const float* __restrict__ w2, const float* __restrict__ wp, const float* __restrict__ h_in,
+               const float* __restrict__ w_next, uint16_t* __restrict__ y_next, float* __restrict__ h_out, int H,
+               float eps, float mul, int next, int xfo, const float* __restrict__ y, const uint32_t* __restrict__ inv,
+               const float* __restrict__ tkw, int K) {
+  __shared__ float sh[64];
+  const int i = 4 * (int)threadIdx.x;
+  const bool on = i < H;
+  const size_t ob = (size_t)blockIdx.x * H;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 a1 = on ? ld4(w1 + i) : z, a2 = on ? ld4(w2 + i) : z, ap = on ? ld4(wp + i) : z,
+               an = on && next ? ld4(w_next + i) : z;
+  pdl_wait();
+  float4 tv = z, hv = z, mv = z;
+  if (on) {
+    tv = ld4(t1 + ob + i);
+    hv = ld4(h_in + ob + i);
+    if (y) {
+      // the slots' rows loaded eight at a time, then added in slot order
+      // (0xffffffff: a dropped entry)
+      for (int k0 = 0; k0 < K; k0 += 8) {
+        float4 yv[8];
+        uint32_t r[8];
+        float wk[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          r[k] = k0 + k < K ? __ldg(inv + (size_t)blockIdx.x * K + k0 + k) : 0xffffffffu;
+          wk[k] = k0 + k < K ? __ldg(tkw + (size_t)blockIdx.x * K + k0 + k) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) yv[k] = r[k] != 0xffffffffu ? ld4(y + (size_t)r[k] * H + i) : z;
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+          if (r[k] != 0xffffffffu) {
+            mv.x += wk[k] * yv[k].x;
+            mv.y += wk[k] * yv[k].y;
+            mv.z += wk[k] * yv[k].z;
+            mv.w += wk[k] * yv[k].w;
+          }
+      }
+    } else {
+      mv = ld4(m + ob + i);
+    }
+  }
+  const float2 s12 = block_sum2(on ? sq4(tv) : 0.f, on ? sq4(mv) : 0.f, sh);
+  const float inv1 = rms_scale(s12.x, H, eps), inv2 = rms_scale(s12.y, H, eps);
+  float4 cc;
+  cc.x = tv.x * inv1 * a1.x + mv.x * inv2 * a2.x;
+  cc.y = tv.y * inv1 * a1.y + mv.y * inv2 * a2.y;
+  cc.z = tv.z * inv1 * a1.z + mv.z * inv2 * a2.z;
+  cc.w = tv.w * inv1 * a1.w + mv.w * inv2 * a2.w;
+  const float inv3 = rms_scale(block_sum(on ? sq4(cc) : 0.f, sh), H, eps);
+  float4 hn;
+  hn.x = (hv.x + cc.x * inv3 * ap.x) * mul;
+  hn.y = (hv.y + cc.y * inv3 * ap.y) * mul;
+  hn.z = (hv.z + cc.z * inv3 * ap.z) * mul;
+  hn.w = (hv.w + cc.w * inv3 * ap.w) * mul;
+  if (on) st4(h_out + ob + i, hn);
+  if (next) {
+    const float inv4 = rms_scale(block_sum(on ? sq4(hn) : 0.f, sh), H, eps);
+    if (on)
+      st_h4(y_next, ob, i, xfo, hn.x * inv4 * an.x, hn.y * inv4 * an.y, hn.z * inv4 * an.z, hn.w * inv4 * an.w);
+  }
+}
+
 __global__ void k_geglumul(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y, int N) {
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -235,6 +400,19 @@ E4B_API int e4b_rmsaccn(e4b_ctx* c, const float* t, const float* w1, float* hidd
   return e4b_launch(c, "rmsaccn", k_rmsaccn, dim3(1), dim3(256), sm, t, w1, hidden, w2, yh, dim, eps, mul, norm2);
 }
 
+// The float4 kernels apply: width a multiple of 4 within one float4 per thread
+// of a 1024-thread CTA, f32 rows 16-byte aligned, f16 rows 8-byte aligned
+// (their stores are scattered in fragment order).
+static bool vec4_ok(int dim, std::initializer_list<const void*> f32, std::initializer_list<const void*> f16, int xfo) {
+  if (dim % 4 != 0 || dim > 4 * 1024) return false;
+  for (const void* p : f32)
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
+  if (!xfo)
+    for (const void* p : f16)
+      if (reinterpret_cast<uintptr_t>(p) % 8 != 0) return false;
+  return true;
+}
+
 E4B_API int e4b_rmsacc3(e4b_ctx* c, const float* t, const float* w_acc, const float* w1, const float* w2,
                         const float* w3, const float* h_in, uint16_t* y1, float* y2, uint16_t* y3, float* h_out,
                         int dim, float eps, int rows, int xfo, int nparts) {
@@ -243,6 +421,9 @@ E4B_API int e4b_rmsacc3(e4b_ctx* c, const float* t, const float* w_acc, const fl
   E4B_REQUIRE(c, !xfo || dim % 32 == 0, "rmsacc3: fragment order needs dim %% 32 == 0");
   E4B_REQUIRE(c, nparts >= 1, "rmsacc3: nparts=%d", nparts);
   if (rows < 1) rows = 1;
+  if (vec4_ok(dim, {t, w_acc, w1, w2, w3, h_in, y2, h_out}, {y1, y3}, xfo))
+    return e4b_launch(c, "rmsacc3", k_rmsacc3v, dim3(rows), dim3(1024), 0, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
+                      h_out, dim, eps, xfo, nparts, (size_t)rows * dim);
   const size_t sm = (size_t)dim * 8;
   if (int r = set_smem(c, (const void*)k_rmsacc3, sm)) return r;
   return e4b_launch(c, "rmsacc3", k_rmsacc3, dim3(rows), dim3(1024), sm, t, w_acc, w1, w2, w3, h_in, y1, y2, y3,
@@ -257,6 +438,10 @@ E4B_API int e4b_a4btail(e4b_ctx* c, const float* t1, const float* w1, const floa
   E4B_REQUIRE(c, !next || (w_next && y_next), "a4btail: next=1 needs w_next and y_next");
   E4B_REQUIRE(c, !xfo || H % 32 == 0, "a4btail: fragment order needs H %% 32 == 0");
   if (rows < 1) rows = 1;
+  if (vec4_ok(H, {t1, w1, m, w2, wp, h_in, next ? w_next : nullptr, h_out}, {next ? y_next : nullptr}, xfo))
+    return e4b_launch(c, "a4btail", k_a4btailv, dim3(rows), dim3(1024), 0, t1, w1, m, w2, wp, h_in, w_next, y_next,
+                      h_out, H, eps, mul, next, xfo, (const float*)nullptr, (const uint32_t*)nullptr,
+                      (const float*)nullptr, 0);
   const size_t sm = (size_t)H * 12;
   if (int r = set_smem(c, (const void*)k_a4btail, sm)) return r;
   return e4b_launch(c, "a4btail", k_a4btail, dim3(rows), dim3(1024), sm, t1, w1, m, w2, wp, h_in, w_next, y_next,
@@ -273,6 +458,9 @@ E4B_API int e4b_a4btail_wacc(e4b_ctx* c, const float* t1, const float* w1, const
               "a4btail_wacc: bad args (K <= 32)");
   E4B_REQUIRE(c, !next || (w_next && y_next), "a4btail_wacc: next=1 needs w_next and y_next");
   E4B_REQUIRE(c, !xfo || H % 32 == 0, "a4btail_wacc: fragment order needs H %% 32 == 0");
+  if (vec4_ok(H, {t1, w1, y, w2, wp, h_in, next ? w_next : nullptr, h_out}, {next ? y_next : nullptr}, xfo))
+    return e4b_launch(c, "a4btail_wacc", k_a4btailv, dim3(rows), dim3(1024), 0, t1, w1, (const float*)nullptr, w2,
+                      wp, h_in, w_next, y_next, h_out, H, eps, mul, next, xfo, y, inv, topk_w, K);
   const size_t sm = (size_t)H * 12;
   if (int r = set_smem(c, (const void*)k_a4btail, sm)) return r;
   return e4b_launch(c, "a4btail_wacc", k_a4btail, dim3(rows), dim3(1024), sm, t1, w1, (const float*)nullptr, w2, wp,
