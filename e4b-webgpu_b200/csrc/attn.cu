@@ -34,11 +34,21 @@ __global__ void k_headprep(const float* __restrict__ qkv, const float* __restric
   if (keqv && head >= QH + KVH) src = head - KVH;  // v reads the k slice
   const size_t qkvS = (size_t)(QH + KVH * (2 - keqv)) * HD;
   const size_t base = (size_t)b * qkvS + (size_t)src * HD;
-  float s = 0.f;
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    const float v = sum_parts(qkv + base + d, part_stride, nparts);
-    xv[d] = v;
-    s = fmaf(v, v, s);
+  // up to four elements per thread (HD <= 4 * blockDim), all their partial
+  // loads in flight together
+  float s = 0.f, v4[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int d = threadIdx.x + j * blockDim.x;
+    v4[j] = d < HD ? sum_parts(qkv + base + d, part_stride, nparts) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int d = threadIdx.x + j * blockDim.x;
+    if (d < HD) {
+      xv[d] = v4[j];
+      s = fmaf(v4[j], v4[j], s);
+    }
   }
   const float inv = rms_scale(block_sum(s, sh), HD, eps);
   const int half = HD / 2;

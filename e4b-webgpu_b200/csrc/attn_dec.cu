@@ -423,22 +423,31 @@ __global__ void k_attcomb_dec(const AttP p, uint16_t* __restrict__ out_h, int xf
     if (ml[2 * c + 1] > 0.f) den += ml[2 * c + 1] * wc[c];
   uint16_t* out = out_h + (size_t)b * p.QH * p.HD;
   const float* po = p.part_o + row * p.max_chunks * p.HD;
-  for (int d = threadIdx.x; d < p.HD; d += blockDim.x) {
-    float acc = 0.f;
-    int c = c_lo;
-    for (; c + 8 <= nch; c += 8) {
-      float o[8];
+  // four dims per thread (HD % 4 == 0), sixteen chunks' loads in flight
+  for (int d = 4 * (int)threadIdx.x; d < p.HD; d += 4 * (int)blockDim.x) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int c = c_lo; c < nch; c += 16) {
+      float4 o[16];
 #pragma unroll
-      for (int u = 0; u < 8; u++) o[u] = wc[c + u] != 0.f ? po[(size_t)(c + u) * p.HD + d] : 0.f;
+      for (int u = 0; u < 16; u++)
+        o[u] = c + u < nch && wc[c + u] != 0.f ? *reinterpret_cast<const float4*>(po + (size_t)(c + u) * p.HD + d)
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int u = 0; u < 8; u++)
-        if (wc[c + u] != 0.f) acc = fmaf(o[u], wc[c + u], acc);
+      for (int u = 0; u < 16; u++)
+        if (c + u < nch && wc[c + u] != 0.f) {
+          const float w = wc[c + u];
+          a0 = fmaf(o[u].x, w, a0);
+          a1 = fmaf(o[u].y, w, a1);
+          a2 = fmaf(o[u].z, w, a2);
+          a3 = fmaf(o[u].w, w, a3);
+        }
     }
-    for (; c < nch; c++)
-      if (wc[c] != 0.f) acc = fmaf(po[(size_t)c * p.HD + d], wc[c], acc);
-    const float v = den > 0.f ? acc / den : 0.f;
-    const int i = h * p.HD + d;
-    out[xfo ? xfo_pos(i) : i] = f2h(v);
+    const float r[4] = {a0, a1, a2, a3};
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int i = h * p.HD + d + e;
+      out[xfo ? xfo_pos(i) : i] = f2h(den > 0.f ? r[e] / den : 0.f);
+    }
   }
 }
 
@@ -810,7 +819,9 @@ E4B_API int e4b_attdec_seq(e4b_ctx* c, const float* q, const uint16_t* kcache, c
   const int cap = c->attn_grid_cap > 0 ? c->attn_grid_cap : c->sm_count;
   const int grid = (int)(most < cap ? most : cap);
   if (int r = e4b_launch(c, "attdec", k_attdec, dim3(grid), dim3(32 * kAW * kAG), smem, p, kmap, vmap)) return r;
-  return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(128), (size_t)max_chunks * 4, p, out_h,
+  // one thread per four dims of a head
+  const int comb_threads = std::max(32, (HD / 4 + 31) / 32 * 32);
+  return e4b_launch(c, "attcomb_dec", k_attcomb_dec, dim3(QH, nseq), dim3(comb_threads), (size_t)max_chunks * 4, p, out_h,
                     xfo);
 }
 
