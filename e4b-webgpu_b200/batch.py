@@ -68,6 +68,13 @@ def nccl_unique_id(dev) -> bytes:
     return bytes(buf)
 
 
+def argmax_parts(rows: int) -> int:
+    """Stage-0 partials per row of e4b_argmax_rows: about 4096 CTAs in all, so
+    a batch's rows give each CTA a few thousand logits (at most ARGMAX_PARTS
+    per row, the size of the partial buffers)."""
+    return max(1, min(ARGMAX_PARTS, 4096 // max(1, rows)))
+
+
 def to_xfo(x: np.ndarray) -> np.ndarray:
     """Rows of x (last axis) permuted into fragment order."""
     out = np.empty_like(x)
@@ -154,6 +161,11 @@ class BatchEngine(Engine):
         A.offsets = d.alloc((E + 1) * 4, "expOffsets")
         A.entries = d.alloc(B * K * 4, "expEntries")
         A.inv = d.alloc(B * K * 4, "expInv")
+        # a second expert grouping: under benchmark routing the next layer's
+        # grouping is formed on the side stream while this layer uses the other
+        A.offsets1 = d.alloc((E + 1) * 4, "expOffsets1")
+        A.entries1 = d.alloc(B * K * 4, "expEntries1")
+        A.inv1 = d.alloc(B * K * 4, "expInv1")
         A.gl = d.alloc(B * K * EF * 2, "expGeglu")
         A.yo = d.alloc(B * K * H * 4, "expOut")
         A.moe_out = d.alloc(B * H * 4, "moeOut")
@@ -391,22 +403,33 @@ class BatchEngine(Engine):
         c, d, A, B = self.cfg, self.dev, self.A, self.nseq
         H, E, K, EF, FF = c.hidden, c.experts, c.topk, c.expert_ff, c.ff
         side = self.overlap_route
+        grp = [(A.offsets, A.entries, A.inv), (A.offsets1, A.entries1, A.inv1)]
+        # expert grouping of this layer (groupings alternate by layer parity): the
+        # first layer's on the main stream, later ones were formed on the previous
+        # layer's side stream, whose join precedes this layer
+        early = side and self.ep is None
+        offs, ents, inv = grp[L.i % 2]
+        if self.ep is None and (L.i == 0 or not early):
+            d.call("e4b_expgroup", topk_idx, B, K, E, offs, ents, inv)
         if side:
             d.call("e4b_side_begin")
         d.call("e4b_routertop", A.router_in, L.wr, L.pes, A.topk_idx, A.topk_w, H, E, K, B)
+        if early and L.i + 1 < c.layers:
+            # the next layer's Zipf routes are known: group them now, into the
+            # grouping the previous layer used (its kernels precede the fork)
+            nidx = ctypes.c_void_p(A.ztop_idx.ptr + (L.i + 1) * B * K * 4)
+            d.call("e4b_expgroup", nidx, B, K, E, *grp[(L.i + 1) % 2])
         if side:
             d.call("e4b_side_end")
         if self.ep is not None:
             if self.ep_overlap:
                 self._moe_ep_send(topk_idx)       # the rows travel while the dense FFN runs
-        else:
-            d.call("e4b_expgroup", topk_idx, B, K, E, A.offsets, A.entries, A.inv)
         d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
         d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
         if self.ep is None:
-            d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
-            d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
-            y_rows, y_map = A.yo, A.inv
+            d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, offs, ents, A.gl, H, EF, E, K)
+            d.call("e4b_q40downgrp", A.gl, L.down_exps, offs, ents, A.yo, EF, H, E)
+            y_rows, y_map = A.yo, inv
         else:
             if not self.ep_overlap:
                 self._moe_ep_send(topk_idx)
@@ -485,12 +508,12 @@ class BatchEngine(Engine):
             Bt = N * B
             d.call("e4b_ep_allgather", A.xf, A.xf_all, ctypes.c_size_t(B * H * 4))
             self._lm_head(self.emb_shard, self.emb_shard_tiles, A.xf_all, A.xsplit_all, A.logits_s, self.vs, Bt)
-            d.call("e4b_argmax_rows", A.logits_s, A.amax_part_s, A.amax_s, self.vs, ARGMAX_PARTS, Bt)
+            d.call("e4b_argmax_rows", A.logits_s, A.amax_part_s, A.amax_s, self.vs, argmax_parts(Bt), Bt)
             d.call("e4b_ep_allgather", A.amax_s, A.amax_all, ctypes.c_size_t(Bt * 8))
             d.call("e4b_argmax_merge", A.amax_all, N, Bt, self.vs, rank * B, B, A.amax)
         else:
             self._lm_head(self.emb, self.emb_tiles, A.xf, A.xsplit, A.logits, V, B)
-            d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
+            d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, argmax_parts(B), B)
         d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
 
     # ------------------------------------------------------------ host API
@@ -615,7 +638,7 @@ class BatchEngine(Engine):
         d.write(A.params, self.host_params)
         d.call("e4b_rmsnorm", last, self.out_norm, A.xf, None, None, H, B, eps, 1, 0, 0)
         self._lm_head(self.emb, self.emb_tiles, A.xf, A.xsplit, A.logits, V, B)
-        d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, ARGMAX_PARTS, B)
+        d.call("e4b_argmax_rows", A.logits, A.amax_part, A.amax, V, argmax_parts(B), B)
         d.call("e4b_feedtok_rows", A.amax, A.params, A.ring, RING_CAP, A.tok, B)
         self.check_status("prefill (last position)")
 

@@ -335,6 +335,32 @@ __global__ void __launch_bounds__(1024, 1)
   }
 }
 
+// k_rmsnorm on float4 columns (the float4 kernels' conditions; one pass over x).
+__global__ void __launch_bounds__(1024, 1)
+    k_rmsnormv(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
+               float* __restrict__ sums, uint16_t* __restrict__ yh, int dim, float eps, int with_scale, int sumout,
+               int f16out) {
+  __shared__ float sh[64];
+  const int i = 4 * (int)threadIdx.x;
+  const bool on = i < dim;
+  const size_t ob = (size_t)blockIdx.x * dim;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 wv = on && with_scale ? ld4(w + i) : z;
+  pdl_wait();
+  const float4 xv = on ? ld4(x + ob + i) : z;
+  const float inv = rms_scale(block_sum(on ? sq4(xv) : 0.f, sh), dim, eps);
+  float4 v = make_float4(xv.x * inv, xv.y * inv, xv.z * inv, xv.w * inv);
+  if (with_scale) v = make_float4(v.x * wv.x, v.y * wv.y, v.z * wv.z, v.w * wv.w);
+  if (on) {
+    if (f16out) st_h4(yh, ob, i, f16out == 2, v.x, v.y, v.z, v.w);
+    else st4(y + ob + i, v);
+  }
+  if (sumout) {
+    const float t = block_sum(on ? ((v.x + v.y) + v.z) + v.w : 0.f, sh);
+    if (threadIdx.x == 0) sums[blockIdx.x] = t;
+  }
+}
+
 __global__ void k_geglumul(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y, int N) {
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -373,6 +399,19 @@ int set_smem(e4b_ctx* c, const void* k, size_t bytes) {
 
 extern "C" {
 
+// The float4 kernels apply: width a multiple of 4 within one float4 per thread
+// of a 1024-thread CTA, f32 rows 16-byte aligned, f16 rows 8-byte aligned
+// (their stores are scattered in fragment order).
+static bool vec4_ok(int dim, std::initializer_list<const void*> f32, std::initializer_list<const void*> f16, int xfo) {
+  if (dim % 4 != 0 || dim > 4 * 1024) return false;
+  for (const void* p : f32)
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
+  if (!xfo)
+    for (const void* p : f16)
+      if (reinterpret_cast<uintptr_t>(p) % 8 != 0) return false;
+  return true;
+}
+
 E4B_API int e4b_rmsnorm(e4b_ctx* c, const float* x, const float* w, float* y, float* sums, uint16_t* yh, int dim,
                         int rows, float eps, int with_scale, int sumout, int f16out) {
   E4B_CHECK_CTX(c);
@@ -381,6 +420,9 @@ E4B_API int e4b_rmsnorm(e4b_ctx* c, const float* x, const float* w, float* y, fl
   E4B_REQUIRE(c, !with_scale || w, "rmsnorm: missing weight");
   E4B_REQUIRE(c, !sumout || sums, "rmsnorm: missing sums");
   E4B_REQUIRE(c, f16out >= 0 && f16out <= 2 && (f16out != 2 || dim % 32 == 0), "rmsnorm: bad f16out=%d", f16out);
+  if (vec4_ok(dim, {x, with_scale ? w : nullptr, f16out ? nullptr : y}, {f16out ? yh : nullptr}, f16out == 2))
+    return e4b_launch(c, "rmsnorm", k_rmsnormv, dim3(rows), dim3(1024), 0, x, w, y, sums, yh, dim, eps, with_scale,
+                      sumout, f16out);
   return e4b_launch(c, "rmsnorm", k_rmsnorm, dim3(rows), dim3(256), 0, x, w, y, sums, yh, dim, eps, with_scale,
                     sumout, f16out);
 }
@@ -400,18 +442,6 @@ E4B_API int e4b_rmsaccn(e4b_ctx* c, const float* t, const float* w1, float* hidd
   return e4b_launch(c, "rmsaccn", k_rmsaccn, dim3(1), dim3(256), sm, t, w1, hidden, w2, yh, dim, eps, mul, norm2);
 }
 
-// The float4 kernels apply: width a multiple of 4 within one float4 per thread
-// of a 1024-thread CTA, f32 rows 16-byte aligned, f16 rows 8-byte aligned
-// (their stores are scattered in fragment order).
-static bool vec4_ok(int dim, std::initializer_list<const void*> f32, std::initializer_list<const void*> f16, int xfo) {
-  if (dim % 4 != 0 || dim > 4 * 1024) return false;
-  for (const void* p : f32)
-    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
-  if (!xfo)
-    for (const void* p : f16)
-      if (reinterpret_cast<uintptr_t>(p) % 8 != 0) return false;
-  return true;
-}
 
 E4B_API int e4b_rmsacc3(e4b_ctx* c, const float* t, const float* w_acc, const float* w1, const float* w2,
                         const float* w3, const float* h_in, uint16_t* y1, float* y2, uint16_t* y3, float* h_out,

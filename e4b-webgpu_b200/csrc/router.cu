@@ -341,7 +341,22 @@ __global__ void k_argmax0(const float* __restrict__ x, uint32_t* __restrict__ pa
   const int lo = blockIdx.x * per, hi = min(lo + per, N);
   float bv = -3.0e38f;
   uint32_t bi = 0xffffffffu;
-  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) argmax_merge(bv, bi, x[i], (uint32_t)i);
+  if ((N & 3) == 0 && (per & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    // float4 loads, four in flight per thread (the merge is order-independent:
+    // larger value first, then lower index)
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 4
+    for (int i4 = lo / 4 + (int)threadIdx.x; i4 < hi / 4; i4 += blockDim.x) {
+      const float4 v = x4[i4];
+      const uint32_t i = 4u * (uint32_t)i4;
+      argmax_merge(bv, bi, v.x, i);
+      argmax_merge(bv, bi, v.y, i + 1);
+      argmax_merge(bv, bi, v.z, i + 2);
+      argmax_merge(bv, bi, v.w, i + 3);
+    }
+  } else {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) argmax_merge(bv, bi, x[i], (uint32_t)i);
+  }
   block_argmax(bv, bi);
   if (threadIdx.x == 0) {
     part[2 * blockIdx.x] = bi;
