@@ -178,6 +178,13 @@ class BatchEngine(Engine):
         # the LM head streams a tile-packed copy of the (tied) q6_K embedding: one
         # contiguous TMA copy per 128 rows x superblock (e4b_q6k_lmhead_tiles)
         self.emb_tiles = self._pack_lm_head(self.emb, c.vocab) if B <= 64 else None
+        # tile-packed copies of the experts' gate|up weights, the largest weight
+        # stream of a step (e4b_q40gugrp_tiles reads them with aligned 16-byte loads)
+        self.gu_tiles = H % 256 == 0 and (2 * EF) % 16 == 0
+        if self.gu_tiles:
+            for L in self.layers:
+                L.gu_exps_t = d.alloc(E * 2 * EF * (H // 32) * 18, "guExpsTiles")
+                d.call("e4b_q40_pack_tiles", L.gu_exps, L.gu_exps_t, E * 2 * EF, H)
         self.emb_shard_tiles = None
         self.zipf_all = bool(self.zipf)
         if self.zipf_all:
@@ -228,7 +235,7 @@ class BatchEngine(Engine):
         per_gu = 2 * EF * (H // 32) * 18
         per_dn = H * (EF // 32) * 18
         for L in self.layers:
-            L.gu_loc = ctypes.c_void_p(L.gu_exps.ptr + rank * self.e_loc * per_gu)
+            L.gu_loc = ctypes.c_void_p((L.gu_exps_t if self.gu_tiles else L.gu_exps).ptr + rank * self.e_loc * per_gu)
             L.dn_loc = ctypes.c_void_p(L.down_exps.ptr + rank * self.e_loc * per_dn)
         # vocabulary-sharded LM head: this rank's V/N rows for every rank's tokens
         V = c.vocab
@@ -245,6 +252,16 @@ class BatchEngine(Engine):
             self.emb_shard = ctypes.c_void_p(self.emb.ptr + rank * Vs * (H // 256) * 210)
             if Bt <= 64:
                 self.emb_shard_tiles = self._pack_lm_head(self.emb_shard, Vs)
+
+    def _gugrp(self, L, offsets, entries):
+        """The experts' gate|up + GeGLU over this layer's expert grouping."""
+        c, A = self.cfg, self.A
+        if self.gu_tiles:
+            self.dev.call("e4b_q40gugrp_tiles", A.moe_in, L.gu_exps_t, offsets, entries, A.gl, c.hidden, c.expert_ff,
+                          c.experts, c.topk)
+        else:
+            self.dev.call("e4b_q40gugrp", A.moe_in, L.gu_exps, offsets, entries, A.gl, c.hidden, c.expert_ff,
+                          c.experts, c.topk)
 
     def _pack_lm_head(self, w, rows):
         d, H = self.dev, self.cfg.hidden
@@ -354,7 +371,8 @@ class BatchEngine(Engine):
         else:
             self._timed("e4b_ep_join")
         d.call("e4b_expgroup", A.ep_rid, rows, 1, self.e_loc, A.ep_off, A.ep_ent, A.ep_inv)
-        d.call("e4b_q40gugrp", A.ep_rx, L.gu_loc, A.ep_off, A.ep_ent, A.ep_gl, H, EF, self.e_loc, 1)
+        d.call("e4b_q40gugrp_tiles" if self.gu_tiles else "e4b_q40gugrp", A.ep_rx, L.gu_loc, A.ep_off, A.ep_ent,
+               A.ep_gl, H, EF, self.e_loc, 1)
         d.call("e4b_q40downgrp", A.ep_gl, L.dn_loc, A.ep_off, A.ep_ent, A.ep_y, EF, H, self.e_loc)
         if p2p:
             d.call("e4b_ep_push_back", A.ep_rid, A.ep_inv, A.ep_y, H, N, rank, self.cap, A.ep_tab[2], A.ep_tab[4],
@@ -427,7 +445,7 @@ class BatchEngine(Engine):
         d.call("e4b_q40gumm", A.normed, L.gu, A.geglu, H, FF, B)
         d.call("e4b_q40mm", A.geglu, L.down, A.tmp, FF, H, B)
         if self.ep is None:
-            d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, offs, ents, A.gl, H, EF, E, K)
+            self._gugrp(L, offs, ents)
             d.call("e4b_q40downgrp", A.gl, L.down_exps, offs, ents, A.yo, EF, H, E)
             y_rows, y_map = A.yo, inv
         else:
@@ -493,7 +511,7 @@ class BatchEngine(Engine):
                     d.call("e4b_join")
                 else:
                     d.call("e4b_expgroup", A.topk_idx, B, K, E, A.offsets, A.entries, A.inv)
-                d.call("e4b_q40gugrp", A.moe_in, L.gu_exps, A.offsets, A.entries, A.gl, H, EF, E, K)
+                self._gugrp(L, A.offsets, A.entries)
                 d.call("e4b_q40downgrp", A.gl, L.down_exps, A.offsets, A.entries, A.yo, EF, H, E)
                 y_rows, y_map = A.yo, A.inv
             else:

@@ -176,6 +176,103 @@ E4B_DEV uint4 lds128(const uint16_t* p) {
   return v;
 }
 
+// ---- tile-packed q4_0 (IN % 256 == 0): per 16-row group and 256-k quantum one
+// 2304-byte piece, [16 rows][8 blocks] f16 scales (256 B) then the nibble words
+// as [k half][row][lane t] uint4 (2048 B): word j of (h, r, t) is the 32-bit
+// A-operand source lane t of row r uses for block 4h + j (nib_odd / nib_even of
+// the GGUF block).  A warp reads a row's 8 scales and 4 blocks' nibble words
+// with one 16-byte load each, conflict-free; the decoded A registers equal the
+// row-major path's, so results are bit-identical.
+constexpr int kPkSub = 2304;
+E4B_DEV uint4 lds128b(const uint8_t* p) { return lds128(reinterpret_cast<const uint16_t*>(p)); }
+E4B_DEV uint32_t u32w(const uint4& v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
+E4B_DEV float half_of(const uint4& v, int k) {
+  const uint32_t w = u32w(v, k >> 1);
+  return h2f((uint16_t)((k & 1) ? w >> 16 : w & 0xFFFFu));
+}
+// One quantum of the gate|up tile from a packed stage (two 16-row pieces).
+template <int TWO>
+E4B_DEV void qmm_quantum_pk(const uint8_t* st, int g, int t, const uint16_t* xq, int xstep, bool two,
+                            float (&acc)[2][2][4]) {
+  uint4 S[2][2];
+#pragma unroll
+  for (int sb = 0; sb < 2; sb++) {
+    S[sb][0] = lds128b(st + sb * kPkSub + 16 * g);
+    S[sb][1] = lds128b(st + sb * kPkSub + 16 * (g + 8));
+  }
+#pragma unroll
+  for (int kh = 0; kh < 2; kh++) {
+    uint4 N[2][2];
+#pragma unroll
+    for (int sb = 0; sb < 2; sb++)
+#pragma unroll
+      for (int h = 0; h < 2; h++) N[sb][h] = lds128b(st + sb * kPkSub + 256 + ((kh * 16 + g + 8 * h) * 4 + t) * 16);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int k = 4 * kh + j;
+      uint32_t A[2][8];
+      float d[2][2];
+#pragma unroll
+      for (int sb = 0; sb < 2; sb++) {
+        dq_row(u32w(N[sb][0], j), A[sb][0], A[sb][1], A[sb][2], A[sb][3]);
+        dq_row(u32w(N[sb][1], j), A[sb][4], A[sb][5], A[sb][6], A[sb][7]);
+        d[sb][0] = half_of(S[sb][0], k);
+        d[sb][1] = half_of(S[sb][1], k);
+      }
+#pragma unroll
+      for (int q = 0; q < (TWO ? 2 : 1); q++) {
+        if (q == 1 && !two) break;
+        const uint4 xb = lds128(xq + 32 * k + q * xstep);
+#pragma unroll
+        for (int sb = 0; sb < 2; sb++) {
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816(c, A[sb][0], A[sb][4], A[sb][1], A[sb][5], xb.x, xb.y);
+          mma16816(c, A[sb][2], A[sb][6], A[sb][3], A[sb][7], xb.z, xb.w);
+          acc[q][sb][0] = fmaf(d[sb][0], c[0], acc[q][sb][0]);
+          acc[q][sb][1] = fmaf(d[sb][0], c[1], acc[q][sb][1]);
+          acc[q][sb][2] = fmaf(d[sb][1], c[2], acc[q][sb][2]);
+          acc[q][sb][3] = fmaf(d[sb][1], c[3], acc[q][sb][3]);
+        }
+      }
+    }
+  }
+}
+
+// Pack rows x IN q4_0 (GGUF blocks) into the tile-packed layout: one CTA of
+// 128 threads per (16-row group, quantum); thread (h, r, t) writes one uint4.
+__global__ void k_q40_pack(const uint8_t* __restrict__ w, uint8_t* __restrict__ wt, int IN) {
+  const int nq = IN / 256, rowbytes = IN / 32 * 18;
+  const int r16 = blockIdx.y, kq = blockIdx.x;
+  uint8_t* out = wt + ((size_t)r16 * nq + kq) * kPkSub;
+  const int i = threadIdx.x, kh = i >> 6, r = (i >> 2) & 15, t = i & 3;
+  const uint8_t* row = w + (size_t)(16 * r16 + r) * rowbytes;
+  uint32_t wd[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int b = 8 * kq + 4 * kh + j;
+    const uint8_t* blk = row + 18 * b;
+    uint32_t v;
+    if (b & 1) {
+      v = blk[2 + 4 * t] | (uint32_t)blk[3 + 4 * t] << 8 | (uint32_t)blk[4 + 4 * t] << 16 | (uint32_t)blk[5 + 4 * t] << 24;
+    } else if (t < 3) {
+      v = blk[4 + 4 * t] | (uint32_t)blk[5 + 4 * t] << 8 | (uint32_t)blk[6 + 4 * t] << 16 | (uint32_t)blk[7 + 4 * t] << 24;
+    } else {
+      v = blk[2] | (uint32_t)blk[3] << 8 | (uint32_t)blk[16] << 16 | (uint32_t)blk[17] << 24;
+    }
+    wd[j] = v;
+  }
+  *reinterpret_cast<uint4*>(out + 256 + 16 * i) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  if (i < 16) {
+    const uint8_t* ri = w + (size_t)(16 * r16 + i) * rowbytes + (size_t)18 * 8 * kq;
+    uint32_t sc[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      sc[k] = ri[36 * k] | (uint32_t)ri[36 * k + 1] << 8 | (uint32_t)ri[36 * k + 18] << 16 |
+              (uint32_t)ri[36 * k + 19] << 24;
+    *reinterpret_cast<uint4*>(out + 16 * i) = make_uint4(sc[0], sc[1], sc[2], sc[3]);
+  }
+}
+
 // Chunk list of this launch (warp 0; dense: arithmetic, grouped: a warp scan of
 // the experts' entry counts).  Returns the number of chunks.
 template <int kTokC>
@@ -246,7 +343,7 @@ E4B_DEV void qmm_block(const uint8_t* a, const uint8_t* b, int sub_bytes, const 
 // KS > 1 (dense batches): the KS warps of a tile group split its quanta and sum
 // their partials through shared memory in a fixed order (deterministic), so a
 // small matrix still spreads over every SM.
-template <int MODE, int EPI, int W, int S, int TOKC, int KS>
+template <int MODE, int EPI, int W, int S, int TOKC, int KS, int PK = 0>
 __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_constant__ CUtensorMap map) {
   constexpr int NS = MODE == 0 ? 2 : 1;
   constexpr int TPI = W / KS;            // tiles per item
@@ -300,7 +397,16 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
     const Chunk c = chunks[pci];
     const int tile = prr * TPI + wt;
     uint8_t* st = stages + s * stage_bytes;
-    if (MODE == 0) {
+    if (MODE == 0 && PK) {
+      // two 16-row pieces of the packed copy (rows of expert c.e)
+      if (lane == 0) {
+        const size_t r0 = ((size_t)c.e * p.ROWS + (EPI == 1 ? 16 * tile : 32 * tile)) / 16;
+        const size_t r1 = ((size_t)c.e * p.ROWS + (EPI == 1 ? p.FF + 16 * tile : 32 * tile + 16)) / 16;
+        mbar_expect_tx(&full[warp][s], 2u * kPkSub);
+        bulk_g2s(st, p.w + (r0 * p.nq + pkq) * kPkSub, kPkSub, &full[warp][s]);
+        bulk_g2s(st + kPkSub, p.w + (r1 * p.nq + pkq) * kPkSub, kPkSub, &full[warp][s]);
+      }
+    } else if (MODE == 0) {
       if (lane == 0) mbar_expect_tx(&full[warp][s], (uint32_t)kQuantumBytes);
       __syncwarp();
       if (lane < 2) {
@@ -364,7 +470,9 @@ __global__ void __launch_bounds__(32 * W, 1) k_qmm(const QmmP p, const __grid_co
       if (ok) {
         constexpr int TWO = TOKC > 8;
         const int xstep = 8 * p.xpitch;
-        if (MODE == 0) {
+        if (MODE == 0 && PK) {
+          qmm_quantum_pk<TWO>(stages + s * stage_bytes, g, t, xr0 + 256 * kq, xstep, two, acc);
+        } else if (MODE == 0) {
           // IN % 256 == 0: always 8 whole blocks, fully unrolled (immediate offsets)
           const uint8_t* a = stages + s * stage_bytes + g * kRowPitch;
           const uint16_t* xq = xr0 + 256 * kq;
@@ -608,9 +716,9 @@ __global__ void __launch_bounds__(32 * kKW, 1) k_qkp(const QkpP p, const __grid_
   }
 }
 
-template <int MODE, int EPI, int W, int S, int TOKC, int KS>
+template <int MODE, int EPI, int W, int S, int TOKC, int KS, int PK = 0>
 int qmm_launch(e4b_ctx* c, const char* name, const QmmP& p, const CUtensorMap& map, size_t smem, int grid) {
-  auto kern = k_qmm<MODE, EPI, W, S, TOKC, KS>;
+  auto kern = k_qmm<MODE, EPI, W, S, TOKC, KS, PK>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e4b_fail(c, E4B_ECUDA, "%s smem attr: %s", name, cudaGetErrorString(e));
   return e4b_launch(c, name, kern, dim3((unsigned)grid), dim3(32 * W), smem, p, map);
@@ -626,7 +734,7 @@ constexpr size_t kQmmSmemCap = 227 * 1024 - 8 * 1024;   // dynamic budget beside
 // x: activations in fragment order; grouped when offsets != null.
 int qmm(e4b_ctx* c, const char* name, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
         const uint32_t* entries, float* y, uint16_t* yh, int IN, int ROWS, int FF, int K, int E, int n_dense,
-        int epi) {
+        int epi, bool packed = false) {
   E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0,
               "%s: weights and activations must be 16-byte aligned", name);
   E4B_REQUIRE(c, IN > 0 && IN % 64 == 0 && IN <= 16384, "%s: IN=%d must be a multiple of 64 (<= 16384)", name, IN);
@@ -677,6 +785,12 @@ int qmm(e4b_ctx* c, const char* name, const uint16_t* x, const uint8_t* w, const
   }
   if (grid < 1) grid = 1;
   const size_t sm = qmm_smem(p, mode, v.W, v.S, v.T, v.KS);
+  if (packed) {
+    // the tile-packed weights: grouped gate|up only, on the grouped variant
+    E4B_REQUIRE(c, mode == 0 && epi == 1 && offsets && vi == 0 && FF % 16 == 0,
+                "%s: the tile-packed path needs IN %% 256 == 0 and the grouped gate|up GEMM (IN=%d)", name, IN);
+    return qmm_launch<0, 1, 16, 2, 8, 1, 1>(c, name, p, map, sm, grid);
+  }
 #define QMM_CASE(M, EP)                                                          \
   if (mode == M && epi == EP) {                                                  \
     switch (vi) {                                                                \
@@ -748,6 +862,24 @@ E4B_API int e4b_q40gugrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const 
   E4B_REQUIRE(c, x && w && offsets && entries && yh, "q40gugrp: null buffer");
   E4B_REQUIRE(c, FF > 0 && FF % 32 == 0 && E > 0 && E <= 4096 && K > 0, "q40gugrp: bad sizes FF=%d E=%d", FF, E);
   return qmm(c, "q40gugrp", x, w, offsets, entries, nullptr, yh, IN, 2 * FF, FF, K, E, 0, 1);
+}
+
+E4B_API int e4b_q40_pack_tiles(e4b_ctx* c, const uint8_t* w, uint8_t* wt, int rows, int IN) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, w && wt && w != wt, "q40_pack_tiles: null or aliased buffers");
+  E4B_REQUIRE(c, rows > 0 && rows % 16 == 0 && rows / 16 <= 65535 && IN > 0 && IN % 256 == 0,
+              "q40_pack_tiles: rows=%d (a multiple of 16) x IN=%d (a multiple of 256)", rows, IN);
+  E4B_REQUIRE(c, reinterpret_cast<uintptr_t>(wt) % 16 == 0, "q40_pack_tiles: packed copy must be 16-byte aligned");
+  return e4b_launch(c, "q40_pack_tiles", k_q40_pack, dim3(IN / 256, rows / 16), dim3(128), 0, w, wt, IN);
+}
+
+E4B_API int e4b_q40gugrp_tiles(e4b_ctx* c, const uint16_t* x, const uint8_t* wt, const uint32_t* offsets,
+                               const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K) {
+  E4B_CHECK_CTX(c);
+  E4B_REQUIRE(c, x && wt && offsets && entries && yh, "q40gugrp_tiles: null buffer");
+  E4B_REQUIRE(c, FF > 0 && FF % 32 == 0 && E > 0 && E <= 4096 && K > 0, "q40gugrp_tiles: bad sizes FF=%d E=%d", FF,
+              E);
+  return qmm(c, "q40gugrp_tiles", x, wt, offsets, entries, nullptr, yh, IN, 2 * FF, FF, K, E, 0, 1, true);
 }
 
 E4B_API int e4b_q40downgrp(e4b_ctx* c, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,

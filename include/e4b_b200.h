@@ -210,6 +210,18 @@ E4B_API int e4b_q40gugrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, cons
                          const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K);
 E4B_API int e4b_q40downgrp(e4b_ctx* ctx, const uint16_t* x, const uint8_t* w, const uint32_t* offsets,
                            const uint32_t* entries, float* y, int IN, int OUT, int E);
+/* Tile-packed copy of a q4_0 matrix (rows % 16 == 0, IN % 256 == 0; the same
+ * number of bytes as the GGUF blocks, wt 16-byte aligned): per 16-row group r
+ * and 256-k quantum q one 2304-byte piece at (r * IN/256 + q) * 2304, the 16
+ * rows' 8 f16 block scales ([row][block], 256 B) then the nibble bytes
+ * regrouped into the 32-bit words the tensor-core A operand of each lane reads
+ * ([block half][row][lane] x 4 words, 2048 B).  e4b_q40gugrp_tiles is
+ * e4b_q40gugrp on that copy of w[E][2FF][IN] (rows = E * 2FF): one 16-byte load
+ * per row for 8 scales and per 4 blocks for the nibbles, no unaligned block
+ * reads; its outputs are bit-identical to e4b_q40gugrp's. */
+E4B_API int e4b_q40_pack_tiles(e4b_ctx* ctx, const uint8_t* w, uint8_t* wt, int rows, int IN);
+E4B_API int e4b_q40gugrp_tiles(e4b_ctx* ctx, const uint16_t* x, const uint8_t* wt, const uint32_t* offsets,
+                               const uint32_t* entries, uint16_t* yh, int IN, int FF, int E, int K);
 /* dst[i] = src[idx[i] / div] for n f16 rows of H (a zero row where idx[i] is
  * 0xffffffff or out of range): the expert-sorted activation rows of a prefill
  * chunk (entries from e4b_expgroup, div = K), contiguous per expert as the

@@ -71,6 +71,62 @@ def test_grouped_moe_matches_per_token_oracle(e4b, dev, n, hot):
     assert worst < 2e-3, worst     # f16 GeGLU intermediates may round one ulp apart
 
 
+def _pack_q40_ref(w: np.ndarray, rows: int, n_in: int) -> np.ndarray:
+    """numpy restatement of the tile-packed q4_0 layout (e4b_q40_pack_tiles)."""
+    nq, rb = n_in // 256, n_in // 32 * 18
+    src = w.reshape(rows, rb)
+    out = np.zeros((rows // 16, nq, 2304), np.uint8)
+    for r16 in range(rows // 16):
+        for q in range(nq):
+            piece = out[r16, q]
+            for r in range(16):
+                row = src[16 * r16 + r]
+                for k in range(8):
+                    b = 8 * q + k
+                    piece[16 * r + 2 * k:16 * r + 2 * k + 2] = row[18 * b:18 * b + 2]
+                for kh in range(2):
+                    for t in range(4):
+                        for j in range(4):
+                            b = 8 * q + 4 * kh + j
+                            blk = row[18 * b:18 * b + 18]
+                            if b & 1:
+                                word = blk[2 + 4 * t:6 + 4 * t]
+                            elif t < 3:
+                                word = blk[4 + 4 * t:8 + 4 * t]
+                            else:
+                                word = np.array([blk[2], blk[3], blk[16], blk[17]], np.uint8)
+                            o = 256 + ((kh * 16 + r) * 4 + t) * 16 + 4 * j
+                            piece[o:o + 4] = word
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("H,n,hot", [(512, 13, 0), (512, 80, 75), (256, 64, 0)])
+def test_q40gugrp_tiles_bit_identical(e4b, dev, H, n, hot):
+    """The tile-packed copy matches its numpy restatement byte for byte, and the
+    grouped gate|up on it equals e4b_q40gugrp bit for bit (ragged groups and a
+    >64-token expert)."""
+    E, K, EF = 16, 4, 192
+    rng = np.random.default_rng(100 + n)
+    wgu = q40(e4b, E * 2 * EF, H, 41)
+    x = O.f16r(rng.standard_normal((n, H)).astype(F32))
+    idx, _ = _topk(rng, n, K, E, hot)
+    d = dev
+    bx, bgu, bidx = d.upload(e4b.batch.to_xfo(x.astype(np.float16))), d.upload(wgu), d.upload(idx)
+    bt = d.alloc(wgu.nbytes)
+    off, ent, inv = d.alloc((E + 1) * 4), d.alloc(n * K * 4), d.alloc(n * K * 4)
+    g0, g1 = d.alloc(n * K * EF * 2), d.alloc(n * K * EF * 2)
+    d.call("e4b_q40_pack_tiles", bgu.ptr, bt.ptr, E * 2 * EF, H)
+    d.call("e4b_expgroup", bidx.ptr, n, K, E, off.ptr, ent.ptr, inv.ptr)
+    d.call("e4b_q40gugrp", bx.ptr, bgu.ptr, off.ptr, ent.ptr, g0.ptr, H, EF, E, K)
+    d.call("e4b_q40gugrp_tiles", bx.ptr, bt.ptr, off.ptr, ent.ptr, g1.ptr, H, EF, E, K)
+    d.sync()
+    assert d.status() == 0
+    packed = d.read(bt, np.uint8, wgu.nbytes)
+    assert np.array_equal(packed, _pack_q40_ref(wgu.view(np.uint8), E * 2 * EF, H))
+    a, b = d.read(g0, np.uint16, n * K * EF), d.read(g1, np.uint16, n * K * EF)
+    assert np.array_equal(a, b)
+
+
 @pytest.mark.parametrize("IN,OUT", [(512, 96), (256, 40), (192, 64), (704, 48)])
 @pytest.mark.parametrize("n", [1, 7, 16, 37, 64])
 def test_dense_q40mm(e4b, dev, IN, OUT, n):
