@@ -188,7 +188,8 @@ E4B_DEV uint4 lds128b(const uint8_t* p) { return lds128(reinterpret_cast<const u
 E4B_DEV uint32_t u32w(const uint4& v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
 E4B_DEV float half_of(const uint4& v, int k) {
   const uint32_t w = u32w(v, k >> 1);
-  return h2f((uint16_t)((k & 1) ? w >> 16 : w & 0xFFFFu));
+  const __half2 h = *reinterpret_cast<const __half2*>(&w);     // the conversion reads either half in place
+  return (k & 1) ? __high2float(h) : __low2float(h);
 }
 // One quantum of the gate|up tile from a packed stage (two 16-row pieces).
 template <int TWO>
