@@ -121,8 +121,8 @@ static_assert(sizeof(MkPhase) % 16 == 0, "phase descriptors are copied in 16-byt
 
 // One entry of a warp's weight schedule: its quanta of one GEMV phase.
 struct SchedEnt {
-  const CUtensorMap* map;
-  int t0, k0, kq, nw, gu, ff;
+  const uint8_t* wt;    // the GEMV's tile-packed weights (2304-byte pieces of 16 rows x 256 k)
+  int t0, k0, kq, nw, gu, ff, nq;
 };
 
 struct MkArgs {
@@ -288,18 +288,12 @@ E4B_DEV uint64_t policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-E4B_DEV void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t pol) {
+E4B_DEV void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
-}
-// Bring a box into L2 only (no shared memory, no barrier).
-E4B_DEV void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
 }
 // Bulk L2 prefetch of [p, p + bytes): p 16-byte aligned, bytes a multiple of 16.
 E4B_DEV void bulk_prefetch_l2(const void* p, uint32_t bytes) {
@@ -402,12 +396,13 @@ E4B_DEV void prod_init(const MkArgs& A, Prod& u, int c, int warp) {
   if (u.idx + 1 < u.end) u.nx = A.sched[u.idx + 1];
 }
 
-// The cursor's quantum: x coordinate and rows of its two boxes.
-E4B_DEV void prod_coords(const Prod& u, int& x, int& r0, int& r1) {
-  const int tile = u.e.t0 + u.tl;
-  x = (u.e.k0 + u.kk) * 18;
-  r0 = u.e.gu ? 16 * tile : 32 * tile;
-  r1 = u.e.gu ? u.e.ff + 16 * tile : 32 * tile + 16;
+// The cursor's quantum: its two 16-row pieces in the packed copy (gate|up:
+// gate rows 16 tile and up rows ff + 16 tile; else rows 32 tile and 32 tile + 16).
+E4B_DEV void prod_src(const Prod& u, const uint8_t*& a, const uint8_t*& b) {
+  const int tile = u.e.t0 + u.tl, kq = u.e.k0 + u.kk;
+  const int r0 = u.e.gu ? tile : 2 * tile, r1 = u.e.gu ? u.e.ff / 16 + tile : 2 * tile + 1;
+  a = u.e.wt + ((size_t)r0 * u.e.nq + kq) * kPkSub;
+  b = u.e.wt + ((size_t)r1 * u.e.nq + kq) * kPkSub;
 }
 E4B_DEV void prod_advance(const MkArgs& A, Prod& u, int warp) {
   u.kk += kWarps;
@@ -426,21 +421,21 @@ E4B_DEV void prod_advance(const MkArgs& A, Prod& u, int warp) {
 // Issue the cursor's quantum into `stage` (lane 0), then advance the cursor.
 E4B_DEV void prod_issue(const MkArgs& A, Prod& u, uint8_t* stage, uint64_t* bar, int warp, int lane, uint64_t pol) {
   if (lane == 0) {
-    int x, r0, r1;
-    prod_coords(u, x, r0, r1);
-    mbar_expect_tx(bar, (uint32_t)kQuantumBytes);
-    tma_load_2d_hint(stage, u.e.map, x, r0, bar, pol);
-    tma_load_2d_hint(stage + kSubBytes, u.e.map, x, r1, bar, pol);
+    const uint8_t *a, *b;
+    prod_src(u, a, b);
+    mbar_expect_tx(bar, 2u * kPkSub);
+    bulk_g2s_hint(stage, a, kPkSub, bar, pol);
+    bulk_g2s_hint(stage + kPkSub, b, kPkSub, bar, pol);
   }
   prod_advance(A, u, warp);
 }
 // L2 prefetch of the prefetch cursor's quantum, then advance it.
 E4B_DEV void prod_prefetch(const MkArgs& A, Prod& u, int warp, int lane) {
   if (lane == 0) {
-    int x, r0, r1;
-    prod_coords(u, x, r0, r1);
-    tma_prefetch_2d(u.e.map, x, r0);
-    tma_prefetch_2d(u.e.map, x, r1);
+    const uint8_t *a, *b;
+    prod_src(u, a, b);
+    bulk_prefetch_l2(a, kPkSub);
+    bulk_prefetch_l2(b, kPkSub);
   }
   prod_advance(A, u, warp);
 }
@@ -454,6 +449,58 @@ struct Ring {
   unsigned long long wait_ns;   // time spent waiting for weights (traced runs)
 };
 
+// quantum_mma_rt on a packed stage (pieces: subtile 0 then 1): the same A
+// registers, scales and MMAs, from one 16-byte load per row and 4 blocks and
+// one 4-byte scale load per row.
+E4B_DEV void quantum_mma_pk(const uint8_t* st, const uint4 xh, const uint4 xl, int g, int t, float (&acc)[4],
+                            bool xf32) {
+  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};   // subtile 0: low / high k-half
+  float c2[4] = {0.f, 0.f, 0.f, 0.f}, c3[4] = {0.f, 0.f, 0.f, 0.f};   // subtile 1
+#pragma unroll
+  for (int kh = 0; kh < 2; kh++) {
+    const uint8_t* nb = st + 256 + ((kh * 16 + g) * 4 + t) * 16;
+    const uint4 N0 = *reinterpret_cast<const uint4*>(nb);                  // subtile 0, row g
+    const uint4 N1 = *reinterpret_cast<const uint4*>(nb + 8 * 64);         // subtile 0, row g + 8
+    const uint4 N2 = *reinterpret_cast<const uint4*>(nb + kPkSub);        // subtile 1, row g
+    const uint4 N3 = *reinterpret_cast<const uint4*>(nb + kPkSub + 8 * 64);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int k = 4 * kh + j;
+      uint32_t A[16];
+      dq_row(u32w(N0, j), A[0], A[1], A[2], A[3]);
+      dq_row(u32w(N1, j), A[4], A[5], A[6], A[7]);
+      dq_row(u32w(N2, j), A[8], A[9], A[10], A[11]);
+      dq_row(u32w(N3, j), A[12], A[13], A[14], A[15]);
+      const bool mine = g == k;
+      const uint32_t b0 = mine ? xh.x : 0u, b1 = mine ? xh.y : 0u, b2 = mine ? xh.z : 0u, b3 = mine ? xh.w : 0u;
+      mma16816(c0, A[0], A[4], A[1], A[5], b0, b1);
+      mma16816(c2, A[8], A[12], A[9], A[13], b0, b1);
+      mma16816(c1, A[2], A[6], A[3], A[7], b2, b3);
+      mma16816(c3, A[10], A[14], A[11], A[15], b2, b3);
+      if (xf32) {
+        const uint32_t l0 = mine ? xl.x : 0u, l1 = mine ? xl.y : 0u, l2 = mine ? xl.z : 0u, l3 = mine ? xl.w : 0u;
+        mma16816(c0, A[0], A[4], A[1], A[5], l0, l1);
+        mma16816(c2, A[8], A[12], A[9], A[13], l0, l1);
+        mma16816(c1, A[2], A[6], A[3], A[7], l2, l3);
+        mma16816(c3, A[10], A[14], A[11], A[15], l2, l3);
+      }
+    }
+  }
+  // C cols 2t, 2t+1 = blocks 2t, 2t+1: word t of each row's 8 scales
+  float d[8];
+  const int so[4] = {16 * g, 16 * (g + 8), kPkSub + 16 * g, kPkSub + 16 * (g + 8)};
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(st + so[r] + 4 * t);
+    d[2 * r] = h2f((uint16_t)(w & 0xFFFFu));
+    d[2 * r + 1] = h2f((uint16_t)(w >> 16));
+  }
+  acc[0] = fmaf(d[0], c0[0] + c1[0], fmaf(d[1], c0[1] + c1[1], acc[0]));
+  acc[1] = fmaf(d[2], c0[2] + c1[2], fmaf(d[3], c0[3] + c1[3], acc[1]));
+  acc[2] = fmaf(d[4], c2[0] + c3[0], fmaf(d[5], c2[1] + c3[1], acc[2]));
+  acc[3] = fmaf(d[6], c2[2] + c3[2], fmaf(d[7], c2[3] + c3[3], acc[3]));
+}
+
 // ------------------------------------------------------------------ GEMV phase
 // x: activations in shared memory indexed by absolute block (8 k + g); XF32:
 // f32 x split into f16 hi + lo (twice the MMAs; one GEMV per token uses it).
@@ -464,10 +511,6 @@ E4B_DEV void gemv_phase(const MkArgs& A, const Work& W, int warp, int lane, Ring
   const int nw = warp_items(W, warp);
   if (nw == 0) return;
   const int gg = lane >> 2, t = lane & 3;
-  Lane L;
-  L.o_odd = 2 + 4 * t;
-  L.o_e1 = t < 3 ? 4 + 4 * t : 0;
-  L.sel = t < 3 ? 0x3210u : 0x5432u;
   const XLane X = xlane(gg, t);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   int tl = warp / W.kq, kk = warp - tl * W.kq;      // item j: warp + 8 j = tl * kq + kk
@@ -486,7 +529,7 @@ E4B_DEV void gemv_phase(const MkArgs& A, const Work& W, int warp, int lane, Ring
     const unsigned long long tw0 = tw ? globaltimer_ns() : 0ull;
     if (R.ok) R.ok = mbar_wait(&R.full[s], (R.cnt / kStages) & 1u, A.status);
     if (tw) R.wait_ns += globaltimer_ns() - tw0;
-    if (R.ok) quantum_mma_rt(R.base + s * kQuantumBytes, xh, xl, L, gg, t, acc, xf32);
+    if (R.ok) quantum_mma_pk(R.base + s * kQuantumBytes, xh, xl, gg, t, acc, xf32);
     R.cnt++;
     // every lane's shared-memory reads of the stage are complete (their values
     // fed the MMAs) before the TMA unit overwrites it
@@ -1223,8 +1266,7 @@ struct Builder {
   DensePlan* plan;
   int G;
   std::vector<MkPhase> ph;
-  std::vector<CUtensorMap> maps;
-  std::vector<int> map_of_phase;   // index into maps, -1: none
+  std::vector<const uint8_t*> wt_of_phase;   // the GEMV's tile-packed weights, null: none
   std::vector<long long> load;     // cumulative weight bytes per CTA (rotation choice)
 
   int alloc(size_t bytes, void** out) {
@@ -1242,7 +1284,7 @@ struct Builder {
     p.kind = kind;
     p.rmul = 1.f;
     ph.push_back(p);
-    map_of_phase.push_back(-1);
+    wt_of_phase.push_back(nullptr);
     return ph.back();
   }
 
@@ -1291,23 +1333,14 @@ struct Builder {
       load[cc] += b[v];
     }
     if (src) *src = SlotSrc{out, g.s, tag};
-    // tensor map over the raw rows as 8-byte words, boxes of 16 rows x 8 blocks
-    const int rowbytes = IN / 32 * 18;
+    // a tile-packed copy of the weights (2304-byte pieces of 16 rows x 256 k),
+    // owned by the plan: every quantum is two contiguous bulk copies
     const int rows_total = gu ? 2 * ff : OUT;
-    CUtensorMap m;
-    const cuuint64_t gdim[2] = {(cuuint64_t)(rowbytes / 8), (cuuint64_t)rows_total};
-    const cuuint64_t gstride[1] = {(cuuint64_t)rowbytes};
-    const cuuint32_t box[2] = {kRowPitch / 8, 16};
-    const cuuint32_t estride[2] = {1, 1};
-    auto enc = tensor_map_encoder();
-    E4B_REQUIRE(c, enc != nullptr, "dense plan: cuTensorMapEncodeTiled unavailable");
-    CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(w), gdim, gstride, box, estride,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    E4B_REQUIRE(c, r == CUDA_SUCCESS, "dense plan: cuTensorMapEncodeTiled failed (%d) IN=%d rows=%d", (int)r, IN,
-                rows_total);
-    maps.push_back(m);
-    map_of_phase.back() = (int)maps.size() - 1;
+    E4B_REQUIRE(c, gu ? ff % 16 == 0 : OUT % 32 == 0, "dense plan: GEMV rows %d (ff %d) not in 32-row tiles", OUT, ff);
+    uint8_t* wt = nullptr;
+    if (int rc = alloc((size_t)rows_total * (IN / 32) * 18, (void**)&wt)) return rc;
+    if (int rc = e4b_q40_pack_tiles(c, w, wt, rows_total, IN)) return rc;
+    wt_of_phase.back() = wt;
     return E4B_OK;
   }
 };
@@ -1330,7 +1363,7 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
   E4B_REQUIRE(c, G > 0, "dense plan: no SMs");
 
   DensePlan* plan = new DensePlan();
-  Builder b{c, plan, G, {}, {}, {}, std::vector<long long>(G, 0)};
+  Builder b{c, plan, G, {}, {}, std::vector<long long>(G, 0)};
   auto fail = [&](int rc) {
     plan_free(plan);
     return rc;
@@ -1545,12 +1578,10 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
     P.dump = m->dump ? m->dump + (size_t)(L - 1) * H : nullptr;
   }
 
-  // ---- device copies: tensor maps, phases, and every warp's weight schedule
-  CUtensorMap* d_maps = nullptr;
+  // ---- device copies: phases and every warp's weight schedule
   MkPhase* d_ph = nullptr;
   SchedEnt* d_sched = nullptr;
   int2* d_rng = nullptr;
-  if ((rc = b.alloc(b.maps.size() * sizeof(CUtensorMap), (void**)&d_maps))) return fail(rc);
   if ((rc = b.alloc(b.ph.size() * sizeof(MkPhase), (void**)&d_ph))) return fail(rc);
   std::vector<SchedEnt> sched;
   std::vector<int2> rng((size_t)G * kWarps);
@@ -1566,7 +1597,8 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
         const int nw = warp_items(W, w);
         if (nw == 0) continue;
         SchedEnt e;
-        e.map = d_maps + b.map_of_phase[i];
+        e.wt = b.wt_of_phase[i];
+        e.nq = P.g.qpr;
         e.t0 = W.t0;
         e.k0 = W.k0;
         e.kq = W.kq;
@@ -1579,10 +1611,7 @@ int plan_create(e4b_ctx* c, const e4b_dense_model* m, int* handle) {
     }
   if ((rc = b.alloc(std::max<size_t>(1, sched.size()) * sizeof(SchedEnt), (void**)&d_sched))) return fail(rc);
   if ((rc = b.alloc(rng.size() * sizeof(int2), (void**)&d_rng))) return fail(rc);
-  cudaError_t e = cudaMemcpyAsync(d_maps, b.maps.data(), b.maps.size() * sizeof(CUtensorMap),
-                                  cudaMemcpyHostToDevice, c->stream);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(d_ph, b.ph.data(), b.ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice, c->stream);
+  cudaError_t e = cudaMemcpyAsync(d_ph, b.ph.data(), b.ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice, c->stream);
   if (e == cudaSuccess && !sched.empty())
     e = cudaMemcpyAsync(d_sched, sched.data(), sched.size() * sizeof(SchedEnt), cudaMemcpyHostToDevice, c->stream);
   if (e == cudaSuccess)

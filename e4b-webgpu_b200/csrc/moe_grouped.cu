@@ -183,9 +183,7 @@ E4B_DEV uint4 lds128(const uint16_t* p) {
 // the GGUF block).  A warp reads a row's 8 scales and 4 blocks' nibble words
 // with one 16-byte load each, conflict-free; the decoded A registers equal the
 // row-major path's, so results are bit-identical.
-constexpr int kPkSub = 2304;
 E4B_DEV uint4 lds128b(const uint8_t* p) { return lds128(reinterpret_cast<const uint16_t*>(p)); }
-E4B_DEV uint32_t u32w(const uint4& v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
 E4B_DEV float half_of(const uint4& v, int k) {
   const uint32_t w = u32w(v, k >> 1);
   const __half2 h = *reinterpret_cast<const __half2*>(&w);     // the conversion reads either half in place

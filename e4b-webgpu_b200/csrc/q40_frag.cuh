@@ -52,6 +52,12 @@ E4B_DEV void dq_row(uint32_t v, uint32_t& lo02, uint32_t& lo13, uint32_t& hi02, 
   hi13 = hfma2(and_or(v8, 0x00F000F0u, kMag), kSixteenth, kM72);
 }
 
+// ---- tile-packed q4_0 (e4b_q40_pack_tiles): per 16 rows x 256 k one piece of
+// kPkSub bytes, [16 rows][8 blocks] f16 scales then, as [block half][row][lane]
+// uint4s, the 32-bit words nib() returns for lane t (word j: block 4 half + j).
+constexpr int kPkSub = 2304;
+E4B_DEV uint32_t u32w(const uint4& v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
+
 // ---- B operand: lane (g, t) supplies column g of B, i.e. the activations of
 // block 8q+g of quantum q at the element indices its A fragments use: low half
 // {j0, j2}, {j1, j3}; high half the same + 16.  A block's parity equals g's
