@@ -10,7 +10,8 @@
 // separated by a grid barrier and the weight stream never stops.
 //
 // Weight stream.  Every GEMV's work is cut into quanta (32 rows x 8 q4_0 blocks,
-// two 16-row TMA boxes of the raw GGUF bytes).  Each warp owns a fixed,
+// two 2304-byte pieces of the plan's tile-packed copy of the weights, one bulk
+// copy each).  Each warp owns a fixed,
 // host-precomputed schedule of quanta spanning ALL GEMV phases of the token and
 // a private ring of mbarrier-tracked shared-memory stages.  A stage is refilled
 // with the warp's next quantum as soon as it has been consumed, whatever phase
