@@ -240,6 +240,7 @@ E4B_DEV void qmm_quantum_pk(const uint8_t* st, int g, int t, const uint16_t* xq,
 // Pack rows x IN q4_0 (GGUF blocks) into the tile-packed layout: one CTA of
 // 128 threads per (16-row group, quantum); thread (h, r, t) writes one uint4.
 __global__ void k_q40_pack(const uint8_t* __restrict__ w, uint8_t* __restrict__ wt, int IN) {
+  pdl_wait();
   const int nq = IN / 256, rowbytes = IN / 32 * 18;
   const int r16 = blockIdx.y, kq = blockIdx.x;
   uint8_t* out = wt + ((size_t)r16 * nq + kq) * kPkSub;

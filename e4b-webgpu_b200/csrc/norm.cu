@@ -222,6 +222,22 @@ E4B_DEV float2 block_sum2(float a, float b, float* sh) {
   }
   return make_float2(ta, tb);
 }
+// The sums of squares in the scalar kernels' order, so both forms give the
+// same bits: the row is staged in shared memory and thread t < T adds elements
+// t, t + T, ... with fmaf (T = the scalar kernel's CTA size; other threads add
+// nothing), then the block sum.
+E4B_DEV float strided_sumsq(const float* row, int n, int T) {
+  float s = 0.f;
+  if ((int)threadIdx.x < T)
+    for (int k = threadIdx.x; k < n; k += T) s = fmaf(row[k], row[k], s);
+  return s;
+}
+E4B_DEV float strided_sum(const float* row, int n, int T) {
+  float s = 0.f;
+  if ((int)threadIdx.x < T)
+    for (int k = threadIdx.x; k < n; k += T) s += row[k];
+  return s;
+}
 // four f16 values of elements i..i+3 (fragment order: scattered positions)
 E4B_DEV void st_h4(uint16_t* __restrict__ y, size_t ob, int i, int xfo, float a, float b, float c, float d) {
   if (xfo) {
@@ -241,6 +257,7 @@ __global__ void __launch_bounds__(1024, 1)
                uint16_t* __restrict__ y1, float* __restrict__ y2, uint16_t* __restrict__ y3, float* __restrict__ h_out,
                int dim, float eps, int xfo, int nparts, size_t part_stride) {
   __shared__ float sh[64];
+  __shared__ __align__(16) float rowv[4096];
   const int i = 4 * (int)threadIdx.x;
   const bool on = i < dim;
   const size_t ob = (size_t)blockIdx.x * dim;
@@ -253,15 +270,21 @@ __global__ void __launch_bounds__(1024, 1)
   if (on) {
     tv = sum_parts4(reinterpret_cast<const float4*>(t + ob + i), part_stride / 4, nparts);
     hv = ld4(h_in + ob + i);
+    st4(rowv + i, tv);
   }
-  const float inv1 = rms_scale(block_sum(on ? sq4(tv) : 0.f, sh), dim, eps);
+  __syncthreads();
+  const float inv1 = rms_scale(block_sum(strided_sumsq(rowv, dim, 1024), sh), dim, eps);
   float4 h;
   h.x = hv.x + tv.x * inv1 * wa.x;
   h.y = hv.y + tv.y * inv1 * wa.y;
   h.z = hv.z + tv.z * inv1 * wa.z;
   h.w = hv.w + tv.w * inv1 * wa.w;
-  if (on) st4(h_out + ob + i, h);
-  const float inv2 = rms_scale(block_sum(on ? sq4(h) : 0.f, sh), dim, eps);
+  if (on) {
+    st4(h_out + ob + i, h);
+    st4(rowv + i, h);        // every thread's reads of rowv preceded block_sum's first barrier
+  }
+  __syncthreads();
+  const float inv2 = rms_scale(block_sum(strided_sumsq(rowv, dim, 1024), sh), dim, eps);
   if (!on) return;
   const float4 v = make_float4(h.x * inv2, h.y * inv2, h.z * inv2, h.w * inv2);
   st_h4(y1, ob, i, xfo, v.x * a1.x, v.y * a1.y, v.z * a1.z, v.w * a1.w);
@@ -276,6 +299,7 @@ __global__ void __launch_bounds__(1024, 1)
                float eps, float mul, int next, int xfo, const float* __restrict__ y, const uint32_t* __restrict__ inv,
                const float* __restrict__ tkw, int K) {
   __shared__ float sh[64];
+  __shared__ __align__(16) float rowa[4096], rowb[4096];
   const int i = 4 * (int)threadIdx.x;
   const bool on = i < H;
   const size_t ob = (size_t)blockIdx.x * H;
@@ -314,22 +338,33 @@ __global__ void __launch_bounds__(1024, 1)
       mv = ld4(m + ob + i);
     }
   }
-  const float2 s12 = block_sum2(on ? sq4(tv) : 0.f, on ? sq4(mv) : 0.f, sh);
+  if (on) {
+    st4(rowa + i, tv);
+    st4(rowb + i, mv);
+  }
+  __syncthreads();
+  const float2 s12 = block_sum2(strided_sumsq(rowa, H, 1024), strided_sumsq(rowb, H, 1024), sh);
   const float inv1 = rms_scale(s12.x, H, eps), inv2 = rms_scale(s12.y, H, eps);
   float4 cc;
   cc.x = tv.x * inv1 * a1.x + mv.x * inv2 * a2.x;
   cc.y = tv.y * inv1 * a1.y + mv.y * inv2 * a2.y;
   cc.z = tv.z * inv1 * a1.z + mv.z * inv2 * a2.z;
   cc.w = tv.w * inv1 * a1.w + mv.w * inv2 * a2.w;
-  const float inv3 = rms_scale(block_sum(on ? sq4(cc) : 0.f, sh), H, eps);
+  if (on) st4(rowa + i, cc);   // rowa's reads preceded block_sum2's first barrier
+  __syncthreads();
+  const float inv3 = rms_scale(block_sum(strided_sumsq(rowa, H, 1024), sh), H, eps);
   float4 hn;
   hn.x = (hv.x + cc.x * inv3 * ap.x) * mul;
   hn.y = (hv.y + cc.y * inv3 * ap.y) * mul;
   hn.z = (hv.z + cc.z * inv3 * ap.z) * mul;
   hn.w = (hv.w + cc.w * inv3 * ap.w) * mul;
-  if (on) st4(h_out + ob + i, hn);
+  if (on) {
+    st4(h_out + ob + i, hn);
+    st4(rowa + i, hn);
+  }
+  __syncthreads();
   if (next) {
-    const float inv4 = rms_scale(block_sum(on ? sq4(hn) : 0.f, sh), H, eps);
+    const float inv4 = rms_scale(block_sum(strided_sumsq(rowa, H, 1024), sh), H, eps);
     if (on)
       st_h4(y_next, ob, i, xfo, hn.x * inv4 * an.x, hn.y * inv4 * an.y, hn.z * inv4 * an.z, hn.w * inv4 * an.w);
   }
@@ -341,6 +376,7 @@ __global__ void __launch_bounds__(1024, 1)
                float* __restrict__ sums, uint16_t* __restrict__ yh, int dim, float eps, int with_scale, int sumout,
                int f16out) {
   __shared__ float sh[64];
+  __shared__ __align__(16) float rowv[4096];
   const int i = 4 * (int)threadIdx.x;
   const bool on = i < dim;
   const size_t ob = (size_t)blockIdx.x * dim;
@@ -348,7 +384,10 @@ __global__ void __launch_bounds__(1024, 1)
   const float4 wv = on && with_scale ? ld4(w + i) : z;
   pdl_wait();
   const float4 xv = on ? ld4(x + ob + i) : z;
-  const float inv = rms_scale(block_sum(on ? sq4(xv) : 0.f, sh), dim, eps);
+  if (on) st4(rowv + i, xv);
+  __syncthreads();
+  // k_rmsnorm's order: 256 threads
+  const float inv = rms_scale(block_sum(strided_sumsq(rowv, dim, 256), sh), dim, eps);
   float4 v = make_float4(xv.x * inv, xv.y * inv, xv.z * inv, xv.w * inv);
   if (with_scale) v = make_float4(v.x * wv.x, v.y * wv.y, v.z * wv.z, v.w * wv.w);
   if (on) {
@@ -356,7 +395,9 @@ __global__ void __launch_bounds__(1024, 1)
     else st4(y + ob + i, v);
   }
   if (sumout) {
-    const float t = block_sum(on ? ((v.x + v.y) + v.z) + v.w : 0.f, sh);
+    if (on) st4(rowv + i, v);
+    __syncthreads();
+    const float t = block_sum(strided_sum(rowv, dim, 256), sh);
     if (threadIdx.x == 0) sums[blockIdx.x] = t;
   }
 }
