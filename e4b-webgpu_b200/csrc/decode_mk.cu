@@ -450,9 +450,10 @@ struct Ring {
   unsigned long long wait_ns;   // time spent waiting for weights (traced runs)
 };
 
-// quantum_mma_rt on a packed stage (pieces: subtile 0 then 1): the same A
-// registers, scales and MMAs, from one 16-byte load per row and 4 blocks and
-// one 4-byte scale load per row.
+// One quantum (8 blocks x 32 rows) of a packed stage (pieces: subtile 0 then
+// 1): quantum_mma's A registers, scales and MMAs, from one 16-byte load per
+// row and 4 blocks and one 4-byte scale load per row; the f32-activation
+// (hi + lo) MMAs chosen at run time, one copy of the code for both kinds.
 E4B_DEV void quantum_mma_pk(const uint8_t* st, const uint4 xh, const uint4 xl, int g, int t, float (&acc)[4],
                             bool xf32) {
   float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};   // subtile 0: low / high k-half

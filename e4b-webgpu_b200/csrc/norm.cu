@@ -180,7 +180,6 @@ __global__ void k_a4btail(const float* __restrict__ t1, const float* __restrict_
 // sums of squares add each thread's four elements first.
 E4B_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 E4B_DEV void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
-E4B_DEV float sq4(float4 v) { return fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, v.x * v.x))); }
 // p[0] + p[stride4] + ... in that order, per component (sum_parts on float4s)
 E4B_DEV float4 sum_parts4(const float4* __restrict__ p, size_t stride4, int n) {
   float4 v = make_float4(0.f, 0.f, 0.f, 0.f);

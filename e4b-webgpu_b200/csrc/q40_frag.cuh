@@ -193,48 +193,4 @@ E4B_DEV void quantum_mma(const uint8_t* q, const uint4 xh, const uint4 xl, const
   acc[3] = fmaf(d[6], c2[2] + c3[2], fmaf(d[7], c2[3] + c3[3], acc[3]));
 }
 
-// quantum_mma with the f32-activation (hi + lo) path chosen at run time: one
-// copy of the code for kernels that run both kinds of GEMV.
-E4B_DEV void quantum_mma_rt(const uint8_t* q, const uint4 xh, const uint4 xl, const Lane& L, int g, int t,
-                            float (&acc)[4], bool xf32) {
-  const uint8_t* r0 = q + g * kRowPitch;
-  const uint8_t* r1 = r0 + 8 * kRowPitch;
-  const uint8_t* r2 = r0 + kSubBytes;
-  const uint8_t* r3 = r1 + kSubBytes;
-  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-  float c2[4] = {0.f, 0.f, 0.f, 0.f}, c3[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int k = 0; k < 8; k++) {
-    uint32_t A[16];
-    dq_row(nib(r0 + 18 * k, k, L), A[0], A[1], A[2], A[3]);
-    dq_row(nib(r1 + 18 * k, k, L), A[4], A[5], A[6], A[7]);
-    dq_row(nib(r2 + 18 * k, k, L), A[8], A[9], A[10], A[11]);
-    dq_row(nib(r3 + 18 * k, k, L), A[12], A[13], A[14], A[15]);
-    const bool mine = g == k;
-    const uint32_t b0 = mine ? xh.x : 0u, b1 = mine ? xh.y : 0u, b2 = mine ? xh.z : 0u, b3 = mine ? xh.w : 0u;
-    mma16816(c0, A[0], A[4], A[1], A[5], b0, b1);
-    mma16816(c2, A[8], A[12], A[9], A[13], b0, b1);
-    mma16816(c1, A[2], A[6], A[3], A[7], b2, b3);
-    mma16816(c3, A[10], A[14], A[11], A[15], b2, b3);
-    if (xf32) {
-      const uint32_t l0 = mine ? xl.x : 0u, l1 = mine ? xl.y : 0u, l2 = mine ? xl.z : 0u, l3 = mine ? xl.w : 0u;
-      mma16816(c0, A[0], A[4], A[1], A[5], l0, l1);
-      mma16816(c2, A[8], A[12], A[9], A[13], l0, l1);
-      mma16816(c1, A[2], A[6], A[3], A[7], l2, l3);
-      mma16816(c3, A[10], A[14], A[11], A[15], l2, l3);
-    }
-  }
-  const uint8_t* rr[4] = {r0, r1, r2, r3};
-  float d[8];
-#pragma unroll
-  for (int r = 0; r < 4; r++) {
-    d[2 * r] = h2f(*reinterpret_cast<const uint16_t*>(rr[r] + 36 * t));
-    d[2 * r + 1] = h2f(*reinterpret_cast<const uint16_t*>(rr[r] + 36 * t + 18));
-  }
-  acc[0] = fmaf(d[0], c0[0] + c1[0], fmaf(d[1], c0[1] + c1[1], acc[0]));
-  acc[1] = fmaf(d[2], c0[2] + c1[2], fmaf(d[3], c0[3] + c1[3], acc[1]));
-  acc[2] = fmaf(d[4], c2[0] + c3[0], fmaf(d[5], c2[1] + c3[1], acc[2]));
-  acc[3] = fmaf(d[6], c2[2] + c3[2], fmaf(d[7], c2[3] + c3[3], acc[3]));
-}
-
 }  // namespace e4b
