@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 
 from oracle import ops as O
+from pack_layout import pack_q40
 
 pytestmark = pytest.mark.gpu
 F32 = np.float32
@@ -71,35 +72,6 @@ def test_grouped_moe_matches_per_token_oracle(e4b, dev, n, hot):
     assert worst < 2e-3, worst     # f16 GeGLU intermediates may round one ulp apart
 
 
-def _pack_q40_ref(w: np.ndarray, rows: int, n_in: int) -> np.ndarray:
-    """numpy restatement of the tile-packed q4_0 layout (e4b_q40_pack_tiles)."""
-    nq, rb = n_in // 256, n_in // 32 * 18
-    src = w.reshape(rows, rb)
-    out = np.zeros((rows // 16, nq, 2304), np.uint8)
-    for r16 in range(rows // 16):
-        for q in range(nq):
-            piece = out[r16, q]
-            for r in range(16):
-                row = src[16 * r16 + r]
-                for k in range(8):
-                    b = 8 * q + k
-                    piece[16 * r + 2 * k:16 * r + 2 * k + 2] = row[18 * b:18 * b + 2]
-                for kh in range(2):
-                    for t in range(4):
-                        for j in range(4):
-                            b = 8 * q + 4 * kh + j
-                            blk = row[18 * b:18 * b + 18]
-                            if b & 1:
-                                word = blk[2 + 4 * t:6 + 4 * t]
-                            elif t < 3:
-                                word = blk[4 + 4 * t:8 + 4 * t]
-                            else:
-                                word = np.array([blk[2], blk[3], blk[16], blk[17]], np.uint8)
-                            o = 256 + ((kh * 16 + r) * 4 + t) * 16 + 4 * j
-                            piece[o:o + 4] = word
-    return out.reshape(-1)
-
-
 @pytest.mark.parametrize("H,n,hot", [(512, 13, 0), (512, 80, 75), (256, 64, 0)])
 def test_q40gugrp_tiles_bit_identical(e4b, dev, H, n, hot):
     """The tile-packed copy matches its numpy restatement byte for byte, and the
@@ -122,7 +94,7 @@ def test_q40gugrp_tiles_bit_identical(e4b, dev, H, n, hot):
     d.sync()
     assert d.status() == 0
     packed = d.read(bt, np.uint8, wgu.nbytes)
-    assert np.array_equal(packed, _pack_q40_ref(wgu.view(np.uint8), E * 2 * EF, H))
+    assert np.array_equal(packed, pack_q40(wgu.view(np.uint8), E * 2 * EF, H))
     a, b = d.read(g0, np.uint16, n * K * EF), d.read(g1, np.uint16, n * K * EF)
     assert np.array_equal(a, b)
 
